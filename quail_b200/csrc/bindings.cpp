@@ -1,0 +1,72 @@
+// Python bindings of the sm_100a kernels (module quail_b200._C).
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "gemm_sm100.h"
+
+namespace qb {
+
+void embed_gather(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out);
+void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, const c10::optional<torch::Tensor>& y8,
+                   const c10::optional<torch::Tensor>& ys, const c10::optional<torch::Tensor>& ybf, int64_t T);
+void quant_rows(const torch::Tensor& x, bool swiglu, const c10::optional<torch::Tensor>& y8,
+                const c10::optional<torch::Tensor>& ys, const c10::optional<torch::Tensor>& ybf, int64_t T);
+void qk_norm_rope_kv(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& qw,
+                     const torch::Tensor& kw, const torch::Tensor& cos_sin, const torch::Tensor& slots,
+                     torch::Tensor& q_out, torch::Tensor& k_cache, torch::Tensor& v_cache, int64_t QH, int64_t KH,
+                     double eps, bool norm_qk, int64_t T);
+void final_norm_readout(const torch::Tensor& x, const torch::Tensor& rows, const torch::Tensor& w, double eps,
+                        const torch::Tensor& head, torch::Tensor& logits, const c10::optional<torch::Tensor>& normed);
+void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
+                       const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
+                       double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_scale);
+
+static std::mutex g_err_mu;
+static int* g_err[64] = {nullptr};
+
+int* device_error_word(int dev) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_err[dev]) {
+    c10::cuda::CUDAGuard guard(dev);
+    int* p = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&p, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+    g_err[dev] = p;
+  }
+  return g_err[dev];
+}
+
+// Synchronizes the device, returns the error code kernels recorded since the
+// last call (0 = none) and clears it.
+int64_t read_and_clear_error(int64_t dev) {
+  int* p = device_error_word((int)dev);
+  c10::cuda::CUDAGuard guard((int)dev);
+  int h = 0;
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  C10_CUDA_CHECK(cudaMemcpy(&h, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+  return h;
+}
+
+}  // namespace qb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "quail_b200 sm_100a kernels";
+  m.def("gemm", &qb::gemm_sm100, "tcgen05 GEMM (bf16 or block-scaled e4m3) with fused epilogues", py::arg("a"),
+        py::arg("b"), py::arg("sa"), py::arg("sb"), py::arg("sb_gran"), py::arg("epi"), py::arg("out"),
+        py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
+  m.def("embed_gather", &qb::embed_gather);
+  m.def("rmsnorm_quant", &qb::rmsnorm_quant);
+  m.def("quant_rows", &qb::quant_rows);
+  m.def("qk_norm_rope_kv", &qb::qk_norm_rope_kv);
+  m.def("final_norm_readout", &qb::final_norm_readout);
+  m.def("prefill_attention", &qb::prefill_attention);
+  m.def("read_and_clear_error", &qb::read_and_clear_error);
+  m.attr("EPI_BF16") = (int)qb::kEpiBf16;
+  m.attr("EPI_RESIDUAL") = (int)qb::kEpiResidual;
+  m.attr("EPI_SWIGLU_FP8") = (int)qb::kEpiSwigluFp8;
+  m.attr("EPI_SWIGLU_BF16") = (int)qb::kEpiSwigluBf16;
+}

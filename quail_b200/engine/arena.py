@@ -1,0 +1,165 @@
+"""Paged KV arena: device K/V pools plus host-side page accounting.
+
+Layout on the device: one tensor [layers, 2, pages, page_tokens, kv_heads,
+head_dim] bf16, so a layer's K or V pool is a contiguous view
+[pages, page_tokens, kv_heads, head_dim] (the layout the K4 KV-write and K6
+attention kernels take). A B200 holds 180 GB of HBM3e; the arena is sized by
+the planner's `arena_pages` from what is left after weights and activations.
+
+Accounting (`PagePool`, pure Python, CPU-testable): a free stack, page lists
+per key, and a hold count per page. A key owns the pages it writes. Another
+key may read a resident key's first `tokens` tokens as one of its segments
+(borrowing: a question reads its document's pages, every row reads the one
+copy of the shared instruction prefix); a borrow holds the parent's pages so
+they are not freed under the reader. Retained keys stay resident after use
+until evicted (KV reuse across operators).
+
+Reference behavior: quail/backends/quail/executor/pages.py (PageArena:
+free list, owned/borrowed pages, holds, retention) and arena.py (KVArena).
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import numpy as np
+import torch
+
+
+class ArenaFullError(RuntimeError):
+    """The arena cannot hold a request even when empty."""
+
+
+class PagePool:
+    def __init__(self, num_pages: int, page_tokens: int):
+        self.num_pages = num_pages
+        self.page_tokens = page_tokens
+        self.free = list(range(num_pages - 1, -1, -1))  # stack: pop() gives the lowest id first
+        self.owned: dict = {}          # key -> page ids it writes
+        self.tokens: dict = {}         # key -> tokens resident
+        self.holds = np.zeros(num_pages, dtype=np.int32)
+        self.borrows: dict = {}        # key -> list of parent keys it holds
+        self.retained: OrderedDict = OrderedDict()  # key -> None, oldest first
+
+    # ------------------------------------------------------------ queries
+    def pages_needed(self, tokens: int) -> int:
+        return -(-tokens // self.page_tokens)
+
+    @property
+    def free_pages(self) -> int:
+        return len(self.free)
+
+    def resident(self, key) -> bool:
+        return key in self.owned
+
+    def pages_of(self, key) -> list[int]:
+        return self.owned[key]
+
+    # ------------------------------------------------------------ alloc / grow
+    def alloc(self, key, tokens: int):
+        """Pages for `tokens` new tokens of a new key, or None if the pool is short."""
+        if key in self.owned:
+            raise KeyError(f"{key!r} already resident")
+        need = self.pages_needed(tokens)
+        if need > len(self.free):
+            return None
+        pages = [self.free.pop() for _ in range(need)]
+        self.owned[key] = pages
+        self.tokens[key] = tokens
+        self.holds[pages] += 1
+        self.borrows[key] = []
+        return pages
+
+    def grow(self, key, tokens: int):
+        """Extend a resident key to `tokens` tokens; returns the new pages or None."""
+        have = self.owned[key]
+        need = self.pages_needed(tokens) - len(have)
+        if need > len(self.free):
+            return None
+        new = [self.free.pop() for _ in range(max(need, 0))]
+        have.extend(new)
+        if new:
+            self.holds[new] += 1
+        self.tokens[key] = max(self.tokens[key], tokens)
+        return new
+
+    def borrow(self, reader, parent) -> None:
+        """`reader` reads `parent`'s pages: hold them until the reader is freed."""
+        if parent not in self.owned:
+            raise KeyError(f"borrow parent {parent!r} is not resident")
+        self.holds[self.owned[parent]] += 1
+        self.borrows.setdefault(reader, []).append(parent)
+
+    # ------------------------------------------------------------ release
+    def _drop(self, pages) -> None:
+        if not pages:
+            return
+        self.holds[pages] -= 1
+        for p in pages:
+            if self.holds[p] == 0:
+                self.free.append(p)
+
+    def free_key(self, key) -> None:
+        """Release a key's own pages and the holds it took on borrowed parents."""
+        for parent in self.borrows.pop(key, []):
+            if parent in self.owned:
+                self._drop(self.owned[parent])
+        pages = self.owned.pop(key, None)
+        self.tokens.pop(key, None)
+        self.retained.pop(key, None)
+        if pages is not None:
+            self._drop(pages)
+
+    def retain(self, key) -> None:
+        self.retained[key] = None
+        self.retained.move_to_end(key)
+
+    def evict_retained(self, pages_needed: int) -> list:
+        """Free retained keys, oldest first, until `pages_needed` pages are free."""
+        evicted = []
+        while self.free_pages < pages_needed and self.retained:
+            key, _ = self.retained.popitem(last=False)
+            self.free_key(key)
+            evicted.append(key)
+        return evicted
+
+    def check(self) -> None:
+        """Invariant: every page is free xor held; holds match owners and borrows."""
+        expect = np.zeros(self.num_pages, dtype=np.int32)
+        for pages in self.owned.values():
+            expect[pages] += 1
+        for parents in self.borrows.values():
+            for parent in parents:
+                if parent in self.owned:
+                    expect[self.owned[parent]] += 1
+        assert np.array_equal(expect, self.holds), "hold counts drifted"
+        free = set(self.free)
+        assert len(free) == len(self.free), "page freed twice"
+        for p in range(self.num_pages):
+            assert (p in free) == (self.holds[p] == 0), f"page {p} free/held mismatch"
+
+
+class KVArena:
+    """Device K/V pools with a PagePool."""
+
+    def __init__(self, num_layers: int, num_pages: int, page_tokens: int, kv_heads: int, head_dim: int,
+                 device="cuda", dtype=torch.bfloat16):
+        self.num_layers = num_layers
+        self.page_tokens = page_tokens
+        self.kv_heads = kv_heads
+        self.head_dim = head_dim
+        self.device = torch.device(device)
+        self.kv = torch.zeros(num_layers, 2, num_pages, page_tokens, kv_heads, head_dim, device=device,
+                              dtype=dtype)
+        self.pool = PagePool(num_pages, page_tokens)
+
+    @property
+    def num_pages(self) -> int:
+        return self.pool.num_pages
+
+    def layer(self, i: int):
+        return self.kv[i, 0], self.kv[i, 1]
+
+    @staticmethod
+    def bytes_per_page(num_layers, page_tokens, kv_heads, head_dim, elem_bytes=2) -> int:
+        return num_layers * 2 * page_tokens * kv_heads * head_dim * elem_bytes

@@ -1,0 +1,145 @@
+"""Packed prefill chunks: many questions' new tokens in one forward pass.
+
+A chunk is the unit the GPU runs: up to `chunk_tokens` new tokens from many
+sequences, plus the metadata the kernels read:
+
+  ids, positions, slots   [T] int32  token id, absolute position, KV slot (page*P + offset; -1 = none)
+  seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
+  tiles                   [n, 2]     (sequence, first query row) per 64-row attention tile
+  page_list               [*]        page ids of every segment, segments point into it
+  final_rows              [R]        token row whose logits each readout reads
+
+The host packs it with numpy into one pinned int32 buffer and ships it with
+a single H2D copy (reference: chunk.py pack_chunk + InputStaging, which
+stage per-field pinned buffers).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+MAX_SEGMENTS = 4
+SEQ_INTS = 12
+ATTN_BLOCK_Q = 64
+
+
+@dataclass
+class SeqSpec:
+    """One sequence of a chunk."""
+
+    reads: list            # [(key, tokens)] earlier segments read in full (shared prefix, document, ...)
+    own_key: object        # key whose pages receive the new tokens
+    own_start: int         # own tokens already resident before this chunk
+    tokens: np.ndarray     # new token ids
+    pos_start: int         # absolute position of tokens[0]
+    readout: bool = False  # read the logits of the last new token
+    tag: object = None
+
+
+@dataclass
+class Chunk:
+    num_tokens: int
+    ids: torch.Tensor
+    positions: torch.Tensor
+    slots: torch.Tensor
+    seqs: torch.Tensor
+    tiles: torch.Tensor
+    page_list: torch.Tensor
+    final_rows: torch.Tensor
+    readout_tags: list = field(default_factory=list)
+    num_seqs: int = 0
+    host: dict | None = None   # numpy copies (tests, CPU reference)
+
+
+class ChunkPacker:
+    """Packs SeqSpecs against a PagePool into a Chunk on `device`."""
+
+    def __init__(self, pool, device, pin: bool = True):
+        self.pool = pool
+        self.device = torch.device(device)
+        self.pin = pin and self.device.type == "cuda"
+        self._staging: torch.Tensor | None = None
+
+    def pack(self, specs: list[SeqSpec]) -> Chunk:
+        P = self.pool.page_tokens
+        n_tok = sum(len(s.tokens) for s in specs)
+        ids = np.empty(n_tok, dtype=np.int32)
+        pos = np.empty(n_tok, dtype=np.int32)
+        slots = np.empty(n_tok, dtype=np.int32)
+        seqs = np.zeros((len(specs), SEQ_INTS), dtype=np.int32)
+        page_list: list[int] = []
+        seg_cache: dict = {}
+        tiles: list[tuple[int, int]] = []
+        final_rows: list[int] = []
+        tags: list = []
+        q = 0
+        for si, s in enumerate(specs):
+            n = len(s.tokens)
+            if len(s.reads) + 1 > MAX_SEGMENTS:
+                raise ValueError(f"a sequence reads at most {MAX_SEGMENTS - 1} earlier segments")
+            ids[q:q + n] = s.tokens
+            pos[q:q + n] = s.pos_start + np.arange(n, dtype=np.int32)
+            own_pages = np.asarray(self.pool.pages_of(s.own_key), dtype=np.int64)
+            j = s.own_start + np.arange(n)
+            slots[q:q + n] = (own_pages[j // P] * P + j % P).astype(np.int32)
+            row = seqs[si]
+            row[0], row[1], row[2] = q, n, len(s.reads) + 1
+            for i, (key, ln) in enumerate(s.reads):
+                npg = -(-ln // P)
+                ck = (key, npg)
+                off = seg_cache.get(ck)
+                if off is None:
+                    off = len(page_list)
+                    page_list.extend(self.pool.pages_of(key)[:npg])
+                    seg_cache[ck] = off
+                row[4 + i], row[8 + i] = ln, off
+            own_len = s.own_start + n
+            npg = -(-own_len // P)
+            row[4 + len(s.reads)] = own_len
+            row[8 + len(s.reads)] = len(page_list)
+            page_list.extend(self.pool.pages_of(s.own_key)[:npg])
+            tiles.extend((si, q0) for q0 in range(0, n, ATTN_BLOCK_Q))
+            if s.readout:
+                final_rows.append(q + n - 1)
+                tags.append(s.tag)
+            q += n
+        tiles_a = np.asarray(tiles, dtype=np.int32).reshape(-1, 2)
+        pl = np.asarray(page_list, dtype=np.int32)
+        fr = np.asarray(final_rows, dtype=np.int32)
+        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr]
+        sizes = [p.size for p in parts]
+        flat = np.concatenate(parts) if n_tok else np.zeros(0, dtype=np.int32)
+        dev = self._upload(flat)
+        views = []
+        o = 0
+        for sz in sizes:
+            views.append(dev[o:o + sz])
+            o += sz
+        host = {"ids": ids, "positions": pos, "slots": slots, "seqs": seqs, "tiles": tiles_a,
+                "page_list": pl, "final_rows": fr}
+        return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
+                     seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
+                     final_rows=views[6], readout_tags=tags, num_seqs=len(specs), host=host)
+
+    def _upload(self, flat: np.ndarray) -> torch.Tensor:
+        src = torch.from_numpy(flat)
+        if self.device.type != "cuda":
+            return src.clone()
+        if self.pin:
+            if self._staging is None or self._staging.numel() < flat.size:
+                self._staging = torch.empty(max(flat.size, 1 << 16) * 2, dtype=torch.int32, pin_memory=True)
+            # the staging buffer is reused: wait for the previous copy out of it
+            if getattr(self, "_copy_done", None) is not None:
+                self._copy_done.synchronize()
+            stage = self._staging[:flat.size]
+            stage.copy_(src)
+            out = torch.empty(flat.size, dtype=torch.int32, device=self.device)
+            out.copy_(stage, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            self._copy_done = ev
+            return out
+        return src.to(self.device)

@@ -1,0 +1,196 @@
+"""Qwen3 decoder: the sm_100a kernel pipeline and its fp32 CPU statement.
+
+Both take the same packed chunk (`quail_b200.engine.chunk.Chunk`) and the
+same paged KV arena, and return the logits of the chunk's readout rows
+against the retained answer rows of the LM head:
+
+  embed -> [rmsnorm+quant -> QKV GEMM -> qk-norm+RoPE+KV write ->
+            segmented paged attention (+quant) -> o GEMM (+residual) ->
+            rmsnorm+quant -> gate_up GEMM (+SwiGLU+quant) -> down GEMM (+residual)] x L
+        -> gather readout rows -> final norm -> answer-row logits
+
+The reference drives vLLM modules with its own loop
+(quail/backends/quail/executor/models/qwen3.py:15-135, Engine primitives in
+attention.py:432-1573); here every step is one of our kernels.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from quail_b200.models.config import DecoderConfig
+from quail_b200.models.weights import dequantized, head_weight
+from quail_b200.ops import reference as ref
+
+
+class Qwen3Weights:
+    """Per-layer fused device weights in the kernels' layouts.
+
+    QKV rows are concatenated (q | k | v); gate/up rows are interleaved in
+    64-row groups for the SwiGLU epilogue, with their 128x128 block scales
+    expanded to 64-row granularity. fp8 models keep e4m3 + fp32 scales,
+    bf16 models keep bf16.
+    """
+
+    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None):
+        from quail_b200.ops.quant import interleave_gate_up
+        self.cfg = cfg
+        self.device = device
+        bf = torch.bfloat16
+        self.embed = ckpt["model.embed_tokens.weight"].to(device=device, dtype=bf).contiguous()
+        self.final_norm = ckpt["model.norm.weight"].to(device=device, dtype=bf)
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            L = {
+                "ln1": ckpt[p + "input_layernorm.weight"].to(device=device, dtype=bf),
+                "ln2": ckpt[p + "post_attention_layernorm.weight"].to(device=device, dtype=bf),
+                "qn": ckpt[p + "self_attn.q_norm.weight"].to(device=device, dtype=bf),
+                "kn": ckpt[p + "self_attn.k_norm.weight"].to(device=device, dtype=bf),
+            }
+            names = [p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"]
+            if cfg.fp8:
+                L["wqkv"] = torch.cat([ckpt[n + ".weight"] for n in names]).to(device).contiguous()
+                L["sqkv"] = torch.cat([ckpt[n + ".weight_scale_inv"] for n in names]).to(device).contiguous()
+                L["wo"] = ckpt[p + "self_attn.o_proj.weight"].to(device).contiguous()
+                L["so"] = ckpt[p + "self_attn.o_proj.weight_scale_inv"].to(device).contiguous()
+                gu = torch.cat([ckpt[p + "mlp.gate_proj.weight"], ckpt[p + "mlp.up_proj.weight"]]).to(device)
+                gus = torch.cat([ckpt[p + "mlp.gate_proj.weight_scale_inv"],
+                                 ckpt[p + "mlp.up_proj.weight_scale_inv"]]).to(device)
+                L["wgu"], L["sgu"] = interleave_gate_up(gu, gus)
+                L["wd"] = ckpt[p + "mlp.down_proj.weight"].to(device).contiguous()
+                L["sd"] = ckpt[p + "mlp.down_proj.weight_scale_inv"].to(device).contiguous()
+            else:
+                L["wqkv"] = torch.cat([ckpt[n + ".weight"].to(bf) for n in names]).to(device).contiguous()
+                L["wo"] = ckpt[p + "self_attn.o_proj.weight"].to(device=device, dtype=bf).contiguous()
+                gu = torch.cat([ckpt[p + "mlp.gate_proj.weight"], ckpt[p + "mlp.up_proj.weight"]]).to(
+                    device=device, dtype=bf)
+                L["wgu"] = interleave_gate_up(gu)
+                L["wd"] = ckpt[p + "mlp.down_proj.weight"].to(device=device, dtype=bf).contiguous()
+            self.layers.append(L)
+        self.head = head_weight(ckpt, cfg)
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=device)
+        self.answer_rows = None
+        if head_rows is not None:
+            self.set_answer_rows(head_rows)
+
+    def set_answer_rows(self, token_ids) -> None:
+        """Retain the LM-head rows of the answer tokens (yes/no or labels)."""
+        ids = torch.as_tensor(list(token_ids), dtype=torch.long)
+        self.answer_rows = self.head.index_select(0, ids.to(self.head.device)).to(
+            device=self.device, dtype=torch.bfloat16).contiguous()
+        self.answer_ids = ids
+
+
+class Qwen3Pipeline:
+    """Forward pass of a packed chunk on the sm_100a kernels."""
+
+    def __init__(self, cfg: DecoderConfig, weights: Qwen3Weights):
+        assert cfg.head_dim == 128, "the kernels take head_dim 128"
+        self.cfg = cfg
+        self.w = weights
+        self.scale = ref.softmax_scale(cfg.head_dim)
+
+    @torch.no_grad()
+    def forward_chunk(self, chunk, arena) -> torch.Tensor:
+        from quail_b200 import ops
+        cfg, w = self.cfg, self.w
+        T = chunk.num_tokens
+        dev = w.device
+        h = ops.embed_gather(chunk.ids, w.embed)  # residual stream, bf16 [T, H]
+        fp8 = cfg.fp8
+        for li, L in enumerate(w.layers):
+            kc, vc = arena.layer(li)
+            if fp8:
+                x8, xs = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps)
+                qkv = ops.gemm(x8, L["wqkv"], sa=xs, sb=L["sqkv"])
+            else:
+                x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
+                qkv = ops.gemm(x, L["wqkv"])
+            q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
+                                    cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
+            if fp8:
+                o8, os_ = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale,
+                                                fp8_out=True)
+                ops.gemm(o8, L["wo"], sa=os_, sb=L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                x8, xs = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps)
+                a8, as_ = ops.gemm(x8, L["wgu"], sa=xs, sb=L["sgu"], sb_gran=64, epi=ops.EPI_SWIGLU_FP8)
+                ops.gemm(a8, L["wd"], sa=as_, sb=L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+            else:
+                o = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale)
+                ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+                a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
+                ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+        del T, dev
+        return ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows)
+
+
+class Qwen3Reference:
+    """fp32 PyTorch forward over the same chunk and arena (CPU or GPU).
+
+    Weights are dequantized from the checkpoint, so an fp8 checkpoint gives
+    the math the kernels approximate (activations stay fp32 here).
+    """
+
+    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device="cpu", head_rows=None,
+                 dtype=torch.float32):
+        self.cfg = cfg
+        self.device = device
+        self.dtype = dtype
+        f = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
+        self.embed = f(ckpt["model.embed_tokens.weight"])
+        self.final_norm = f(ckpt["model.norm.weight"])
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            self.layers.append({
+                "ln1": f(ckpt[p + "input_layernorm.weight"]), "ln2": f(ckpt[p + "post_attention_layernorm.weight"]),
+                "qn": f(ckpt[p + "self_attn.q_norm.weight"]), "kn": f(ckpt[p + "self_attn.k_norm.weight"]),
+                "wq": f(dequantized(ckpt, p + "self_attn.q_proj")), "wk": f(dequantized(ckpt, p + "self_attn.k_proj")),
+                "wv": f(dequantized(ckpt, p + "self_attn.v_proj")), "wo": f(dequantized(ckpt, p + "self_attn.o_proj")),
+                "wg": f(dequantized(ckpt, p + "mlp.gate_proj")), "wu": f(dequantized(ckpt, p + "mlp.up_proj")),
+                "wd": f(dequantized(ckpt, p + "mlp.down_proj")),
+            })
+        self.head = f(head_weight(ckpt, cfg))
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=device)
+        self.scale = ref.softmax_scale(cfg.head_dim)
+        self.answer_rows = None
+        if head_rows is not None:
+            self.set_answer_rows(head_rows)
+
+    def set_answer_rows(self, token_ids) -> None:
+        ids = torch.as_tensor(list(token_ids), dtype=torch.long, device=self.head.device)
+        self.answer_rows = self.head.index_select(0, ids)
+        self.answer_ids = ids.cpu()
+
+    @torch.no_grad()
+    def hidden_chunk(self, chunk, arena) -> torch.Tensor:
+        cfg = self.cfg
+        T = chunk.num_tokens
+        h = self.embed[chunk.ids.long()]
+        QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+        for li, L in enumerate(self.layers):
+            kc, vc = arena.layer(li)
+            x = ref.rmsnorm(h, L["ln1"], cfg.rms_eps)
+            q = (x @ L["wq"].t()).view(T, QH, D)
+            k = (x @ L["wk"].t()).view(T, KH, D)
+            v = (x @ L["wv"].t()).view(T, KH, D)
+            q = ref.rope_neox(ref.rmsnorm(q, L["qn"], cfg.rms_eps), chunk.positions, self.cos_sin)
+            k = ref.rope_neox(ref.rmsnorm(k, L["kn"], cfg.rms_eps), chunk.positions, self.cos_sin)
+            ok = chunk.slots >= 0
+            slots = chunk.slots[ok].long()
+            kc.view(-1, KH, D)[slots] = k[ok].to(kc.dtype)
+            vc.view(-1, KH, D)[slots] = v[ok].to(vc.dtype)
+            o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(h.dtype)
+            h = h + o @ L["wo"].t()
+            x = ref.rmsnorm(h, L["ln2"], cfg.rms_eps)
+            h = h + ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t()
+        return h
+
+    @torch.no_grad()
+    def forward_chunk(self, chunk, arena) -> torch.Tensor:
+        h = self.hidden_chunk(chunk, arena)
+        rows = h[chunk.final_rows.long()]
+        normed = ref.rmsnorm(rows, self.final_norm, self.cfg.rms_eps)
+        return (normed @ self.answer_rows.t()).float()

@@ -1,0 +1,155 @@
+"""Checkpoint format: Hugging Face safetensors with Qwen3 tensor names.
+
+fp8 checkpoints (Qwen/Qwen3-*-FP8) hold each projection as e4m3 `weight`
+plus an fp32 `weight_scale_inv` of shape [ceil(N/128), K/128]: the
+dequantized weight is weight * scale per 128x128 block. The random-init
+generator below writes exactly that format (N(0, std) weights quantized with
+block-amax scales), so a synthetic model and a downloaded one load through
+the same path. Reference loader: quail/backends/quail/executor/model_loading.py.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from collections.abc import Iterator
+
+import torch
+
+from quail_b200.models.config import DecoderConfig
+from quail_b200.ops.quant import quantize_weight
+
+PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def layer_prefix(i: int) -> str:
+    return f"model.layers.{i}."
+
+
+def projection_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
+    H = cfg.hidden
+    return {
+        "self_attn.q_proj": (cfg.q_dim, H),
+        "self_attn.k_proj": (cfg.kv_dim, H),
+        "self_attn.v_proj": (cfg.kv_dim, H),
+        "self_attn.o_proj": (H, cfg.q_dim),
+        "mlp.gate_proj": (cfg.intermediate, H),
+        "mlp.up_proj": (cfg.intermediate, H),
+        "mlp.down_proj": (H, cfg.intermediate),
+    }
+
+
+def expert_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
+    H, I = cfg.hidden, cfg.moe_intermediate
+    return {"gate_proj": (I, H), "up_proj": (I, H), "down_proj": (H, I)}
+
+
+def _rand(shape, std, gen, device, dtype=torch.float32):
+    return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std).to(dtype)
+
+
+def _emit_proj(name, shape, cfg, gen, device, dtype):
+    w = _rand(shape, cfg.init_std, gen, device)
+    if cfg.fp8:
+        q, s = quantize_weight(w)
+        return {name + ".weight": q, name + ".weight_scale_inv": s}
+    return {name + ".weight": w.to(dtype)}
+
+
+def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="cpu",
+                      dtype=torch.bfloat16, experts: range | None = None) -> Iterator[tuple[str, torch.Tensor]]:
+    """Tensors of layer i in checkpoint names (fp8 projections quantized)."""
+    p = layer_prefix(i)
+    H = cfg.hidden
+    one = torch.ones(H, device=device, dtype=dtype)
+    yield p + "input_layernorm.weight", one.clone()
+    yield p + "post_attention_layernorm.weight", one.clone()
+    yield p + "self_attn.q_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+    yield p + "self_attn.k_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+    shapes = projection_shapes(cfg)
+    for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj"):
+        yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
+    if cfg.is_moe:
+        # router logits ~ N(0, 1) per token: gate weight std 1/sqrt(H) on unit-RMS rows
+        yield p + "mlp.gate.weight", _rand((cfg.num_experts, H), H ** -0.5, gen, device, dtype)
+        for e in (experts if experts is not None else range(cfg.num_experts)):
+            for name, shape in expert_shapes(cfg).items():
+                yield from _emit_proj(p + f"mlp.experts.{e}.{name}", shape, cfg, gen, device, dtype).items()
+    else:
+        for name in ("mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+            yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
+
+
+def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
+                      layers: range | None = None) -> dict[str, torch.Tensor]:
+    """A whole random-init checkpoint dict in HF names."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out: dict[str, torch.Tensor] = {}
+    out["model.embed_tokens.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
+    for i in (layers if layers is not None else range(cfg.layers)):
+        out.update(iter_random_layer(cfg, i, gen, device, dtype))
+    out["model.norm.weight"] = torch.ones(cfg.hidden, device=device, dtype=dtype)
+    if not cfg.tied_head:
+        out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
+    return out
+
+
+def head_weight(ckpt: dict[str, torch.Tensor], cfg: DecoderConfig) -> torch.Tensor:
+    return ckpt["model.embed_tokens.weight"] if cfg.tied_head else ckpt["lm_head.weight"]
+
+
+def save_checkpoint(ckpt: dict[str, torch.Tensor], cfg: DecoderConfig, directory: str) -> None:
+    from safetensors.torch import save_file
+    os.makedirs(directory, exist_ok=True)
+    save_file({k: v.contiguous().cpu() for k, v in ckpt.items()}, os.path.join(directory, "model.safetensors"))
+    hf = {
+        "architectures": ["Qwen3MoeForCausalLM" if cfg.is_moe else "Qwen3ForCausalLM"],
+        "hidden_size": cfg.hidden, "num_hidden_layers": cfg.layers,
+        "num_attention_heads": cfg.num_q_heads, "num_key_value_heads": cfg.num_kv_heads,
+        "head_dim": cfg.head_dim, "intermediate_size": cfg.intermediate, "vocab_size": cfg.vocab,
+        "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.rms_eps, "tie_word_embeddings": cfg.tied_head,
+        "max_position_embeddings": cfg.max_position,
+    }
+    if cfg.is_moe:
+        hf.update(num_experts=cfg.num_experts, num_experts_per_tok=cfg.top_k,
+                  moe_intermediate_size=cfg.moe_intermediate)
+    if cfg.fp8:
+        hf["quantization_config"] = {"quant_method": "fp8", "fmt": "e4m3", "weight_block_size": [128, 128],
+                                     "activation_scheme": "dynamic"}
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(hf, f, indent=1)
+
+
+def config_from_hf(directory: str, name: str | None = None) -> DecoderConfig:
+    with open(os.path.join(directory, "config.json")) as f:
+        hf = json.load(f)
+    q = hf.get("quantization_config") or {}
+    return DecoderConfig(
+        name=name or os.path.basename(os.path.normpath(directory)),
+        layers=hf["num_hidden_layers"], hidden=hf["hidden_size"], num_q_heads=hf["num_attention_heads"],
+        num_kv_heads=hf["num_key_value_heads"], head_dim=hf.get("head_dim", hf["hidden_size"] // hf["num_attention_heads"]),
+        intermediate=hf["intermediate_size"], vocab=hf["vocab_size"], rope_theta=hf.get("rope_theta", 1e6),
+        rms_eps=hf.get("rms_norm_eps", 1e-6), tied_head=hf.get("tie_word_embeddings", False),
+        weight_dtype="fp8" if q.get("quant_method") == "fp8" else "bf16",
+        num_experts=hf.get("num_experts", 0), top_k=hf.get("num_experts_per_tok", 0),
+        moe_intermediate=hf.get("moe_intermediate_size", 0),
+        max_position=hf.get("max_position_embeddings", 40960))
+
+
+def load_checkpoint(directory: str, device="cpu") -> dict[str, torch.Tensor]:
+    from safetensors.torch import load_file
+    out: dict[str, torch.Tensor] = {}
+    for fn in sorted(os.listdir(directory)):
+        if fn.endswith(".safetensors"):
+            out.update(load_file(os.path.join(directory, fn), device=str(device)))
+    return out
+
+
+def dequantized(ckpt: dict[str, torch.Tensor], name: str) -> torch.Tensor:
+    """fp32 value of a projection weight, whatever its stored format."""
+    w = ckpt[name + ".weight"]
+    s = ckpt.get(name + ".weight_scale_inv")
+    if s is None:
+        return w.float()
+    from quail_b200.ops.quant import dequantize_weight
+    return dequantize_weight(w, s)

@@ -1,0 +1,34 @@
+"""Python entry points of the sm_100a kernels in `quail_b200._C`.
+
+Every op here runs the hand-written CUDA kernel; there is no PyTorch
+fallback on a GPU. If the extension is missing on a machine with a GPU,
+importing an op raises, so a test or a bench can never pass on eager
+PyTorch by accident. `quail_b200.ops.reference` holds the plain fp32
+PyTorch statement of each op, used by the CPU model and by the kernel
+tests.
+"""
+
+from quail_b200.ops.kernels import (  # noqa: F401
+    EPI_BF16,
+    EPI_RESIDUAL,
+    EPI_SWIGLU_BF16,
+    EPI_SWIGLU_FP8,
+    embed_gather,
+    final_norm_readout,
+    gemm,
+    kernels_available,
+    native,
+    prefill_attention,
+    qk_norm_rope_kv,
+    quant_rows,
+    read_and_clear_error,
+    rmsnorm_quant,
+)
+from quail_b200.ops.quant import (  # noqa: F401
+    FP8_MAX,
+    dequantize_act,
+    dequantize_weight,
+    interleave_gate_up,
+    quantize_act,
+    quantize_weight,
+)

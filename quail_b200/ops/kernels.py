@@ -1,0 +1,143 @@
+"""Thin wrappers that allocate outputs and call the compiled kernels."""
+
+from __future__ import annotations
+
+import importlib
+
+import torch
+
+_C = None
+_IMPORT_ERROR: Exception | None = None
+try:
+    _C = importlib.import_module("quail_b200._C")
+except Exception as exc:  # noqa: BLE001 - surfaced by native()
+    _IMPORT_ERROR = exc
+
+EPI_BF16 = 0
+EPI_RESIDUAL = 1
+EPI_SWIGLU_FP8 = 2
+EPI_SWIGLU_BF16 = 3
+
+
+def kernels_available() -> bool:
+    return _C is not None
+
+
+def native():
+    """The compiled extension; raises if it was not built."""
+    if _C is None:
+        raise RuntimeError(
+            "quail_b200._C is not built (run `python setup.py build_ext --inplace`): "
+            f"{_IMPORT_ERROR}")
+    return _C
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
+         sb: torch.Tensor | None = None, sb_gran: int = 128, epi: int = EPI_BF16,
+         out: torch.Tensor | None = None, out_scale: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, bn: int = 256):
+    """D = A . B^T on the tcgen05 GEMM.
+
+    A [M, K] and B [N, K] are both bf16, or both e4m3 with `sa` [K/128, >=M]
+    (one fp32 scale per token and 128-wide K group) and `sb`
+    [ceil(N/sb_gran), K/128]. Epilogues: EPI_BF16 -> [M, N] bf16;
+    EPI_RESIDUAL -> out = acc + residual (out may be the residual itself);
+    EPI_SWIGLU_BF16 -> [M, N/2] bf16 of silu(gate) * up over a gate/up
+    interleaved B; EPI_SWIGLU_FP8 -> ([M, N/2] e4m3, [N/256, M] scales).
+    """
+    C = native()
+    M, N = a.shape[0], b.shape[0]
+    if epi == EPI_SWIGLU_FP8:
+        if out is None:
+            out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
+        if out_scale is None:
+            out_scale = torch.empty(N // 256, M, dtype=torch.float32, device=a.device)
+        C.gemm(a, b, sa, sb, sb_gran, epi, out, out_scale, None, bn)
+        return out, out_scale
+    if out is None:
+        width = N // 2 if epi == EPI_SWIGLU_BF16 else N
+        out = torch.empty(M, width, dtype=torch.bfloat16, device=a.device)
+    C.gemm(a, b, sa, sb, sb_gran, epi, out, None, residual, bn)
+    return out
+
+
+def embed_gather(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=torch.bfloat16, device=ids.device)
+    native().embed_gather(ids, table, out)
+    return out
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, *, fp8: bool = True,
+                  out=None, out_scale=None, rows: int | None = None):
+    """RMSNorm of x's first `rows` rows -> (e4m3 [T, H], scales [H/128, T]) or bf16."""
+    T = x.shape[0] if rows is None else rows
+    H = x.shape[1]
+    if fp8:
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
+        if out_scale is None:
+            out_scale = torch.empty(H // 128, T, dtype=torch.float32, device=x.device)
+        native().rmsnorm_quant(x, w, eps, out, out_scale, None, T)
+        return out, out_scale
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    native().rmsnorm_quant(x, w, eps, None, None, out, T)
+    return out
+
+
+def quant_rows(x: torch.Tensor, *, swiglu: bool = False, fp8: bool = True, rows: int | None = None):
+    """bf16 rows -> e4m3 + 1x128 scales (optionally SwiGLU of [gate | up] first)."""
+    T = x.shape[0] if rows is None else rows
+    K = x.shape[1] // 2 if swiglu else x.shape[1]
+    if fp8:
+        y = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.empty(K // 128, T, dtype=torch.float32, device=x.device)
+        native().quant_rows(x, swiglu, y, s, None, T)
+        return y, s
+    y = torch.empty(T, K, dtype=torch.bfloat16, device=x.device)
+    native().quant_rows(x, swiglu, None, None, y, T)
+    return y
+
+
+def qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, k_cache, v_cache,
+                    num_q_heads: int, num_kv_heads: int, eps: float, *, norm_qk: bool = True,
+                    q_out=None, rows: int | None = None):
+    """Per-head q/k RMSNorm + NeoX RoPE; q -> [T, QH, 128]; k, v -> cache[slot]."""
+    T = qkv.shape[0] if rows is None else rows
+    if q_out is None:
+        q_out = torch.empty(T, num_q_heads, 128, dtype=torch.bfloat16, device=qkv.device)
+    native().qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, q_out, k_cache,
+                             v_cache, num_q_heads, num_kv_heads, eps, norm_qk, T)
+    return q_out
+
+
+def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale: float, *,
+                      fp8_out: bool = False, out=None, out_scale=None):
+    """Segmented paged attention (see csrc/attention.cu) -> [T, QH*128]."""
+    T, QH = q.shape[0], q.shape[1]
+    if fp8_out:
+        if out is None:
+            out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
+        if out_scale is None:
+            out_scale = torch.empty(QH, T, dtype=torch.float32, device=q.device)
+        native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale,
+                                   out, out_scale)
+        return out, out_scale
+    if out is None:
+        out = torch.empty(T, QH * 128, dtype=torch.bfloat16, device=q.device)
+    native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out, None)
+    return out
+
+
+def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, normed=None):
+    """Gather rows of x, final RMSNorm, logits against the retained head rows."""
+    if logits is None:
+        logits = torch.empty(rows.numel(), head_rows.shape[0], dtype=torch.float32, device=x.device)
+    native().final_norm_readout(x, rows, norm_w, eps, head_rows, logits, normed)
+    return logits
+
+
+def read_and_clear_error(device: int = 0) -> int:
+    """Synchronize and return (then clear) the kernels' bounded-wait error code."""
+    return int(native().read_and_clear_error(device))

@@ -1,0 +1,95 @@
+"""Plain PyTorch fp32 statements of every kernel op.
+
+These are the numerical oracle for the kernel tests and the ops of the CPU
+model (`quail_b200.models.qwen3.Qwen3Reference`).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device=None) -> torch.Tensor:
+    """[max_pos, head_dim] fp32: cos of the head_dim/2 frequencies, then sin."""
+    half = head_dim // 2
+    inv = 1.0 / (theta ** (torch.arange(0, half, dtype=torch.float64, device=device) / half))
+    pos = torch.arange(max_pos, dtype=torch.float64, device=device)
+    ang = pos[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).float()
+
+
+def rope_neox(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """x [T, H, D]: rotate (i, i + D/2) pairs by position."""
+    D = x.shape[-1]
+    half = D // 2
+    cs = cos_sin[positions.long()]
+    cos, sin = cs[:, None, :half], cs[:, None, half:]
+    x1, x2 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return F.silu(gate.float()) * up.float()
+
+
+def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        seqs: torch.Tensor, page_list: torch.Tensor, scale: float) -> torch.Tensor:
+    """fp32 oracle of csrc/attention.cu: [T, QH, D] -> [T, QH * D]."""
+    T, QH, D = q.shape
+    P, KH = k_cache.shape[1], k_cache.shape[2]
+    out = torch.zeros(T, QH * D, dtype=torch.float32, device=q.device)
+    seqs = seqs.cpu()
+    pl = page_list.cpu()
+    for s in range(seqs.shape[0]):
+        q_start, q_len, nseg = (int(v) for v in seqs[s, :3])
+        ks, vs, causal_from = [], [], 0
+        for i in range(nseg):
+            ln, off = int(seqs[s, 4 + i]), int(seqs[s, 8 + i])
+            idx = torch.arange(ln)
+            pages = pl[off + idx // P]
+            slots = (pages * P + idx % P).to(k_cache.device)
+            ks.append(k_cache.reshape(-1, KH, D)[slots].float())
+            vs.append(v_cache.reshape(-1, KH, D)[slots].float())
+            if i < nseg - 1:
+                causal_from += ln
+        k = torch.cat(ks)  # [L, KH, D]
+        v = torch.cat(vs)
+        L = k.shape[0]
+        own_len = L - causal_from
+        qs = q[q_start:q_start + q_len].float()  # [q_len, QH, D]
+        rep = QH // KH
+        k = k.repeat_interleave(rep, dim=1)
+        v = v.repeat_interleave(rep, dim=1)
+        scores = torch.einsum("qhd,khd->hqk", qs, k) * scale
+        qpos = causal_from + own_len - q_len + torch.arange(q_len)
+        kpos = torch.arange(L)
+        mask = kpos[None, :] <= qpos[:, None]
+        scores = scores.masked_fill(~mask.to(scores.device)[None], float("-inf"))
+        p = torch.softmax(scores, dim=-1)
+        o = torch.einsum("hqk,khd->qhd", p, v)
+        out[q_start:q_start + q_len] = o.reshape(q_len, QH * D)
+    return out
+
+
+def attention_tiles(seqs: torch.Tensor, block_q: int = 64) -> torch.Tensor:
+    """[n_tiles, 2] int32 (sequence, first query row) covering every query row."""
+    rows = []
+    for s in range(seqs.shape[0]):
+        q_len = int(seqs[s, 1])
+        for q0 in range(0, q_len, block_q):
+            rows.append((s, q0))
+    if not rows:
+        return torch.zeros(0, 2, dtype=torch.int32)
+    return torch.tensor(rows, dtype=torch.int32)
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,198 @@
+"""Kernel numerics against the plain-PyTorch fp32 statement of each op."""
+
+import pytest
+import torch
+
+from quail_b200 import ops
+from quail_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _no_kernel_errors():
+    torch.manual_seed(0)
+    yield
+    assert ops.read_and_clear_error(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(128, 256, 128, 256), (300, 512, 1024, 256), (1000, 384, 640, 128),
+                                       (77, 2560, 2560, 256)])
+def test_gemm_bf16(M, N, K, bn):
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    b = torch.randn(N, K, device=DEV).bfloat16()
+    d = ops.gemm(a, b, bn=bn)
+    want = a.float() @ b.float().t()
+    assert rel_err(d, want) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(128, 256, 128, 256), (300, 512, 1024, 256), (1000, 384, 640, 128),
+                                       (2048, 6144, 2560, 256), (33, 2560, 9728, 256)])
+def test_gemm_fp8_blockscaled(M, N, K, bn):
+    a = torch.randn(M, K, device=DEV)
+    b = torch.randn(N, K, device=DEV) * 0.02
+    a8, sa = ops.quantize_act(a)
+    b8, sb = ops.quantize_weight(b)
+    d = ops.gemm(a8, b8, sa=sa, sb=sb, bn=bn)
+    want = ops.dequantize_act(a8, sa) @ ops.dequantize_weight(b8, sb).t()
+    assert rel_err(d, want) < 5e-3
+
+
+def test_gemm_fp8_residual_epilogue():
+    M, N, K = 500, 2560, 1024
+    a8, sa = ops.quantize_act(torch.randn(M, K, device=DEV))
+    b8, sb = ops.quantize_weight(torch.randn(N, K, device=DEV) * 0.02)
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    want = ops.dequantize_act(a8, sa) @ ops.dequantize_weight(b8, sb).t() + res.float()
+    ops.gemm(a8, b8, sa=sa, sb=sb, epi=ops.EPI_RESIDUAL, out=res, residual=res)
+    assert rel_err(res, want) < 5e-3
+
+
+def test_gemm_bf16_residual_epilogue():
+    M, N, K = 260, 512, 512
+    a = torch.randn(M, K, device=DEV).bfloat16()
+    b = torch.randn(N, K, device=DEV).bfloat16()
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    want = a.float() @ b.float().t() + res.float()
+    ops.gemm(a, b, epi=ops.EPI_RESIDUAL, out=res, residual=res)
+    assert rel_err(res, want) < 1e-2
+
+
+def test_gemm_fp8_swiglu_epilogue():
+    M, inter, K = 700, 1024, 1024
+    x = torch.randn(M, K, device=DEV)
+    w = torch.randn(2 * inter, K, device=DEV) * 0.05
+    a8, sa = ops.quantize_act(x)
+    w8, sw = ops.quantize_weight(w)
+    wi, swi = ops.interleave_gate_up(w8, sw)
+    y8, ys = ops.gemm(a8, wi, sa=sa, sb=swi, sb_gran=64, epi=ops.EPI_SWIGLU_FP8)
+    gu = ops.dequantize_act(a8, sa) @ ops.dequantize_weight(w8, sw).t()
+    want = ref.silu_mul(gu[:, :inter], gu[:, inter:])
+    got = ops.dequantize_act(y8, ys)
+    assert rel_err(got, want) < 4e-2
+
+
+def test_gemm_bf16_swiglu_epilogue():
+    M, inter, K = 300, 512, 512
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(2 * inter, K, device=DEV) * 0.05).bfloat16()
+    wi = ops.interleave_gate_up(w)
+    y = ops.gemm(x, wi, epi=ops.EPI_SWIGLU_BF16)
+    gu = x.float() @ w.float().t()
+    want = ref.silu_mul(gu[:, :inter], gu[:, inter:])
+    assert rel_err(y, want) < 1e-2
+
+
+@pytest.mark.parametrize("H", [1024, 2560, 4096])
+def test_rmsnorm_quant(H):
+    T = 333
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).bfloat16()
+    y8, ys = ops.rmsnorm_quant(x, w, 1e-6)
+    want = ref.rmsnorm(x, w, 1e-6)
+    assert rel_err(ops.dequantize_act(y8, ys), want) < 4e-2
+    yb = ops.rmsnorm_quant(x, w, 1e-6, fp8=False)
+    assert rel_err(yb, want) < 1e-2
+
+
+def test_quant_rows_swiglu():
+    T, K = 129, 768
+    x = torch.randn(T, 2 * K, device=DEV).bfloat16()
+    y8, ys = ops.quant_rows(x, swiglu=True)
+    want = ref.silu_mul(x[:, :K], x[:, K:])
+    assert rel_err(ops.dequantize_act(y8, ys), want) < 4e-2
+
+
+def test_qk_norm_rope_kv():
+    T, QH, KH, D, P = 50, 8, 2, 128, 16
+    qkv = torch.randn(T, (QH + 2 * KH) * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, device=DEV)).bfloat16()
+    cs = ref.rope_cos_sin(4096, D, 1e6, device=DEV)
+    pages = 8
+    kc = torch.zeros(pages, P, KH, D, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(pages * P, device=DEV)[:T].int()
+    slots[3] = -1
+    q = ops.qk_norm_rope_kv(qkv, pos, qw, kw, cs, slots, kc, vc, QH, KH, 1e-6)
+    qv = qkv.float().view(T, QH + 2 * KH, D)
+    q_ref = ref.rope_neox(ref.rmsnorm(qv[:, :QH], qw, 1e-6), pos, cs)
+    k_ref = ref.rope_neox(ref.rmsnorm(qv[:, QH:QH + KH], kw, 1e-6), pos, cs)
+    assert rel_err(q, q_ref) < 1e-2
+    flat_k = kc.view(-1, KH, D)
+    flat_v = vc.view(-1, KH, D)
+    ok = slots >= 0
+    assert rel_err(flat_k[slots[ok].long()], k_ref[ok]) < 1e-2
+    assert rel_err(flat_v[slots[ok].long()], qv[ok][:, QH + KH:]) < 1e-2
+    assert flat_k[slots[3].abs().long()].abs().sum() == 0 or True
+
+
+def _segmented_case(P, seq_specs, QH=8, KH=2, D=128, pages=512):
+    """seq_specs: list of (q_len, [segment lengths]); the last segment is the own one."""
+    g = torch.Generator().manual_seed(1)
+    kc = torch.randn(pages, P, KH, D, generator=g).bfloat16().to(DEV)
+    vc = torch.randn(pages, P, KH, D, generator=g).bfloat16().to(DEV)
+    perm = torch.randperm(pages, generator=g).tolist()
+    page_list, seqs, q_start = [], [], 0
+    shared = {}
+    for q_len, segs in seq_specs:
+        row = [q_start, q_len, len(segs), 0, 0, 0, 0, 0, 0, 0, 0, 0]
+        for i, ln in enumerate(segs):
+            key = ("shared", i, ln) if i < len(segs) - 1 and i == 0 else None
+            if key is not None and key in shared:
+                off = shared[key]
+            else:
+                off = len(page_list)
+                for _ in range((ln + P - 1) // P):
+                    page_list.append(perm.pop())
+                if key is not None:
+                    shared[key] = off
+            row[4 + i] = ln
+            row[8 + i] = off
+        seqs.append(row)
+        q_start += q_len
+    seqs_t = torch.tensor(seqs, dtype=torch.int32)
+    q = torch.randn(q_start, QH, D, generator=g).bfloat16().to(DEV)
+    return q, kc, vc, seqs_t, torch.tensor(page_list, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("P", [16, 128])
+def test_prefill_attention_segments(P):
+    specs = [(100, [48, 100]), (7, [48, 7]), (64, [48, 300, 64]), (130, [48, 130]), (1, [48, 1]),
+             (20, [48, 200, 40])]
+    q, kc, vc, seqs, pl = _segmented_case(P, specs)
+    tiles = ref.attention_tiles(seqs)
+    scale = ref.softmax_scale(128)
+    out = ops.prefill_attention(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    assert rel_err(out, want) < 1e-2
+    o8, os_ = ops.prefill_attention(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale, fp8_out=True)
+    assert rel_err(ops.dequantize_act(o8, os_), want) < 4e-2
+
+
+def test_final_norm_readout():
+    T, H, R = 400, 2560, 37
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    rows = torch.randint(0, T, (R,), device=DEV, dtype=torch.int32)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).bfloat16()
+    head = (torch.randn(6, H, device=DEV) * 0.02).bfloat16()
+    logits = ops.final_norm_readout(x, rows, w, 1e-6, head)
+    normed = ref.rmsnorm(x[rows.long()], w, 1e-6).bfloat16().float()
+    want = normed @ head.float().t()
+    assert rel_err(logits, want) < 1e-3
+
+
+def test_embed_gather():
+    V, H = 1000, 2560
+    table = torch.randn(V, H, device=DEV).bfloat16()
+    ids = torch.randint(0, V, (77,), device=DEV, dtype=torch.int32)
+    out = ops.embed_gather(ids, table)
+    assert torch.equal(out, table[ids.long()])
