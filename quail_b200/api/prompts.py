@@ -1,0 +1,172 @@
+"""Prompt text of each AI function call, in the model's chat format.
+
+The prompt layout is an interface the answers depend on token for token, so
+its strings are the same as the reference's
+(crates/quail-planner/src/prompts.rs:16-31, the spec's turn_prefix /
+turn_suffix in quail/specs/data/models/qwen3-4b-fp8.toml):
+
+  turn_prefix + "DOCUMENT:\\n" + <document> +
+  "\\n\\n" + "Evaluate TRUE or FALSE for the following question: " + <question> + "\\nANSWER:" +
+  turn_suffix
+
+A `PROMPT('<instruction> {0}', col)` template puts the document at {0}; the
+text before the placeholder becomes the question asked after it (the
+reference's "frame" move, prompts.rs:290-314).
+"""
+
+from __future__ import annotations
+
+import re
+from dataclasses import dataclass, field
+
+SHARED_PRE = "DOCUMENT:\n"
+JOIN_QUESTION_SEP = "\n\n"
+TASK_INSTRUCTION = "Evaluate TRUE or FALSE for the following question: "
+ANSWER_CUE = "\nANSWER:"
+CLASSIFY_INSTRUCTION = "Answer with exactly one of the categories below for the following question: "
+CATEGORIES_HEADER = "\n\nCategories:"
+CHOICE_QUESTION = "Which option best fits the context?"
+EXTRACT_QUESTION_LABEL = "\n\nQuestion: "
+EXTRACT_INSTRUCTION = ("Copy the words that answer the question from the document. Copy them exactly. "
+                       "Use the fewest words that answer it. If the document does not answer the question, "
+                       "leave the phrase empty.")
+EXTRACT_FORMAT = "Answer in this format:"
+EXTRACT_PHRASE_FORMAT = "Phrase: <copied words>"
+EXTRACT_PHRASE_CUE = "Phrase:"
+
+QWEN3_TURN_PREFIX = "<|im_start|>system\nYou are an expert at text analysis<|im_end|>\n<|im_start|>user\n"
+QWEN3_TURN_SUFFIX = "<|im_end|>\n<|im_start|>assistant\n<think>\n\n</think>\n\n"
+
+# answer spellings read for AI.IF / AI.SCORE (the max over spellings is the side's logit)
+TRUE_SPELLINGS = ("TRUE", " TRUE", "True", " True")
+FALSE_SPELLINGS = ("FALSE", " FALSE", "False", " False")
+
+_PLACEHOLDER = re.compile(r"\{(\d+)\}")
+
+
+class PromptError(ValueError):
+    pass
+
+
+def placeholders(template: str) -> list[int]:
+    return [int(m.group(1)) for m in _PLACEHOLDER.finditer(template)]
+
+
+def check_placeholders(template: str, num_args: int) -> None:
+    used = sorted(set(placeholders(template)))
+    if num_args == 0:
+        if used:
+            raise PromptError(f"template uses placeholders {used} but no argument is given")
+        return
+    want = list(range(num_args))
+    if used != want:
+        raise PromptError(f"template placeholders {used} must be exactly {{0}}..{{{num_args - 1}}}")
+
+
+@dataclass(frozen=True)
+class Turn:
+    prefix: str = QWEN3_TURN_PREFIX
+    suffix: str = QWEN3_TURN_SUFFIX
+
+
+@dataclass
+class BoundPrompt:
+    """A call's prompt split around the document.
+
+    preamble: text before the document (turn prefix + "DOCUMENT:\\n"), shared
+    by every row; tail: text after the document (question block + answer cue +
+    turn suffix); question: the question text alone.
+    """
+
+    kind: str
+    template: str
+    preamble: str
+    tail: str
+    question: str
+    labels: list = field(default_factory=list)
+    descriptions: list = field(default_factory=list)
+
+    def text(self, document: str) -> str:
+        return self.preamble + document + self.tail
+
+
+def split_frame(template: str) -> tuple[str, str]:
+    """(question, rest after the document placeholder)."""
+    i = template.find("{")
+    if i < 0:
+        return template.strip(), ""
+    pre, tail = template[:i], template[i:]
+    m = re.match(r"\{\d+\}", tail)
+    if not m:
+        raise PromptError("template text before the first placeholder must not contain a stray brace")
+    question = pre.strip()
+    rest = tail[m.end():]
+    return question, rest
+
+
+def bind_prompt(template: str, num_args: int = 1, turn: Turn = Turn()) -> BoundPrompt:
+    """AI.IF / AI_FILTER prompt of a one-document template."""
+    check_placeholders(template, num_args)
+    if num_args > 1:
+        raise PromptError("This filter must read a materialized document expression.")
+    question, rest = split_frame(template)
+    rest_q = rest.strip()
+    if question and rest_q:
+        question = f"{question}\n\n{rest_q}"
+    elif rest_q:
+        question = rest_q
+    tail = JOIN_QUESTION_SEP + TASK_INSTRUCTION + question + ANSWER_CUE + turn.suffix
+    return BoundPrompt(kind="filter", template=template, preamble=turn.prefix + SHARED_PRE, tail=tail,
+                       question=question)
+
+
+def bind_score_prompt(template: str, num_args: int = 1, turn: Turn = Turn()) -> BoundPrompt:
+    p = bind_prompt(template, num_args, turn)
+    p.kind = "score"
+    return p
+
+
+def render_categories(labels: list[str], descriptions: list[str] | None = None) -> str:
+    lines = []
+    for i, label in enumerate(labels):
+        d = descriptions[i] if descriptions and i < len(descriptions) and descriptions[i] else ""
+        lines.append(f"- {label}: {d}" if d else f"- {label}")
+    return CATEGORIES_HEADER + "\n" + "\n".join(lines)
+
+
+def bind_classify_prompt(template: str | None, labels: list[str], descriptions: list[str] | None = None,
+                         task_description: str = "", turn: Turn = Turn()) -> BoundPrompt:
+    """AI.CLASSIFY prompt: the categories follow the question; the answer is a label."""
+    if template:
+        question, rest = split_frame(template)
+        question = (question + ("\n\n" + rest.strip() if rest.strip() else "")).strip()
+    else:
+        question = ""
+    if not question:
+        question = task_description or CHOICE_QUESTION
+    tail = (JOIN_QUESTION_SEP + CLASSIFY_INSTRUCTION + question + render_categories(labels, descriptions)
+            + ANSWER_CUE + turn.suffix)
+    return BoundPrompt(kind="classify", template=template or "", preamble=turn.prefix + SHARED_PRE, tail=tail,
+                       question=question, labels=list(labels), descriptions=list(descriptions or []))
+
+
+def bind_map_prompt(instruction: str, turn: Turn = Turn()) -> BoundPrompt:
+    """AI.MAP: the document, then the instruction; the answer is free text."""
+    tail = JOIN_QUESTION_SEP + instruction + turn.suffix
+    return BoundPrompt(kind="map", template="{0}\n\n" + instruction, preamble=turn.prefix, tail=tail,
+                       question=instruction)
+
+
+def bind_extract_prompt(question: str, turn: Turn = Turn()) -> BoundPrompt:
+    tail = (EXTRACT_QUESTION_LABEL + question + "\n\n" + EXTRACT_INSTRUCTION + "\n\n" + EXTRACT_FORMAT + "\n"
+            + EXTRACT_PHRASE_FORMAT + turn.suffix + EXTRACT_PHRASE_CUE)
+    return BoundPrompt(kind="extract", template="{0}", preamble=turn.prefix + SHARED_PRE, tail=tail,
+                       question=question)
+
+
+def bind_join_prompt(template: str, turn: Turn = Turn()) -> BoundPrompt:
+    """Two-document AI.IF (a join): {0} and {1} become DOCUMENT 1 / DOCUMENT 2."""
+    check_placeholders(template, 2)
+    question = _PLACEHOLDER.sub("", template).strip()
+    tail = JOIN_QUESTION_SEP + TASK_INSTRUCTION + question + ANSWER_CUE + turn.suffix
+    return BoundPrompt(kind="join", template=template, preamble=turn.prefix, tail=tail, question=question)

@@ -38,7 +38,7 @@ class PagePool:
         self.owned: dict = {}          # key -> page ids it writes
         self.tokens: dict = {}         # key -> tokens resident
         self.holds = np.zeros(num_pages, dtype=np.int32)
-        self.borrows: dict = {}        # key -> list of parent keys it holds
+        self.borrows: dict = {}        # key -> page lists it holds of the keys it reads
         self.retained: OrderedDict = OrderedDict()  # key -> None, oldest first
 
     # ------------------------------------------------------------ queries
@@ -87,8 +87,9 @@ class PagePool:
         """`reader` reads `parent`'s pages: hold them until the reader is freed."""
         if parent not in self.owned:
             raise KeyError(f"borrow parent {parent!r} is not resident")
-        self.holds[self.owned[parent]] += 1
-        self.borrows.setdefault(reader, []).append(parent)
+        pages = list(self.owned[parent])
+        self.holds[pages] += 1
+        self.borrows.setdefault(reader, []).append(pages)
 
     # ------------------------------------------------------------ release
     def _drop(self, pages) -> None:
@@ -101,9 +102,8 @@ class PagePool:
 
     def free_key(self, key) -> None:
         """Release a key's own pages and the holds it took on borrowed parents."""
-        for parent in self.borrows.pop(key, []):
-            if parent in self.owned:
-                self._drop(self.owned[parent])
+        for pages in self.borrows.pop(key, []):
+            self._drop(pages)
         pages = self.owned.pop(key, None)
         self.tokens.pop(key, None)
         self.retained.pop(key, None)
@@ -128,10 +128,9 @@ class PagePool:
         expect = np.zeros(self.num_pages, dtype=np.int32)
         for pages in self.owned.values():
             expect[pages] += 1
-        for parents in self.borrows.values():
-            for parent in parents:
-                if parent in self.owned:
-                    expect[self.owned[parent]] += 1
+        for held in self.borrows.values():
+            for pages in held:
+                expect[pages] += 1
         assert np.array_equal(expect, self.holds), "hold counts drifted"
         free = set(self.free)
         assert len(free) == len(self.free), "page freed twice"

@@ -52,6 +52,7 @@ class Chunk:
     readout_tags: list = field(default_factory=list)
     num_seqs: int = 0
     host: dict | None = None   # numpy copies (tests, CPU reference)
+    upload_bytes: int = 0
 
 
 class ChunkPacker:
@@ -122,24 +123,34 @@ class ChunkPacker:
                 "page_list": pl, "final_rows": fr}
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
-                     final_rows=views[6], readout_tags=tags, num_seqs=len(specs), host=host)
+                     final_rows=views[6], readout_tags=tags, num_seqs=len(specs), host=host,
+                     upload_bytes=int(flat.nbytes))
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:
         src = torch.from_numpy(flat)
         if self.device.type != "cuda":
             return src.clone()
-        if self.pin:
-            if self._staging is None or self._staging.numel() < flat.size:
-                self._staging = torch.empty(max(flat.size, 1 << 16) * 2, dtype=torch.int32, pin_memory=True)
-            # the staging buffer is reused: wait for the previous copy out of it
-            if getattr(self, "_copy_done", None) is not None:
-                self._copy_done.synchronize()
-            stage = self._staging[:flat.size]
-            stage.copy_(src)
-            out = torch.empty(flat.size, dtype=torch.int32, device=self.device)
-            out.copy_(stage, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record()
-            self._copy_done = ev
-            return out
-        return src.to(self.device)
+        if not self.pin:
+            return src.to(self.device)
+        # two pinned staging buffers, used in turn: a buffer is refilled only
+        # after the copy out of it two chunks ago has finished
+        if self._staging is None:
+            self._staging = [None, None]
+            self._copy_done = [None, None]
+            self._turn = 0
+        i = self._turn
+        self._turn ^= 1
+        buf = self._staging[i]
+        if self._copy_done[i] is not None:
+            self._copy_done[i].synchronize()
+        if buf is None or buf.numel() < flat.size:
+            buf = torch.empty(max(flat.size, 1 << 16) * 2, dtype=torch.int32, pin_memory=True)
+            self._staging[i] = buf
+        stage = buf[:flat.size]
+        stage.copy_(src)
+        out = torch.empty(flat.size, dtype=torch.int32, device=self.device)
+        out.copy_(stage, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._copy_done[i] = ev
+        return out

@@ -1,0 +1,221 @@
+"""The per-GPU prefill scheduler: admission, chunk packing, forward, readout.
+
+Work arrives as `Task`s: a sequence of new tokens that writes one arena key
+and reads earlier keys (the shared instruction prefix, a document another
+task wrote). The executor packs the tasks at the head of the queue into a
+chunk of at most `chunk_tokens` new tokens, splitting a task that does not
+fit into prefill pieces (chunked prefill over its own pages), and admits a
+task only when
+
+  - every key it reads was fully written by an already launched chunk
+    (stream order then guarantees the KV is there), and
+  - its own pages fit in the free pool (after evicting retained keys).
+
+While the GPU runs chunk k the host packs and launches chunk k+1, then
+collects chunk k's readout (one pinned D2H copy + an event) and hands each
+readout row to its task's `on_done`, which may submit follow-up tasks (a
+CLASSIFY on the rows an AI.IF kept reads the same document pages).
+
+Reference behavior: quail/backends/quail/executor/stage_executor.py
+(StageExecutor.run, _run_one, forward_chunk), admission.py (next_chunk,
+prefill pieces, Borrowing) and readout.py (async readouts drained in order).
+"""
+
+from __future__ import annotations
+
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Callable
+
+import numpy as np
+import torch
+
+from quail_b200.engine.arena import ArenaFullError
+from quail_b200.engine.chunk import ChunkPacker, SeqSpec
+
+
+class OversizedDocumentError(ArenaFullError):
+    """A single task needs more pages than the whole arena has."""
+
+
+@dataclass
+class Task:
+    key: object
+    tokens: np.ndarray
+    pos_start: int
+    reads: list = field(default_factory=list)       # [(key, tokens)]
+    readout: bool = False
+    on_done: Callable | None = None                  # on_done(task, logits_row | None)
+    free_after: bool = True
+    own_prefix: int = 0                              # own tokens already resident (continuation)
+    done: int = 0                                    # new tokens already launched
+    tag: object = None
+
+    @property
+    def remaining(self) -> int:
+        return len(self.tokens) - self.done
+
+
+@dataclass
+class ExecutorStats:
+    passes: int = 0
+    tokens: int = 0
+    readouts: int = 0
+    gpu_ms: float = 0.0
+    pass_tokens: list = field(default_factory=list)
+    pass_rows: list = field(default_factory=list)
+    h2d_bytes: int = 0
+    d2h_bytes: int = 0
+    wall_s: float = 0.0
+
+
+class StageExecutor:
+    def __init__(self, model, arena, chunk_tokens: int, *, min_piece: int = 64, gpu_timing: bool = False,
+                 max_seqs: int | None = None):
+        self.model = model
+        self.arena = arena
+        self.pool = arena.pool
+        self.chunk_tokens = chunk_tokens
+        self.min_piece = min_piece
+        self.max_seqs = max_seqs
+        self.device = arena.device
+        self.packer = ChunkPacker(self.pool, self.device)
+        self.queue: deque[Task] = deque()
+        self.written: dict = {}     # key -> tokens written by launched chunks
+        self.stats = ExecutorStats()
+        self.gpu_timing = gpu_timing and self.device.type == "cuda"
+        self._inflight: deque = deque()
+
+    # ------------------------------------------------------------ submission
+    def submit(self, task: Task) -> None:
+        need = self.pool.pages_needed(task.own_prefix + len(task.tokens))
+        if need > self.pool.num_pages:
+            raise OversizedDocumentError(
+                f"task {task.key!r} needs {need} pages; the arena has {self.pool.num_pages}")
+        self.queue.append(task)
+
+    def free(self, key) -> None:
+        self.pool.free_key(key)
+        self.written.pop(key, None)
+
+    # ------------------------------------------------------------ admission
+    def _readable(self, task: Task) -> bool:
+        return all(self.written.get(k, -1) >= n for k, n in task.reads)
+
+    def _admit(self) -> list[SeqSpec]:
+        room = self.chunk_tokens
+        specs: list[SeqSpec] = []
+        deferred: list[Task] = []
+        scanned = 0
+        while self.queue and room > 0 and scanned < 4096:
+            if self.max_seqs is not None and len(specs) >= self.max_seqs:
+                break
+            task = self.queue.popleft()
+            scanned += 1
+            if not self._readable(task):
+                deferred.append(task)
+                continue
+            if not self.pool.resident(task.key):
+                total = task.own_prefix + len(task.tokens)
+                pages = self.pool.alloc(task.key, total)
+                if pages is None:
+                    self.pool.evict_retained(self.pool.pages_needed(total))
+                    pages = self.pool.alloc(task.key, total)
+                if pages is None:
+                    deferred.append(task)
+                    break  # keep FIFO order under memory pressure
+                for rk, _ in task.reads:
+                    self.pool.borrow(task.key, rk)
+            piece = min(task.remaining, room)
+            if piece < task.remaining and piece < self.min_piece and specs:
+                deferred.append(task)
+                break
+            last = piece == task.remaining
+            specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix + task.done,
+                                 tokens=task.tokens[task.done:task.done + piece],
+                                 pos_start=task.pos_start + task.done, readout=task.readout and last, tag=task))
+            task.done += piece
+            room -= piece
+            if not last:
+                deferred.append(task)  # the rest goes in a later chunk
+                break
+        # deferred tasks go back to the head in their original order
+        for t in reversed(deferred):
+            self.queue.appendleft(t)
+        return specs
+
+    # ------------------------------------------------------------ run
+    def _launch(self, specs: list[SeqSpec]):
+        chunk = self.packer.pack(specs)
+        ev0 = ev1 = None
+        if self.gpu_timing:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        logits = self.model.forward_chunk(chunk, self.arena)
+        if self.gpu_timing:
+            ev1.record()
+        for s in specs:
+            self.written[s.own_key] = s.own_start + len(s.tokens)
+        if self.device.type == "cuda" and logits is not None:
+            host = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+            host.copy_(logits, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record()
+        else:
+            host, done = logits, None
+        self.stats.passes += 1
+        self.stats.tokens += chunk.num_tokens
+        self.stats.pass_tokens.append(chunk.num_tokens)
+        self.stats.pass_rows.append(sum(1 for s in specs if s.readout))
+        self.stats.h2d_bytes += chunk.upload_bytes
+        if logits is not None:
+            self.stats.d2h_bytes += logits.numel() * logits.element_size()
+        self._inflight.append((specs, chunk, host, done, ev0, ev1))
+
+    def _collect_one(self):
+        specs, chunk, host, done, ev0, ev1 = self._inflight.popleft()
+        if done is not None:
+            done.synchronize()
+        if ev0 is not None:
+            self.stats.gpu_ms += ev0.elapsed_time(ev1)
+        r = 0
+        for s in specs:
+            task: Task = s.tag
+            last = s.own_start + len(s.tokens) == task.own_prefix + len(task.tokens)
+            row = None
+            if s.readout:
+                row = host[r]
+                r += 1
+                self.stats.readouts += 1
+            if last:
+                if task.on_done:
+                    task.on_done(task, row)
+                if task.free_after:
+                    self.free(task.key)
+
+    def step(self) -> bool:
+        """Launch one chunk if any task is admissible; collect finished chunks."""
+        specs = self._admit()
+        if specs:
+            self._launch(specs)
+            # keep one chunk queued behind the running one
+            while len(self._inflight) > 1:
+                self._collect_one()
+            return True
+        if self._inflight:
+            self._collect_one()
+            return True
+        return False
+
+    def run(self) -> ExecutorStats:
+        t0 = time.perf_counter()
+        while self.queue or self._inflight:
+            if not self.step():
+                if self.queue:
+                    raise ArenaFullError(
+                        f"{len(self.queue)} tasks cannot be admitted: {self.pool.free_pages} free pages; "
+                        f"head {self.queue[0].key!r} reads {self.queue[0].reads}")
+                break
+        self.stats.wall_s += time.perf_counter() - t0
+        return self.stats

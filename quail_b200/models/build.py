@@ -1,0 +1,38 @@
+"""Building a model replica on a GPU from a checkpoint or from random init."""
+
+from __future__ import annotations
+
+import torch
+
+from quail_b200.models.config import DecoderConfig
+from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights
+from quail_b200.models.weights import iter_random_layer
+
+# answer-row token ids used by the synthetic configs (TRUE spellings, then FALSE)
+SYNTHETIC_TRUE_IDS = (20611, 3007, 2514, 3007 + 1)
+SYNTHETIC_FALSE_IDS = (30351, 4049, 4049 + 1, 30351 + 1)
+
+
+def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Random-init weights in checkpoint format, generated layer by layer on `device`."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out: dict[str, torch.Tensor] = {}
+    out["model.embed_tokens.weight"] = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device)
+                                        * cfg.init_std).bfloat16()
+    for i in range(cfg.layers):
+        out.update(iter_random_layer(cfg, i, gen, device=device, dtype=torch.bfloat16))
+    out["model.norm.weight"] = torch.ones(cfg.hidden, device=device, dtype=torch.bfloat16)
+    if not cfg.tied_head:
+        out["lm_head.weight"] = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device)
+                                 * cfg.init_std).bfloat16()
+    return out
+
+
+def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
+                   answer_ids=SYNTHETIC_TRUE_IDS + SYNTHETIC_FALSE_IDS):
+    if ckpt is None:
+        ckpt = random_checkpoint_on(cfg, device, seed)
+    weights = Qwen3Weights(cfg, ckpt, device, head_rows=answer_ids)
+    del ckpt
+    torch.cuda.empty_cache() if torch.cuda.is_available() else None
+    return Qwen3Pipeline(cfg, weights)

@@ -17,6 +17,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     final_norm_readout,
     gemm,
     kernels_available,
+    launch_count,
     native,
     prefill_attention,
     qk_norm_rope_kv,

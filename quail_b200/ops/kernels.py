@@ -13,6 +13,18 @@ try:
 except Exception as exc:  # noqa: BLE001 - surfaced by native()
     _IMPORT_ERROR = exc
 
+# kernels launched through these wrappers (bench.py reports the count per timed region)
+_LAUNCHES = [0]
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]
+
+
+def _count(n: int = 1) -> None:
+    _LAUNCHES[0] += n
+
+
 EPI_BF16 = 0
 EPI_RESIDUAL = 1
 EPI_SWIGLU_FP8 = 2
@@ -52,11 +64,13 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
             out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
         if out_scale is None:
             out_scale = torch.empty(N // 256, M, dtype=torch.float32, device=a.device)
+        _count()
         C.gemm(a, b, sa, sb, sb_gran, epi, out, out_scale, None, bn)
         return out, out_scale
     if out is None:
         width = N // 2 if epi == EPI_SWIGLU_BF16 else N
         out = torch.empty(M, width, dtype=torch.bfloat16, device=a.device)
+    _count()
     C.gemm(a, b, sa, sb, sb_gran, epi, out, None, residual, bn)
     return out
 
@@ -64,6 +78,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
 def embed_gather(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=torch.bfloat16, device=ids.device)
+    _count()
     native().embed_gather(ids, table, out)
     return out
 
@@ -78,10 +93,12 @@ def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, *, fp8: bool = T
             out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
         if out_scale is None:
             out_scale = torch.empty(H // 128, T, dtype=torch.float32, device=x.device)
+        _count()
         native().rmsnorm_quant(x, w, eps, out, out_scale, None, T)
         return out, out_scale
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    _count()
     native().rmsnorm_quant(x, w, eps, None, None, out, T)
     return out
 
@@ -93,9 +110,11 @@ def quant_rows(x: torch.Tensor, *, swiglu: bool = False, fp8: bool = True, rows:
     if fp8:
         y = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=x.device)
         s = torch.empty(K // 128, T, dtype=torch.float32, device=x.device)
+        _count()
         native().quant_rows(x, swiglu, y, s, None, T)
         return y, s
     y = torch.empty(T, K, dtype=torch.bfloat16, device=x.device)
+    _count()
     native().quant_rows(x, swiglu, None, None, y, T)
     return y
 
@@ -107,6 +126,7 @@ def qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, k_cache,
     T = qkv.shape[0] if rows is None else rows
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, 128, dtype=torch.bfloat16, device=qkv.device)
+    _count()
     native().qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, q_out, k_cache,
                              v_cache, num_q_heads, num_kv_heads, eps, norm_qk, T)
     return q_out
@@ -121,11 +141,13 @@ def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale
             out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
         if out_scale is None:
             out_scale = torch.empty(QH, T, dtype=torch.float32, device=q.device)
+        _count()
         native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale,
                                    out, out_scale)
         return out, out_scale
     if out is None:
         out = torch.empty(T, QH * 128, dtype=torch.bfloat16, device=q.device)
+    _count()
     native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out, None)
     return out
 
@@ -134,6 +156,7 @@ def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, n
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
     if logits is None:
         logits = torch.empty(rows.numel(), head_rows.shape[0], dtype=torch.float32, device=x.device)
+    _count()
     native().final_norm_readout(x, rows, norm_w, eps, head_rows, logits, normed)
     return logits
 

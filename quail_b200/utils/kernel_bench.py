@@ -1,0 +1,103 @@
+"""Device-timed microbenchmarks of the hot kernels at the model shapes.
+
+    python -m quail_b200.utils.kernel_bench [--model qwen3-4b-fp8] [--tokens 16384]
+
+Each case is timed with CUDA events on the launching stream after warm-up,
+with an L2 flush (a 512 MiB write) before every timed launch, and reported
+as achieved TFLOP/s or GB/s next to the library bars the reference would
+call on the same GPU (cuBLAS bf16 matmul, cuBLASLt fp8 `_scaled_mm`).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from quail_b200 import ops
+from quail_b200.models.config import MODEL_CONFIGS
+
+
+def _timeit(fn, iters=10, warmup=3, flush=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def gemm_cases(cfg, T):
+    H = cfg.hidden
+    return [("qkv", T, cfg.qkv_dim, H), ("o_proj", T, H, cfg.q_dim), ("gate_up", T, 2 * cfg.intermediate, H),
+            ("down", T, H, cfg.intermediate)]
+
+
+def run(model: str, T: int, iters: int = 10) -> list[dict]:
+    cfg = MODEL_CONFIGS[model]
+    dev = "cuda"
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    out = []
+    for name, M, N, K in gemm_cases(cfg, T):
+        flops = 2.0 * M * N * K
+        a = torch.randn(M, K, device=dev)
+        b = torch.randn(N, K, device=dev) * 0.02
+        row = {"case": name, "M": M, "N": N, "K": K}
+        if cfg.fp8:
+            a8, sa = ops.quantize_act(a)
+            b8, sb = ops.quantize_weight(b)
+            epi = ops.EPI_BF16
+            if name == "gate_up":
+                b8, sb = ops.interleave_gate_up(b8, sb)
+                ms = _timeit(lambda: ops.gemm(a8, b8, sa=sa, sb=sb, sb_gran=64, epi=ops.EPI_SWIGLU_FP8),
+                             iters, flush=flush)
+            else:
+                dout = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                ms = _timeit(lambda: ops.gemm(a8, b8, sa=sa, sb=sb, epi=epi, out=dout), iters, flush=flush)
+            row["ours_ms"] = ms
+            row["ours_tflops"] = flops / ms / 1e9
+            try:
+                one = torch.ones((), device=dev)
+                bt = b8.t()
+                ms_l = _timeit(lambda: torch._scaled_mm(a8, bt, scale_a=one, scale_b=one, out_dtype=torch.bfloat16),
+                               iters, flush=flush)
+                row["cublaslt_fp8_tensorwise_ms"] = ms_l
+                row["cublaslt_fp8_tensorwise_tflops"] = flops / ms_l / 1e9
+            except Exception as exc:  # noqa: BLE001
+                row["cublaslt_fp8_error"] = str(exc)[:120]
+        ab, bb = a.bfloat16(), b.bfloat16()
+        ms_c = _timeit(lambda: ab @ bb.t(), iters, flush=flush)
+        row["cublas_bf16_ms"] = ms_c
+        row["cublas_bf16_tflops"] = flops / ms_c / 1e9
+        if not cfg.fp8:
+            ms = _timeit(lambda: ops.gemm(ab, bb), iters, flush=flush)
+            row["ours_ms"] = ms
+            row["ours_tflops"] = flops / ms / 1e9
+        out.append(row)
+        del a, b
+    assert ops.read_and_clear_error(0) == 0
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen3-4b-fp8")
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    for row in run(args.model, args.tokens, args.iters):
+        print(json.dumps(row))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+"""The arena, packer and stage executor on CPU with the fp32 model.
+
+The check that matters: packing rows into chunks (shared prefix read through
+its pages, documents split into prefill pieces, follow-up questions reading a
+document's pages) gives the same readout logits as running every prompt alone
+through the plain causal model.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from quail_b200.engine.arena import KVArena, PagePool
+from quail_b200.engine.region import Call, RegionRun
+from quail_b200.engine.stage_executor import StageExecutor, Task
+from quail_b200.models.config import QWEN3_TINY
+from quail_b200.models.qwen3 import Qwen3Reference
+from quail_b200.models.weights import random_checkpoint
+from quail_b200.ops import reference as ref
+
+
+def _model(cfg=QWEN3_TINY, answer_ids=(11, 12, 13, 14)):
+    ckpt = random_checkpoint(cfg.with_(vocab=1000, max_position=4096), seed=3, dtype=torch.float32)
+    cfg = cfg.with_(vocab=1000, max_position=4096)
+    return cfg, Qwen3Reference(cfg, ckpt, head_rows=answer_ids)
+
+
+def _plain_logits(model, cfg, tokens):
+    """Logits of the last token of one prompt, no arena, plain causal attention."""
+    T = len(tokens)
+    h = model.embed[torch.as_tensor(tokens).long()]
+    pos = torch.arange(T)
+    QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+    for L in model.layers:
+        x = ref.rmsnorm(h, L["ln1"], cfg.rms_eps)
+        q = ref.rope_neox(ref.rmsnorm((x @ L["wq"].t()).view(T, QH, D), L["qn"], cfg.rms_eps), pos, model.cos_sin)
+        k = ref.rope_neox(ref.rmsnorm((x @ L["wk"].t()).view(T, KH, D), L["kn"], cfg.rms_eps), pos, model.cos_sin)
+        v = (x @ L["wv"].t()).view(T, KH, D)
+        k = k.repeat_interleave(QH // KH, 1)
+        v = v.repeat_interleave(QH // KH, 1)
+        o = torch.nn.functional.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1),
+                                                             is_causal=True, scale=model.scale)
+        h = h + o.transpose(0, 1).reshape(T, -1) @ L["wo"].t()
+        x = ref.rmsnorm(h, L["ln2"], cfg.rms_eps)
+        h = h + ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t()
+    n = ref.rmsnorm(h[-1:], model.final_norm, cfg.rms_eps)
+    return (n @ model.answer_rows.t())[0]
+
+
+def test_page_pool_borrow_and_free():
+    pool = PagePool(10, 4)
+    assert pool.alloc("a", 9) == [0, 1, 2]
+    assert pool.alloc("b", 4) == [3]
+    pool.borrow("b", "a")
+    pool.free_key("a")
+    assert pool.free_pages == 6  # a's pages still held by b
+    pool.check()
+    pool.free_key("b")
+    assert pool.free_pages == 10
+    pool.check()
+    assert pool.alloc("c", 41) is None
+
+
+def test_retained_eviction():
+    pool = PagePool(4, 4)
+    pool.alloc("a", 8)
+    pool.retain("a")
+    pool.alloc("b", 4)
+    pool.retain("b")
+    assert pool.evict_retained(3) == ["a"]
+    assert pool.free_pages == 3
+    pool.check()
+
+
+@pytest.mark.parametrize("chunk_tokens,page_tokens", [(64, 16), (1000, 128), (37, 8)])
+def test_packed_chunks_match_plain_prompts(chunk_tokens, page_tokens):
+    cfg, model = _model()
+    arena = KVArena(cfg.layers, 64, page_tokens, cfg.num_kv_heads, cfg.head_dim, device="cpu",
+                    dtype=torch.float32)
+    ex = StageExecutor(model, arena, chunk_tokens, min_piece=4)
+    rng = np.random.default_rng(0)
+    prefix = rng.integers(0, 1000, 10).astype(np.int32)
+    docs = [rng.integers(0, 1000, n).astype(np.int32) for n in (5, 40, 17, 90, 3)]
+    suffix = rng.integers(0, 1000, 6).astype(np.int32)
+    got = {}
+    ex.submit(Task(key="prefix", tokens=prefix, pos_start=0, free_after=False))
+    for i, d in enumerate(docs):
+        toks = np.concatenate([d, suffix])
+        ex.submit(Task(key=("d", i), tokens=toks, pos_start=len(prefix), reads=[("prefix", len(prefix))],
+                       readout=True, on_done=lambda t, row, i=i: got.__setitem__(i, row.clone())))
+    ex.run()
+    ex.free("prefix")
+    assert arena.pool.free_pages == arena.num_pages
+    for i, d in enumerate(docs):
+        want = _plain_logits(model, cfg, np.concatenate([prefix, d, suffix]))
+        torch.testing.assert_close(got[i], want, rtol=1e-4, atol=1e-4)
+
+
+def test_region_followup_questions_read_document_pages():
+    cfg, model = _model()
+    arena = KVArena(cfg.layers, 128, 16, cfg.num_kv_heads, cfg.head_dim, device="cpu", dtype=torch.float32)
+    ex = StageExecutor(model, arena, 80, min_piece=4)
+    rng = np.random.default_rng(1)
+    prefix = rng.integers(0, 1000, 12).astype(np.int32)
+    docs = [rng.integers(0, 1000, n).astype(np.int32) for n in (30, 7, 66)]
+    s1 = rng.integers(0, 1000, 5).astype(np.int32)
+    s2 = rng.integers(0, 1000, 9).astype(np.int32)
+    calls = [Call(kind="score", suffix=s1, true_cols=[0, 1], false_cols=[2, 3], name="a"),
+             Call(kind="score", suffix=s2, true_cols=[0], false_cols=[2], name="b")]
+    res = RegionRun(ex, prefix, docs, calls).run()
+    assert arena.pool.free_pages == arena.num_pages
+    arena.pool.check()
+    for r, d in enumerate(docs):
+        la = _plain_logits(model, cfg, np.concatenate([prefix, d, s1]))
+        lb = _plain_logits(model, cfg, np.concatenate([prefix, d, s2]))
+        ma = max(la[0], la[1]) - max(la[2], la[3])
+        mb = la.new_tensor(lb[0] - lb[2])
+        assert abs(res[r].values["a"] - torch.sigmoid(ma).item()) < 1e-4
+        assert abs(res[r].values["b"] - torch.sigmoid(mb).item()) < 1e-4
+
+
+def test_filter_guards_followups():
+    cfg, model = _model()
+    arena = KVArena(cfg.layers, 128, 16, cfg.num_kv_heads, cfg.head_dim, device="cpu", dtype=torch.float32)
+    ex = StageExecutor(model, arena, 200)
+    rng = np.random.default_rng(2)
+    prefix = rng.integers(0, 1000, 8).astype(np.int32)
+    docs = [rng.integers(0, 1000, 20).astype(np.int32) for _ in range(12)]
+    calls = [Call(kind="filter", suffix=rng.integers(0, 1000, 4).astype(np.int32), true_cols=[0], false_cols=[2],
+                  name="f"),
+             Call(kind="score", suffix=rng.integers(0, 1000, 4).astype(np.int32), true_cols=[1], false_cols=[3],
+                  name="s")]
+    res = RegionRun(ex, prefix, docs, calls).run()
+    kept = [r for r in res if r.values["f"]]
+    dropped = [r for r in res if not r.values["f"]]
+    assert all("s" in r.values for r in kept)
+    assert all("s" not in r.values for r in dropped)
+    assert arena.pool.free_pages == arena.num_pages

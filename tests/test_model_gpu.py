@@ -1,0 +1,57 @@
+"""Whole-model numerics: the kernel pipeline against the fp32 PyTorch model.
+
+Both run the same packed chunks through the same executor; the fp32 model
+uses the dequantized checkpoint weights, so the difference is activation
+quantization (fp8 models) and bf16 rounding.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from quail_b200 import ops
+from quail_b200.engine.arena import KVArena
+from quail_b200.engine.stage_executor import StageExecutor, Task
+from quail_b200.models.config import QWEN3_GPU_TINY
+from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Reference, Qwen3Weights
+from quail_b200.models.weights import random_checkpoint
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(model, cfg, prefix, docs, suffix, dtype):
+    arena = KVArena(cfg.layers, 96, 128, cfg.num_kv_heads, cfg.head_dim, device="cuda", dtype=dtype)
+    ex = StageExecutor(model, arena, 300, min_piece=16)
+    got = {}
+    ex.submit(Task(key="p", tokens=prefix, pos_start=0, free_after=False))
+    for i, d in enumerate(docs):
+        ex.submit(Task(key=i, tokens=np.concatenate([d, suffix]), pos_start=len(prefix), reads=[("p", len(prefix))],
+                       readout=True, on_done=lambda t, row, i=i: got.__setitem__(i, row.float().cpu())))
+    ex.run()
+    return torch.stack([got[i] for i in range(len(docs))])
+
+
+@pytest.mark.parametrize("weight_dtype", ["fp8", "bf16"])
+def test_pipeline_matches_fp32_model(weight_dtype):
+    cfg = QWEN3_GPU_TINY.with_(weight_dtype=weight_dtype, vocab=4096, max_position=8192, init_std=0.05)
+    ckpt = random_checkpoint(cfg, seed=7, device="cuda")
+    ids = list(range(16))
+    pipe = Qwen3Pipeline(cfg, Qwen3Weights(cfg, ckpt, "cuda", head_rows=ids))
+    refm = Qwen3Reference(cfg, ckpt, device="cuda", head_rows=ids)
+    rng = np.random.default_rng(0)
+    prefix = rng.integers(0, 4096, 48).astype(np.int32)
+    docs = [rng.integers(0, 4096, n).astype(np.int32) for n in (10, 200, 64, 450, 129)]
+    suffix = rng.integers(0, 4096, 24).astype(np.int32)
+    got = _run(pipe, cfg, prefix, docs, suffix, torch.bfloat16)
+    want = _run(refm, cfg, prefix, docs, suffix, torch.float32)
+    assert ops.read_and_clear_error(0) == 0
+    err = ((got - want).norm() / want.norm()).item()
+    assert err < (0.08 if weight_dtype == "fp8" else 0.03), err
+    # the argmax answer row agrees on most rows
+    agree = (got.argmax(1) == want.argmax(1)).float().mean().item()
+    assert agree >= 0.8
+
+
+def test_smoke_entry():
+    from quail_b200.models.smoke import run_smoke
+    run_smoke()
