@@ -1,0 +1,13 @@
+// Epilogue selector of the tcgen05 GEMM kernel.
+#pragma once
+
+namespace qb {
+
+enum Epi : int {
+  kEpiBf16 = 0,        // D = acc (bf16)
+  kEpiResidual = 1,    // D = acc + R (bf16; R may alias D)
+  kEpiSwigluFp8 = 2,   // Y = e4m3(silu(g) * u), one fp32 scale per 128 outputs
+  kEpiSwigluBf16 = 3,  // D = silu(g) * u (bf16)
+};
+
+}  // namespace qb

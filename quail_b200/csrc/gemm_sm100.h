@@ -4,15 +4,9 @@
 #include <torch/extension.h>
 #include <cuda.h>
 
-namespace qb {
+#include "gemm_epi.h"
 
-// GEMM epilogues
-enum Epi : int {
-  kEpiBf16 = 0,        // D = acc (bf16)
-  kEpiResidual = 1,    // D = acc + R (bf16; R may alias D)
-  kEpiSwigluFp8 = 2,   // Y = e4m3(silu(g) * u), one fp32 scale per 128 outputs
-  kEpiSwigluBf16 = 3,  // D = silu(g) * u (bf16)
-};
+namespace qb {
 
 void gemm_sm100(const torch::Tensor& a, const torch::Tensor& b, const c10::optional<torch::Tensor>& sa,
                 const c10::optional<torch::Tensor>& sb, int64_t sb_gran, int64_t epi, torch::Tensor& out,
