@@ -72,13 +72,24 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint8_t ue8m0_amax(float amax) {
+  const float sc = fmaxf(amax, 1e-30f) / kFp8Max;
+  uint32_t bits = __float_as_uint(sc);
+  uint32_t e = (bits >> 23) & 0xff;
+  if (bits & 0x7fffff) e += 1;
+  return (uint8_t)min(max(e, 1u), 253u);
+}
+__device__ __forceinline__ float ue8m0_inv_f(uint8_t e) { return __uint_as_float((uint32_t)(254 - e) << 23); }
+
 // smem tile: 64 rows x 128 bf16 (256 B), 16-byte chunk c of row r stored at
 // chunk c ^ (r & 7)
 __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
   return base + row * 256 + ((chunk ^ (row & 7)) << 4);
 }
 
-template <bool FP8_OUT>
+// MODE: 0 bf16 out; 1 e4m3 + fp32 scale per (token, head) [QH, ldos];
+// 2 e4m3 + UE8M0 bytes per 32 values in the MX scale atom layout (K = QH*128)
+template <int MODE>
 __global__ void __launch_bounds__(128)
     prefill_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
                         const __nv_bfloat16* __restrict__ vc, const int* __restrict__ seqs,
@@ -294,7 +305,7 @@ __global__ void __launch_bounds__(128)
   const float inv1 = lrow[1] > 0.f ? 1.f / lrow[1] : 0.f;
   const int r0 = rbase, r1 = rbase + 8;
   const size_t tok0 = (size_t)q_start + q0 + r0, tok1 = tok0 + 8;
-  if constexpr (!FP8_OUT) {
+  if constexpr (MODE == 0) {
 #pragma unroll
     for (int db = 0; db < 16; ++db) {
       const int col = head * D + db * 8 + 2 * t4;
@@ -303,7 +314,7 @@ __global__ void __launch_bounds__(128)
       if (r1 < rows_here)
         *reinterpret_cast<uint32_t*>(o + tok1 * ldo + col) = pack_bf16(oacc[db][2] * inv1, oacc[db][3] * inv1);
     }
-  } else {
+  } else if constexpr (MODE == 1) {
     float am0 = 0.f, am1 = 0.f;
 #pragma unroll
     for (int db = 0; db < 16; ++db) {
@@ -336,6 +347,52 @@ __global__ void __launch_bounds__(128)
       if (r0 < rows_here) os[(size_t)head * ldos + tok0] = s0;
       if (r1 < rows_here) os[(size_t)head * ldos + tok1] = s1;
     }
+  } else {
+    // four 32-wide groups per head: group j = d-blocks 4j..4j+3, spread over the quad
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float am0 = 0.f, am1 = 0.f;
+#pragma unroll
+      for (int db = 4 * j; db < 4 * j + 4; ++db) {
+        oacc[db][0] *= inv0;
+        oacc[db][1] *= inv0;
+        oacc[db][2] *= inv1;
+        oacc[db][3] *= inv1;
+        am0 = fmaxf(am0, fmaxf(fabsf(oacc[db][0]), fabsf(oacc[db][1])));
+        am1 = fmaxf(am1, fmaxf(fabsf(oacc[db][2]), fabsf(oacc[db][3])));
+      }
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, 1));
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, 2));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, 1));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, 2));
+      const uint8_t e0 = ue8m0_amax(am0), e1 = ue8m0_amax(am1);
+      w0 |= (uint32_t)e0 << (8 * j);
+      w1 |= (uint32_t)e1 << (8 * j);
+      const float i0 = ue8m0_inv_f(e0), i1 = ue8m0_inv_f(e1);
+#pragma unroll
+      for (int db = 4 * j; db < 4 * j + 4; ++db) {
+        const int col = head * D + db * 8 + 2 * t4;
+        if (r0 < rows_here) {
+          __nv_fp8x2_e4m3 v(make_float2(oacc[db][0] * i0, oacc[db][1] * i0));
+          *reinterpret_cast<__nv_fp8x2_e4m3*>(o8 + tok0 * ldo + col) = v;
+        }
+        if (r1 < rows_here) {
+          __nv_fp8x2_e4m3 v(make_float2(oacc[db][2] * i1, oacc[db][3] * i1));
+          *reinterpret_cast<__nv_fp8x2_e4m3*>(o8 + tok1 * ldo + col) = v;
+        }
+      }
+    }
+    if (t4 == 0) {
+      // K stage = head (head_dim 128): the 4 bytes of one atom word
+      uint8_t* sfb = reinterpret_cast<uint8_t*>(os);
+      auto word = [&](size_t tok) {
+        return reinterpret_cast<uint32_t*>(sfb + ((tok >> 7) * QH + head) * 512 + (tok & 31) * 16 +
+                                           ((tok & 127) >> 5) * 4);
+      };
+      if (r0 < rows_here) *word(tok0) = w0;
+      if (r1 < rows_here) *word(tok1) = w1;
+    }
   }
 }
 
@@ -358,23 +415,30 @@ void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, con
   constexpr int smem = 64 * 256 + 2 * 2 * 64 * 256;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
   const float sl2 = (float)(softmax_scale * 1.4426950408889634);
   auto qp = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   auto kp = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
   auto vp = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
-  if (out.scalar_type() == at::kFloat8_e4m3fn) {
+  if (out.scalar_type() == at::kFloat8_e4m3fn && out_scale.has_value() && out_scale->scalar_type() == at::kByte) {
+    TORCH_CHECK(out_scale->numel() >= (q.size(0) + 127) / 128 * QH * 512, "MX attention output scale bytes");
+    prefill_attn_kernel<2><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
+                                                   page_list.data_ptr<int>(), P, QH, KH, sl2, nullptr,
+                                                   out.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
+                                                   reinterpret_cast<float*>(out_scale->data_ptr()), 0);
+  } else if (out.scalar_type() == at::kFloat8_e4m3fn) {
     TORCH_CHECK(out_scale.has_value() && out_scale->size(0) == QH, "fp8 attention output needs [QH, >=T] scales");
-    prefill_attn_kernel<true><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
+    prefill_attn_kernel<1><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
                                                    page_list.data_ptr<int>(), P, QH, KH, sl2, nullptr,
                                                    out.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
                                                    out_scale->data_ptr<float>(), out_scale->stride(0));
   } else {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "attention output bf16 or e4m3");
-    prefill_attn_kernel<false><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
+    prefill_attn_kernel<0><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
                                                     page_list.data_ptr<int>(), P, QH, KH, sl2,
                                                     reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
                                                     out.stride(0), nullptr, nullptr, 0);

@@ -24,6 +24,13 @@ void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, con
                        const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
                        double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_scale);
 
+void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
+             int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
+             const c10::optional<torch::Tensor>& residual);
+void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps, torch::Tensor& y8,
+                      torch::Tensor& sf, int64_t T);
+void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch::Tensor& sf, int64_t T);
+
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
 
@@ -58,6 +65,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &qb::gemm_sm100, "tcgen05 GEMM (bf16 or block-scaled e4m3) with fused epilogues", py::arg("a"),
         py::arg("b"), py::arg("sa"), py::arg("sb"), py::arg("sb_gran"), py::arg("epi"), py::arg("out"),
         py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
+  m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
+  m.def("rmsnorm_quant_mx", &qb::rmsnorm_quant_mx);
+  m.def("quant_rows_mx", &qb::quant_rows_mx);
   m.def("embed_gather", &qb::embed_gather);
   m.def("rmsnorm_quant", &qb::rmsnorm_quant);
   m.def("quant_rows", &qb::quant_rows);

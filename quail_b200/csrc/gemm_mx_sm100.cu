@@ -1,0 +1,426 @@
+// K1 (MX): fp8 GEMM with hardware block scaling on tcgen05.
+//
+//   D[M, N] = sum_k (A[m, k] * 2^(ea[m, k/32] - 127)) * (B[n, k] * 2^(eb[n, k/32] - 127))
+//
+// A and B are e4m3, K-major. The scales are UE8M0 (power-of-two) bytes, one
+// per row and 32-wide K block, stored in the tcgen05 scale-factor atom
+// layout: for a 128-row x 128-K chunk, 512 bytes where row r, K block j sits
+// at byte (r % 32) * 16 + ((r % 128) / 32) * 4 + j; chunks ordered
+// [row / 128][K / 128]. Weights quantized with 128x128 blocks repeat one
+// byte over their 4 K blocks; activations get one byte per 32 values.
+//
+// Mainloop per 128-wide K stage: the producer TMA-loads the A and B tiles
+// (128B swizzle, no multicast) and bulk-copies the stage's scale chunks
+// into shared memory; the MMA thread copies the scale chunks into TMEM
+// (tcgen05.cp 32x128b.warpx4: 32 rows x 16 bytes broadcast to the 4 lane
+// quarters) and issues four kind::mxf8f6f4.block_scale MMAs (K = 32 each,
+// scale byte selected by sf_id). The accumulator stays in TMEM for the
+// whole K loop: no promotion work in registers. The epilogue drains it to
+// registers, hands the TMEM buffer back, then converts and stores.
+//
+// This is the reference's DeepGEMM-on-Blackwell path (vLLM fp8_gemm_nt with
+// UE8M0 scales, quail/backends/quail/executor/attention.py:483-492), written
+// here as our own kernel.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+namespace qb {
+
+struct MxParams {
+  int M, N, K;
+  __nv_bfloat16* D;
+  int ldd;
+  const __nv_bfloat16* R;
+  int ldr;
+  uint8_t* Y;       // e4m3 SwiGLU output [M, N/2]
+  int ldy;
+  uint8_t* Ysf;     // its UE8M0 scales in the atom layout, K = N/2
+  const uint8_t* sfa;  // [ceil(M/128)][K/128][512]
+  const uint8_t* sfb;  // [ceil(N/128)][K/128][512]
+  int* err;
+  int num_m_tiles, num_n_tiles;
+};
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// tcgen05.cp 32 rows x 128 bits from shared memory to TMEM lanes 0..31,
+// replicated to the four lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// K-major, no-swizzle descriptor of a 32-row x 16-byte chunk (8-row core
+// matrices 128 bytes apart)
+__device__ __forceinline__ uint64_t sf_chunk_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(128 >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1 << 46;           // sm_100 descriptor version
+  return d;                          // layout type 0: no swizzle
+}
+
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// block-scaled instruction descriptor: e4m3 x e4m3 -> f32, UE8M0 scales
+__host__ __device__ constexpr uint32_t make_idesc_mx(int M, int N, int a_sf_id, int b_sf_id) {
+  return ((uint32_t)b_sf_id << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(M >> 4) << 24) | ((uint32_t)a_sf_id << 29);
+}
+
+__device__ __forceinline__ uint8_t ue8m0_of(float amax) {
+  // smallest power of two >= amax / 448, as a biased exponent
+  const float s = fmaxf(amax, 1e-30f) / kFp8Max;
+  uint32_t bits = __float_as_uint(s);
+  uint32_t e = (bits >> 23) & 0xff;
+  if (bits & 0x7fffff) e += 1;
+  return (uint8_t)min(max(e, 1u), 253u);
+}
+__device__ __forceinline__ float ue8m0_inv(uint8_t e) { return __uint_as_float((uint32_t)(254 - e) << 23); }
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ void st_bf16x8(__nv_bfloat16* dst, const float* v) {
+  __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+}
+__device__ __forceinline__ void ld_bf16x8f(const __nv_bfloat16* src, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+constexpr int kMxBN = 256;
+constexpr int kMxStages = 4;
+constexpr int kMxABytes = 128 * 128;
+constexpr int kMxBBytes = kMxBN * 128;
+constexpr int kMxSfaBytes = 512;
+constexpr int kMxSfbBytes = 512 * (kMxBN / 128);
+constexpr int kMxSmem = kMxStages * (kMxABytes + kMxBBytes) + kMxStages * (kMxSfaBytes + kMxSfbBytes) + 1024 + 256;
+constexpr int kMxSfaCol = kMxBN;       // TMEM columns after the accumulator
+constexpr int kMxSfbCol = kMxBN + 4;
+
+template <int EPI>
+__global__ void __launch_bounds__(64 + kMxBN, 1)
+    gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const MxParams p) {
+  constexpr int BM = 128, BN = kMxBN, STAGES = kMxStages;
+  constexpr int EPI_THREADS = BN;
+  constexpr int TMEM_COLS = 512;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kMxABytes;
+  uint8_t* sSFA = sB + STAGES * kMxBBytes;
+  uint8_t* sSFB = sSFA + STAGES * kMxSfaBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * kMxSfbBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* done_bar = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_k = p.K / 128;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int sfb_chunks = (p.N + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, EPI_THREADS);
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+        const int nchunks = min(BN / 128, sfb_chunks - tn * (BN / 128));
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kMxABytes + kMxBBytes + kMxSfaBytes + nchunks * 512);
+          tma_load_2d(&tmA, &full[stage], sA + stage * kMxABytes, kb * 128, tm * BM);
+          tma_load_2d(&tmB, &full[stage], sB + stage * kMxBBytes, kb * 128, tn * BN);
+          bulk_load(sSFA + stage * kMxSfaBytes, p.sfa + ((size_t)tm * num_k + kb) * 512, 512, &full[stage]);
+          for (int c = 0; c < nchunks; ++c)
+            bulk_load(sSFB + stage * kMxSfbBytes + c * 512,
+                      p.sfb + ((size_t)(tn * (BN / 128) + c) * num_k + kb) * 512, 512, &full[stage]);
+          last_par[stage] = (int)phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(&full[s], (uint32_t)last_par[s], p.err, kErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      const uint32_t t_sfa = tmem_base + kMxSfaCol;
+      const uint32_t t_sfb = tmem_base + kMxSfbCol;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(acc_empty, aphase ^ 1, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // scale factors of this stage into TMEM (in order with the MMAs below)
+          tmem_cp_sf(t_sfa, sf_chunk_desc(smem_u32(sSFA + stage * kMxSfaBytes)));
+#pragma unroll
+          for (int c = 0; c < BN / 128; ++c)
+            tmem_cp_sf(t_sfb + c * 4, sf_chunk_desc(smem_u32(sSFB + stage * kMxSfbBytes + c * 512)));
+          const uint32_t a0 = smem_u32(sA + stage * kMxABytes);
+          const uint32_t b0 = smem_u32(sB + stage * kMxBBytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            umma_mx(tmem_base, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32),
+                    make_idesc_mx(BM, BN, k, k), t_sfa | ((uint32_t)k << 30), t_sfb | ((uint32_t)k << 30),
+                    (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) {
+          tc_commit(acc_full);
+          aphase ^= 1;
+        }
+      }
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, p.err, kErrTimeoutMma);
+    }
+  } else {
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int h = ew >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+      const int m = tm * BM + row;
+      const int n0 = tn * BN + h * 128;
+      if (!mbar_wait(acc_full, aphase, p.err, kErrTimeoutEpilogue)) break;
+      aphase ^= 1;
+      tc_fence_after();
+      float acc[128];
+      const uint32_t taddr = tmem_base + lane_base + (uint32_t)(h * 128);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        QB_TMEM_LD32(taddr + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      // the accumulator is in registers: the next tile's MMAs may start
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      if (m >= p.M) continue;
+      if constexpr (EPI == kEpiBf16 || EPI == kEpiResidual) {
+        __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + n0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 8) {
+          if (n0 + j < p.N) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = acc[j + i];
+            if constexpr (EPI == kEpiResidual) {
+              float rv[8];
+              ld_bf16x8f(p.R + (size_t)m * p.ldr + n0 + j, rv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[i] += rv[i];
+            }
+            st_bf16x8(dst + j, v);
+          }
+        }
+      } else {
+        // gate = acc[0..63], up = acc[64..127] of outputs out0 .. out0+63
+        const int out0 = tn * (BN / 2) + h * 64;
+        if (out0 >= p.N / 2) continue;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = silu_f(acc[i]) * acc[64 + i];
+        if constexpr (EPI == kEpiSwigluBf16) {
+          __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + out0;
+#pragma unroll
+          for (int j = 0; j < 64; j += 8) st_bf16x8(dst + j, &acc[j]);
+        } else {
+          // two 32-wide groups, one UE8M0 scale each, in the next GEMM's A-scale layout
+          uint8_t e[2];
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(acc[g * 32 + i]));
+            e[g] = ue8m0_of(amax);
+            const float inv = ue8m0_inv(e[g]);
+            uint8_t* dst = p.Y + (size_t)m * p.ldy + out0 + g * 32;
+#pragma unroll
+            for (int j = 0; j < 32; j += 16) {
+              __align__(16) __nv_fp8x4_e4m3 pk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                pk[i] = __nv_fp8x4_e4m3(make_float4(acc[g * 32 + j + 4 * i] * inv, acc[g * 32 + j + 4 * i + 1] * inv,
+                                                    acc[g * 32 + j + 4 * i + 2] * inv,
+                                                    acc[g * 32 + j + 4 * i + 3] * inv));
+              *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(pk);
+            }
+          }
+          const int kst = out0 / 128, kblk = (out0 % 128) / 32;
+          const int ko = p.N / 2 / 128;
+          uint8_t* sf = p.Ysf + ((size_t)(m / 128) * ko + kst) * 512 + (m % 32) * 16 + ((m % 128) / 32) * 4 + kblk;
+          *reinterpret_cast<uint16_t*>(sf) = (uint16_t)e[0] | ((uint16_t)e[1] << 8);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc<TMEM_COLS>(tmem_base);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int EPI>
+static void launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, MxParams& p, cudaStream_t st, int dev) {
+  auto kern = gemm_mx_kernel<EPI>;
+  static bool configured[64] = {false};
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxSmem));
+    configured[dev] = true;
+  }
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  kern<<<std::min(tiles, num_sms(dev)), 64 + kMxBN, kMxSmem, st>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// a: [M, K] e4m3, sfa: MX scale bytes of a; b: [N, K] e4m3, sfb: of b.
+void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
+             int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
+             const c10::optional<torch::Tensor>& residual) {
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "gemm_mx: e4m3");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
+              "gemm_mx: shapes");
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(K % 128 == 0 && N % 16 == 0, "gemm_mx: K % 128 == 0 and N % 16 == 0");
+  TORCH_CHECK(sfa.scalar_type() == at::kByte && sfb.scalar_type() == at::kByte && sfa.is_contiguous() &&
+                  sfb.is_contiguous(),
+              "gemm_mx: uint8 scale bytes");
+  TORCH_CHECK(sfa.numel() >= (int64_t)((M + 127) / 128) * (K / 128) * 512, "gemm_mx: A scale bytes too small");
+  TORCH_CHECK(sfb.numel() >= (int64_t)((N + 127) / 128) * (K / 128) * 512, "gemm_mx: B scale bytes too small");
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  if (M == 0) return;
+  MxParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.sfa = sfa.data_ptr<uint8_t>();
+  p.sfb = sfb.data_ptr<uint8_t>();
+  p.err = device_error_word(dev);
+  p.num_m_tiles = (M + 127) / 128;
+  p.num_n_tiles = (N + kMxBN - 1) / kMxBN;
+  if (epi == kEpiSwigluFp8) {
+    TORCH_CHECK(N % kMxBN == 0, "SwiGLU: N must be a multiple of 256");
+    TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.size(0) == M && out.size(1) == N / 2 &&
+                    out.stride(1) == 1 && out.stride(0) % 16 == 0,
+                "SwiGLU fp8 output");
+    TORCH_CHECK(out_sf.has_value() && out_sf->numel() >= (int64_t)((M + 127) / 128) * (N / 2 / 128) * 512,
+                "SwiGLU fp8 output scale bytes");
+    p.Y = reinterpret_cast<uint8_t*>(out.data_ptr());
+    p.ldy = out.stride(0);
+    p.Ysf = out_sf->data_ptr<uint8_t>();
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.stride(0) % 8 == 0, "bf16 out");
+    TORCH_CHECK(out.size(0) == M && out.size(1) == (epi == kEpiSwigluBf16 ? N / 2 : N), "gemm_mx: out shape");
+    p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    p.ldd = out.stride(0);
+  }
+  if (epi == kEpiResidual) {
+    TORCH_CHECK(residual.has_value() && residual->scalar_type() == at::kBFloat16, "residual");
+    p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a.stride(0), 128, 128,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  switch (epi) {
+    case kEpiBf16: launch_mx<kEpiBf16>(ta, tb, p, st, dev); break;
+    case kEpiResidual: launch_mx<kEpiResidual>(ta, tb, p, st, dev); break;
+    case kEpiSwigluFp8: launch_mx<kEpiSwigluFp8>(ta, tb, p, st, dev); break;
+    case kEpiSwigluBf16: launch_mx<kEpiSwigluBf16>(ta, tb, p, st, dev); break;
+    default: TORCH_CHECK(false, "gemm_mx: unknown epilogue ", epi);
+  }
+}
+
+}  // namespace qb

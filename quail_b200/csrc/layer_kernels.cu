@@ -68,7 +68,22 @@ __global__ void embed_gather_kernel(const int* __restrict__ ids, const __nv_bflo
 // ---------------------------------------------------------------- K3 norm
 // One warp per row; each lane owns 8 contiguous columns of every 256-column
 // slab, so a 128-column quant group is 16 lanes (half a warp).
-template <int H, bool FP8>
+__device__ __forceinline__ uint8_t ue8m0_of_amax(float amax) {
+  const float sc = fmaxf(amax, 1e-30f) / kFp8Max;
+  uint32_t bits = __float_as_uint(sc);
+  uint32_t e = (bits >> 23) & 0xff;
+  if (bits & 0x7fffff) e += 1;
+  return (uint8_t)min(max(e, 1u), 253u);
+}
+__device__ __forceinline__ float ue8m0_inverse(uint8_t e) { return __uint_as_float((uint32_t)(254 - e) << 23); }
+
+// byte offset of (row m, 32-wide K block j) in the MX scale atom layout of a
+// matrix with kst = K/128 K stages
+__device__ __forceinline__ size_t sf_atom_offset(int m, int j, int kst) {
+  return ((size_t)(m >> 7) * kst + (j >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (j & 3);
+}
+
+template <int H, bool FP8, bool MX = false>
 __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                      const __nv_bfloat16* __restrict__ w, float eps,
                                      uint8_t* __restrict__ y8, float* __restrict__ ys, int ldys,
@@ -94,7 +109,17 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int ld
     ld_bf16x8(w + s * 256 + lane * 8, wv);
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[s][i] = v[s][i] * rinv * wv[i];
-    if constexpr (FP8) {
+    if constexpr (FP8 && MX) {
+      // one UE8M0 scale per 32 columns (4 lanes)
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const uint8_t e = ue8m0_of_amax(amax);
+      *reinterpret_cast<uint2*>(y8 + (size_t)warp * H + s * 256 + lane * 8) = pack_fp8x8(v[s], ue8m0_inverse(e));
+      if ((lane & 3) == 0) reinterpret_cast<uint8_t*>(ys)[sf_atom_offset(warp, s * 8 + (lane >> 2), H / 128)] = e;
+    } else if constexpr (FP8) {
       float amax = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
@@ -110,7 +135,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int ld
 }
 
 // ---------------------------------------------------------------- quant rows
-template <bool SWIGLU>
+template <bool SWIGLU, bool MX = false>
 __global__ void quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
                                   uint8_t* __restrict__ y8, int ldy, float* __restrict__ ys, int ldys,
                                   __nv_bfloat16* __restrict__ ybf, int T) {
@@ -132,7 +157,16 @@ __global__ void quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx, 
   } else {
     ld_bf16x8(x + (size_t)t * ldx + col, v);
   }
-  if (y8) {
+  if (MX) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const uint8_t e = ue8m0_of_amax(amax);
+    *reinterpret_cast<uint2*>(y8 + (size_t)t * ldy + col) = pack_fp8x8(v, ue8m0_inverse(e));
+    if ((lane & 3) == 0) reinterpret_cast<uint8_t*>(ys)[sf_atom_offset(t, col / 32, K / 128)] = e;
+  } else if (y8) {
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -324,6 +358,38 @@ void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, c
   TORCH_CHECK(false, "rmsnorm_quant: unsupported hidden size ", H);
 }
 
+// x: [T, H] bf16 -> e4m3 [T, H] + UE8M0 scale bytes (MX atom layout, one per 32 columns)
+void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps, torch::Tensor& y8,
+                      torch::Tensor& sf, int64_t T) {
+  const int H = x.size(1);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && w.numel() == H, "rmsnorm_quant_mx inputs");
+  TORCH_CHECK(y8.is_contiguous() && y8.size(1) == H && y8.size(0) >= T, "rmsnorm_quant_mx output");
+  TORCH_CHECK(sf.scalar_type() == at::kByte && sf.numel() >= (T + 127) / 128 * (H / 128) * 512, "scale bytes");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(x.get_device());
+  const int threads = 256, blocks = (int)((T * 32 + threads - 1) / threads);
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto yp = reinterpret_cast<uint8_t*>(y8.data_ptr());
+  auto sp = reinterpret_cast<float*>(sf.data_ptr());
+#define QB_NORM_MX(HH)                                                                                   \
+  if (H == HH) {                                                                                         \
+    rmsnorm_quant_kernel<HH, true, true><<<blocks, threads, 0, cur_stream(x)>>>(xp, x.stride(0), wp, eps, yp, \
+                                                                                sp, 0, nullptr, 0, T);   \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                      \
+    return;                                                                                              \
+  }
+  QB_NORM_MX(256)
+  QB_NORM_MX(512)
+  QB_NORM_MX(1024)
+  QB_NORM_MX(2048)
+  QB_NORM_MX(2560)
+  QB_NORM_MX(4096)
+  QB_NORM_MX(5120)
+#undef QB_NORM_MX
+  TORCH_CHECK(false, "rmsnorm_quant_mx: unsupported hidden size ", H);
+}
+
 // x: [T, K] (or [T, 2K] with swiglu) bf16 -> e4m3 [T, K] + scales [K/128, >=T], or bf16 [T, K]
 void quant_rows(const torch::Tensor& x, bool swiglu, const c10::optional<torch::Tensor>& y8,
                 const c10::optional<torch::Tensor>& ys, const c10::optional<torch::Tensor>& ybf, int64_t T) {
@@ -343,6 +409,27 @@ void quant_rows(const torch::Tensor& x, bool swiglu, const c10::optional<torch::
     quant_rows_kernel<true><<<blocks, threads, 0, cur_stream(x)>>>(xp, x.stride(0), K, y8p, ldy, ysp, ldys, ybp, T);
   else
     quant_rows_kernel<false><<<blocks, threads, 0, cur_stream(x)>>>(xp, x.stride(0), K, y8p, ldy, ysp, ldys, ybp, T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch::Tensor& sf, int64_t T) {
+  const int K = swiglu ? x.size(1) / 2 : x.size(1);
+  TORCH_CHECK(K % 256 == 0 && x.stride(1) == 1 && x.scalar_type() == at::kBFloat16, "quant_rows_mx: K % 256");
+  TORCH_CHECK(y8.stride(1) == 1 && y8.size(1) == K && sf.numel() >= (T + 127) / 128 * (K / 128) * 512,
+              "quant_rows_mx outputs");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(x.get_device());
+  const int warps = (int)T * (K / 256);
+  const int threads = 256, blocks = (warps * 32 + threads - 1) / threads;
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto yp = reinterpret_cast<uint8_t*>(y8.data_ptr());
+  auto sp = reinterpret_cast<float*>(sf.data_ptr());
+  if (swiglu)
+    quant_rows_kernel<true, true><<<blocks, threads, 0, cur_stream(x)>>>(xp, x.stride(0), K, yp, y8.stride(0), sp, 0,
+                                                                         nullptr, T);
+  else
+    quant_rows_kernel<false, true><<<blocks, threads, 0, cur_stream(x)>>>(xp, x.stride(0), K, yp, y8.stride(0), sp,
+                                                                          0, nullptr, T);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -19,7 +19,7 @@ from __future__ import annotations
 import torch
 
 from quail_b200.models.config import DecoderConfig
-from quail_b200.models.weights import dequantized, head_weight
+from quail_b200.models.weights import head_weight
 from quail_b200.ops import reference as ref
 
 
@@ -27,13 +27,14 @@ class Qwen3Weights:
     """Per-layer fused device weights in the kernels' layouts.
 
     QKV rows are concatenated (q | k | v); gate/up rows are interleaved in
-    64-row groups for the SwiGLU epilogue, with their 128x128 block scales
-    expanded to 64-row granularity. fp8 models keep e4m3 + fp32 scales,
-    bf16 models keep bf16.
+    64-row groups for the SwiGLU epilogue. fp8 models keep e4m3 weights with
+    power-of-two 128x128 block scales as UE8M0 bytes in the MX atom layout
+    (the tcgen05 block-scaled MMA's scale format); bf16 models keep bf16.
     """
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None):
-        from quail_b200.ops.quant import interleave_gate_up
+        from quail_b200.ops.quant import (dequantize_weight, interleave_gate_up, interleave_gate_up_mx,
+                                          quantize_weight_mx)
         self.cfg = cfg
         self.device = device
         bf = torch.bfloat16
@@ -50,16 +51,16 @@ class Qwen3Weights:
             }
             names = [p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"]
             if cfg.fp8:
-                L["wqkv"] = torch.cat([ckpt[n + ".weight"] for n in names]).to(device).contiguous()
-                L["sqkv"] = torch.cat([ckpt[n + ".weight_scale_inv"] for n in names]).to(device).contiguous()
-                L["wo"] = ckpt[p + "self_attn.o_proj.weight"].to(device).contiguous()
-                L["so"] = ckpt[p + "self_attn.o_proj.weight_scale_inv"].to(device).contiguous()
-                gu = torch.cat([ckpt[p + "mlp.gate_proj.weight"], ckpt[p + "mlp.up_proj.weight"]]).to(device)
-                gus = torch.cat([ckpt[p + "mlp.gate_proj.weight_scale_inv"],
-                                 ckpt[p + "mlp.up_proj.weight_scale_inv"]]).to(device)
-                L["wgu"], L["sgu"] = interleave_gate_up(gu, gus)
-                L["wd"] = ckpt[p + "mlp.down_proj.weight"].to(device).contiguous()
-                L["sd"] = ckpt[p + "mlp.down_proj.weight_scale_inv"].to(device).contiguous()
+                # fp8 checkpoints carry fp32 128x128 block scales; the tcgen05
+                # block-scaled MMA takes power-of-two (UE8M0) scales, so each
+                # projection is requantized once at load with the same blocks
+                deq = lambda n: dequantize_weight(ckpt[n + ".weight"].to(device),  # noqa: E731
+                                                  ckpt[n + ".weight_scale_inv"].to(device))
+                L["wqkv"], L["sqkv"] = quantize_weight_mx(torch.cat([deq(n) for n in names]))
+                L["wo"], L["so"] = quantize_weight_mx(deq(p + "self_attn.o_proj"))
+                L["wgu"], L["sgu"] = interleave_gate_up_mx(torch.cat([deq(p + "mlp.gate_proj"),
+                                                                      deq(p + "mlp.up_proj")]))
+                L["wd"], L["sd"] = quantize_weight_mx(deq(p + "mlp.down_proj"))
             else:
                 L["wqkv"] = torch.cat([ckpt[n + ".weight"].to(bf) for n in names]).to(device).contiguous()
                 L["wo"] = ckpt[p + "self_attn.o_proj.weight"].to(device=device, dtype=bf).contiguous()
@@ -102,8 +103,8 @@ class Qwen3Pipeline:
         for li, L in enumerate(w.layers):
             kc, vc = arena.layer(li)
             if fp8:
-                x8, xs = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps)
-                qkv = ops.gemm(x8, L["wqkv"], sa=xs, sb=L["sqkv"])
+                x8, xs = ops.rmsnorm_quant_mx(h, L["ln1"], cfg.rms_eps)
+                qkv = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
             else:
                 x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
                 qkv = ops.gemm(x, L["wqkv"])
@@ -111,11 +112,11 @@ class Qwen3Pipeline:
                                     cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
             if fp8:
                 o8, os_ = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale,
-                                                fp8_out=True)
-                ops.gemm(o8, L["wo"], sa=os_, sb=L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-                x8, xs = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps)
-                a8, as_ = ops.gemm(x8, L["wgu"], sa=xs, sb=L["sgu"], sb_gran=64, epi=ops.EPI_SWIGLU_FP8)
-                ops.gemm(a8, L["wd"], sa=as_, sb=L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                                                fp8_out=True, mx=True)
+                ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
+                a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
+                ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
             else:
                 o = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale)
                 ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
@@ -134,11 +135,22 @@ class Qwen3Reference:
     """
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device="cpu", head_rows=None,
-                 dtype=torch.float32):
+                 dtype=torch.float32, emulate_kernels: bool = False):
         self.cfg = cfg
         self.device = device
         self.dtype = dtype
+        # round where the kernels round: bf16 residual stream, q/k/v and KV;
+        # e4m3 + 1x128 scales on every GEMM input of an fp8 model
+        self.emulate = emulate_kernels
         f = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
+        if self.emulate and cfg.fp8:
+            from quail_b200.ops.quant import dequantize_mx, quantize_weight_mx
+
+            def dequantized(ck, name):  # noqa: F811 - the kernels' power-of-two requantization
+                from quail_b200.models.weights import dequantized as plain
+                return dequantize_mx(*quantize_weight_mx(plain(ck, name).to(device)))
+        else:
+            from quail_b200.models.weights import dequantized
         self.embed = f(ckpt["model.embed_tokens.weight"])
         self.final_norm = f(ckpt["model.norm.weight"])
         self.layers = []
@@ -164,28 +176,43 @@ class Qwen3Reference:
         self.answer_rows = self.head.index_select(0, ids)
         self.answer_ids = ids.cpu()
 
+    def _q(self, x: torch.Tensor) -> torch.Tensor:
+        """fake-quantize a GEMM input the way the fp8 kernels do."""
+        if not (self.emulate and self.cfg.fp8):
+            return x
+        from quail_b200.ops.quant import dequantize_mx, quantize_act_mx
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        return dequantize_mx(*quantize_act_mx(x2)).reshape(shape)
+
+    def _bf(self, x: torch.Tensor) -> torch.Tensor:
+        return x.bfloat16().float() if self.emulate else x
+
     @torch.no_grad()
     def hidden_chunk(self, chunk, arena) -> torch.Tensor:
         cfg = self.cfg
         T = chunk.num_tokens
-        h = self.embed[chunk.ids.long()]
+        h = self._bf(self.embed[chunk.ids.long()])
         QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
         for li, L in enumerate(self.layers):
             kc, vc = arena.layer(li)
-            x = ref.rmsnorm(h, L["ln1"], cfg.rms_eps)
-            q = (x @ L["wq"].t()).view(T, QH, D)
-            k = (x @ L["wk"].t()).view(T, KH, D)
-            v = (x @ L["wv"].t()).view(T, KH, D)
-            q = ref.rope_neox(ref.rmsnorm(q, L["qn"], cfg.rms_eps), chunk.positions, self.cos_sin)
+            x = self._q(self._bf(ref.rmsnorm(h, L["ln1"], cfg.rms_eps)))
+            q = self._bf(x @ L["wq"].t()).view(T, QH, D)
+            k = self._bf(x @ L["wk"].t()).view(T, KH, D)
+            v = self._bf(x @ L["wv"].t()).view(T, KH, D)
+            q = self._bf(ref.rope_neox(ref.rmsnorm(q, L["qn"], cfg.rms_eps), chunk.positions, self.cos_sin))
             k = ref.rope_neox(ref.rmsnorm(k, L["kn"], cfg.rms_eps), chunk.positions, self.cos_sin)
             ok = chunk.slots >= 0
             slots = chunk.slots[ok].long()
-            kc.view(-1, KH, D)[slots] = k[ok].to(kc.dtype)
-            vc.view(-1, KH, D)[slots] = v[ok].to(vc.dtype)
+            kc.view(-1, KH, D)[slots] = self._bf(k[ok]).to(kc.dtype)
+            vc.view(-1, KH, D)[slots] = self._bf(v[ok]).to(vc.dtype)
             o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(h.dtype)
-            h = h + o @ L["wo"].t()
-            x = ref.rmsnorm(h, L["ln2"], cfg.rms_eps)
-            h = h + ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t()
+            o = self._q(o) if self.cfg.fp8 else self._bf(o)
+            h = self._bf(h + o @ L["wo"].t())
+            x = self._q(self._bf(ref.rmsnorm(h, L["ln2"], cfg.rms_eps)))
+            a = ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t())
+            a = self._q(a) if self.cfg.fp8 else self._bf(a)
+            h = self._bf(h + a @ L["wd"].t())
         return h
 
     @torch.no_grad()

@@ -16,6 +16,10 @@ from quail_b200.ops.kernels import (  # noqa: F401
     embed_gather,
     final_norm_readout,
     gemm,
+    gemm_mx,
+    sf_bytes,
+    rmsnorm_quant_mx,
+    quant_rows_mx,
     kernels_available,
     launch_count,
     native,
@@ -28,6 +32,13 @@ from quail_b200.ops.kernels import (  # noqa: F401
 from quail_b200.ops.quant import (  # noqa: F401
     FP8_MAX,
     dequantize_act,
+    dequantize_mx,
+    interleave_gate_up_mx,
+    quantize_act_mx,
+    quantize_weight_mx,
+    requantize_weight_mx,
+    pack_sf_atoms,
+    unpack_sf_atoms,
     dequantize_weight,
     interleave_gate_up,
     quantize_act,

@@ -75,6 +75,59 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
     return out
 
 
+def sf_bytes(rows: int, K: int) -> int:
+    """Bytes of MX scale atoms for a [rows, K] e4m3 matrix."""
+    return -(-rows // 128) * (K // 128) * 512
+
+
+def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, *, epi: int = EPI_BF16,
+            out: torch.Tensor | None = None, out_sf: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None):
+    """D = A . B^T with UE8M0 block scales on the tcgen05 block-scaled MMA.
+
+    A [M, K], B [N, K] e4m3; sfa / sfb their scale bytes in the MX atom
+    layout (quail_b200.ops.quant.pack_sf_atoms). EPI_SWIGLU_FP8 returns
+    (e4m3 [M, N/2], its scale bytes) ready to be the next GEMM's A.
+    """
+    C = native()
+    M, N = a.shape[0], b.shape[0]
+    _count()
+    if epi == EPI_SWIGLU_FP8:
+        if out is None:
+            out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
+        if out_sf is None:
+            out_sf = torch.empty(sf_bytes(M, N // 2), dtype=torch.uint8, device=a.device)
+        C.gemm_mx(a, sfa, b, sfb, epi, out, out_sf, None)
+        return out, out_sf
+    if out is None:
+        out = torch.empty(M, N // 2 if epi == EPI_SWIGLU_BF16 else N, dtype=torch.bfloat16, device=a.device)
+    C.gemm_mx(a, sfa, b, sfb, epi, out, None, residual)
+    return out
+
+
+def rmsnorm_quant_mx(x: torch.Tensor, w: torch.Tensor, eps: float, *, out=None, out_sf=None, rows=None):
+    """RMSNorm -> (e4m3 [T, H], UE8M0 scale bytes, one per 32 columns)."""
+    T = x.shape[0] if rows is None else rows
+    H = x.shape[1]
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
+    if out_sf is None:
+        out_sf = torch.empty(sf_bytes(T, H), dtype=torch.uint8, device=x.device)
+    _count()
+    native().rmsnorm_quant_mx(x, w, eps, out, out_sf, T)
+    return out, out_sf
+
+
+def quant_rows_mx(x: torch.Tensor, *, swiglu: bool = False, rows: int | None = None):
+    T = x.shape[0] if rows is None else rows
+    K = x.shape[1] // 2 if swiglu else x.shape[1]
+    y = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=x.device)
+    sf = torch.empty(sf_bytes(T, K), dtype=torch.uint8, device=x.device)
+    _count()
+    native().quant_rows_mx(x, swiglu, y, sf, T)
+    return y, sf
+
+
 def embed_gather(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=torch.bfloat16, device=ids.device)
@@ -133,9 +186,21 @@ def qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, k_cache,
 
 
 def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale: float, *,
-                      fp8_out: bool = False, out=None, out_scale=None):
-    """Segmented paged attention (see csrc/attention.cu) -> [T, QH*128]."""
+                      fp8_out: bool = False, mx: bool = False, out=None, out_scale=None):
+    """Segmented paged attention (see csrc/attention.cu) -> [T, QH*128].
+
+    fp8_out: e4m3 + one fp32 scale per (token, head) [QH, T]; with mx, e4m3 +
+    UE8M0 scale bytes per 32 values in the MX atom layout (the o_proj A input).
+    """
     T, QH = q.shape[0], q.shape[1]
+    if fp8_out and mx:
+        if out is None:
+            out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
+        if out_scale is None:
+            out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+        _count()
+        native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out, out_scale)
+        return out, out_scale
     if fp8_out:
         if out is None:
             out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)

@@ -73,3 +73,94 @@ def interleave_gate_up(w: torch.Tensor, scale: torch.Tensor | None = None, block
     src_group = torch.where(groups % 2 == 0, groups // 2, inter // 64 + groups // 2)
     src_block = (src_group * 64) // block
     return out.contiguous(), scale[src_block].contiguous()
+
+
+# ---------------------------------------------------------------- MX (UE8M0) formats
+#
+# The tcgen05 block-scaled MMA (kind::mxf8f6f4.block_scale) takes one
+# power-of-two scale byte (UE8M0: value 2^(e - 127)) per row and 32-wide K
+# block. The kernels read them in the scale-factor atom layout: per
+# 128-row x 128-K chunk, 512 bytes with row r, K block j at byte
+# (r % 32) * 16 + ((r % 128) // 32) * 4 + j; chunks ordered [row/128][K/128].
+
+def ue8m0_exponent(amax: torch.Tensor) -> torch.Tensor:
+    """Biased exponent of the smallest power of two >= amax / 448 (clamped to [1, 253])."""
+    s = (amax.float().clamp(min=1e-30) / FP8_MAX)
+    bits = s.view(torch.int32)
+    e = (bits >> 23) & 0xFF
+    e = e + ((bits & 0x7FFFFF) != 0).to(torch.int32)
+    return e.clamp(1, 253).to(torch.uint8)
+
+
+def ue8m0_value(e: torch.Tensor) -> torch.Tensor:
+    return torch.exp2(e.float() - 127.0)
+
+
+def pack_sf_atoms(e: torch.Tensor) -> torch.Tensor:
+    """[R, K/32] uint8 exponents -> flat uint8 in the atom layout."""
+    R, KB = e.shape
+    assert KB % 4 == 0
+    Rp = -(-R // 128) * 128
+    ep = torch.zeros(Rp, KB, dtype=torch.uint8, device=e.device)
+    ep[:R] = e
+    x = ep.view(Rp // 128, 4, 32, KB // 4, 4).permute(0, 3, 2, 1, 4)
+    return x.contiguous().view(-1)
+
+
+def unpack_sf_atoms(sf: torch.Tensor, R: int, K: int) -> torch.Tensor:
+    """Inverse of pack_sf_atoms -> [R, K/32] uint8."""
+    KB = K // 32
+    Rp = -(-R // 128) * 128
+    x = sf[:(Rp // 128) * (KB // 4) * 512].view(Rp // 128, KB // 4, 32, 4, 4).permute(0, 3, 2, 1, 4)
+    return x.contiguous().view(Rp, KB)[:R]
+
+
+def quantize_act_mx(x: torch.Tensor, group: int = 32):
+    """[T, K] float -> (e4m3 [T, K], atom-packed UE8M0 bytes), one scale per `group` columns."""
+    T, K = x.shape
+    g = x.float().view(T, K // group, group)
+    e = ue8m0_exponent(g.abs().amax(dim=2))
+    q = (g / ue8m0_value(e)[:, :, None]).clamp(-FP8_MAX, FP8_MAX).view(T, K).to(torch.float8_e4m3fn)
+    e32 = e.repeat_interleave(group // 32, dim=1)
+    return q, pack_sf_atoms(e32)
+
+
+def quantize_weight_mx(w: torch.Tensor, block: int = 128):
+    """[N, K] float -> (e4m3 [N, K], atom-packed UE8M0 bytes) with power-of-two 128x128 block scales."""
+    N, K = w.shape
+    nb = -(-N // block)
+    wp = torch.zeros(nb * block, K, dtype=torch.float32, device=w.device)
+    wp[:N] = w.float()
+    blocks = wp.view(nb, block, K // 128, 128)
+    e = ue8m0_exponent(blocks.abs().amax(dim=(1, 3)))          # [nb, K/128]
+    q = (blocks / ue8m0_value(e)[:, None, :, None]).clamp(-FP8_MAX, FP8_MAX)
+    q = q.view(nb * block, K)[:N].to(torch.float8_e4m3fn)
+    rows = e.repeat_interleave(block, dim=0)[:N].repeat_interleave(4, dim=1)  # [N, K/32]
+    return q.contiguous(), pack_sf_atoms(rows)
+
+
+def requantize_weight_mx(q: torch.Tensor, scale: torch.Tensor, block: int = 128):
+    """HF fp8 weight + fp32 128x128 `weight_scale_inv` -> the MX (power-of-two scale) form."""
+    return quantize_weight_mx(dequantize_weight(q, scale, block), block)
+
+
+def dequantize_mx(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
+    R, K = q.shape
+    e = unpack_sf_atoms(sf, R, K)
+    return q.float() * ue8m0_value(e).repeat_interleave(32, dim=1)
+
+
+def interleave_gate_up_mx(w: torch.Tensor, block: int = 128):
+    """fp32/bf16 [2I, K] gate_up -> MX-quantized, rows interleaved for the SwiGLU epilogue.
+
+    Quantizes gate and up separately with 128x128 blocks, then reorders the
+    rows (64-row groups g0 u0 g1 u1 ...) together with their scale rows.
+    """
+    I2, K = w.shape
+    inter = I2 // 2
+    qg, sg = quantize_weight_mx(w[:inter], block)
+    qu, su = quantize_weight_mx(w[inter:], block)
+    eg, eu = unpack_sf_atoms(sg, inter, K), unpack_sf_atoms(su, inter, K)
+    q = torch.stack([qg.view(inter // 64, 64, K), qu.view(inter // 64, 64, K)], dim=1).reshape(I2, K)
+    e = torch.stack([eg.view(inter // 64, 64, -1), eu.view(inter // 64, 64, -1)], dim=1).reshape(I2, -1)
+    return q.contiguous(), pack_sf_atoms(e)

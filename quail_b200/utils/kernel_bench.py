@@ -66,6 +66,17 @@ def run(model: str, T: int, iters: int = 10) -> list[dict]:
                 ms = _timeit(lambda: ops.gemm(a8, b8, sa=sa, sb=sb, epi=epi, out=dout), iters, flush=flush)
             row["ours_ms"] = ms
             row["ours_tflops"] = flops / ms / 1e9
+            # MX (UE8M0) block-scaled path
+            a8m, sfa = ops.quantize_act_mx(a)
+            if name == "gate_up":
+                b8m, sfb = ops.interleave_gate_up_mx(b)
+                ms_mx = _timeit(lambda: ops.gemm_mx(a8m, sfa, b8m, sfb, epi=ops.EPI_SWIGLU_FP8), iters, flush=flush)
+            else:
+                b8m, sfb = ops.quantize_weight_mx(b)
+                dmx = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                ms_mx = _timeit(lambda: ops.gemm_mx(a8m, sfa, b8m, sfb, out=dmx), iters, flush=flush)
+            row["mx_ms"] = ms_mx
+            row["mx_tflops"] = flops / ms_mx / 1e9
             try:
                 one = torch.ones((), device=dev)
                 bt = b8.t()

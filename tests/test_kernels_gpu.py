@@ -196,3 +196,67 @@ def test_embed_gather():
     ids = torch.randint(0, V, (77,), device=DEV, dtype=torch.int32)
     out = ops.embed_gather(ids, table)
     assert torch.equal(out, table[ids.long()])
+
+
+# ---------------------------------------------------------------- MX (UE8M0) block-scaled path
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 512, 1024), (2048, 6144, 2560), (33, 2560, 9728),
+                                   (1000, 384, 640)])
+def test_gemm_mx(M, N, K):
+    a8, sfa = ops.quantize_act_mx(torch.randn(M, K, device=DEV))
+    b8, sfb = ops.quantize_weight_mx(torch.randn(N, K, device=DEV) * 0.02)
+    d = ops.gemm_mx(a8, sfa, b8, sfb)
+    want = ops.dequantize_mx(a8, sfa) @ ops.dequantize_mx(b8, sfb).t()
+    assert rel_err(d, want) < 5e-3
+
+
+def test_gemm_mx_residual():
+    M, N, K = 500, 2560, 1024
+    a8, sfa = ops.quantize_act_mx(torch.randn(M, K, device=DEV))
+    b8, sfb = ops.quantize_weight_mx(torch.randn(N, K, device=DEV) * 0.02)
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    want = ops.dequantize_mx(a8, sfa) @ ops.dequantize_mx(b8, sfb).t() + res.float()
+    ops.gemm_mx(a8, sfa, b8, sfb, epi=ops.EPI_RESIDUAL, out=res, residual=res)
+    assert rel_err(res, want) < 5e-3
+
+
+def test_gemm_mx_swiglu_fp8_feeds_the_next_gemm():
+    M, inter, K = 700, 1024, 1024
+    x8, sx = ops.quantize_act_mx(torch.randn(M, K, device=DEV))
+    w = torch.randn(2 * inter, K, device=DEV) * 0.05
+    wi, swi = ops.interleave_gate_up_mx(w)
+    y8, ysf = ops.gemm_mx(x8, sx, wi, swi, epi=ops.EPI_SWIGLU_FP8)
+    wq_g, sg = ops.quantize_weight_mx(w[:inter])
+    wq_u, su = ops.quantize_weight_mx(w[inter:])
+    xd = ops.dequantize_mx(x8, sx)
+    want = ref.silu_mul(xd @ ops.dequantize_mx(wq_g, sg).t(), xd @ ops.dequantize_mx(wq_u, su).t())
+    assert rel_err(ops.dequantize_mx(y8, ysf), want) < 4e-2
+    # the output and its scale bytes are a valid A operand
+    wd8, sdn = ops.quantize_weight_mx(torch.randn(512, inter, device=DEV) * 0.02)
+    d = ops.gemm_mx(y8, ysf, wd8, sdn)
+    assert rel_err(d, ops.dequantize_mx(y8, ysf) @ ops.dequantize_mx(wd8, sdn).t()) < 5e-3
+
+
+@pytest.mark.parametrize("H", [1024, 2560, 5120])
+def test_rmsnorm_quant_mx(H):
+    T = 333
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).bfloat16()
+    y8, sf = ops.rmsnorm_quant_mx(x, w, 1e-6)
+    assert rel_err(ops.dequantize_mx(y8, sf), ref.rmsnorm(x, w, 1e-6)) < 4e-2
+
+
+def test_quant_rows_mx_swiglu():
+    T, K = 129, 768
+    x = torch.randn(T, 2 * K, device=DEV).bfloat16()
+    y8, sf = ops.quant_rows_mx(x, swiglu=True)
+    assert rel_err(ops.dequantize_mx(y8, sf), ref.silu_mul(x[:, :K], x[:, K:])) < 4e-2
+
+
+def test_prefill_attention_mx_output():
+    specs = [(100, [48, 100]), (7, [48, 7]), (64, [48, 300, 64]), (130, [48, 130])]
+    q, kc, vc, seqs, pl = _segmented_case(128, specs)
+    tiles = ref.attention_tiles(seqs)
+    scale = ref.softmax_scale(128)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    o8, sf = ops.prefill_attention(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale, fp8_out=True, mx=True)
+    assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
