@@ -18,8 +18,8 @@
 // call over the parent's pages + LSE merge) and "unified" paths
 // (quail/backends/quail/executor/attention.py:1395-1573) in one kernel.
 //
-// Tiles: one CTA = 64 query rows of one sequence x one q head, 4 warps of 16
-// rows; KV tiles of 64 rows double-buffered with cp.async; QK^T and PV on
+// Tiles: one CTA = 32 query tokens of one sequence x up to 4 q heads of one
+// GQA group (two warps of 16 rows per head); KV tiles of 64 rows double-buffered with cp.async; QK^T and PV on
 // mma.sync m16n8k16 bf16 with fp32 accumulators and an online softmax in
 // registers. Output is bf16 or e4m3 + one fp32 scale per (token, head) = the
 // 1x128 A-scale layout [QH, lds] that the fp8 o_proj GEMM reads.
@@ -89,24 +89,29 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
 
 // MODE: 0 bf16 out; 1 e4m3 + fp32 scale per (token, head) [QH, ldos];
 // 2 e4m3 + UE8M0 bytes per 32 values in the MX scale atom layout (K = QH*128)
-template <int MODE>
-__global__ void __launch_bounds__(128)
+//
+// One CTA = 32 query tokens of one sequence x HPB q heads of one GQA group
+// (HPB * 32 rows, two warps of 16 rows per head): the group's K/V tiles are
+// loaded once into shared memory and read by every head of the group.
+template <int MODE, int HPB>
+__global__ void __launch_bounds__(HPB * 64)
     prefill_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
                         const __nv_bfloat16* __restrict__ vc, const int* __restrict__ seqs,
                         const int* __restrict__ tiles, const int* __restrict__ page_list, int page_tokens,
                         int QH, int KH, float scale_log2, __nv_bfloat16* __restrict__ o, int ldo,
                         uint8_t* __restrict__ o8, float* __restrict__ os, int ldos) {
-  constexpr int D = 128, BQ = 64, BKV = 64;
+  constexpr int D = 128, TPB = 32, ROWS = HPB * TPB, BKV = 64, NT = HPB * 64;
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK0 = sQ + BQ * 256;
+  const uint32_t sK0 = sQ + ROWS * 256;
   const uint32_t sV0 = sK0 + 2 * BKV * 256;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int seq = tiles[blockIdx.x * 2], q0 = tiles[blockIdx.x * 2 + 1];
-  const int head = blockIdx.y;
-  const int kvh = head / (QH / KH);
+  const int head0 = blockIdx.y * HPB;
+  const int head = head0 + (warp >> 1);
+  const int kvh = head0 / (QH / KH);
   const int* sd = seqs + seq * kSeqDescInts;
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
   int seg_len[kMaxSeg], seg_off[kMaxSeg];
@@ -116,8 +121,8 @@ __global__ void __launch_bounds__(128)
     seg_off[i] = i < nseg ? sd[8 + i] : 0;
   }
   const int own_len = seg_len[nseg - 1];
-  const int rows_here = min(BQ, q_len - q0);
-  // own-segment position of this tile's last query row
+  const int rows_here = min(TPB, q_len - q0);
+  // own-segment position of this tile's last query token
   const int max_pos = own_len - q_len + q0 + rows_here - 1;
   int seg_tiles[kMaxSeg];
 #pragma unroll
@@ -132,11 +137,13 @@ __global__ void __launch_bounds__(128)
 
   const size_t row_stride = (size_t)KH * D;  // elements between consecutive token slots
 
-  // ---- Q tile
-  for (int it = 0; it < 8; ++it) {
-    const int idx = it * 128 + tid, r = idx >> 4, c = idx & 15;
-    const bool valid = r < rows_here;
-    const __nv_bfloat16* src = q + ((size_t)(q_start + q0 + (valid ? r : 0)) * QH + head) * D + c * 8;
+  // ---- Q tile: smem row r = head offset (r / 32) x token (r % 32)
+#pragma unroll
+  for (int it = 0; it < ROWS * 16 / NT; ++it) {
+    const int idx = it * NT + tid, r = idx >> 4, c = idx & 15;
+    const int tok = r & (TPB - 1), hh = r / TPB;
+    const bool valid = tok < rows_here;
+    const __nv_bfloat16* src = q + ((size_t)(q_start + q0 + (valid ? tok : 0)) * QH + head0 + hh) * D + c * 8;
     cp_async16(swz(sQ, r, c), src, valid);
   }
   cp_async_commit();
@@ -158,8 +165,8 @@ __global__ void __launch_bounds__(128)
       }
     const uint32_t kb = sK0 + buf * BKV * 256, vb = sV0 + buf * BKV * 256;
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int idx = it * 128 + tid, r = idx >> 4, c = idx & 15;
+    for (int it = 0; it < BKV * 16 / NT; ++it) {
+      const int idx = it * NT + tid, r = idx >> 4, c = idx & 15;
       const int j = tt * BKV + r;
       const bool valid = j < slen;
       size_t off = 0;
@@ -176,8 +183,8 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int i = 0; i < 16; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-  // own-segment positions of this thread's two rows
-  const int rbase = warp * 16 + g;
+  // token offsets (within the 32-token tile) of this thread's two rows
+  const int rbase = (warp & 1) * 16 + g;
   const int pos0 = own_len - q_len + q0 + rbase, pos1 = pos0 + 8;
 
   if (total_tiles > 0) load_kv(0, 0);
@@ -396,8 +403,38 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+template <int MODE, int HPB>
+static void launch_attn(dim3 grid, cudaStream_t st, const __nv_bfloat16* qp, const __nv_bfloat16* kp,
+                        const __nv_bfloat16* vp, const int* seqs, const int* tiles, const int* pl, int P, int QH,
+                        int KH, float sl2, __nv_bfloat16* o, int ldo, uint8_t* o8, float* os, int ldos) {
+  constexpr int smem = HPB * 32 * 256 + 2 * 2 * 64 * 256;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<MODE, HPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem));
+    configured = true;
+  }
+  prefill_attn_kernel<MODE, HPB><<<grid, HPB * 64, smem, st>>>(qp, kp, vp, seqs, tiles, pl, P, QH, KH, sl2, o, ldo, o8,
+                                                               os, ldos);
+}
+
+template <int MODE>
+static void launch_attn_hpb(int hpb, int n_tiles, int QH, cudaStream_t st, const __nv_bfloat16* qp,
+                            const __nv_bfloat16* kp, const __nv_bfloat16* vp, const int* seqs, const int* tiles,
+                            const int* pl, int P, int KH, float sl2, __nv_bfloat16* o, int ldo, uint8_t* o8,
+                            float* os, int ldos) {
+  dim3 grid(n_tiles, QH / hpb);
+  if (hpb == 4)
+    launch_attn<MODE, 4>(grid, st, qp, kp, vp, seqs, tiles, pl, P, QH, KH, sl2, o, ldo, o8, os, ldos);
+  else if (hpb == 2)
+    launch_attn<MODE, 2>(grid, st, qp, kp, vp, seqs, tiles, pl, P, QH, KH, sl2, o, ldo, o8, os, ldos);
+  else
+    launch_attn<MODE, 1>(grid, st, qp, kp, vp, seqs, tiles, pl, P, QH, KH, sl2, o, ldo, o8, os, ldos);
+}
+
 // q: [T, QH, 128] bf16; caches: [pages, P, KH, 128] bf16; seqs: [S, 12] int32;
-// tiles: [n_tiles, 2] int32 (sequence, first query row); page_list: int32.
+// tiles: [n_tiles, 2] int32 (sequence, first query token; 32-token tiles);
+// page_list: int32.
 void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                        const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
                        double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_scale) {
@@ -407,41 +444,40 @@ void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, con
   TORCH_CHECK(seqs.size(1) == kSeqDescInts && seqs.scalar_type() == at::kInt, "seqs: [S, 12] int32");
   const int QH = q.size(1), KH = k_cache.size(2), P = k_cache.size(1);
   TORCH_CHECK(QH % KH == 0, "QH must be a multiple of KH");
+  const int group = QH / KH;
+  // heads per CTA (QB_ATTN_HPB caps it): 4 shares each K/V tile across a whole
+  // GQA group of 4 q heads; measured fastest on Qwen3-4B (88.3 vs 90.3 ms/step at 2)
+  static const int max_hpb = [] {
+    const char* e = getenv("QB_ATTN_HPB");
+    return e ? atoi(e) : 4;
+  }();
+  int hpb = group % 4 == 0 ? 4 : (group % 2 == 0 ? 2 : 1);
+  hpb = std::min(hpb, std::max(max_hpb, 1));
   const int n_tiles = tiles.size(0);
   if (n_tiles == 0) return;
   c10::cuda::CUDAGuard guard(q.get_device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream(q.get_device());
-  dim3 grid(n_tiles, QH);
-  constexpr int smem = 64 * 256 + 2 * 2 * 64 * 256;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
   const float sl2 = (float)(softmax_scale * 1.4426950408889634);
   auto qp = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   auto kp = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
   auto vp = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  const int* sq = seqs.data_ptr<int>();
+  const int* tl = tiles.data_ptr<int>();
+  const int* pl = page_list.data_ptr<int>();
   if (out.scalar_type() == at::kFloat8_e4m3fn && out_scale.has_value() && out_scale->scalar_type() == at::kByte) {
     TORCH_CHECK(out_scale->numel() >= (q.size(0) + 127) / 128 * QH * 512, "MX attention output scale bytes");
-    prefill_attn_kernel<2><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
-                                                   page_list.data_ptr<int>(), P, QH, KH, sl2, nullptr,
-                                                   out.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
-                                                   reinterpret_cast<float*>(out_scale->data_ptr()), 0);
+    launch_attn_hpb<2>(hpb, n_tiles, QH, st, qp, kp, vp, sq, tl, pl, P, KH, sl2, nullptr, out.stride(0),
+                       reinterpret_cast<uint8_t*>(out.data_ptr()), reinterpret_cast<float*>(out_scale->data_ptr()),
+                       0);
   } else if (out.scalar_type() == at::kFloat8_e4m3fn) {
     TORCH_CHECK(out_scale.has_value() && out_scale->size(0) == QH, "fp8 attention output needs [QH, >=T] scales");
-    prefill_attn_kernel<1><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
-                                                   page_list.data_ptr<int>(), P, QH, KH, sl2, nullptr,
-                                                   out.stride(0), reinterpret_cast<uint8_t*>(out.data_ptr()),
-                                                   out_scale->data_ptr<float>(), out_scale->stride(0));
+    launch_attn_hpb<1>(hpb, n_tiles, QH, st, qp, kp, vp, sq, tl, pl, P, KH, sl2, nullptr, out.stride(0),
+                       reinterpret_cast<uint8_t*>(out.data_ptr()), out_scale->data_ptr<float>(),
+                       out_scale->stride(0));
   } else {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "attention output bf16 or e4m3");
-    prefill_attn_kernel<0><<<grid, 128, smem, st>>>(qp, kp, vp, seqs.data_ptr<int>(), tiles.data_ptr<int>(),
-                                                    page_list.data_ptr<int>(), P, QH, KH, sl2,
-                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                    out.stride(0), nullptr, nullptr, 0);
+    launch_attn_hpb<0>(hpb, n_tiles, QH, st, qp, kp, vp, sq, tl, pl, P, KH, sl2,
+                       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), nullptr, nullptr, 0);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -5,7 +5,7 @@ sequences, plus the metadata the kernels read:
 
   ids, positions, slots   [T] int32  token id, absolute position, KV slot (page*P + offset; -1 = none)
   seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
-  tiles                   [n, 2]     (sequence, first query row) per 64-row attention tile
+  tiles                   [n, 2]     (sequence, first query token) per 32-token attention tile
   page_list               [*]        page ids of every segment, segments point into it
   final_rows              [R]        token row whose logits each readout reads
 
@@ -23,7 +23,7 @@ import torch
 
 MAX_SEGMENTS = 4
 SEQ_INTS = 12
-ATTN_BLOCK_Q = 64
+ATTN_BLOCK_Q = 32
 
 
 @dataclass

@@ -79,7 +79,7 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     return out
 
 
-def attention_tiles(seqs: torch.Tensor, block_q: int = 64) -> torch.Tensor:
+def attention_tiles(seqs: torch.Tensor, block_q: int = 32) -> torch.Tensor:
     """[n_tiles, 2] int32 (sequence, first query row) covering every query row."""
     rows = []
     for s in range(seqs.shape[0]):
