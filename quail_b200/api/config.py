@@ -1,0 +1,76 @@
+"""The engine configuration a session runs on.
+
+Same fields as the reference's EngineConfig (quail/api/config.py:21-42):
+`model` and `device` name the weights and the hardware, `gpus` counts model
+copies on one host (1, 2, 4 or 8), `gpu_timing` records a CUDA event pair
+per forward chunk, `canvas_draws` and `attention` are kept for API parity.
+Two additions: `weights`, a directory of HF safetensors to load instead of
+random-init weights of the named architecture, and `parallel`, how a model
+larger than one GPU is split ("tp" or "ep") when gpus > 1.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+
+@dataclass(frozen=True)
+class Refusal:
+    reasons: tuple
+    constraint: str
+    needed: float = 1
+    available: float = 0
+    unit: str = ""
+
+
+class RefusalError(RuntimeError):
+    """The planner refuses to run a query or configuration, and says why."""
+
+    def __init__(self, refusal: Refusal):
+        self.refusal = refusal
+        super().__init__("; ".join(refusal.reasons))
+
+
+DEVICES = ("b200", "cpu")
+
+
+@dataclass(frozen=True, kw_only=True)
+class EngineConfig:
+    model: str
+    device: str
+    gpus: int = 1
+    backend: str = "quail"
+    gpu_timing: bool = False
+    canvas_draws: int = 4
+    attention: str | None = None
+    weights: str | None = None
+    parallel: str = "dp"
+    chunk_tokens: int | None = None
+    seed: int = 0
+    extra: dict = field(default_factory=dict)
+
+
+def resolve_model(name: str):
+    from quail_b200.models.config import MODEL_CONFIGS
+    if name in MODEL_CONFIGS:
+        return MODEL_CONFIGS[name]
+    return Refusal(reasons=(f"unknown model {name!r}; registered models: {sorted(MODEL_CONFIGS)}",),
+                   constraint="unknown_model", needed=1, available=0, unit="specs")
+
+
+def check_config(config: EngineConfig):
+    model = resolve_model(config.model)
+    if isinstance(model, Refusal):
+        raise RefusalError(model)
+    if config.device not in DEVICES:
+        raise RefusalError(Refusal(reasons=(f"unknown device {config.device!r}; devices: {list(DEVICES)}",),
+                                   constraint="unknown_device"))
+    if config.backend != "quail":
+        raise RefusalError(Refusal(reasons=(f"unknown backend {config.backend!r}",), constraint="unknown_backend"))
+    if config.gpus not in (1, 2, 4, 8):
+        raise RefusalError(Refusal(reasons=(f"gpus must be 1, 2, 4 or 8, not {config.gpus}",),
+                                   constraint="unsupported_backend_configuration"))
+    if config.attention not in (None, "tree", "unified"):
+        raise RefusalError(Refusal(reasons=("attention is 'tree', 'unified' or None",),
+                                   constraint="unsupported_backend_configuration"))
+    return model

@@ -1,0 +1,178 @@
+"""The model engine behind a session: one model replica per GPU.
+
+`ModelEngine` owns a model replica, its paged KV arena and a stage executor,
+and runs *regions*: one table's documents with a chain of AI calls. It
+tokenizes the prompt pieces, deduplicates identical documents (each is read
+once), retains the LM-head rows every call reads (TRUE/FALSE spellings and
+label tokens), runs the chain and turns readouts into SQL values.
+
+device="b200" runs the sm_100a kernel pipeline on the current GPU;
+device="cpu" runs the fp32 PyTorch statement of the same model (the CPU
+plumbing configuration of the benchmark). With gpus > 1 the session hands
+each replica a shard of the documents (`quail_b200.runtime.workers`).
+
+Reference: quail/backends/quail/worker.py (LoadedGpu: load weights, size
+the arena, bind answer rows), executor/runtime.py and executor/region.py.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from quail_b200.api import prompts as P
+from quail_b200.api.config import EngineConfig, check_config
+from quail_b200.api.tokenizer import load_tokenizer
+
+
+@dataclass
+class CallSpec:
+    """One AI call as text: what follows the document, and how to read the answer."""
+
+    kind: str                 # filter | score | classify | map | extract
+    tail: str                 # text after the document (question block + answer cue + turn suffix)
+    name: str
+    labels: list = field(default_factory=list)
+    max_tokens: int = 256
+    probabilities: bool = False
+
+
+@dataclass
+class RegionOutput:
+    values: list              # per input row: dict call name -> value
+    stats: dict
+
+
+class ModelEngine:
+    def __init__(self, config: EngineConfig, device_index: int = 0, pages: int | None = None):
+        self.config = config
+        self.cfg = check_config(config)
+        self.on_gpu = config.device != "cpu"
+        if self.on_gpu:
+            if not torch.cuda.is_available():
+                raise RuntimeError(f"device {config.device!r} needs a CUDA GPU; use device='cpu' to run on the host")
+            self.device = torch.device("cuda", device_index)
+            torch.cuda.set_device(self.device)
+        else:
+            self.device = torch.device("cpu")
+        self.tokenizer = load_tokenizer(config.weights, self.cfg.vocab)
+        from quail_b200.planner.budgets import Budgets
+        self.budgets = Budgets.for_model(self.cfg, config.device, gpus=1)
+        self.chunk_tokens = config.chunk_tokens or self.budgets.chunk_tokens
+        self._build(pages)
+
+    # ------------------------------------------------------------ model
+    def _checkpoint(self):
+        from quail_b200.models.weights import load_checkpoint, random_checkpoint
+        if self.config.weights:
+            return load_checkpoint(self.config.weights, device=self.device)
+        if self.on_gpu:
+            from quail_b200.models.build import random_checkpoint_on
+            return random_checkpoint_on(self.cfg, self.device, seed=self.config.seed)
+        return random_checkpoint(self.cfg, seed=self.config.seed, dtype=torch.float32)
+
+    def _build(self, pages: int | None):
+        from quail_b200.engine.arena import KVArena
+        from quail_b200.engine.stage_executor import StageExecutor
+        ckpt = self._checkpoint()
+        if self.on_gpu:
+            from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights
+            self.model = Qwen3Pipeline(self.cfg, Qwen3Weights(self.cfg, ckpt, self.device))
+            page_tokens, dtype = 128, torch.bfloat16
+        else:
+            from quail_b200.models.qwen3 import Qwen3Reference
+            self.model = Qwen3Reference(self.cfg, ckpt, device="cpu")
+            page_tokens, dtype = 16, torch.float32
+        del ckpt
+        n_pages = pages or self.budgets.arena_pages(page_tokens)
+        self.arena = KVArena(self.cfg.layers, n_pages, page_tokens, self.cfg.num_kv_heads, self.cfg.head_dim,
+                             device=self.device, dtype=dtype)
+        self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
+                                      gpu_timing=self.config.gpu_timing)
+
+    def _set_answer_rows(self, ids):
+        if self.on_gpu:
+            self.model.w.set_answer_rows(ids)
+        else:
+            self.model.set_answer_rows(ids)
+
+    # ------------------------------------------------------------ regions
+    def tokenize_doc(self, doc) -> np.ndarray:
+        if isinstance(doc, np.ndarray):
+            return doc.astype(np.int32)
+        if isinstance(doc, (list, tuple)) and (not doc or isinstance(doc[0], (int, np.integer))):
+            return np.asarray(doc, dtype=np.int32)
+        return self.tokenizer.encode("" if doc is None else str(doc))
+
+    def run_region(self, preamble: str, docs: list, calls: list[CallSpec]) -> RegionOutput:
+        from quail_b200.engine.region import Call, RegionRun
+        tok = self.tokenizer
+        # one read per distinct document
+        keys, uniq, where = {}, [], []
+        for d in docs:
+            t = self.tokenize_doc(d)
+            k = t.tobytes()
+            if k not in keys:
+                keys[k] = len(uniq)
+                uniq.append(t)
+            where.append(keys[k])
+        true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
+        false_ids = tok.answer_ids(P.FALSE_SPELLINGS)
+        both = set(true_ids) & set(false_ids)
+        true_ids = [i for i in true_ids if i not in both]
+        false_ids = [i for i in false_ids if i not in both]
+        answer: list[int] = []
+
+        def col(i: int) -> int:
+            if i not in answer:
+                answer.append(i)
+            return answer.index(i)
+
+        rcalls = []
+        for c in calls:
+            rc = Call(kind=c.kind, suffix=tok.encode(c.tail), name=c.name, max_tokens=c.max_tokens,
+                      stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities)
+            if c.kind in ("filter", "score"):
+                rc.true_cols = [col(i) for i in true_ids]
+                rc.false_cols = [col(i) for i in false_ids]
+            elif c.kind == "classify":
+                for label in c.labels:
+                    ids = tok.encode(str(label))
+                    if len(ids) == 0:
+                        raise ValueError("an empty classification label")
+                    rc.labels.append(ids)
+                    rc.label_cols.append([col(int(i)) for i in ids])
+            rcalls.append(rc)
+        if not answer:
+            answer = [0]
+        self._set_answer_rows(answer)
+        ex = self.executor
+        passes0, tok0 = ex.stats.passes, ex.stats.tokens
+        run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer))
+        results = run.run()
+        if self.on_gpu:
+            from quail_b200 import ops
+            err = ops.read_and_clear_error(self.device.index)
+            if err:
+                raise RuntimeError(f"a kernel's bounded wait ran out (code {err})")
+        values = []
+        for u in where:
+            v = dict(results[u].values)
+            for c in calls:
+                if c.kind in ("map", "extract") and c.name in v:
+                    v[c.name] = tok.decode(v[c.name])
+                if c.kind == "classify" and c.name in v:
+                    v[c.name] = c.labels[v[c.name]]
+            values.append(v)
+        stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
+                 "documents": len(uniq), "rows": len(docs), "asked": run.asked}
+        return RegionOutput(values=values, stats=stats)
+
+    def close(self):
+        self.executor = None
+        self.arena = None
+        self.model = None
+        if self.on_gpu:
+            torch.cuda.empty_cache()

@@ -1,13 +1,174 @@
-"""Session entry points (filled in by the SQL front end)."""
+"""Session, Query and QueryResult: the public query API.
+
+    config = EngineConfig(model="qwen3-4b-fp8", device="b200")
+    with Session(config=config) as session:
+        session.register("reviews", DocumentProvider.from_table(reviews, id_col="id"))
+        table = session.sql("SELECT r.id FROM reviews r WHERE AI.IF(PROMPT('... {0}', r.body))").collect()
+
+Same surface as the reference (quail/api/session.py:22-232, query.py:102-333,
+execution/result.py:312-439): register / register_parquet / register_json /
+register_csv, sql() returning a Query with run / collect / execute_stream /
+explain / plan, and a QueryResult holding the table, a report of the model
+work (fresh tokens, documents, passes, wall time) and the plan text. With
+`endpoint=` the session talks to a Quail server instead
+(quail_b200.server.client).
+"""
 
 from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import pyarrow as pa
+
+from quail_b200.api.config import EngineConfig, check_config
+from quail_b200.catalog.providers import ArrowDatasetProvider, as_provider
+
+
+@dataclass
+class QueryResult:
+    table: pa.Table
+    report: dict = field(default_factory=dict)
+    plan: str = ""
+
+    def collect(self) -> pa.Table:
+        return self.table
+
+    def explain(self) -> str:
+        return self.plan
+
+    def __repr__(self) -> str:
+        return f"QueryResult({self.table.num_rows} rows, {self.report.get('wall_s', 0):.3f} s)"
+
+
+class Query:
+    def __init__(self, session: "Session", text: str, dialect: str = "snowflake"):
+        from quail_b200.sql.executor import parse
+        self.session = session
+        self.text = text
+        self.dialect = dialect
+        self.tree = parse(text)  # syntax errors surface here, before any model work
+
+    def plan(self):
+        from quail_b200.planner.plan import plan_query
+        return plan_query(self.tree, self.session)
+
+    def explain(self, *, verbose: bool = False, analyze: bool = False) -> str:
+        plan = self.plan()
+        text = plan.explain(verbose=verbose)
+        if analyze:
+            result = self.run()
+            text += "\n" + plan.explain_measured(result.report)
+        return text
+
+    def run(self) -> QueryResult:
+        from quail_b200.sql.executor import Executor
+        s = self.session
+        if s._remote is not None:
+            return s._remote.run(self.text)
+        t0 = time.perf_counter()
+        engine = s.engine() if s._needs_model(self.tree) else None
+        boot = time.perf_counter() - t0
+        ex = Executor(s.catalog, engine, settings=s.settings)
+        t1 = time.perf_counter()
+        if self.tree.get("type") == "set":
+            s.settings[self.tree["name"]] = self.tree["value"].get("value")
+            table = pa.table({"ok": [True]})
+        else:
+            table = ex.run(self.tree if self.tree.get("type") != "explain" else self.tree["query"])
+        wall = time.perf_counter() - t1
+        rep = dict(ex.report)
+        rep.update(wall_s=wall, boot_s=boot, output_rows=table.num_rows)
+        rep["documents_per_second"] = rep["evaluated_documents"] / wall if wall > 0 else 0.0
+        return QueryResult(table=table, report=rep, plan=self.plan().explain())
+
+    def collect(self, limit: int | None = None) -> pa.Table:
+        t = self.run().table
+        return t if limit is None else t.slice(0, limit)
+
+    def execute_stream(self, batch_rows: int = 65_536, limit: int | None = None):
+        t = self.collect(limit)
+        return pa.RecordBatchReader.from_batches(t.schema, t.to_batches(max_chunksize=batch_rows))
+
+    def submit(self, **options):
+        if self.session._remote is None:
+            raise RuntimeError("submit() sends a query to a Quail server; this session has no endpoint")
+        return self.session._remote.submit(self.text, **options)
+
+
+class Session:
+    def __init__(self, config: EngineConfig, *, tokenizer=None, registry=None, endpoint: str | None = None):
+        self.config = config
+        self.model_cfg = check_config(config)
+        self.catalog: dict = {}
+        self.settings: dict = {}
+        self.tokenizer_path = tokenizer
+        self.registry = registry
+        self._engine = None
+        self._remote = None
+        if endpoint is not None:
+            from quail_b200.server.client import RemoteConnection
+            self._remote = RemoteConnection(endpoint)
+
+    # ------------------------------------------------------------ tables
+    def register(self, name: str, provider) -> None:
+        if self._remote is not None:
+            self._remote.register(name, provider)
+            return
+        self.catalog[name] = as_provider(provider)
+
+    def register_parquet(self, name: str, path: str) -> None:
+        self.register(name, ArrowDatasetProvider(path, "parquet"))
+
+    def register_csv(self, name: str, path: str) -> None:
+        self.register(name, ArrowDatasetProvider(path, "csv"))
+
+    def register_json(self, name: str, path: str) -> None:
+        self.register(name, ArrowDatasetProvider(path, "json"))
+
+    def deregister(self, name: str) -> None:
+        self.catalog.pop(name, None)
+
+    # ------------------------------------------------------------ queries
+    def sql(self, text: str, dialect: str = "snowflake") -> Query:
+        return Query(self, text, dialect)
+
+    def _needs_model(self, tree) -> bool:
+        from quail_b200.sql.executor import has_model_call
+        return has_model_call(tree)
+
+    def engine(self):
+        """The model engine (started on first use: weights loaded, arena sized)."""
+        if self._engine is None:
+            if self.config.gpus > 1:
+                from quail_b200.runtime.workers import WorkerPool
+                self._engine = WorkerPool(self.config)
+            else:
+                from quail_b200.api.engine import ModelEngine
+                self._engine = ModelEngine(self.config)
+        return self._engine
+
+    def close(self) -> None:
+        if self._engine is not None:
+            self._engine.close()
+            self._engine = None
+        if self._remote is not None:
+            self._remote.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def run_filter_query(pipe, arena, workload, *, chunk_tokens: int = 16384, name: str = "if"):
     """Run `SELECT ... WHERE AI.IF(PROMPT(<instruction> {0}, body))` over a token table.
 
     `workload` holds the tokenized template prefix, the question suffix and
-    one body per row. Returns the kept row indices and executor stats.
+    one body per row (the benchmark's synthetic table); this is the region a
+    session runs for that query, on an already loaded replica. Returns the
+    kept row indices and executor stats.
     """
     from quail_b200.engine.region import Call, RegionRun
     from quail_b200.engine.stage_executor import StageExecutor

@@ -1,0 +1,109 @@
+"""Tokenizers: the model's own (HF tokenizer.json) or a self-contained byte-level one.
+
+A model loaded from a checkpoint directory uses the `tokenizer.json` beside
+the weights (byte-level BPE, read by `tokenizers`). Random-init models, and
+the tests, use `ByteTokenizer`: one id per UTF-8 byte plus the chat special
+tokens, so prompts tokenize the same on every machine without downloads.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+
+SPECIALS = ("<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>")
+
+
+class ByteTokenizer:
+    """id = 256 + byte for text; specials at 0..4; answer words get ids of their own."""
+
+    def __init__(self, vocab: int = 151_936):
+        self.vocab = vocab
+        self.special = {s: i for i, s in enumerate(SPECIALS)}
+        self.eos_ids = (self.special["<|im_end|>"], self.special["<|endoftext|>"])
+
+    def encode(self, text: str) -> np.ndarray:
+        out: list[int] = []
+        i, n = 0, len(text)
+        while i < n:
+            if text[i] == "<":
+                for s, sid in self.special.items():
+                    if text.startswith(s, i):
+                        out.append(sid)
+                        i += len(s)
+                        break
+                else:
+                    out.extend(256 + b for b in text[i].encode("utf-8"))
+                    i += 1
+            else:
+                j = text.find("<", i)
+                j = n if j < 0 else j
+                out.extend(256 + b for b in text[i:j].encode("utf-8"))
+                i = j
+        return np.asarray(out, dtype=np.int32)
+
+    def decode(self, ids) -> str:
+        inv = {v: k for k, v in self.special.items()}
+        parts, buf = [], bytearray()
+        for t in ids:
+            t = int(t)
+            if t in inv:
+                if buf:
+                    parts.append(buf.decode("utf-8", errors="replace"))
+                    buf = bytearray()
+                parts.append(inv[t])
+            elif 256 <= t < 512:
+                buf.append(t - 256)
+        if buf:
+            parts.append(buf.decode("utf-8", errors="replace"))
+        return "".join(parts)
+
+    def token_id(self, word: str) -> int | None:
+        ids = self.encode(word)
+        return int(ids[0]) if len(ids) == 1 else None
+
+    def answer_ids(self, spellings) -> list[int]:
+        """First token of each answer spelling (deduplicated, order kept)."""
+        out = []
+        for s in spellings:
+            ids = self.encode(s)
+            if len(ids) and int(ids[0]) not in out:
+                out.append(int(ids[0]))
+        return out
+
+
+class HFTokenizer:
+    """A Hugging Face tokenizer.json (byte-level BPE) through the `tokenizers` library."""
+
+    def __init__(self, path: str):
+        from tokenizers import Tokenizer
+        if os.path.isdir(path):
+            path = os.path.join(path, "tokenizer.json")
+        self.tok = Tokenizer.from_file(path)
+        self.vocab = self.tok.get_vocab_size()
+        ids = [self.tok.token_to_id(s) for s in ("<|im_end|>", "<|endoftext|>")]
+        self.eos_ids = tuple(i for i in ids if i is not None)
+
+    def encode(self, text: str) -> np.ndarray:
+        return np.asarray(self.tok.encode(text, add_special_tokens=False).ids, dtype=np.int32)
+
+    def decode(self, ids) -> str:
+        return self.tok.decode([int(i) for i in ids], skip_special_tokens=False)
+
+    def token_id(self, word: str):
+        return self.tok.token_to_id(word)
+
+    def answer_ids(self, spellings) -> list[int]:
+        out = []
+        for s in spellings:
+            ids = self.encode(s)
+            if len(ids) and int(ids[0]) not in out:
+                out.append(int(ids[0]))
+        return out
+
+
+def load_tokenizer(path: str | None, vocab: int):
+    if path is not None and os.path.exists(path if not os.path.isdir(path) else os.path.join(path, "tokenizer.json")):
+        return HFTokenizer(path)
+    return ByteTokenizer(vocab)

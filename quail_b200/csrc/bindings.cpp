@@ -31,6 +31,8 @@ void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps
                       torch::Tensor& sf, int64_t T);
 void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch::Tensor& sf, int64_t T);
 
+void row_argmax_lse(const torch::Tensor& logits, torch::Tensor& arg, torch::Tensor& lse);
+
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
 
@@ -68,6 +70,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
   m.def("rmsnorm_quant_mx", &qb::rmsnorm_quant_mx);
   m.def("quant_rows_mx", &qb::quant_rows_mx);
+  m.def("row_argmax_lse", &qb::row_argmax_lse);
   m.def("embed_gather", &qb::embed_gather);
   m.def("rmsnorm_quant", &qb::rmsnorm_quant);
   m.def("quant_rows", &qb::quant_rows);

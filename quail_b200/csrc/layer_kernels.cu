@@ -299,6 +299,71 @@ __global__ void final_norm_readout_kernel(const __nv_bfloat16* __restrict__ x, i
   (void)PER;
 }
 
+
+// ---------------------------------------------------------------- full-vocab readout
+// One CTA per row of bf16 logits [R, V]: argmax and log-sum-exp over the
+// vocabulary (greedy decoding for AI.MAP / AI.EXTRACT, normalized label
+// log-probabilities for AI.CLASSIFY). Online max/sum per thread, then a
+// block reduction.
+__global__ void row_argmax_lse_kernel(const __nv_bfloat16* __restrict__ logits, int ld, int V,
+                                      int* __restrict__ arg, float* __restrict__ lse) {
+  const int r = blockIdx.x;
+  const __nv_bfloat16* row = logits + (size_t)r * ld;
+  float m = -INFINITY, s = 0.f;
+  int am = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = __bfloat162float(row[i]);
+    if (x > m) {
+      s = s * __expf(m - x) + 1.f;
+      m = x;
+      am = i;
+    } else {
+      s += __expf(x - m);
+    }
+  }
+  __shared__ float sm[32], ss[32];
+  __shared__ int sa[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const int a2 = __shfl_xor_sync(0xffffffffu, am, o);
+    const float mn = fmaxf(m, m2);
+    const float sn = (m == -INFINITY ? 0.f : s * __expf(m - mn)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mn));
+    if (m2 > m || (m2 == m && a2 < am)) am = a2;
+    m = mn;
+    s = sn;
+  }
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+    sa[warp] = am;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+    am = lane < nw ? sa[lane] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const int a2 = __shfl_xor_sync(0xffffffffu, am, o);
+      const float mn = fmaxf(m, m2);
+      const float sn = (m == -INFINITY ? 0.f : s * __expf(m - mn)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mn));
+      if (m2 > m || (m2 == m && a2 < am)) am = a2;
+      m = mn;
+      s = sn;
+    }
+    if (lane == 0) {
+      arg[r] = am;
+      lse[r] = m + __logf(s);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 static cudaStream_t cur_stream(const torch::Tensor& t) {
@@ -481,6 +546,18 @@ void final_norm_readout(const torch::Tensor& x, const torch::Tensor& rows, const
   QB_RO_CASE(5120)
 #undef QB_RO_CASE
   TORCH_CHECK(false, "final_norm_readout: unsupported hidden size ", H);
+}
+
+void row_argmax_lse(const torch::Tensor& logits, torch::Tensor& arg, torch::Tensor& lse) {
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1, "row_argmax_lse: bf16 rows");
+  TORCH_CHECK(arg.scalar_type() == at::kInt && lse.scalar_type() == at::kFloat, "row_argmax_lse outputs");
+  const int R = logits.size(0), V = logits.size(1);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard g(logits.get_device());
+  row_argmax_lse_kernel<<<R, 512, 0, cur_stream(logits)>>>(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()),
+                                                           logits.stride(0), V, arg.data_ptr<int>(),
+                                                           lse.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace qb

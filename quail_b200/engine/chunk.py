@@ -37,6 +37,8 @@ class SeqSpec:
     pos_start: int         # absolute position of tokens[0]
     readout: bool = False  # read the logits of the last new token
     tag: object = None
+    readout_rows: tuple | None = None  # offsets of new tokens to read (default: the last one)
+    full: bool = False     # also read argmax and log-sum-exp over the whole vocabulary
 
 
 @dataclass
@@ -53,6 +55,7 @@ class Chunk:
     num_seqs: int = 0
     host: dict | None = None   # numpy copies (tests, CPU reference)
     upload_bytes: int = 0
+    full_readout: bool = False  # readout rows also need full-vocabulary argmax / log-sum-exp
 
 
 class ChunkPacker:
@@ -104,7 +107,9 @@ class ChunkPacker:
             page_list.extend(self.pool.pages_of(s.own_key)[:npg])
             tiles.extend((si, q0) for q0 in range(0, n, ATTN_BLOCK_Q))
             if s.readout:
-                final_rows.append(q + n - 1)
+                offs = s.readout_rows if s.readout_rows is not None else (n - 1,)
+                for o in offs:
+                    final_rows.append(q + o)
                 tags.append(s.tag)
             q += n
         tiles_a = np.asarray(tiles, dtype=np.int32).reshape(-1, 2)
@@ -124,7 +129,7 @@ class ChunkPacker:
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
                      final_rows=views[6], readout_tags=tags, num_seqs=len(specs), host=host,
-                     upload_bytes=int(flat.nbytes))
+                     upload_bytes=int(flat.nbytes), full_readout=any(s.full and s.readout for s in specs))
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:
         src = torch.from_numpy(flat)

@@ -2,17 +2,31 @@
 
 A region holds the documents (token ids) and an ordered chain of calls; a
 call after a filter runs only on the rows that filter kept (the reference's
-guards: quail/backends/quail/executor/region.py, model_operator.py,
-operators/filter.py, score.py). For every row:
+guards: quail/backends/quail/executor/region.py, model_operator.py and the
+operators in operators/filter.py, score.py, classify.py, map.py). For each
+row:
 
-  first call   one task: reads the shared instruction prefix, writes
-               document + question, reads out the last token.
-  next calls   one task each: reads the prefix and the first call's
-               document tokens (borrowed pages), writes only the question.
+  first call   one task: reads the shared instruction prefix, writes the
+               document + the call's question, reads out the last token.
+  next calls   one task each: reads the prefix and the first task's document
+               tokens (borrowed pages), writes only its own question.
+               Consecutive non-filter calls run side by side; a filter
+               waits for the calls before it.
+
+Readouts:
+  filter    max logit over the TRUE spellings > max over FALSE
+  score     sigmoid(max TRUE - max FALSE)
+  classify  sum over each label's tokens of log p(token | context): the
+            question's last row gives log p(first token) against the
+            full-vocabulary log-sum-exp; a label of n tokens adds one
+            continuation sequence of its first n-1 tokens read out at every
+            position (the reference's label trie, label_stages.py)
+  map       greedy decoding: each step appends the argmax token to the
+            question's own pages until a stop token or max_tokens
+            (map_decoder.py); extract decodes the same way after the phrase cue
 
 The document's pages stay resident until the row's last call has answered
-or a filter dropped it. Readouts: a filter compares the max logit over the
-TRUE spellings with the max over FALSE; a score is sigmoid(true - false).
+or a filter dropped it.
 """
 
 from __future__ import annotations
@@ -31,12 +45,16 @@ PREFIX_KEY = ("prefix",)
 class Call:
     """One AI call of the chain, already tokenized."""
 
-    kind: str                      # "filter" | "score" | "classify"
+    kind: str                      # "filter" | "score" | "classify" | "map" | "extract"
     suffix: np.ndarray             # token ids after the document
-    true_cols: list = field(default_factory=list)    # answer-row columns (filter/score)
+    true_cols: list = field(default_factory=list)    # answer-row columns (filter / score)
     false_cols: list = field(default_factory=list)
-    label_cols: list = field(default_factory=list)   # classify: column of each label's first token
+    labels: list = field(default_factory=list)       # classify: token ids of each label
+    label_cols: list = field(default_factory=list)   # classify: answer column of each label token
+    max_tokens: int = 256                            # map / extract
+    stop_ids: tuple = ()
     name: str = ""
+    probabilities: bool = False
 
 
 @dataclass
@@ -46,54 +64,162 @@ class RowResult:
 
 
 class RegionRun:
-    def __init__(self, executor: StageExecutor, prefix: np.ndarray, docs: list[np.ndarray], calls: list[Call],
-                 doc_ids: list | None = None):
+    def __init__(self, executor: StageExecutor, prefix: np.ndarray, docs: list, calls: list[Call],
+                 doc_ids: list | None = None, answer_width: int | None = None):
         self.ex = executor
         self.prefix = np.asarray(prefix, dtype=np.int32)
-        self.docs = docs
+        self.docs = [np.asarray(d, dtype=np.int32) for d in docs]
         self.calls = calls
         self.doc_ids = doc_ids if doc_ids is not None else list(range(len(docs)))
         self.results = [RowResult() for _ in docs]
         self.asked = 0
         self.fresh_tokens = 0
+        self._next = [0] * len(docs)          # next call index to submit per row
+        self._pending = [0] * len(docs)       # calls in flight per row
+        self._label_parts: dict = {}
+        # columns after the answer rows in a full readout: argmax, lse
+        self.nans = answer_width
+
+    # ------------------------------------------------------------ geometry
+    def _question(self, r: int, ci: int):
+        """(own key, reads, position of the first own token, own length) of call ci's question."""
+        P = len(self.prefix)
+        doc_len = len(self.docs[r])
+        if ci == 0:
+            return ("doc", r), [(PREFIX_KEY, P)], P, doc_len + len(self.calls[0].suffix)
+        return ("q", r, ci), [(PREFIX_KEY, P), (("doc", r), doc_len)], P + doc_len, len(self.calls[ci].suffix)
+
+    def _full_cols(self, row):
+        na = self.nans if self.nans is not None else len(row) - 2
+        return na, na + 1
 
     # ------------------------------------------------------------ readouts
     @staticmethod
-    def _filter_margin(call: Call, row) -> float:
+    def _margin(call: Call, row) -> float:
         t = max(float(row[c]) for c in call.true_cols)
         f = max(float(row[c]) for c in call.false_cols)
         return t - f
 
-    def _answer(self, r: int, ci: int, row) -> None:
+    def _answered(self, r: int, ci: int, row) -> None:
         call = self.calls[ci]
         res = self.results[r]
         if call.kind == "filter":
-            keep = self._filter_margin(call, row) > 0
+            keep = self._margin(call, row) > 0
             res.values[call.name] = bool(keep)
             if not keep:
                 res.kept = False
+            self._finish_call(r, ci)
         elif call.kind == "score":
-            m = self._filter_margin(call, row)
-            res.values[call.name] = 1.0 / (1.0 + math.exp(-m))
+            res.values[call.name] = 1.0 / (1.0 + math.exp(-self._margin(call, row)))
+            self._finish_call(r, ci)
         elif call.kind == "classify":
-            scores = [float(row[c]) for c in call.label_cols]
-            res.values[call.name] = int(np.argmax(scores))
+            self._classify_first(r, ci, row)
+        elif call.kind in ("map", "extract"):
+            self._decode_step(r, ci, row, generated=[])
         self.asked += 1
-        nxt = ci + 1
-        if res.kept and nxt < len(self.calls):
-            self._submit_followup(r, nxt)
-        else:
-            self.ex.free(("doc", r))
 
-    # ------------------------------------------------------------ tasks
-    def _submit_followup(self, r: int, ci: int) -> None:
-        doc_len = len(self.docs[r])
+    def _classify_first(self, r, ci, row):
         call = self.calls[ci]
-        P = len(self.prefix)
+        _, lse_col = self._full_cols(row)
+        lse = float(row[lse_col])
+        scores = [float(row[cols[0]]) - lse for cols in call.label_cols]
+        waiting = [li for li, lab in enumerate(call.labels) if len(lab) > 1]
+        self._label_parts[(r, ci)] = [scores, len(waiting)]
+        if not waiting:
+            self._classify_done(r, ci)
+            return
+        key, reads, pos, own_len = self._question(r, ci)
+        for li in waiting:
+            lab = np.asarray(call.labels[li], dtype=np.int32)
+            toks = lab[:-1]
+            self.fresh_tokens += len(toks)
+            self.ex.submit(Task(key=("lab", r, ci, li), tokens=toks, pos_start=pos + own_len,
+                                reads=reads + [(key, own_len)], readout=True,
+                                readout_rows=tuple(range(len(toks))), full_readout=True,
+                                on_done=lambda t, rows, r=r, ci=ci, li=li: self._label_rows(r, ci, li, rows)))
+
+    def _label_rows(self, r, ci, li, rows):
+        call = self.calls[ci]
+        parts = self._label_parts[(r, ci)]
+        _, lse_col = self._full_cols(rows[0])
+        for j in range(rows.shape[0]):
+            col = call.label_cols[li][j + 1]
+            parts[0][li] += float(rows[j][col]) - float(rows[j][lse_col])
+        parts[1] -= 1
+        if parts[1] == 0:
+            self._classify_done(r, ci)
+
+    def _classify_done(self, r, ci):
+        call = self.calls[ci]
+        scores, _ = self._label_parts.pop((r, ci))
+        best = int(np.argmax(scores))
+        res = self.results[r]
+        res.values[call.name] = best
+        if call.probabilities:
+            m = max(scores)
+            e = [math.exp(s - m) for s in scores]
+            z = sum(e)
+            res.values[call.name + "#probs"] = [x / z for x in e]
+        self._finish_call(r, ci)
+
+    def _decode_step(self, r, ci, row, generated):
+        call = self.calls[ci]
+        arg_col, _ = self._full_cols(row)
+        tok = int(round(float(row[arg_col])))
+        stop = tok in call.stop_ids
+        if not stop:
+            generated = generated + [tok]
+        if stop or len(generated) >= call.max_tokens:
+            self.results[r].values[call.name] = generated
+            self._finish_call(r, ci)
+            return
+        key, reads, pos, own_len = self._question(r, ci)
+        n_prev = len(generated) - 1
+        self.fresh_tokens += 1
+        self.ex.submit(Task(key=key, tokens=np.asarray([tok], dtype=np.int32), pos_start=pos + own_len + n_prev,
+                            reads=reads, readout=True, full_readout=True, own_prefix=own_len + n_prev,
+                            free_after=False,
+                            on_done=lambda t, row, r=r, ci=ci, g=generated: self._decode_step(r, ci, row, g)))
+
+    # ------------------------------------------------------------ scheduling
+    def _finish_call(self, r: int, ci: int) -> None:
+        if ci > 0:
+            self.ex.free(("q", r, ci))
+        for li in range(len(self.calls[ci].labels)):
+            if self.ex.pool.resident(("lab", r, ci, li)):
+                self.ex.free(("lab", r, ci, li))
+        self._pending[r] -= 1
+        if self._pending[r] == 0:
+            self._advance(r)
+
+    def _advance(self, r: int) -> None:
+        res = self.results[r]
+        ci = self._next[r]
+        if not res.kept or ci >= len(self.calls):
+            self.ex.free(("doc", r))
+            return
+        # a filter runs alone; non-filter calls up to the next filter run side by side
+        batch = [ci]
+        if self.calls[ci].kind != "filter":
+            j = ci + 1
+            while j < len(self.calls) and self.calls[j].kind != "filter":
+                batch.append(j)
+                j += 1
+        self._next[r] = batch[-1] + 1
+        self._pending[r] = len(batch)
+        for c in batch:
+            self._submit_question(r, c)
+
+    def _needs_full(self, call: Call) -> bool:
+        return call.kind in ("classify", "map", "extract")
+
+    def _submit_question(self, r: int, ci: int) -> None:
+        call = self.calls[ci]
+        key, reads, pos, own_len = self._question(r, ci)
         self.fresh_tokens += len(call.suffix)
-        self.ex.submit(Task(key=("q", r, ci), tokens=call.suffix, pos_start=P + doc_len,
-                            reads=[(PREFIX_KEY, P), (("doc", r), doc_len)], readout=True,
-                            on_done=lambda t, row, r=r, ci=ci: self._answer(r, ci, row), free_after=True))
+        self.ex.submit(Task(key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
+                            full_readout=self._needs_full(call),
+                            on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
 
     def submit_all(self) -> None:
         P = len(self.prefix)
@@ -101,10 +227,13 @@ class RegionRun:
         self.ex.submit(Task(key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
         first = self.calls[0]
         for r, doc in enumerate(self.docs):
-            toks = np.concatenate([np.asarray(doc, dtype=np.int32), first.suffix])
+            toks = np.concatenate([doc, first.suffix])
             self.fresh_tokens += len(toks)
+            self._next[r] = 1
+            self._pending[r] = 1
             self.ex.submit(Task(key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
-                                on_done=lambda t, row, r=r: self._answer(r, 0, row), free_after=False))
+                                full_readout=self._needs_full(first),
+                                on_done=lambda t, row, r=r: self._answered(r, 0, row), free_after=False))
 
     def run(self):
         self.submit_all()

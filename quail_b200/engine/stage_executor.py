@@ -51,6 +51,8 @@ class Task:
     own_prefix: int = 0                              # own tokens already resident (continuation)
     done: int = 0                                    # new tokens already launched
     tag: object = None
+    readout_rows: tuple | None = None                # offsets read out (default: the last token)
+    full_readout: bool = False                       # also argmax / log-sum-exp over the vocabulary
 
     @property
     def remaining(self) -> int:
@@ -116,8 +118,8 @@ class StageExecutor:
             if not self._readable(task):
                 deferred.append(task)
                 continue
+            total = task.own_prefix + len(task.tokens)
             if not self.pool.resident(task.key):
-                total = task.own_prefix + len(task.tokens)
                 pages = self.pool.alloc(task.key, total)
                 if pages is None:
                     self.pool.evict_retained(self.pool.pages_needed(total))
@@ -127,14 +129,27 @@ class StageExecutor:
                     break  # keep FIFO order under memory pressure
                 for rk, _ in task.reads:
                     self.pool.borrow(task.key, rk)
+            elif self.pool.tokens[task.key] < total:
+                # a continuation (decode step, prefill piece) of a resident key
+                if self.pool.grow(task.key, total) is None:
+                    self.pool.evict_retained(self.pool.pages_needed(total))
+                    if self.pool.grow(task.key, total) is None:
+                        deferred.append(task)
+                        break
             piece = min(task.remaining, room)
             if piece < task.remaining and piece < self.min_piece and specs:
                 deferred.append(task)
                 break
             last = piece == task.remaining
+            rows = None
+            if task.readout and last and task.readout_rows is not None:
+                if task.done:
+                    raise ValueError("a task with several readout rows must fit in one chunk")
+                rows = tuple(task.readout_rows)
             specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix + task.done,
                                  tokens=task.tokens[task.done:task.done + piece],
-                                 pos_start=task.pos_start + task.done, readout=task.readout and last, tag=task))
+                                 pos_start=task.pos_start + task.done, readout=task.readout and last, tag=task,
+                                 readout_rows=rows, full=task.full_readout))
             task.done += piece
             room -= piece
             if not last:
@@ -167,7 +182,7 @@ class StageExecutor:
         self.stats.passes += 1
         self.stats.tokens += chunk.num_tokens
         self.stats.pass_tokens.append(chunk.num_tokens)
-        self.stats.pass_rows.append(sum(1 for s in specs if s.readout))
+        self.stats.pass_rows.append(sum(1 for s in specs if s.readout and s.readout_rows is None))
         self.stats.h2d_bytes += chunk.upload_bytes
         if logits is not None:
             self.stats.d2h_bytes += logits.numel() * logits.element_size()
@@ -185,8 +200,9 @@ class StageExecutor:
             last = s.own_start + len(s.tokens) == task.own_prefix + len(task.tokens)
             row = None
             if s.readout:
-                row = host[r]
-                r += 1
+                k = len(s.readout_rows) if s.readout_rows is not None else 1
+                row = host[r] if s.readout_rows is None else host[r:r + k]
+                r += k
                 self.stats.readouts += 1
             if last:
                 if task.on_done:

@@ -75,6 +75,12 @@ class Qwen3Weights:
         if head_rows is not None:
             self.set_answer_rows(head_rows)
 
+    def head_bf16(self) -> torch.Tensor:
+        """The whole LM head on the device in bf16 (for full-vocabulary readouts)."""
+        if getattr(self, "_head_dev", None) is None:
+            self._head_dev = self.head.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        return self._head_dev
+
     def set_answer_rows(self, token_ids) -> None:
         """Retain the LM-head rows of the answer tokens (yes/no or labels)."""
         ids = torch.as_tensor(list(token_ids), dtype=torch.long)
@@ -124,7 +130,13 @@ class Qwen3Pipeline:
                 a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
                 ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
         del T, dev
-        return ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows)
+        if not getattr(chunk, "full_readout", False):
+            return ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows)
+        R = chunk.final_rows.numel()
+        normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
+        ans = ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows, normed=normed)
+        arg, lse = ops.row_argmax_lse(ops.gemm(normed, w.head_bf16()))
+        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)
 
 
 class Qwen3Reference:
@@ -220,4 +232,10 @@ class Qwen3Reference:
         h = self.hidden_chunk(chunk, arena)
         rows = h[chunk.final_rows.long()]
         normed = ref.rmsnorm(rows, self.final_norm, self.cfg.rms_eps)
-        return (normed @ self.answer_rows.t()).float()
+        ans = (normed @ self.answer_rows.t()).float()
+        if not getattr(chunk, "full_readout", False):
+            return ans
+        full = (normed @ self.head.t()).float()
+        arg = full.argmax(dim=1).float()
+        lse = torch.logsumexp(full, dim=1)
+        return torch.cat([ans, arg[:, None], lse[:, None]], dim=1)

@@ -28,6 +28,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     quant_rows,
     read_and_clear_error,
     rmsnorm_quant,
+    row_argmax_lse,
 )
 from quail_b200.ops.quant import (  # noqa: F401
     FP8_MAX,

@@ -226,6 +226,16 @@ def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, n
     return logits
 
 
+def row_argmax_lse(logits: torch.Tensor):
+    """Row-wise argmax and log-sum-exp of bf16 logits [R, V] -> (int32 [R], fp32 [R])."""
+    R = logits.shape[0]
+    arg = torch.empty(R, dtype=torch.int32, device=logits.device)
+    lse = torch.empty(R, dtype=torch.float32, device=logits.device)
+    _count()
+    native().row_argmax_lse(logits, arg, lse)
+    return arg, lse
+
+
 def read_and_clear_error(device: int = 0) -> int:
     """Synchronize and return (then clear) the kernels' bounded-wait error code."""
     return int(native().read_and_clear_error(device))

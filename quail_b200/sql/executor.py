@@ -1,0 +1,902 @@
+"""Binding and running a parsed query over Arrow tables, with AI calls on the model.
+
+The C++ parser (quail_b200._native.parse_sql) gives a JSON tree; this module
+binds names against the session's tables and runs the relational operators
+with pyarrow (scans, hash joins, filters, projections, aggregates, sorts,
+limits). AI calls are the reference's logical rules in small
+(crates/quail-datafusion/src/rules):
+
+- lowering: each AI.* call in WHERE, SELECT, ORDER BY or HAVING becomes a
+  model call bound to a prompt (`quail_b200.api.prompts`);
+- placement / guards: WHERE conjuncts without AI calls run first, so the
+  model sees only the rows they keep; AI.IF conjuncts then run as a guarded
+  chain (each later call only on the rows every earlier filter kept); the
+  SELECT / ORDER BY calls run on the survivors, next to them;
+- merge: identical calls (same function, prompt and document column) are
+  evaluated once per row, and identical documents once per table
+  (`ModelEngine.run_region` deduplicates).
+
+A call inside an expression the rules cannot split (an OR of AI calls, a
+CASE) is evaluated on every row that reaches that operator, then the
+expression is computed from its values.
+"""
+
+from __future__ import annotations
+
+import json
+import re
+from dataclasses import dataclass, field
+
+import numpy as np
+import pyarrow as pa
+import pyarrow.compute as pc
+
+from quail_b200.api import prompts as P
+
+CPU_AI_FUNCTIONS = ("AI.PARSE_DOCUMENT", "AI.PDF_PAGES", "AI.IMAGE")
+MODEL_AI_FUNCTIONS = ("AI.IF", "AI_FILTER", "AI.SCORE", "AI.CLASSIFY", "AI.EXTRACT", "AI.EXTRACT_SPAN",
+                      "AI.MAP", "AI.SAE_FEATURES")
+AGGREGATES = ("COUNT", "SUM", "AVG", "MIN", "MAX", "ARRAY_AGG", "ANY_VALUE")
+MAP_MAX_TOKENS_LIMIT = 32_768
+MAP_DEFAULT_TOKENS = 256
+
+
+class QueryError(ValueError):
+    pass
+
+
+def parse(text: str) -> dict:
+    from quail_b200 import _native
+    return json.loads(_native.parse_sql(text))
+
+
+# ---------------------------------------------------------------- expression helpers
+
+def walk(node):
+    """Yield every dict node of a tree."""
+    if isinstance(node, dict):
+        yield node
+        for v in node.values():
+            yield from walk(v)
+    elif isinstance(node, list):
+        for v in node:
+            yield from walk(v)
+
+
+def is_model_call(node) -> bool:
+    return isinstance(node, dict) and node.get("type") == "call" and node.get("name") in MODEL_AI_FUNCTIONS
+
+
+def has_model_call(node) -> bool:
+    return any(is_model_call(n) for n in walk(node))
+
+
+def is_aggregate(node) -> bool:
+    return isinstance(node, dict) and node.get("type") == "call" and node.get("name") in AGGREGATES
+
+
+def conjuncts(node) -> list:
+    if node is None:
+        return []
+    if node.get("type") == "binary" and node.get("op") == "AND":
+        return conjuncts(node["left"]) + conjuncts(node["right"])
+    return [node]
+
+
+def node_key(node) -> str:
+    return json.dumps(node, sort_keys=True)
+
+
+def expr_name(node) -> str:
+    t = node.get("type")
+    if t == "column":
+        return node["name"]
+    if t == "call":
+        return node["name"].lower()
+    if t == "literal":
+        return str(node["value"])
+    return t
+
+
+def literal_value(node):
+    if node is None:
+        return None
+    t = node.get("type")
+    if t == "literal":
+        return node["value"]
+    if t == "array":
+        return [literal_value(x) for x in node["items"]]
+    if t == "object":
+        return {k: literal_value(v) for k, v in node["items"]}
+    if t == "unary" and node["op"] == "-":
+        v = literal_value(node["arg"])
+        return -v if isinstance(v, (int, float)) else None
+    raise QueryError(f"expected a constant, got {t}")
+
+
+# ---------------------------------------------------------------- relations
+
+@dataclass
+class Relation:
+    """An Arrow table whose columns are addressed as (qualifier, name)."""
+
+    table: pa.Table
+    cols: list  # [(qualifier or None, name)] parallel to table columns
+
+    @classmethod
+    def from_table(cls, t: pa.Table, qualifier: str | None) -> "Relation":
+        names = t.column_names
+        return cls(t.rename_columns([f"c{i}" for i in range(len(names))]), [(qualifier, n) for n in names])
+
+    @property
+    def num_rows(self) -> int:
+        return self.table.num_rows
+
+    def resolve(self, qualifier: str | None, name: str) -> int:
+        hits = [i for i, (q, n) in enumerate(self.cols)
+                if n.lower() == name.lower() and (qualifier is None or (q or "").lower() == qualifier.lower())]
+        if not hits:
+            raise QueryError(f"unknown column {qualifier + '.' if qualifier else ''}{name}")
+        if len(hits) > 1:
+            exact = [i for i in hits if self.cols[i][1] == name]
+            if len(exact) == 1:
+                return exact[0]
+            raise QueryError(f"ambiguous column {name}")
+        return hits[0]
+
+    def column(self, i: int):
+        return self.table.column(i)
+
+    def take(self, idx) -> "Relation":
+        return Relation(self.table.take(idx), list(self.cols))
+
+    def filter(self, mask) -> "Relation":
+        return Relation(self.table.filter(mask), list(self.cols))
+
+    def with_column(self, arr, qualifier, name) -> "Relation":
+        t = self.table.append_column(f"c{len(self.cols)}", arr)
+        return Relation(t, self.cols + [(qualifier, name)])
+
+
+def concat_relations(left: Relation, right: Relation) -> Relation:
+    t = left.table
+    for i in range(right.table.num_columns):
+        t = t.append_column(f"c{t.num_columns}", right.table.column(i))
+    return Relation(t.rename_columns([f"c{i}" for i in range(t.num_columns)]), left.cols + right.cols)
+
+
+# ---------------------------------------------------------------- AI call binding
+
+@dataclass
+class BoundCall:
+    """An AI call ready for the engine: which rows' documents, which prompt."""
+
+    key: str
+    kind: str                   # filter | score | classify | map | extract
+    preamble: str
+    tail: str
+    doc_expr: dict              # expression giving each row's document
+    labels: list = field(default_factory=list)
+    max_tokens: int = MAP_DEFAULT_TOKENS
+    probabilities: bool = False
+    selectivity: float | None = None
+    questions: list = field(default_factory=list)   # extract: one call per question
+    span: bool = False
+
+
+def _options(node) -> dict:
+    if node is None:
+        return {}
+    v = literal_value(node)
+    if not isinstance(v, dict):
+        raise QueryError("AI function options must be an object such as {'selectivity': 0.3}")
+    return v
+
+
+def _prompt_parts(arg) -> tuple[str, dict, int]:
+    """(template, document expression, number of documents) of a PROMPT(...) or a plain column."""
+    if arg.get("type") == "call" and arg["name"] == "PROMPT":
+        args = arg["args"]
+        if not args or args[0].get("type") != "literal" or args[0]["kind"] != "string":
+            raise QueryError("PROMPT takes a template string first")
+        template = args[0]["value"]
+        values = args[1:]
+        P.check_placeholders(template, len(values))
+        if len(values) == 1:
+            return template, values[0], 1
+        if len(values) == 0:
+            return template, {"type": "literal", "kind": "string", "value": ""}, 0
+        # several values: one computed document, DOCUMENT k labels in order
+        parts = []
+        for i, v in enumerate(values):
+            label = {"type": "literal", "kind": "string", "value": f"DOCUMENT {i + 1}:\n" if i == 0 else
+                     f"\n\nDOCUMENT {i + 1}:\n"}
+            parts += [label, v]
+        doc = parts[0]
+        for p in parts[1:]:
+            doc = {"type": "binary", "op": "||", "left": doc, "right": p}
+        tmpl = re.sub(r"\{\d+\}", "", template).strip()
+        return tmpl + " {0}", doc, len(values)
+    return "{0}", arg, 1
+
+
+def bind_call(node, turn: P.Turn) -> BoundCall:
+    name = node["name"]
+    args = [a for a in node["args"] if a.get("type") != "named_arg"]
+    named = {a["name"].lower(): a["value"] for a in node["args"] if a.get("type") == "named_arg"}
+    key = node_key(node)
+    if name in ("AI.IF", "AI_FILTER", "AI.SCORE"):
+        if not args:
+            raise QueryError(f"{name} takes a prompt")
+        template, doc, ndocs = _prompt_parts(args[0])
+        opts = _options(args[1] if len(args) > 1 else named.get("options"))
+        bp = P.bind_prompt(template if ndocs <= 1 else template, 1, turn)
+        kind = "score" if name == "AI.SCORE" else "filter"
+        return BoundCall(key=key, kind=kind, preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                         selectivity=opts.get("selectivity"))
+    if name == "AI.CLASSIFY":
+        if len(args) < 2:
+            raise QueryError("AI.CLASSIFY takes an input and a list of categories")
+        template, doc, _ = _prompt_parts(args[0])
+        cats = literal_value(args[1])
+        if not isinstance(cats, list) or not cats:
+            raise QueryError("AI.CLASSIFY categories must be a non-empty array literal")
+        labels, descriptions = [], []
+        for c in cats:
+            if isinstance(c, dict):
+                labels.append(str(c.get("label")))
+                descriptions.append(str(c.get("description", "")))
+            else:
+                labels.append(str(c))
+                descriptions.append("")
+        if len(set(labels)) != len(labels):
+            raise QueryError("AI.CLASSIFY categories must be distinct")
+        opts = _options(args[2] if len(args) > 2 else named.get("options"))
+        bp = P.bind_classify_prompt(template if template != "{0}" else None, labels, descriptions,
+                                    opts.get("task_description", ""), turn)
+        return BoundCall(key=key, kind="classify", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, labels=labels,
+                         probabilities=bool(opts.get("probabilities", False)))
+    if name == "AI.MAP":
+        if len(args) < 2:
+            raise QueryError("AI.MAP takes an input and an instruction")
+        _, doc, _ = _prompt_parts(args[0])
+        instruction = literal_value(args[1])
+        max_tokens = literal_value(args[2]) if len(args) > 2 else MAP_DEFAULT_TOKENS
+        if not isinstance(max_tokens, int) or not 1 <= max_tokens <= MAP_MAX_TOKENS_LIMIT:
+            raise QueryError(f"AI.MAP max_tokens must be an integer in [1, {MAP_MAX_TOKENS_LIMIT}]")
+        bp = P.bind_map_prompt(str(instruction), turn)
+        return BoundCall(key=key, kind="map", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, max_tokens=max_tokens)
+    if name in ("AI.EXTRACT", "AI.EXTRACT_SPAN"):
+        if len(args) < 2:
+            raise QueryError(f"{name} takes an input and a list of questions")
+        _, doc, _ = _prompt_parts(args[0])
+        qs = literal_value(args[1])
+        qs = [qs] if isinstance(qs, str) else list(qs)
+        bp = P.bind_extract_prompt(qs[0], turn)
+        return BoundCall(key=key, kind="extract", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, questions=qs,
+                         span=name == "AI.EXTRACT_SPAN", max_tokens=64)
+    if name == "AI.SAE_FEATURES":
+        from quail_b200.api.config import Refusal, RefusalError
+        raise RefusalError(Refusal(reasons=("AI.SAE_FEATURES needs a model with a sparse autoencoder spec",),
+                                   constraint="unsupported_function"))
+    raise QueryError(f"unknown AI function {name}")
+
+
+# ---------------------------------------------------------------- the executor
+
+class Executor:
+    def __init__(self, catalog: dict, engine=None, turn: P.Turn = P.Turn(), settings: dict | None = None):
+        self.catalog = catalog
+        self.engine = engine
+        self.turn = turn
+        self.settings = settings or {}
+        self.ctes: dict = {}
+        self.report = {"regions": [], "asked": 0, "fresh_tokens": 0, "passes": 0, "evaluated_documents": 0}
+        self.ai_values: dict = {}   # (call key) -> Arrow array aligned with the relation being evaluated
+
+    # ------------------------------------------------------------ entry
+    def run(self, tree: dict) -> pa.Table:
+        t = tree.get("type")
+        if t == "explain":
+            raise QueryError("EXPLAIN is answered by Query.explain()")
+        return self.query(tree)
+
+    def query(self, node) -> pa.Table:
+        saved = dict(self.ctes)
+        for w in node.get("with", []):
+            self.ctes[w["name"].lower()] = self.query(w["query"])
+        if node["type"] == "union":
+            left = self.query(node["left"])
+            right = self.query(node["right"])
+            right = right.rename_columns(left.column_names).cast(left.schema)
+            out = pa.concat_tables([left, right])
+            if not node["all"]:
+                out = _distinct(out)
+            out = self._order_limit_output(out, node)
+        else:
+            out = self.select(node)
+        self.ctes = saved
+        return out
+
+    # ------------------------------------------------------------ FROM
+    def table_ref(self, ref) -> Relation:
+        alias = ref.get("alias")
+        if ref["type"] == "subquery":
+            return Relation.from_table(self.query(ref["query"]), alias)
+        name = ref["name"]
+        low = name.lower()
+        if low in self.ctes:
+            return Relation.from_table(self.ctes[low], alias or name)
+        for k, prov in self.catalog.items():
+            if k.lower() == low:
+                t = prov.scan().read_all()
+                return Relation.from_table(t, alias or name)
+        raise QueryError(f"unknown table {name}; registered: {sorted(self.catalog)}")
+
+    def from_clause(self, node) -> Relation:
+        if "from" not in node:
+            return Relation(pa.table({"c0": [0]}), [(None, "__dual")])
+        rel = self.table_ref(node["from"][0])
+        for j in node.get("joins", []):
+            right = self.table_ref(j["table"])
+            rel = self.join(rel, right, j)
+        return rel
+
+    def join(self, left: Relation, right: Relation, j) -> Relation:
+        kind = j["kind"]
+        on = j.get("on")
+        if "using" in j:
+            on = None
+            for c in j["using"]:
+                eq = {"type": "binary", "op": "=", "left": {"type": "column", "table": left.cols[left.resolve(None, c)][0],
+                                                              "name": c},
+                      "right": {"type": "column", "table": right.cols[right.resolve(None, c)][0], "name": c}}
+                on = eq if on is None else {"type": "binary", "op": "AND", "left": on, "right": eq}
+        if kind == "cross" or on is None:
+            return self._cross(left, right)
+        # equi-join keys between the two sides; the rest filters the joined rows
+        keys, rest = [], []
+        for c in conjuncts(on):
+            pair = self._equi_pair(c, left, right)
+            if pair is not None and not has_model_call(c):
+                keys.append(pair)
+            else:
+                rest.append(c)
+        if keys:
+            lk = [f"c{i}" for i, _ in keys]
+            rk = [f"c{i}" for _, i in keys]
+            lt = left.table.append_column("__lrow", pa.array(np.arange(left.num_rows)))
+            rt = right.table.append_column("__rrow", pa.array(np.arange(right.num_rows)))
+            rt = rt.rename_columns([f"r{n}" for n in rt.column_names])
+            jt = {"inner": "inner", "left": "left outer", "right": "right outer", "full": "full outer"}[kind]
+            joined = lt.join(rt, keys=lk, right_keys=[f"r{k}" for k in rk], join_type=jt, coalesce_keys=False)
+            li = joined.column("__lrow")
+            ri = joined.column("r__rrow")
+            lrel = Relation(left.table.take(li), list(left.cols))
+            rrel = Relation(right.table.take(ri), list(right.cols))
+            rel = concat_relations(lrel, rrel)
+        else:
+            if kind != "inner":
+                raise QueryError(f"{kind.upper()} JOIN needs an equality condition")
+            rel = self._cross(left, right)
+        for c in rest:
+            if kind != "inner":
+                raise QueryError("an outer join's ON may only hold equalities")
+            rel = self.apply_where(rel, c)
+        return rel
+
+    def _cross(self, left: Relation, right: Relation) -> Relation:
+        n, m = left.num_rows, right.num_rows
+        li = pa.array(np.repeat(np.arange(n), m))
+        ri = pa.array(np.tile(np.arange(m), n))
+        return concat_relations(Relation(left.table.take(li), list(left.cols)),
+                                Relation(right.table.take(ri), list(right.cols)))
+
+    def _equi_pair(self, c, left: Relation, right: Relation):
+        if c.get("type") != "binary" or c.get("op") != "=":
+            return None
+        a, b = c["left"], c["right"]
+        if a.get("type") != "column" or b.get("type") != "column":
+            return None
+        for x, y in ((a, b), (b, a)):
+            try:
+                i = left.resolve(x.get("table"), x["name"])
+                k = right.resolve(y.get("table"), y["name"])
+                return i, k
+            except QueryError:
+                continue
+        return None
+
+    # ------------------------------------------------------------ WHERE with AI placement
+    def apply_where(self, rel: Relation, where) -> Relation:
+        plain = [c for c in conjuncts(where) if not has_model_call(c)]
+        ai = [c for c in conjuncts(where) if has_model_call(c)]
+        for c in plain:
+            rel = rel.filter(_as_mask(self.eval(c, rel)))
+        if not ai:
+            return rel
+        # AI.IF conjuncts: a guarded chain; others evaluated on the survivors
+        filters = []
+        others = []
+        for c in ai:
+            inner = c
+            if inner.get("type") == "call" and inner["name"] == "HINT":
+                inner = inner["args"][0]
+            if is_model_call(inner) and inner["name"] in ("AI.IF", "AI_FILTER"):
+                filters.append(inner)
+            else:
+                others.append(c)
+        if filters:
+            bound = [bind_call(f, self.turn) for f in filters]
+            # the most selective hinted filter first
+            order = sorted(range(len(bound)), key=lambda i: bound[i].selectivity if bound[i].selectivity is not None
+                           else 1.0)
+            rel = self.run_filters(rel, [bound[i] for i in order])
+        for c in others:
+            self.compute_ai(rel, [c])
+            rel = rel.filter(_as_mask(self.eval(c, rel)))
+            self.ai_values = {}
+        return rel
+
+    def run_filters(self, rel: Relation, calls: list[BoundCall]) -> Relation:
+        """AI.IF calls as one guarded chain over the relation's documents."""
+        if rel.num_rows == 0 or not calls:
+            return rel
+        groups = {}
+        for c in calls:
+            groups.setdefault((c.preamble, node_key(c.doc_expr)), []).append(c)
+        keep = np.ones(rel.num_rows, dtype=bool)
+        for (_, _), cs in groups.items():
+            docs = _to_pylist(self.eval(cs[0].doc_expr, rel))
+            idx = np.nonzero(keep)[0]
+            vals = self._engine_region(cs[0].preamble, [docs[i] for i in idx], cs)
+            for j, i in enumerate(idx):
+                for c in cs:
+                    if not vals[j].get(c.key, False):
+                        keep[i] = False
+        return rel.filter(pa.array(keep))
+
+    def compute_ai(self, rel: Relation, exprs: list) -> None:
+        """Evaluate every model call inside `exprs` on all rows of `rel` (merged per prompt)."""
+        calls = {}
+        for e in exprs:
+            for n in walk(e):
+                if is_model_call(n):
+                    k = node_key(n)
+                    if k not in calls and k not in self.ai_values:
+                        calls[k] = bind_call(n, self.turn)
+        if not calls:
+            return
+        groups = {}
+        for c in calls.values():
+            groups.setdefault((c.preamble, node_key(c.doc_expr)), []).append(c)
+        for (_, _), cs in groups.items():
+            docs = _to_pylist(self.eval(cs[0].doc_expr, rel)) if rel.num_rows else []
+            expanded = []
+            for c in cs:
+                if c.kind == "extract":
+                    for qi, q in enumerate(c.questions):
+                        bp = P.bind_extract_prompt(q, self.turn)
+                        expanded.append(BoundCall(key=f"{c.key}#{qi}", kind="extract", preamble=bp.preamble,
+                                                  tail=bp.tail, doc_expr=c.doc_expr, max_tokens=c.max_tokens))
+                else:
+                    expanded.append(c)
+            vals = self._engine_region(cs[0].preamble, docs, expanded) if docs else []
+            for c in cs:
+                if c.kind == "extract":
+                    out = []
+                    for r, v in enumerate(vals):
+                        answers = [_clean_phrase(v.get(f"{c.key}#{qi}")) for qi in range(len(c.questions))]
+                        if c.span:
+                            doc = "" if docs[r] is None else str(docs[r])
+                            answers = [_span(doc, a) for a in answers]
+                        out.append(answers)
+                    self.ai_values[c.key] = pa.array(out)
+                elif c.kind == "classify" and c.probabilities:
+                    self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], pa.string())
+                    self.ai_values[c.key + "#probs"] = pa.array([v.get(c.key + "#probs") for v in vals])
+                else:
+                    typ = {"filter": pa.bool_(), "score": pa.float64(), "classify": pa.string(),
+                           "map": pa.string()}[c.kind]
+                    self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], typ)
+
+    def _engine_region(self, preamble: str, docs: list, calls: list[BoundCall]) -> list[dict]:
+        if self.engine is None:
+            raise QueryError("this query needs a model; the session has none")
+        from quail_b200.api.engine import CallSpec
+        specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
+                          probabilities=c.probabilities) for c in calls]
+        out = self.engine.run_region(preamble, docs, specs)
+        self.report["regions"].append(out.stats)
+        for k in ("asked", "fresh_tokens", "passes"):
+            self.report[k] += out.stats.get(k, 0)
+        self.report["evaluated_documents"] += out.stats.get("documents", 0)
+        return out.values
+
+    # ------------------------------------------------------------ SELECT
+    def select(self, node) -> pa.Table:
+        rel = self.from_clause(node)
+        if node.get("where"):
+            rel = self.apply_where(rel, node["where"])
+        items = node["items"]
+        group_by = node.get("group_by")
+        aggregated = group_by is not None or any(is_aggregate(n) for it in items for n in walk(it["expr"]))
+        # AI calls in the projection / ORDER BY / HAVING run on the surviving rows
+        self.ai_values = {}
+        ai_exprs = [it["expr"] for it in items] + [o["expr"] for o in node.get("order_by", [])]
+        if node.get("having"):
+            ai_exprs.append(node["having"])
+        self.compute_ai(rel, ai_exprs)
+        if aggregated:
+            out = self._aggregate(rel, node)
+        else:
+            names, arrays = [], []
+            for it in items:
+                e = it["expr"]
+                if e.get("type") == "star":
+                    for i, (q, n) in enumerate(rel.cols):
+                        if e.get("table") is None or (q or "").lower() == e["table"].lower():
+                            if n.startswith("__"):
+                                continue
+                            names.append(n)
+                            arrays.append(rel.column(i))
+                    continue
+                names.append(it.get("alias") or expr_name(e))
+                arrays.append(_as_array(self.eval(e, rel), rel.num_rows))
+            out = pa.Table.from_arrays(arrays, names=_dedupe(names))
+            if node.get("order_by"):
+                keys = []
+                for k, o in enumerate(node["order_by"]):
+                    arr = self._order_key(o["expr"], rel, out, items)
+                    out = out.append_column(f"__order{k}", arr)
+                    keys.append((f"__order{k}", "descending" if o["desc"] else "ascending"))
+                idx = pc.sort_indices(out, sort_keys=keys, null_placement="at_end")
+                out = out.take(idx).drop_columns([k for k, _ in keys])
+            self.ai_values = {}
+            if node.get("distinct"):
+                out = _distinct(out)
+            return self._limit(out, node)
+        self.ai_values = {}
+        if node.get("distinct"):
+            out = _distinct(out)
+        return self._order_limit_output(out, node)
+
+    def _order_key(self, e, rel: Relation, out: pa.Table, items):
+        if e.get("type") == "literal" and e["kind"] == "int":
+            return out.column(int(e["value"]) - 1)
+        if e.get("type") == "column" and e.get("table") is None:
+            for it in items:
+                if (it.get("alias") or "").lower() == e["name"].lower():
+                    return out.column(it["alias"])
+        return _as_array(self.eval(e, rel), rel.num_rows)
+
+    def _order_limit_output(self, out: pa.Table, node) -> pa.Table:
+        if node.get("order_by"):
+            keys = []
+            tmp = out
+            rel = Relation.from_table(out, None)
+            for k, o in enumerate(node["order_by"]):
+                e = o["expr"]
+                if e.get("type") == "literal" and e["kind"] == "int":
+                    arr = out.column(int(e["value"]) - 1)
+                else:
+                    arr = _as_array(self.eval(e, rel), out.num_rows)
+                tmp = tmp.append_column(f"__order{k}", arr)
+                keys.append((f"__order{k}", "descending" if o["desc"] else "ascending"))
+            idx = pc.sort_indices(tmp, sort_keys=keys, null_placement="at_end")
+            out = out.take(idx)
+        return self._limit(out, node)
+
+    def _limit(self, out: pa.Table, node) -> pa.Table:
+        off = int(literal_value(node["offset"])) if node.get("offset") else 0
+        if node.get("limit") is not None:
+            return out.slice(off, int(literal_value(node["limit"])))
+        return out.slice(off) if off else out
+
+    # ------------------------------------------------------------ aggregates
+    def _aggregate(self, rel: Relation, node) -> pa.Table:
+        group_by = node.get("group_by") or []
+        items = node["items"]
+        # resolve GROUP BY ordinal / alias references
+        gexprs = []
+        for g in group_by:
+            if g.get("type") == "literal" and g["kind"] == "int":
+                gexprs.append(items[int(g["value"]) - 1]["expr"])
+            elif g.get("type") == "column" and g.get("table") is None and any(
+                    (it.get("alias") or "").lower() == g["name"].lower() for it in items):
+                gexprs.append(next(it["expr"] for it in items if (it.get("alias") or "").lower() == g["name"].lower()))
+            else:
+                gexprs.append(g)
+        aggs = []
+        for e in [it["expr"] for it in items] + ([node["having"]] if node.get("having") else []) + \
+                [o["expr"] for o in node.get("order_by", [])]:
+            for n in walk(e):
+                if is_aggregate(n) and node_key(n) not in [node_key(a) for a in aggs]:
+                    aggs.append(n)
+        cols = {}
+        for i, g in enumerate(gexprs):
+            cols[f"g{i}"] = _as_array(self.eval(g, rel), rel.num_rows)
+        specs = []
+        for i, a in enumerate(aggs):
+            fn = a["name"]
+            args = a["args"]
+            if fn == "COUNT" and (not args or args[0].get("type") == "star"):
+                cols[f"a{i}"] = pa.array(np.ones(rel.num_rows, dtype=np.int64))
+                specs.append((f"a{i}", "count", None))
+                continue
+            cols[f"a{i}"] = _as_array(self.eval(args[0], rel), rel.num_rows)
+            op = {"COUNT": "count_distinct" if a.get("distinct") else "count", "SUM": "sum", "AVG": "mean",
+                  "MIN": "min", "MAX": "max", "ARRAY_AGG": "list", "ANY_VALUE": "first"}[fn]
+            specs.append((f"a{i}", op, None))
+        if not gexprs:
+            # one group holding every row (an empty input still gives one row)
+            cols["g_all"] = pa.array(np.zeros(rel.num_rows, dtype=np.int64))
+        base = pa.table(cols)
+        keys = [f"g{i}" for i in range(len(gexprs))] or ["g_all"]
+        grouped = base.group_by(keys, use_threads=False).aggregate([(c, op) for c, op, _ in specs])
+        rename = {f"{c}_{op}": c for c, op, _ in specs}
+        grouped = grouped.rename_columns([rename.get(n, n) for n in grouped.column_names])
+        if not gexprs and grouped.num_rows == 0:
+            empty = {}
+            for c, op, _ in specs:
+                empty[c] = pa.array([0 if op in ("count", "count_distinct") else None])
+            grouped = pa.table(empty) if empty else pa.table({"g_all": [0]})
+        grel = Relation.from_table(grouped, None)
+        self._agg_map = {node_key(a): grel.resolve(None, f"a{i}") for i, a in enumerate(aggs)}
+        self._group_map = {node_key(g): grel.resolve(None, f"g{i}") for i, g in enumerate(gexprs)}
+        if node.get("having"):
+            grel = grel.filter(_as_mask(self.eval(node["having"], grel)))
+        names, arrays = [], []
+        for it in items:
+            names.append(it.get("alias") or expr_name(it["expr"]))
+            arrays.append(_as_array(self.eval(it["expr"], grel), grel.num_rows))
+        out = pa.Table.from_arrays(arrays, names=_dedupe(names))
+        if node.get("order_by"):
+            keys = []
+            for k, o in enumerate(node["order_by"]):
+                arr = self._order_key(o["expr"], grel, out, items)
+                out = out.append_column(f"__order{k}", arr)
+                keys.append((f"__order{k}", "descending" if o["desc"] else "ascending"))
+            idx = pc.sort_indices(out, sort_keys=keys, null_placement="at_end")
+            out = out.take(idx).drop_columns([k for k, _ in keys])
+        self._agg_map, self._group_map = {}, {}
+        return out
+
+    # ------------------------------------------------------------ scalar expressions
+    def eval(self, e, rel: Relation):
+        t = e.get("type")
+        k = node_key(e)
+        if getattr(self, "_agg_map", None) and k in self._agg_map:
+            return rel.column(self._agg_map[k])
+        if getattr(self, "_group_map", None) and k in self._group_map:
+            return rel.column(self._group_map[k])
+        if t == "column":
+            return rel.column(rel.resolve(e.get("table"), e["name"]))
+        if t == "literal":
+            return pa.scalar(e["value"]) if e["value"] is not None else pa.scalar(None, pa.null())
+        if t == "binary":
+            return self._binary(e, rel)
+        if t == "unary":
+            v = self.eval(e["arg"], rel)
+            return pc.invert(_bool(v)) if e["op"] == "NOT" else pc.negate(v)
+        if t == "is_null":
+            v = self.eval(e["arg"], rel)
+            r = pc.is_null(v)
+            return pc.invert(r) if e["negated"] else r
+        if t == "is_bool":
+            v = _bool(self.eval(e["arg"], rel))
+            r = pc.fill_null(pc.equal(v, pa.scalar(e["value"])), False)
+            return pc.invert(r) if e["negated"] else r
+        if t == "in":
+            v = self.eval(e["arg"], rel)
+            vals = [literal_value(x) for x in e["list"]]
+            r = pc.is_in(_as_array(v, rel.num_rows), value_set=pa.array(vals))
+            return pc.invert(r) if e["negated"] else r
+        if t == "between":
+            v = self.eval(e["arg"], rel)
+            r = pc.and_(pc.greater_equal(v, self.eval(e["low"], rel)), pc.less_equal(v, self.eval(e["high"], rel)))
+            return pc.invert(r) if e["negated"] else r
+        if t == "like":
+            v = self.eval(e["arg"], rel)
+            pat = literal_value(e["pattern"])
+            r = pc.match_like(_as_array(v, rel.num_rows), pat, ignore_case=e.get("case_insensitive", False))
+            return pc.invert(r) if e["negated"] else r
+        if t == "case":
+            return self._case(e, rel)
+        if t == "cast":
+            return _cast(self.eval(e["arg"], rel), e["to"])
+        if t == "array":
+            return pa.scalar([literal_value(x) for x in e["items"]])
+        if t == "subscript":
+            v = _as_array(self.eval(e["arg"], rel), rel.num_rows)
+            idx = literal_value(e["index"])
+            if isinstance(idx, int):
+                return pc.list_element(v, idx)
+            return pc.struct_field(v, idx)
+        if t == "call":
+            return self._call(e, rel)
+        if t == "star":
+            raise QueryError("* is not an expression here")
+        if t == "scalar_subquery":
+            sub = self.query(e["query"])
+            if sub.num_columns != 1 or sub.num_rows > 1:
+                raise QueryError("a scalar subquery returns one value")
+            return sub.column(0)[0] if sub.num_rows else pa.scalar(None)
+        raise QueryError(f"unsupported expression {t}")
+
+    def _binary(self, e, rel):
+        op = e["op"]
+        a, b = self.eval(e["left"], rel), self.eval(e["right"], rel)
+        if op == "AND":
+            return pc.and_kleene(_bool(a), _bool(b))
+        if op == "OR":
+            return pc.or_kleene(_bool(a), _bool(b))
+        if op == "||":
+            return pc.binary_join_element_wise(_str(a), _str(b), "")
+        fn = {"=": pc.equal, "<>": pc.not_equal, "<": pc.less, "<=": pc.less_equal, ">": pc.greater,
+              ">=": pc.greater_equal, "+": pc.add, "-": pc.subtract, "*": pc.multiply, "%": _mod}.get(op)
+        if op == "/":
+            return pc.divide(_float(a), _float(b))
+        if fn is None:
+            raise QueryError(f"unsupported operator {op}")
+        return fn(a, b)
+
+    def _case(self, e, rel):
+        n = rel.num_rows
+        result = None
+        remaining = pa.array(np.ones(n, dtype=bool))
+        operand = self.eval(e["operand"], rel) if e.get("operand") else None
+        out_vals = [None] * n
+        for cond, val in e["whens"]:
+            c = pc.equal(operand, self.eval(cond, rel)) if operand is not None else self.eval(cond, rel)
+            c = pc.fill_null(_as_array(_bool(c), n), False)
+            take = pc.and_(remaining, c)
+            v = _as_array(self.eval(val, rel), n).to_pylist()
+            for i, tk in enumerate(take.to_pylist()):
+                if tk:
+                    out_vals[i] = v[i]
+            remaining = pc.and_(remaining, pc.invert(c))
+        if e.get("else") is not None:
+            v = _as_array(self.eval(e["else"], rel), n).to_pylist()
+            for i, r in enumerate(remaining.to_pylist()):
+                if r:
+                    out_vals[i] = v[i]
+        result = pa.array(out_vals)
+        return result
+
+    def _call(self, e, rel):
+        name = e["name"]
+        if is_model_call(e):
+            k = node_key(e)
+            if k not in self.ai_values:
+                self.compute_ai(rel, [e])
+            v = self.ai_values[k]
+            return v
+        if name == "HINT":
+            return self.eval(e["args"][0], rel)
+        if name == "PROMPT":
+            raise QueryError("PROMPT is the input of an AI function, not a value")
+        if name in CPU_AI_FUNCTIONS:
+            from quail_b200.sql import documents
+            args = [self.eval(a, rel) for a in e["args"]]
+            return documents.call(name, args, rel.num_rows)
+        args = [self.eval(a, rel) for a in e["args"] if a.get("type") != "named_arg"]
+        fns = {
+            "UPPER": lambda a: pc.utf8_upper(a[0]), "LOWER": lambda a: pc.utf8_lower(a[0]),
+            "LENGTH": lambda a: pc.utf8_length(a[0]), "CHAR_LENGTH": lambda a: pc.utf8_length(a[0]),
+            "TRIM": lambda a: pc.utf8_trim_whitespace(a[0]), "ABS": lambda a: pc.abs(a[0]),
+            "ROUND": lambda a: pc.round(a[0], int(a[1].as_py()) if len(a) > 1 else 0),
+            "FLOOR": lambda a: pc.floor(a[0]), "CEIL": lambda a: pc.ceil(a[0]),
+            "COALESCE": lambda a: pc.coalesce(*a), "CONCAT": lambda a: pc.binary_join_element_wise(*[_str(x) for x in a], ""),
+            "SUBSTR": lambda a: _substr(a), "SUBSTRING": lambda a: _substr(a),
+            "STARTS_WITH": lambda a: pc.starts_with(a[0], a[1].as_py()),
+            "CONTAINS": lambda a: pc.match_substring(a[0], a[1].as_py()),
+            "REGEXP_LIKE": lambda a: pc.match_substring_regex(a[0], a[1].as_py()),
+            "ARRAY_LENGTH": lambda a: pc.list_value_length(a[0]),
+            "CARDINALITY": lambda a: pc.list_value_length(a[0]),
+            "IFF": lambda a: pc.if_else(_bool(a[0]), a[1], a[2]),
+            "NULLIF": lambda a: pc.if_else(pc.equal(a[0], a[1]), pa.scalar(None, a[0].type), a[0]),
+            "GREATEST": lambda a: pc.max_element_wise(*a), "LEAST": lambda a: pc.min_element_wise(*a),
+        }
+        if name in fns:
+            return fns[name](args)
+        raise QueryError(f"unknown function {name}")
+
+
+# ---------------------------------------------------------------- small helpers
+
+def _as_array(v, n):
+    if isinstance(v, pa.Scalar):
+        return pa.array([v.as_py()] * n, type=v.type if v.type != pa.null() else None)
+    if isinstance(v, pa.ChunkedArray):
+        return v.combine_chunks() if v.num_chunks != 1 else v.chunk(0)
+    return v
+
+
+def _as_mask(v):
+    if isinstance(v, pa.Scalar):
+        return v.as_py() is True
+    return pc.fill_null(_bool(v), False)
+
+
+def _bool(v):
+    t = v.type
+    if t == pa.bool_():
+        return v
+    if t == pa.null():
+        return pc.cast(v, pa.bool_()) if not isinstance(v, pa.Scalar) else pa.scalar(None, pa.bool_())
+    return pc.cast(v, pa.bool_())
+
+
+def _str(v):
+    return pc.cast(v, pa.string()) if v.type != pa.string() else v
+
+
+def _float(v):
+    return pc.cast(v, pa.float64()) if not pa.types.is_floating(v.type) else v
+
+
+def _mod(a, b):
+    return pc.subtract(a, pc.multiply(pc.floor(pc.divide(_float(a), _float(b))).cast(pa.int64()), b))
+
+
+def _substr(a):
+    start = int(a[1].as_py()) - 1
+    if len(a) > 2:
+        return pc.utf8_slice_codeunits(a[0], start, start + int(a[2].as_py()))
+    return pc.utf8_slice_codeunits(a[0], start)
+
+
+def _cast(v, to: str):
+    base = to.split("(")[0]
+    typ = {"INT": pa.int64(), "INTEGER": pa.int64(), "BIGINT": pa.int64(), "FLOAT": pa.float64(),
+           "DOUBLE": pa.float64(), "REAL": pa.float32(), "DECIMAL": pa.float64(), "NUMBER": pa.float64(),
+           "VARCHAR": pa.string(), "STRING": pa.string(), "TEXT": pa.string(), "BOOLEAN": pa.bool_(),
+           "BOOL": pa.bool_(), "DATE": pa.date32(), "TIMESTAMP": pa.timestamp("us")}.get(base)
+    if typ is None:
+        raise QueryError(f"unsupported CAST type {to}")
+    return pc.cast(v, typ)
+
+
+def _dedupe(names):
+    seen, out = {}, []
+    for n in names:
+        if n in seen:
+            seen[n] += 1
+            out.append(f"{n}_{seen[n]}")
+        else:
+            seen[n] = 0
+            out.append(n)
+    return out
+
+
+def _distinct(t: pa.Table) -> pa.Table:
+    if t.num_rows == 0:
+        return t
+    rows = {}
+    for i, r in enumerate(zip(*[c.to_pylist() for c in t.columns])):
+        key = json.dumps(r, default=str)
+        rows.setdefault(key, i)
+    return t.take(pa.array(sorted(rows.values())))
+
+
+def _to_pylist(v):
+    if isinstance(v, pa.Scalar):
+        return v.as_py()
+    return v.to_pylist()
+
+
+def _clean_phrase(text):
+    if text is None:
+        return None
+    s = str(text).strip()
+    if s.lower().startswith("phrase:"):
+        s = s[7:].strip()
+    return s or None
+
+
+def _span(doc: str, answer):
+    if not answer:
+        return None
+    i = doc.find(answer)
+    return None if i < 0 else {"start": i, "end": i + len(answer)}

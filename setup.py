@@ -11,7 +11,7 @@
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("quail_b200", "csrc")
@@ -44,10 +44,13 @@ ext_modules = [
     ),
 ]
 if native_sources:
-    ext_modules.append(CppExtension(
-        name="quail_b200._native",
+    from pybind11.setup_helpers import Pybind11Extension
+    ext_modules.append(Pybind11Extension(
+        "quail_b200._native",
         sources=native_sources,
-        extra_compile_args={"cxx": ["-O3", "-std=c++20", "-fvisibility=hidden"]},
+        cxx_std=20,
+        extra_compile_args=["-O3", "-fvisibility=hidden"],
+        extra_link_args=["-lpthread"],
     ))
 
 # torch's own arch list must not add targets: the -gencode above is the only one
