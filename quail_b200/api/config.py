@@ -46,6 +46,7 @@ class EngineConfig:
     weights: str | None = None
     parallel: str = "dp"
     chunk_tokens: int | None = None
+    tokenizer: str | None = None   # a tokenizer.json (or its directory), or "words" / "bytes"
     seed: int = 0
     extra: dict = field(default_factory=dict)
 

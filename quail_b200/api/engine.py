@@ -46,6 +46,24 @@ class RegionOutput:
 
 
 class ModelEngine:
+    @classmethod
+    def from_replica(cls, config: EngineConfig, model, arena, tokenizer=None) -> "ModelEngine":
+        """An engine around an already built model replica and arena (benchmarks, workers)."""
+        from quail_b200.engine.stage_executor import StageExecutor
+        from quail_b200.planner.budgets import Budgets
+        self = cls.__new__(cls)
+        self.config = config
+        self.cfg = check_config(config)
+        self.on_gpu = config.device != "cpu"
+        self.device = arena.device
+        self.tokenizer = tokenizer or load_tokenizer(config.tokenizer, self.cfg.vocab)
+        self.budgets = Budgets.for_model(self.cfg, config.device, gpus=1)
+        self.chunk_tokens = config.chunk_tokens or self.budgets.chunk_tokens
+        self.model = model
+        self.arena = arena
+        self.executor = StageExecutor(model, arena, self.chunk_tokens, gpu_timing=config.gpu_timing)
+        return self
+
     def __init__(self, config: EngineConfig, device_index: int = 0, pages: int | None = None):
         self.config = config
         self.cfg = check_config(config)
@@ -57,7 +75,7 @@ class ModelEngine:
             torch.cuda.set_device(self.device)
         else:
             self.device = torch.device("cpu")
-        self.tokenizer = load_tokenizer(config.weights, self.cfg.vocab)
+        self.tokenizer = load_tokenizer(config.tokenizer or config.weights, self.cfg.vocab)
         from quail_b200.planner.budgets import Budgets
         self.budgets = Budgets.for_model(self.cfg, config.device, gpus=1)
         self.chunk_tokens = config.chunk_tokens or self.budgets.chunk_tokens

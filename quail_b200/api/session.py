@@ -137,6 +137,10 @@ class Session:
         from quail_b200.sql.executor import has_model_call
         return has_model_call(tree)
 
+    def attach_engine(self, engine) -> None:
+        """Use an already started engine (a replica loaded elsewhere in this process)."""
+        self._engine = engine
+
     def engine(self):
         """The model engine (started on first use: weights loaded, arena sized)."""
         if self._engine is None:

@@ -103,7 +103,35 @@ class HFTokenizer:
         return out
 
 
+class WordTokenizer(ByteTokenizer):
+    """One token per word or punctuation mark, id from a stable hash of its text.
+
+    Lengths come out close to a BPE tokenizer's on English text, which makes
+    it the tokenizer of the synthetic benchmark tables; decode() is not
+    available (hashes do not invert), so it is not for AI.MAP output.
+    """
+
+    def __init__(self, vocab: int = 151_936):
+        super().__init__(vocab)
+        import re
+        self._split = re.compile(r"<\|[a-z_]+\|>|</?think>|\s*[A-Za-z0-9]+|\s*[^\sA-Za-z0-9]|\s+")
+
+    def encode(self, text: str) -> np.ndarray:
+        import zlib
+        out = []
+        for m in self._split.finditer(text):
+            piece = m.group(0)
+            sid = self.special.get(piece.strip()) if piece.strip() in self.special else None
+            out.append(sid if sid is not None else 1024 + zlib.crc32(piece.encode()) % (self.vocab - 1024))
+        return np.asarray(out, dtype=np.int32)
+
+    def decode(self, ids) -> str:
+        return " ".join(f"<{int(i)}>" for i in ids)
+
+
 def load_tokenizer(path: str | None, vocab: int):
+    if path == "words":
+        return WordTokenizer(vocab)
     if path is not None and os.path.exists(path if not os.path.isdir(path) else os.path.join(path, "tokenizer.json")):
         return HFTokenizer(path)
     return ByteTokenizer(vocab)

@@ -1,0 +1,247 @@
+"""Data-parallel worker processes: one model replica per GPU.
+
+The session's process spawns one worker per GPU (`CUDA_VISIBLE_DEVICES` =
+that GPU), talks to each over a Unix socket with length-prefixed JSON frames,
+and ships each region's documents as an Arrow IPC file in /dev/shm that the
+worker maps (the C++ side is quail_b200._native: frames, spawn, shm).
+Documents are hash-partitioned across the replicas by their content, so a
+document and every question about it land on one GPU and each question is
+asked once. Reference: crates/quail/src/workers.rs (spawn / connect / boot /
+run_region / revive / interrupt, 120 s connect patience), stages.rs
+(hash-partitioned stages) and shared.rs (/dev/shm tables).
+
+Failure handling, host side only: a worker that exits or closes its socket
+fails the region with its traceback; the next region revives (kills and
+re-spawns) every worker, which reloads the model.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+import tempfile
+import threading
+import time
+import zlib
+
+import pyarrow as pa
+
+from quail_b200 import _native
+
+PATIENCE_MS = 120_000
+MAX_FRAME = 1 << 34
+
+
+class WorkerError(RuntimeError):
+    pass
+
+
+def _config_dict(config) -> dict:
+    from dataclasses import asdict
+    return asdict(config)
+
+
+def docs_table(docs: list) -> pa.Table:
+    if docs and not isinstance(docs[0], str) and docs[0] is not None and not isinstance(docs[0], (bytes,)):
+        try:
+            return pa.table({"doc": pa.array([list(map(int, d)) for d in docs], pa.list_(pa.int32()))})
+        except TypeError:
+            pass
+    return pa.table({"doc": pa.array([None if d is None else str(d) for d in docs], pa.string())})
+
+
+def table_bytes(t: pa.Table) -> bytes:
+    sink = pa.BufferOutputStream()
+    with pa.ipc.new_stream(sink, t.schema) as w:
+        w.write_table(t)
+    return sink.getvalue().to_pybytes()
+
+
+def shard_of(doc, n: int) -> int:
+    if isinstance(doc, str) or doc is None:
+        b = ("" if doc is None else doc).encode()
+    else:
+        b = b",".join(str(int(x)).encode() for x in doc)
+    return zlib.crc32(b) % n
+
+
+class Worker:
+    def __init__(self, index: int, pid: int, fd: int):
+        self.index, self.pid, self.fd = index, pid, fd
+
+    def call(self, msg: dict, timeout_ms: int = -1) -> dict:
+        _native.send_frame(self.fd, json.dumps(msg).encode(), timeout_ms)
+        return self.receive(timeout_ms)
+
+    def receive(self, timeout_ms: int = -1) -> dict:
+        try:
+            reply = json.loads(_native.recv_frame(self.fd, MAX_FRAME, timeout_ms))
+        except _native.IpcClosed as exc:
+            raise WorkerError(f"worker {self.index} closed its connection (exit status "
+                              f"{_native.poll_exit(self.pid)})") from exc
+        if "error" in reply:
+            raise WorkerError(f"worker {self.index} failed:\n{reply['error']}")
+        return reply
+
+
+class WorkerPool:
+    """`gpus` worker processes behind the session; same run_region as ModelEngine."""
+
+    def __init__(self, config, python: str | None = None, boot: bool = True):
+        self.config = config
+        self.n = config.gpus
+        self.python = python or sys.executable
+        self.dir = tempfile.mkdtemp(prefix=f"qb-{os.getpid()}-")
+        self.sock = os.path.join(self.dir, "s")
+        self.listen_fd = _native.listen_unix(self.sock)
+        self.workers: list[Worker] = []
+        self._region = 0
+        self.tokenizer = None
+        self._spawn()
+        if boot:
+            self.boot()
+
+    # ------------------------------------------------------------ lifecycle
+    def _spawn(self):
+        pids = []
+        for i in range(self.n):
+            env = [f"QB_WORKER_INDEX={i}"]
+            if self.config.device != "cpu":
+                env.append(f"CUDA_VISIBLE_DEVICES={i}")
+            argv = [self.python, "-m", "quail_b200.runtime.worker_main", "--socket", self.sock, "--index", str(i)]
+            pids.append(_native.spawn(argv, env))
+        fds = {}
+        deadline = time.monotonic() + PATIENCE_MS / 1e3
+        while len(fds) < self.n:
+            for i, pid in enumerate(pids):
+                st = _native.poll_exit(pid)
+                if st >= 0 and i not in fds:
+                    self._kill_all(pids)
+                    raise WorkerError(f"worker {i} exited with status {st} before connecting")
+            if time.monotonic() > deadline:
+                self._kill_all(pids)
+                raise WorkerError("workers did not connect within the patience")
+            try:
+                fd = _native.accept_unix(self.listen_fd, 200)
+            except _native.IpcTimeout:
+                continue
+            hello = json.loads(_native.recv_frame(fd, 1 << 16, 10_000))
+            fds[int(hello["index"])] = fd
+        self.workers = [Worker(i, pids[i], fds[i]) for i in range(self.n)]
+
+    @staticmethod
+    def _kill_all(pids):
+        for p in pids:
+            _native.kill_pid(p, 9)
+        for p in pids:
+            for _ in range(100):
+                if _native.poll_exit(p) != -1:
+                    break
+                time.sleep(0.01)
+
+    def boot(self):
+        replies = self._all({"boot": _config_dict(self.config)})
+        self.boot_s = max(r.get("boot_s", 0.0) for r in replies)
+        from quail_b200.api.tokenizer import load_tokenizer
+        from quail_b200.api.config import check_config
+        self.tokenizer = load_tokenizer(self.config.tokenizer or self.config.weights, check_config(self.config).vocab)
+
+    def alive(self) -> bool:
+        return all(_native.poll_exit(w.pid) == -1 for w in self.workers)
+
+    def revive(self):
+        """Kill and re-spawn every worker, then boot them again (models reload)."""
+        self._kill_all([w.pid for w in self.workers])
+        for w in self.workers:
+            _native.close_fd(w.fd)
+        self._spawn()
+        self.boot()
+
+    def interrupt(self):
+        """Stop every worker now; the next region revives them."""
+        self._kill_all([w.pid for w in self.workers])
+
+    def close(self):
+        for w in self.workers:
+            try:
+                _native.send_frame(w.fd, json.dumps({"shutdown": True}).encode(), 2000)
+            except _native.IpcError:
+                pass
+        t0 = time.monotonic()
+        for w in self.workers:
+            while _native.poll_exit(w.pid) == -1 and time.monotonic() - t0 < 10:
+                time.sleep(0.02)
+            if _native.poll_exit(w.pid) == -1:
+                _native.kill_pid(w.pid, 9)
+            _native.close_fd(w.fd)
+        self.workers = []
+        _native.close_fd(self.listen_fd)
+        try:
+            os.unlink(self.sock)
+            os.rmdir(self.dir)
+        except OSError:
+            pass
+
+    def _all(self, msg: dict, per_worker: list | None = None) -> list:
+        """Send to every worker (or per_worker messages), then gather every reply in order."""
+        errors, replies = [], [None] * self.n
+
+        def one(i):
+            try:
+                m = per_worker[i] if per_worker is not None else msg
+                replies[i] = self.workers[i].call(m)
+            except Exception as exc:  # noqa: BLE001 - every worker is told to finish; errors re-raised below
+                errors.append(exc)
+
+        threads = [threading.Thread(target=one, args=(i,)) for i in range(self.n)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return replies
+
+    # ------------------------------------------------------------ regions
+    def run_region(self, preamble: str, docs: list, calls: list):
+        from dataclasses import asdict
+
+        from quail_b200.api.engine import RegionOutput
+        if not self.alive():
+            self.revive()
+        self._region += 1
+        shards = [[] for _ in range(self.n)]
+        for i, d in enumerate(docs):
+            shards[shard_of(d, self.n)].append(i)
+        paths, msgs = [], []
+        for w in range(self.n):
+            t = docs_table([docs[i] for i in shards[w]])
+            name = f"qb-{os.getpid()}-{self._region}-{w}"
+            path = _native.shm_write(name, table_bytes(t))
+            paths.append(path)
+            msgs.append({"region": {"preamble": preamble, "path": path, "calls": [asdict(c) for c in calls]}})
+        try:
+            replies = self._all(None, msgs)
+        finally:
+            for p in paths:
+                _native.unlink_path(p)
+        values = [None] * len(docs)
+        stats = {"passes": 0, "fresh_tokens": 0, "documents": 0, "rows": len(docs), "asked": 0,
+                 "per_worker": []}
+        for w, rep in enumerate(replies):
+            for j, i in enumerate(shards[w]):
+                values[i] = rep["values"][j]
+            for k in ("passes", "fresh_tokens", "documents", "asked"):
+                stats[k] += rep["stats"].get(k, 0)
+            stats["per_worker"].append(rep["stats"])
+        return RegionOutput(values=values, stats=stats)
+
+    @property
+    def chunk_tokens(self):
+        return self.config.chunk_tokens
+
+
+def content_hash(b: bytes) -> str:
+    return hashlib.sha256(b).hexdigest()[:16]

@@ -1,42 +1,66 @@
 """End-to-end timing of the flagship query through the public API.
 
-The timed region covers what a user's call pays per step: packing each
-chunk on the host, its host->device copy from pinned memory, the forward
-pass, and the device->host read of the answers, wall-clock with a device
-synchronize on both sides and the max over ranks.
+The timed region is one `Session.sql(...).run()` of
+
+    SELECT id FROM docs WHERE AI.IF(PROMPT('<16-word instruction> {0}', body))
+
+over a registered table of synthetic token-id bodies: SQL parsing and
+planning, prompt tokenization, chunk packing on the host, each chunk's
+host->device copy from pinned memory, the forward passes, and the
+device->host copy of every chunk's answers, wall-clock with a device
+synchronize on both sides; the max over ranks.
 """
 
 from __future__ import annotations
 
 import time
 
+import numpy as np
+import pyarrow as pa
 import torch
+
+INSTRUCTION = ("Does this document describe a product defect that a customer reported after using the item "
+               "for several weeks")
 
 
 def run_e2e(pipe, arena, cfg, args, rank: int, world: int, dev) -> dict:
     import torch.distributed as dist
 
-    from quail_b200.api.session import run_filter_query
+    import quail_b200 as quail
+    from quail_b200.api.engine import ModelEngine
     from quail_b200.utils.synthetic import make_workload, rows_for_tokens
 
     wl = make_workload(rows_for_tokens(args.steps * args.chunk_tokens), seed=2000 + rank)
+    table = pa.table({"id": np.arange(wl.rows, dtype=np.int64),
+                      "body": pa.array([b.tolist() for b in wl.bodies], pa.list_(pa.int32()))})
+    config = quail.EngineConfig(model=args.model, device="b200", chunk_tokens=args.chunk_tokens, tokenizer="words")
+    session = quail.Session(config=config)
+    engine = ModelEngine.from_replica(config, pipe, arena)
+    session.attach_engine(engine)
+    session.register("docs", table)
+    query = session.sql(f"SELECT id FROM docs WHERE AI.IF(PROMPT('{INSTRUCTION} {{0}}', body))")
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    result = run_filter_query(pipe, arena, wl, chunk_tokens=args.chunk_tokens)
+    result = query.run()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    stats = result["stats"]
-    t = torch.tensor([wall, float(wl.prompt_tokens()), float(wl.rows), float(stats.passes),
-                      float(stats.h2d_bytes), float(stats.d2h_bytes)], dtype=torch.float64, device=dev)
+    st = engine.executor.stats
+    tok = engine.tokenizer
+    from quail_b200.api.prompts import bind_prompt
+    bp = bind_prompt(f"{INSTRUCTION} {{0}}")
+    per_row = len(tok.encode(bp.preamble)) + len(tok.encode(bp.tail))
+    prompt_tokens = sum(len(b) for b in wl.bodies) + per_row * wl.rows
+    t = torch.tensor([wall, float(prompt_tokens), float(wl.rows), float(st.passes), float(st.h2d_bytes),
+                      float(st.d2h_bytes), float(result.table.num_rows)], dtype=torch.float64, device=dev)
     if world > 1:
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         wall = float(mx[0])
-    prompt, rows, passes, h2d, d2h = (float(v) for v in t[1:])
+    prompt, rows, passes, h2d, d2h, kept = (float(v) for v in t[1:])
     return {"value": round(prompt / wall, 1), "unit": "prompt tokens/s", "rows_per_second": round(rows / wall, 1),
             "h2d_bytes_per_step": int(h2d / max(passes, 1)), "d2h_bytes_per_step": int(d2h / max(passes, 1)),
-            "rows": int(rows), "passes": int(passes), "wall_s": round(wall, 3),
-            "api": "quail_b200.api.session.run_filter_query (AI.IF region over a registered token table)"}
+            "rows": int(rows), "kept_rows": int(kept), "passes": int(passes), "wall_s": round(wall, 3),
+            "api": "quail_b200.Session.sql(\"SELECT id FROM docs WHERE AI.IF(PROMPT(...))\").run()"}

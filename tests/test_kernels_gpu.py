@@ -260,3 +260,13 @@ def test_prefill_attention_mx_output():
     want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
     o8, sf = ops.prefill_attention(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale, fp8_out=True, mx=True)
     assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
+
+
+def test_row_argmax_lse():
+    R, V = 7, 151936
+    x = (torch.randn(R, V, device=DEV) * 3).bfloat16()
+    x[3, 12345] = 40.0
+    arg, lse = ops.row_argmax_lse(x)
+    xf = x.float()
+    assert torch.equal(arg.long(), xf.argmax(1))
+    assert torch.allclose(lse, torch.logsumexp(xf, 1), atol=1e-3, rtol=1e-4)

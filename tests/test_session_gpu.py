@@ -1,0 +1,39 @@
+"""The query API on a B200: SQL through the kernel pipeline (fp8 tiny Qwen3)."""
+
+import numpy as np
+import pyarrow as pa
+import pytest
+
+import quail_b200 as quail
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def session():
+    rng = np.random.default_rng(0)
+    words = ["ending", "music", "cast", "plot", "money", "great", "bad", "long"]
+    bodies = [" ".join(rng.choice(words, size=int(rng.integers(3, 40)))) for _ in range(40)]
+    cfg = quail.EngineConfig(model="qwen3-gpu-tiny", device="b200", chunk_tokens=2048)
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": list(range(40)), "body": bodies}))
+        yield s
+
+
+def test_filter_is_the_projection_of_the_same_call(session):
+    kept = session.sql("SELECT id FROM t WHERE AI.IF(PROMPT('Is it about music? {0}', body)) ORDER BY id").collect()
+    flags = session.sql("SELECT id, AI.IF(PROMPT('Is it about music? {0}', body)) AS f FROM t ORDER BY id").collect()
+    want = [i for i, f in zip(flags.column("id").to_pylist(), flags.column("f").to_pylist()) if f]
+    assert kept.column("id").to_pylist() == want
+
+
+def test_classify_map_and_score_on_the_kernels(session):
+    t = session.sql("""
+        SELECT id, AI.SCORE(PROMPT('Positive? {0}', body)) AS s,
+               AI.CLASSIFY(body, ['praise', 'complaint'], {'probabilities': true}) AS k,
+               AI.MAP(body, 'Summarize.', 4) AS m
+        FROM t WHERE id < 6 ORDER BY id""").collect()
+    assert t.num_rows == 6
+    assert all(0.0 <= s <= 1.0 for s in t.column("s").to_pylist())
+    assert set(t.column("k").to_pylist()) <= {"praise", "complaint"}
+    assert all(isinstance(m, str) for m in t.column("m").to_pylist())
