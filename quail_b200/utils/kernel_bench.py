@@ -100,14 +100,62 @@ def run(model: str, T: int, iters: int = 10) -> list[dict]:
     return out
 
 
+def attention_case(cfg, tokens: int, seed: int = 0):
+    """A packed chunk like the AI.IF benchmark's: 48-token shared prefix, lognormal rows."""
+    import numpy as np
+
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.engine.chunk import ChunkPacker, SeqSpec
+    from quail_b200.utils.synthetic import make_workload, rows_for_tokens
+    wl = make_workload(rows_for_tokens(tokens), seed=seed)
+    arena = KVArena(1, 4096, 128, cfg.num_kv_heads, cfg.head_dim, device="cuda")
+    pool = arena.pool
+    pool.alloc("p", 48)
+    specs, n = [], 0
+    for i, b in enumerate(wl.bodies):
+        toks = np.concatenate([b, wl.suffix])
+        if n + len(toks) > tokens:
+            break
+        pool.alloc(i, len(toks))
+        specs.append(SeqSpec(reads=[("p", 48)], own_key=i, own_start=0, tokens=toks, pos_start=48, readout=True))
+        n += len(toks)
+    chunk = ChunkPacker(pool, "cuda").pack(specs)
+    kc, vc = arena.layer(0)
+    kc.normal_()
+    vc.normal_()
+    q = torch.randn(chunk.num_tokens, cfg.num_q_heads, 128, device="cuda").bfloat16()
+    # causal FLOPs actually needed: each token attends to the prefix and its own earlier tokens
+    ctx = 0.0
+    for s_ in specs:
+        L = len(s_.tokens)
+        ctx += L * 48 + L * (L + 1) / 2
+    flops = 4.0 * ctx * cfg.num_q_heads * 128
+    return chunk, q, kc, vc, flops
+
+
+def run_attention(model: str, tokens: int, iters: int = 10) -> dict:
+    from quail_b200.ops import reference as ref
+    cfg = MODEL_CONFIGS[model]
+    chunk, q, kc, vc, flops = attention_case(cfg, tokens)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    ms = _timeit(lambda: ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list,
+                                               ref.softmax_scale(128), fp8_out=True, mx=True), iters, flush=flush)
+    assert ops.read_and_clear_error(0) == 0
+    return {"case": "prefill_attention", "tokens": chunk.num_tokens, "ms": ms, "useful_tflops": flops / ms / 1e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen3-4b-fp8")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "attention"])
     args = ap.parse_args()
-    for row in run(args.model, args.tokens, args.iters):
-        print(json.dumps(row))
+    if args.only in ("all", "gemm"):
+        for row in run(args.model, args.tokens, args.iters):
+            print(json.dumps(row))
+    if args.only in ("all", "attention"):
+        print(json.dumps(run_attention(args.model, args.tokens, args.iters)))
 
 
 if __name__ == "__main__":
