@@ -33,6 +33,10 @@ void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch
 
 void row_argmax_lse(const torch::Tensor& logits, torch::Tensor& arg, torch::Tensor& lse);
 
+void prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
+                          const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
+                          double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
+
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
 
@@ -77,6 +81,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_kv", &qb::qk_norm_rope_kv);
   m.def("final_norm_readout", &qb::final_norm_readout);
   m.def("prefill_attention", &qb::prefill_attention);
+  m.def("prefill_attention_tc", &qb::prefill_attention_tc, "tcgen05/TMEM packed-prompt prefill attention");
   m.def("read_and_clear_error", &qb::read_and_clear_error);
   m.attr("EPI_BF16") = (int)qb::kEpiBf16;
   m.attr("EPI_RESIDUAL") = (int)qb::kEpiResidual;

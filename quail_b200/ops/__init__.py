@@ -24,6 +24,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     launch_count,
     native,
     prefill_attention,
+    prefill_attention_tc,
     qk_norm_rope_kv,
     quant_rows,
     read_and_clear_error,

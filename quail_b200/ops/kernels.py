@@ -217,6 +217,20 @@ def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale
     return out
 
 
+def prefill_attention_tc(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale: float, *,
+                         fp8_out: bool = True, out=None, out_scale=None):
+    """The tcgen05/TMEM attention kernel (needs 4 q heads per KV head): bf16 or e4m3 + MX scale bytes."""
+    T, QH = q.shape[0], q.shape[1]
+    if out is None:
+        out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if fp8_out else torch.bfloat16, device=q.device)
+    if fp8_out and out_scale is None:
+        out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+    _count()
+    native().prefill_attention_tc(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out,
+                                  out_scale if fp8_out else None)
+    return (out, out_scale) if fp8_out else out
+
+
 def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, normed=None):
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
     if logits is None:

@@ -140,8 +140,11 @@ def run_attention(model: str, tokens: int, iters: int = 10) -> dict:
     flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
     ms = _timeit(lambda: ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list,
                                                ref.softmax_scale(128), fp8_out=True, mx=True), iters, flush=flush)
+    ms_tc = _timeit(lambda: ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list,
+                                                     ref.softmax_scale(128)), iters, flush=flush)
     assert ops.read_and_clear_error(0) == 0
-    return {"case": "prefill_attention", "tokens": chunk.num_tokens, "ms": ms, "useful_tflops": flops / ms / 1e9}
+    return {"case": "prefill_attention", "tokens": chunk.num_tokens, "mma_sync_ms": ms,
+            "mma_sync_useful_tflops": flops / ms / 1e9, "tcgen05_ms": ms_tc, "tcgen05_useful_tflops": flops / ms_tc / 1e9}
 
 
 def main():

@@ -270,3 +270,17 @@ def test_row_argmax_lse():
     xf = x.float()
     assert torch.equal(arg.long(), xf.argmax(1))
     assert torch.allclose(lse, torch.logsumexp(xf, 1), atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("P", [16, 128])
+def test_prefill_attention_tcgen05(P):
+    specs = [(100, [48, 100]), (7, [48, 7]), (64, [48, 300, 64]), (130, [48, 130]), (1, [48, 1]),
+             (20, [48, 200, 40]), (300, [48, 300])]
+    q, kc, vc, seqs, pl = _segmented_case(P, specs)
+    tiles = ref.attention_tiles(seqs)
+    scale = ref.softmax_scale(128)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    out = ops.prefill_attention_tc(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale, fp8_out=False)
+    assert rel_err(out, want) < 1e-2
+    o8, sf = ops.prefill_attention_tc(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale)
+    assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
