@@ -37,6 +37,18 @@ void prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& k_cache, 
                           const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
 
+void tp_ag_gemm(const torch::Tensor& a_local, const torch::Tensor& sfa_local, const std::vector<int64_t>& a_peer,
+                const std::vector<int64_t>& sfa_peer, const std::vector<int64_t>& flag_peer,
+                const torch::Tensor& tile_ready, int64_t epoch, int64_t rank, int64_t rpr, const torch::Tensor& b,
+                const torch::Tensor& sfb, int64_t mode, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
+void tp_gemm_rs(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
+                const std::vector<int64_t>& slot_ptrs, int64_t ld_slot, const std::vector<int64_t>& counter_ptrs,
+                int64_t rank, int64_t rpr);
+void tp_reduce_norm(const torch::Tensor& slots, int64_t tp_slots, const torch::Tensor& counters, int64_t want,
+                    torch::Tensor& resid, const torch::Tensor& w, double eps, torch::Tensor& a_sym,
+                    torch::Tensor& sf_sym, int64_t row0, torch::Tensor& done_ctr, int64_t done_base,
+                    torch::Tensor& flag, int64_t epoch);
+
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
 
@@ -83,6 +95,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &qb::prefill_attention);
   m.def("prefill_attention_tc", &qb::prefill_attention_tc, "tcgen05/TMEM packed-prompt prefill attention");
   m.def("read_and_clear_error", &qb::read_and_clear_error);
+  m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");
+  m.def("tp_gemm_rs", &qb::tp_gemm_rs, "MX GEMM -> reduce-scatter fused: epilogue pushes tiles to owner ranks");
+  m.def("tp_reduce_norm", &qb::tp_reduce_norm, "sum RS slots + residual, RMSNorm, MX quant into the AG buffer");
   m.attr("EPI_BF16") = (int)qb::kEpiBf16;
   m.attr("EPI_RESIDUAL") = (int)qb::kEpiResidual;
   m.attr("EPI_SWIGLU_FP8") = (int)qb::kEpiSwigluFp8;

@@ -98,7 +98,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled TMA load into this CTA's shared memory (no multicast).
+// 2-D tiled TMA load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
                                             int c0, int c1) {
   asm volatile(

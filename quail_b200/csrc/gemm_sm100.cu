@@ -16,7 +16,7 @@
 // bf16 projections (attention.py:480-481).
 //
 // Warp roles (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer (one elected thread; no cluster multicast)
+//   warp 0      TMA producer (one elected thread; each CTA loads its own tiles)
 //   warp 1      TMEM allocator + UMMA issuer (one elected thread)
 //   warps 2..   epilogue: BN/32 warps; warp w reads TMEM lanes 32*(w%4)..+31
 //               and half (w-2)/4 of the tile's columns.

@@ -1,0 +1,612 @@
+// K12: tensor-parallel projections with the collective fused into the GEMM,
+// over NVLink peer memory (no NCCL on these paths).
+//
+// Layout: the residual stream is sharded by tokens (rank r owns rows
+// [r * rpr, (r + 1) * rpr), rpr a multiple of 128); weights are sharded by
+// output columns (QKV, gate_up) or by input columns (o_proj, down).
+//
+//   AG -> GEMM (QKV, gate_up): every rank's normalized e4m3 shard and its MX
+//     scale atoms sit at their own rows of a symmetric buffer. The GEMM CTA
+//     has two gather warps that copy peer shards, one 128-row m-tile at a
+//     time, from the peer's buffer into the same rows of the local one with
+//     plain P2P loads (each remote tile crosses NVLink once), then release a
+//     per-m-tile ready word. The TMA producer starts with the local shard's
+//     m-tiles and waits (bounded) on the ready word of each remote m-tile
+//     before its first TMA load. Peers announce their shard with a ready flag
+//     (written by the norm kernel that produced it).
+//   GEMM -> RS (o_proj, down): the epilogue writes each bf16 output tile
+//     straight into the owning rank's receive slot for this source (P2P
+//     stores), fences, and adds the tile count to that rank's counter.
+//   rs_reduce_norm: each rank waits (bounded) for every source's tiles, sums
+//     the slots into its residual rows, applies RMSNorm and writes the e4m3 +
+//     MX scales of its shard for the next AG -> GEMM, then raises its flag.
+//
+// TMA loads here read only this GPU's memory, each CTA its own tiles; peer
+// memory is read by ld.global / written by st.global in the gather warps and
+// the RS epilogue. Every wait on a peer has a clock budget and sets an error
+// code instead of hanging.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+#include "mx_common.cuh"
+
+namespace qb {
+
+constexpr int kTpMax = 8;
+
+enum TpMode : int { kTpAgBf16 = 0, kTpAgSwiglu = 1, kTpRs = 2 };
+
+struct TpParams {
+  int M, N, K;            // M = tokens over all ranks, N = this rank's output columns
+  int rank, tp, rpr;      // rows per rank (multiple of 128)
+  uint32_t epoch;
+  // AG
+  const uint8_t* a_peer[kTpMax];     // each rank's symmetric A buffer [M, K] e4m3
+  const uint8_t* sfa_peer[kTpMax];   // each rank's symmetric A scale atoms
+  const uint32_t* flag_peer[kTpMax]; // each rank's shard-ready flag
+  uint8_t* a_local;                  // == a_peer[rank]
+  uint8_t* sfa_local;
+  uint32_t* tile_ready;              // local, one word per m-tile
+  // RS
+  __nv_bfloat16* rs_slot[kTpMax];    // on rank d: receive slot of this source, [rpr, ldr] bf16
+  int ld_slot;
+  uint32_t* rs_counter[kTpMax];      // on rank d: tile counter of this source
+  // outputs (AG modes, all M rows)
+  __nv_bfloat16* D;
+  int ldd;
+  uint8_t* Y;
+  int ldy;
+  uint8_t* Ysf;
+  const uint8_t* sfa;  // A scale atoms read by the producer (a_local's)
+  const uint8_t* sfb;
+  int* err;
+  int num_m_tiles, num_n_tiles;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// spin until *p >= want (wrap-safe), with a clock budget
+template <bool SYS>
+__device__ __forceinline__ bool wait_word(const uint32_t* p, uint32_t want, int* err) {
+  const long long t0 = clock64();
+  while (true) {
+    const uint32_t v = SYS ? ld_acquire_sys(p) : ld_acquire_gpu(p);
+    if ((int32_t)(v - want) >= 0) return true;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      atomicCAS(err, 0, kErrTimeoutPeer);
+      return false;
+    }
+  }
+}
+
+constexpr int kTpWarps = 12;  // producer, MMA, 8 epilogue, 2 gather
+constexpr int kTpThreads = kTpWarps * 32;
+
+template <int MODE>
+__global__ void __launch_bounds__(kTpThreads, 1)
+    tp_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const TpParams p) {
+  constexpr int BM = 128, BN = kMxBN, STAGES = kMxStages;
+  constexpr int EPI_THREADS = BN;
+  constexpr int TMEM_COLS = 512;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kMxABytes;
+  uint8_t* sSFA = sB + STAGES * kMxBBytes;
+  uint8_t* sSFB = sSFA + STAGES * kMxSfaBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * kMxSfbBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* done_bar = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  int* push_count = reinterpret_cast<int*>(tmem_slot + 4);  // [kTpMax] tiles this CTA sent to each rank
+  volatile int* gather_ok = push_count + kTpMax;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_k = p.K / 128;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int sfb_chunks = (p.N + 127) / 128;
+  const int tpr = p.rpr / BM;  // m-tiles per rank
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, EPI_THREADS);
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x < kTpMax) push_count[threadIdx.x] = 0;
+  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // m-tile of tile t: the local shard's tiles first, then the ring of peers
+  auto tile_of = [&](int t, int& tm, int& tn) {
+    const int tr = t % p.num_m_tiles;
+    tn = t / p.num_m_tiles;
+    tm = (MODE == kTpRs) ? tr : (tr + p.rank * tpr) % p.num_m_tiles;
+  };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_of(t, tm, tn);
+        if (MODE != kTpRs && tm / tpr != p.rank) {
+          // a peer's m-tile: wait until the gather warps of some CTA copied it here
+          if (!wait_word<false>(&p.tile_ready[tm], p.epoch, p.err)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
+        const int nchunks = min(BN / 128, sfb_chunks - tn * (BN / 128));
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kMxABytes + kMxBBytes + kMxSfaBytes + nchunks * 512);
+          tma_load_2d(&tmA, &full[stage], sA + stage * kMxABytes, kb * 128, tm * BM);
+          tma_load_2d(&tmB, &full[stage], sB + stage * kMxBBytes, kb * 128, tn * BN);
+          bulk_load(sSFA + stage * kMxSfaBytes, p.sfa + ((size_t)tm * num_k + kb) * 512, 512, &full[stage]);
+          for (int c = 0; c < nchunks; ++c)
+            bulk_load(sSFB + stage * kMxSfbBytes + c * 512,
+                      p.sfb + ((size_t)(tn * (BN / 128) + c) * num_k + kb) * 512, 512, &full[stage]);
+          last_par[stage] = (int)phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(&full[s], (uint32_t)last_par[s], p.err, kErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      const uint32_t t_sfa = tmem_base + kMxSfaCol;
+      const uint32_t t_sfb = tmem_base + kMxSfbCol;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(acc_empty, aphase ^ 1, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tmem_cp_sf(t_sfa, sf_chunk_desc(smem_u32(sSFA + stage * kMxSfaBytes)));
+#pragma unroll
+          for (int c = 0; c < BN / 128; ++c)
+            tmem_cp_sf(t_sfb + c * 4, sf_chunk_desc(smem_u32(sSFB + stage * kMxSfbBytes + c * 512)));
+          const uint32_t a0 = smem_u32(sA + stage * kMxABytes);
+          const uint32_t b0 = smem_u32(sB + stage * kMxBBytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_mx(tmem_base, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32),
+                    make_idesc_mx(BM, BN, k, k), t_sfa | ((uint32_t)k << 30), t_sfb | ((uint32_t)k << 30),
+                    (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) {
+          tc_commit(acc_full);
+          aphase ^= 1;
+        }
+      }
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, p.err, kErrTimeoutMma);
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int h = ew >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_of(t, tm, tn);
+      const int m = tm * BM + row;
+      const int n0 = tn * BN + h * 128;
+      if (!mbar_wait(acc_full, aphase, p.err, kErrTimeoutEpilogue)) break;
+      aphase ^= 1;
+      tc_fence_after();
+      float acc[128];
+      const uint32_t taddr = tmem_base + lane_base + (uint32_t)(h * 128);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        QB_TMEM_LD32(taddr + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      if (m >= p.M) continue;
+      if constexpr (MODE == kTpAgBf16) {
+        __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + n0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 8)
+          if (n0 + j < p.N) st_bf16x8(dst + j, &acc[j]);
+      } else if constexpr (MODE == kTpRs) {
+        // rows of rank d's shard go to d's receive slot for this source
+        const int d = m / p.rpr;
+        __nv_bfloat16* dst = p.rs_slot[d] + (size_t)(m - d * p.rpr) * p.ld_slot + n0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 8)
+          if (n0 + j < p.N) st_bf16x8(dst + j, &acc[j]);
+        if (row == 0 && h == 0) push_count[d] += 1;  // one count per tile (rows of a tile share d)
+      } else {
+        const int out0 = tn * (BN / 2) + h * 64;
+        if (out0 >= p.N / 2) continue;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = silu_f(acc[i]) * acc[64 + i];
+        uint8_t e[2];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          float amax = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(acc[g * 32 + i]));
+          e[g] = ue8m0_of(amax);
+          const float inv = ue8m0_inv(e[g]);
+          uint8_t* dst = p.Y + (size_t)m * p.ldy + out0 + g * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 16) {
+            __align__(16) __nv_fp8x4_e4m3 pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              pk[i] = __nv_fp8x4_e4m3(make_float4(acc[g * 32 + j + 4 * i] * inv, acc[g * 32 + j + 4 * i + 1] * inv,
+                                                  acc[g * 32 + j + 4 * i + 2] * inv,
+                                                  acc[g * 32 + j + 4 * i + 3] * inv));
+            *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(pk);
+          }
+        }
+        const int kst = out0 / 128, kblk = (out0 % 128) / 32;
+        const int ko = p.N / 2 / 128;
+        uint8_t* sf = p.Ysf + ((size_t)(m / 128) * ko + kst) * 512 + (m % 32) * 16 + ((m % 128) / 32) * 4 + kblk;
+        *reinterpret_cast<uint16_t*>(sf) = (uint16_t)e[0] | ((uint16_t)e[1] << 8);
+      }
+    }
+    if constexpr (MODE == kTpRs) {
+      // every epilogue thread's P2P stores are visible system-wide before the counts
+      __threadfence_system();
+      named_bar_sync(1, EPI_THREADS);
+      if (warp == 2 && lane == 0) {
+        for (int d = 0; d < p.tp; ++d)
+          if (push_count[d]) atomicAdd_system(p.rs_counter[d], (unsigned)push_count[d]);
+      }
+    }
+  } else if constexpr (MODE != kTpRs) {
+    // ------------------------------------------------------------ gather warps (AG)
+    const int gt = threadIdx.x - 10 * 32;  // 0..63
+    const int remote_tiles = (p.tp - 1) * tpr;
+    int seen_peer = -1;
+    bool ok = true;
+    for (int g = blockIdx.x; g < remote_tiles && ok; g += gridDim.x) {
+      const int o = (p.rank + 1 + g / tpr) % p.tp;  // nearest peer first
+      const int tm = o * tpr + g % tpr;
+      if (o != seen_peer) {
+        // one thread waits on the peer's flag; both gather warps read the outcome
+        if (gt == 0) *gather_ok = wait_word<true>(p.flag_peer[o], p.epoch, p.err) ? 1 : 0;
+        named_bar_sync(2, 64);
+        if (!*gather_ok) {
+          ok = false;
+          break;
+        }
+        seen_peer = o;
+      }
+      // rows [tm*128, tm*128+128) x K bytes, then the m-tile's scale atoms
+      const size_t a_off = (size_t)tm * BM * p.K;
+      const uint4* src = reinterpret_cast<const uint4*>(p.a_peer[o] + a_off);
+      uint4* dst = reinterpret_cast<uint4*>(p.a_local + a_off);
+      const int n16 = BM * p.K / 16;
+      for (int i = gt; i < n16; i += 64 * 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * 64 < n16) v[u] = src[i + u * 64];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * 64 < n16) dst[i + u * 64] = v[u];
+      }
+      const size_t s_off = (size_t)tm * num_k * 512;
+      const uint4* ssrc = reinterpret_cast<const uint4*>(p.sfa_peer[o] + s_off);
+      uint4* sdst = reinterpret_cast<uint4*>(p.sfa_local + s_off);
+      for (int i = gt; i < num_k * 32; i += 64) sdst[i] = ssrc[i];
+      __threadfence();
+      named_bar_sync(2, 64);
+      if (gt == 0) {
+        fence_proxy_async_global();
+        st_release_gpu(&p.tile_ready[tm], p.epoch);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc<TMEM_COLS>(tmem_base);
+  }
+}
+
+// ---------------------------------------------------------------- reduce + norm
+// One warp per local row; each lane owns 8 columns of every 256-column slab.
+// With `tp_slots` > 0 the CTA first waits for every source's tiles; the row is
+// then residual + sum of the slots. The result is the new residual row; its
+// RMSNorm goes out as e4m3 + UE8M0 atoms into this rank's rows of the
+// symmetric A buffer. The last CTA to finish raises this rank's flag.
+template <int H>
+__global__ void rs_reduce_norm_kernel(const __nv_bfloat16* __restrict__ slots, int tp_slots, int rpr,
+                                      const uint32_t* __restrict__ counters, uint32_t want,
+                                      __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ w,
+                                      float eps, uint8_t* __restrict__ a_sym, uint8_t* __restrict__ sf_sym,
+                                      int row0, uint32_t* __restrict__ done_ctr, uint32_t done_want,
+                                      uint32_t* __restrict__ flag, uint32_t epoch, int* err) {
+  constexpr int SLABS = H / 256;
+  __shared__ int go;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int s = 0; s < tp_slots && ok; ++s) ok = wait_word<true>(&counters[s], want, err) ? 1 : 0;
+    go = ok;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (go && r < rpr) {
+    float v[SLABS][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int s = 0; s < SLABS; ++s) {
+      ld_bf16x8f(resid + (size_t)r * H + s * 256 + lane * 8, v[s]);
+      for (int k = 0; k < tp_slots; ++k) {
+        float u[8];
+        ld_bf16x8f(slots + ((size_t)k * rpr + r) * H + s * 256 + lane * 8, u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[s][i] += u[i];
+      }
+      if (tp_slots) st_bf16x8(resid + (size_t)r * H + s * 256 + lane * 8, v[s]);
+      // the stored residual is bf16: normalize what was stored
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[s][i] = __bfloat162float(__float2bfloat16(v[s][i]));
+        ss += v[s][i] * v[s][i];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rinv = rsqrtf(ss / H + eps);
+    const int m = row0 + r;  // row in the full [M, H] symmetric buffer
+#pragma unroll
+    for (int s = 0; s < SLABS; ++s) {
+      float wv[8];
+      ld_bf16x8f(w + s * 256 + lane * 8, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[s][i] = v[s][i] * rinv * wv[i];
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const uint8_t e = ue8m0_of(amax);
+      const float inv = ue8m0_inv(e);
+      __nv_fp8x4_e4m3 a(make_float4(v[s][0] * inv, v[s][1] * inv, v[s][2] * inv, v[s][3] * inv));
+      __nv_fp8x4_e4m3 b(make_float4(v[s][4] * inv, v[s][5] * inv, v[s][6] * inv, v[s][7] * inv));
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&a);
+      pk.y = *reinterpret_cast<uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(a_sym + (size_t)m * H + s * 256 + lane * 8) = pk;
+      if ((lane & 3) == 0) {
+        const int j = s * 8 + (lane >> 2);  // 32-wide K block
+        sf_sym[((size_t)(m >> 7) * (H / 128) + (j >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (j & 3)] = e;
+      }
+    }
+  }
+  // last CTA out raises this rank's shard-ready flag for the peers
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(done_ctr, 1u);
+    if (prev + 1 == done_want) st_release_sys(flag, epoch);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct TpBuffers {
+  std::vector<int64_t> a_peer, sfa_peer, flag_peer, rs_slot, rs_counter;
+};
+
+static void fill_ptrs(TpParams& p, const std::vector<int64_t>& a, const std::vector<int64_t>& sfa,
+                      const std::vector<int64_t>& flag, const std::vector<int64_t>& slot,
+                      const std::vector<int64_t>& ctr) {
+  for (int i = 0; i < kTpMax; ++i) {
+    p.a_peer[i] = i < (int)a.size() ? reinterpret_cast<const uint8_t*>(a[i]) : nullptr;
+    p.sfa_peer[i] = i < (int)sfa.size() ? reinterpret_cast<const uint8_t*>(sfa[i]) : nullptr;
+    p.flag_peer[i] = i < (int)flag.size() ? reinterpret_cast<const uint32_t*>(flag[i]) : nullptr;
+    p.rs_slot[i] = i < (int)slot.size() ? reinterpret_cast<__nv_bfloat16*>(slot[i]) : nullptr;
+    p.rs_counter[i] = i < (int)ctr.size() ? reinterpret_cast<uint32_t*>(ctr[i]) : nullptr;
+  }
+}
+
+template <int MODE>
+static void launch_tp(const CUtensorMap& ta, const CUtensorMap& tb, TpParams& p, cudaStream_t st, int dev) {
+  constexpr int smem = kMxSmem + 64;
+  static bool configured[64] = {false};
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(tp_gemm_mx_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured[dev] = true;
+  }
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  tp_gemm_mx_kernel<MODE><<<std::min(tiles, num_sms(dev)), kTpThreads, smem, st>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// AG -> GEMM. a_local: this rank's symmetric A buffer [M, K] e4m3 (its own
+// rows already written); sfa_local its scale atoms; peers' buffers and flags
+// by pointer. mode 0: out bf16 [M, N]; mode 1: SwiGLU out e4m3 [M, N/2] + atoms.
+void tp_ag_gemm(const torch::Tensor& a_local, const torch::Tensor& sfa_local, const std::vector<int64_t>& a_peer,
+                const std::vector<int64_t>& sfa_peer, const std::vector<int64_t>& flag_peer,
+                const torch::Tensor& tile_ready, int64_t epoch, int64_t rank, int64_t rpr, const torch::Tensor& b,
+                const torch::Tensor& sfb, int64_t mode, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf) {
+  const int M = a_local.size(0), K = a_local.size(1), N = b.size(0);
+  const int tp = (int)a_peer.size();
+  TORCH_CHECK(tp >= 1 && tp <= kTpMax && rpr % 128 == 0 && (int64_t)M == rpr * tp, "tp_ag_gemm: M = tp x rpr");
+  TORCH_CHECK(K % 128 == 0 && N % 16 == 0, "tp_ag_gemm: K % 128, N % 16");
+  TORCH_CHECK(tile_ready.numel() >= M / 128 && tile_ready.scalar_type() == at::kInt, "tile_ready words");
+  const int dev = a_local.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  TpParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.rank = (int)rank;
+  p.tp = tp;
+  p.rpr = (int)rpr;
+  p.epoch = (uint32_t)epoch;
+  fill_ptrs(p, a_peer, sfa_peer, flag_peer, {}, {});
+  p.a_local = reinterpret_cast<uint8_t*>(a_local.data_ptr());
+  p.sfa_local = sfa_local.data_ptr<uint8_t>();
+  p.sfa = p.sfa_local;
+  p.tile_ready = reinterpret_cast<uint32_t*>(tile_ready.data_ptr<int>());
+  p.sfb = sfb.data_ptr<uint8_t>();
+  p.err = device_error_word(dev);
+  p.num_m_tiles = M / 128;
+  p.num_n_tiles = (N + kMxBN - 1) / kMxBN;
+  CUtensorMap ta = make_tmap_2d(a_local.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a_local.stride(0), 128,
+                                128, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (mode == 0) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == M && out.size(1) == N, "bf16 out [M, N]");
+    p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    p.ldd = out.stride(0);
+    launch_tp<kTpAgBf16>(ta, tb, p, st, dev);
+  } else {
+    TORCH_CHECK(N % kMxBN == 0 && out.scalar_type() == at::kFloat8_e4m3fn && out.size(1) == N / 2 && out_sf.has_value(),
+                "SwiGLU e4m3 out [M, N/2] + scale atoms");
+    p.Y = reinterpret_cast<uint8_t*>(out.data_ptr());
+    p.ldy = out.stride(0);
+    p.Ysf = out_sf->data_ptr<uint8_t>();
+    launch_tp<kTpAgSwiglu>(ta, tb, p, st, dev);
+  }
+}
+
+// GEMM -> RS: a [M, K] e4m3 (local), output rows pushed to their owner's slot.
+void tp_gemm_rs(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
+                const std::vector<int64_t>& slot_ptrs, int64_t ld_slot, const std::vector<int64_t>& counter_ptrs,
+                int64_t rank, int64_t rpr) {
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  const int tp = (int)slot_ptrs.size();
+  TORCH_CHECK(tp >= 1 && tp <= kTpMax && (int64_t)M == rpr * tp && rpr % 128 == 0, "tp_gemm_rs: M = tp x rpr");
+  TORCH_CHECK(K % 128 == 0 && N % 16 == 0 && ld_slot % 8 == 0, "tp_gemm_rs shapes");
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  TpParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.rank = (int)rank;
+  p.tp = tp;
+  p.rpr = (int)rpr;
+  fill_ptrs(p, {}, {}, {}, slot_ptrs, counter_ptrs);
+  p.ld_slot = (int)ld_slot;
+  p.sfa = sfa.data_ptr<uint8_t>();
+  p.sfb = sfb.data_ptr<uint8_t>();
+  p.err = device_error_word(dev);
+  p.num_m_tiles = M / 128;
+  p.num_n_tiles = (N + kMxBN - 1) / kMxBN;
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a.stride(0), 128, 128,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  launch_tp<kTpRs>(ta, tb, p, st, dev);
+}
+
+void tp_reduce_norm(const torch::Tensor& slots, int64_t tp_slots, const torch::Tensor& counters, int64_t want,
+                    torch::Tensor& resid, const torch::Tensor& w, double eps, torch::Tensor& a_sym,
+                    torch::Tensor& sf_sym, int64_t row0, torch::Tensor& done_ctr, int64_t done_base,
+                    torch::Tensor& flag, int64_t epoch) {
+  const int rpr = resid.size(0), H = resid.size(1);
+  TORCH_CHECK(resid.scalar_type() == at::kBFloat16 && resid.is_contiguous(), "residual rows bf16");
+  const int dev = resid.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  const int rows_per_cta = 8;
+  const int grid = (rpr + rows_per_cta - 1) / rows_per_cta;
+  auto sp = reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr());
+#define QB_RS_CASE(HH)                                                                                           \
+  if (H == HH) {                                                                                                 \
+    rs_reduce_norm_kernel<HH><<<grid, rows_per_cta * 32, 0, st>>>(                                               \
+        sp, (int)tp_slots, rpr, reinterpret_cast<const uint32_t*>(counters.data_ptr<int>()), (uint32_t)want,     \
+        reinterpret_cast<__nv_bfloat16*>(resid.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), \
+        (float)eps, reinterpret_cast<uint8_t*>(a_sym.data_ptr()), sf_sym.data_ptr<uint8_t>(), (int)row0,         \
+        reinterpret_cast<uint32_t*>(done_ctr.data_ptr<int>()), (uint32_t)(done_base + grid),                    \
+        reinterpret_cast<uint32_t*>(flag.data_ptr<int>()), (uint32_t)epoch, device_error_word(dev));            \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
+    return;                                                                                                      \
+  }
+  QB_RS_CASE(1024)
+  QB_RS_CASE(2048)
+  QB_RS_CASE(2560)
+  QB_RS_CASE(4096)
+  QB_RS_CASE(5120)
+#undef QB_RS_CASE
+  TORCH_CHECK(false, "tp_reduce_norm: unsupported hidden size ", H);
+}
+
+}  // namespace qb

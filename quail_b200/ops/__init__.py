@@ -20,6 +20,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     sf_bytes,
     rmsnorm_quant_mx,
     quant_rows_mx,
+    count_launch,
     kernels_available,
     launch_count,
     native,

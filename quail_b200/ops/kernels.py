@@ -21,7 +21,7 @@ def launch_count() -> int:
     return _LAUNCHES[0]
 
 
-def _count(n: int = 1) -> None:
+def count_launch(n: int = 1) -> None:
     _LAUNCHES[0] += n
 
 
@@ -64,13 +64,13 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
             out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
         if out_scale is None:
             out_scale = torch.empty(N // 256, M, dtype=torch.float32, device=a.device)
-        _count()
+        count_launch()
         C.gemm(a, b, sa, sb, sb_gran, epi, out, out_scale, None, bn)
         return out, out_scale
     if out is None:
         width = N // 2 if epi == EPI_SWIGLU_BF16 else N
         out = torch.empty(M, width, dtype=torch.bfloat16, device=a.device)
-    _count()
+    count_launch()
     C.gemm(a, b, sa, sb, sb_gran, epi, out, None, residual, bn)
     return out
 
@@ -91,7 +91,7 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     """
     C = native()
     M, N = a.shape[0], b.shape[0]
-    _count()
+    count_launch()
     if epi == EPI_SWIGLU_FP8:
         if out is None:
             out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
@@ -113,7 +113,7 @@ def rmsnorm_quant_mx(x: torch.Tensor, w: torch.Tensor, eps: float, *, out=None, 
         out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
     if out_sf is None:
         out_sf = torch.empty(sf_bytes(T, H), dtype=torch.uint8, device=x.device)
-    _count()
+    count_launch()
     native().rmsnorm_quant_mx(x, w, eps, out, out_sf, T)
     return out, out_sf
 
@@ -123,7 +123,7 @@ def quant_rows_mx(x: torch.Tensor, *, swiglu: bool = False, rows: int | None = N
     K = x.shape[1] // 2 if swiglu else x.shape[1]
     y = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=x.device)
     sf = torch.empty(sf_bytes(T, K), dtype=torch.uint8, device=x.device)
-    _count()
+    count_launch()
     native().quant_rows_mx(x, swiglu, y, sf, T)
     return y, sf
 
@@ -131,7 +131,7 @@ def quant_rows_mx(x: torch.Tensor, *, swiglu: bool = False, rows: int | None = N
 def embed_gather(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=torch.bfloat16, device=ids.device)
-    _count()
+    count_launch()
     native().embed_gather(ids, table, out)
     return out
 
@@ -146,12 +146,12 @@ def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, *, fp8: bool = T
             out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
         if out_scale is None:
             out_scale = torch.empty(H // 128, T, dtype=torch.float32, device=x.device)
-        _count()
+        count_launch()
         native().rmsnorm_quant(x, w, eps, out, out_scale, None, T)
         return out, out_scale
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
-    _count()
+    count_launch()
     native().rmsnorm_quant(x, w, eps, None, None, out, T)
     return out
 
@@ -163,11 +163,11 @@ def quant_rows(x: torch.Tensor, *, swiglu: bool = False, fp8: bool = True, rows:
     if fp8:
         y = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=x.device)
         s = torch.empty(K // 128, T, dtype=torch.float32, device=x.device)
-        _count()
+        count_launch()
         native().quant_rows(x, swiglu, y, s, None, T)
         return y, s
     y = torch.empty(T, K, dtype=torch.bfloat16, device=x.device)
-    _count()
+    count_launch()
     native().quant_rows(x, swiglu, None, None, y, T)
     return y
 
@@ -179,7 +179,7 @@ def qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, k_cache,
     T = qkv.shape[0] if rows is None else rows
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, 128, dtype=torch.bfloat16, device=qkv.device)
-    _count()
+    count_launch()
     native().qk_norm_rope_kv(qkv, positions, q_norm_w, k_norm_w, cos_sin, slots, q_out, k_cache,
                              v_cache, num_q_heads, num_kv_heads, eps, norm_qk, T)
     return q_out
@@ -198,7 +198,7 @@ def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale
             out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
         if out_scale is None:
             out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
-        _count()
+        count_launch()
         native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out, out_scale)
         return out, out_scale
     if fp8_out:
@@ -206,13 +206,13 @@ def prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale
             out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
         if out_scale is None:
             out_scale = torch.empty(QH, T, dtype=torch.float32, device=q.device)
-        _count()
+        count_launch()
         native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale,
                                    out, out_scale)
         return out, out_scale
     if out is None:
         out = torch.empty(T, QH * 128, dtype=torch.bfloat16, device=q.device)
-    _count()
+    count_launch()
     native().prefill_attention(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out, None)
     return out
 
@@ -225,7 +225,7 @@ def prefill_attention_tc(q, k_cache, v_cache, seqs, tiles, page_list, softmax_sc
         out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if fp8_out else torch.bfloat16, device=q.device)
     if fp8_out and out_scale is None:
         out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
-    _count()
+    count_launch()
     native().prefill_attention_tc(q, k_cache, v_cache, seqs, tiles, page_list, softmax_scale, out,
                                   out_scale if fp8_out else None)
     return (out, out_scale) if fp8_out else out
@@ -235,7 +235,7 @@ def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, n
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
     if logits is None:
         logits = torch.empty(rows.numel(), head_rows.shape[0], dtype=torch.float32, device=x.device)
-    _count()
+    count_launch()
     native().final_norm_readout(x, rows, norm_w, eps, head_rows, logits, normed)
     return logits
 
@@ -245,7 +245,7 @@ def row_argmax_lse(logits: torch.Tensor):
     R = logits.shape[0]
     arg = torch.empty(R, dtype=torch.int32, device=logits.device)
     lse = torch.empty(R, dtype=torch.float32, device=logits.device)
-    _count()
+    count_launch()
     native().row_argmax_lse(logits, arg, lse)
     return arg, lse
 
