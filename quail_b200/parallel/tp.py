@@ -100,9 +100,13 @@ class TPQwen3:
     """One rank's shard of a Qwen3 dense model and its forward over a packed chunk."""
 
     def __init__(self, cfg: DecoderConfig, group, *, seed: int = 0, max_tokens: int = 16384, answer_ids=(0, 1),
-                 full_weights: dict | None = None):
+                 full_weights: dict | None = None, comm: str = "fused"):
         from quail_b200.ops.quant import interleave_gate_up_mx, quantize_weight_mx
         assert cfg.fp8 and cfg.head_dim == 128
+        assert comm in ("fused", "nccl")
+        # "nccl": the baseline the fused kernels are measured against: NCCL
+        # all-gather / reduce-scatter around the same MX GEMMs
+        self.comm = comm
         self.cfg = cfg
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.st = TPState(cfg, group, max_tokens, self.device)
@@ -205,6 +209,22 @@ class TPQwen3:
         ops.native().tp_gemm_rs(a, sfa, w, sfw, st.peer(slot_off), H,
                                 [p + st.off_ctr + 4 * st.rank for p in st.peers], st.rank, rpr)
 
+    # ------------------------------------------------------------ NCCL baseline pieces
+    def _nccl_ag(self, h_local, w_norm, M, rpr):
+        from quail_b200 import ops
+        H = self.cfg.hidden
+        x8, sf = ops.rmsnorm_quant_mx(h_local, w_norm, self.cfg.rms_eps)
+        full = torch.empty(M, H, dtype=torch.uint8, device=self.device)
+        sff = torch.empty(sf.numel() * self.st.tp, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(full, x8.view(torch.uint8), group=self.st.group)
+        dist.all_gather_into_tensor(sff, sf, group=self.st.group)
+        return full.view(torch.float8_e4m3fn), sff
+
+    def _nccl_rs_add(self, part, h_local):
+        out = torch.empty_like(h_local)
+        dist.reduce_scatter_tensor(out, part, group=self.st.group)
+        h_local += out
+
     # ------------------------------------------------------------ forward
     @torch.no_grad()
     def forward_chunk(self, chunk, arena) -> torch.Tensor:
@@ -224,22 +244,34 @@ class TPQwen3:
         slots = torch.full((M,), -1, dtype=torch.int32, device=dev)
         slots[:T] = chunk.slots
         h = ops.embed_gather(ids[r * rpr:(r + 1) * rpr].contiguous(), self.embed)  # own residual rows
+        fused = self.comm == "fused"
         for li, L in enumerate(self.layers):
             kc, vc = arena.layer(li)
-            self._norm(h, L["ln1"], M, rpr, tp_slots=tp if li > 0 else 0)
-            qkv = self._ag(M, H, rpr, L["wqkv"], L["sqkv"], mode=0)
+            if fused:
+                self._norm(h, L["ln1"], M, rpr, tp_slots=tp if li > 0 else 0)
+                qkv = self._ag(M, H, rpr, L["wqkv"], L["sqkv"], mode=0)
+            else:
+                xa, sa = self._nccl_ag(h, L["ln1"], M, rpr)
+                qkv = ops.gemm_mx(xa, sa, L["wqkv"], L["sqkv"])
             q = ops.qk_norm_rope_kv(qkv, pos, L["qn"], L["kn"], self.cos_sin, slots, kc, vc, self.qh, self.kh,
                                     cfg.rms_eps)
             o8 = torch.zeros(M, self.qh * 128, dtype=torch.float8_e4m3fn, device=dev)  # padding rows stay 0
             os_ = torch.zeros(ops.sf_bytes(M, self.qh * 128), dtype=torch.uint8, device=dev)
             ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale, out=o8,
                                      out_scale=os_)
-            self._rs(o8, os_, L["wo"], L["so"], rpr)
-            self._norm(h, L["ln2"], M, rpr, tp_slots=tp)
-            a8, as_ = self._ag(M, H, rpr, L["wgu"], L["sgu"], mode=1)
-            self._rs(a8, as_, L["wd"], L["sd"], rpr)
-        # last down-projection: sum it into the residual (the final norm runs in the readout)
-        self._norm(h, self.final_norm, M, rpr, tp_slots=tp)
+            if fused:
+                self._rs(o8, os_, L["wo"], L["so"], rpr)
+                self._norm(h, L["ln2"], M, rpr, tp_slots=tp)
+                a8, as_ = self._ag(M, H, rpr, L["wgu"], L["sgu"], mode=1)
+                self._rs(a8, as_, L["wd"], L["sd"], rpr)
+            else:
+                self._nccl_rs_add(ops.gemm_mx(o8, os_, L["wo"], L["so"]), h)
+                xa, sa = self._nccl_ag(h, L["ln2"], M, rpr)
+                a8, as_ = ops.gemm_mx(xa, sa, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
+                self._nccl_rs_add(ops.gemm_mx(a8, as_, L["wd"], L["sd"]), h)
+        if fused:
+            # last down-projection: sum it into the residual (the final norm runs in the readout)
+            self._norm(h, self.final_norm, M, rpr, tp_slots=tp)
         rows = chunk.final_rows.long()
         mine = (rows >= r * rpr) & (rows < (r + 1) * rpr)
         local = torch.where(mine, rows - r * rpr, torch.zeros_like(rows)).int()
