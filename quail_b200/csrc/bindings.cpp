@@ -49,6 +49,28 @@ void tp_reduce_norm(const torch::Tensor& slots, int64_t tp_slots, const torch::T
                     torch::Tensor& sf_sym, int64_t row0, torch::Tensor& done_ctr, int64_t done_base,
                     torch::Tensor& flag, int64_t epoch);
 
+void moe_route(const torch::Tensor& logits, int64_t E, int64_t topk, torch::Tensor& ids, torch::Tensor& wts,
+               torch::Tensor& pos, torch::Tensor& counts);
+int64_t moe_plan_ints(int64_t E, int64_t Epr, int64_t tcap);
+void moe_plan(torch::Tensor& counts, const std::vector<int64_t>& counts_all_peer,
+              const std::vector<int64_t>& cflag_peer, const torch::Tensor& counts_all_local,
+              const torch::Tensor& cflag_local, torch::Tensor& plan, torch::Tensor& cum, int64_t rank, int64_t E,
+              int64_t tcap, int64_t epoch);
+void moe_sort(const torch::Tensor& ids, const torch::Tensor& pos, int64_t n, const torch::Tensor& plan, int64_t E,
+              torch::Tensor& src_list);
+void moe_gate_up(const torch::Tensor& x8, const torch::Tensor& xsf, const torch::Tensor& src_list,
+                 const torch::Tensor& wts, const torch::Tensor& plan, int64_t rank, int64_t E, int64_t topk,
+                 int64_t tcap, const std::vector<int64_t>& recv_a_peer, const std::vector<int64_t>& recv_sf_peer,
+                 const std::vector<int64_t>& recv_meta_peer, const std::vector<int64_t>& recv_count_peer,
+                 const torch::Tensor& recv_a, const torch::Tensor& recv_sf, const torch::Tensor& recv_count,
+                 const torch::Tensor& w_gu, const torch::Tensor& s_gu, torch::Tensor& y, torch::Tensor& ysf);
+void moe_down(const torch::Tensor& y, const torch::Tensor& ysf, const torch::Tensor& plan, int64_t E, int64_t tcap,
+              const torch::Tensor& recv_meta, const torch::Tensor& w_d, const torch::Tensor& s_d,
+              const std::vector<int64_t>& comb_peer, const std::vector<int64_t>& comb_counter_peer);
+void moe_combine(const torch::Tensor& comb, int64_t M, int64_t topk, const torch::Tensor& counter, int64_t want,
+                 torch::Tensor& resid, const c10::optional<torch::Tensor>& w, double eps,
+                 const c10::optional<torch::Tensor>& y8, const c10::optional<torch::Tensor>& ysf);
+
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
 
@@ -98,6 +120,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");
   m.def("tp_gemm_rs", &qb::tp_gemm_rs, "MX GEMM -> reduce-scatter fused: epilogue pushes tiles to owner ranks");
   m.def("tp_reduce_norm", &qb::tp_reduce_norm, "sum RS slots + residual, RMSNorm, MX quant into the AG buffer");
+  m.def("moe_route", &qb::moe_route, "MoE router: softmax, top-k, renormalized weights, per-expert slots");
+  m.def("moe_plan_ints", &qb::moe_plan_ints);
+  m.def("moe_plan", &qb::moe_plan, "MoE count exchange over peers and dispatch / tile planning");
+  m.def("moe_sort", &qb::moe_sort);
+  m.def("moe_gate_up", &qb::moe_gate_up, "token dispatch (P2P) fused into the grouped MX gate_up GEMM + SwiGLU");
+  m.def("moe_down", &qb::moe_down, "grouped MX down GEMM with the weighted combine pushed from the epilogue");
+  m.def("moe_combine", &qb::moe_combine, "sum expert rows into the residual + next RMSNorm as MX");
   m.attr("EPI_BF16") = (int)qb::kEpiBf16;
   m.attr("EPI_RESIDUAL") = (int)qb::kEpiResidual;
   m.attr("EPI_SWIGLU_FP8") = (int)qb::kEpiSwigluFp8;

@@ -26,6 +26,7 @@ enum ErrorCode : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutPeer = 4,
   kErrBadShape = 5,
+  kErrCapacity = 6,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

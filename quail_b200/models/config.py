@@ -84,8 +84,13 @@ QWEN3_TINY = DecoderConfig(name="qwen3-tiny", layers=2, hidden=256, num_q_heads=
 # the smallest model the GPU kernels take (head_dim 128, hidden multiple of 256)
 QWEN3_GPU_TINY = DecoderConfig(name="qwen3-gpu-tiny", layers=2, hidden=1024, num_q_heads=8,
                                num_kv_heads=4, head_dim=128, intermediate=1024)
+# the smallest MoE the GPU kernels take: 16 experts, top-4, expert width 256
+QWEN3_MOE_GPU_TINY = DecoderConfig(name="qwen3-moe-gpu-tiny", layers=2, hidden=1024, num_q_heads=8,
+                                   num_kv_heads=2, head_dim=128, intermediate=1024, num_experts=16, top_k=4,
+                                   moe_intermediate=256)
 
-CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY)}
+CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
+                               QWEN3_MOE_GPU_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -96,4 +101,5 @@ MODEL_CONFIGS = {
     "qwen3-30b-a3b-fp8": QWEN3_30B_A3B,
     "qwen3-tiny": QWEN3_TINY,
     "qwen3-gpu-tiny": QWEN3_GPU_TINY,
+    "qwen3-moe-gpu-tiny": QWEN3_MOE_GPU_TINY,
 }

@@ -181,14 +181,22 @@ class Qwen3Reference:
         self.layers = []
         for i in range(cfg.layers):
             p = f"model.layers.{i}."
-            self.layers.append({
+            L = {
                 "ln1": f(ckpt[p + "input_layernorm.weight"]), "ln2": f(ckpt[p + "post_attention_layernorm.weight"]),
                 "qn": f(ckpt[p + "self_attn.q_norm.weight"]), "kn": f(ckpt[p + "self_attn.k_norm.weight"]),
                 "wq": f(dequantized(ckpt, p + "self_attn.q_proj")), "wk": f(dequantized(ckpt, p + "self_attn.k_proj")),
                 "wv": f(dequantized(ckpt, p + "self_attn.v_proj")), "wo": f(dequantized(ckpt, p + "self_attn.o_proj")),
-                "wg": f(dequantized(ckpt, p + "mlp.gate_proj")), "wu": f(dequantized(ckpt, p + "mlp.up_proj")),
-                "wd": f(dequantized(ckpt, p + "mlp.down_proj")),
-            })
+            }
+            if cfg.is_moe:
+                # router (kept bf16 in checkpoints) and the experts' SwiGLU weights
+                L["router"] = f(ckpt[p + "mlp.gate.weight"])
+                L["experts"] = [tuple(f(dequantized(ckpt, p + f"mlp.experts.{e}.{n}"))
+                                      for n in ("gate_proj", "up_proj", "down_proj"))
+                                for e in range(cfg.num_experts)]
+            else:
+                L.update(wg=f(dequantized(ckpt, p + "mlp.gate_proj")), wu=f(dequantized(ckpt, p + "mlp.up_proj")),
+                         wd=f(dequantized(ckpt, p + "mlp.down_proj")))
+            self.layers.append(L)
         self.head = f(head_weight(ckpt, cfg))
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=device)
         self.scale = ref.softmax_scale(cfg.head_dim)
@@ -235,10 +243,29 @@ class Qwen3Reference:
             o = self._q(o) if self.cfg.fp8 else self._bf(o)
             h = self._bf(h + o @ L["wo"].t())
             x = self._q(self._bf(ref.rmsnorm(h, L["ln2"], cfg.rms_eps)))
+            if cfg.is_moe:
+                h = self._bf(h + self._moe(x, self._bf(ref.rmsnorm(h, L["ln2"], cfg.rms_eps)), L))
+                continue
             a = ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t())
             a = self._q(a) if self.cfg.fp8 else self._bf(a)
             h = self._bf(h + a @ L["wd"].t())
         return h
+
+    def _moe(self, x: torch.Tensor, xr: torch.Tensor, L) -> torch.Tensor:
+        """Softmax router, top-k with renormalized weights, SwiGLU experts (Qwen3-MoE)."""
+        logits = self._bf(xr @ L["router"].t())
+        ids, wts = ref.moe_route(logits, self.cfg.top_k)
+        out = torch.zeros_like(x)
+        for e, (wg, wu, wd) in enumerate(L["experts"]):
+            rows, ks = (ids == e).nonzero(as_tuple=True)
+            if rows.numel() == 0:
+                continue
+            xe = x[rows]
+            a = ref.silu_mul(xe @ wg.t(), xe @ wu.t())
+            a = self._q(a) if self.cfg.fp8 else self._bf(a)
+            # each weighted expert row is stored in bf16 before the sum over k
+            out.index_add_(0, rows, self._bf((a @ wd.t()) * wts[rows, ks][:, None]))
+        return out
 
     @torch.no_grad()
     def forward_chunk(self, chunk, arena) -> torch.Tensor:

@@ -93,3 +93,13 @@ def attention_tiles(seqs: torch.Tensor, block_q: int = 32) -> torch.Tensor:
 
 def softmax_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+def moe_route(logits: torch.Tensor, top_k: int):
+    """Qwen3-MoE routing: softmax over experts (fp32), top-k, weights renormalized to sum 1.
+
+    Returns (expert ids [T, k] int64, weights [T, k] fp32).
+    """
+    p = torch.softmax(logits.float(), dim=-1)
+    w, ids = p.topk(top_k, dim=-1)
+    return ids, w / w.sum(dim=-1, keepdim=True)

@@ -1,0 +1,173 @@
+"""Expert-parallel MoE layer on the fused dispatch/combine kernels.
+
+W ranks (one process per GPU) each own E / W experts and run attention on
+their own tokens (data-parallel attention). Per MoE layer, every rank runs,
+in stream order (kernels in `quail_b200/csrc/moe.cu`):
+
+  router GEMM (bf16 tcgen05) -> moe_route -> moe_plan (count exchange with
+  every peer) -> moe_sort -> moe_gate_up (dispatch warps push token rows to
+  the experts' owners while the grouped GEMM consumes arrived experts) ->
+  moe_down (epilogue pushes weighted rows back to each token's home) ->
+  moe_combine (sum of the K rows + residual, next layer's RMSNorm as MX).
+
+With W = 1 the same kernels run on local buffers: the dispatch is the
+permutation into expert-contiguous rows, the combine the weighted un-permute.
+For W > 1 the receive buffers, combine buffers, counters and flags live in
+one symmetric arena (torch.distributed symmetric memory gives the peer
+pointers; every byte between GPUs is moved by the kernels).
+
+Reference: MoE runs on one GPU only, through vLLM's fused Triton experts
+(quail/backends/quail/executor/moe.py:12-87; FP8Experts asserts
+tp == ep == dp == 1); expert parallelism is this engine's own.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from quail_b200.models.config import DecoderConfig
+
+
+def _align(n: int, a: int) -> int:
+    return -(-n // a) * a
+
+
+class EPState:
+    """Buffers, peer pointers and monotonic counters of the MoE layers of one rank."""
+
+    def __init__(self, cfg: DecoderConfig, max_tokens: int, device, group=None):
+        import torch.distributed as dist
+        from quail_b200 import ops
+        assert cfg.is_moe and cfg.fp8
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        self.W = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        E, K, H, I = cfg.num_experts, cfg.top_k, cfg.hidden, cfg.moe_intermediate
+        assert E % self.W == 0 and H % 256 == 0 and I % 128 == 0 and (2 * I) % 256 == 0
+        self.E, self.K, self.H, self.I = E, K, H, I
+        self.Epr = E // self.W
+        self.M_max = _align(max_tokens, 128)
+        # rows one rank can receive: every token of every rank sends at most
+        # min(K, Epr) rows here; each local expert pads to 128
+        self.R_cap = self.W * self.M_max * min(K, self.Epr) + self.Epr * 128
+        self.t_cap = self.R_cap // 128
+        dev = self.device
+        i32 = torch.int32
+        n_items = self.M_max * K
+        self.ids = torch.zeros(n_items, dtype=i32, device=dev)
+        self.wts = torch.zeros(n_items, dtype=torch.float32, device=dev)
+        self.pos = torch.zeros(n_items, dtype=i32, device=dev)
+        self.src_list = torch.zeros(n_items, dtype=i32, device=dev)
+        self.counts = torch.zeros(E, dtype=i32, device=dev)
+        self.plan = torch.zeros(ops.native().moe_plan_ints(E, self.Epr, self.t_cap), dtype=i32, device=dev)
+        self.cum = torch.zeros(self.Epr, dtype=i32, device=dev)
+        self.y = torch.empty(self.R_cap, I, dtype=torch.float8_e4m3fn, device=dev)
+        self.ysf = torch.empty(ops.sf_bytes(self.R_cap, I), dtype=torch.uint8, device=dev)
+        # the arena: [recv A | recv SF | recv meta | comb | recv counts | comb counter | counts_all | cflags]
+        sizes = [
+            ("recv_a", self.R_cap * H),
+            ("recv_sf", ops.sf_bytes(self.R_cap, H)),
+            ("recv_meta", self.R_cap * 8),
+            ("comb", n_items * H * 2),
+            ("recv_count", 4 * self.Epr),
+            ("comb_counter", 4),
+            ("counts_all", 4 * 2 * self.W * E),
+            ("cflag", 4 * 2 * self.W),
+        ]
+        self.off = {}
+        total = 0
+        for name, nbytes in sizes:
+            self.off[name] = total
+            total += _align(nbytes, 256)
+        if self.W > 1:
+            import torch.distributed._symmetric_memory as symm
+            self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
+            self.buf.zero_()
+            name = group.group_name if hasattr(group, "group_name") else dist.group.WORLD.group_name
+            self.handle = symm.rendezvous(self.buf, name)
+            self.peers = [int(p) for p in self.handle.buffer_ptrs]
+        else:
+            self.buf = torch.zeros(total, dtype=torch.uint8, device=dev)
+            self.peers = [self.buf.data_ptr()]
+        self.epoch = 0          # MoE layers run so far (count-exchange flags carry it)
+        self.comb_units = 0     # cumulative (row, 128-column) units this rank expects in its combine buffer
+        if self.W > 1:
+            torch.cuda.synchronize(dev)
+            dist.barrier(group)
+
+    # ------------------------------------------------------------ views
+    def _view(self, name, nbytes):
+        o = self.off[name]
+        return self.buf[o:o + nbytes]
+
+    def recv_a(self):
+        return self._view("recv_a", self.R_cap * self.H).view(torch.float8_e4m3fn).view(self.R_cap, self.H)
+
+    def recv_sf(self):
+        from quail_b200 import ops
+        return self._view("recv_sf", ops.sf_bytes(self.R_cap, self.H))
+
+    def recv_meta(self):
+        return self._view("recv_meta", self.R_cap * 8).view(torch.int32).view(self.R_cap, 2)
+
+    def comb(self, M):
+        return self._view("comb", M * self.K * self.H * 2).view(torch.bfloat16).view(M * self.K, self.H)
+
+    def recv_count(self):
+        return self._view("recv_count", 4 * self.Epr).view(torch.int32)
+
+    def comb_counter(self):
+        return self._view("comb_counter", 4).view(torch.int32)
+
+    def counts_all(self):
+        return self._view("counts_all", 4 * 2 * self.W * self.E).view(torch.int32)
+
+    def cflag(self):
+        return self._view("cflag", 4 * 2 * self.W).view(torch.int32)
+
+    def peer(self, name) -> list[int]:
+        return [p + self.off[name] for p in self.peers]
+
+    def plan_header(self) -> tuple[int, int]:
+        """(m-tiles, dispatch units) of the last plan (synchronizes; for tests)."""
+        h = self.plan[:2].tolist()
+        return h[0], h[1]
+
+    # ------------------------------------------------------------ one MoE layer
+    def forward(self, x8, xsf, xb, h, L, next_norm=None, eps: float = 1e-6):
+        """MoE MLP of one layer for this rank's M tokens.
+
+        x8/xsf: the post-attention RMSNorm of `h` as e4m3 + MX atoms, xb the
+        same in bf16 (router input). h [M, H] bf16 is updated in place
+        (residual + expert outputs). With `next_norm`, returns the next
+        layer's input RMSNorm of the new h as (e4m3, atoms); else None.
+        """
+        from quail_b200 import ops
+        C = ops.native()
+        M = h.shape[0]
+        assert M <= self.M_max, f"{M} tokens > the MoE buffers' {self.M_max}"
+        E, K = self.E, self.K
+        logits = ops.gemm(xb, L["router"], bn=128)
+        self.epoch += 1
+        ops.count_launch(6)
+        C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+        C.moe_plan(self.counts, self.peer("counts_all") if self.W > 1 else [],
+                   self.peer("cflag") if self.W > 1 else [], self.counts_all(), self.cflag(),
+                   self.plan, self.cum, self.rank, E, self.t_cap, self.epoch)
+        C.moe_sort(self.ids, self.pos, M * K, self.plan, E, self.src_list)
+        C.moe_gate_up(x8, xsf, self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
+                      self.peer("recv_a"), self.peer("recv_sf"), self.peer("recv_meta"), self.peer("recv_count"),
+                      self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
+        C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, self.recv_meta(), L["wd"], L["sd"],
+                   self.peer("comb"), self.peer("comb_counter"))
+        self.comb_units = (self.comb_units + M * K * (self.H // 128)) & 0xFFFFFFFF
+        want = self.comb_units  # compared modulo 2^32 on the device
+        if next_norm is None:
+            C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, None, eps, None, None)
+            return None
+        y8 = torch.empty(M, self.H, dtype=torch.float8_e4m3fn, device=h.device)
+        ysf = torch.empty(ops.sf_bytes(M, self.H), dtype=torch.uint8, device=h.device)
+        C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, next_norm, eps, y8, ysf)
+        return y8, ysf
