@@ -36,9 +36,13 @@ def test_moe_route(M, E, K):
     C.moe_route(logits, E, K, ids, wts, pos, counts)
     rid, rw = ref.moe_route(logits.float(), K)
     got_ids = ids.view(M, K).long()
-    # same weights in the same (descending) order; ids equal except at exact ties
+    # same weights in the same (descending) order; at exact ties (bf16 logits
+    # tie often) any of the tied experts is a valid pick
     assert torch.allclose(wts.view(M, K), rw, atol=1e-5)
-    assert (got_ids == rid).float().mean().item() > 0.99
+    probs = torch.softmax(logits.float(), dim=-1)
+    top = probs.topk(K, dim=-1).values
+    assert torch.allclose(probs.gather(1, got_ids), top, atol=1e-6)
+    assert torch.equal(got_ids.sort(1).values.unique_consecutive(dim=1).shape[1] * torch.ones(1), K * torch.ones(1))
     # slots: for each expert, positions 0..count-1 each used once
     assert torch.equal(counts.cpu(), torch.bincount(got_ids.flatten().cpu(), minlength=E).int())
     for e in range(E):
@@ -102,11 +106,12 @@ def test_moe_layer_single_rank(M):
         ids = st.ids[:M * K].view(M, K).long()
         wts = st.wts[:M * K].view(M, K)
         rid, rw = ref.moe_route((xb.float() @ L["router"].float().t()).bfloat16().float(), K)
-        assert (ids == rid).float().mean().item() > 0.98
+        assert (ids.sort(1).values == rid.sort(1).values).all(1).float().mean().item() > 0.9
         x = ops.dequantize_mx(x8, xs)
         want = h0 + _moe_ref(x, ids, wts, ex)
         assert rel_err(h, want) < 2e-2, (step, rel_err(h, want))
-        assert rel_err(h.float() - h0, want - h0) < 3e-2
+        # the expert contribution itself (h is bf16: compare against the rounded sum)
+        assert rel_err(h.float() - h0, want.bfloat16().float() - h0) < 3e-2
         # the next layer's input norm
         want_n = ref.rmsnorm(h.float(), ln1.float(), 1e-6)
         assert rel_err(ops.dequantize_mx(y8, ysf), want_n) < 6e-2
