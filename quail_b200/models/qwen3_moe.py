@@ -168,6 +168,16 @@ class Qwen3MoePipeline:
         return h
 
     @torch.no_grad()
+    def idle_pass(self) -> None:
+        """The MoE half of every layer with no tokens of this rank (expert parallelism)."""
+        cfg, w = self.cfg, self.w
+        h = torch.empty(0, cfg.hidden, dtype=torch.bfloat16, device=w.device)
+        e8 = torch.empty(0, cfg.hidden, dtype=torch.float8_e4m3fn, device=w.device)
+        esf = torch.empty(0, dtype=torch.uint8, device=w.device)
+        for L in w.layers:
+            self.ep.forward(e8, esf, h, h, L, next_norm=None, eps=cfg.rms_eps)
+
+    @torch.no_grad()
     def forward_chunk(self, chunk, arena) -> torch.Tensor:
         from quail_b200 import ops
         cfg, w = self.cfg, self.w

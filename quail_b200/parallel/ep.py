@@ -149,10 +149,15 @@ class EPState:
         M = h.shape[0]
         assert M <= self.M_max, f"{M} tokens > the MoE buffers' {self.M_max}"
         E, K = self.E, self.K
-        logits = ops.gemm(xb, L["router"], bn=128)
         self.epoch += 1
-        ops.count_launch(6)
-        C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+        ops.count_launch(5)
+        if M > 0:
+            logits = ops.gemm(xb, L["router"], bn=128)
+            ops.count_launch(1)
+            C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+        else:
+            # a rank without tokens this step still serves its experts to the others
+            x8 = self.recv_a()[:0]
         C.moe_plan(self.counts, self.peer("counts_all") if self.W > 1 else [],
                    self.peer("cflag") if self.W > 1 else [], self.counts_all(), self.cflag(),
                    self.plan, self.cum, self.rank, E, self.t_cap, self.epoch)
@@ -171,3 +176,40 @@ class EPState:
         ysf = torch.empty(ops.sf_bytes(M, self.H), dtype=torch.uint8, device=h.device)
         C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, next_norm, eps, y8, ysf)
         return y8, ysf
+
+
+def run_lockstep(executor, pipe, cpu_group) -> None:
+    """Run a stage executor on every rank of an expert-parallel job in lockstep.
+
+    Each MoE layer exchanges per-expert counts with every peer, so every rank
+    must run the same number of forward passes. Each round, every rank
+    launches exactly one pass: its next chunk, or an idle pass (MoE layers
+    only, no tokens of its own: it still computes its experts for the
+    others' tokens). The rounds end when no rank has queued or in-flight
+    work; that decision is a host-side all-reduce on `cpu_group` (gloo), so
+    the GPU stream never waits for it.
+    """
+    import time
+
+    import torch
+    import torch.distributed as dist
+    ex = executor
+    t0 = time.perf_counter()
+    flag = torch.zeros(1, dtype=torch.int32)
+    while True:
+        flag[0] = 1 if (ex.queue or ex._inflight) else 0
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=cpu_group)
+        if int(flag[0]) == 0:
+            break
+        specs = ex._admit() if ex.queue else []
+        if specs:
+            ex._launch(specs)
+            while len(ex._inflight) > 1:
+                ex._collect_one()
+        else:
+            pipe.idle_pass()
+            if ex._inflight:
+                ex._collect_one()
+    if ex.queue:
+        raise RuntimeError(f"{len(ex.queue)} tasks were never admitted")
+    ex.stats.wall_s += time.perf_counter() - t0
