@@ -5,7 +5,8 @@ sequences, plus the metadata the kernels read:
 
   ids, positions, slots   [T] int32  token id, absolute position, KV slot (page*P + offset; -1 = none)
   seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
-  tiles                   [n, 2]     (sequence, first query token) per 32-token attention tile
+  tiles                   [n, 2]     (sequence, first query token) per 32-token prefill-attention tile
+  dseqs                   [d]        sequences with one new token (decode attention: one CTA per KV head)
   page_list               [*]        page ids of every segment, segments point into it
   final_rows              [R]        token row whose logits each readout reads
 
@@ -52,6 +53,7 @@ class Chunk:
     page_list: torch.Tensor
     final_rows: torch.Tensor
     readout_tags: list = field(default_factory=list)
+    dseqs: torch.Tensor | None = None
     num_seqs: int = 0
     host: dict | None = None   # numpy copies (tests, CPU reference)
     upload_bytes: int = 0
@@ -61,8 +63,10 @@ class Chunk:
 class ChunkPacker:
     """Packs SeqSpecs against a PagePool into a Chunk on `device`."""
 
-    def __init__(self, pool, device, pin: bool = True):
+    def __init__(self, pool, device, pin: bool = True, split_decode: bool = True):
         self.pool = pool
+        # one-token sequences go to the decode attention kernel instead of prefill tiles
+        self.split_decode = split_decode
         self.device = torch.device(device)
         self.pin = pin and self.device.type == "cuda"
         self._staging: torch.Tensor | None = None
@@ -77,6 +81,7 @@ class ChunkPacker:
         page_list: list[int] = []
         seg_cache: dict = {}
         tiles: list[tuple[int, int]] = []
+        dseqs: list[int] = []
         final_rows: list[int] = []
         tags: list = []
         q = 0
@@ -105,7 +110,10 @@ class ChunkPacker:
             row[4 + len(s.reads)] = own_len
             row[8 + len(s.reads)] = len(page_list)
             page_list.extend(self.pool.pages_of(s.own_key)[:npg])
-            tiles.extend((si, q0) for q0 in range(0, n, ATTN_BLOCK_Q))
+            if n == 1 and self.split_decode:
+                dseqs.append(si)
+            else:
+                tiles.extend((si, q0) for q0 in range(0, n, ATTN_BLOCK_Q))
             if s.readout:
                 offs = s.readout_rows if s.readout_rows is not None else (n - 1,)
                 for o in offs:
@@ -115,7 +123,8 @@ class ChunkPacker:
         tiles_a = np.asarray(tiles, dtype=np.int32).reshape(-1, 2)
         pl = np.asarray(page_list, dtype=np.int32)
         fr = np.asarray(final_rows, dtype=np.int32)
-        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr]
+        ds = np.asarray(dseqs, dtype=np.int32)
+        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr, ds]
         sizes = [p.size for p in parts]
         flat = np.concatenate(parts) if n_tok else np.zeros(0, dtype=np.int32)
         dev = self._upload(flat)
@@ -125,10 +134,10 @@ class ChunkPacker:
             views.append(dev[o:o + sz])
             o += sz
         host = {"ids": ids, "positions": pos, "slots": slots, "seqs": seqs, "tiles": tiles_a,
-                "page_list": pl, "final_rows": fr}
+                "page_list": pl, "final_rows": fr, "dseqs": ds}
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
-                     final_rows=views[6], readout_tags=tags, num_seqs=len(specs), host=host,
+                     final_rows=views[6], dseqs=views[7], readout_tags=tags, num_seqs=len(specs), host=host,
                      upload_bytes=int(flat.nbytes), full_readout=any(s.full and s.readout for s in specs))
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:

@@ -119,25 +119,20 @@ class Qwen3Pipeline:
             q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
                                     cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
             if fp8 and self.tc_attention:
-                o8, os_ = ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale)
+                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
                 ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
                 a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
                 ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 continue
             if fp8:
-                o8, os_ = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale,
-                                                fp8_out=True, mx=True)
+                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=False)
                 ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
                 a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
                 ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
             else:
-                if self.tc_attention:
-                    o = ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale,
-                                                 fp8_out=False)
-                else:
-                    o = ops.prefill_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale)
+                o = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=False, tc=self.tc_attention)
                 ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
                 a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)

@@ -157,7 +157,7 @@ class Qwen3MoePipeline:
             qkv = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
             q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
                                     cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
-            o8, os_ = ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale)
+            o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
             ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
             x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
             xb = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)

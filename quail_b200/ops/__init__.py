@@ -13,6 +13,8 @@ from quail_b200.ops.kernels import (  # noqa: F401
     EPI_RESIDUAL,
     EPI_SWIGLU_BF16,
     EPI_SWIGLU_FP8,
+    chunk_attention,
+    decode_attention,
     embed_gather,
     final_norm_readout,
     gemm,

@@ -231,6 +231,42 @@ def prefill_attention_tc(q, k_cache, v_cache, seqs, tiles, page_list, softmax_sc
     return (out, out_scale) if fp8_out else out
 
 
+def decode_attention(q, k_cache, v_cache, seqs, dseqs, page_list, softmax_scale: float, out, out_scale=None):
+    """One-query-token sequences (decode steps): csrc/attention_decode.cu, into `out` (bf16 or e4m3 + atoms)."""
+    if dseqs.numel() == 0:
+        return
+    count_launch()
+    native().decode_attention(q, k_cache, v_cache, seqs, dseqs, page_list, softmax_scale, out, out_scale)
+
+
+def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: bool, tc: bool,
+                    out=None, out_scale=None):
+    """Attention of every query row of a packed chunk.
+
+    Prefill tiles (sequences with several new tokens) run on the tcgen05
+    kernel (`tc`, needs 4 q heads per KV head) or the mma.sync kernel; the
+    chunk's one-token sequences run on the decode kernel. Both write their
+    own rows of one output: e4m3 + MX scale atoms (`mx`) or bf16.
+    """
+    T, QH = q.shape[0], q.shape[1]
+    if out is None:
+        out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if mx else torch.bfloat16, device=q.device)
+    if mx and out_scale is None:
+        out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+    if chunk.tiles.shape[0] > 0:
+        if tc:
+            prefill_attention_tc(q, k_cache, v_cache, chunk.seqs, chunk.tiles, chunk.page_list, softmax_scale,
+                                 fp8_out=mx, out=out, out_scale=out_scale)
+        else:
+            prefill_attention(q, k_cache, v_cache, chunk.seqs, chunk.tiles, chunk.page_list, softmax_scale,
+                              fp8_out=mx, mx=mx, out=out, out_scale=out_scale)
+    dseqs = getattr(chunk, "dseqs", None)
+    if dseqs is not None and dseqs.numel() > 0:
+        decode_attention(q, k_cache, v_cache, chunk.seqs, dseqs, chunk.page_list, softmax_scale, out,
+                         out_scale if mx else None)
+    return (out, out_scale) if mx else out
+
+
 def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, normed=None):
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
     if logits is None:

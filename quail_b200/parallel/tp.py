@@ -257,8 +257,7 @@ class TPQwen3:
                                     cfg.rms_eps)
             o8 = torch.zeros(M, self.qh * 128, dtype=torch.float8_e4m3fn, device=dev)  # padding rows stay 0
             os_ = torch.zeros(ops.sf_bytes(M, self.qh * 128), dtype=torch.uint8, device=dev)
-            ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list, self.scale, out=o8,
-                                     out_scale=os_)
+            ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True, out=o8, out_scale=os_)
             if fused:
                 self._rs(o8, os_, L["wo"], L["so"], rpr)
                 self._norm(h, L["ln2"], M, rpr, tp_slots=tp)

@@ -284,3 +284,26 @@ def test_prefill_attention_tcgen05(P):
     assert rel_err(out, want) < 1e-2
     o8, sf = ops.prefill_attention_tc(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale)
     assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
+
+
+@pytest.mark.parametrize("QH,KH,P", [(8, 2, 16), (32, 4, 16), (32, 8, 128), (16, 16, 16), (16, 1, 64)])
+def test_decode_attention(QH, KH, P):
+    """One-token sequences (decode steps) on the decode kernel, mixed with prefill tiles in one chunk."""
+    from types import SimpleNamespace
+    specs = [(1, [48, 1]), (1, [48, 300, 65]), (40, [48, 40]), (1, [48, 2047]), (1, [48, 200, 16]),
+             (1, [17]), (130, [48, 130])]
+    q, kc, vc, seqs, pl = _segmented_case(P, specs, QH=QH, KH=KH, pages=2048)
+    scale = ref.softmax_scale(128)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    tiles = ref.attention_tiles(seqs)
+    one = [i for i, (n, _) in enumerate(specs) if n == 1]
+    tiles = torch.tensor([t for t in tiles.tolist() if t[0] not in one], dtype=torch.int32)
+    chunk = SimpleNamespace(seqs=seqs.to(DEV), tiles=tiles.to(DEV), page_list=pl.to(DEV),
+                            dseqs=torch.tensor(one, dtype=torch.int32, device=DEV))
+    tc = (QH // KH) % 4 == 0
+    out = ops.chunk_attention(q, kc, vc, chunk, scale, mx=False, tc=tc)
+    assert rel_err(out, want) < 1e-2
+    rows = torch.tensor([int(seqs[i, 0]) for i in one])
+    assert rel_err(out[rows.to(DEV)], want[rows]) < 1e-2
+    o8, sf = ops.chunk_attention(q, kc, vc, chunk, scale, mx=True, tc=tc)
+    assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
