@@ -56,11 +56,13 @@ class PagePool:
         return self.owned[key]
 
     # ------------------------------------------------------------ alloc / grow
-    def alloc(self, key, tokens: int):
-        """Pages for `tokens` new tokens of a new key, or None if the pool is short."""
+    def alloc(self, key, tokens: int, capacity: int = 0):
+        """Pages for `tokens` new tokens of a new key (at least `capacity` tokens
+        of room, so later growth up to it needs no new pages), or None if the
+        pool is short."""
         if key in self.owned:
             raise KeyError(f"{key!r} already resident")
-        need = self.pages_needed(tokens)
+        need = self.pages_needed(max(tokens, capacity))
         if need > len(self.free):
             return None
         pages = [self.free.pop() for _ in range(need)]

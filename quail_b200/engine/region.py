@@ -210,6 +210,11 @@ class RegionRun:
         for c in batch:
             self._submit_question(r, c)
 
+    @staticmethod
+    def _reserve(call: Call) -> int:
+        """Decode headroom: a decoding call's generated tokens land in its own pages."""
+        return call.max_tokens if call.kind in ("map", "extract") else 0
+
     def _needs_full(self, call: Call) -> bool:
         return call.kind in ("classify", "map", "extract")
 
@@ -218,7 +223,7 @@ class RegionRun:
         key, reads, pos, own_len = self._question(r, ci)
         self.fresh_tokens += len(call.suffix)
         self.ex.submit(Task(key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
-                            full_readout=self._needs_full(call),
+                            full_readout=self._needs_full(call), reserve_tokens=self._reserve(call),
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
 
     def submit_all(self) -> None:
@@ -232,7 +237,7 @@ class RegionRun:
             self._next[r] = 1
             self._pending[r] = 1
             self.ex.submit(Task(key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
-                                full_readout=self._needs_full(first),
+                                full_readout=self._needs_full(first), reserve_tokens=self._reserve(first),
                                 on_done=lambda t, row, r=r: self._answered(r, 0, row), free_after=False))
 
     def run(self):

@@ -53,6 +53,7 @@ class Task:
     tag: object = None
     readout_rows: tuple | None = None                # offsets read out (default: the last token)
     full_readout: bool = False                       # also argmax / log-sum-exp over the vocabulary
+    reserve_tokens: int = 0                          # decode headroom allocated with the key's pages
 
     @property
     def remaining(self) -> int:
@@ -84,6 +85,9 @@ class StageExecutor:
         self.device = arena.device
         self.packer = ChunkPacker(self.pool, self.device)
         self.queue: deque[Task] = deque()
+        # continuations of resident keys (decode steps, label continuations):
+        # admitted before new work, they need at most a page-list extension
+        self.cont: deque[Task] = deque()
         self.written: dict = {}     # key -> tokens written by launched chunks
         self.stats = ExecutorStats()
         self.gpu_timing = gpu_timing and self.device.type == "cuda"
@@ -95,7 +99,10 @@ class StageExecutor:
         if need > self.pool.num_pages:
             raise OversizedDocumentError(
                 f"task {task.key!r} needs {need} pages; the arena has {self.pool.num_pages}")
-        self.queue.append(task)
+        if task.own_prefix > 0 and self.pool.resident(task.key):
+            self.cont.append(task)
+        else:
+            self.queue.append(task)
 
     def free(self, key) -> None:
         self.pool.free_key(key)
@@ -108,8 +115,28 @@ class StageExecutor:
     def _admit(self) -> list[SeqSpec]:
         room = self.chunk_tokens
         specs: list[SeqSpec] = []
+        # continuations first: each is one or a few tokens of a resident key
+        while self.cont and room > 0:
+            if self.max_seqs is not None and len(specs) >= self.max_seqs:
+                break
+            task = self.cont[0]
+            total = task.own_prefix + len(task.tokens)
+            if len(task.tokens) > room:
+                break
+            if self.pool.tokens[task.key] < total and self.pool.grow(task.key, total) is None:
+                self.pool.evict_retained(self.pool.pages_needed(total))
+                if self.pool.grow(task.key, total) is None:
+                    break
+            self.cont.popleft()
+            rows = tuple(task.readout_rows) if task.readout and task.readout_rows is not None else None
+            specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix,
+                                 tokens=task.tokens, pos_start=task.pos_start, readout=task.readout, tag=task,
+                                 readout_rows=rows, full=task.full_readout))
+            task.done = len(task.tokens)
+            room -= len(task.tokens)
         deferred: list[Task] = []
         scanned = 0
+        no_new = False
         while self.queue and room > 0 and scanned < 4096:
             if self.max_seqs is not None and len(specs) >= self.max_seqs:
                 break
@@ -120,13 +147,20 @@ class StageExecutor:
                 continue
             total = task.own_prefix + len(task.tokens)
             if not self.pool.resident(task.key):
-                pages = self.pool.alloc(task.key, total)
-                if pages is None:
-                    self.pool.evict_retained(self.pool.pages_needed(total))
-                    pages = self.pool.alloc(task.key, total)
-                if pages is None:
+                if no_new:
                     deferred.append(task)
-                    break  # keep FIFO order under memory pressure
+                    continue
+                cap = total + task.reserve_tokens
+                pages = self.pool.alloc(task.key, total, cap)
+                if pages is None:
+                    self.pool.evict_retained(self.pool.pages_needed(cap))
+                    pages = self.pool.alloc(task.key, total, cap)
+                if pages is None:
+                    # keep new work in FIFO order under memory pressure, but
+                    # still admit pieces of keys that are already resident
+                    deferred.append(task)
+                    no_new = True
+                    continue
                 for rk, _ in task.reads:
                     self.pool.borrow(task.key, rk)
             elif self.pool.tokens[task.key] < total:
@@ -226,9 +260,9 @@ class StageExecutor:
 
     def run(self) -> ExecutorStats:
         t0 = time.perf_counter()
-        while self.queue or self._inflight:
+        while self.queue or self.cont or self._inflight:
             if not self.step():
-                if self.queue:
+                if self.queue or self.cont:
                     raise ArenaFullError(
                         f"{len(self.queue)} tasks cannot be admitted: {self.pool.free_pages} free pages; "
                         f"head {self.queue[0].key!r} reads {self.queue[0].reads}")

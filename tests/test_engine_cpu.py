@@ -136,3 +136,32 @@ def test_filter_guards_followups():
     assert all("s" in r.values for r in kept)
     assert all("s" not in r.values for r in dropped)
     assert arena.pool.free_pages == arena.num_pages
+
+
+class _CountingModel:
+    """Full readouts whose argmax is the next token id: every row decodes to max_tokens."""
+
+    def forward_chunk(self, chunk, arena):
+        ids = torch.as_tensor(chunk.host["ids"]).long()
+        rows = torch.as_tensor(chunk.host["final_rows"]).long()
+        out = torch.zeros(rows.numel(), 4 + 2)
+        out[:, 4] = ((ids[rows] + 1) % 500).float()
+        return out
+
+
+@pytest.mark.parametrize("pages", [64, 400])
+def test_decode_headroom_under_memory_pressure(pages):
+    """AI.MAP rows reserve their decode pages at admission, and decode steps are
+    admitted before new documents, so a small arena finishes every row."""
+    arena = KVArena(1, pages, 16, 1, 8, device="cpu", dtype=torch.float32)
+    ex = StageExecutor(_CountingModel(), arena, 256)
+    rng = np.random.default_rng(0)
+    docs = [rng.integers(0, 500, int(n)).astype(np.int32) for n in rng.integers(20, 200, 40)]
+    call = Call(kind="map", suffix=np.array([1, 2, 3], dtype=np.int32), max_tokens=24, stop_ids=(999,), name="m")
+    res = RegionRun(ex, np.arange(48, dtype=np.int32), docs, [call], answer_width=4).run()
+    for d, r in zip(docs, res):
+        g = r.values["m"]
+        assert len(g) == 24
+        assert g[0] == (3 + 1) % 500 and g[1] == (g[0] + 1) % 500
+    assert ex.pool.free_pages == pages
+    ex.pool.check()
