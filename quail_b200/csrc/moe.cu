@@ -162,6 +162,33 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int l
   }
 }
 
+// exclusive prefix sum of v(0 .. n-1) by one warp (each lane a run of
+// consecutive items); out(i, prefix) per item; returns the total
+template <class V, class O>
+__device__ __forceinline__ int warp_scan_excl(int n, int lane, V v, O out) {
+  const int per = (n + 31) / 32;
+  int local = 0;
+  for (int k = 0; k < per; ++k) {
+    const int i = lane * per + k;
+    if (i < n) local += v(i);
+  }
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int run = incl - local;
+  for (int k = 0; k < per; ++k) {
+    const int i = lane * per + k;
+    if (i < n) {
+      out(i, run);
+      run += v(i);
+    }
+  }
+  return __shfl_sync(0xffffffffu, incl, 31);
+}
+
 // ------------------------------------------------------------------ plan
 struct PlanParams {
   int* counts;                             // local per-expert counts (zeroed here after use)
@@ -209,38 +236,35 @@ __global__ void __launch_bounds__(256) moe_plan_kernel(const PlanParams p) {
     p.counts[e] = 0;  // ready for the next layer's route
   }
   __syncthreads();
-  if (t < p.W) {
-    // owner t's receive buffer: its experts' rows back to back, each padded to 128
-    int b = 0;
-    for (int le = 0; le < p.Epr; ++le) {
-      const int e = t * p.Epr + le;
-      base[e] = b;
-      b += (total[e] + 127) & ~127;
-    }
+  const int warp = t >> 5, lane = t & 31;
+  // owner `warp`'s receive buffer: its experts' rows back to back, each padded to 128
+  if (warp < p.W) {
+    const int d = warp;
+    warp_scan_excl(p.Epr, lane, [&](int le) { return (total[d * p.Epr + le] + 127) & ~127; },
+                   [&](int le, int v) { base[d * p.Epr + le] = v; });
   }
-  if (t == 32) {
-    // this rank's dispatch units and item offsets in order o = le * W + owner
-    int u = 0, s = 0;
-    for (int o = 0; o < p.E; ++o) {
-      const int e = (o % p.W) * p.Epr + o / p.W;
-      pv.unit_start[o] = u;
-      pv.src_off[e] = s;
-      const int c = cnt[p.rank][e];
-      u += (c + kUnitRows - 1) / kUnitRows;
-      s += c;
+  __syncthreads();
+  if (warp == 0) {
+    // this rank's dispatch units in order o = le * W + owner
+    const int u = warp_scan_excl(
+        p.E, lane, [&](int o) { return (cnt[p.rank][(o % p.W) * p.Epr + o / p.W] + kUnitRows - 1) / kUnitRows; },
+        [&](int o, int v) { pv.unit_start[o] = v; });
+    if (lane == 0) {
+      pv.unit_start[p.E] = u;
+      *pv.num_units = ok ? u : 0;
     }
-    pv.unit_start[p.E] = u;
-    *pv.num_units = ok ? u : 0;
-  }
-  if (t == 64) {
-    int ts = 0;
-    for (int le = 0; le < p.Epr; ++le) {
-      tile_start[le] = ts;
-      ts += (total[p.rank * p.Epr + le] + 127) >> 7;
+  } else if (warp == 1) {
+    // item offsets of this rank's sorted list, same order
+    warp_scan_excl(p.E, lane, [&](int o) { return cnt[p.rank][(o % p.W) * p.Epr + o / p.W]; },
+                   [&](int o, int v) { pv.src_off[(o % p.W) * p.Epr + o / p.W] = v; });
+  } else if (warp == 2) {
+    const int ts = warp_scan_excl(p.Epr, lane, [&](int le) { return (total[p.rank * p.Epr + le] + 127) >> 7; },
+                                  [&](int le, int v) { tile_start[le] = v; });
+    if (lane == 0) {
+      tile_start[p.Epr] = ts;
+      *pv.num_tiles = (ok && ts <= p.tcap) ? ts : 0;
+      if (ts > p.tcap) atomicCAS(p.err, 0, kErrCapacity);
     }
-    tile_start[p.Epr] = ts;
-    *pv.num_tiles = (ok && ts <= p.tcap) ? ts : 0;
-    if (ts > p.tcap) atomicCAS(p.err, 0, kErrCapacity);
   }
   __syncthreads();
   for (int e = t; e < p.E; e += blockDim.x) {
@@ -255,7 +279,6 @@ __global__ void __launch_bounds__(256) moe_plan_kernel(const PlanParams p) {
     pv.recv_target[le] = p.cum[le];
   }
   // tile table: one warp per local expert
-  const int warp = t >> 5, lane = t & 31;
   for (int le = warp; le < p.Epr; le += blockDim.x >> 5) {
     const int e = p.rank * p.Epr + le;
     const int tot = total[e];
@@ -585,65 +608,69 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 }
 
 // ------------------------------------------------------------------ combine + norm
-// One warp per token: waits for all K rows of every token of this rank, then
-// resid[t] += sum_k comb[t * K + k]; with a norm weight, also the next layer's
-// RMSNorm of the new residual as e4m3 + MX scale atoms.
+// One CTA of H / 8 threads per token (8 columns each): waits for all K rows of
+// every token of this rank, then resid[t] += sum_k comb[t * K + k]; with a
+// norm weight, also the next layer's RMSNorm of the new residual as e4m3 +
+// MX scale atoms (4 threads share a 32-column scale block).
 template <int H>
-__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ comb, int M, int K,
-                                   const uint32_t* __restrict__ counter, uint32_t want,
-                                   __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ w, float eps,
-                                   uint8_t* __restrict__ y8, uint8_t* __restrict__ ysf, int* err) {
-  constexpr int SLABS = H / 256;
+__global__ void __launch_bounds__(H / 8) moe_combine_kernel(const __nv_bfloat16* __restrict__ comb, int M, int K,
+                                                           const uint32_t* __restrict__ counter, uint32_t want,
+                                                           __nv_bfloat16* __restrict__ resid,
+                                                           const __nv_bfloat16* __restrict__ w, float eps,
+                                                           uint8_t* __restrict__ y8, uint8_t* __restrict__ ysf,
+                                                           int* err) {
+  constexpr int NT = H / 8, NW = NT / 32;
   __shared__ int go;
+  __shared__ float red[NW];
   if (threadIdx.x == 0) go = wait_word<true>(counter, want, err) ? 1 : 0;
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int r = blockIdx.x;
   if (!go || r >= M) return;
-  float v[SLABS][8];
+  const int c0 = threadIdx.x * 8;
+  float v[8];
+  ld_bf16x8f(resid + (size_t)r * H + c0, v);
+  for (int k = 0; k < K; ++k) {
+    float u[8];
+    ld_bf16x8f(comb + ((size_t)r * K + k) * H + c0, u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] += u[i];
+  }
+  st_bf16x8(resid + (size_t)r * H + c0, v);
+  if (w == nullptr) return;
   float ss = 0.f;
 #pragma unroll
-  for (int s = 0; s < SLABS; ++s) {
-    ld_bf16x8f(resid + (size_t)r * H + s * 256 + lane * 8, v[s]);
-    for (int k = 0; k < K; ++k) {
-      float u[8];
-      ld_bf16x8f(comb + ((size_t)r * K + k) * H + s * 256 + lane * 8, u);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[s][i] += u[i];
-    }
-    st_bf16x8(resid + (size_t)r * H + s * 256 + lane * 8, v[s]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[s][i] = __bfloat162float(__float2bfloat16(v[s][i]));
-      ss += v[s][i] * v[s][i];
-    }
+  for (int i = 0; i < 8; ++i) {
+    v[i] = __bfloat162float(__float2bfloat16(v[i]));
+    ss += v[i] * v[i];
   }
-  if (w == nullptr) return;
   ss = warp_sum(ss);
-  const float rinv = rsqrtf(ss / H + eps);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
 #pragma unroll
-  for (int s = 0; s < SLABS; ++s) {
-    float wv[8];
-    ld_bf16x8f(w + s * 256 + lane * 8, wv);
+  for (int i = 0; i < NW; ++i) tot += red[i];
+  const float rinv = rsqrtf(tot / H + eps);
+  float wv[8];
+  ld_bf16x8f(w + c0, wv);
+  float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[s][i] = v[s][i] * rinv * wv[i];
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    const uint8_t e = ue8m0_of(amax);
-    const float inv = ue8m0_inv(e);
-    __nv_fp8x4_e4m3 a(make_float4(v[s][0] * inv, v[s][1] * inv, v[s][2] * inv, v[s][3] * inv));
-    __nv_fp8x4_e4m3 b(make_float4(v[s][4] * inv, v[s][5] * inv, v[s][6] * inv, v[s][7] * inv));
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&a);
-    pk.y = *reinterpret_cast<uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(y8 + (size_t)r * H + s * 256 + lane * 8) = pk;
-    if ((lane & 3) == 0) {
-      const int j = s * 8 + (lane >> 2);
-      ysf[((size_t)(r >> 7) * (H / 128) + (j >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (j & 3)] = e;
-    }
+  for (int i = 0; i < 8; ++i) {
+    v[i] = v[i] * rinv * wv[i];
+    amax = fmaxf(amax, fabsf(v[i]));
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const uint8_t e = ue8m0_of(amax);
+  const float inv = ue8m0_inv(e);
+  __nv_fp8x4_e4m3 a(make_float4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv));
+  __nv_fp8x4_e4m3 b(make_float4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv));
+  uint2 pk;
+  pk.x = *reinterpret_cast<uint32_t*>(&a);
+  pk.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(y8 + (size_t)r * H + c0) = pk;
+  if ((threadIdx.x & 3) == 0) {
+    const int j = c0 / 32;
+    ysf[((size_t)(r >> 7) * (H / 128) + (j >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (j & 3)] = e;
   }
 }
 
@@ -832,15 +859,13 @@ void moe_combine(const torch::Tensor& comb, int64_t M, int64_t topk, const torch
   const int dev = resid.get_device();
   c10::cuda::CUDAGuard guard(dev);
   cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
-  const int rows_per_cta = 8;
-  const int grid = (M + rows_per_cta - 1) / rows_per_cta;
   auto cp = reinterpret_cast<const __nv_bfloat16*>(comb.data_ptr());
   auto wp = w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr()) : nullptr;
   uint8_t* yp = y8.has_value() ? reinterpret_cast<uint8_t*>(y8->data_ptr()) : nullptr;
   uint8_t* sp = ysf.has_value() ? ysf->data_ptr<uint8_t>() : nullptr;
 #define QB_MOE_CASE(HH)                                                                                      \
   if (H == HH) {                                                                                             \
-    moe_combine_kernel<HH><<<grid, rows_per_cta * 32, 0, st>>>(                                             \
+    moe_combine_kernel<HH><<<(int)M, HH / 8, 0, st>>>(                                                     \
         cp, (int)M, (int)topk, reinterpret_cast<const uint32_t*>(counter.data_ptr<int>()), (uint32_t)want,  \
         reinterpret_cast<__nv_bfloat16*>(resid.data_ptr()), wp, (float)eps, yp, sp, device_error_word(dev)); \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                          \

@@ -91,6 +91,7 @@ class EPState:
         else:
             self.buf = torch.zeros(total, dtype=torch.uint8, device=dev)
             self.peers = [self.buf.data_ptr()]
+        self.comm = "fused"     # "nccl": the NCCL all-to-all baseline (forward_nccl)
         self.epoch = 0          # MoE layers run so far (count-exchange flags carry it)
         self.comb_units = 0     # cumulative (row, 128-column) units this rank expects in its combine buffer
         if self.W > 1:
@@ -144,6 +145,8 @@ class EPState:
         (residual + expert outputs). With `next_norm`, returns the next
         layer's input RMSNorm of the new h as (e4m3, atoms); else None.
         """
+        if self.comm == "nccl":
+            return self.forward_nccl(x8, xsf, xb, h, L, next_norm, eps)
         from quail_b200 import ops
         C = ops.native()
         M = h.shape[0]
@@ -175,6 +178,114 @@ class EPState:
         y8 = torch.empty(M, self.H, dtype=torch.float8_e4m3fn, device=h.device)
         ysf = torch.empty(ops.sf_bytes(M, self.H), dtype=torch.uint8, device=h.device)
         C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, next_norm, eps, y8, ysf)
+        return y8, ysf
+
+    # ------------------------------------------------------------ NCCL baseline
+    def forward_nccl(self, x8, xsf, xb, h, L, next_norm=None, eps: float = 1e-6):
+        """The same MoE layer with NCCL all-to-all dispatch and combine (the baseline).
+
+        Route on the device; per-expert counts exchanged with all_to_all and
+        read on the host (the split sizes); token rows (e4m3 + row-major scale
+        bytes) sorted by expert and sent with all_to_all_single; received rows
+        laid out expert by expert for the same grouped GEMMs (no dispatch
+        work in the kernel, no peer stores in the epilogue); outputs sent home
+        with a second all_to_all_single, weighted and summed into the residual.
+        """
+        import torch.distributed as dist
+        from quail_b200 import ops
+        from quail_b200.ops.quant import pack_sf_atoms, unpack_sf_atoms
+        C = ops.native()
+        M, H, K, E, Epr, W = h.shape[0], self.H, self.K, self.E, self.Epr, self.W
+        dev = h.device
+        g = self.group
+        if not hasattr(self, "_nb"):
+            self._nb = {"out": torch.empty(self.R_cap, H, dtype=torch.bfloat16, device=dev),
+                        "ctr": torch.zeros(8, dtype=torch.int32, device=dev)}
+        self.epoch += 1
+        if M > 0:
+            logits = ops.gemm(xb, L["router"], bn=128)
+            C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+            ops.count_launch(1)
+            ids = self.ids[:M * K].long()
+        else:
+            ids = torch.zeros(0, dtype=torch.long, device=dev)
+        self.counts.zero_()
+        order = torch.argsort(ids, stable=True)
+        cnt_e = torch.bincount(ids, minlength=E).to(torch.int32)
+        recv_cnt = torch.empty(E, dtype=torch.int32, device=dev)     # [W sources][Epr local experts]
+        dist.all_to_all_single(recv_cnt, cnt_e, group=g)
+        host = torch.cat([cnt_e, recv_cnt]).cpu()                    # the host needs the split sizes
+        send_sizes = host[:E].view(W, Epr).sum(1).tolist()
+        rc = host[E:].view(W, Epr)
+        recv_sizes = rc.sum(1).tolist()
+        n_recv = int(sum(recv_sizes))
+        # payload rows: e4m3 bytes + row-major scale bytes of each item's token
+        tok = (order // K)
+        if M > 0:
+            rows = torch.cat([x8.view(torch.uint8), unpack_sf_atoms(xsf, M, H)], dim=1)[tok]
+        else:
+            rows = torch.zeros(0, H + H // 32, dtype=torch.uint8, device=dev)
+        recv = torch.empty(n_recv, H + H // 32, dtype=torch.uint8, device=dev)
+        dist.all_to_all_single(recv, rows, output_split_sizes=recv_sizes, input_split_sizes=send_sizes, group=g)
+        # expert-major padded layout of the received rows
+        tot = rc.sum(0)                                               # rows per local expert
+        padded = ((tot + 127) // 128) * 128
+        base = torch.cumsum(padded, 0) - padded
+        le = torch.repeat_interleave(torch.arange(Epr).repeat(W), rc.flatten())   # received order
+        perm = torch.argsort(le, stable=True)
+        le_s = le[perm]
+        first = torch.cumsum(tot, 0) - tot
+        dest = (base[le_s] + torch.arange(n_recv) - first[le_s]).to(dev)
+        perm_d = perm.to(dev)
+        R = int(padded.sum())
+        ra = self.recv_a()
+        ra.view(torch.uint8)[dest] = recv[perm_d, :H]
+        sfm = torch.zeros(max(R, 128), H // 32, dtype=torch.uint8, device=dev)
+        sfm[dest] = recv[perm_d, H:]
+        packed = pack_sf_atoms(sfm)
+        self.recv_sf()[:packed.numel()].copy_(packed)
+        meta = self.recv_meta()
+        meta[dest, 0] = (self.rank << 28) | perm_d.to(torch.int32)
+        meta[dest, 1] = torch.ones(1, dtype=torch.float32, device=dev).view(torch.int32)
+        # tile table on the host: (expert, first row, valid rows)
+        tiles = []
+        for j in range(Epr):
+            for i in range(int(padded[j]) // 128):
+                tiles.append((j, int(base[j]) + i * 128, min(128, int(tot[j]) - i * 128)))
+        pv = torch.zeros(self.plan.numel(), dtype=torch.int32)
+        pv[0], pv[1] = len(tiles), 0
+        tofs = 8 + 4 * E + 1 + Epr
+        if tiles:
+            t = torch.tensor(tiles, dtype=torch.int32)
+            pv[tofs:tofs + len(tiles)] = t[:, 0]
+            pv[tofs + self.t_cap:tofs + self.t_cap + len(tiles)] = t[:, 1]
+            pv[tofs + 2 * self.t_cap:tofs + 2 * self.t_cap + len(tiles)] = t[:, 2]
+        self.plan.copy_(pv, non_blocking=False)
+        ops.count_launch(2)
+        e8 = x8[:0] if M > 0 else self.recv_a()[:0]
+        C.moe_gate_up(e8, self.recv_sf(), self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
+                      self.peer("recv_a")[self.rank:self.rank + 1] * W, self.peer("recv_sf")[:1] * W,
+                      self.peer("recv_meta")[:1] * W, self.peer("recv_count")[:1] * W,
+                      self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
+        out = self._nb["out"]
+        C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, meta, L["wd"], L["sd"],
+                   [out.data_ptr()] * W, [self._nb["ctr"].data_ptr()] * W)
+        back = torch.empty(M * K, H, dtype=torch.bfloat16, device=dev)
+        dist.all_to_all_single(back, out[:n_recv], output_split_sizes=send_sizes, input_split_sizes=recv_sizes,
+                               group=g)
+        if M == 0:
+            return None
+        items = torch.empty_like(back)
+        items[order] = back
+        items = (items.float() * self.wts[:M * K, None]).bfloat16()
+        zero = self._nb["ctr"][4:5]
+        ops.count_launch(1)
+        if next_norm is None:
+            C.moe_combine(items, M, K, zero, 0, h, None, eps, None, None)
+            return None
+        y8 = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+        ysf = torch.empty(ops.sf_bytes(M, H), dtype=torch.uint8, device=dev)
+        C.moe_combine(items, M, K, zero, 0, h, next_norm, eps, y8, ysf)
         return y8, ysf
 
 

@@ -7,7 +7,8 @@ Every rank builds the same replicated weights and its own E / W experts
 lengths on every rank, different tokens, so every rank runs the same number
 of chunks and MoE layers) through the stage executor with expert
 parallelism, then runs the same documents through a one-rank pipeline that
-holds all experts and compares the readout logits. The expert math of a row
+holds all experts and compares the readout logits; then the same with the
+NCCL all-to-all baseline path. The expert math of a row
 does not depend on where it runs, so the two agree to rounding. Prints one
 JSON line on rank 0 (max error over ranks).
 """
@@ -50,16 +51,23 @@ def main():
     got = _run(ep, arena, prefix, docs, suffix, 1024)
     err_ep = ops.read_and_clear_error(local)
     dist.barrier()
+    # the NCCL all-to-all baseline on the same weights and rows
+    ep.ep.comm = "nccl"
+    arena_n = KVArena(cfg.layers, 128, 128, cfg.num_kv_heads, 128, device=dev)
+    got_n = _run(ep, arena_n, prefix, docs, suffix, 1024)
+    err_ep = max(err_ep, ops.read_and_clear_error(local))
+    dist.barrier()
     one = Qwen3MoePipeline(cfg, Qwen3MoeWeights(cfg, None, dev, head_rows=ids, seed=4), max_tokens=1024)
     arena1 = KVArena(cfg.layers, 128, 128, cfg.num_kv_heads, 128, device=dev)
     want = _run(one, arena1, prefix, docs, suffix, 1024)
     err_one = ops.read_and_clear_error(local)
-    rel = torch.tensor([float(((got - want).norm() / want.norm()).item()), float(err_ep), float(err_one)],
-                       device=dev)
+    rel = torch.tensor([float(((got - want).norm() / want.norm()).item()), float(err_ep), float(err_one),
+                        float(((got_n - want).norm() / want.norm()).item())], device=dev)
     dist.all_reduce(rel, op=dist.ReduceOp.MAX)
-    out = {"world": world, "rel_err": rel[0].item(), "kernel_error": int(rel[1].item()),
-           "one_rank_error": int(rel[2].item())}
-    out["ok"] = out["rel_err"] < 1e-2 and out["kernel_error"] == 0 and out["one_rank_error"] == 0
+    out = {"world": world, "rel_err": rel[0].item(), "rel_err_nccl": rel[3].item(),
+           "kernel_error": int(rel[1].item()), "one_rank_error": int(rel[2].item())}
+    out["ok"] = (out["rel_err"] < 1e-2 and out["rel_err_nccl"] < 1e-2 and out["kernel_error"] == 0
+                 and out["one_rank_error"] == 0)
     if rank == 0:
         print(json.dumps(out), flush=True)
     dist.barrier()
