@@ -188,8 +188,10 @@ class EPState:
         read on the host (the split sizes); token rows (e4m3 + row-major scale
         bytes) sorted by expert and sent with all_to_all_single; received rows
         laid out expert by expert for the same grouped GEMMs (no dispatch
-        work in the kernel, no peer stores in the epilogue); outputs sent home
-        with a second all_to_all_single, weighted and summed into the residual.
+        work in the kernel, no peer stores in the epilogue; the routing weight
+        travels with the row and is applied in the down epilogue, as in the
+        fused path); outputs sent home with a second all_to_all_single and
+        summed into the residual.
         """
         import torch.distributed as dist
         from quail_b200 import ops
@@ -221,11 +223,13 @@ class EPState:
         n_recv = int(sum(recv_sizes))
         # payload rows: e4m3 bytes + row-major scale bytes of each item's token
         tok = (order // K)
+        RB = H + H // 32 + 4   # e4m3 row | scale bytes | routing weight (fp32)
         if M > 0:
-            rows = torch.cat([x8.view(torch.uint8), unpack_sf_atoms(xsf, M, H)], dim=1)[tok]
+            w4 = self.wts[:M * K][order].contiguous().view(torch.uint8).view(-1, 4)
+            rows = torch.cat([torch.cat([x8.view(torch.uint8), unpack_sf_atoms(xsf, M, H)], dim=1)[tok], w4], dim=1)
         else:
-            rows = torch.zeros(0, H + H // 32, dtype=torch.uint8, device=dev)
-        recv = torch.empty(n_recv, H + H // 32, dtype=torch.uint8, device=dev)
+            rows = torch.zeros(0, RB, dtype=torch.uint8, device=dev)
+        recv = torch.empty(n_recv, RB, dtype=torch.uint8, device=dev)
         dist.all_to_all_single(recv, rows, output_split_sizes=recv_sizes, input_split_sizes=send_sizes, group=g)
         # expert-major padded layout of the received rows
         tot = rc.sum(0)                                               # rows per local expert
@@ -241,12 +245,12 @@ class EPState:
         ra = self.recv_a()
         ra.view(torch.uint8)[dest] = recv[perm_d, :H]
         sfm = torch.zeros(max(R, 128), H // 32, dtype=torch.uint8, device=dev)
-        sfm[dest] = recv[perm_d, H:]
+        sfm[dest] = recv[perm_d, H:H + H // 32]
         packed = pack_sf_atoms(sfm)
         self.recv_sf()[:packed.numel()].copy_(packed)
         meta = self.recv_meta()
         meta[dest, 0] = (self.rank << 28) | perm_d.to(torch.int32)
-        meta[dest, 1] = torch.ones(1, dtype=torch.float32, device=dev).view(torch.int32)
+        meta[dest, 1] = recv[perm_d, H + H // 32:].contiguous().view(torch.int32).flatten()
         # tile table on the host: (expert, first row, valid rows)
         tiles = []
         for j in range(Epr):
@@ -276,8 +280,7 @@ class EPState:
         if M == 0:
             return None
         items = torch.empty_like(back)
-        items[order] = back
-        items = (items.float() * self.wts[:M * K, None]).bfloat16()
+        items[order] = back       # rows come back weighted by the expert owner's epilogue
         zero = self._nb["ctr"][4:5]
         ops.count_launch(1)
         if next_norm is None:
