@@ -167,6 +167,8 @@ class ModelEngine:
             answer = [0]
         self._set_answer_rows(answer)
         ex = self.executor
+        stop = getattr(self, "interrupt", None)
+        ex.should_stop = stop.is_set if stop is not None else None
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
         run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer))
         results = run.run()

@@ -11,7 +11,7 @@ register_csv, sql() returning a Query with run / collect / execute_stream /
 explain / plan, and a QueryResult holding the table, a report of the model
 work (fresh tokens, documents, passes, wall time) and the plan text. With
 `endpoint=` the session talks to a Quail server instead
-(quail_b200.server.client).
+(quail_b200.server.client, quail_b200.server.service).
 """
 
 from __future__ import annotations
@@ -64,8 +64,6 @@ class Query:
     def run(self) -> QueryResult:
         from quail_b200.sql.executor import Executor
         s = self.session
-        if s._remote is not None:
-            return s._remote.run(self.text)
         t0 = time.perf_counter()
         engine = s.engine() if s._needs_model(self.tree) else None
         boot = time.perf_counter() - t0
@@ -91,15 +89,14 @@ class Query:
         return pa.RecordBatchReader.from_batches(t.schema, t.to_batches(max_chunksize=batch_rows))
 
     def submit(self, **options):
-        if self.session._remote is None:
-            raise RuntimeError("submit() sends a query to a Quail server; this session has no endpoint")
-        return self.session._remote.submit(self.text, **options)
+        raise RuntimeError("submit() sends a query to a Quail server; this session has no endpoint")
 
 
 class Session:
-    def __init__(self, config: EngineConfig, *, tokenizer=None, registry=None, endpoint: str | None = None):
+    def __init__(self, config: EngineConfig | None = None, *, tokenizer=None, registry=None,
+                 endpoint: str | None = None, token: str | None = None):
         self.config = config
-        self.model_cfg = check_config(config)
+        self.model_cfg = check_config(config) if config is not None else None
         self.catalog: dict = {}
         self.settings: dict = {}
         self.tokenizer_path = tokenizer
@@ -108,7 +105,7 @@ class Session:
         self._remote = None
         if endpoint is not None:
             from quail_b200.server.client import RemoteConnection
-            self._remote = RemoteConnection(endpoint)
+            self._remote = RemoteConnection(endpoint, token)
 
     # ------------------------------------------------------------ tables
     def register(self, name: str, provider) -> None:
@@ -130,8 +127,17 @@ class Session:
         self.catalog.pop(name, None)
 
     # ------------------------------------------------------------ queries
-    def sql(self, text: str, dialect: str = "snowflake") -> Query:
+    def sql(self, text: str, dialect: str = "snowflake"):
+        if self._remote is not None:
+            from quail_b200.server.client import RemoteQuery
+            return RemoteQuery(self, text, dialect)
         return Query(self, text, dialect)
+
+    def get_run(self, query_id: str):
+        """The run of a query a server already has (remote sessions)."""
+        if self._remote is None:
+            raise RuntimeError("get_run() reads a Quail server's submission; this session has no endpoint")
+        return self._remote.run(query_id)
 
     def _needs_model(self, tree) -> bool:
         from quail_b200.sql.executor import has_model_call

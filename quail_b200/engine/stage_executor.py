@@ -39,6 +39,10 @@ class OversizedDocumentError(ArenaFullError):
     """A single task needs more pages than the whole arena has."""
 
 
+class QueryCancelled(RuntimeError):
+    """The executor's stop hook asked it to stop between passes."""
+
+
 @dataclass
 class Task:
     key: object
@@ -92,6 +96,7 @@ class StageExecutor:
         self.stats = ExecutorStats()
         self.gpu_timing = gpu_timing and self.device.type == "cuda"
         self._inflight: deque = deque()
+        self.should_stop: Callable | None = None   # checked between passes (cancel / timeout)
 
     # ------------------------------------------------------------ submission
     def submit(self, task: Task) -> None:
@@ -261,6 +266,9 @@ class StageExecutor:
     def run(self) -> ExecutorStats:
         t0 = time.perf_counter()
         while self.queue or self.cont or self._inflight:
+            if self.should_stop is not None and self.should_stop():
+                self.abort()
+                raise QueryCancelled("the query was stopped")
             if not self.step():
                 if self.queue or self.cont:
                     raise ArenaFullError(
@@ -269,3 +277,15 @@ class StageExecutor:
                 break
         self.stats.wall_s += time.perf_counter() - t0
         return self.stats
+
+    def abort(self) -> None:
+        """Drop queued work, wait for in-flight passes, release every resident key."""
+        self.queue.clear()
+        self.cont.clear()
+        while self._inflight:
+            _, _, _, done, _, _ = self._inflight.popleft()
+            if done is not None:
+                done.synchronize()
+        for key in list(self.pool.owned):
+            self.pool.free_key(key)
+        self.written.clear()
