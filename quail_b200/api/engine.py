@@ -37,6 +37,7 @@ class CallSpec:
     labels: list = field(default_factory=list)
     max_tokens: int = 256
     probabilities: bool = False
+    pooling: str = "last"     # features: "last" or "max"
 
 
 @dataclass
@@ -148,10 +149,16 @@ class ModelEngine:
                 answer.append(i)
             return answer.index(i)
 
+        from quail_b200.api.config import Refusal, RefusalError
+        for c in calls:
+            if (c.kind == "features") != self.cfg.has_sae:
+                why = ("AI.SAE_FEATURES needs a model with a sparse autoencoder spec" if c.kind == "features"
+                       else f"{self.cfg.name} serves AI.SAE_FEATURES only")
+                raise RefusalError(Refusal(reasons=(why,), constraint="unsupported_function"))
         rcalls = []
         for c in calls:
             rc = Call(kind=c.kind, suffix=tok.encode(c.tail), name=c.name, max_tokens=c.max_tokens,
-                      stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities)
+                      stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling)
             if c.kind in ("filter", "score"):
                 rc.true_cols = [col(i) for i in true_ids]
                 rc.false_cols = [col(i) for i in false_ids]

@@ -120,6 +120,22 @@ def bind_prompt(template: str, num_args: int = 1, turn: Turn = Turn()) -> BoundP
                        question=question)
 
 
+def bind_features_prompt(template: str, turn: Turn = Turn()) -> BoundPrompt:
+    """AI.SAE_FEATURES: the user's prompt as written, in one user turn.
+
+    The text after the document is required: the features are read at (or
+    pooled up to) the prompt's tokens after the document
+    (quail/backends/quail/executor/operators/sae_features.py:83-86).
+    """
+    check_placeholders(template, 1)
+    i = template.find("{0}")
+    head, rest = template[:i], template[i + 3:]
+    if not rest.strip():
+        raise PromptError("AI.SAE_FEATURES needs a question after the document")
+    return BoundPrompt(kind="features", template=template, preamble=turn.prefix + head, tail=rest,
+                       question=rest.strip())
+
+
 def bind_score_prompt(template: str, num_args: int = 1, turn: Turn = Turn()) -> BoundPrompt:
     p = bind_prompt(template, num_args, turn)
     p.kind = "score"

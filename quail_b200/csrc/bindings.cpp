@@ -73,6 +73,7 @@ void moe_combine(const torch::Tensor& comb, int64_t M, int64_t topk, const torch
 void decode_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                       const torch::Tensor& seqs, const torch::Tensor& dseqs, const torch::Tensor& page_list,
                       double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
+void sae_topk(const torch::Tensor& pre, const torch::Tensor& bias, int64_t keep, torch::Tensor& out);
 
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
@@ -120,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &qb::prefill_attention);
   m.def("prefill_attention_tc", &qb::prefill_attention_tc, "tcgen05/TMEM packed-prompt prefill attention");
   m.def("decode_attention", &qb::decode_attention, "split-KV decode attention, all q heads of a KV head per CTA");
+  m.def("sae_topk", &qb::sae_topk, "SAE features: bias + per-row top-k (radix select), packed indices + strengths");
   m.def("read_and_clear_error", &qb::read_and_clear_error);
   m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");
   m.def("tp_gemm_rs", &qb::tp_gemm_rs, "MX GEMM -> reduce-scatter fused: epilogue pushes tiles to owner ranks");

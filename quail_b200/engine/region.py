@@ -24,6 +24,10 @@ Readouts:
   map       greedy decoding: each step appends the argmax token to the
             question's own pages until a stop token or max_tokens
             (map_decoder.py); extract decodes the same way after the phrase cue
+  features  SAE features of the residual stream (a model with an SAE returns
+            packed [feature ids | strengths] rows): the last token's, or
+            with max pooling each feature's largest strength over the row's
+            own tokens (sae/encoder.py, sae/max_pooling.py)
 
 The document's pages stay resident until the row's last call has answered
 or a filter dropped it.
@@ -55,6 +59,7 @@ class Call:
     stop_ids: tuple = ()
     name: str = ""
     probabilities: bool = False
+    pooling: str = "last"                            # features: "last" token or "max" over the row's tokens
 
 
 @dataclass
@@ -116,6 +121,9 @@ class RegionRun:
             self._classify_first(r, ci, row)
         elif call.kind in ("map", "extract"):
             self._decode_step(r, ci, row, generated=[])
+        elif call.kind == "features":
+            res.values[call.name] = feature_list(row)
+            self._finish_call(r, ci)
         self.asked += 1
 
     def _classify_first(self, r, ci, row):
@@ -211,6 +219,11 @@ class RegionRun:
             self._submit_question(r, c)
 
     @staticmethod
+    def _pooled_rows(call: Call, n: int):
+        """Readout offsets: every own token for max-pooled features, else the last token only."""
+        return tuple(range(n)) if call.kind == "features" and call.pooling == "max" else None
+
+    @staticmethod
     def _reserve(call: Call) -> int:
         """Decode headroom: a decoding call's generated tokens land in its own pages."""
         return call.max_tokens if call.kind in ("map", "extract") else 0
@@ -224,6 +237,7 @@ class RegionRun:
         self.fresh_tokens += len(call.suffix)
         self.ex.submit(Task(key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
                             full_readout=self._needs_full(call), reserve_tokens=self._reserve(call),
+                            readout_rows=self._pooled_rows(call, len(call.suffix)),
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
 
     def submit_all(self) -> None:
@@ -238,6 +252,7 @@ class RegionRun:
             self._pending[r] = 1
             self.ex.submit(Task(key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
                                 full_readout=self._needs_full(first), reserve_tokens=self._reserve(first),
+                                readout_rows=self._pooled_rows(first, len(toks)),
                                 on_done=lambda t, row, r=r: self._answered(r, 0, row), free_after=False))
 
     def run(self):
@@ -245,3 +260,27 @@ class RegionRun:
         self.ex.run()
         self.ex.free(PREFIX_KEY)
         return self.results
+
+
+def feature_list(rows) -> list:
+    """Packed SAE readout rows ([k ids | k strengths] each) -> [(feature, strength)], strongest first.
+
+    One row: its nonzero features. Several rows (max pooling over tokens):
+    each feature's largest strength over the rows.
+    """
+    a = np.asarray(rows, dtype=np.float32)
+    a = a.reshape(-1, a.shape[-1])
+    k = a.shape[1] // 2
+    ids = a[:, :k].astype(np.int64).ravel()
+    st = a[:, k:].ravel()
+    keep = st > 0
+    ids, st = ids[keep], st[keep]
+    if ids.size == 0:
+        return []
+    order = np.lexsort((-st, ids))            # by feature, strongest first within a feature
+    ids, st = ids[order], st[order]
+    first = np.ones(ids.size, dtype=bool)
+    first[1:] = ids[1:] != ids[:-1]
+    ids, st = ids[first], st[first]
+    by = np.lexsort((ids, -st))              # strongest first, lower id on ties
+    return [(int(i), float(v)) for i, v in zip(ids[by], st[by])]

@@ -176,7 +176,8 @@ class StageExecutor:
                         deferred.append(task)
                         break
             piece = min(task.remaining, room)
-            if piece < task.remaining and piece < self.min_piece and specs:
+            if piece < task.remaining and (piece < self.min_piece or task.readout_rows is not None) and specs:
+                # a task read out at several rows runs whole: wait for a chunk with room
                 deferred.append(task)
                 break
             last = piece == task.remaining

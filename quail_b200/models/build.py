@@ -25,6 +25,8 @@ def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str,
     if not cfg.tied_head:
         out["lm_head.weight"] = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device)
                                  * cfg.init_std).bfloat16()
+    from quail_b200.models.weights import random_sae
+    out.update(random_sae(cfg, gen, device))
     return out
 
 

@@ -29,6 +29,10 @@ class DecoderConfig:
     moe_intermediate: int = 0
     max_position: int = 40_960
     init_std: float = 0.02
+    # sparse autoencoder on the residual stream after the last loaded layer
+    # (a model with one serves AI.SAE_FEATURES only); 0 = none
+    sae_features: int = 0
+    sae_keep: int = 0
 
     @property
     def q_dim(self) -> int:
@@ -45,6 +49,10 @@ class DecoderConfig:
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    @property
+    def has_sae(self) -> bool:
+        return self.sae_features > 0
 
     @property
     def fp8(self) -> bool:
@@ -88,9 +96,17 @@ QWEN3_GPU_TINY = DecoderConfig(name="qwen3-gpu-tiny", layers=2, hidden=1024, num
 QWEN3_MOE_GPU_TINY = DecoderConfig(name="qwen3-moe-gpu-tiny", layers=2, hidden=1024, num_q_heads=8,
                                    num_kv_heads=2, head_dim=128, intermediate=1024, num_experts=16, top_k=4,
                                    moe_intermediate=256)
+# AI.SAE_FEATURES models: a Qwen3 decoder truncated after the SAE's layer with a
+# 32K-feature, keep-100 SAE (the shape of the reference's
+# qwen3.5-2b-sae-bf16 spec: layers 0-11 of 24, W32K, L0 100), random init
+QWEN3_4B_SAE = QWEN3_4B.with_(name="qwen3-4b-sae-bf16", layers=12, weight_dtype="bf16", sae_features=32768,
+                              sae_keep=100)
+QWEN3_SAE_TINY = QWEN3_TINY.with_(name="qwen3-sae-tiny", sae_features=512, sae_keep=16)
+QWEN3_GPU_SAE_TINY = QWEN3_GPU_TINY.with_(name="qwen3-gpu-sae-tiny", weight_dtype="bf16", sae_features=2048,
+                                          sae_keep=32)
 
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
-                               QWEN3_MOE_GPU_TINY)}
+                               QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -102,4 +118,7 @@ MODEL_CONFIGS = {
     "qwen3-tiny": QWEN3_TINY,
     "qwen3-gpu-tiny": QWEN3_GPU_TINY,
     "qwen3-moe-gpu-tiny": QWEN3_MOE_GPU_TINY,
+    "qwen3-4b-sae-bf16": QWEN3_4B_SAE,
+    "qwen3-sae-tiny": QWEN3_SAE_TINY,
+    "qwen3-gpu-sae-tiny": QWEN3_GPU_SAE_TINY,
 }

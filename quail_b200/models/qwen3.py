@@ -71,6 +71,9 @@ class Qwen3Weights:
             self.layers.append(L)
         self.head = head_weight(ckpt, cfg)
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=device)
+        if cfg.has_sae:
+            self.sae_w = ckpt["sae.W_enc"].to(device=device, dtype=bf).contiguous()
+            self.sae_b = ckpt["sae.b_enc"].to(device=device, dtype=torch.float32).contiguous()
         self.answer_rows = None
         if head_rows is not None:
             self.set_answer_rows(head_rows)
@@ -138,6 +141,9 @@ class Qwen3Pipeline:
                 a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
                 ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
         del T, dev
+        if cfg.has_sae:
+            # resid_post of the last loaded layer -> packed SAE features per readout row
+            return ops.sae_features(h.index_select(0, chunk.final_rows.long()), w.sae_w, w.sae_b, cfg.sae_keep)
         if not getattr(chunk, "full_readout", False):
             return ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows)
         R = chunk.final_rows.numel()
@@ -193,6 +199,9 @@ class Qwen3Reference:
                          wd=f(dequantized(ckpt, p + "mlp.down_proj")))
             self.layers.append(L)
         self.head = f(head_weight(ckpt, cfg))
+        if cfg.has_sae:
+            self.sae_w = f(ckpt["sae.W_enc"])
+            self.sae_b = f(ckpt["sae.b_enc"])
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=device)
         self.scale = ref.softmax_scale(cfg.head_dim)
         self.answer_rows = None
@@ -266,6 +275,9 @@ class Qwen3Reference:
     def forward_chunk(self, chunk, arena) -> torch.Tensor:
         h = self.hidden_chunk(chunk, arena)
         rows = h[chunk.final_rows.long()]
+        if self.cfg.has_sae:
+            x = self._bf(rows) if self.emulate else rows
+            return ref.sae_features(x, self.sae_w, self.sae_b, self.cfg.sae_keep)
         normed = ref.rmsnorm(rows, self.final_norm, self.cfg.rms_eps)
         ans = (normed @ self.answer_rows.t()).float()
         if not getattr(chunk, "full_readout", False):

@@ -91,7 +91,21 @@ def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=tor
     out["model.norm.weight"] = torch.ones(cfg.hidden, device=device, dtype=dtype)
     if not cfg.tied_head:
         out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
+    out.update(random_sae(cfg, gen, device))
     return out
+
+
+def random_sae(cfg: DecoderConfig, gen: torch.Generator, device="cpu") -> dict[str, torch.Tensor]:
+    """SAE encoder tensors under `sae.W_enc` [F, H] and `sae.b_enc` [F] (the names of SAE
+    checkpoints); empty for a model without one. Encoder rows are unit-norm
+    directions scaled to the residual stream's size, the bias a small
+    negative threshold, so a row activates a few percent of the features."""
+    if not cfg.has_sae:
+        return {}
+    w = torch.randn(cfg.sae_features, cfg.hidden, generator=gen, device=device, dtype=torch.float32)
+    w = w / w.norm(dim=1, keepdim=True) * (0.5 * cfg.hidden ** 0.5)
+    b = -0.5 * torch.rand(cfg.sae_features, generator=gen, device=device, dtype=torch.float32)
+    return {"sae.W_enc": w.to(torch.bfloat16), "sae.b_enc": b}
 
 
 def head_weight(ckpt: dict[str, torch.Tensor], cfg: DecoderConfig) -> torch.Tensor:

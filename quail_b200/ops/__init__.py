@@ -32,6 +32,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     quant_rows,
     read_and_clear_error,
     rmsnorm_quant,
+    sae_features,
     row_argmax_lse,
 )
 from quail_b200.ops.quant import (  # noqa: F401

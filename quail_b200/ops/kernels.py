@@ -267,6 +267,19 @@ def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: boo
     return (out, out_scale) if mx else out
 
 
+def sae_features(x: torch.Tensor, w_enc: torch.Tensor, b_enc: torch.Tensor, keep: int) -> torch.Tensor:
+    """SAE encode of residual rows x [R, H] bf16: [R, 2*keep] fp32 = keep feature ids, then strengths.
+
+    The encode GEMM is the bf16 tcgen05 GEMM; csrc/sae.cu adds the bias and
+    selects the `keep` largest per row (clamped at 0, strongest first).
+    """
+    pre = gemm(x.contiguous(), w_enc)
+    out = torch.empty(x.shape[0], 2 * keep, dtype=torch.float32, device=x.device)
+    count_launch()
+    native().sae_topk(pre, b_enc, keep, out)
+    return out
+
+
 def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, normed=None):
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
     if logits is None:

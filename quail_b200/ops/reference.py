@@ -103,3 +103,12 @@ def moe_route(logits: torch.Tensor, top_k: int):
     p = torch.softmax(logits.float(), dim=-1)
     w, ids = p.topk(top_k, dim=-1)
     return ids, w / w.sum(dim=-1, keepdim=True)
+
+
+def sae_features(x: torch.Tensor, w_enc: torch.Tensor, b_enc: torch.Tensor, keep: int) -> torch.Tensor:
+    """fp32 statement of the SAE readout: [R, 2*keep] = top-keep feature ids, then strengths (>= 0)."""
+    pre = x.float() @ w_enc.float().t() + b_enc.float()
+    v, i = pre.topk(keep, dim=1)
+    v = v.clamp(min=0.0)
+    i = torch.where(v > 0, i, torch.zeros_like(i))
+    return torch.cat([i.float(), v], dim=1)

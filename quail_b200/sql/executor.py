@@ -33,6 +33,9 @@ import pyarrow.compute as pc
 
 from quail_b200.api import prompts as P
 
+# AI.SAE_FEATURES' type: one {feature, strength} struct per nonzero feature, strongest first
+FEATURE_LIST = pa.list_(pa.struct([("feature", pa.int32()), ("strength", pa.float32())]))
+
 CPU_AI_FUNCTIONS = ("AI.PARSE_DOCUMENT", "AI.PDF_PAGES", "AI.IMAGE")
 MODEL_AI_FUNCTIONS = ("AI.IF", "AI_FILTER", "AI.SCORE", "AI.CLASSIFY", "AI.EXTRACT", "AI.EXTRACT_SPAN",
                       "AI.MAP", "AI.SAE_FEATURES")
@@ -182,6 +185,7 @@ class BoundCall:
     selectivity: float | None = None
     questions: list = field(default_factory=list)   # extract: one call per question
     span: bool = False
+    pooling: str = "last"                            # features
 
 
 def _options(node) -> dict:
@@ -276,9 +280,17 @@ def bind_call(node, turn: P.Turn) -> BoundCall:
         return BoundCall(key=key, kind="extract", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, questions=qs,
                          span=name == "AI.EXTRACT_SPAN", max_tokens=64)
     if name == "AI.SAE_FEATURES":
-        from quail_b200.api.config import Refusal, RefusalError
-        raise RefusalError(Refusal(reasons=("AI.SAE_FEATURES needs a model with a sparse autoencoder spec",),
-                                   constraint="unsupported_function"))
+        opts = _options(args[1]) if len(args) == 2 else {}
+        pooling = opts.get("pooling")
+        if len(args) != 2 or pooling not in ("last", "max"):
+            raise QueryError("AI.SAE_FEATURES needs a PROMPT and pooling set to 'last' or 'max'.")
+        template, doc, _ = _prompt_parts(args[0])
+        try:
+            bp = P.bind_features_prompt(template, turn)
+        except P.PromptError as exc:
+            raise QueryError(str(exc)) from None
+        return BoundCall(key=key, kind="features", preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                         pooling=pooling)
     raise QueryError(f"unknown AI function {name}")
 
 
@@ -495,6 +507,10 @@ class Executor:
                 elif c.kind == "classify" and c.probabilities:
                     self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], pa.string())
                     self.ai_values[c.key + "#probs"] = pa.array([v.get(c.key + "#probs") for v in vals])
+                elif c.kind == "features":
+                    self.ai_values[c.key] = pa.array(
+                        [None if v.get(c.key) is None else [{"feature": f, "strength": x} for f, x in v[c.key]]
+                         for v in vals], FEATURE_LIST)
                 else:
                     typ = {"filter": pa.bool_(), "score": pa.float64(), "classify": pa.string(),
                            "map": pa.string()}[c.kind]
@@ -505,7 +521,7 @@ class Executor:
             raise QueryError("this query needs a model; the session has none")
         from quail_b200.api.engine import CallSpec
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
-                          probabilities=c.probabilities) for c in calls]
+                          probabilities=c.probabilities, pooling=c.pooling) for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self.report["regions"].append(out.stats)
         for k in ("asked", "fresh_tokens", "passes"):

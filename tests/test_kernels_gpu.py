@@ -307,3 +307,23 @@ def test_decode_attention(QH, KH, P):
     assert rel_err(out[rows.to(DEV)], want[rows]) < 1e-2
     o8, sf = ops.chunk_attention(q, kc, vc, chunk, scale, mx=True, tc=tc)
     assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
+
+
+@pytest.mark.parametrize("R,F,keep", [(1, 512, 16), (37, 32768, 100), (5, 2048, 1024), (64, 65536, 64)])
+def test_sae_topk(R, F, keep):
+    H = 256
+    x = torch.randn(R, H, device=DEV).bfloat16()
+    w = (torch.randn(F, H, device=DEV) * 0.1).bfloat16()
+    b = -0.3 * torch.rand(F, device=DEV)
+    got = ops.sae_features(x, w, b, keep)
+    pre = (x.float() @ w.float().t()).bfloat16().float() + b   # the kernel's bf16 GEMM output + fp32 bias
+    v, i = pre.topk(keep, dim=1)
+    v = v.clamp(min=0)
+    # strengths: identical multiset (ties may pick different ids), sorted descending
+    assert torch.allclose(got[:, keep:], v, atol=1e-5, rtol=1e-5)
+    ids = got[:, :keep].long()
+    pos = got[:, keep:] > 0
+    assert torch.allclose(pre.gather(1, ids)[pos], got[:, keep:][pos], atol=1e-5, rtol=1e-5)
+    for r in range(R):
+        sel = ids[r][pos[r]]
+        assert sel.unique().numel() == sel.numel()

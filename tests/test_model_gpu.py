@@ -65,3 +65,26 @@ def test_pipeline_matches_fp32_model(weight_dtype, layers):
 def test_smoke_entry():
     from quail_b200.models.smoke import run_smoke
     run_smoke()
+
+
+def test_sae_pipeline_matches_fp32_model():
+    """SAE readout of the kernel pipeline vs the fp32 model rounding where the kernels round."""
+    from quail_b200.models.config import QWEN3_GPU_SAE_TINY
+    cfg = QWEN3_GPU_SAE_TINY.with_(vocab=4096, max_position=8192)
+    ckpt = random_checkpoint(cfg, seed=5, device="cuda")
+    pipe = Qwen3Pipeline(cfg, Qwen3Weights(cfg, ckpt, "cuda", head_rows=[0]))
+    emul = Qwen3Reference(cfg, ckpt, device="cuda", head_rows=[0], emulate_kernels=True)
+    rng = np.random.default_rng(2)
+    prefix = rng.integers(0, 4096, 48).astype(np.int32)
+    docs = [rng.integers(0, 4096, n).astype(np.int32) for n in (10, 200, 64, 129)]
+    suffix = rng.integers(0, 4096, 12).astype(np.int32)
+    got = _run(pipe, cfg, prefix, docs, suffix, torch.bfloat16)
+    want = _run(emul, cfg, prefix, docs, suffix, torch.float32)
+    assert ops.read_and_clear_error(0) == 0
+    k = cfg.sae_keep
+    for g, w in zip(got, want):
+        gs = {int(i) for i, s in zip(g[:k], g[k:]) if s > 0}
+        ws = {int(i) for i, s in zip(w[:k], w[k:]) if s > 0}
+        assert len(gs & ws) >= 0.8 * max(len(ws), 1), (len(gs & ws), len(ws))
+        top = min(len(ws), 8)
+        assert torch.allclose(g[k:k + top], w[k:k + top], rtol=0.05, atol=0.05)
