@@ -218,9 +218,12 @@ __global__ void __launch_bounds__(256) moe_plan_kernel(const PlanParams p) {
       const int c = p.counts[e];
       for (int d = 0; d < p.W; ++d) p.counts_all_peer[d][((size_t)parity * p.W + p.rank) * p.E + e] = c;
     }
-    __threadfence_system();
+    // the CTA's count stores, then one release per peer (cumulative over the barrier)
     __syncthreads();
-    if (t < p.W) st_release_sys(&p.cflag_peer[t][parity * p.W + p.rank], p.epoch);
+    if (t < p.W) {
+      __threadfence_system();
+      st_release_sys(&p.cflag_peer[t][parity * p.W + p.rank], p.epoch);
+    }
     if (t < p.W && !wait_word<true>(&p.cflag_local[parity * p.W + t], p.epoch, p.err)) ok = 0;
     __syncthreads();
     for (int i = t; i < p.W * p.E; i += blockDim.x)
@@ -551,10 +554,13 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       }
     }
     if constexpr (MODE == kMoeDown) {
-      // every epilogue thread's stores are visible system-wide before the counts
-      __threadfence_system();
+      // every epilogue thread's stores, then one system fence (cumulative over the barrier) before the counts
       named_bar_sync(1, EPI_THREADS);
-      if (warp == 2 && lane < p.W && push_count[lane]) atomicAdd_system(p.comb_counter_peer[lane], (unsigned)push_count[lane]);
+      if (warp == 2 && lane == 0) {
+        __threadfence_system();
+        for (int d = 0; d < p.W; ++d)
+          if (push_count[d]) atomicAdd_system(p.comb_counter_peer[d], (unsigned)push_count[d]);
+      }
     }
   } else if constexpr (MODE == kMoeGateUp) {
     // ------------------------------------------------------------ dispatch warps
@@ -592,9 +598,11 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         if (lane == 31)
           p.recv_meta_peer[d][R] = make_int2((int)(((uint32_t)p.rank << 28) | (uint32_t)item), __float_as_int(p.wts[item]));
       }
-      __threadfence_system();
       __syncwarp();
-      if (lane == 0) atomicAdd_system(p.recv_count_peer[d] + le, (unsigned)n);
+      if (lane == 0) {
+        __threadfence_system();  // the warp's row stores (ordered by the warp barrier) before the count
+        atomicAdd_system(p.recv_count_peer[d] + le, (unsigned)n);
+      }
     }
   }
 

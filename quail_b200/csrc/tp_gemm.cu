@@ -67,7 +67,24 @@ struct TpParams {
   int num_m_tiles, num_n_tiles;
 };
 
-constexpr int kTpWarps = 12;  // producer, MMA, 8 epilogue, 2 gather
+constexpr int kTpWarps = 12;  // producer, MMA, 8 epilogue, 2 gather (one elected thread copies)
+constexpr int kTpGatherPiece = 8192;  // bytes per bulk copy; two in flight per CTA
+constexpr int kTpGatherSmem = 2 * kTpGatherPiece + 256;
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(smem_src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 constexpr int kTpThreads = kTpWarps * 32;
 
 template <int MODE>
@@ -92,7 +109,9 @@ __global__ void __launch_bounds__(kTpThreads, 1)
   uint64_t* done_bar = acc_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   int* push_count = reinterpret_cast<int*>(tmem_slot + 4);  // [kTpMax] tiles this CTA sent to each rank
-  volatile int* gather_ok = push_count + kTpMax;
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(push_count + kTpMax + 2);  // 8-byte aligned: 2 gather barriers
+  uint8_t* gstage = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(gbar + 2) + 127) & ~static_cast<uintptr_t>(127));  // 2 x kTpGatherPiece
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_k = p.K / 128;
@@ -108,6 +127,8 @@ __global__ void __launch_bounds__(kTpThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, EPI_THREADS);
     mbar_init(done_bar, 1);
+    mbar_init(&gbar[0], 1);
+    mbar_init(&gbar[1], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -287,57 +308,88 @@ __global__ void __launch_bounds__(kTpThreads, 1)
       }
     }
     if constexpr (MODE == kTpRs) {
-      // every epilogue thread's P2P stores are visible system-wide before the counts
-      __threadfence_system();
+      // every epilogue thread's P2P stores, then one system fence (cumulative over the barrier)
       named_bar_sync(1, EPI_THREADS);
       if (warp == 2 && lane == 0) {
+        __threadfence_system();
         for (int d = 0; d < p.tp; ++d)
           if (push_count[d]) atomicAdd_system(p.rs_counter[d], (unsigned)push_count[d]);
       }
     }
   } else if constexpr (MODE != kTpRs) {
-    // ------------------------------------------------------------ gather warps (AG)
-    const int gt = threadIdx.x - 10 * 32;  // 0..63
-    const int remote_tiles = (p.tp - 1) * tpr;
-    int seen_peer = -1;
-    bool ok = true;
-    for (int g = blockIdx.x; g < remote_tiles && ok; g += gridDim.x) {
-      const int o = (p.rank + 1 + g / tpr) % p.tp;  // nearest peer first
-      const int tm = o * tpr + g % tpr;
-      if (o != seen_peer) {
-        // one thread waits on the peer's flag; both gather warps read the outcome
-        if (gt == 0) *gather_ok = wait_word<true>(p.flag_peer[o], p.epoch, p.err) ? 1 : 0;
-        named_bar_sync(2, 64);
-        if (!*gather_ok) {
-          ok = false;
-          break;
+    // ------------------------------------------------------------ gather (AG)
+    // One elected thread streams each remote m-tile (its 128 rows, then its
+    // scale atoms: two contiguous ranges) from the peer's symmetric buffer
+    // into the same rows here: bulk loads peer -> shared memory (two 8 KB
+    // slots, both in flight) and bulk stores shared -> local memory. Then it
+    // releases the m-tile's ready word for the TMA producers of every CTA.
+    if (threadIdx.x == 10 * 32) {
+      const int remote_tiles = (p.tp - 1) * tpr;
+      int seen_peer = -1;
+      uint32_t gph[2] = {0u, 0u};
+      bool pend[2] = {false, false};  // a bulk load into the slot is issued and not yet waited for
+      bool ok = true;
+      for (int g = blockIdx.x; g < remote_tiles && ok; g += gridDim.x) {
+        const int o = (p.rank + 1 + g / tpr) % p.tp;  // nearest peer first
+        const int tm = o * tpr + g % tpr;
+        if (o != seen_peer) {
+          if (!wait_word<true>(p.flag_peer[o], p.epoch, p.err)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();  // the bulk loads below read what the acquire made visible
+          seen_peer = o;
         }
-        seen_peer = o;
-      }
-      // rows [tm*128, tm*128+128) x K bytes, then the m-tile's scale atoms
-      const size_t a_off = (size_t)tm * BM * p.K;
-      const uint4* src = reinterpret_cast<const uint4*>(p.a_peer[o] + a_off);
-      uint4* dst = reinterpret_cast<uint4*>(p.a_local + a_off);
-      const int n16 = BM * p.K / 16;
-      for (int i = gt; i < n16; i += 64 * 4) {
-        uint4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (i + u * 64 < n16) v[u] = src[i + u * 64];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (i + u * 64 < n16) dst[i + u * 64] = v[u];
-      }
-      const size_t s_off = (size_t)tm * num_k * 512;
-      const uint4* ssrc = reinterpret_cast<const uint4*>(p.sfa_peer[o] + s_off);
-      uint4* sdst = reinterpret_cast<uint4*>(p.sfa_local + s_off);
-      for (int i = gt; i < num_k * 32; i += 64) sdst[i] = ssrc[i];
-      __threadfence();
-      named_bar_sync(2, 64);
-      if (gt == 0) {
+        const size_t a_off = (size_t)tm * BM * p.K, a_len = (size_t)BM * p.K;
+        const size_t s_off = (size_t)tm * num_k * 512, s_len = (size_t)num_k * 512;
+        const size_t total = a_len + s_len;
+        const int pieces = (int)((total + kTpGatherPiece - 1) / kTpGatherPiece);
+        auto src_of = [&](int i) -> const uint8_t* {
+          const size_t off = (size_t)i * kTpGatherPiece;
+          return off < a_len ? p.a_peer[o] + a_off + off : p.sfa_peer[o] + s_off + (off - a_len);
+        };
+        auto dst_of = [&](int i) -> uint8_t* {
+          const size_t off = (size_t)i * kTpGatherPiece;
+          return off < a_len ? p.a_local + a_off + off : p.sfa_local + s_off + (off - a_len);
+        };
+        // pieces never straddle the A / scale boundary: a_len is a multiple of the piece size
+        auto size_of = [&](int i) -> uint32_t {
+          const size_t off = (size_t)i * kTpGatherPiece;
+          const size_t end = off < a_len ? a_len : total;
+          return (uint32_t)min((size_t)kTpGatherPiece, end - off);
+        };
+        auto issue = [&](int i) {
+          const int slot = i & 1;
+          mbar_arrive_expect_tx(&gbar[slot], size_of(i));
+          bulk_load(gstage + slot * kTpGatherPiece, src_of(i), size_of(i), &gbar[slot]);
+          pend[slot] = true;
+        };
+        issue(0);
+        if (pieces > 1) issue(1);
+        for (int i = 0; i < pieces; ++i) {
+          const int slot = i & 1;
+          if (!mbar_wait(&gbar[slot], gph[slot], p.err, kErrTimeoutPeer)) {
+            ok = false;
+            break;
+          }
+          gph[slot] ^= 1u;
+          pend[slot] = false;
+          bulk_store(dst_of(i), gstage + slot * kTpGatherPiece, size_of(i));
+          bulk_commit();
+          if (i + 2 < pieces) {
+            bulk_wait_read<0>();  // the slot's bytes have left shared memory
+            issue(i + 2);
+          }
+        }
+        bulk_wait<0>();  // every store of this m-tile is in local memory
+        if (!ok) break;
         fence_proxy_async_global();
         st_release_gpu(&p.tile_ready[tm], p.epoch);
       }
+      // on a timeout, wait (bounded) for the loads still landing in shared memory
+      for (int slot = 0; slot < 2; ++slot)
+        if (pend[slot] && mbar_wait(&gbar[slot], gph[slot], p.err, kErrTimeoutPeer)) gph[slot] ^= 1u;
+      bulk_wait<0>();
     }
   }
 
@@ -422,9 +474,9 @@ __global__ void rs_reduce_norm_kernel(const __nv_bfloat16* __restrict__ slots, i
     }
   }
   // last CTA out raises this rank's shard-ready flag for the peers
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();  // the CTA's rows (ordered by the barrier) before the count and the flag
     const uint32_t prev = atomicAdd(done_ctr, 1u);
     if (prev + 1 == done_want) st_release_sys(flag, epoch);
   }
@@ -450,7 +502,7 @@ static void fill_ptrs(TpParams& p, const std::vector<int64_t>& a, const std::vec
 
 template <int MODE>
 static void launch_tp(const CUtensorMap& ta, const CUtensorMap& tb, TpParams& p, cudaStream_t st, int dev) {
-  constexpr int smem = kMxSmem + 64;
+  constexpr int smem = kMxSmem + 64 + kTpGatherSmem;
   static bool configured[64] = {false};
   if (!configured[dev]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(tp_gemm_mx_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

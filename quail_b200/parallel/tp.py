@@ -107,6 +107,8 @@ class TPQwen3:
         # "nccl": the baseline the fused kernels are measured against: NCCL
         # all-gather / reduce-scatter around the same MX GEMMs
         self.comm = comm
+        from quail_b200.utils.op_timer import OpTimer
+        self.timer = OpTimer()
         self.cfg = cfg
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.st = TPState(cfg, group, max_tokens, self.device)
@@ -245,29 +247,48 @@ class TPQwen3:
         slots[:T] = chunk.slots
         h = ops.embed_gather(ids[r * rpr:(r + 1) * rpr].contiguous(), self.embed)  # own residual rows
         fused = self.comm == "fused"
+        tm = self.timer
         for li, L in enumerate(self.layers):
             kc, vc = arena.layer(li)
             if fused:
-                self._norm(h, L["ln1"], M, rpr, tp_slots=tp if li > 0 else 0)
-                qkv = self._ag(M, H, rpr, L["wqkv"], L["sqkv"], mode=0)
+                with tm("norm_ln1"):
+                    self._norm(h, L["ln1"], M, rpr, tp_slots=tp if li > 0 else 0)
+                with tm("ag_gemm_qkv"):
+                    qkv = self._ag(M, H, rpr, L["wqkv"], L["sqkv"], mode=0)
             else:
-                xa, sa = self._nccl_ag(h, L["ln1"], M, rpr)
-                qkv = ops.gemm_mx(xa, sa, L["wqkv"], L["sqkv"])
-            q = ops.qk_norm_rope_kv(qkv, pos, L["qn"], L["kn"], self.cos_sin, slots, kc, vc, self.qh, self.kh,
-                                    cfg.rms_eps)
-            o8 = torch.zeros(M, self.qh * 128, dtype=torch.float8_e4m3fn, device=dev)  # padding rows stay 0
-            os_ = torch.zeros(ops.sf_bytes(M, self.qh * 128), dtype=torch.uint8, device=dev)
-            ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True, out=o8, out_scale=os_)
+                with tm("nccl_ag_ln1"):
+                    xa, sa = self._nccl_ag(h, L["ln1"], M, rpr)
+                with tm("gemm_qkv"):
+                    qkv = ops.gemm_mx(xa, sa, L["wqkv"], L["sqkv"])
+            with tm("rope_kv"):
+                q = ops.qk_norm_rope_kv(qkv, pos, L["qn"], L["kn"], self.cos_sin, slots, kc, vc, self.qh, self.kh,
+                                        cfg.rms_eps)
+            with tm("attention"):
+                o8 = torch.zeros(M, self.qh * 128, dtype=torch.float8_e4m3fn, device=dev)  # padding rows stay 0
+                os_ = torch.zeros(ops.sf_bytes(M, self.qh * 128), dtype=torch.uint8, device=dev)
+                ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True, out=o8, out_scale=os_)
             if fused:
-                self._rs(o8, os_, L["wo"], L["so"], rpr)
-                self._norm(h, L["ln2"], M, rpr, tp_slots=tp)
-                a8, as_ = self._ag(M, H, rpr, L["wgu"], L["sgu"], mode=1)
-                self._rs(a8, as_, L["wd"], L["sd"], rpr)
+                with tm("gemm_rs_o"):
+                    self._rs(o8, os_, L["wo"], L["so"], rpr)
+                with tm("norm_ln2"):
+                    self._norm(h, L["ln2"], M, rpr, tp_slots=tp)
+                with tm("ag_gemm_gate_up"):
+                    a8, as_ = self._ag(M, H, rpr, L["wgu"], L["sgu"], mode=1)
+                with tm("gemm_rs_down"):
+                    self._rs(a8, as_, L["wd"], L["sd"], rpr)
             else:
-                self._nccl_rs_add(ops.gemm_mx(o8, os_, L["wo"], L["so"]), h)
-                xa, sa = self._nccl_ag(h, L["ln2"], M, rpr)
-                a8, as_ = ops.gemm_mx(xa, sa, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
-                self._nccl_rs_add(ops.gemm_mx(a8, as_, L["wd"], L["sd"]), h)
+                with tm("gemm_o"):
+                    part = ops.gemm_mx(o8, os_, L["wo"], L["so"])
+                with tm("nccl_rs_o"):
+                    self._nccl_rs_add(part, h)
+                with tm("nccl_ag_ln2"):
+                    xa, sa = self._nccl_ag(h, L["ln2"], M, rpr)
+                with tm("gemm_gate_up"):
+                    a8, as_ = ops.gemm_mx(xa, sa, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
+                with tm("gemm_down"):
+                    part = ops.gemm_mx(a8, as_, L["wd"], L["sd"])
+                with tm("nccl_rs_down"):
+                    self._nccl_rs_add(part, h)
         if fused:
             # last down-projection: sum it into the residual (the final norm runs in the readout)
             self._norm(h, self.final_norm, M, rpr, tp_slots=tp)

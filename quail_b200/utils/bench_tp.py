@@ -63,6 +63,7 @@ def main():
     torch.cuda.synchronize()
     dist.barrier()
     tok0, passes0 = ex.stats.tokens, ex.stats.passes
+    model.timer.reset()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(args.steps):
@@ -72,6 +73,7 @@ def main():
     ms = s.elapsed_time(e)
     fresh = ex.stats.tokens - tok0
     rows = sum(ex.stats.pass_rows[passes0:])
+    ops_ms = model.timer.summary()  # QB_OP_TIMING=1: device ms per op over the timed steps (this rank)
     err = model.check_errors()
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -83,7 +85,8 @@ def main():
                           "unit": "prompt tokens/s", "rows_per_second": round(rows / (ms_max / 1e3), 1),
                           "fresh_tokens_per_second": round(fresh / (ms_max / 1e3), 1),
                           "ms_per_step": round(ms_max / args.steps, 3), "steps": args.steps,
-                          "chunk_tokens": args.chunk_tokens, "kernel_error": err}), flush=True)
+                          "chunk_tokens": args.chunk_tokens, "kernel_error": err,
+                          **({"op_ms_rank0": ops_ms} if ops_ms else {})}), flush=True)
     dist.barrier()
     del model
     dist.destroy_process_group()
