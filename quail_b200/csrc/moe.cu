@@ -342,7 +342,9 @@ template <int MODE>
 __global__ void __launch_bounds__(kMoeThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const MoeGemmParams p) {
-  constexpr int BM = 128, BN = kMxBN, STAGES = kMxStages;
+  // the down GEMM stages its output rows in shared memory for coalesced
+  // stores to the tokens' homes (64 KB), so it keeps three pipeline stages
+  constexpr int BM = 128, BN = kMxBN, STAGES = MODE == kMoeDown ? 3 : kMxStages;
   constexpr int EPI_THREADS = BN;
   constexpr int TMEM_COLS = 512;
 
@@ -361,6 +363,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   int* push_count = reinterpret_cast<int*>(tmem_slot + 4);  // [kMoeMaxRanks]
   int* s_unit = push_count + kMoeMaxRanks;                  // [E + 1] dispatch unit prefix
+  uint8_t* rstage = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(s_unit + kMoeMaxExperts + 1) + 127) & ~static_cast<uintptr_t>(127));  // down: 8 x 8 KB
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_k = p.K / 128;
@@ -509,20 +513,30 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
-      if (row >= valid) continue;
       if constexpr (MODE == kMoeDown) {
-        const int2 meta = p.recv_meta[m];
-        const int home = (int)((uint32_t)meta.x >> 28);
-        const int item = meta.x & 0x0fffffff;
-        const float w = __int_as_float(meta.y);
+        // each row: weighted by its routing weight, stored at (token, k) of its home's combine buffer
+        const bool live = row < valid;
+        int home = 0, item = 0;
+        if (live) {
+          const int2 meta = p.recv_meta[m];
+          home = (int)((uint32_t)meta.x >> 28);
+          item = meta.x & 0x0fffffff;
+          const float w = __int_as_float(meta.y);
 #pragma unroll
-        for (int i = 0; i < 128; ++i) acc[i] *= w;
+          for (int i = 0; i < 128; ++i) acc[i] *= w;
+          atomicAdd(&push_count[home], 1);
+        }
         const int n0 = tn * BN + h * 128;
-        __nv_bfloat16* dst = p.comb_peer[home] + (size_t)item * p.N + n0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 8) st_bf16x8(dst + j, &acc[j]);
-        atomicAdd(&push_count[home], 1);
-      } else {
+        warp_push_rows(acc, rstage + ew * 8192, lane, [&](int r) -> __nv_bfloat16* {
+          const int hr = __shfl_sync(0xffffffffu, home, r);
+          const int ir = __shfl_sync(0xffffffffu, item, r);
+          const bool lv = __shfl_sync(0xffffffffu, (int)live, r) != 0;
+          return lv ? p.comb_peer[hr] + (size_t)ir * p.N + n0 : nullptr;
+        });
+        continue;
+      }
+      if (row >= valid) continue;
+      {
         // gate = acc[0..63], up = acc[64..127] of outputs out0 .. out0+63
         const int out0 = tn * (BN / 2) + h * 64;
 #pragma unroll
@@ -749,7 +763,8 @@ void moe_sort(const torch::Tensor& ids, const torch::Tensor& pos, int64_t n, con
 template <int MODE>
 static void launch_moe(const CUtensorMap& ta, const CUtensorMap& tb, MoeGemmParams& p, int grid, cudaStream_t st,
                        int dev) {
-  constexpr int smem = kMxSmem + kMoeExtraSmem;
+  constexpr int smem = MODE == kMoeDown ? mx_pipeline_smem(3) + kMoeExtraSmem + 128 + 8 * 8192
+                                       : kMxSmem + kMoeExtraSmem;
   static bool configured[64] = {false};
   if (!configured[dev]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

@@ -86,4 +86,39 @@ constexpr int kMxSmem = kMxStages * (kMxABytes + kMxBBytes) + kMxStages * (kMxSf
 constexpr int kMxSfaCol = kMxBN;       // TMEM columns after the accumulator
 constexpr int kMxSfbCol = kMxBN + 4;
 
+
+// Bytes of shared memory that a pipeline of `stages` MX stages needs (tiles,
+// scale chunks, 1024 alignment slack, barriers).
+__host__ __device__ constexpr int mx_pipeline_smem(int stages) {
+  return stages * (kMxABytes + kMxBBytes + kMxSfaBytes + kMxSfbBytes) + 1024 + 256;
+}
+
+// Store a warp's 32 accumulator rows (row = lane, 128 fp32 columns in acc) as
+// bf16 to per-row destinations, through an 8 KB shared buffer, so that each
+// store instruction writes two rows' contiguous 256 bytes instead of 32 rows'
+// 16 bytes: peer stores then cross NVLink in large packets. dst_of(r) gives
+// row r's first column, or nullptr to skip the row. The 16-byte chunks of a
+// row are XOR-swizzled by the row index against bank conflicts.
+template <class DstOf>
+__device__ __forceinline__ void warp_push_rows(const float* acc, uint8_t* wbuf, int lane, DstOf dst_of) {
+  uint4* mine = reinterpret_cast<uint4*>(wbuf + lane * 256);
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(acc[c * 8 + 2 * i], acc[c * 8 + 2 * i + 1]);
+    mine[c ^ (lane & 15)] = *reinterpret_cast<const uint4*>(h);
+  }
+  __syncwarp();
+  const int c = lane & 15;
+#pragma unroll 4
+  for (int k = 0; k < 16; ++k) {
+    const int r = 2 * k + (lane >> 4);
+    const uint4 v = reinterpret_cast<const uint4*>(wbuf + r * 256)[c ^ (r & 15)];
+    __nv_bfloat16* dst = dst_of(r);
+    if (dst != nullptr) reinterpret_cast<uint4*>(dst)[c] = v;
+  }
+  __syncwarp();
+}
+
 }  // namespace qb

@@ -91,7 +91,9 @@ template <int MODE>
 __global__ void __launch_bounds__(kTpThreads, 1)
     tp_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const TpParams p) {
-  constexpr int BM = 128, BN = kMxBN, STAGES = kMxStages;
+  // GEMM -> RS stages its output rows in shared memory for coalesced peer
+  // stores (64 KB), so it keeps three pipeline stages instead of four
+  constexpr int BM = 128, BN = kMxBN, STAGES = MODE == kTpRs ? 3 : kMxStages;
   constexpr int EPI_THREADS = BN;
   constexpr int TMEM_COLS = 512;
 
@@ -262,19 +264,20 @@ __global__ void __launch_bounds__(kTpThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
-      if (m >= p.M) continue;
+      if (MODE != kTpRs && m >= p.M) continue;
       if constexpr (MODE == kTpAgBf16) {
         __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + n0;
 #pragma unroll
         for (int j = 0; j < 128; j += 8)
           if (n0 + j < p.N) st_bf16x8(dst + j, &acc[j]);
       } else if constexpr (MODE == kTpRs) {
-        // rows of rank d's shard go to d's receive slot for this source
-        const int d = m / p.rpr;
-        __nv_bfloat16* dst = p.rs_slot[d] + (size_t)(m - d * p.rpr) * p.ld_slot + n0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 8)
-          if (n0 + j < p.N) st_bf16x8(dst + j, &acc[j]);
+        // the tile's rows all belong to rank d's shard: d's receive slot for this source
+        const int m0 = tm * BM + q * 32;  // this warp's first row
+        const int d = m0 / p.rpr;
+        __nv_bfloat16* base = p.rs_slot[d] + (size_t)(m0 - d * p.rpr) * p.ld_slot + n0;
+        warp_push_rows(acc, gstage + ew * 8192, lane, [&](int r) -> __nv_bfloat16* {
+          return m0 + r < p.M ? base + (size_t)r * p.ld_slot : nullptr;
+        });
         if (row == 0 && h == 0) push_count[d] += 1;  // one count per tile (rows of a tile share d)
       } else {
         const int out0 = tn * (BN / 2) + h * 64;
@@ -502,7 +505,9 @@ static void fill_ptrs(TpParams& p, const std::vector<int64_t>& a, const std::vec
 
 template <int MODE>
 static void launch_tp(const CUtensorMap& ta, const CUtensorMap& tb, TpParams& p, cudaStream_t st, int dev) {
-  constexpr int smem = kMxSmem + 64 + kTpGatherSmem;
+  // AG modes: 4 stages + the gather's staging; RS: 3 stages + 8 KB of row staging per epilogue warp
+  constexpr int smem = MODE == kTpRs ? mx_pipeline_smem(3) + 64 + 256 + 8 * 8192
+                                     : mx_pipeline_smem(kMxStages) + 64 + kTpGatherSmem;
   static bool configured[64] = {false};
   if (!configured[dev]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(tp_gemm_mx_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -571,7 +576,7 @@ void tp_gemm_rs(const torch::Tensor& a, const torch::Tensor& sfa, const torch::T
   const int M = a.size(0), K = a.size(1), N = b.size(0);
   const int tp = (int)slot_ptrs.size();
   TORCH_CHECK(tp >= 1 && tp <= kTpMax && (int64_t)M == rpr * tp && rpr % 128 == 0, "tp_gemm_rs: M = tp x rpr");
-  TORCH_CHECK(K % 128 == 0 && N % 16 == 0 && ld_slot % 8 == 0, "tp_gemm_rs shapes");
+  TORCH_CHECK(K % 128 == 0 && N % kMxBN == 0 && ld_slot % 8 == 0, "tp_gemm_rs shapes: K % 128, N % 256");
   const int dev = a.get_device();
   c10::cuda::CUDAGuard guard(dev);
   cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
