@@ -96,6 +96,22 @@ class ModelEngine:
         from quail_b200.engine.arena import KVArena
         from quail_b200.engine.stage_executor import StageExecutor
         ckpt = self._checkpoint()
+        if self.cfg.is_hybrid:
+            from quail_b200.models.qwen3_5 import Qwen35Reference
+            if self.on_gpu:
+                from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
+                self.model = Qwen35Pipeline(self.cfg, ckpt, self.device)
+                page_tokens, dtype = 128, torch.bfloat16
+            else:
+                self.model = Qwen35Reference(self.cfg, ckpt, device="cpu")
+                page_tokens, dtype = 16, torch.float32
+            del ckpt
+            n_pages = pages or self.budgets.arena_pages(page_tokens)
+            self.arena = KVArena.for_model(self.cfg, n_pages, page_tokens, device=self.device, dtype=dtype,
+                                           state_slots=self.budgets.state_slots(self.cfg))
+            self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
+                                          gpu_timing=self.config.gpu_timing)
+            return
         if self.on_gpu:
             from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights
             self.model = Qwen3Pipeline(self.cfg, Qwen3Weights(self.cfg, ckpt, self.device))
@@ -112,7 +128,7 @@ class ModelEngine:
                                       gpu_timing=self.config.gpu_timing)
 
     def _set_answer_rows(self, ids):
-        if self.on_gpu:
+        if self.on_gpu and not self.cfg.is_hybrid:
             self.model.w.set_answer_rows(ids)
         else:
             self.model.set_answer_rows(ids)

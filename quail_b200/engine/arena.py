@@ -31,9 +31,22 @@ class ArenaFullError(RuntimeError):
 
 
 class PagePool:
-    def __init__(self, num_pages: int, page_tokens: int):
+    """Page accounting; with `state_slots`, also one recurrent-state slot per key.
+
+    Hybrid models (Gated DeltaNet layers) keep a fixed-size state per key
+    instead of per-token KV: the state after the key's tokens. A reader of a
+    key starts its own state from it, so borrowing holds the parent's slot
+    as it holds the parent's pages.
+    """
+
+    def __init__(self, num_pages: int, page_tokens: int, state_slots: int = 0):
         self.num_pages = num_pages
         self.page_tokens = page_tokens
+        self.state_slots = state_slots
+        self.slot_free = list(range(state_slots - 1, -1, -1))
+        self.slot_of: dict = {}          # key -> its state slot
+        self.slot_holds = np.zeros(max(state_slots, 1), dtype=np.int32)
+        self.slot_borrows: dict = {}     # key -> slots of the keys it reads
         self.free = list(range(num_pages - 1, -1, -1))  # stack: pop() gives the lowest id first
         self.owned: dict = {}          # key -> page ids it writes
         self.tokens: dict = {}         # key -> tokens resident
@@ -63,9 +76,14 @@ class PagePool:
         if key in self.owned:
             raise KeyError(f"{key!r} already resident")
         need = self.pages_needed(max(tokens, capacity))
-        if need > len(self.free):
+        if need > len(self.free) or (self.state_slots and not self.slot_free):
             return None
         pages = [self.free.pop() for _ in range(need)]
+        if self.state_slots:
+            slot = self.slot_free.pop()
+            self.slot_of[key] = slot
+            self.slot_holds[slot] += 1
+            self.slot_borrows[key] = []
         self.owned[key] = pages
         self.tokens[key] = tokens
         self.holds[pages] += 1
@@ -92,6 +110,10 @@ class PagePool:
         pages = list(self.owned[parent])
         self.holds[pages] += 1
         self.borrows.setdefault(reader, []).append(pages)
+        if self.state_slots:
+            slot = self.slot_of[parent]
+            self.slot_holds[slot] += 1
+            self.slot_borrows.setdefault(reader, []).append(slot)
 
     # ------------------------------------------------------------ release
     def _drop(self, pages) -> None:
@@ -102,10 +124,19 @@ class PagePool:
             if self.holds[p] == 0:
                 self.free.append(p)
 
+    def _drop_slot(self, slot: int) -> None:
+        self.slot_holds[slot] -= 1
+        if self.slot_holds[slot] == 0:
+            self.slot_free.append(slot)
+
     def free_key(self, key) -> None:
         """Release a key's own pages and the holds it took on borrowed parents."""
         for pages in self.borrows.pop(key, []):
             self._drop(pages)
+        for slot in self.slot_borrows.pop(key, []):
+            self._drop_slot(slot)
+        if key in self.slot_of:
+            self._drop_slot(self.slot_of.pop(key))
         pages = self.owned.pop(key, None)
         self.tokens.pop(key, None)
         self.retained.pop(key, None)
@@ -138,13 +169,25 @@ class PagePool:
         assert len(free) == len(self.free), "page freed twice"
         for p in range(self.num_pages):
             assert (p in free) == (self.holds[p] == 0), f"page {p} free/held mismatch"
+        if self.state_slots:
+            want = np.zeros(self.state_slots, dtype=np.int32)
+            for slot in self.slot_of.values():
+                want[slot] += 1
+            for slots in self.slot_borrows.values():
+                for slot in slots:
+                    want[slot] += 1
+            assert np.array_equal(want, self.slot_holds[:self.state_slots]), "state slot holds drifted"
+            sf = set(self.slot_free)
+            assert len(sf) == len(self.slot_free), "state slot freed twice"
+            for q in range(self.state_slots):
+                assert (q in sf) == (want[q] == 0), f"state slot {q} free/held mismatch"
 
 
 class KVArena:
     """Device K/V pools with a PagePool."""
 
     def __init__(self, num_layers: int, num_pages: int, page_tokens: int, kv_heads: int, head_dim: int,
-                 device="cuda", dtype=torch.bfloat16):
+                 device="cuda", dtype=torch.bfloat16, state_slots: int = 0, state_shapes: dict | None = None):
         self.num_layers = num_layers
         self.page_tokens = page_tokens
         self.kv_heads = kv_heads
@@ -152,7 +195,23 @@ class KVArena:
         self.device = torch.device(device)
         self.kv = torch.zeros(num_layers, 2, num_pages, page_tokens, kv_heads, head_dim, device=device,
                               dtype=dtype)
-        self.pool = PagePool(num_pages, page_tokens)
+        self.pool = PagePool(num_pages, page_tokens, state_slots)
+        # recurrent states of hybrid models: name -> [slots, *shape] fp32 (e.g. conv window, delta-rule state)
+        self.states = {name: torch.zeros(state_slots, *shape, device=device, dtype=torch.float32)
+                       for name, shape in (state_shapes or {}).items()}
+
+    @classmethod
+    def for_model(cls, cfg, num_pages: int, page_tokens: int, device="cuda", dtype=torch.bfloat16,
+                  state_slots: int = 0) -> "KVArena":
+        """KV pages for the model's attention layers; state slots for its Gated DeltaNet layers."""
+        shapes = None
+        if cfg.is_hybrid:
+            G = len(cfg.gdn_layers)
+            shapes = {"conv": (G, cfg.conv_width - 1, cfg.gdn_conv_dim),
+                      "ssm": (G, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim)}
+            state_slots = state_slots or 64
+        return cls(len(cfg.attn_layers), num_pages, page_tokens, cfg.num_kv_heads, cfg.head_dim, device=device,
+                   dtype=dtype, state_slots=state_slots if cfg.is_hybrid else 0, state_shapes=shapes)
 
     @property
     def num_pages(self) -> int:

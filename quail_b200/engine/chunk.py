@@ -7,6 +7,7 @@ sequences, plus the metadata the kernels read:
   seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
   tiles                   [n, 2]     (sequence, first query token) per 32-token prefill-attention tile
   dseqs                   [d]        sequences with one new token (decode attention: one CTA per KV head)
+  state_io                [S, 2]     hybrid models: state slot each sequence starts from (-1 = zeros), slot it ends in
   page_list               [*]        page ids of every segment, segments point into it
   final_rows              [R]        token row whose logits each readout reads
 
@@ -54,6 +55,7 @@ class Chunk:
     final_rows: torch.Tensor
     readout_tags: list = field(default_factory=list)
     dseqs: torch.Tensor | None = None
+    state_io: torch.Tensor | None = None
     num_seqs: int = 0
     host: dict | None = None   # numpy copies (tests, CPU reference)
     upload_bytes: int = 0
@@ -78,6 +80,8 @@ class ChunkPacker:
         pos = np.empty(n_tok, dtype=np.int32)
         slots = np.empty(n_tok, dtype=np.int32)
         seqs = np.zeros((len(specs), SEQ_INTS), dtype=np.int32)
+        state_io = np.full((len(specs), 2), -1, dtype=np.int32)
+        slots_on = self.pool.state_slots > 0
         page_list: list[int] = []
         seg_cache: dict = {}
         tiles: list[tuple[int, int]] = []
@@ -96,6 +100,11 @@ class ChunkPacker:
             slots[q:q + n] = (own_pages[j // P] * P + j % P).astype(np.int32)
             row = seqs[si]
             row[0], row[1], row[2] = q, n, len(s.reads) + 1
+            if slots_on:
+                # continue the key's own state, else start from the last segment it reads
+                dst = self.pool.slot_of[s.own_key]
+                src = dst if s.own_start > 0 else (self.pool.slot_of[s.reads[-1][0]] if s.reads else -1)
+                state_io[si] = (src, dst)
             for i, (key, ln) in enumerate(s.reads):
                 npg = -(-ln // P)
                 ck = (key, npg)
@@ -124,7 +133,7 @@ class ChunkPacker:
         pl = np.asarray(page_list, dtype=np.int32)
         fr = np.asarray(final_rows, dtype=np.int32)
         ds = np.asarray(dseqs, dtype=np.int32)
-        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr, ds]
+        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr, ds, state_io.reshape(-1)]
         sizes = [p.size for p in parts]
         flat = np.concatenate(parts) if n_tok else np.zeros(0, dtype=np.int32)
         dev = self._upload(flat)
@@ -134,10 +143,10 @@ class ChunkPacker:
             views.append(dev[o:o + sz])
             o += sz
         host = {"ids": ids, "positions": pos, "slots": slots, "seqs": seqs, "tiles": tiles_a,
-                "page_list": pl, "final_rows": fr, "dseqs": ds}
+                "page_list": pl, "final_rows": fr, "dseqs": ds, "state_io": state_io}
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
-                     final_rows=views[6], dseqs=views[7], readout_tags=tags, num_seqs=len(specs), host=host,
+                     final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2), readout_tags=tags, num_seqs=len(specs), host=host,
                      upload_bytes=int(flat.nbytes), full_readout=any(s.full and s.readout for s in specs))
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:

@@ -33,6 +33,17 @@ class DecoderConfig:
     # (a model with one serves AI.SAE_FEATURES only); 0 = none
     sae_features: int = 0
     sae_keep: int = 0
+    # hybrid (Qwen3.5) decoders: per-layer kinds ("gdn" = Gated DeltaNet,
+    # "attn" = gated full attention); empty = every layer is attention
+    layer_kinds: tuple = ()
+    attn_output_gate: bool = False   # attention output * sigmoid(gate), gate from q_proj
+    partial_rotary: float = 1.0      # fraction of head_dim that RoPE rotates
+    norm_offset: bool = False        # RMSNorm scales by (1 + w) (zero-centered weights)
+    gdn_key_heads: int = 0
+    gdn_value_heads: int = 0
+    gdn_key_dim: int = 0
+    gdn_value_dim: int = 0
+    conv_width: int = 0
 
     @property
     def q_dim(self) -> int:
@@ -49,6 +60,30 @@ class DecoderConfig:
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    @property
+    def is_hybrid(self) -> bool:
+        return any(k == "gdn" for k in self.layer_kinds)
+
+    def kind(self, i: int) -> str:
+        return self.layer_kinds[i] if self.layer_kinds else "attn"
+
+    @property
+    def attn_layers(self) -> list:
+        """Indices of the layers with a KV cache."""
+        return [i for i in range(self.layers) if self.kind(i) == "attn"]
+
+    @property
+    def gdn_layers(self) -> list:
+        return [i for i in range(self.layers) if self.kind(i) == "gdn"]
+
+    @property
+    def gdn_conv_dim(self) -> int:
+        return 2 * self.gdn_key_heads * self.gdn_key_dim + self.gdn_value_heads * self.gdn_value_dim
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary)
 
     @property
     def has_sae(self) -> bool:
@@ -105,8 +140,22 @@ QWEN3_SAE_TINY = QWEN3_TINY.with_(name="qwen3-sae-tiny", sae_features=512, sae_k
 QWEN3_GPU_SAE_TINY = QWEN3_GPU_TINY.with_(name="qwen3-gpu-sae-tiny", weight_dtype="bf16", sae_features=2048,
                                           sae_keep=32)
 
+# Qwen3.5 hybrid: three Gated DeltaNet layers per gated full-attention layer
+# (the reference spec quail/specs/data/models/qwen3.5-4b-bf16.toml)
+_Q35_KINDS = ("gdn", "gdn", "gdn", "attn")
+QWEN35_4B = DecoderConfig(name="qwen3.5-4b", layers=32, hidden=2560, num_q_heads=16, num_kv_heads=4,
+                          head_dim=256, intermediate=9216, vocab=248_320, rope_theta=10_000_000.0,
+                          tied_head=True, weight_dtype="bf16", layer_kinds=_Q35_KINDS * 8,
+                          attn_output_gate=True, partial_rotary=0.25, norm_offset=True, gdn_key_heads=16,
+                          gdn_value_heads=32, gdn_key_dim=128, gdn_value_dim=128, conv_width=4,
+                          max_position=262_144)
+QWEN35_TINY = QWEN35_4B.with_(name="qwen3.5-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2,
+                              head_dim=64, intermediate=512, vocab=151_936, gdn_key_heads=2, gdn_value_heads=4,
+                              gdn_key_dim=32, gdn_value_dim=32, layer_kinds=_Q35_KINDS, max_position=40_960)
+
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
-                               QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY)}
+                               QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
+                               QWEN35_4B, QWEN35_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -121,4 +170,6 @@ MODEL_CONFIGS = {
     "qwen3-4b-sae-bf16": QWEN3_4B_SAE,
     "qwen3-sae-tiny": QWEN3_SAE_TINY,
     "qwen3-gpu-sae-tiny": QWEN3_GPU_SAE_TINY,
+    "qwen3.5-4b-bf16": QWEN35_4B,
+    "qwen3.5-tiny": QWEN35_TINY,
 }

@@ -1,0 +1,221 @@
+"""Qwen3.5 hybrid decoder: Gated DeltaNet layers and gated full attention.
+
+Layer kinds follow `DecoderConfig.layer_kinds` (three Gated DeltaNet layers per
+full-attention layer in the released models). Every layer is
+`h += mixer(norm(h)); h += SwiGLU(norm(h))` with zero-centered RMSNorms
+(scale 1 + w).
+
+Gated DeltaNet (per token t, value head h; q/k heads shared by
+gdn_value_heads / gdn_key_heads value heads):
+
+  x_qkv = causal depthwise conv (width w) over in_proj_qkv(x), then SiLU
+  q, k  = L2-normalized per head (q also scaled by d_k^-1/2); v as is
+  g     = -exp(A_log) * softplus(in_proj_a(x) + dt_bias)     (log decay)
+  beta  = sigmoid(in_proj_b(x))
+  S     = exp(g) * S;  S += beta * k (v - S^T k)^T;  o = S^T q     (S: d_k x d_v)
+  out   = out_proj(RMSNorm(o) * norm_w * silu(in_proj_z(x)))
+
+The state of a sequence (conv window of its last w-1 inputs and S per head)
+lives in the arena's state slot of its key; a sequence starts from its own
+slot when it continues its key, else from the slot of the last segment it
+reads (the shared prefix for a document, the document for a question).
+
+Gated attention: q_proj emits [q | gate] per head; q/k RMSNorm (1 + w) per
+head, RoPE on the first `rotary_dim` dims (NeoX halves), paged attention,
+output * sigmoid(gate), o_proj.
+
+Reference: the reference runs Qwen3.5 through vLLM with its own GDN phases
+and checkpoint slots (quail/backends/quail/executor/models/qwen3_5.py:36-391,
+gdn.py:27-1088); this module states the same math in fp32 PyTorch.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from quail_b200.models.config import DecoderConfig
+from quail_b200.models.weights import head_weight
+from quail_b200.ops import reference as ref
+
+
+def rmsnorm_offset(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm with zero-centered weights: x / rms(x) * (1 + w)."""
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())
+
+
+def rope_partial(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, rotary_dim: int) -> torch.Tensor:
+    """NeoX RoPE on the first `rotary_dim` dims of each head; the rest pass through."""
+    if rotary_dim == x.shape[-1]:
+        return ref.rope_neox(x, positions, cos_sin)
+    rot = ref.rope_neox(x[..., :rotary_dim], positions, cos_sin)
+    return torch.cat([rot, x[..., rotary_dim:]], dim=-1)
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor):
+    """(g, beta) per token and value head: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)."""
+    g = -torch.exp(A_log.float()) * F.softplus(a.float() + dt_bias.float())
+    return g, torch.sigmoid(b.float())
+
+
+def causal_conv(x: torch.Tensor, window: torch.Tensor, w: torch.Tensor):
+    """Depthwise causal conv of x [n, C] continuing `window` [w-1, C]; weights w [C, width].
+
+    Returns (SiLU(conv) [n, C], the new window: the last w-1 inputs)."""
+    width = w.shape[1]
+    full = torch.cat([window.to(x.dtype), x], dim=0)                 # [w-1+n, C]
+    n = x.shape[0]
+    out = torch.zeros_like(x)
+    for j in range(width):
+        out += full[j:j + n] * w[:, j]
+    return F.silu(out), full[-(width - 1):].clone()
+
+
+def delta_rule(q, k, v, g, beta, S):
+    """Gated delta rule over n tokens. q, k [n, Hv, dk] (normalized, q scaled), v [n, Hv, dv],
+    g, beta [n, Hv], S [Hv, dk, dv] (updated in place). Returns o [n, Hv, dv]."""
+    n = q.shape[0]
+    out = torch.empty(n, v.shape[1], v.shape[2], dtype=S.dtype, device=S.device)
+    for t in range(n):
+        S.mul_(torch.exp(g[t])[:, None, None])
+        kv = torch.einsum("hk,hkv->hv", k[t], S)
+        delta = (v[t] - kv) * beta[t][:, None]
+        S.add_(k[t][:, :, None] * delta[:, None, :])
+        out[t] = torch.einsum("hk,hkv->hv", q[t], S)
+    return out
+
+
+class Qwen35Reference:
+    """fp32 PyTorch forward of a Qwen3.5 hybrid over packed chunks (CPU or GPU).
+
+    Same contract as `Qwen3Reference`: forward_chunk(chunk, arena) returns the
+    readout rows' logits against the retained answer rows (plus argmax and
+    log-sum-exp columns for full readouts). The arena holds KV pages for the
+    attention layers (layer index -> position in cfg.attn_layers) and state
+    slots for the Gated DeltaNet layers.
+    """
+
+    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device="cpu", head_rows=None,
+                 dtype=torch.float32):
+        from quail_b200.models.weights import dequantized
+        assert cfg.is_hybrid
+        self.cfg = cfg
+        self.device = device
+        f = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
+        self.embed = f(ckpt["model.embed_tokens.weight"])
+        self.final_norm = f(ckpt["model.norm.weight"])
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            L = {"ln1": f(ckpt[p + "input_layernorm.weight"]), "ln2": f(ckpt[p + "post_attention_layernorm.weight"]),
+                 "wg": f(dequantized(ckpt, p + "mlp.gate_proj")), "wu": f(dequantized(ckpt, p + "mlp.up_proj")),
+                 "wd": f(dequantized(ckpt, p + "mlp.down_proj"))}
+            if cfg.kind(i) == "gdn":
+                q = p + "linear_attn."
+                L.update(qkv=f(dequantized(ckpt, q + "in_proj_qkv")), z=f(dequantized(ckpt, q + "in_proj_z")),
+                         b=f(dequantized(ckpt, q + "in_proj_b")), a=f(dequantized(ckpt, q + "in_proj_a")),
+                         out=f(dequantized(ckpt, q + "out_proj")), conv=f(ckpt[q + "conv1d.weight"][:, 0, :]),
+                         A_log=f(ckpt[q + "A_log"]), dt_bias=f(ckpt[q + "dt_bias"]),
+                         norm=f(ckpt[q + "norm.weight"]))
+            else:
+                q = p + "self_attn."
+                L.update(wq=f(dequantized(ckpt, q + "q_proj")), wk=f(dequantized(ckpt, q + "k_proj")),
+                         wv=f(dequantized(ckpt, q + "v_proj")), wo=f(dequantized(ckpt, q + "o_proj")),
+                         qn=f(ckpt[q + "q_norm.weight"]), kn=f(ckpt[q + "k_norm.weight"]))
+            self.layers.append(L)
+        self.head = f(head_weight(ckpt, cfg))
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.rotary_dim, cfg.rope_theta, device=device)
+        self.scale = ref.softmax_scale(cfg.head_dim)
+        self.answer_rows = None
+        if head_rows is not None:
+            self.set_answer_rows(head_rows)
+
+    def set_answer_rows(self, token_ids) -> None:
+        ids = torch.as_tensor(list(token_ids), dtype=torch.long, device=self.head.device)
+        self.answer_rows = self.head.index_select(0, ids)
+        self.answer_ids = ids.cpu()
+
+    # ------------------------------------------------------------ mixers
+    def _gdn(self, x, L, gi, chunk, arena):
+        """Gated DeltaNet layer gi (index among the GDN layers) over every sequence of the chunk."""
+        cfg = self.cfg
+        Hk, Hv, dk, dv = cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim
+        conv_s, ssm_s = arena.states["conv"], arena.states["ssm"]
+        mixed = x @ L["qkv"].t()
+        z = x @ L["z"].t()
+        g, beta = gdn_gates(x @ L["a"].t(), x @ L["b"].t(), L["A_log"], L["dt_bias"])
+        out = torch.empty(x.shape[0], Hv * dv, dtype=x.dtype, device=x.device)
+        seqs = chunk.seqs.cpu() if chunk.seqs.is_cuda else chunk.seqs
+        sio = chunk.state_io.cpu() if chunk.state_io.is_cuda else chunk.state_io
+        for s in range(seqs.shape[0]):
+            q0, n = int(seqs[s, 0]), int(seqs[s, 1])
+            src, dst = int(sio[s, 0]), int(sio[s, 1])
+            if src >= 0:
+                window, S = conv_s[src, gi].clone(), ssm_s[src, gi].clone()
+            else:
+                window = torch.zeros_like(conv_s[0, gi])
+                S = torch.zeros_like(ssm_s[0, gi])
+            c, window = causal_conv(mixed[q0:q0 + n], window, L["conv"])
+            qq = c[:, :Hk * dk].view(n, Hk, dk)
+            kk = c[:, Hk * dk:2 * Hk * dk].view(n, Hk, dk)
+            vv = c[:, 2 * Hk * dk:].view(n, Hv, dv)
+            qq = F.normalize(qq.float(), dim=-1) * dk ** -0.5
+            kk = F.normalize(kk.float(), dim=-1)
+            rep = Hv // Hk
+            qq, kk = qq.repeat_interleave(rep, 1), kk.repeat_interleave(rep, 1)
+            o = delta_rule(qq, kk, vv.float(), g[q0:q0 + n], beta[q0:q0 + n], S)
+            conv_s[dst, gi] = window.float()
+            ssm_s[dst, gi] = S
+            o = ref.rmsnorm(o, L["norm"], cfg.rms_eps) * F.silu(z[q0:q0 + n].view(n, Hv, dv).float())
+            out[q0:q0 + n] = o.reshape(n, Hv * dv).to(out.dtype)
+        return out @ L["out"].t()
+
+    def _attn(self, x, L, ai, chunk, arena):
+        """Gated full attention; ai = the layer's index among the attention layers (its KV pages)."""
+        cfg = self.cfg
+        T = x.shape[0]
+        QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+        kc, vc = arena.layer(ai)
+        qg = (x @ L["wq"].t()).view(T, QH, 2 * D if cfg.attn_output_gate else D)
+        q, gate = (qg[..., :D], qg[..., D:]) if cfg.attn_output_gate else (qg, None)
+        k = (x @ L["wk"].t()).view(T, KH, D)
+        v = (x @ L["wv"].t()).view(T, KH, D)
+        q = rope_partial(rmsnorm_offset(q, L["qn"], cfg.rms_eps), chunk.positions, self.cos_sin, cfg.rotary_dim)
+        k = rope_partial(rmsnorm_offset(k, L["kn"], cfg.rms_eps), chunk.positions, self.cos_sin, cfg.rotary_dim)
+        ok = chunk.slots >= 0
+        slots = chunk.slots[ok].long()
+        kc.view(-1, KH, D)[slots] = k[ok].to(kc.dtype)
+        vc.view(-1, KH, D)[slots] = v[ok].to(vc.dtype)
+        o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(x.dtype)
+        if gate is not None:
+            o = o.view(T, QH, D) * torch.sigmoid(gate.float())
+        return o.reshape(T, QH * D) @ L["wo"].t()
+
+    # ------------------------------------------------------------ forward
+    @torch.no_grad()
+    def hidden_chunk(self, chunk, arena) -> torch.Tensor:
+        cfg = self.cfg
+        h = self.embed[chunk.ids.long()]
+        gi = ai = 0
+        for i, L in enumerate(self.layers):
+            x = rmsnorm_offset(h, L["ln1"], cfg.rms_eps)
+            if cfg.kind(i) == "gdn":
+                h = h + self._gdn(x, L, gi, chunk, arena)
+                gi += 1
+            else:
+                h = h + self._attn(x, L, ai, chunk, arena)
+                ai += 1
+            x = rmsnorm_offset(h, L["ln2"], cfg.rms_eps)
+            h = h + ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t()
+        return h
+
+    @torch.no_grad()
+    def forward_chunk(self, chunk, arena) -> torch.Tensor:
+        h = self.hidden_chunk(chunk, arena)
+        normed = rmsnorm_offset(h[chunk.final_rows.long()], self.final_norm, self.cfg.rms_eps)
+        ans = (normed @ self.answer_rows.t()).float()
+        if not getattr(chunk, "full_readout", False):
+            return ans
+        full = (normed @ self.head.t()).float()
+        return torch.cat([ans, full.argmax(dim=1).float()[:, None], torch.logsumexp(full, dim=1)[:, None]], dim=1)

@@ -29,7 +29,8 @@ def layer_prefix(i: int) -> str:
 def projection_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
     H = cfg.hidden
     return {
-        "self_attn.q_proj": (cfg.q_dim, H),
+        # with an output gate, q_proj emits [q_h | gate_h] per head
+        "self_attn.q_proj": (cfg.q_dim * (2 if cfg.attn_output_gate else 1), H),
         "self_attn.k_proj": (cfg.kv_dim, H),
         "self_attn.v_proj": (cfg.kv_dim, H),
         "self_attn.o_proj": (H, cfg.q_dim),
@@ -56,19 +57,33 @@ def _emit_proj(name, shape, cfg, gen, device, dtype):
     return {name + ".weight": w.to(dtype)}
 
 
+def gdn_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
+    """Projections of a Gated DeltaNet layer (HF Qwen3.5 names under linear_attn.)."""
+    H = cfg.hidden
+    kd, vd = cfg.gdn_key_heads * cfg.gdn_key_dim, cfg.gdn_value_heads * cfg.gdn_value_dim
+    return {"linear_attn.in_proj_qkv": (2 * kd + vd, H), "linear_attn.in_proj_z": (vd, H),
+            "linear_attn.in_proj_b": (cfg.gdn_value_heads, H), "linear_attn.in_proj_a": (cfg.gdn_value_heads, H),
+            "linear_attn.out_proj": (H, vd)}
+
+
 def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="cpu",
                       dtype=torch.bfloat16, experts: range | None = None) -> Iterator[tuple[str, torch.Tensor]]:
     """Tensors of layer i in checkpoint names (fp8 projections quantized)."""
     p = layer_prefix(i)
     H = cfg.hidden
-    one = torch.ones(H, device=device, dtype=dtype)
+    # zero-centered norms (scale 1 + w) start at 0; plain ones at 1
+    base = torch.zeros if cfg.norm_offset else torch.ones
+    one = base(H, device=device, dtype=dtype)
     yield p + "input_layernorm.weight", one.clone()
     yield p + "post_attention_layernorm.weight", one.clone()
-    yield p + "self_attn.q_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
-    yield p + "self_attn.k_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
     shapes = projection_shapes(cfg)
-    for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj"):
-        yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
+    if cfg.kind(i) == "gdn":
+        yield from _iter_gdn(cfg, p, gen, device, dtype)
+    else:
+        yield p + "self_attn.q_norm.weight", base(cfg.head_dim, device=device, dtype=dtype)
+        yield p + "self_attn.k_norm.weight", base(cfg.head_dim, device=device, dtype=dtype)
+        for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj"):
+            yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
     if cfg.is_moe:
         # router logits ~ N(0, 1) per token: gate weight std 1/sqrt(H) on unit-RMS rows
         yield p + "mlp.gate.weight", _rand((cfg.num_experts, H), H ** -0.5, gen, device, dtype)
@@ -80,6 +95,22 @@ def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="
             yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
 
 
+def _iter_gdn(cfg: DecoderConfig, p: str, gen: torch.Generator, device, dtype):
+    """A Gated DeltaNet layer: projections, depthwise conv, decay (A_log, dt_bias), gated-norm weight."""
+    Hv = cfg.gdn_value_heads
+    for name, shape in gdn_shapes(cfg).items():
+        yield from _emit_proj(p + name, shape, cfg, gen, device, dtype).items()
+    yield p + "linear_attn.conv1d.weight", _rand((cfg.gdn_conv_dim, 1, cfg.conv_width), 0.3, gen, device, dtype)
+    # per-head decay rate A in [1, 16] and step dt in [1e-3, 1e-1] (softplus(dt_bias) = dt)
+    a = 1.0 + 15.0 * torch.rand(Hv, generator=gen, device=device)
+    dt = torch.exp(torch.rand(Hv, generator=gen, device=device) * (torch.log(torch.tensor(0.1)) -
+                                                                    torch.log(torch.tensor(1e-3))).item()
+                   + torch.log(torch.tensor(1e-3)).item())
+    yield p + "linear_attn.A_log", torch.log(a).float()
+    yield p + "linear_attn.dt_bias", (dt + torch.log(-torch.expm1(-dt))).float()
+    yield p + "linear_attn.norm.weight", torch.ones(cfg.gdn_value_dim, device=device, dtype=dtype)
+
+
 def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
                       layers: range | None = None) -> dict[str, torch.Tensor]:
     """A whole random-init checkpoint dict in HF names."""
@@ -88,7 +119,8 @@ def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=tor
     out["model.embed_tokens.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     for i in (layers if layers is not None else range(cfg.layers)):
         out.update(iter_random_layer(cfg, i, gen, device, dtype))
-    out["model.norm.weight"] = torch.ones(cfg.hidden, device=device, dtype=dtype)
+    out["model.norm.weight"] = (torch.zeros if cfg.norm_offset else torch.ones)(cfg.hidden, device=device,
+                                                                               dtype=dtype)
     if not cfg.tied_head:
         out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     out.update(random_sae(cfg, gen, device))

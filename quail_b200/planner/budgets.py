@@ -71,11 +71,24 @@ class Budgets:
             chunk //= 2
         return cls(cfg, dev, chunk, gpus)
 
+    def state_slots(self, cfg) -> int:
+        """Recurrent-state slots of a hybrid model: one per resident key (prefix, documents,
+        questions in flight), bounded by a tenth of device memory (fp32 conv window + delta-rule
+        state of every Gated DeltaNet layer per slot)."""
+        if not cfg.is_hybrid:
+            return 0
+        per = len(cfg.gdn_layers) * 4 * ((cfg.conv_width - 1) * cfg.gdn_conv_dim
+                                         + cfg.gdn_value_heads * cfg.gdn_key_dim * cfg.gdn_value_dim)
+        cap = int(self.device.mem_bytes * 0.1 // per)
+        if self.device.name == "cpu":
+            cap = min(cap, 256)
+        return max(16, min(cap, 4096))
+
     def arena_pages(self, page_tokens: int) -> int:
         cfg = self.cfg
         free = (self.device.mem_bytes * POOL_FRACTION - weight_bytes(cfg)
                 - ACT_RESERVE_CHUNKS * self.chunk_tokens * activation_bytes_per_token(cfg))
-        page_bytes = cfg.layers * 2 * page_tokens * cfg.kv_dim * 2
+        page_bytes = len(cfg.attn_layers) * 2 * page_tokens * cfg.kv_dim * 2
         if self.device.name == "cpu":
             free = min(free, 2 << 30)
         pages = int(free // page_bytes)
