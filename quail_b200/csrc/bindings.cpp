@@ -74,6 +74,19 @@ void decode_attention(const torch::Tensor& q, const torch::Tensor& k_cache, cons
                       const torch::Tensor& seqs, const torch::Tensor& dseqs, const torch::Tensor& page_list,
                       double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
 void sae_topk(const torch::Tensor& pre, const torch::Tensor& bias, int64_t keep, torch::Tensor& out);
+void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torch::Tensor& A_log,
+               const torch::Tensor& dt_bias, const torch::Tensor& norm_w, const torch::Tensor& seqs,
+               const torch::Tensor& state_io, torch::Tensor& conv_state, torch::Tensor& ssm_state, int64_t gi,
+               int64_t Hk, int64_t Hv, int64_t DK, int64_t DV, double eps, torch::Tensor& conv_out,
+               torch::Tensor& o, torch::Tensor& y);
+void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
+                     const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& dseqs,
+                     const torch::Tensor& page_list, double softmax_scale, torch::Tensor& out,
+                     const c10::optional<torch::Tensor>& gate, int64_t gate_hstride);
+void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated, const torch::Tensor& positions,
+                       const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
+                       const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
+                       torch::Tensor& q_out, double eps);
 
 static std::mutex g_err_mu;
 static int* g_err[64] = {nullptr};
@@ -122,6 +135,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention_tc", &qb::prefill_attention_tc, "tcgen05/TMEM packed-prompt prefill attention");
   m.def("decode_attention", &qb::decode_attention, "split-KV decode attention, all q heads of a KV head per CTA");
   m.def("sae_topk", &qb::sae_topk, "SAE features: bias + per-row top-k (radix select), packed indices + strengths");
+  m.def("gdn_layer", &qb::gdn_layer, "Gated DeltaNet: causal conv + L2 norm, delta-rule recurrence, gated RMSNorm");
+  m.def("small_attention", &qb::small_attention, "paged attention for any head_dim <= 256, optional sigmoid gate");
+  m.def("hybrid_qk_rope_kv", &qb::hybrid_qk_rope_kv, "q/k RMSNorm + partial RoPE + KV write of gated attention");
   m.def("read_and_clear_error", &qb::read_and_clear_error);
   m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");
   m.def("tp_gemm_rs", &qb::tp_gemm_rs, "MX GEMM -> reduce-scatter fused: epilogue pushes tiles to owner ranks");

@@ -152,10 +152,15 @@ QWEN35_4B = DecoderConfig(name="qwen3.5-4b", layers=32, hidden=2560, num_q_heads
 QWEN35_TINY = QWEN35_4B.with_(name="qwen3.5-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2,
                               head_dim=64, intermediate=512, vocab=151_936, gdn_key_heads=2, gdn_value_heads=4,
                               gdn_key_dim=32, gdn_value_dim=32, layer_kinds=_Q35_KINDS, max_position=40_960)
+# the smallest hybrid the GPU kernels take: head_dim 256 attention (2 q heads per KV
+# head), 128-dim Gated DeltaNet heads (2 key, 4 value heads)
+QWEN35_GPU_TINY = QWEN35_4B.with_(name="qwen3.5-gpu-tiny", layers=4, hidden=1024, num_q_heads=4, num_kv_heads=2,
+                                  intermediate=1024, vocab=4096, gdn_key_heads=2, gdn_value_heads=4,
+                                  layer_kinds=_Q35_KINDS, max_position=8192)
 
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
-                               QWEN35_4B, QWEN35_TINY)}
+                               QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -172,4 +177,5 @@ MODEL_CONFIGS = {
     "qwen3-gpu-sae-tiny": QWEN3_GPU_SAE_TINY,
     "qwen3.5-4b-bf16": QWEN35_4B,
     "qwen3.5-tiny": QWEN35_TINY,
+    "qwen3.5-gpu-tiny": QWEN35_GPU_TINY,
 }

@@ -1,0 +1,153 @@
+"""Qwen3.5 hybrid decoder on the sm_100a kernels (bf16 weights).
+
+Per layer, on our kernels:
+  RMSNorm (bf16 out) ->
+    Gated DeltaNet: in-projection GEMM [qkv | z | b | a] -> gdn_layer (causal
+      conv + L2 norm, delta-rule recurrence over the state slots, gated RMSNorm)
+      -> out_proj GEMM (+ residual)
+    gated attention: q|gate|k|v GEMM -> q/k norm + partial RoPE + KV write ->
+      small-tile paged attention with the sigmoid gate -> o_proj GEMM (+ residual)
+  -> RMSNorm -> gate_up GEMM (+ SwiGLU) -> down GEMM (+ residual)
+then the final norm and the readout. The zero-centered norms (scale 1 + w)
+are folded into the weights at load.
+
+Reference: quail/backends/quail/executor/models/qwen3_5.py:36-391 (the
+reference's Qwen3.5 pipeline over vLLM modules).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from quail_b200.models.config import DecoderConfig
+from quail_b200.models.weights import dequantized, head_weight
+from quail_b200.ops import reference as ref
+
+
+def _pad_rows(w: torch.Tensor, multiple: int = 16) -> torch.Tensor:
+    n = w.shape[0]
+    m = -(-n // multiple) * multiple
+    if m == n:
+        return w.contiguous()
+    out = torch.zeros(m, w.shape[1], dtype=w.dtype, device=w.device)
+    out[:n] = w
+    return out
+
+
+class Qwen35Pipeline:
+    """Forward pass of a packed chunk of a Qwen3.5 hybrid on the GPU kernels."""
+
+    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None):
+        from quail_b200.ops.quant import interleave_gate_up
+        assert cfg.is_hybrid
+        self.cfg = cfg
+        self.device = device
+        bf = torch.bfloat16
+        dev = device
+        off = 1.0 if cfg.norm_offset else 0.0
+
+        def norm_w(t):
+            return (t.float() + off).to(device=dev, dtype=bf)
+
+        def proj(name):
+            return dequantized(ckpt, name).to(device=dev, dtype=bf)
+
+        self.embed = ckpt["model.embed_tokens.weight"].to(device=dev, dtype=bf).contiguous()
+        self.final_norm = norm_w(ckpt["model.norm.weight"])
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            L = {"ln1": norm_w(ckpt[p + "input_layernorm.weight"]),
+                 "ln2": norm_w(ckpt[p + "post_attention_layernorm.weight"])}
+            if cfg.kind(i) == "gdn":
+                q = p + "linear_attn."
+                L["win"] = _pad_rows(torch.cat([proj(q + "in_proj_qkv"), proj(q + "in_proj_z"),
+                                                proj(q + "in_proj_b"), proj(q + "in_proj_a")]))
+                L["wout"] = proj(q + "out_proj").contiguous()
+                L["conv"] = ckpt[q + "conv1d.weight"][:, 0, :].to(device=dev, dtype=torch.float32).contiguous()
+                L["A_log"] = ckpt[q + "A_log"].to(device=dev, dtype=torch.float32).contiguous()
+                L["dt_bias"] = ckpt[q + "dt_bias"].to(device=dev, dtype=torch.float32).contiguous()
+                L["norm"] = ckpt[q + "norm.weight"].to(device=dev, dtype=bf).contiguous()
+            else:
+                q = p + "self_attn."
+                L["wqkv"] = _pad_rows(torch.cat([proj(q + "q_proj"), proj(q + "k_proj"), proj(q + "v_proj")]))
+                L["wo"] = proj(q + "o_proj").contiguous()
+                L["qn"] = ckpt[q + "q_norm.weight"].to(device=dev, dtype=bf).contiguous()
+                L["kn"] = ckpt[q + "k_norm.weight"].to(device=dev, dtype=bf).contiguous()
+            gu = torch.cat([proj(p + "mlp.gate_proj"), proj(p + "mlp.up_proj")])
+            L["wgu"] = interleave_gate_up(gu)
+            L["wd"] = proj(p + "mlp.down_proj").contiguous()
+            self.layers.append(L)
+        self.head = head_weight(ckpt, cfg)
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.rotary_dim, cfg.rope_theta, device=dev)
+        self.scale = ref.softmax_scale(cfg.head_dim)
+        self.answer_rows = None
+        if head_rows is not None:
+            self.set_answer_rows(head_rows)
+
+    def set_answer_rows(self, token_ids) -> None:
+        ids = torch.as_tensor(list(token_ids), dtype=torch.long)
+        self.answer_rows = self.head.index_select(0, ids.to(self.head.device)).to(
+            device=self.device, dtype=torch.bfloat16).contiguous()
+        self.answer_ids = ids
+
+    def head_bf16(self) -> torch.Tensor:
+        if getattr(self, "_head_dev", None) is None:
+            self._head_dev = self.head.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        return self._head_dev
+
+    @torch.no_grad()
+    def forward_hidden(self, chunk, arena) -> torch.Tensor:
+        from quail_b200 import ops
+        C = ops.native()
+        cfg = self.cfg
+        T = chunk.num_tokens
+        dev = self.device
+        QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
+        Hk, Hv, dk, dv = cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim
+        h = ops.embed_gather(chunk.ids, self.embed)
+        gi = ai = 0
+        for i, L in enumerate(self.layers):
+            x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
+            if cfg.kind(i) == "gdn":
+                p = ops.gemm(x, L["win"])
+                conv_out = torch.empty(T, cfg.gdn_conv_dim, dtype=torch.float32, device=dev)
+                o = torch.empty(T, Hv * dv, dtype=torch.float32, device=dev)
+                y = torch.empty(T, Hv * dv, dtype=torch.bfloat16, device=dev)
+                ops.count_launch(3)
+                C.gdn_layer(p, L["conv"], L["A_log"], L["dt_bias"], L["norm"], chunk.seqs, chunk.state_io,
+                            arena.states["conv"], arena.states["ssm"], gi, Hk, Hv, dk, dv, cfg.rms_eps, conv_out, o, y)
+                ops.gemm(y, L["wout"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                gi += 1
+            else:
+                p = ops.gemm(x, L["wqkv"])
+                kc, vc = arena.layer(ai)
+                q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=dev)
+                ops.count_launch(1)
+                C.hybrid_qk_rope_kv(p, QH, KH, cfg.attn_output_gate, chunk.positions, L["qn"], L["kn"],
+                                    cfg.norm_offset, self.cos_sin, chunk.slots, kc, vc, q, cfg.rms_eps)
+                o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=dev)
+                gate = p[:, D:] if cfg.attn_output_gate else None
+                ops.count_launch(int(chunk.tiles.shape[0] > 0) + int(chunk.dseqs.numel() > 0))
+                C.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
+                                  gate, 2 * D)
+                ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                ai += 1
+            x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+            a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
+            ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+        return h
+
+    @torch.no_grad()
+    def forward_chunk(self, chunk, arena) -> torch.Tensor:
+        from quail_b200 import ops
+        cfg = self.cfg
+        h = self.forward_hidden(chunk, arena)
+        if not getattr(chunk, "full_readout", False):
+            return ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows)
+        R = chunk.final_rows.numel()
+        normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
+        ans = ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows,
+                                     normed=normed)
+        arg, lse = ops.row_argmax_lse(ops.gemm(normed, self.head_bf16()))
+        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)

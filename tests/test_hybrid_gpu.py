@@ -1,0 +1,165 @@
+"""Hybrid (Qwen3.5) kernels and pipeline against their fp32 PyTorch statements."""
+
+import numpy as np
+import pytest
+import torch
+
+from quail_b200 import ops
+from quail_b200.models import qwen3_5 as Q
+from quail_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _no_kernel_errors():
+    torch.manual_seed(0)
+    yield
+    assert ops.read_and_clear_error(0) == 0
+
+
+def _seqs(lengths, q_lens, P, KH, D, pages=1024):
+    """One own segment per sequence (plus a shared 48-token prefix segment when lengths[i] > q_lens[i])."""
+    from test_kernels_gpu import _segmented_case
+    specs = []
+    for n, q in zip(lengths, q_lens):
+        specs.append((q, [48, n]) if n != q else (q, [n]))
+    return _segmented_case(P, specs, QH=KH * 1, KH=KH, D=D, pages=pages)
+
+
+@pytest.mark.parametrize("D,QH,KH", [(256, 4, 2), (256, 16, 4), (64, 8, 2), (128, 16, 4)])
+def test_small_attention_with_gate(D, QH, KH):
+    from test_kernels_gpu import _segmented_case
+    specs = [(100, [48, 100]), (1, [48, 300, 65]), (7, [48, 7]), (1, [17]), (40, [48, 200, 40]), (130, [130])]
+    q, kc, vc, seqs, pl = _segmented_case(16, specs, QH=QH, KH=KH, D=D, pages=2048)
+    scale = ref.softmax_scale(D)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale).view(-1, QH, D)
+    T = q.shape[0]
+    gate_src = torch.randn(T, QH, 2 * D, device=DEV).bfloat16()
+    tiles = ref.attention_tiles(seqs)
+    one = [i for i, (n, _) in enumerate(specs) if n == 1]
+    tiles = torch.tensor([t for t in tiles.tolist() if t[0] not in one], dtype=torch.int32, device=DEV)
+    dseqs = torch.tensor(one, dtype=torch.int32, device=DEV)
+    out = torch.empty(T, QH * D, dtype=torch.bfloat16, device=DEV)
+    gate = gate_src.view(T, QH * 2 * D)[:, D:]
+    ops.native().small_attention(q, kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out, gate, 2 * D)
+    want_g = want * torch.sigmoid(gate_src[:, :, D:].float())
+    assert rel_err(out.view(T, QH, D), want_g) < 1e-2
+    out2 = torch.empty_like(out)
+    ops.native().small_attention(q, kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out2, None, 0)
+    assert rel_err(out2.view(T, QH, D), want) < 1e-2
+
+
+def test_hybrid_qk_rope_kv():
+    T, QH, KH, D, rd = 37, 4, 2, 256, 64
+    proj = torch.randn(T, QH * 2 * D + 2 * KH * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    qw = (0.1 * torch.randn(D, device=DEV)).bfloat16()
+    kw = (0.1 * torch.randn(D, device=DEV)).bfloat16()
+    cs = ref.rope_cos_sin(8192, rd, 1e7, device=DEV)
+    kc = torch.zeros(8, 16, KH, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(128, device=DEV)[:T].int()
+    slots[3] = -1
+    q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=DEV)
+    ops.native().hybrid_qk_rope_kv(proj, QH, KH, True, pos, qw, kw, True, cs, slots, kc, vc, q, 1e-6)
+    qg = proj[:, :QH * 2 * D].view(T, QH, 2 * D)
+    want_q = Q.rope_partial(Q.rmsnorm_offset(qg[..., :D], qw, 1e-6), pos, cs, rd)
+    assert rel_err(q, want_q) < 1e-2
+    k = proj[:, QH * 2 * D:QH * 2 * D + KH * D].view(T, KH, D)
+    v = proj[:, QH * 2 * D + KH * D:].view(T, KH, D)
+    want_k = Q.rope_partial(Q.rmsnorm_offset(k, kw, 1e-6), pos, cs, rd)
+    ok = slots >= 0
+    assert rel_err(kc.view(-1, KH, D)[slots[ok].long()], want_k[ok]) < 1e-2
+    assert torch.equal(vc.view(-1, KH, D)[slots[ok].long()], v[ok])
+
+
+@pytest.mark.parametrize("dk", [128, 64])
+def test_gdn_layer_against_recurrence(dk):
+    Hk, Hv, dv, W = 2, 4, dk, 4
+    C = 2 * Hk * dk + Hv * dv
+    lens = [5, 1, 70, 33]
+    T = sum(lens)
+    G, slots = 3, 8
+    gi = 1
+    proj = (torch.randn(T, C + Hv * dv + 2 * Hv, device=DEV) * 0.5).bfloat16()
+    conv_w = torch.randn(C, W, device=DEV) * 0.3
+    A_log = torch.log(1 + 15 * torch.rand(Hv, device=DEV))
+    dt_bias = torch.randn(Hv, device=DEV) - 3
+    norm_w = (1 + 0.1 * torch.randn(dv, device=DEV)).bfloat16()
+    seqs = torch.zeros(len(lens), 12, dtype=torch.int32)
+    q0 = 0
+    for i, n in enumerate(lens):
+        seqs[i, 0], seqs[i, 1], seqs[i, 2], seqs[i, 4] = q0, n, 1, n
+        q0 += n
+    sio = torch.tensor([[-1, 0], [2, 1], [3, 3], [-1, 4]], dtype=torch.int32)   # fresh, from a slot, continue
+    conv_state = torch.randn(slots, G, W - 1, C, device=DEV)
+    ssm_state = torch.randn(slots, G, Hv, dk, dv, device=DEV) * 0.1
+    cs0, ss0 = conv_state.clone(), ssm_state.clone()
+    conv_out = torch.empty(T, C, device=DEV)
+    o = torch.empty(T, Hv * dv, device=DEV)
+    y = torch.empty(T, Hv * dv, dtype=torch.bfloat16, device=DEV)
+    ops.native().gdn_layer(proj, conv_w, A_log, dt_bias, norm_w, seqs.to(DEV), sio.to(DEV), conv_state, ssm_state,
+                           gi, Hk, Hv, dk, dv, 1e-6, conv_out, o, y)
+    pf = proj.float()
+    g, beta = Q.gdn_gates(pf[:, C + Hv * dv + Hv:C + Hv * dv + 2 * Hv], pf[:, C + Hv * dv:C + Hv * dv + Hv],
+                          A_log, dt_bias)
+    for i, n in enumerate(lens):
+        a = int(seqs[i, 0])
+        src, dst = sio[i].tolist()
+        win = cs0[src, gi].clone() if src >= 0 else torch.zeros(W - 1, C, device=DEV)
+        S = ss0[src, gi].clone() if src >= 0 else torch.zeros(Hv, dk, dv, device=DEV)
+        c, win = Q.causal_conv(pf[a:a + n, :C], win, conv_w)
+        qq = torch.nn.functional.normalize(c[:, :Hk * dk].view(n, Hk, dk), dim=-1) * dk ** -0.5
+        kk = torch.nn.functional.normalize(c[:, Hk * dk:2 * Hk * dk].view(n, Hk, dk), dim=-1)
+        vv = c[:, 2 * Hk * dk:].view(n, Hv, dv)
+        rep = Hv // Hk
+        out = Q.delta_rule(qq.repeat_interleave(rep, 1), kk.repeat_interleave(rep, 1), vv, g[a:a + n],
+                           beta[a:a + n], S)
+        assert rel_err(o[a:a + n].view(n, Hv, dv), out) < 1e-3, i
+        assert rel_err(conv_state[dst, gi], win) < 1e-5
+        assert rel_err(ssm_state[dst, gi], S) < 1e-3
+        z = pf[a:a + n, C:C + Hv * dv].view(n, Hv, dv)
+        want_y = ref.rmsnorm(out, norm_w, 1e-6) * torch.nn.functional.silu(z)
+        assert rel_err(y[a:a + n].view(n, Hv, dv), want_y) < 1e-2
+
+
+def test_hybrid_pipeline_matches_fp32_model():
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.engine.stage_executor import StageExecutor, Task
+    from quail_b200.models.config import QWEN35_GPU_TINY
+    from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
+    from quail_b200.models.weights import random_checkpoint
+    cfg = QWEN35_GPU_TINY
+    ckpt = random_checkpoint(cfg, seed=9, device=DEV)
+    ids = list(range(16))
+    pipe = Qwen35Pipeline(cfg, ckpt, DEV, head_rows=ids)
+    exact = Q.Qwen35Reference(cfg, ckpt, device=DEV, head_rows=ids)
+
+    def run(model, dtype):
+        arena = KVArena.for_model(cfg, 128, 16, device=DEV, dtype=dtype, state_slots=32)
+        ex = StageExecutor(model, arena, 256, min_piece=16)
+        got = {}
+        rng = np.random.default_rng(0)
+        prefix = rng.integers(0, 4096, 48).astype(np.int32)
+        docs = [rng.integers(0, 4096, n).astype(np.int32) for n in (10, 200, 64, 300)]
+        suffix = rng.integers(0, 4096, 12).astype(np.int32)
+        ex.submit(Task(key="p", tokens=prefix, pos_start=0, free_after=False))
+        for i, d in enumerate(docs):
+            ex.submit(Task(key=i, tokens=np.concatenate([d, suffix]), pos_start=48, reads=[("p", 48)], readout=True,
+                           on_done=lambda t, row, i=i: got.__setitem__(i, row.float().cpu())))
+        ex.run()
+        return torch.stack([got[i] for i in range(len(docs))])
+
+    got = run(pipe, torch.bfloat16)
+    want = run(exact, torch.float32)
+    assert ops.read_and_clear_error(0) == 0
+    d = rel_err(got, want)
+    print(f"hybrid kernel-vs-fp32: {d:.4f}")
+    assert d < 0.1
