@@ -83,7 +83,7 @@ def main():
 
     cfg = MODEL_CONFIGS[args.model]
     pipe = build_pipeline(cfg, device=dev, seed=0)
-    arena = KVArena(cfg.layers, args.pages, 128, cfg.num_kv_heads, cfg.head_dim, device=dev)
+    arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=1024)
     nt = len(SYNTHETIC_TRUE_IDS)
     call = lambda suffix: Call(kind="filter", suffix=suffix, true_cols=list(range(nt)),  # noqa: E731
                                false_cols=list(range(nt, 2 * nt)), name="if")

@@ -183,7 +183,7 @@ def run_filter_query(pipe, arena, workload, *, chunk_tokens: int = 16384, name: 
     from quail_b200.engine.region import Call, RegionRun
     from quail_b200.engine.stage_executor import StageExecutor
 
-    rows = pipe.w.answer_rows.shape[0]
+    rows = getattr(pipe, "w", pipe).answer_rows.shape[0]
     half = rows // 2
     ex = StageExecutor(pipe, arena, chunk_tokens)
     call = Call(kind="filter", suffix=workload.suffix, true_cols=list(range(half)),

@@ -34,6 +34,12 @@ def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
                    answer_ids=SYNTHETIC_TRUE_IDS + SYNTHETIC_FALSE_IDS):
     if ckpt is None:
         ckpt = random_checkpoint_on(cfg, device, seed)
+    if cfg.is_hybrid:
+        from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
+        pipe = Qwen35Pipeline(cfg, ckpt, device, head_rows=answer_ids)
+        del ckpt
+        torch.cuda.empty_cache() if torch.cuda.is_available() else None
+        return pipe
     weights = Qwen3Weights(cfg, ckpt, device, head_rows=answer_ids)
     del ckpt
     torch.cuda.empty_cache() if torch.cuda.is_available() else None

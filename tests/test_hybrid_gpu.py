@@ -163,3 +163,18 @@ def test_hybrid_pipeline_matches_fp32_model():
     d = rel_err(got, want)
     print(f"hybrid kernel-vs-fp32: {d:.4f}")
     assert d < 0.1
+
+
+def test_hybrid_session_on_gpu():
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    cfg = quail.EngineConfig(model="qwen3.5-gpu-tiny", device="b200", chunk_tokens=512)
+    t = pa.table({"id": list(range(6)), "body": ["the plot is long", "great music", "bad ending", "short story",
+                                                  "money talk", "cast list"]})
+    with quail.Session(config=cfg) as s:
+        s.register("r", quail.DocumentProvider.from_table(t, id_col="id"))
+        kept = s.sql("SELECT id FROM r WHERE AI.IF(PROMPT('Is it about music? {0}', body))").collect()
+        assert set(kept.column("id").to_pylist()) <= set(range(6))
+        out = s.sql("SELECT id, AI.MAP(body, 'Summarize', 4) AS m FROM r").collect()
+        assert out.num_rows == 6
