@@ -5,9 +5,10 @@
 //                  conv window of its source state slot; SiLU; q and k heads
 //                  L2-normalized (q also scaled by d_k^-1/2); the new window
 //                  (last W-1 inputs) written to the sequence's destination slot.
-//   gdn_recurrent  one CTA per (sequence, value head), threads 2j and 2j+1 own
-//                  column j of the d_k x d_v state S in registers (half the rows
-//                  each, partial sums combined by one shuffle): per token
+//   gdn_recurrent  per (sequence, value head, column block): a few adjacent
+//                  threads own one column j of the d_k x d_v state S in registers
+//                  (the columns evolve independently; row partial sums combine by
+//                  shuffles): per token
 //                    S = exp(g) S;  S += k (beta (v - S^T k))^T;  o = S^T q
 //                  with g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b);
 //                  the reductions run over i inside a thread pair, so a token
@@ -92,26 +93,28 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const __nv_bfloat16* __re
 // conv_out fp32 [T, C]: q at head hk*DK, k at qk/2 + hk*DK, v at qk + h*DV.
 // ab: bf16 [T, ldab] with b at column b_col + h, a at column a_col + h.
 // out: fp32 [T, Hv*DV].
-template <int DK>
-__global__ void __launch_bounds__(256) gdn_recurrent_kernel(
+template <int DK, int PARTS>
+__global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ conv_out, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
     int b_col, int a_col, const float* __restrict__ A_log, const float* __restrict__ dt_bias, int Hv, int Hk, int DV,
     const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
     float* __restrict__ out) {
-  // thread pair (2j, 2j+1) owns column j of S: rows [0, DK/2) and [DK/2, DK)
-  constexpr int HALF = DK / 2;
+  // PARTS adjacent threads own one column j of S (ROWS rows each; partial sums
+  // combined by shuffles); a CTA owns 128 / PARTS columns, blockIdx.z picks them
+  constexpr int ROWS = DK / PARTS;
+  constexpr int CPC = 128 / PARTS;
   __shared__ float sq[2][DK], sk[2][DK], sgb[2][2];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int j = tid >> 1, part = tid & 1, r0 = part * HALF;
+  const int j = blockIdx.z * CPC + tid / PARTS, part = tid % PARTS, r0 = part * ROWS;
   const int hk = h / (Hv / Hk);
   const int q0 = seqs[s * kGdnSeqInts], n = seqs[s * kGdnSeqInts + 1];
   const int src = sio[2 * s], dst = sio[2 * s + 1];
   const bool live = j < DV;
-  float S[HALF];
+  float S[ROWS];
   const size_t slot_stride = (size_t)G * Hv * DK * DV;
   const size_t head_off = ((size_t)gi * Hv + h) * DK * DV;
 #pragma unroll
-  for (int i = 0; i < HALF; ++i)
+  for (int i = 0; i < ROWS; ++i)
     S[i] = (live && src >= 0) ? ssm_state[(size_t)src * slot_stride + head_off + (size_t)(r0 + i) * DV + j] : 0.f;
   const float A = -__expf(A_log[h]);
   const float dtb = dt_bias[h];
@@ -129,6 +132,11 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(
       sgb[buf][1] = 1.f / (1.f + __expf(-b));              // beta
     }
   };
+  auto part_sum = [&](float x) {
+#pragma unroll
+    for (int o = 1; o < PARTS; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+  };
   if (n > 0) stage(0, 0);
   __syncthreads();
   for (int t = 0; t < n; ++t) {
@@ -140,29 +148,27 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(
     const float* qq = sq[buf] + r0;
     float kv0 = 0.f, kv1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < HALF; i += 2) {
+    for (int i = 0; i < ROWS; i += 2) {
       kv0 += S[i] * kk[i];
       kv1 += S[i + 1] * kk[i + 1];
     }
-    float kv = kv0 + kv1;
-    kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+    const float kv = part_sum(kv0 + kv1);
     const float delta = beta * (v - decay * kv);
     float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < HALF; i += 2) {
+    for (int i = 0; i < ROWS; i += 2) {
       S[i] = decay * S[i] + kk[i] * delta;
       S[i + 1] = decay * S[i + 1] + kk[i + 1] * delta;
       o0 += S[i] * qq[i];
       o1 += S[i + 1] * qq[i + 1];
     }
-    float o = o0 + o1;
-    o += __shfl_xor_sync(0xffffffffu, o, 1);
+    const float o = part_sum(o0 + o1);
     if (live && part == 0) out[(size_t)(q0 + t) * Hv * DV + h * DV + j] = o;
     __syncthreads();
   }
   if (live)
 #pragma unroll
-    for (int i = 0; i < HALF; ++i)
+    for (int i = 0; i < ROWS; ++i)
       ssm_state[(size_t)dst * slot_stride + head_off + (size_t)(r0 + i) * DV + j] = S[i];
 }
 
@@ -220,22 +226,21 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
                                          conv_state.data_ptr<float>(), (int)gi, G, q_scale,
                                          conv_out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  dim3 g2(S, Hv);
   const int b_col = C + Hv * DV, a_col = b_col + Hv;
-  const int threads = ((int)DV * 2 + 31) / 32 * 32;  // two threads per state column
-  TORCH_CHECK(threads <= 256, "gdn: d_v <= 128");
-#define QB_GDN_REC(DKK)                                                                                          \
-  if (DK == DKK) {                                                                                               \
-    gdn_recurrent_kernel<DKK><<<g2, threads, 0, st>>>(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),         \
-                                                      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()),  \
-                                                      ld, b_col, a_col, A_log.data_ptr<float>(),                \
+  TORCH_CHECK(DV <= 128, "gdn: d_v <= 128");
+#define QB_GDN_REC(DKK, PP)                                                                                     \
+  if (DK == DKK) {                                                                                              \
+    dim3 g2(S, Hv, ((int)DV + 128 / PP - 1) / (128 / PP));                                                      \
+    gdn_recurrent_kernel<DKK, PP><<<g2, 128, 0, st>>>(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),        \
+                                                      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), \
+                                                      ld, b_col, a_col, A_log.data_ptr<float>(),               \
                                                       dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, (int)DV, sq, \
-                                                      sio, ssm_state.data_ptr<float>(), (int)gi, G,             \
-                                                      o.data_ptr<float>());                                     \
+                                                      sio, ssm_state.data_ptr<float>(), (int)gi, G,            \
+                                                      o.data_ptr<float>());                                    \
   }
-  QB_GDN_REC(32)
-  QB_GDN_REC(64)
-  QB_GDN_REC(128)
+  QB_GDN_REC(32, 1)
+  QB_GDN_REC(64, 2)
+  QB_GDN_REC(128, 4)
 #undef QB_GDN_REC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int warps = T * (int)Hv;
