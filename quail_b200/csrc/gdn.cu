@@ -94,15 +94,16 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const __nv_bfloat16* __re
 // ab: bf16 [T, ldab] with b at column b_col + h, a at column a_col + h.
 // out: fp32 [T, Hv*DV].
 template <int DK, int PARTS>
-__global__ void __launch_bounds__(128) gdn_recurrent_kernel(
+__global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     const float* __restrict__ conv_out, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
     int b_col, int a_col, const float* __restrict__ A_log, const float* __restrict__ dt_bias, int Hv, int Hk, int DV,
     const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
     float* __restrict__ out) {
   // PARTS adjacent threads own one column j of S (ROWS rows each; partial sums
-  // combined by shuffles); a CTA owns 128 / PARTS columns, blockIdx.z picks them
+  // combined by shuffles); one CTA owns all (up to 128) columns of the head, so
+  // the per-token staging and barrier are shared by the whole state
   constexpr int ROWS = DK / PARTS;
-  constexpr int CPC = 128 / PARTS;
+  constexpr int CPC = 128;
   __shared__ float sq[2][DK], sk[2][DK], sgb[2][2];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int j = blockIdx.z * CPC + tid / PARTS, part = tid % PARTS, r0 = part * ROWS;
@@ -230,8 +231,8 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   TORCH_CHECK(DV <= 128, "gdn: d_v <= 128");
 #define QB_GDN_REC(DKK, PP)                                                                                     \
   if (DK == DKK) {                                                                                              \
-    dim3 g2(S, Hv, ((int)DV + 128 / PP - 1) / (128 / PP));                                                      \
-    gdn_recurrent_kernel<DKK, PP><<<g2, 128, 0, st>>>(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),        \
+    dim3 g2(S, Hv, 1);                                                                                           \
+    gdn_recurrent_kernel<DKK, PP><<<g2, 128 * PP, 0, st>>>(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),        \
                                                       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), \
                                                       ld, b_col, a_col, A_log.data_ptr<float>(),               \
                                                       dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, (int)DV, sq, \
@@ -240,7 +241,7 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   }
   QB_GDN_REC(32, 1)
   QB_GDN_REC(64, 2)
-  QB_GDN_REC(128, 4)
+  QB_GDN_REC(128, 2)
 #undef QB_GDN_REC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int warps = T * (int)Hv;
