@@ -97,13 +97,16 @@ class ModelEngine:
         from quail_b200.engine.stage_executor import StageExecutor
         ckpt = self._checkpoint()
         if self.cfg.is_hybrid:
-            from quail_b200.models.qwen3_5 import Qwen35Reference
+            if self.cfg.arch == "lfm2":
+                from quail_b200.models.lfm2 import Lfm2Pipeline as GpuModel, Lfm2Reference as CpuModel
+            else:
+                from quail_b200.models.qwen3_5 import Qwen35Reference as CpuModel
+                from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline as GpuModel
             if self.on_gpu:
-                from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
-                self.model = Qwen35Pipeline(self.cfg, ckpt, self.device)
+                self.model = GpuModel(self.cfg, ckpt, self.device)
                 page_tokens, dtype = 128, torch.bfloat16
             else:
-                self.model = Qwen35Reference(self.cfg, ckpt, device="cpu")
+                self.model = CpuModel(self.cfg, ckpt, device="cpu")
                 page_tokens, dtype = 16, torch.float32
             del ckpt
             n_pages = pages or self.budgets.arena_pages(page_tokens)

@@ -15,6 +15,8 @@
 //                  costs one barrier. S is read from the source slot and written
 //                  to the destination slot.
 //   gdn_gated_norm one warp per (token, value head): RMSNorm(o) * w * silu(z) -> bf16.
+//   short_conv     LFM2's gated short convolution: y = C * conv(B * x), one thread
+//                  per channel over a sequence's tokens, window in a state slot.
 //
 // The state slots are fp32: conv [slots, G, W-1, C], ssm [slots, G, Hv, d_k, d_v]
 // (G = Gated DeltaNet layers). Source slot -1 means a zero state.
@@ -192,6 +194,65 @@ __global__ void gdn_gated_norm_kernel(const float* __restrict__ o, const __nv_bf
     const float v = row[d] * r * __bfloat162float(w[d]) * (zz / (1.f + __expf(-zz)));
     y[(size_t)t * Hv * DV + h * DV + d] = __float2bfloat16(v);
   }
+}
+
+// ------------------------------------------------------------------ short conv (LFM2)
+// bcx bf16 [T, ld] = [B (H) | C (H) | x (H)]; y = C * causal_conv(B * x), no activation,
+// continuing the window (last W-1 values of B * x) of the source slot.
+template <int W>
+__global__ void __launch_bounds__(128) short_conv_kernel(const __nv_bfloat16* __restrict__ bcx, int ld, int H,
+                                                         const float* __restrict__ wconv, const int* __restrict__ seqs,
+                                                         const int* __restrict__ sio, float* __restrict__ state,
+                                                         int li, int NL, __nv_bfloat16* __restrict__ y) {
+  const int s = blockIdx.x;
+  const int c = blockIdx.y * 128 + threadIdx.x;
+  if (c >= H) return;
+  const int q0 = seqs[s * kGdnSeqInts], n = seqs[s * kGdnSeqInts + 1];
+  const int src = sio[2 * s], dst = sio[2 * s + 1];
+  float w[W], win[W - 1];
+#pragma unroll
+  for (int j = 0; j < W; ++j) w[j] = wconv[(size_t)c * W + j];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) win[j] = src >= 0 ? state[(((size_t)src * NL + li) * (W - 1) + j) * H + c] : 0.f;
+  for (int t = 0; t < n; ++t) {
+    const __nv_bfloat16* row = bcx + (size_t)(q0 + t) * ld;
+    const float bx = __bfloat162float(row[c]) * __bfloat162float(row[2 * H + c]);
+    float acc = w[W - 1] * bx;
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) acc += w[j] * win[j];
+#pragma unroll
+    for (int j = 0; j < W - 2; ++j) win[j] = win[j + 1];
+    win[W - 2] = bx;
+    y[(size_t)(q0 + t) * H + c] = __float2bfloat16(__bfloat162float(row[H + c]) * acc);
+  }
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) state[(((size_t)dst * NL + li) * (W - 1) + j) * H + c] = win[j];
+}
+
+void short_conv(const torch::Tensor& bcx, const torch::Tensor& wconv, const torch::Tensor& seqs,
+                const torch::Tensor& state_io, torch::Tensor& state, int64_t li, torch::Tensor& y) {
+  TORCH_CHECK(bcx.scalar_type() == at::kBFloat16 && bcx.stride(1) == 1, "short_conv: bf16 [T, 3H]");
+  const int H = y.size(1), W = wconv.size(1);
+  TORCH_CHECK(wconv.scalar_type() == at::kFloat && wconv.size(0) == H && state.size(3) == H && state.size(2) == W - 1,
+              "short_conv: fp32 weight [H, W], state [slots, L, W-1, H]");
+  const int S = seqs.size(0);
+  if (S == 0 || bcx.size(0) == 0) return;
+  const int dev = bcx.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  dim3 grid(S, (H + 127) / 128);
+  TORCH_CHECK(W == 3 || W == 4, "short_conv: width 3 or 4");
+  if (W == 3)
+    short_conv_kernel<3><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(bcx.data_ptr()),
+                                                (int)bcx.stride(0), H, wconv.data_ptr<float>(), seqs.data_ptr<int>(),
+                                                state_io.data_ptr<int>(), state.data_ptr<float>(), (int)li,
+                                                (int)state.size(1), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+  else
+    short_conv_kernel<4><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(bcx.data_ptr()),
+                                                (int)bcx.stride(0), H, wconv.data_ptr<float>(), seqs.data_ptr<int>(),
+                                                state_io.data_ptr<int>(), state.data_ptr<float>(), (int)li,
+                                                (int)state.size(1), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // ------------------------------------------------------------------ host side

@@ -206,9 +206,13 @@ class KVArena:
         """KV pages for the model's attention layers; state slots for its Gated DeltaNet layers."""
         shapes = None
         if cfg.is_hybrid:
+            shapes = {}
             G = len(cfg.gdn_layers)
-            shapes = {"conv": (G, cfg.conv_width - 1, cfg.gdn_conv_dim),
-                      "ssm": (G, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim)}
+            if G:
+                shapes["conv"] = (G, cfg.conv_width - 1, cfg.gdn_conv_dim)
+                shapes["ssm"] = (G, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim)
+            if cfg.conv_layers:
+                shapes["sconv"] = (len(cfg.conv_layers), cfg.conv_width - 1, cfg.hidden)
             state_slots = state_slots or 64
         return cls(len(cfg.attn_layers), num_pages, page_tokens, cfg.num_kv_heads, cfg.head_dim, device=device,
                    dtype=dtype, state_slots=state_slots if cfg.is_hybrid else 0, state_shapes=shapes)

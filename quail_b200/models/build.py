@@ -21,7 +21,9 @@ def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str,
                                         * cfg.init_std).bfloat16()
     for i in range(cfg.layers):
         out.update(iter_random_layer(cfg, i, gen, device=device, dtype=torch.bfloat16))
-    out["model.norm.weight"] = torch.ones(cfg.hidden, device=device, dtype=torch.bfloat16)
+    from quail_b200.models.weights import final_norm_name
+    out[final_norm_name(cfg)] = (torch.zeros if cfg.norm_offset else torch.ones)(cfg.hidden, device=device,
+                                                                                dtype=torch.bfloat16)
     if not cfg.tied_head:
         out["lm_head.weight"] = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device)
                                  * cfg.init_std).bfloat16()
@@ -35,8 +37,11 @@ def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
     if ckpt is None:
         ckpt = random_checkpoint_on(cfg, device, seed)
     if cfg.is_hybrid:
-        from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
-        pipe = Qwen35Pipeline(cfg, ckpt, device, head_rows=answer_ids)
+        if cfg.arch == "lfm2":
+            from quail_b200.models.lfm2 import Lfm2Pipeline as Pipe
+        else:
+            from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline as Pipe
+        pipe = Pipe(cfg, ckpt, device, head_rows=answer_ids)
         del ckpt
         torch.cuda.empty_cache() if torch.cuda.is_available() else None
         return pipe

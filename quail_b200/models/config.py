@@ -33,9 +33,11 @@ class DecoderConfig:
     # (a model with one serves AI.SAE_FEATURES only); 0 = none
     sae_features: int = 0
     sae_keep: int = 0
-    # hybrid (Qwen3.5) decoders: per-layer kinds ("gdn" = Gated DeltaNet,
-    # "attn" = gated full attention); empty = every layer is attention
+    # hybrid decoders: per-layer kinds ("gdn" = Gated DeltaNet (Qwen3.5),
+    # "conv" = gated short convolution (LFM2), "attn" = full attention);
+    # empty = every layer is attention
     layer_kinds: tuple = ()
+    arch: str = "qwen3"              # checkpoint naming: "qwen3", "qwen3_5" or "lfm2"
     attn_output_gate: bool = False   # attention output * sigmoid(gate), gate from q_proj
     partial_rotary: float = 1.0      # fraction of head_dim that RoPE rotates
     norm_offset: bool = False        # RMSNorm scales by (1 + w) (zero-centered weights)
@@ -63,7 +65,11 @@ class DecoderConfig:
 
     @property
     def is_hybrid(self) -> bool:
-        return any(k == "gdn" for k in self.layer_kinds)
+        return any(k != "attn" for k in self.layer_kinds)
+
+    @property
+    def conv_layers(self) -> list:
+        return [i for i in range(self.layers) if self.kind(i) == "conv"]
 
     def kind(self, i: int) -> str:
         return self.layer_kinds[i] if self.layer_kinds else "attn"
@@ -146,7 +152,8 @@ _Q35_KINDS = ("gdn", "gdn", "gdn", "attn")
 QWEN35_4B = DecoderConfig(name="qwen3.5-4b", layers=32, hidden=2560, num_q_heads=16, num_kv_heads=4,
                           head_dim=256, intermediate=9216, vocab=248_320, rope_theta=10_000_000.0,
                           tied_head=True, weight_dtype="bf16", layer_kinds=_Q35_KINDS * 8,
-                          attn_output_gate=True, partial_rotary=0.25, norm_offset=True, gdn_key_heads=16,
+                          attn_output_gate=True, partial_rotary=0.25, norm_offset=True, arch="qwen3_5",
+                          gdn_key_heads=16,
                           gdn_value_heads=32, gdn_key_dim=128, gdn_value_dim=128, conv_width=4,
                           max_position=262_144)
 QWEN35_TINY = QWEN35_4B.with_(name="qwen3.5-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2,
@@ -157,10 +164,23 @@ QWEN35_TINY = QWEN35_4B.with_(name="qwen3.5-tiny", layers=4, hidden=256, num_q_h
 QWEN35_GPU_TINY = QWEN35_4B.with_(name="qwen3.5-gpu-tiny", layers=4, hidden=1024, num_q_heads=4, num_kv_heads=2,
                                   intermediate=1024, vocab=4096, gdn_key_heads=2, gdn_value_heads=4,
                                   layer_kinds=_Q35_KINDS, max_position=8192)
+# LFM2: gated short convolutions (width 3) and GQA attention (head_dim 64)
+# (the reference spec quail/specs/data/models/lfm2-2.6b-bf16.toml)
+_LFM2_KINDS = tuple("conv conv attn conv conv attn conv conv conv attn conv conv conv attn conv conv conv attn "
+                    "conv conv conv attn conv conv attn conv conv attn conv conv".split())
+LFM2_2_6B = DecoderConfig(name="lfm2-2.6b", layers=30, hidden=2048, num_q_heads=32, num_kv_heads=8, head_dim=64,
+                          intermediate=10752, vocab=65_536, tied_head=True, weight_dtype="bf16", arch="lfm2",
+                          layer_kinds=_LFM2_KINDS, conv_width=3, rms_eps=1e-5, max_position=128_000)
+LFM2_TINY = LFM2_2_6B.with_(name="lfm2-tiny", layers=3, hidden=256, num_q_heads=4, num_kv_heads=2,
+                            intermediate=512, vocab=151_936, layer_kinds=("conv", "conv", "attn"),
+                            max_position=40_960)
+LFM2_GPU_TINY = LFM2_2_6B.with_(name="lfm2-gpu-tiny", layers=3, hidden=1024, num_q_heads=16, num_kv_heads=4,
+                                intermediate=1024, vocab=4096, layer_kinds=("conv", "attn", "conv"),
+                                max_position=8192)
 
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
-                               QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY)}
+                               QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -178,4 +198,7 @@ MODEL_CONFIGS = {
     "qwen3.5-4b-bf16": QWEN35_4B,
     "qwen3.5-tiny": QWEN35_TINY,
     "qwen3.5-gpu-tiny": QWEN35_GPU_TINY,
+    "lfm2-2.6b-bf16": LFM2_2_6B,
+    "lfm2-tiny": LFM2_TINY,
+    "lfm2-gpu-tiny": LFM2_GPU_TINY,
 }

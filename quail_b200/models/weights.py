@@ -69,6 +69,9 @@ def gdn_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
 def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="cpu",
                       dtype=torch.bfloat16, experts: range | None = None) -> Iterator[tuple[str, torch.Tensor]]:
     """Tensors of layer i in checkpoint names (fp8 projections quantized)."""
+    if cfg.arch == "lfm2":
+        yield from _iter_lfm2_layer(cfg, i, gen, device, dtype)
+        return
     p = layer_prefix(i)
     H = cfg.hidden
     # zero-centered norms (scale 1 + w) start at 0; plain ones at 1
@@ -95,6 +98,27 @@ def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="
             yield from _emit_proj(p + name, shapes[name], cfg, gen, device, dtype).items()
 
 
+def _iter_lfm2_layer(cfg: DecoderConfig, i: int, gen, device, dtype):
+    """An LFM2 layer in HF names: operator_norm / ffn_norm, conv.{in_proj, conv, out_proj} or
+    self_attn.{q,k,v,out}_proj + q/k_layernorm, feed_forward.w1 (gate), w3 (up), w2 (down)."""
+    p = layer_prefix(i)
+    H = cfg.hidden
+    yield p + "operator_norm.weight", torch.ones(H, device=device, dtype=dtype)
+    yield p + "ffn_norm.weight", torch.ones(H, device=device, dtype=dtype)
+    if cfg.kind(i) == "conv":
+        yield from _emit_proj(p + "conv.in_proj", (3 * H, H), cfg, gen, device, dtype).items()
+        yield p + "conv.conv.weight", _rand((H, 1, cfg.conv_width), 0.4, gen, device, dtype)
+        yield from _emit_proj(p + "conv.out_proj", (H, H), cfg, gen, device, dtype).items()
+    else:
+        yield p + "self_attn.q_layernorm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+        yield p + "self_attn.k_layernorm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+        for name, shape in (("q_proj", (cfg.q_dim, H)), ("k_proj", (cfg.kv_dim, H)), ("v_proj", (cfg.kv_dim, H)),
+                            ("out_proj", (H, cfg.q_dim))):
+            yield from _emit_proj(p + "self_attn." + name, shape, cfg, gen, device, dtype).items()
+    for name, shape in (("w1", (cfg.intermediate, H)), ("w3", (cfg.intermediate, H)), ("w2", (H, cfg.intermediate))):
+        yield from _emit_proj(p + "feed_forward." + name, shape, cfg, gen, device, dtype).items()
+
+
 def _iter_gdn(cfg: DecoderConfig, p: str, gen: torch.Generator, device, dtype):
     """A Gated DeltaNet layer: projections, depthwise conv, decay (A_log, dt_bias), gated-norm weight."""
     Hv = cfg.gdn_value_heads
@@ -119,8 +143,8 @@ def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=tor
     out["model.embed_tokens.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     for i in (layers if layers is not None else range(cfg.layers)):
         out.update(iter_random_layer(cfg, i, gen, device, dtype))
-    out["model.norm.weight"] = (torch.zeros if cfg.norm_offset else torch.ones)(cfg.hidden, device=device,
-                                                                               dtype=dtype)
+    out[final_norm_name(cfg)] = (torch.zeros if cfg.norm_offset else torch.ones)(cfg.hidden, device=device,
+                                                                                dtype=dtype)
     if not cfg.tied_head:
         out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     out.update(random_sae(cfg, gen, device))
@@ -138,6 +162,10 @@ def random_sae(cfg: DecoderConfig, gen: torch.Generator, device="cpu") -> dict[s
     w = w / w.norm(dim=1, keepdim=True) * (0.5 * cfg.hidden ** 0.5)
     b = -0.5 * torch.rand(cfg.sae_features, generator=gen, device=device, dtype=torch.float32)
     return {"sae.W_enc": w.to(torch.bfloat16), "sae.b_enc": b}
+
+
+def final_norm_name(cfg: DecoderConfig) -> str:
+    return "model.embedding_norm.weight" if cfg.arch == "lfm2" else "model.norm.weight"
 
 
 def head_weight(ckpt: dict[str, torch.Tensor], cfg: DecoderConfig) -> torch.Tensor:

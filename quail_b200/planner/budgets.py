@@ -79,6 +79,7 @@ class Budgets:
             return 0
         per = len(cfg.gdn_layers) * 4 * ((cfg.conv_width - 1) * cfg.gdn_conv_dim
                                          + cfg.gdn_value_heads * cfg.gdn_key_dim * cfg.gdn_value_dim)
+        per += len(cfg.conv_layers) * 4 * (cfg.conv_width - 1) * cfg.hidden
         cap = int(self.device.mem_bytes * 0.1 // per)
         if self.device.name == "cpu":
             cap = min(cap, 256)

@@ -106,3 +106,39 @@ def test_hybrid_session_filter_and_map():
         assert set(kept.column("id").to_pylist()) <= {0, 1, 2, 3}
         out = s.sql("SELECT id, AI.MAP(body, 'Summarize', 4) AS m FROM r").collect()
         assert out.num_rows == 4 and all(isinstance(v, str) for v in out.column("m").to_pylist())
+
+
+@pytest.mark.parametrize("chunk_tokens", [64, 1000])
+def test_lfm2_chunks_match_prompts_alone(chunk_tokens):
+    from quail_b200.models.config import LFM2_TINY
+    from quail_b200.models.lfm2 import Lfm2Reference
+    cfg = LFM2_TINY.with_(vocab=1000, max_position=4096)
+    m = Lfm2Reference(cfg, random_checkpoint(cfg, seed=6, dtype=torch.float32), head_rows=(1, 2, 3))
+    rng = np.random.default_rng(1)
+    prefix = rng.integers(0, 1000, 48).astype(np.int32)
+    docs = [rng.integers(0, 1000, n).astype(np.int32) for n in (3, 90, 150)]
+    suffix = rng.integers(0, 1000, 5).astype(np.int32)
+    arena = _arena(cfg)
+    ex = StageExecutor(m, arena, chunk_tokens, min_piece=8)
+    got = {}
+    ex.submit(Task(key="p", tokens=prefix, pos_start=0, free_after=False))
+    for i, d in enumerate(docs):
+        ex.submit(Task(key=("d", i), tokens=np.concatenate([d, suffix]), pos_start=len(prefix),
+                       reads=[("p", len(prefix))], readout=True,
+                       on_done=lambda t, row, i=i: got.__setitem__(i, row.float())))
+    ex.run()
+    for i, d in enumerate(docs):
+        want = _alone(m, cfg, np.concatenate([prefix, d, suffix]))
+        assert torch.allclose(got[i], want, rtol=1e-4, atol=1e-4), (i, (got[i] - want).abs().max())
+
+
+def test_lfm2_session():
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    cfg = quail.EngineConfig(model="lfm2-tiny", device="cpu", chunk_tokens=128)
+    t = pa.table({"id": [0, 1, 2], "body": ["the plot is long", "great music", "bad ending"]})
+    with quail.Session(config=cfg) as s:
+        s.register("r", quail.DocumentProvider.from_table(t, id_col="id"))
+        r = s.sql("SELECT id, AI.SCORE(PROMPT('Is it about music? {0}', body)) AS s FROM r").collect()
+        assert r.num_rows == 3 and all(0.0 <= v <= 1.0 for v in r.column("s").to_pylist())

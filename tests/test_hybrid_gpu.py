@@ -178,3 +178,62 @@ def test_hybrid_session_on_gpu():
         assert set(kept.column("id").to_pylist()) <= set(range(6))
         out = s.sql("SELECT id, AI.MAP(body, 'Summarize', 4) AS m FROM r").collect()
         assert out.num_rows == 6
+
+
+def test_short_conv_kernel():
+    from quail_b200.models.lfm2 import short_conv_ref
+    H, W = 384, 3
+    lens = [4, 1, 50]
+    T = sum(lens)
+    bcx = torch.randn(T, 3 * H, device=DEV).bfloat16()
+    w = torch.randn(H, W, device=DEV) * 0.4
+    seqs = torch.zeros(len(lens), 12, dtype=torch.int32)
+    q0 = 0
+    for i, n in enumerate(lens):
+        seqs[i, 0], seqs[i, 1], seqs[i, 2], seqs[i, 4] = q0, n, 1, n
+        q0 += n
+    sio = torch.tensor([[-1, 0], [2, 1], [3, 3]], dtype=torch.int32)
+    state = torch.randn(6, 2, W - 1, H, device=DEV)
+    s0 = state.clone()
+    y = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    ops.native().short_conv(bcx, w, seqs.to(DEV), sio.to(DEV), state, 1, y)
+    for i, n in enumerate(lens):
+        a = int(seqs[i, 0])
+        src, dst = sio[i].tolist()
+        win = s0[src, 1] if src >= 0 else torch.zeros(W - 1, H, device=DEV)
+        out, win = short_conv_ref(bcx[a:a + n], win, w)
+        assert rel_err(y[a:a + n], out) < 1e-2
+        assert rel_err(state[dst, 1], win) < 1e-5
+
+
+def test_lfm2_pipeline_matches_fp32_model():
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.engine.stage_executor import StageExecutor, Task
+    from quail_b200.models.config import LFM2_GPU_TINY
+    from quail_b200.models.lfm2 import Lfm2Pipeline, Lfm2Reference
+    from quail_b200.models.weights import random_checkpoint
+    cfg = LFM2_GPU_TINY
+    ckpt = random_checkpoint(cfg, seed=2, device=DEV)
+    ids = list(range(16))
+
+    def run(model, dtype):
+        arena = KVArena.for_model(cfg, 128, 16, device=DEV, dtype=dtype, state_slots=32)
+        ex = StageExecutor(model, arena, 256, min_piece=16)
+        got = {}
+        rng = np.random.default_rng(3)
+        prefix = rng.integers(0, 4096, 48).astype(np.int32)
+        docs = [rng.integers(0, 4096, n).astype(np.int32) for n in (10, 200, 64, 300)]
+        suffix = rng.integers(0, 4096, 12).astype(np.int32)
+        ex.submit(Task(key="p", tokens=prefix, pos_start=0, free_after=False))
+        for i, d in enumerate(docs):
+            ex.submit(Task(key=i, tokens=np.concatenate([d, suffix]), pos_start=48, reads=[("p", 48)], readout=True,
+                           on_done=lambda t, row, i=i: got.__setitem__(i, row.float().cpu())))
+        ex.run()
+        return torch.stack([got[i] for i in range(len(docs))])
+
+    got = run(Lfm2Pipeline(cfg, ckpt, DEV, head_rows=ids), torch.bfloat16)
+    want = run(Lfm2Reference(cfg, ckpt, device=DEV, head_rows=ids), torch.float32)
+    assert ops.read_and_clear_error(0) == 0
+    d = rel_err(got, want)
+    print(f"lfm2 kernel-vs-fp32: {d:.4f}")
+    assert d < 0.1
