@@ -2,7 +2,8 @@
 // attention: head_dim 256, partial RoPE, sigmoid output gate).
 //
 // One CTA per (16 query rows, KV head): the rows are TOK = 16 / G tokens x the
-// G = QH / KH query heads of the KV head, so every K/V row read from the arena
+// G = QH / KH query heads of the KV head (rows past TOK x G idle when G does not
+// divide 16), so every K/V row read from the arena
 // serves all G heads. The sequence's visible KV (up to four segments; causal in
 // the own segment) streams through shared memory in 16-token blocks
 // (cp.async, double-buffered, page lookups per row). Each of the four warps
@@ -342,6 +343,7 @@ void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const
   QB_SMALL(128, 4)
   QB_SMALL(256, 2)
   QB_SMALL(256, 4)
+  QB_SMALL(256, 6)
   QB_SMALL(256, 8)
 #undef QB_SMALL
   TORCH_CHECK(false, "small_attention: unsupported head_dim / group ", D, " / ", G);

@@ -177,10 +177,25 @@ LFM2_TINY = LFM2_2_6B.with_(name="lfm2-tiny", layers=3, hidden=256, num_q_heads=
 LFM2_GPU_TINY = LFM2_2_6B.with_(name="lfm2-gpu-tiny", layers=3, hidden=1024, num_q_heads=16, num_kv_heads=4,
                                 intermediate=1024, vocab=4096, layer_kinds=("conv", "attn", "conv"),
                                 max_position=8192)
+# further reference specs on the architectures above (quail/specs/data/models/*.toml)
+QWEN3_06B = DecoderConfig(name="qwen3-0.6b", layers=28, hidden=1024, num_q_heads=16, num_kv_heads=8, head_dim=128,
+                          intermediate=3072, tied_head=True, weight_dtype="bf16")
+QWEN3_RERANKER_06B = QWEN3_06B.with_(name="qwen3-reranker-0.6b", vocab=151_669)
+QWEN3_RERANKER_4B = QWEN3_4B.with_(name="qwen3-reranker-4b", vocab=151_669, weight_dtype="bf16")
+DECISION2_06B = QWEN3_06B.with_(name="decision-2.0-kai-0.6b")
+QWEN35_9B = QWEN35_4B.with_(name="qwen3.5-9b", hidden=4096, intermediate=12288, tied_head=False)
+QWEN35_27B = QWEN35_4B.with_(name="qwen3.5-27b", layers=64, hidden=5120, num_q_heads=24, num_kv_heads=4,
+                             intermediate=17408, tied_head=False, gdn_value_heads=48, layer_kinds=_Q35_KINDS * 16)
+QWEN35_2B_SAE = QWEN35_4B.with_(name="qwen3.5-2b-sae", layers=12, hidden=2048, num_q_heads=8, num_kv_heads=2,
+                                intermediate=6144, gdn_value_heads=16, layer_kinds=_Q35_KINDS * 3,
+                                sae_features=32768, sae_keep=100)
+QWEN35_SAE_TINY = QWEN35_TINY.with_(name="qwen3.5-sae-tiny", sae_features=256, sae_keep=8)
 
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
-                               QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY)}
+                               QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
+                               QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
+                               QWEN35_2B_SAE, QWEN35_SAE_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -201,4 +216,11 @@ MODEL_CONFIGS = {
     "lfm2-2.6b-bf16": LFM2_2_6B,
     "lfm2-tiny": LFM2_TINY,
     "lfm2-gpu-tiny": LFM2_GPU_TINY,
+    "qwen3-reranker-0.6b-bf16": QWEN3_RERANKER_06B,
+    "qwen3-reranker-4b-bf16": QWEN3_RERANKER_4B,
+    "decision-2.0-kai-0.6b-bf16": DECISION2_06B,
+    "qwen3.5-9b-bf16": QWEN35_9B,
+    "qwen3.5-27b-bf16": QWEN35_27B,
+    "qwen3.5-2b-sae-bf16": QWEN35_2B_SAE,
+    "qwen3.5-sae-tiny": QWEN35_SAE_TINY,
 }

@@ -125,6 +125,8 @@ class Qwen35Reference:
                          qn=f(ckpt[q + "q_norm.weight"]), kn=f(ckpt[q + "k_norm.weight"]))
             self.layers.append(L)
         self.head = f(head_weight(ckpt, cfg))
+        if cfg.has_sae:
+            self.sae_w, self.sae_b = f(ckpt["sae.W_enc"]), f(ckpt["sae.b_enc"])
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.rotary_dim, cfg.rope_theta, device=device)
         self.scale = ref.softmax_scale(cfg.head_dim)
         self.answer_rows = None
@@ -213,6 +215,8 @@ class Qwen35Reference:
     @torch.no_grad()
     def forward_chunk(self, chunk, arena) -> torch.Tensor:
         h = self.hidden_chunk(chunk, arena)
+        if self.cfg.has_sae:
+            return ref.sae_features(h[chunk.final_rows.long()], self.sae_w, self.sae_b, self.cfg.sae_keep)
         normed = rmsnorm_offset(h[chunk.final_rows.long()], self.final_norm, self.cfg.rms_eps)
         ans = (normed @ self.answer_rows.t()).float()
         if not getattr(chunk, "full_readout", False):

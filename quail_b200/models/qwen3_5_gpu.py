@@ -79,6 +79,9 @@ class Qwen35Pipeline:
             L["wd"] = proj(p + "mlp.down_proj").contiguous()
             self.layers.append(L)
         self.head = head_weight(ckpt, cfg)
+        if cfg.has_sae:
+            self.sae_w = ckpt["sae.W_enc"].to(device=dev, dtype=bf).contiguous()
+            self.sae_b = ckpt["sae.b_enc"].to(device=dev, dtype=torch.float32).contiguous()
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.rotary_dim, cfg.rope_theta, device=dev)
         self.scale = ref.softmax_scale(cfg.head_dim)
         self.answer_rows = None
@@ -143,6 +146,8 @@ class Qwen35Pipeline:
         from quail_b200 import ops
         cfg = self.cfg
         h = self.forward_hidden(chunk, arena)
+        if cfg.has_sae:
+            return ops.sae_features(h.index_select(0, chunk.final_rows.long()), self.sae_w, self.sae_b, cfg.sae_keep)
         if not getattr(chunk, "full_readout", False):
             return ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows)
         R = chunk.final_rows.numel()

@@ -142,3 +142,17 @@ def test_lfm2_session():
         s.register("r", quail.DocumentProvider.from_table(t, id_col="id"))
         r = s.sql("SELECT id, AI.SCORE(PROMPT('Is it about music? {0}', body)) AS s FROM r").collect()
         assert r.num_rows == 3 and all(0.0 <= v <= 1.0 for v in r.column("s").to_pylist())
+
+
+def test_hybrid_sae_features_session():
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    cfg = quail.EngineConfig(model="qwen3.5-sae-tiny", device="cpu", chunk_tokens=128)
+    t = pa.table({"id": [0, 1], "body": ["the plot is long", "great music"]})
+    with quail.Session(config=cfg) as s:
+        s.register("r", quail.DocumentProvider.from_table(t, id_col="id"))
+        r = s.sql("SELECT id, AI.SAE_FEATURES(PROMPT('{0} What is it?', body), {'pooling': 'max'}) AS f FROM r").collect()
+        for feats in r.column("f").to_pylist():
+            x = [d["strength"] for d in feats]
+            assert x == sorted(x, reverse=True) and all(v > 0 for v in x)
