@@ -33,7 +33,7 @@ def _seqs(lengths, q_lens, P, KH, D, pages=1024):
     return _segmented_case(P, specs, QH=KH * 1, KH=KH, D=D, pages=pages)
 
 
-@pytest.mark.parametrize("D,QH,KH", [(256, 4, 2), (256, 16, 4), (64, 8, 2), (128, 16, 4)])
+@pytest.mark.parametrize("D,QH,KH", [(256, 4, 2), (256, 16, 4), (256, 12, 2), (64, 8, 2), (128, 16, 4)])
 def test_small_attention_with_gate(D, QH, KH):
     from test_kernels_gpu import _segmented_case
     specs = [(100, [48, 100]), (1, [48, 300, 65]), (7, [48, 7]), (1, [17]), (40, [48, 200, 40]), (130, [130])]
