@@ -83,7 +83,9 @@ def main():
 
     cfg = MODEL_CONFIGS[args.model]
     pipe = build_pipeline(cfg, device=dev, seed=0)
-    arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=1024)
+    from quail_b200.planner.budgets import Budgets
+    slots = Budgets.for_model(cfg, "b200", gpus=1).state_slots(cfg) if cfg.is_hybrid else 0
+    arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=slots)
     nt = len(SYNTHETIC_TRUE_IDS)
     call = lambda suffix: Call(kind="filter", suffix=suffix, true_cols=list(range(nt)),  # noqa: E731
                                false_cols=list(range(nt, 2 * nt)), name="if")
