@@ -115,7 +115,10 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
   // combined by shuffles); one CTA owns all (up to 128) columns of the head
   constexpr int ROWS = DK / PARTS;
   constexpr int L = kGdnChunk;
-  __shared__ float sq[L][DK + 1], sk[L][DK + 1];  // +1: the pair terms read 16 rows at one column
+  // rows padded by 4 floats: 16-byte aligned for float4 reads, and the pair
+  // terms' 16 rows at one column fall in different banks
+  constexpr int PAD = DK + 4;
+  __shared__ __align__(16) float sq[L][PAD], sk[L][PAD];
   __shared__ float sG[L], sB[L], sg[L];
   __shared__ float sA[L][L], sQK[L][L];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
@@ -169,9 +172,12 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
       float kk = 0.f, qk = 0.f;
       if (t < Lc && u <= t) {
 #pragma unroll 8
-        for (int i = 0; i < DK; ++i) {
-          kk += sk[t][i] * sk[u][i];
-          qk += sq[t][i] * sk[u][i];
+        for (int i = 0; i < DK; i += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(&sk[t][i]);
+          const float4 b = *reinterpret_cast<const float4*>(&sk[u][i]);
+          const float4 c = *reinterpret_cast<const float4*>(&sq[t][i]);
+          kk += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+          qk += c.x * b.x + c.y * b.y + c.z * b.z + c.w * b.w;
         }
         const float e = __expf(sG[t] - sG[u]);
         kk *= e;
@@ -185,24 +191,20 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     float sk0[L], sq0[L];
 #pragma unroll
     for (int t = 0; t < L; ++t) {
-      float a0 = 0.f, a1 = 0.f;
+      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
       if (t < Lc) {
 #pragma unroll
-        for (int i = 0; i < ROWS; i += 2) {
-          a0 += S[i] * sk[t][r0 + i];
-          a1 += S[i + 1] * sk[t][r0 + i + 1];
+        for (int i = 0; i < ROWS; i += 4) {
+          const float4 kk4 = *reinterpret_cast<const float4*>(&sk[t][r0 + i]);
+          const float4 qq4 = *reinterpret_cast<const float4*>(&sq[t][r0 + i]);
+          a0 += S[i] * kk4.x + S[i + 1] * kk4.y;
+          a1 += S[i + 2] * kk4.z + S[i + 3] * kk4.w;
+          b0 += S[i] * qq4.x + S[i + 1] * qq4.y;
+          b1 += S[i + 2] * qq4.z + S[i + 3] * qq4.w;
         }
       }
       sk0[t] = part_sum(a0 + a1);
-      a0 = a1 = 0.f;
-      if (t < Lc) {
-#pragma unroll
-        for (int i = 0; i < ROWS; i += 2) {
-          a0 += S[i] * sq[t][r0 + i];
-          a1 += S[i + 1] * sq[t][r0 + i + 1];
-        }
-      }
-      sq0[t] = part_sum(a0 + a1);
+      sq0[t] = part_sum(b0 + b1);
     }
     // pseudo-values u_t (sequential in t, no barrier) and outputs o_t
     float u[L];
@@ -234,11 +236,22 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
 #pragma unroll
     for (int t = 0; t < L; ++t) wu[t] = t < Lc ? __expf(GL - sG[t]) * u[t] : 0.f;
 #pragma unroll
-    for (int i = 0; i < ROWS; ++i) {
-      float acc = dL * S[i];
+    for (int i = 0; i < ROWS; i += 4) {
+      float4 acc = make_float4(dL * S[i], dL * S[i + 1], dL * S[i + 2], dL * S[i + 3]);
 #pragma unroll
-      for (int t = 0; t < L; ++t) acc += sk[t][r0 + i] * wu[t];
-      S[i] = acc;
+      for (int t = 0; t < L; ++t) {
+        if (t < Lc) {  // rows past the chunk's end hold nothing defined
+          const float4 kk4 = *reinterpret_cast<const float4*>(&sk[t][r0 + i]);
+          acc.x += kk4.x * wu[t];
+          acc.y += kk4.y * wu[t];
+          acc.z += kk4.z * wu[t];
+          acc.w += kk4.w * wu[t];
+        }
+      }
+      S[i] = acc.x;
+      S[i + 1] = acc.y;
+      S[i + 2] = acc.z;
+      S[i + 3] = acc.w;
     }
     __syncthreads();  // the chunk's shared data is read out before the next chunk overwrites it
   }
