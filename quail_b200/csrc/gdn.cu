@@ -5,14 +5,14 @@
 //                  conv window of its source state slot; SiLU; q and k heads
 //                  L2-normalized (q also scaled by d_k^-1/2); the new window
 //                  (last W-1 inputs) written to the sequence's destination slot.
-//   gdn_recurrent  one CTA per (sequence, value head); a thread pair owns one
-//                  column j of the d_k x d_v state S in registers (the columns
-//                  evolve independently). The recurrence
+//   gdn_recurrent  per (sequence, value head, column block): a few adjacent
+//                  threads own one column j of the d_k x d_v state S in registers
+//                  (the columns evolve independently; row partial sums combine by
+//                  shuffles): per token
 //                    S = exp(g) S;  S += k (beta (v - S^T k))^T;  o = S^T q
-//                  (g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)) runs in
-//                  16-token chunks: pair terms once per chunk, then per column a
-//                  short sequential solve and three independent products, so a
-//                  chunk costs three barriers instead of one per token. S is read from the source slot and written
+//                  with g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b);
+//                  the reductions run over i inside a thread pair, so a token
+//                  costs one barrier. S is read from the source slot and written
 //                  to the destination slot.
 //   gdn_gated_norm one warp per (token, value head): RMSNorm(o) * w * silu(z) -> bf16.
 //   short_conv     LFM2's gated short convolution: y = C * conv(B * x), one thread
@@ -95,16 +95,6 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const __nv_bfloat16* __re
 // conv_out fp32 [T, C]: q at head hk*DK, k at qk/2 + hk*DK, v at qk + h*DV.
 // ab: bf16 [T, ldab] with b at column b_col + h, a at column a_col + h.
 // out: fp32 [T, Hv*DV].
-// Chunks of kGdnChunk tokens. With S0 the state before the chunk, G_t the
-// cumulative log decay inside it, and u_t = beta_t (v_t - exp(g_t) S_{t-1}^T k_t):
-//   u_t = beta_t (v_t - exp(G_t) (S0^T k_t) - sum_{s<t} exp(G_t - G_s) (k_t . k_s) u_s)
-//   o_t = exp(G_t) (S0^T q_t) + sum_{s<=t} exp(G_t - G_s) (q_t . k_s) u_s
-//   S   = exp(G_L) S0 + sum_t exp(G_L - G_t) k_t u_t^T
-// The dot products k_t . k_s and q_t . k_s are shared by every column and
-// computed once per chunk; each column then needs only its own u's, computed
-// sequentially over the chunk's tokens without barriers.
-constexpr int kGdnChunk = 16;
-
 template <int DK, int PARTS>
 __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     const float* __restrict__ conv_out, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
@@ -112,17 +102,13 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
     float* __restrict__ out) {
   // PARTS adjacent threads own one column j of S (ROWS rows each; partial sums
-  // combined by shuffles); one CTA owns all (up to 128) columns of the head
+  // combined by shuffles); one CTA owns all (up to 128) columns of the head, so
+  // the per-token staging and barrier are shared by the whole state
   constexpr int ROWS = DK / PARTS;
-  constexpr int L = kGdnChunk;
-  // rows padded by 4 floats: 16-byte aligned for float4 reads, and the pair
-  // terms' 16 rows at one column fall in different banks
-  constexpr int PAD = DK + 4;
-  __shared__ __align__(16) float sq[L][PAD], sk[L][PAD];
-  __shared__ float sG[L], sB[L], sg[L];
-  __shared__ float sA[L][L], sQK[L][L];
+  constexpr int CPC = 128;
+  __shared__ float sq[2][DK], sk[2][DK], sgb[2][2];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int j = tid / PARTS, part = tid % PARTS, r0 = part * ROWS;
+  const int j = blockIdx.z * CPC + tid / PARTS, part = tid % PARTS, r0 = part * ROWS;
   const int hk = h / (Hv / Hk);
   const int q0 = seqs[s * kGdnSeqInts], n = seqs[s * kGdnSeqInts + 1];
   const int src = sio[2 * s], dst = sio[2 * s + 1];
@@ -135,125 +121,53 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     S[i] = (live && src >= 0) ? ssm_state[(size_t)src * slot_stride + head_off + (size_t)(r0 + i) * DV + j] : 0.f;
   const float A = -__expf(A_log[h]);
   const float dtb = dt_bias[h];
+  auto stage = [&](int t, int buf) {
+    const float* row = conv_out + (size_t)(q0 + t) * C;
+    for (int i = tid; i < DK; i += blockDim.x) {
+      sq[buf][i] = row[hk * DK + i];
+      sk[buf][i] = row[qk_channels / 2 + hk * DK + i];
+    }
+    if (tid == 0) {
+      const float a = __bfloat162float(ab[(size_t)(q0 + t) * ldab + a_col + h]) + dtb;
+      const float sp = a > 20.f ? a : log1pf(__expf(a));  // softplus
+      sgb[buf][0] = __expf(A * sp);                        // decay exp(g)
+      const float b = __bfloat162float(ab[(size_t)(q0 + t) * ldab + b_col + h]);
+      sgb[buf][1] = 1.f / (1.f + __expf(-b));              // beta
+    }
+  };
   auto part_sum = [&](float x) {
 #pragma unroll
     for (int o = 1; o < PARTS; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
     return x;
   };
-  for (int c0 = 0; c0 < n; c0 += L) {
-    const int Lc = min(L, n - c0);
-    // stage the chunk's q and k, per-token log decay and beta
-    for (int idx = tid; idx < Lc * DK; idx += blockDim.x) {
-      const int t = idx / DK, i = idx % DK;
-      const float* row = conv_out + (size_t)(q0 + c0 + t) * C;
-      sq[t][i] = row[hk * DK + i];
-      sk[t][i] = row[qk_channels / 2 + hk * DK + i];
+  if (n > 0) stage(0, 0);
+  __syncthreads();
+  for (int t = 0; t < n; ++t) {
+    const int buf = t & 1;
+    const float v = live ? conv_out[(size_t)(q0 + t) * C + qk_channels + h * DV + j] : 0.f;
+    if (t + 1 < n) stage(t + 1, buf ^ 1);  // the other buffer: read last iteration, freed by its barrier
+    const float decay = sgb[buf][0], beta = sgb[buf][1];
+    const float* kk = sk[buf] + r0;
+    const float* qq = sq[buf] + r0;
+    float kv0 = 0.f, kv1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < ROWS; i += 2) {
+      kv0 += S[i] * kk[i];
+      kv1 += S[i + 1] * kk[i + 1];
     }
-    if (tid < Lc) {
-      const size_t r = (size_t)(q0 + c0 + tid) * ldab;
-      const float a = __bfloat162float(ab[r + a_col + h]) + dtb;
-      const float sp = a > 20.f ? a : log1pf(__expf(a));  // softplus
-      sg[tid] = A * sp;                                    // log decay g_t
-      const float b = __bfloat162float(ab[r + b_col + h]);
-      sB[tid] = 1.f / (1.f + __expf(-b));                  // beta_t
+    const float kv = part_sum(kv0 + kv1);
+    const float delta = beta * (v - decay * kv);
+    float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < ROWS; i += 2) {
+      S[i] = decay * S[i] + kk[i] * delta;
+      S[i + 1] = decay * S[i + 1] + kk[i + 1] * delta;
+      o0 += S[i] * qq[i];
+      o1 += S[i + 1] * qq[i + 1];
     }
+    const float o = part_sum(o0 + o1);
+    if (live && part == 0) out[(size_t)(q0 + t) * Hv * DV + h * DV + j] = o;
     __syncthreads();
-    if (tid == 0) {
-      float acc = 0.f;
-      for (int t = 0; t < Lc; ++t) {
-        acc += sg[t];
-        sG[t] = acc;
-      }
-    }
-    __syncthreads();
-    // shared pair terms: A[t][s] = exp(G_t - G_s) k_t.k_s (s < t), QK[t][s] = exp(G_t - G_s) q_t.k_s (s <= t)
-    for (int idx = tid; idx < L * L; idx += blockDim.x) {
-      const int t = idx / L, u = idx % L;
-      float kk = 0.f, qk = 0.f;
-      if (t < Lc && u <= t) {
-#pragma unroll 8
-        for (int i = 0; i < DK; i += 4) {
-          const float4 a = *reinterpret_cast<const float4*>(&sk[t][i]);
-          const float4 b = *reinterpret_cast<const float4*>(&sk[u][i]);
-          const float4 c = *reinterpret_cast<const float4*>(&sq[t][i]);
-          kk += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
-          qk += c.x * b.x + c.y * b.y + c.z * b.z + c.w * b.w;
-        }
-        const float e = __expf(sG[t] - sG[u]);
-        kk *= e;
-        qk *= e;
-      }
-      sA[t][u] = (u < t) ? kk : 0.f;
-      sQK[t][u] = qk;
-    }
-    __syncthreads();
-    // this column: S0^T k_t and S0^T q_t for every token of the chunk
-    float sk0[L], sq0[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) {
-      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-      if (t < Lc) {
-#pragma unroll
-        for (int i = 0; i < ROWS; i += 4) {
-          const float4 kk4 = *reinterpret_cast<const float4*>(&sk[t][r0 + i]);
-          const float4 qq4 = *reinterpret_cast<const float4*>(&sq[t][r0 + i]);
-          a0 += S[i] * kk4.x + S[i + 1] * kk4.y;
-          a1 += S[i + 2] * kk4.z + S[i + 3] * kk4.w;
-          b0 += S[i] * qq4.x + S[i + 1] * qq4.y;
-          b1 += S[i + 2] * qq4.z + S[i + 3] * qq4.w;
-        }
-      }
-      sk0[t] = part_sum(a0 + a1);
-      sq0[t] = part_sum(b0 + b1);
-    }
-    // pseudo-values u_t (sequential in t, no barrier) and outputs o_t
-    float u[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) {
-      float x = 0.f;
-      if (t < Lc) {
-        const float v = live ? conv_out[(size_t)(q0 + c0 + t) * C + qk_channels + h * DV + j] : 0.f;
-        x = v - __expf(sG[t]) * sk0[t];
-#pragma unroll
-        for (int w = 0; w < t; ++w) x -= sA[t][w] * u[w];
-        x *= sB[t];
-      }
-      u[t] = x;
-    }
-#pragma unroll
-    for (int t = 0; t < L; ++t) {
-      if (t < Lc) {
-        float o = __expf(sG[t]) * sq0[t];
-#pragma unroll
-        for (int w = 0; w <= t; ++w) o += sQK[t][w] * u[w];
-        if (live && part == 0) out[(size_t)(q0 + c0 + t) * Hv * DV + h * DV + j] = o;
-      }
-    }
-    // state after the chunk
-    const float GL = sG[Lc - 1];
-    const float dL = __expf(GL);
-    float wu[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) wu[t] = t < Lc ? __expf(GL - sG[t]) * u[t] : 0.f;
-#pragma unroll
-    for (int i = 0; i < ROWS; i += 4) {
-      float4 acc = make_float4(dL * S[i], dL * S[i + 1], dL * S[i + 2], dL * S[i + 3]);
-#pragma unroll
-      for (int t = 0; t < L; ++t) {
-        if (t < Lc) {  // rows past the chunk's end hold nothing defined
-          const float4 kk4 = *reinterpret_cast<const float4*>(&sk[t][r0 + i]);
-          acc.x += kk4.x * wu[t];
-          acc.y += kk4.y * wu[t];
-          acc.z += kk4.z * wu[t];
-          acc.w += kk4.w * wu[t];
-        }
-      }
-      S[i] = acc.x;
-      S[i + 1] = acc.y;
-      S[i + 2] = acc.z;
-      S[i + 3] = acc.w;
-    }
-    __syncthreads();  // the chunk's shared data is read out before the next chunk overwrites it
   }
   if (live)
 #pragma unroll
