@@ -705,8 +705,15 @@ class Executor:
             return pc.invert(r) if e["negated"] else r
         if t == "in":
             v = self.eval(e["arg"], rel)
-            vals = [literal_value(x) for x in e["list"]]
-            r = pc.is_in(_as_array(v, rel.num_rows), value_set=pa.array(vals))
+            if "query" in e:
+                # IN (SELECT ...): the subquery's single column is the value set
+                sub = self.query(e["query"])
+                if sub.num_columns != 1:
+                    raise QueryError("IN (SELECT ...) needs a subquery of one column")
+                vals = sub.column(0).combine_chunks()
+            else:
+                vals = pa.array([literal_value(x) for x in e["list"]])
+            r = pc.fill_null(pc.is_in(_as_array(v, rel.num_rows), value_set=vals), False)
             return pc.invert(r) if e["negated"] else r
         if t == "between":
             v = self.eval(e["arg"], rel)
