@@ -144,13 +144,22 @@ class ModelEngine:
             return np.asarray(doc, dtype=np.int32)
         return self.tokenizer.encode("" if doc is None else str(doc))
 
+    def tokenize_docs(self, docs: list) -> list[np.ndarray]:
+        """Token ids of every document; text goes through the tokenizer in one batch when it has one."""
+        batch = getattr(self.tokenizer, "encode_batch", None)
+        texts = [i for i, d in enumerate(docs) if d is None or isinstance(d, str)]
+        out = [None] * len(docs)
+        if batch is not None and len(texts) > 1:
+            for i, ids in zip(texts, batch(["" if docs[i] is None else docs[i] for i in texts])):
+                out[i] = ids
+        return [self.tokenize_doc(d) if o is None else o for d, o in zip(docs, out)]
+
     def run_region(self, preamble: str, docs: list, calls: list[CallSpec]) -> RegionOutput:
         from quail_b200.engine.region import Call, RegionRun
         tok = self.tokenizer
         # one read per distinct document
         keys, uniq, where = {}, [], []
-        for d in docs:
-            t = self.tokenize_doc(d)
+        for t in self.tokenize_docs(docs):
             k = t.tobytes()
             if k not in keys:
                 keys[k] = len(uniq)

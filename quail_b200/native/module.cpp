@@ -25,6 +25,34 @@ PYBIND11_MODULE(_native, m) {
       },
       "SQL text -> JSON syntax tree");
 
+  // ---------------------------------------------------------------- tokenizer
+  py::class_<qbn::BpeTokenizer, std::shared_ptr<qbn::BpeTokenizer>>(m, "BpeTokenizer")
+      .def(py::init<const std::unordered_map<std::string, int>&,
+                    const std::vector<std::pair<std::string, std::string>>&,
+                    const std::unordered_map<std::string, int>&, bool>(),
+           py::arg("vocab"), py::arg("merges"), py::arg("added"), py::arg("ignore_merges") = false)
+      .def("encode", [](qbn::BpeTokenizer& t, const std::string& text) {
+        std::vector<int> ids;
+        {
+          py::gil_scoped_release nogil;
+          ids = t.encode(text);
+        }
+        return ids;
+      })
+      .def("encode_batch", [](qbn::BpeTokenizer& t, const std::vector<std::string>& texts, int threads) {
+        std::vector<std::vector<int>> out;
+        {
+          py::gil_scoped_release nogil;
+          out = t.encode_batch(texts, threads);
+        }
+        return out;
+      }, py::arg("texts"), py::arg("threads") = 0)
+      .def("decode", [](const qbn::BpeTokenizer& t, const std::vector<int>& ids, bool skip_special) {
+        return py::bytes(t.decode(ids, skip_special));
+      }, py::arg("ids"), py::arg("skip_special") = false)
+      .def("token_to_id", &qbn::BpeTokenizer::token_to_id)
+      .def_property_readonly("vocab_size", &qbn::BpeTokenizer::vocab_size);
+
   // ---------------------------------------------------------------- worker IPC
   auto& ipc_error = py::register_exception<qbn::IpcError>(m, "IpcError", PyExc_OSError);
   py::register_exception<qbn::IpcTimeout>(m, "IpcTimeout", ipc_error.ptr());

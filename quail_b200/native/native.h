@@ -5,7 +5,10 @@
 #include <map>
 #include <memory>
 #include <stdexcept>
+#include <mutex>
 #include <string>
+#include <unordered_map>
+#include <unordered_set>
 #include <utility>
 #include <vector>
 
@@ -63,5 +66,36 @@ struct SqlError : std::runtime_error {
 
 // SQL text -> JSON syntax tree (throws SqlError)
 std::string parse_sql(const std::string& text);
+
+// Byte-level BPE (HF tokenizer.json, GPT-2 / Qwen2 pre-tokenizer): tokenizer.cpp.
+class BpeTokenizer {
+ public:
+  BpeTokenizer(const std::unordered_map<std::string, int>& vocab,
+               const std::vector<std::pair<std::string, std::string>>& merges,
+               const std::unordered_map<std::string, int>& added, bool ignore_merges);
+  std::vector<int> encode(const std::string& text);
+  // threads <= 0: one per hardware thread (fewer for small batches)
+  std::vector<std::vector<int>> encode_batch(const std::vector<std::string>& texts, int threads);
+  std::string decode(const std::vector<int>& ids, bool skip_special) const;
+  int token_to_id(const std::string& token) const;
+  size_t vocab_size() const { return id_tok_.size(); }
+
+ private:
+  using Cache = std::unordered_map<std::string, std::vector<int>>;
+  void encode_into(const std::string& text, std::vector<int>& out, Cache& cache) const;
+  void encode_plain(const std::string& text, std::vector<int>& out, Cache& cache) const;
+  void bpe(const std::string& word, std::vector<int>& out, Cache& cache) const;
+  std::unordered_map<std::string, int> vocab_, added_;
+  bool ignore_merges_;
+  std::string byte_sym_[256];
+  std::unordered_map<uint32_t, uint8_t> sym_byte_;
+  std::unordered_map<std::string, int> ranks_;
+  std::vector<std::string> id_tok_;
+  std::unordered_set<int> added_ids_;
+  std::vector<std::string> added_sorted_;  // longest first
+  bool added_first_[256] = {};
+  Cache cache_;
+  std::mutex mu_;  // encode mutates the cache; callers may release the GIL
+};
 
 }  // namespace qbn
