@@ -38,6 +38,8 @@ class CallSpec:
     max_tokens: int = 256
     probabilities: bool = False
     pooling: str = "last"     # features: "last" or "max"
+    segments: list | None = None   # tail tokenized piece by piece (decision prompts); joins to `tail`
+    read: list = field(default_factory=list)   # segments whose last token the decision head reads
 
 
 @dataclass
@@ -92,6 +94,12 @@ class ModelEngine:
             return random_checkpoint_on(self.cfg, self.device, seed=self.config.seed)
         return random_checkpoint(self.cfg, seed=self.config.seed, dtype=torch.float32)
 
+    def _attach_head(self, ckpt) -> None:
+        """A decision model's option-scoring head, kept in fp32 beside the backbone."""
+        if self.cfg.role == "decision":
+            from quail_b200.models.decision import DecisionHead, head_tensors
+            self.model.decision = DecisionHead(head_tensors(ckpt), self.device)
+
     def _build(self, pages: int | None):
         from quail_b200.engine.arena import KVArena
         from quail_b200.engine.stage_executor import StageExecutor
@@ -108,6 +116,7 @@ class ModelEngine:
             else:
                 self.model = CpuModel(self.cfg, ckpt, device="cpu")
                 page_tokens, dtype = 16, torch.float32
+            self._attach_head(ckpt)
             del ckpt
             n_pages = pages or self.budgets.arena_pages(page_tokens)
             self.arena = KVArena.for_model(self.cfg, n_pages, page_tokens, device=self.device, dtype=dtype,
@@ -123,6 +132,7 @@ class ModelEngine:
             from quail_b200.models.qwen3 import Qwen3Reference
             self.model = Qwen3Reference(self.cfg, ckpt, device="cpu")
             page_tokens, dtype = 16, torch.float32
+        self._attach_head(ckpt)
         del ckpt
         n_pages = pages or self.budgets.arena_pages(page_tokens)
         self.arena = KVArena(self.cfg.layers, n_pages, page_tokens, self.cfg.num_kv_heads, self.cfg.head_dim,
@@ -131,10 +141,8 @@ class ModelEngine:
                                       gpu_timing=self.config.gpu_timing)
 
     def _set_answer_rows(self, ids):
-        if self.on_gpu and not self.cfg.is_hybrid:
-            self.model.w.set_answer_rows(ids)
-        else:
-            self.model.set_answer_rows(ids)
+        w = getattr(self.model, "w", None)
+        (w if w is not None and hasattr(w, "set_answer_rows") else self.model).set_answer_rows(ids)
 
     # ------------------------------------------------------------ regions
     def tokenize_doc(self, doc) -> np.ndarray:
@@ -165,8 +173,12 @@ class ModelEngine:
                 keys[k] = len(uniq)
                 uniq.append(t)
             where.append(keys[k])
-        true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
-        false_ids = tok.answer_ids(P.FALSE_SPELLINGS)
+        if self.cfg.role == "reranker":
+            # a Qwen3 reranker answers "yes" or "no" (lowering.rs:549-551)
+            true_ids, false_ids = tok.answer_ids(["yes"]), tok.answer_ids(["no"])
+        else:
+            true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
+            false_ids = tok.answer_ids(P.FALSE_SPELLINGS)
         both = set(true_ids) & set(false_ids)
         true_ids = [i for i in true_ids if i not in both]
         false_ids = [i for i in false_ids if i not in both]
@@ -183,11 +195,34 @@ class ModelEngine:
                 why = ("AI.SAE_FEATURES needs a model with a sparse autoencoder spec" if c.kind == "features"
                        else f"{self.cfg.name} serves AI.SAE_FEATURES only")
                 raise RefusalError(Refusal(reasons=(why,), constraint="unsupported_function"))
+        decision = self.cfg.role == "decision"
+        for c in calls:
+            why = None
+            if decision and c.segments is None:
+                why = f"{c.kind} is not a call {self.cfg.name!r} answers: its head scores listed options"
+            elif not decision and c.segments is not None:
+                why = f"an option-scoring prompt needs a decision model, not {self.cfg.name!r}"
+            elif self.cfg.role == "reranker" and c.kind != "score":
+                why = "a reranker model can only be used with AI.SCORE"
+            if why:
+                raise RefusalError(Refusal(reasons=(why,), constraint="unsupported_function"))
         rcalls = []
         for c in calls:
-            rc = Call(kind=c.kind, suffix=tok.encode(c.tail), name=c.name, max_tokens=c.max_tokens,
-                      stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling)
-            if c.kind in ("filter", "score"):
+            offsets = ()
+            if c.segments is not None:
+                parts = [tok.encode(seg) for seg in c.segments]
+                suffix = np.concatenate(parts).astype(np.int32) if parts else np.zeros(0, np.int32)
+                lens = [len(p) for p in parts]
+                # distance of each read segment's last token before the prompt's last row (lowering.rs:51-72)
+                offsets = tuple(sum(lens[i + 1:]) for i in c.read) + (0,)
+            else:
+                suffix = tok.encode(c.tail)
+            rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
+                      stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
+                      offsets=offsets)
+            if offsets:
+                pass
+            elif c.kind in ("filter", "score"):
                 rc.true_cols = [col(i) for i in true_ids]
                 rc.false_cols = [col(i) for i in false_ids]
             elif c.kind == "classify":
@@ -205,7 +240,8 @@ class ModelEngine:
         stop = getattr(self, "interrupt", None)
         ex.should_stop = stop.is_set if stop is not None else None
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
-        run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer))
+        run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer),
+                        decision=getattr(self.model, "decision", None))
         results = run.run()
         if self.on_gpu:
             from quail_b200 import ops

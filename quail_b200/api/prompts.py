@@ -186,3 +186,116 @@ def bind_join_prompt(template: str, turn: Turn = Turn()) -> BoundPrompt:
     question = _PLACEHOLDER.sub("", template).strip()
     tail = JOIN_QUESTION_SEP + TASK_INSTRUCTION + question + ANSWER_CUE + turn.suffix
     return BoundPrompt(kind="join", template=template, preamble=turn.prefix, tail=tail, question=question)
+
+
+# ---------------------------------------------------------------- model roles
+#
+# A model's role picks the prompt it reads (crates/quail-planner/src/prompts.rs:
+# 144-178 for the decision2-noul layout; lowering.rs:448-465 for the Qwen3
+# reranker's chat text). These strings are interfaces of the checkpoints, so
+# they are the reference's, character for character.
+
+DECISION2_DOCUMENT_LABEL = "Context:\n"
+DECISION2_QUESTION_LABEL = "Task type: noul\nQuestion:\n"
+DECISION2_CHOICE_LABEL = "Task type: choice\nQuestion:\n"
+DECISION2_QUESTION_END = "\nOptions:"
+DECISION2_CLOSING = ("\n\nSelect the single option best supported by the context and instructions."
+                     "\nDecision:")
+RERANKER_SYSTEM = ("You are an expert at text analysis. Judge whether the Document meets the requirements "
+                   "based on the Query and the Instruct provided. Note that the answer can only be \"yes\" "
+                   "or \"no\".")
+RERANKER_INSTRUCTION = "Judge whether the document meets the requirements in the query."
+
+
+@dataclass(frozen=True)
+class PromptModel:
+    """What the binder needs to know of a model: its role, prompt layout and chat turn."""
+
+    role: str = "generative"
+    layout: str = "ai-if"
+    turn: Turn = Turn()
+    name: str = ""
+
+
+def prompt_model(cfg) -> PromptModel:
+    """The prompt model of a decoder config: rerankers and decision models bring their own text."""
+    role = getattr(cfg, "role", "generative")
+    turn = Turn(prefix="", suffix="") if role in ("reranker", "decision") else Turn()
+    return PromptModel(role=role, layout=getattr(cfg, "prompt_layout", "ai-if"), turn=turn,
+                       name=getattr(cfg, "name", ""))
+
+
+def decision2_option(key: str, description: str | None) -> str:
+    """One option block: its fields as compact JSON with sorted keys."""
+    import json
+    body = json.dumps({"description": description, "key": key}, separators=(",", ":"), ensure_ascii=False,
+                      sort_keys=True)
+    return f"\n<option>\n{body}\n</option>"
+
+
+@dataclass
+class SegmentedPrompt(BoundPrompt):
+    """A prompt whose tail is tokenized one segment at a time; `read` lists the
+    segments whose last token the decision head reads (the last segment's last
+    token, the prompt's last row, is always read)."""
+
+    segments: list = field(default_factory=list)
+    read: list = field(default_factory=list)
+
+
+def bind_decision_prompt(template: str, kind: str, turn: Turn = Turn(prefix="", suffix="")) -> SegmentedPrompt:
+    """AI.IF / AI.SCORE for a decision model: the question, then the options No and Yes."""
+    base = bind_prompt(template, 1, turn)
+    question = base.question
+    segments = [JOIN_QUESTION_SEP + DECISION2_QUESTION_LABEL + question + DECISION2_QUESTION_END,
+                decision2_option("false", "No"), decision2_option("true", "Yes"),
+                DECISION2_CLOSING + turn.suffix]
+    return SegmentedPrompt(kind=kind, template=template, preamble=turn.prefix + DECISION2_DOCUMENT_LABEL,
+                           tail="".join(segments), question=question, segments=segments, read=[1, 2])
+
+
+def bind_decision_choice_prompt(template: str | None, labels: list[str], descriptions: list[str] | None = None,
+                                task_description: str = "",
+                                turn: Turn = Turn(prefix="", suffix="")) -> SegmentedPrompt:
+    """AI.CLASSIFY for a decision model: one option block per label, each read by the head."""
+    if template:
+        question, rest = split_frame(template)
+        question = (question + ("\n\n" + rest.strip() if rest.strip() else "")).strip()
+    else:
+        question = ""
+    if task_description:
+        question = f"{question}\n{task_description}" if question else task_description
+    question = question or CHOICE_QUESTION
+    descriptions = list(descriptions or [])
+    segments = [JOIN_QUESTION_SEP + DECISION2_CHOICE_LABEL + question + DECISION2_QUESTION_END]
+    for i, label in enumerate(labels):
+        d = descriptions[i] if i < len(descriptions) and descriptions[i] else None
+        segments.append(decision2_option(str(label), d))
+    segments.append(DECISION2_CLOSING + turn.suffix)
+    return SegmentedPrompt(kind="classify", template=template or "", preamble=turn.prefix + DECISION2_DOCUMENT_LABEL,
+                           tail="".join(segments), question=question, labels=list(labels),
+                           descriptions=descriptions, segments=segments, read=list(range(1, len(labels) + 1)))
+
+
+def reranker_text(query: str, document: str) -> str:
+    """The Qwen3 reranker's whole prompt for one (query, document) pair."""
+    return ("<|im_start|>system\n" + RERANKER_SYSTEM + "<|im_end|>\n<|im_start|>user\n<Instruct>: "
+            + RERANKER_INSTRUCTION + "\n<Query>: " + query + "\n<Document>: " + document
+            + "<|im_end|>\n<|im_start|>assistant\n<think>\n\n</think>\n\n")
+
+
+def bind_reranker_prompt(template: str) -> BoundPrompt:
+    """AI.SCORE on a reranker: the query (the template without its document) goes before the document.
+
+    The query is the template with a leading or trailing placeholder removed
+    and any other occurrence read as "this document" (lowering.rs:420-446).
+    """
+    check_placeholders(template, 1)
+    text = template.strip()
+    if text.startswith("{0}"):
+        text = text[3:].lstrip()
+    if text.endswith("{0}"):
+        text = text[:-3].rstrip()
+    query = text.replace("{0}", "this document")
+    before, after = reranker_text(query, "\x00").split("\x00")
+    return BoundPrompt(kind="score", template=template, preamble=before, tail=after, question=query)

@@ -24,6 +24,9 @@ Readouts:
   map       greedy decoding: each step appends the argmax token to the
             question's own pages until a stop token or max_tokens
             (map_decoder.py); extract decodes the same way after the phrase cue
+  decision  a decision model's head scores the option rows against the last
+            row (filter: Yes > No; score: sigmoid(Yes - No); classify: the
+            best label), readout.py:633-728
   features  SAE features of the residual stream (a model with an SAE returns
             packed [feature ids | strengths] rows): the last token's, or
             with max pooling each feature's largest strength over the row's
@@ -60,6 +63,9 @@ class Call:
     name: str = ""
     probabilities: bool = False
     pooling: str = "last"                            # features: "last" token or "max" over the row's tokens
+    # decision models: rows read by the decision head, as distances before the
+    # last row (one per option, then 0); empty = an LM-head readout
+    offsets: tuple = ()
 
 
 @dataclass
@@ -70,8 +76,9 @@ class RowResult:
 
 class RegionRun:
     def __init__(self, executor: StageExecutor, prefix: np.ndarray, docs: list, calls: list[Call],
-                 doc_ids: list | None = None, answer_width: int | None = None):
+                 doc_ids: list | None = None, answer_width: int | None = None, decision=None):
         self.ex = executor
+        self.decision = decision              # models.decision.DecisionHead of a decision model
         self.prefix = np.asarray(prefix, dtype=np.int32)
         self.docs = [np.asarray(d, dtype=np.int32) for d in docs]
         self.calls = calls
@@ -105,9 +112,32 @@ class RegionRun:
         f = max(float(row[c]) for c in call.false_cols)
         return t - f
 
+    def _decided(self, r: int, ci: int, rows) -> None:
+        """A decision head's answer: option scores (No, Yes for a filter or score; the labels for classify)."""
+        call = self.calls[ci]
+        res = self.results[r]
+        scores = self.decision.combine(rows)
+        if call.kind == "filter":
+            keep = bool(scores[1] > scores[0])
+            res.values[call.name] = keep
+            if not keep:
+                res.kept = False
+        elif call.kind == "score":
+            res.values[call.name] = 1.0 / (1.0 + math.exp(-(float(scores[1]) - float(scores[0]))))
+        else:
+            res.values[call.name] = int(np.argmax(scores))
+            if call.probabilities:
+                e = np.exp(scores - scores.max())
+                res.values[call.name + "#probs"] = [float(x) for x in e / e.sum()]
+        self.asked += 1
+        self._finish_call(r, ci)
+
     def _answered(self, r: int, ci: int, row) -> None:
         call = self.calls[ci]
         res = self.results[r]
+        if call.offsets:
+            self._decided(r, ci, row)
+            return
         if call.kind == "filter":
             keep = self._margin(call, row) > 0
             res.values[call.name] = bool(keep)
@@ -220,7 +250,10 @@ class RegionRun:
 
     @staticmethod
     def _pooled_rows(call: Call, n: int):
-        """Readout offsets: every own token for max-pooled features, else the last token only."""
+        """Readout offsets: every own token for max-pooled features, the option rows and the
+        last row for a decision head, else the last token only."""
+        if call.offsets:
+            return tuple(n - 1 - o for o in call.offsets)
         return tuple(range(n)) if call.kind == "features" and call.pooling == "max" else None
 
     @staticmethod
@@ -229,7 +262,7 @@ class RegionRun:
         return call.max_tokens if call.kind in ("map", "extract") else 0
 
     def _needs_full(self, call: Call) -> bool:
-        return call.kind in ("classify", "map", "extract")
+        return call.kind in ("classify", "map", "extract") and not call.offsets
 
     def _submit_question(self, r: int, ci: int) -> None:
         call = self.calls[ci]

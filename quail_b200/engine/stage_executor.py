@@ -58,6 +58,7 @@ class Task:
     readout_rows: tuple | None = None                # offsets read out (default: the last token)
     full_readout: bool = False                       # also argmax / log-sum-exp over the vocabulary
     reserve_tokens: int = 0                          # decode headroom allocated with the key's pages
+    got_rows: list = field(default_factory=list)     # readout rows of the pieces already collected
 
     @property
     def remaining(self) -> int:
@@ -176,20 +177,20 @@ class StageExecutor:
                         deferred.append(task)
                         break
             piece = min(task.remaining, room)
-            if piece < task.remaining and (piece < self.min_piece or task.readout_rows is not None) and specs:
-                # a task read out at several rows runs whole: wait for a chunk with room
+            if piece < task.remaining and piece < self.min_piece and specs:
                 deferred.append(task)
                 break
             last = piece == task.remaining
             rows = None
-            if task.readout and last and task.readout_rows is not None:
-                if task.done:
-                    raise ValueError("a task with several readout rows must fit in one chunk")
-                rows = tuple(task.readout_rows)
+            readout = task.readout and last
+            if task.readout and task.readout_rows is not None:
+                # a task read at several rows reads, in each piece, the rows that fall in it
+                rows = tuple(r - task.done for r in task.readout_rows if task.done <= r < task.done + piece)
+                readout = bool(rows)
             specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix + task.done,
                                  tokens=task.tokens[task.done:task.done + piece],
-                                 pos_start=task.pos_start + task.done, readout=task.readout and last, tag=task,
-                                 readout_rows=rows, full=task.full_readout))
+                                 pos_start=task.pos_start + task.done, readout=readout, tag=task,
+                                 readout_rows=rows if readout else None, full=task.full_readout))
             task.done += piece
             room -= piece
             if not last:
@@ -244,6 +245,12 @@ class StageExecutor:
                 row = host[r] if s.readout_rows is None else host[r:r + k]
                 r += k
                 self.stats.readouts += 1
+            if task.readout_rows is not None and task.readout:
+                if row is not None:
+                    task.got_rows.append(row.numpy().copy() if hasattr(row, "numpy") else np.array(row))
+                if last:
+                    row = np.concatenate(task.got_rows) if len(task.got_rows) != 1 else task.got_rows[0]
+                    task.got_rows = []
             if last:
                 if task.on_done:
                     task.on_done(task, row)

@@ -46,6 +46,12 @@ class DecoderConfig:
     gdn_key_dim: int = 0
     gdn_value_dim: int = 0
     conv_width: int = 0
+    # what the model answers with: "generative" (LM head), "reranker" (yes / no
+    # logits of a Qwen3 reranker prompt, AI.SCORE only) or "decision" (an
+    # option-scoring head over the backbone's rows, no text output)
+    role: str = "generative"
+    prompt_layout: str = "ai-if"     # "ai-if" or "decision2-noul"
+    decision_head_dim: int = 0
 
     @property
     def q_dim(self) -> int:
@@ -180,9 +186,16 @@ LFM2_GPU_TINY = LFM2_2_6B.with_(name="lfm2-gpu-tiny", layers=3, hidden=1024, num
 # further reference specs on the architectures above (quail/specs/data/models/*.toml)
 QWEN3_06B = DecoderConfig(name="qwen3-0.6b", layers=28, hidden=1024, num_q_heads=16, num_kv_heads=8, head_dim=128,
                           intermediate=3072, tied_head=True, weight_dtype="bf16")
-QWEN3_RERANKER_06B = QWEN3_06B.with_(name="qwen3-reranker-0.6b", vocab=151_669)
-QWEN3_RERANKER_4B = QWEN3_4B.with_(name="qwen3-reranker-4b", vocab=151_669, weight_dtype="bf16")
-DECISION2_06B = QWEN3_06B.with_(name="decision-2.0-kai-0.6b")
+QWEN3_RERANKER_06B = QWEN3_06B.with_(name="qwen3-reranker-0.6b", vocab=151_669, role="reranker")
+QWEN3_RERANKER_4B = QWEN3_4B.with_(name="qwen3-reranker-4b", vocab=151_669, weight_dtype="bf16", role="reranker")
+DECISION2_06B = QWEN3_06B.with_(name="decision-2.0-kai-0.6b", role="decision", prompt_layout="decision2-noul",
+                                decision_head_dim=256)
+# small stand-ins of the two roles for the tests (CPU and GPU kernel shapes)
+DECISION_TINY = QWEN3_TINY.with_(name="decision-tiny", role="decision", prompt_layout="decision2-noul",
+                                 decision_head_dim=32, weight_dtype="bf16")
+DECISION_GPU_TINY = QWEN3_GPU_TINY.with_(name="decision-gpu-tiny", role="decision", prompt_layout="decision2-noul",
+                                         decision_head_dim=128, weight_dtype="bf16")
+RERANKER_TINY = QWEN3_TINY.with_(name="reranker-tiny", role="reranker", weight_dtype="bf16")
 QWEN35_9B = QWEN35_4B.with_(name="qwen3.5-9b", hidden=4096, intermediate=12288, tied_head=False)
 QWEN35_27B = QWEN35_4B.with_(name="qwen3.5-27b", layers=64, hidden=5120, num_q_heads=24, num_kv_heads=4,
                              intermediate=17408, tied_head=False, gdn_value_heads=48, layer_kinds=_Q35_KINDS * 16)
@@ -195,7 +208,7 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
                                QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
-                               QWEN35_2B_SAE, QWEN35_SAE_TINY)}
+                               QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -223,4 +236,7 @@ MODEL_CONFIGS = {
     "qwen3.5-27b-bf16": QWEN35_27B,
     "qwen3.5-2b-sae-bf16": QWEN35_2B_SAE,
     "qwen3.5-sae-tiny": QWEN35_SAE_TINY,
+    "decision-tiny": DECISION_TINY,
+    "decision-gpu-tiny": DECISION_GPU_TINY,
+    "reranker-tiny": RERANKER_TINY,
 }

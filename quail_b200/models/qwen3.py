@@ -95,6 +95,8 @@ class Qwen3Weights:
 class Qwen3Pipeline:
     """Forward pass of a packed chunk on the sm_100a kernels."""
 
+    decision = None   # a decision model's head (models.decision.DecisionHead), set by the engine
+
     def __init__(self, cfg: DecoderConfig, weights: Qwen3Weights):
         assert cfg.head_dim == 128, "the kernels take head_dim 128"
         self.cfg = cfg
@@ -144,6 +146,11 @@ class Qwen3Pipeline:
         if cfg.has_sae:
             # resid_post of the last loaded layer -> packed SAE features per readout row
             return ops.sae_features(h.index_select(0, chunk.final_rows.long()), w.sae_w, w.sae_b, cfg.sae_keep)
+        if self.decision is not None:
+            # decision model: the head's projections of the final-normed rows
+            normed = torch.empty(chunk.final_rows.numel(), cfg.hidden, dtype=torch.bfloat16, device=h.device)
+            ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows, normed=normed)
+            return self.decision.features(normed)
         if not getattr(chunk, "full_readout", False):
             return ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows)
         R = chunk.final_rows.numel()
@@ -159,6 +166,8 @@ class Qwen3Reference:
     Weights are dequantized from the checkpoint, so an fp8 checkpoint gives
     the math the kernels approximate (activations stay fp32 here).
     """
+
+    decision = None
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device="cpu", head_rows=None,
                  dtype=torch.float32, emulate_kernels: bool = False):
@@ -279,6 +288,8 @@ class Qwen3Reference:
             x = self._bf(rows) if self.emulate else rows
             return ref.sae_features(x, self.sae_w, self.sae_b, self.cfg.sae_keep)
         normed = ref.rmsnorm(rows, self.final_norm, self.cfg.rms_eps)
+        if self.decision is not None:
+            return self.decision.features(normed)
         ans = (normed @ self.answer_rows.t()).float()
         if not getattr(chunk, "full_readout", False):
             return ans

@@ -148,6 +148,9 @@ def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=tor
     if not cfg.tied_head:
         out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     out.update(random_sae(cfg, gen, device))
+    if cfg.role == "decision":
+        from quail_b200.models.decision import random_decision_head
+        out.update(random_decision_head(cfg.hidden, cfg.decision_head_dim, gen, device))
     return out
 
 
@@ -211,8 +214,25 @@ def config_from_hf(directory: str, name: str | None = None) -> DecoderConfig:
 
 
 def load_checkpoint(directory: str, device="cpu") -> dict[str, torch.Tensor]:
+    """Every safetensors file of a checkpoint directory, by HF tensor name.
+
+    A Decision 2.0 package keeps a bare Qwen3Model (no `model.` prefix) under
+    `backbone/` and the head in `decision_head.safetensors`; its backbone
+    tensors get the prefix and the head's the `decision_head.` prefix
+    (quail/backends/quail/executor/models/decision2_vllm.py:13-25).
+    """
     from safetensors.torch import load_file
     out: dict[str, torch.Tensor] = {}
+    backbone = os.path.join(directory, "backbone")
+    if os.path.isdir(backbone):
+        for fn in sorted(os.listdir(backbone)):
+            if fn.endswith(".safetensors"):
+                for k, v in load_file(os.path.join(backbone, fn), device=str(device)).items():
+                    out[k if k.startswith(("model.", "lm_head.")) else "model." + k] = v
+        head = os.path.join(directory, "decision_head.safetensors")
+        if os.path.exists(head):
+            out.update({"decision_head." + k: v for k, v in load_file(head, device=str(device)).items()})
+        return out
     for fn in sorted(os.listdir(directory)):
         if fn.endswith(".safetensors"):
             out.update(load_file(os.path.join(directory, fn), device=str(device)))

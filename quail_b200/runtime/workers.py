@@ -90,7 +90,9 @@ class WorkerPool:
     """`gpus` worker processes behind the session; same run_region as ModelEngine."""
 
     def __init__(self, config, python: str | None = None, boot: bool = True):
+        from quail_b200.api.config import check_config
         self.config = config
+        self.cfg = check_config(config)   # the decoder config (roles, prompt layout) the workers serve
         self.n = config.gpus
         self.python = python or sys.executable
         self.dir = tempfile.mkdtemp(prefix=f"qb-{os.getpid()}-")

@@ -186,6 +186,9 @@ class BoundCall:
     questions: list = field(default_factory=list)   # extract: one call per question
     span: bool = False
     pooling: str = "last"                            # features
+    descriptions: list = field(default_factory=list)  # classify: per-label descriptions
+    segments: list | None = None                     # decision prompts: the tail's segments
+    read: list = field(default_factory=list)         # decision prompts: segments the head reads
 
 
 def _options(node) -> dict:
@@ -224,7 +227,61 @@ def _prompt_parts(arg) -> tuple[str, dict, int]:
     return "{0}", arg, 1
 
 
-def bind_call(node, turn: P.Turn) -> BoundCall:
+def _refuse(reason: str, constraint: str):
+    from quail_b200.api.config import Refusal, RefusalError
+    raise RefusalError(Refusal(reasons=(reason,), constraint=constraint))
+
+
+def bind_role_call(node, model: P.PromptModel) -> BoundCall:
+    """A call on a reranker or a decision model: their own prompts, their own readouts.
+
+    Reranker: AI.SCORE only (crates/quail-planner/src/graph.rs:1719-1738).
+    Decision: AI.IF / AI_FILTER / AI.SCORE read the No and Yes options,
+    AI.CLASSIFY one option per label; neither decodes text
+    (validation.rs:207-231).
+    """
+    name = node["name"]
+    args = [a for a in node["args"] if a.get("type") != "named_arg"]
+    named = {a["name"].lower(): a["value"] for a in node["args"] if a.get("type") == "named_arg"}
+    key = node_key(node)
+    if name in ("AI.MAP", "AI.EXTRACT", "AI.EXTRACT_SPAN"):
+        _refuse(f"{name} decodes the model's next tokens, which {model.name!r} does not give",
+                f"unsupported_{name[3:].lower()}_query")
+    if model.role == "reranker":
+        if name == "AI.CLASSIFY":
+            _refuse("a reranker model cannot run AI.CLASSIFY", "reranker_only_scores")
+        if name != "AI.SCORE":
+            _refuse("a reranker model can only be used with AI.SCORE", "reranker_only_scores")
+        if not args:
+            raise QueryError(f"{name} takes a prompt")
+        template, doc, ndocs = _prompt_parts(args[0])
+        if ndocs > 1:
+            raise QueryError("AI.SCORE on a reranker reads one document")
+        bp = P.bind_reranker_prompt(template)
+        return BoundCall(key=key, kind="score", preamble=bp.preamble, tail=bp.tail, doc_expr=doc)
+    if name in ("AI.IF", "AI_FILTER", "AI.SCORE"):
+        if not args:
+            raise QueryError(f"{name} takes a prompt")
+        template, doc, _ = _prompt_parts(args[0])
+        opts = _options(args[1] if len(args) > 1 else named.get("options"))
+        kind = "score" if name == "AI.SCORE" else "filter"
+        bp = P.bind_decision_prompt(template, kind, model.turn)
+        return BoundCall(key=key, kind=kind, preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                         selectivity=opts.get("selectivity"), segments=bp.segments, read=bp.read)
+    if name == "AI.CLASSIFY":
+        call = bind_call(node, model.turn)
+        opts = _options(args[2] if len(args) > 2 else named.get("options"))
+        template, _, _ = _prompt_parts(args[0])
+        bp = P.bind_decision_choice_prompt(template if template != "{0}" else None, call.labels,
+                                           call.descriptions, opts.get("task_description", ""), model.turn)
+        call.preamble, call.tail, call.segments, call.read = bp.preamble, bp.tail, bp.segments, bp.read
+        return call
+    return bind_call(node, model.turn)
+
+
+def bind_call(node, turn: P.Turn, model: P.PromptModel | None = None) -> BoundCall:
+    if model is not None and model.role in ("reranker", "decision"):
+        return bind_role_call(node, model)
     name = node["name"]
     args = [a for a in node["args"] if a.get("type") != "named_arg"]
     named = {a["name"].lower(): a["value"] for a in node["args"] if a.get("type") == "named_arg"}
@@ -259,7 +316,7 @@ def bind_call(node, turn: P.Turn) -> BoundCall:
         bp = P.bind_classify_prompt(template if template != "{0}" else None, labels, descriptions,
                                     opts.get("task_description", ""), turn)
         return BoundCall(key=key, kind="classify", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, labels=labels,
-                         probabilities=bool(opts.get("probabilities", False)))
+                         probabilities=bool(opts.get("probabilities", False)), descriptions=descriptions)
     if name == "AI.MAP":
         if len(args) < 2:
             raise QueryError("AI.MAP takes an input and an instruction")
@@ -297,10 +354,17 @@ def bind_call(node, turn: P.Turn) -> BoundCall:
 # ---------------------------------------------------------------- the executor
 
 class Executor:
-    def __init__(self, catalog: dict, engine=None, turn: P.Turn = P.Turn(), settings: dict | None = None):
+    def __init__(self, catalog: dict, engine=None, turn: P.Turn | None = None, settings: dict | None = None,
+                 model: P.PromptModel | None = None):
         self.catalog = catalog
         self.engine = engine
-        self.turn = turn
+        cfg = getattr(engine, "cfg", None)
+        if model is None:
+            model = P.prompt_model(cfg) if cfg is not None else P.PromptModel()
+        if turn is not None:
+            model = P.PromptModel(role=model.role, layout=model.layout, turn=turn, name=model.name)
+        self.model = model
+        self.turn = model.turn
         self.settings = settings or {}
         self.ctes: dict = {}
         self.report = {"regions": [], "asked": 0, "fresh_tokens": 0, "passes": 0, "evaluated_documents": 0}
@@ -439,7 +503,7 @@ class Executor:
             else:
                 others.append(c)
         if filters:
-            bound = [bind_call(f, self.turn) for f in filters]
+            bound = [bind_call(f, self.turn, self.model) for f in filters]
             # the most selective hinted filter first
             order = sorted(range(len(bound)), key=lambda i: bound[i].selectivity if bound[i].selectivity is not None
                            else 1.0)
@@ -476,7 +540,7 @@ class Executor:
                 if is_model_call(n):
                     k = node_key(n)
                     if k not in calls and k not in self.ai_values:
-                        calls[k] = bind_call(n, self.turn)
+                        calls[k] = bind_call(n, self.turn, self.model)
         if not calls:
             return
         groups = {}
@@ -521,7 +585,8 @@ class Executor:
             raise QueryError("this query needs a model; the session has none")
         from quail_b200.api.engine import CallSpec
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
-                          probabilities=c.probabilities, pooling=c.pooling) for c in calls]
+                          probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read)
+                 for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self.report["regions"].append(out.stats)
         for k in ("asked", "fresh_tokens", "passes"):

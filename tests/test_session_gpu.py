@@ -37,3 +37,36 @@ def test_classify_map_and_score_on_the_kernels(session):
     assert all(0.0 <= s <= 1.0 for s in t.column("s").to_pylist())
     assert set(t.column("k").to_pylist()) <= {"praise", "complaint"}
     assert all(isinstance(m, str) for m in t.column("m").to_pylist())
+
+
+
+def test_decision_model_on_the_kernels():
+    """A decision model (Qwen3 backbone on the bf16 kernels + option-scoring head) against
+    the same weights in the fp32 reference model: same SQL, scores to bf16 accuracy."""
+    import torch
+    from quail_b200.api.engine import ModelEngine
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.models.build import random_checkpoint_on
+    from quail_b200.models.qwen3 import Qwen3Reference
+    rng = np.random.default_rng(1)
+    words = ["refund", "late", "broken", "great", "thanks", "order"]
+    bodies = [" ".join(rng.choice(words, size=int(rng.integers(3, 30)))) for _ in range(12)]
+    q = ("SELECT id, AI.SCORE(PROMPT('Refund request? {0}', body)) AS s, "
+         "AI.CLASSIFY(body, ['billing', 'shipping']) AS c FROM t ORDER BY id")
+    cfg = quail.EngineConfig(model="decision-gpu-tiny", device="b200", chunk_tokens=2048)
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": list(range(12)), "body": bodies}))
+        got = s.sql(q).collect()
+        eng = s.engine()
+        m = eng.cfg
+        ref_model = Qwen3Reference(m, random_checkpoint_on(m, eng.device, seed=0), device=eng.device)
+        ref_model.decision = eng.model.decision
+        arena = KVArena(m.layers, 256, 16, m.num_kv_heads, m.head_dim, device=eng.device, dtype=torch.float32)
+        s._engine = ModelEngine.from_replica(cfg, ref_model, arena, tokenizer=eng.tokenizer)
+        want = s.sql(q).collect()
+        s._engine = eng
+    a, b = np.array(got.column("s").to_pylist()), np.array(want.column("s").to_pylist())
+    assert np.all((a >= 0) & (a <= 1))
+    np.testing.assert_allclose(a, b, atol=0.03)
+    agree = np.mean(np.array(got.column("c").to_pylist()) == np.array(want.column("c").to_pylist()))
+    assert agree >= 0.9
