@@ -17,6 +17,7 @@ the arena, bind answer rows), executor/runtime.py and executor/region.py.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -139,6 +140,9 @@ class ModelEngine:
                              device=self.device, dtype=dtype)
         self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
                                       gpu_timing=self.config.gpu_timing)
+        if self.on_gpu and os.environ.get("QB_GRAPHS", "1") != "0":
+            # decode passes (AI.MAP / AI.EXTRACT steps) replay captured CUDA graphs
+            self.executor.enable_graphs()
 
     def _set_answer_rows(self, ids):
         w = getattr(self.model, "w", None)

@@ -25,6 +25,8 @@ import torch
 
 MAX_SEGMENTS = 4
 SEQ_INTS = 12
+# the metadata arrays in upload order
+PARTS = ("ids", "positions", "slots", "seqs", "tiles", "page_list", "final_rows", "dseqs", "state_io")
 ATTN_BLOCK_Q = 32
 
 
@@ -74,6 +76,25 @@ class ChunkPacker:
         self._staging: torch.Tensor | None = None
 
     def pack(self, specs: list[SeqSpec]) -> Chunk:
+        host, tags = self.host_parts(specs)
+        n_tok = host["ids"].size
+        parts = [host[k] for k in PARTS]
+        sizes = [p.size for p in parts]
+        flat = np.concatenate([p.reshape(-1) for p in parts]) if n_tok else np.zeros(0, dtype=np.int32)
+        dev = self._upload(flat)
+        views = []
+        o = 0
+        for sz in sizes:
+            views.append(dev[o:o + sz])
+            o += sz
+        return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
+                     seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
+                     final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2), readout_tags=tags,
+                     num_seqs=len(specs), host=host, upload_bytes=int(flat.nbytes),
+                     full_readout=any(s.full and s.readout for s in specs))
+
+    def host_parts(self, specs: list[SeqSpec]) -> tuple[dict, list]:
+        """The chunk's metadata as numpy arrays (keys of PARTS) and its readout tags."""
         P = self.pool.page_tokens
         n_tok = sum(len(s.tokens) for s in specs)
         ids = np.empty(n_tok, dtype=np.int32)
@@ -133,21 +154,9 @@ class ChunkPacker:
         pl = np.asarray(page_list, dtype=np.int32)
         fr = np.asarray(final_rows, dtype=np.int32)
         ds = np.asarray(dseqs, dtype=np.int32)
-        parts = [ids, pos, slots, seqs.reshape(-1), tiles_a.reshape(-1), pl, fr, ds, state_io.reshape(-1)]
-        sizes = [p.size for p in parts]
-        flat = np.concatenate(parts) if n_tok else np.zeros(0, dtype=np.int32)
-        dev = self._upload(flat)
-        views = []
-        o = 0
-        for sz in sizes:
-            views.append(dev[o:o + sz])
-            o += sz
         host = {"ids": ids, "positions": pos, "slots": slots, "seqs": seqs, "tiles": tiles_a,
                 "page_list": pl, "final_rows": fr, "dseqs": ds, "state_io": state_io}
-        return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
-                     seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
-                     final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2), readout_tags=tags, num_seqs=len(specs), host=host,
-                     upload_bytes=int(flat.nbytes), full_readout=any(s.full and s.readout for s in specs))
+        return host, tags
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:
         src = torch.from_numpy(flat)

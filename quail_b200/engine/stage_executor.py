@@ -66,6 +66,14 @@ class Task:
 
 
 @dataclass
+class _Replayed:
+    """What the executor keeps of a pass that ran as a graph replay."""
+
+    num_tokens: int
+    upload_bytes: int
+
+
+@dataclass
 class ExecutorStats:
     passes: int = 0
     tokens: int = 0
@@ -96,6 +104,7 @@ class StageExecutor:
         self.written: dict = {}     # key -> tokens written by launched chunks
         self.stats = ExecutorStats()
         self.gpu_timing = gpu_timing and self.device.type == "cuda"
+        self.graphs = None        # engine.graphs.DecodeGraphs once enable_graphs() is called
         self._inflight: deque = deque()
         self.should_stop: Callable | None = None   # checked between passes (cancel / timeout)
 
@@ -202,13 +211,27 @@ class StageExecutor:
         return specs
 
     # ------------------------------------------------------------ run
+    def enable_graphs(self) -> None:
+        """Run decode passes (one token per sequence) as CUDA graph replays (engine/graphs.py)."""
+        if self.device.type == "cuda" and self.graphs is None:
+            from quail_b200.engine.graphs import DecodeGraphs
+            self.graphs = DecodeGraphs(self.model, self.arena, self.device)
+
     def _launch(self, specs: list[SeqSpec]):
-        chunk = self.packer.pack(specs)
         ev0 = ev1 = None
         if self.gpu_timing:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        logits = self.model.forward_chunk(chunk, self.arena)
+        res = None
+        if self.graphs is not None and self.graphs.eligible(specs):
+            host, _ = self.packer.host_parts(specs)
+            res = self.graphs.run(host, any(s.full and s.readout for s in specs))
+        if res is not None:
+            logits, nbytes = res
+            chunk = _Replayed(num_tokens=len(specs), upload_bytes=nbytes)
+        else:
+            chunk = self.packer.pack(specs)
+            logits = self.model.forward_chunk(chunk, self.arena)
         if self.gpu_timing:
             ev1.record()
         for s in specs:

@@ -87,8 +87,12 @@ class Qwen3Weights:
     def set_answer_rows(self, token_ids) -> None:
         """Retain the LM-head rows of the answer tokens (yes/no or labels)."""
         ids = torch.as_tensor(list(token_ids), dtype=torch.long)
-        self.answer_rows = self.head.index_select(0, ids.to(self.head.device)).to(
-            device=self.device, dtype=torch.bfloat16).contiguous()
+        rows = self.head.index_select(0, ids.to(self.head.device)).to(device=self.device, dtype=torch.bfloat16)
+        old = getattr(self, "answer_rows", None)
+        if old is not None and old.shape == rows.shape:
+            old.copy_(rows)      # same buffer: captured decode graphs stay valid
+        else:
+            self.answer_rows = rows.contiguous()
         self.answer_ids = ids
 
 
