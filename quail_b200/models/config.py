@@ -197,8 +197,12 @@ DECISION_GPU_TINY = QWEN3_GPU_TINY.with_(name="decision-gpu-tiny", role="decisio
                                          decision_head_dim=128, weight_dtype="bf16")
 RERANKER_TINY = QWEN3_TINY.with_(name="reranker-tiny", role="reranker", weight_dtype="bf16")
 QWEN35_9B = QWEN35_4B.with_(name="qwen3.5-9b", hidden=4096, intermediate=12288, tied_head=False)
+QWEN35_4B_FP8 = QWEN35_4B.with_(name="qwen3.5-4b-fp8", weight_dtype="fp8")
+QWEN35_GPU_TINY_FP8 = QWEN35_GPU_TINY.with_(name="qwen3.5-gpu-tiny-fp8", weight_dtype="fp8")
 QWEN35_27B = QWEN35_4B.with_(name="qwen3.5-27b", layers=64, hidden=5120, num_q_heads=24, num_kv_heads=4,
                              intermediate=17408, tied_head=False, gdn_value_heads=48, layer_kinds=_Q35_KINDS * 16)
+QWEN35_27B_FP8 = QWEN35_27B.with_(name="qwen3.5-27b-fp8", weight_dtype="fp8")
+QWEN38_27B_FP8 = QWEN35_27B_FP8.with_(name="qwen3.8-27b-fp8")
 QWEN35_2B_SAE = QWEN35_4B.with_(name="qwen3.5-2b-sae", layers=12, hidden=2048, num_q_heads=8, num_kv_heads=2,
                                 intermediate=6144, gdn_value_heads=16, layer_kinds=_Q35_KINDS * 3,
                                 sae_features=32768, sae_keep=100)
@@ -208,7 +212,8 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
                                QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
-                               QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY)}
+                               QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY,
+                               QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, QWEN35_27B_FP8, QWEN38_27B_FP8)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -239,4 +244,8 @@ MODEL_CONFIGS = {
     "decision-tiny": DECISION_TINY,
     "decision-gpu-tiny": DECISION_GPU_TINY,
     "reranker-tiny": RERANKER_TINY,
+    "qwen3.5-4b-fp8": QWEN35_4B_FP8,
+    "qwen3.5-gpu-tiny-fp8": QWEN35_GPU_TINY_FP8,
+    "qwen3.5-27b-fp8": QWEN35_27B_FP8,
+    "qwen3.8-27b-fp8": QWEN38_27B_FP8,
 }

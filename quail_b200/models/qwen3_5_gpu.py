@@ -1,6 +1,7 @@
 """Qwen3.5 hybrid decoder on the sm_100a kernels (bf16 weights).
 
-Per layer, on our kernels:
+Per layer, on our kernels (fp8 checkpoints: attention and MLP GEMMs on the
+block-scaled fp8 tcgen05 GEMM with MX activations, Gated DeltaNet in bf16):
   RMSNorm (bf16 out) ->
     Gated DeltaNet: in-projection GEMM [qkv | z | b | a] -> gdn_layer (causal
       conv + L2 norm, delta-rule recurrence over the state slots, gated RMSNorm)
@@ -38,7 +39,7 @@ class Qwen35Pipeline:
     """Forward pass of a packed chunk of a Qwen3.5 hybrid on the GPU kernels."""
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None):
-        from quail_b200.ops.quant import interleave_gate_up
+        from quail_b200.ops.quant import interleave_gate_up, interleave_gate_up_mx, quantize_weight_mx
         assert cfg.is_hybrid
         self.cfg = cfg
         self.device = device
@@ -49,8 +50,16 @@ class Qwen35Pipeline:
         def norm_w(t):
             return (t.float() + off).to(device=dev, dtype=bf)
 
+        def fp32(name):
+            return dequantized(ckpt, name).to(device=dev)
+
         def proj(name):
-            return dequantized(ckpt, name).to(device=dev, dtype=bf)
+            return fp32(name).to(bf)
+
+        # fp8 checkpoints: attention and MLP projections on the block-scaled fp8
+        # GEMM (requantized to power-of-two 128x128 blocks); the Gated DeltaNet
+        # projections stay bf16
+        self.fp8 = cfg.fp8
 
         self.embed = ckpt["model.embed_tokens.weight"].to(device=dev, dtype=bf).contiguous()
         self.final_norm = norm_w(ckpt["model.norm.weight"])
@@ -70,13 +79,22 @@ class Qwen35Pipeline:
                 L["norm"] = ckpt[q + "norm.weight"].to(device=dev, dtype=bf).contiguous()
             else:
                 q = p + "self_attn."
-                L["wqkv"] = _pad_rows(torch.cat([proj(q + "q_proj"), proj(q + "k_proj"), proj(q + "v_proj")]))
-                L["wo"] = proj(q + "o_proj").contiguous()
+                qkv = torch.cat([fp32(q + "q_proj"), fp32(q + "k_proj"), fp32(q + "v_proj")])
+                if self.fp8:
+                    L["wqkv"], L["sqkv"] = quantize_weight_mx(qkv)
+                    L["wo"], L["so"] = quantize_weight_mx(fp32(q + "o_proj"))
+                else:
+                    L["wqkv"] = _pad_rows(qkv.to(bf))
+                    L["wo"] = proj(q + "o_proj").contiguous()
                 L["qn"] = ckpt[q + "q_norm.weight"].to(device=dev, dtype=bf).contiguous()
                 L["kn"] = ckpt[q + "k_norm.weight"].to(device=dev, dtype=bf).contiguous()
-            gu = torch.cat([proj(p + "mlp.gate_proj"), proj(p + "mlp.up_proj")])
-            L["wgu"] = interleave_gate_up(gu)
-            L["wd"] = proj(p + "mlp.down_proj").contiguous()
+            gu = torch.cat([fp32(p + "mlp.gate_proj"), fp32(p + "mlp.up_proj")])
+            if self.fp8:
+                L["wgu"], L["sgu"] = interleave_gate_up_mx(gu)
+                L["wd"], L["sd"] = quantize_weight_mx(fp32(p + "mlp.down_proj"))
+            else:
+                L["wgu"] = interleave_gate_up(gu.to(bf))
+                L["wd"] = proj(p + "mlp.down_proj").contiguous()
             self.layers.append(L)
         self.head = head_weight(ckpt, cfg)
         if cfg.has_sae:
@@ -111,8 +129,8 @@ class Qwen35Pipeline:
         h = ops.embed_gather(chunk.ids, self.embed)
         gi = ai = 0
         for i, L in enumerate(self.layers):
-            x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
             if cfg.kind(i) == "gdn":
+                x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
                 p = ops.gemm(x, L["win"])
                 conv_out = torch.empty(T, cfg.gdn_conv_dim, dtype=torch.float32, device=dev)
                 o = torch.empty(T, Hv * dv, dtype=torch.float32, device=dev)
@@ -123,7 +141,11 @@ class Qwen35Pipeline:
                 ops.gemm(y, L["wout"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 gi += 1
             else:
-                p = ops.gemm(x, L["wqkv"])
+                if self.fp8:
+                    x8, xs = ops.rmsnorm_quant_mx(h, L["ln1"], cfg.rms_eps)
+                    p = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
+                else:
+                    p = ops.gemm(ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False), L["wqkv"])
                 kc, vc = arena.layer(ai)
                 q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=dev)
                 ops.count_launch(1)
@@ -134,8 +156,17 @@ class Qwen35Pipeline:
                 ops.count_launch(int(chunk.tiles.shape[0] > 0) + int(chunk.dseqs.numel() > 0))
                 C.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
                                   gate, 2 * D)
-                ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                if self.fp8:
+                    o8, os_ = ops.quant_rows_mx(o)
+                    ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                else:
+                    ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 ai += 1
+            if self.fp8:
+                x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
+                a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
+                ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                continue
             x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
             a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
             ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)

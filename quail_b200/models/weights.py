@@ -49,9 +49,9 @@ def _rand(shape, std, gen, device, dtype=torch.float32):
     return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std).to(dtype)
 
 
-def _emit_proj(name, shape, cfg, gen, device, dtype):
+def _emit_proj(name, shape, cfg, gen, device, dtype, fp8: bool | None = None):
     w = _rand(shape, cfg.init_std, gen, device)
-    if cfg.fp8:
+    if cfg.fp8 if fp8 is None else fp8:
         q, s = quantize_weight(w)
         return {name + ".weight": q, name + ".weight_scale_inv": s}
     return {name + ".weight": w.to(dtype)}
@@ -123,7 +123,8 @@ def _iter_gdn(cfg: DecoderConfig, p: str, gen: torch.Generator, device, dtype):
     """A Gated DeltaNet layer: projections, depthwise conv, decay (A_log, dt_bias), gated-norm weight."""
     Hv = cfg.gdn_value_heads
     for name, shape in gdn_shapes(cfg).items():
-        yield from _emit_proj(p + name, shape, cfg, gen, device, dtype).items()
+        # Gated DeltaNet projections stay bf16 in the fp8 checkpoints (gdn_weight_precision = "bf16")
+        yield from _emit_proj(p + name, shape, cfg, gen, device, dtype, fp8=False).items()
     yield p + "linear_attn.conv1d.weight", _rand((cfg.gdn_conv_dim, 1, cfg.conv_width), 0.3, gen, device, dtype)
     # per-head decay rate A in [1, 16] and step dt in [1e-3, 1e-1] (softplus(dt_bias) = dt)
     a = 1.0 + 15.0 * torch.rand(Hv, generator=gen, device=device)
@@ -240,10 +241,15 @@ def load_checkpoint(directory: str, device="cpu") -> dict[str, torch.Tensor]:
 
 
 def dequantized(ckpt: dict[str, torch.Tensor], name: str) -> torch.Tensor:
-    """fp32 value of a projection weight, whatever its stored format."""
+    """fp32 value of a projection weight, whatever its stored format: plain, fp8 with
+    128x128 block scales (`weight_scale_inv`), or fp8 with per-channel scales
+    (`weight_scale`, the FP8-dynamic checkpoints)."""
     w = ckpt[name + ".weight"]
     s = ckpt.get(name + ".weight_scale_inv")
     if s is None:
+        pc = ckpt.get(name + ".weight_scale")
+        if pc is not None:
+            return w.float() * pc.float().reshape(-1, 1).to(w.device)
         return w.float()
     from quail_b200.ops.quant import dequantize_weight
     return dequantize_weight(w, s)

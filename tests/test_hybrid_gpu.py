@@ -130,13 +130,16 @@ def test_gdn_layer_against_recurrence(dk):
         assert rel_err(y[a:a + n].view(n, Hv, dv), want_y) < 1e-2
 
 
-def test_hybrid_pipeline_matches_fp32_model():
+@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.5-gpu-tiny-fp8"])
+def test_hybrid_pipeline_matches_fp32_model(name):
+    """bf16 and fp8 checkpoints (the fp8 one: attention and MLP on the block-scaled fp8 GEMM)
+    against the fp32 model of the same (dequantized) weights."""
     from quail_b200.engine.arena import KVArena
     from quail_b200.engine.stage_executor import StageExecutor, Task
-    from quail_b200.models.config import QWEN35_GPU_TINY
+    from quail_b200.models.config import MODEL_CONFIGS
     from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline
     from quail_b200.models.weights import random_checkpoint
-    cfg = QWEN35_GPU_TINY
+    cfg = MODEL_CONFIGS[name]
     ckpt = random_checkpoint(cfg, seed=9, device=DEV)
     ids = list(range(16))
     pipe = Qwen35Pipeline(cfg, ckpt, DEV, head_rows=ids)
@@ -161,7 +164,7 @@ def test_hybrid_pipeline_matches_fp32_model():
     want = run(exact, torch.float32)
     assert ops.read_and_clear_error(0) == 0
     d = rel_err(got, want)
-    print(f"hybrid kernel-vs-fp32: {d:.4f}")
+    print(f"hybrid {name} kernel-vs-fp32: {d:.4f}")
     assert d < 0.1
 
 
