@@ -93,7 +93,11 @@ class PagePool:
     def grow(self, key, tokens: int):
         """Extend a resident key to `tokens` tokens; returns the new pages or None."""
         have = self.owned[key]
-        need = self.pages_needed(tokens) - len(have)
+        need = -(-tokens // self.page_tokens) - len(have)
+        if need <= 0:
+            if tokens > self.tokens[key]:
+                self.tokens[key] = tokens
+            return []
         if need > len(self.free):
             return None
         new = [self.free.pop() for _ in range(max(need, 0))]

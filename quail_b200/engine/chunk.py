@@ -94,68 +94,85 @@ class ChunkPacker:
                      full_readout=any(s.full and s.readout for s in specs))
 
     def host_parts(self, specs: list[SeqSpec]) -> tuple[dict, list]:
-        """The chunk's metadata as numpy arrays (keys of PARTS) and its readout tags."""
+        """The chunk's metadata as numpy arrays (keys of PARTS) and its readout tags.
+
+        Built in Python lists and converted once: a decode pass has a thousand
+        one-token sequences, so per-sequence numpy calls would dominate."""
         P = self.pool.page_tokens
-        n_tok = sum(len(s.tokens) for s in specs)
-        ids = np.empty(n_tok, dtype=np.int32)
-        pos = np.empty(n_tok, dtype=np.int32)
-        slots = np.empty(n_tok, dtype=np.int32)
-        seqs = np.zeros((len(specs), SEQ_INTS), dtype=np.int32)
-        state_io = np.full((len(specs), 2), -1, dtype=np.int32)
+        owned = self.pool.owned
+        ids: list[int] = []
+        pos: list[int] = []
+        slots: list[int] = []
+        seqs: list[int] = []
+        state_io: list[int] = []
         slots_on = self.pool.state_slots > 0
+        slot_of = self.pool.slot_of if slots_on else None
         page_list: list[int] = []
         seg_cache: dict = {}
-        tiles: list[tuple[int, int]] = []
+        tiles: list[int] = []
         dseqs: list[int] = []
         final_rows: list[int] = []
         tags: list = []
+        split = self.split_decode
         q = 0
         for si, s in enumerate(specs):
-            n = len(s.tokens)
-            if len(s.reads) + 1 > MAX_SEGMENTS:
+            toks = s.tokens
+            n = len(toks)
+            reads = s.reads
+            nr = len(reads)
+            if nr + 1 > MAX_SEGMENTS:
                 raise ValueError(f"a sequence reads at most {MAX_SEGMENTS - 1} earlier segments")
-            ids[q:q + n] = s.tokens
-            pos[q:q + n] = s.pos_start + np.arange(n, dtype=np.int32)
-            own_pages = np.asarray(self.pool.pages_of(s.own_key), dtype=np.int64)
-            j = s.own_start + np.arange(n)
-            slots[q:q + n] = (own_pages[j // P] * P + j % P).astype(np.int32)
-            row = seqs[si]
-            row[0], row[1], row[2] = q, n, len(s.reads) + 1
+            own = owned[s.own_key]
+            j0 = s.own_start
+            if n == 1:
+                ids.append(int(toks[0]))
+                pos.append(s.pos_start)
+                slots.append(own[j0 // P] * P + j0 % P)
+            else:
+                ids.extend(toks.tolist() if hasattr(toks, "tolist") else toks)
+                pos.extend(range(s.pos_start, s.pos_start + n))
+                slots.extend(own[j // P] * P + j % P for j in range(j0, j0 + n))
+            row = [q, n, nr + 1, 0, 0, 0, 0, 0, 0, 0, 0, 0]
             if slots_on:
                 # continue the key's own state, else start from the last segment it reads
-                dst = self.pool.slot_of[s.own_key]
-                src = dst if s.own_start > 0 else (self.pool.slot_of[s.reads[-1][0]] if s.reads else -1)
-                state_io[si] = (src, dst)
-            for i, (key, ln) in enumerate(s.reads):
+                dst = slot_of[s.own_key]
+                src = dst if j0 > 0 else (slot_of[reads[-1][0]] if reads else -1)
+                state_io += (src, dst)
+            for i, (key, ln) in enumerate(reads):
                 npg = -(-ln // P)
                 ck = (key, npg)
                 off = seg_cache.get(ck)
                 if off is None:
                     off = len(page_list)
-                    page_list.extend(self.pool.pages_of(key)[:npg])
+                    page_list.extend(owned[key][:npg])
                     seg_cache[ck] = off
-                row[4 + i], row[8 + i] = ln, off
-            own_len = s.own_start + n
-            npg = -(-own_len // P)
-            row[4 + len(s.reads)] = own_len
-            row[8 + len(s.reads)] = len(page_list)
-            page_list.extend(self.pool.pages_of(s.own_key)[:npg])
-            if n == 1 and self.split_decode:
+                row[4 + i] = ln
+                row[8 + i] = off
+            own_len = j0 + n
+            row[4 + nr] = own_len
+            row[8 + nr] = len(page_list)
+            page_list.extend(own[:-(-own_len // P)])
+            seqs += row
+            if n == 1 and split:
                 dseqs.append(si)
             else:
-                tiles.extend((si, q0) for q0 in range(0, n, ATTN_BLOCK_Q))
+                for q0 in range(0, n, ATTN_BLOCK_Q):
+                    tiles += (si, q0)
             if s.readout:
-                offs = s.readout_rows if s.readout_rows is not None else (n - 1,)
-                for o in offs:
-                    final_rows.append(q + o)
+                if s.readout_rows is None:
+                    final_rows.append(q + n - 1)
+                else:
+                    final_rows.extend(q + o for o in s.readout_rows)
                 tags.append(s.tag)
             q += n
-        tiles_a = np.asarray(tiles, dtype=np.int32).reshape(-1, 2)
-        pl = np.asarray(page_list, dtype=np.int32)
-        fr = np.asarray(final_rows, dtype=np.int32)
-        ds = np.asarray(dseqs, dtype=np.int32)
-        host = {"ids": ids, "positions": pos, "slots": slots, "seqs": seqs, "tiles": tiles_a,
-                "page_list": pl, "final_rows": fr, "dseqs": ds, "state_io": state_io}
+        i32 = np.int32
+        S = len(specs)
+        sio = np.asarray(state_io, dtype=i32).reshape(S, 2) if slots_on else np.full((S, 2), -1, dtype=i32)
+        host = {"ids": np.asarray(ids, dtype=i32), "positions": np.asarray(pos, dtype=i32),
+                "slots": np.asarray(slots, dtype=i32), "seqs": np.asarray(seqs, dtype=i32).reshape(S, SEQ_INTS),
+                "tiles": np.asarray(tiles, dtype=i32).reshape(-1, 2), "page_list": np.asarray(page_list, dtype=i32),
+                "final_rows": np.asarray(final_rows, dtype=i32), "dseqs": np.asarray(dseqs, dtype=i32),
+                "state_io": sio}
         return host, tags
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:

@@ -40,6 +40,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
+from functools import partial
 
 import numpy as np
 
@@ -150,7 +151,7 @@ class RegionRun:
         elif call.kind == "classify":
             self._classify_first(r, ci, row)
         elif call.kind in ("map", "extract"):
-            self._decode_step(r, ci, row, generated=[])
+            self._decode_step(r, ci, row, [])
         elif call.kind == "features":
             res.values[call.name] = feature_list(row)
             self._finish_call(r, ci)
@@ -201,12 +202,13 @@ class RegionRun:
         self._finish_call(r, ci)
 
     def _decode_step(self, r, ci, row, generated):
+        """One greedy step of row r's call ci; `generated` is the row's token list (appended in place)."""
         call = self.calls[ci]
-        arg_col, _ = self._full_cols(row)
-        tok = int(round(float(row[arg_col])))
+        arg_col = self.nans if self.nans is not None else len(row) - 2
+        tok = int(round(float(row.numpy()[arg_col] if hasattr(row, "numpy") else row[arg_col])))
         stop = tok in call.stop_ids
         if not stop:
-            generated = generated + [tok]
+            generated.append(tok)
         if stop or len(generated) >= call.max_tokens:
             self.results[r].values[call.name] = generated
             self._finish_call(r, ci)
@@ -214,10 +216,12 @@ class RegionRun:
         key, reads, pos, own_len = self._question(r, ci)
         n_prev = len(generated) - 1
         self.fresh_tokens += 1
-        self.ex.submit(Task(key=key, tokens=np.asarray([tok], dtype=np.int32), pos_start=pos + own_len + n_prev,
-                            reads=reads, readout=True, full_readout=True, own_prefix=own_len + n_prev,
-                            free_after=False,
-                            on_done=lambda t, row, r=r, ci=ci, g=generated: self._decode_step(r, ci, row, g)))
+        self.ex.submit_continuation(Task(key=key, tokens=[tok], pos_start=pos + own_len + n_prev, reads=reads,
+                                         readout=True, full_readout=True, own_prefix=own_len + n_prev,
+                                         free_after=False, on_done=partial(self._decode_next, r, ci, generated)))
+
+    def _decode_next(self, r, ci, generated, task, row):
+        self._decode_step(r, ci, row, generated)
 
     # ------------------------------------------------------------ scheduling
     def _finish_call(self, r: int, ci: int) -> None:

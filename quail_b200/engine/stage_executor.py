@@ -119,6 +119,10 @@ class StageExecutor:
         else:
             self.queue.append(task)
 
+    def submit_continuation(self, task: Task) -> None:
+        """A continuation of a resident key (a decode step): straight to the continuation queue."""
+        self.cont.append(task)
+
     def free(self, key) -> None:
         self.pool.free_key(key)
         self.written.pop(key, None)
@@ -131,24 +135,24 @@ class StageExecutor:
         room = self.chunk_tokens
         specs: list[SeqSpec] = []
         # continuations first: each is one or a few tokens of a resident key
-        while self.cont and room > 0:
-            if self.max_seqs is not None and len(specs) >= self.max_seqs:
+        cont, pool = self.cont, self.pool
+        max_seqs = self.max_seqs if self.max_seqs is not None else 1 << 30
+        while cont and room > 0 and len(specs) < max_seqs:
+            task = cont[0]
+            n = len(task.tokens)
+            total = task.own_prefix + n
+            if n > room:
                 break
-            task = self.cont[0]
-            total = task.own_prefix + len(task.tokens)
-            if len(task.tokens) > room:
-                break
-            if self.pool.tokens[task.key] < total and self.pool.grow(task.key, total) is None:
-                self.pool.evict_retained(self.pool.pages_needed(total))
-                if self.pool.grow(task.key, total) is None:
+            if pool.tokens[task.key] < total and pool.grow(task.key, total) is None:
+                pool.evict_retained(pool.pages_needed(total))
+                if pool.grow(task.key, total) is None:
                     break
-            self.cont.popleft()
+            cont.popleft()
             rows = tuple(task.readout_rows) if task.readout and task.readout_rows is not None else None
-            specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix,
-                                 tokens=task.tokens, pos_start=task.pos_start, readout=task.readout, tag=task,
-                                 readout_rows=rows, full=task.full_readout))
-            task.done = len(task.tokens)
-            room -= len(task.tokens)
+            specs.append(SeqSpec(task.reads, task.key, task.own_prefix, task.tokens, task.pos_start, task.readout,
+                                 task, rows, task.full_readout))
+            task.done = n
+            room -= n
         deferred: list[Task] = []
         scanned = 0
         no_new = False

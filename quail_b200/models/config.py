@@ -27,6 +27,8 @@ class DecoderConfig:
     num_experts: int = 0
     top_k: int = 0
     moe_intermediate: int = 0
+    # a shared expert beside the routed ones, scaled per token by sigmoid(x . w_gate) (Qwen3.5 MoE); 0 = none
+    shared_intermediate: int = 0
     max_position: int = 40_960
     init_std: float = 0.02
     # sparse autoencoder on the residual stream after the last loaded layer
@@ -203,6 +205,19 @@ QWEN35_27B = QWEN35_4B.with_(name="qwen3.5-27b", layers=64, hidden=5120, num_q_h
                              intermediate=17408, tied_head=False, gdn_value_heads=48, layer_kinds=_Q35_KINDS * 16)
 QWEN35_27B_FP8 = QWEN35_27B.with_(name="qwen3.5-27b-fp8", weight_dtype="fp8")
 QWEN38_27B_FP8 = QWEN35_27B_FP8.with_(name="qwen3.8-27b-fp8")
+# Qwen3.6-35B-A3B: the Qwen3.5 hybrid with 256 routed experts (top 8) and a shared expert
+# (the reference spec quail/specs/data/models/qwen3.6-35b-a3b-fp8.toml; HF Qwen3_5MoeSparseMoeBlock)
+QWEN36_35B_A3B = QWEN35_4B.with_(name="qwen3.6-35b-a3b-fp8", layers=40, hidden=2048, num_q_heads=16,
+                                 num_kv_heads=2, intermediate=512, tied_head=False, weight_dtype="fp8",
+                                 num_experts=256, top_k=8, moe_intermediate=512, shared_intermediate=512,
+                                 layer_kinds=_Q35_KINDS * 10)
+QWEN36_MOE_GPU_TINY = QWEN36_35B_A3B.with_(name="qwen3.6-moe-gpu-tiny", layers=4, hidden=1024, num_q_heads=4,
+                                           num_kv_heads=2, vocab=4096, num_experts=16, top_k=4,
+                                           gdn_key_heads=2, gdn_value_heads=4, layer_kinds=_Q35_KINDS,
+                                           max_position=8192, moe_intermediate=256, shared_intermediate=256)
+QWEN36_MOE_TINY = QWEN36_MOE_GPU_TINY.with_(name="qwen3.6-moe-tiny", hidden=256, head_dim=64, num_experts=8,
+                                            top_k=2, moe_intermediate=128, shared_intermediate=128,
+                                            gdn_key_dim=32, gdn_value_dim=32, weight_dtype="bf16")
 QWEN35_2B_SAE = QWEN35_4B.with_(name="qwen3.5-2b-sae", layers=12, hidden=2048, num_q_heads=8, num_kv_heads=2,
                                 intermediate=6144, gdn_value_heads=16, layer_kinds=_Q35_KINDS * 3,
                                 sae_features=32768, sae_keep=100)
@@ -213,7 +228,8 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
                                QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY,
-                               QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, QWEN35_27B_FP8, QWEN38_27B_FP8)}
+                               QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, QWEN35_27B_FP8, QWEN38_27B_FP8,
+                               QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -248,4 +264,7 @@ MODEL_CONFIGS = {
     "qwen3.5-gpu-tiny-fp8": QWEN35_GPU_TINY_FP8,
     "qwen3.5-27b-fp8": QWEN35_27B_FP8,
     "qwen3.8-27b-fp8": QWEN38_27B_FP8,
+    "qwen3.6-35b-a3b-fp8": QWEN36_35B_A3B,
+    "qwen3.6-moe-gpu-tiny": QWEN36_MOE_GPU_TINY,
+    "qwen3.6-moe-tiny": QWEN36_MOE_TINY,
 }

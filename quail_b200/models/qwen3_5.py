@@ -108,9 +108,21 @@ class Qwen35Reference:
         self.layers = []
         for i in range(cfg.layers):
             p = f"model.layers.{i}."
-            L = {"ln1": f(ckpt[p + "input_layernorm.weight"]), "ln2": f(ckpt[p + "post_attention_layernorm.weight"]),
-                 "wg": f(dequantized(ckpt, p + "mlp.gate_proj")), "wu": f(dequantized(ckpt, p + "mlp.up_proj")),
-                 "wd": f(dequantized(ckpt, p + "mlp.down_proj"))}
+            L = {"ln1": f(ckpt[p + "input_layernorm.weight"]), "ln2": f(ckpt[p + "post_attention_layernorm.weight"])}
+            if cfg.is_moe:
+                m = p + "mlp."
+                L["router"] = f(ckpt[m + "gate.weight"])
+                L["experts"] = [(f(dequantized(ckpt, m + f"experts.{e}.gate_proj")),
+                                 f(dequantized(ckpt, m + f"experts.{e}.up_proj")),
+                                 f(dequantized(ckpt, m + f"experts.{e}.down_proj"))) for e in range(cfg.num_experts)]
+                if cfg.shared_intermediate:
+                    L["shared"] = (f(dequantized(ckpt, m + "shared_expert.gate_proj")),
+                                   f(dequantized(ckpt, m + "shared_expert.up_proj")),
+                                   f(dequantized(ckpt, m + "shared_expert.down_proj")))
+                    L["shared_gate"] = f(ckpt[m + "shared_expert_gate.weight"])
+            else:
+                L.update(wg=f(dequantized(ckpt, p + "mlp.gate_proj")), wu=f(dequantized(ckpt, p + "mlp.up_proj")),
+                         wd=f(dequantized(ckpt, p + "mlp.down_proj")))
             if cfg.kind(i) == "gdn":
                 q = p + "linear_attn."
                 L.update(qkv=f(dequantized(ckpt, q + "in_proj_qkv")), z=f(dequantized(ckpt, q + "in_proj_z")),
@@ -209,8 +221,23 @@ class Qwen35Reference:
                 h = h + self._attn(x, L, ai, chunk, arena)
                 ai += 1
             x = rmsnorm_offset(h, L["ln2"], cfg.rms_eps)
-            h = h + ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t()
+            h = h + (self._moe(x, L) if cfg.is_moe else ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t())
         return h
+
+    def _moe(self, x, L):
+        """Routed experts (softmax top-k, renormalized) plus the sigmoid-gated shared expert
+        (HF Qwen3_5MoeSparseMoeBlock)."""
+        ids, w = ref.moe_route(x @ L["router"].t(), self.cfg.top_k)
+        out = torch.zeros_like(x)
+        for e in ids.unique().tolist():
+            t, j = (ids == e).nonzero(as_tuple=True)
+            wg, wu, wd = L["experts"][e]
+            xe = x[t]
+            out.index_add_(0, t, (ref.silu_mul(xe @ wg.t(), xe @ wu.t()) @ wd.t()) * w[t, j, None].to(x.dtype))
+        if "shared" in L:
+            wg, wu, wd = L["shared"]
+            out = out + torch.sigmoid(x @ L["shared_gate"].t()) * (ref.silu_mul(x @ wg.t(), x @ wu.t()) @ wd.t())
+        return out
 
     @torch.no_grad()
     def forward_chunk(self, chunk, arena) -> torch.Tensor:

@@ -90,6 +90,11 @@ def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="
     if cfg.is_moe:
         # router logits ~ N(0, 1) per token: gate weight std 1/sqrt(H) on unit-RMS rows
         yield p + "mlp.gate.weight", _rand((cfg.num_experts, H), H ** -0.5, gen, device, dtype)
+        if cfg.shared_intermediate:
+            S = cfg.shared_intermediate
+            for name, shape in (("gate_proj", (S, H)), ("up_proj", (S, H)), ("down_proj", (H, S))):
+                yield from _emit_proj(p + f"mlp.shared_expert.{name}", shape, cfg, gen, device, dtype).items()
+            yield p + "mlp.shared_expert_gate.weight", _rand((1, H), H ** -0.5, gen, device, dtype)
         for e in (experts if experts is not None else range(cfg.num_experts)):
             for name, shape in expert_shapes(cfg).items():
                 yield from _emit_proj(p + f"mlp.experts.{e}.{name}", shape, cfg, gen, device, dtype).items()

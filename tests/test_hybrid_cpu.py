@@ -12,9 +12,10 @@ from quail_b200.models.qwen3_5 import Qwen35Reference, delta_rule
 from quail_b200.models.weights import random_checkpoint
 
 
-@pytest.fixture(scope="module")
-def model():
-    cfg = QWEN35_TINY.with_(vocab=1000, max_position=4096)
+@pytest.fixture(scope="module", params=["qwen3.5-tiny", "qwen3.6-moe-tiny"])
+def model(request):
+    from quail_b200.models.config import MODEL_CONFIGS
+    cfg = MODEL_CONFIGS[request.param].with_(vocab=1000, max_position=4096)
     ckpt = random_checkpoint(cfg, seed=4, dtype=torch.float32)
     return cfg, Qwen35Reference(cfg, ckpt, head_rows=(11, 12, 13, 14))
 

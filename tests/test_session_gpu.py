@@ -61,7 +61,7 @@ def test_decision_model_on_the_kernels():
         m = eng.cfg
         ref_model = Qwen3Reference(m, random_checkpoint_on(m, eng.device, seed=0), device=eng.device)
         ref_model.decision = eng.model.decision
-        arena = KVArena(m.layers, 256, 16, m.num_kv_heads, m.head_dim, device=eng.device, dtype=torch.float32)
+        arena = KVArena(m.layers, 4096, 16, m.num_kv_heads, m.head_dim, device=eng.device, dtype=torch.float32)
         s._engine = ModelEngine.from_replica(cfg, ref_model, arena, tokenizer=eng.tokenizer)
         want = s.sql(q).collect()
         s._engine = eng
