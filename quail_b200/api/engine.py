@@ -112,7 +112,8 @@ class ModelEngine:
                 from quail_b200.models.qwen3_5 import Qwen35Reference as CpuModel
                 from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline as GpuModel
             if self.on_gpu:
-                self.model = GpuModel(self.cfg, ckpt, self.device)
+                kw = {"max_tokens": self.chunk_tokens + 256} if self.cfg.is_moe else {}
+                self.model = GpuModel(self.cfg, ckpt, self.device, **kw)
                 page_tokens, dtype = 128, torch.bfloat16
             else:
                 self.model = CpuModel(self.cfg, ckpt, device="cpu")

@@ -38,7 +38,8 @@ def _pad_rows(w: torch.Tensor, multiple: int = 16) -> torch.Tensor:
 class Qwen35Pipeline:
     """Forward pass of a packed chunk of a Qwen3.5 hybrid on the GPU kernels."""
 
-    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None):
+    def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None,
+                 max_tokens: int = 16384):
         from quail_b200.ops.quant import interleave_gate_up, interleave_gate_up_mx, quantize_weight_mx
         assert cfg.is_hybrid
         self.cfg = cfg
@@ -88,6 +89,10 @@ class Qwen35Pipeline:
                     L["wo"] = proj(q + "o_proj").contiguous()
                 L["qn"] = ckpt[q + "q_norm.weight"].to(device=dev, dtype=bf).contiguous()
                 L["kn"] = ckpt[q + "k_norm.weight"].to(device=dev, dtype=bf).contiguous()
+            if cfg.is_moe:
+                self._moe_weights(L, p + "mlp.", fp32, quantize_weight_mx, interleave_gate_up_mx)
+                self.layers.append(L)
+                continue
             gu = torch.cat([fp32(p + "mlp.gate_proj"), fp32(p + "mlp.up_proj")])
             if self.fp8:
                 L["wgu"], L["sgu"] = interleave_gate_up_mx(gu)
@@ -100,11 +105,52 @@ class Qwen35Pipeline:
         if cfg.has_sae:
             self.sae_w = ckpt["sae.W_enc"].to(device=dev, dtype=bf).contiguous()
             self.sae_b = ckpt["sae.b_enc"].to(device=dev, dtype=torch.float32).contiguous()
+        self.ep = None
+        if cfg.is_moe:
+            from quail_b200.parallel.ep import EPState
+            self.ep = EPState(cfg, max_tokens, dev, None)
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.rotary_dim, cfg.rope_theta, device=dev)
         self.scale = ref.softmax_scale(cfg.head_dim)
         self.answer_rows = None
         if head_rows is not None:
             self.set_answer_rows(head_rows)
+
+    def _moe_weights(self, L, m, fp32, quantize_weight_mx, interleave_gate_up_mx):
+        """Router (bf16), the routed experts stacked in the MX layout the grouped GEMMs read, and
+        the shared expert (MX) with its gate row (bf16, padded to 16 rows for the GEMM)."""
+        cfg, dev = self.cfg, self.device
+        L["router"] = fp32(m + "gate").to(torch.bfloat16).contiguous()
+        gq, gs, dq, ds = [], [], [], []
+        for e in range(cfg.num_experts):
+            q, sc = interleave_gate_up_mx(torch.cat([fp32(m + f"experts.{e}.gate_proj"),
+                                                     fp32(m + f"experts.{e}.up_proj")]))
+            gq.append(q)
+            gs.append(sc)
+            q, sc = quantize_weight_mx(fp32(m + f"experts.{e}.down_proj"))
+            dq.append(q)
+            ds.append(sc)
+        L["wgu"], L["sgu"] = torch.cat(gq).contiguous(), torch.cat(gs).contiguous()
+        L["wd"], L["sd"] = torch.cat(dq).contiguous(), torch.cat(ds).contiguous()
+        if cfg.shared_intermediate:
+            L["wgu_s"], L["sgu_s"] = interleave_gate_up_mx(torch.cat([fp32(m + "shared_expert.gate_proj"),
+                                                                      fp32(m + "shared_expert.up_proj")]))
+            L["wd_s"], L["sd_s"] = quantize_weight_mx(fp32(m + "shared_expert.down_proj"))
+            g = torch.zeros(16, cfg.hidden, dtype=torch.bfloat16, device=dev)
+            g[0] = fp32(m + "shared_expert_gate")[0].to(torch.bfloat16)
+            L["wsg"] = g
+
+    def _moe_mlp(self, h, L):
+        """h += sigmoid(x . w_gate) * shared(x) + sum_k w_k expert_k(x), x = norm(h)."""
+        from quail_b200 import ops
+        cfg = self.cfg
+        x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
+        xb = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+        if "wgu_s" in L:
+            a8, as_ = ops.gemm_mx(x8, xs, L["wgu_s"], L["sgu_s"], epi=ops.EPI_SWIGLU_FP8)
+            sh = ops.gemm_mx(a8, as_, L["wd_s"], L["sd_s"])
+            g = ops.gemm(xb, L["wsg"])
+            h.add_(sh * torch.sigmoid(g[:, :1].float()).to(sh.dtype))
+        self.ep.forward(x8, xs, xb, h, L, next_norm=None, eps=cfg.rms_eps)
 
     def set_answer_rows(self, token_ids) -> None:
         ids = torch.as_tensor(list(token_ids), dtype=torch.long)
@@ -162,6 +208,9 @@ class Qwen35Pipeline:
                 else:
                     ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 ai += 1
+            if self.ep is not None:
+                self._moe_mlp(h, L)
+                continue
             if self.fp8:
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
                 a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)

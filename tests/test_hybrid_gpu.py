@@ -130,7 +130,7 @@ def test_gdn_layer_against_recurrence(dk):
         assert rel_err(y[a:a + n].view(n, Hv, dv), want_y) < 1e-2
 
 
-@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.5-gpu-tiny-fp8"])
+@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.5-gpu-tiny-fp8", "qwen3.6-moe-gpu-tiny"])
 def test_hybrid_pipeline_matches_fp32_model(name):
     """bf16 and fp8 checkpoints (the fp8 one: attention and MLP on the block-scaled fp8 GEMM)
     against the fp32 model of the same (dequantized) weights."""
@@ -168,11 +168,12 @@ def test_hybrid_pipeline_matches_fp32_model(name):
     assert d < 0.1
 
 
-def test_hybrid_session_on_gpu():
+@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.6-moe-gpu-tiny"])
+def test_hybrid_session_on_gpu(name):
     import pyarrow as pa
 
     import quail_b200 as quail
-    cfg = quail.EngineConfig(model="qwen3.5-gpu-tiny", device="b200", chunk_tokens=512)
+    cfg = quail.EngineConfig(model=name, device="b200", chunk_tokens=512)
     t = pa.table({"id": list(range(6)), "body": ["the plot is long", "great music", "bad ending", "short story",
                                                   "money talk", "cast list"]})
     with quail.Session(config=cfg) as s:
