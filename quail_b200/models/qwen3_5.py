@@ -97,11 +97,21 @@ class Qwen35Reference:
     """
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device="cpu", head_rows=None,
-                 dtype=torch.float32):
-        from quail_b200.models.weights import dequantized
+                 dtype=torch.float32, emulate_kernels: bool = False):
+        from quail_b200.models.weights import dequantized as plain
         assert cfg.is_hybrid
         self.cfg = cfg
         self.device = device
+        # emulate_kernels (fp8 checkpoints): the kernels' power-of-two weight
+        # requantization, e4m3 + 1x32 scales on every fp8 GEMM input, and a
+        # bf16 residual stream; the Gated DeltaNet projections stay as stored
+        self.emulate = emulate_kernels and cfg.fp8
+
+        def dequantized(ck, name):
+            if not self.emulate or ".linear_attn." in name or ck.get(name + ".weight_scale_inv") is None:
+                return plain(ck, name)
+            from quail_b200.ops.quant import dequantize_mx, quantize_weight_mx
+            return dequantize_mx(*quantize_weight_mx(plain(ck, name).to(device)))
         f = lambda t: t.to(device=device, dtype=dtype)  # noqa: E731
         self.embed = f(ckpt["model.embed_tokens.weight"])
         self.final_norm = f(ckpt["model.norm.weight"])
@@ -191,6 +201,7 @@ class Qwen35Reference:
         T = x.shape[0]
         QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
         kc, vc = arena.layer(ai)
+        x = self._q(x)
         qg = (x @ L["wq"].t()).view(T, QH, 2 * D if cfg.attn_output_gate else D)
         q, gate = (qg[..., :D], qg[..., D:]) if cfg.attn_output_gate else (qg, None)
         k = (x @ L["wk"].t()).view(T, KH, D)
@@ -204,7 +215,17 @@ class Qwen35Reference:
         o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(x.dtype)
         if gate is not None:
             o = o.view(T, QH, D) * torch.sigmoid(gate.float())
-        return o.reshape(T, QH * D) @ L["wo"].t()
+        return self._q(o.reshape(T, QH * D)) @ L["wo"].t()
+
+    def _q(self, x: torch.Tensor) -> torch.Tensor:
+        """Fake-quantize an fp8 GEMM input the way the kernels do (emulation only)."""
+        if not self.emulate:
+            return x
+        from quail_b200.ops.quant import dequantize_mx, quantize_act_mx
+        return dequantize_mx(*quantize_act_mx(x.bfloat16().float())).to(x.dtype)
+
+    def _mlp(self, x, wg, wu, wd):
+        return self._q(ref.silu_mul(self._q(x) @ wg.t(), self._q(x) @ wu.t())) @ wd.t()
 
     # ------------------------------------------------------------ forward
     @torch.no_grad()
@@ -220,8 +241,12 @@ class Qwen35Reference:
             else:
                 h = h + self._attn(x, L, ai, chunk, arena)
                 ai += 1
+            if self.emulate:
+                h = h.bfloat16().float()
             x = rmsnorm_offset(h, L["ln2"], cfg.rms_eps)
-            h = h + (self._moe(x, L) if cfg.is_moe else ref.silu_mul(x @ L["wg"].t(), x @ L["wu"].t()) @ L["wd"].t())
+            h = h + (self._moe(x, L) if cfg.is_moe else self._mlp(x, L["wg"], L["wu"], L["wd"]))
+            if self.emulate:
+                h = h.bfloat16().float()
         return h
 
     def _moe(self, x, L):
@@ -232,11 +257,10 @@ class Qwen35Reference:
         for e in ids.unique().tolist():
             t, j = (ids == e).nonzero(as_tuple=True)
             wg, wu, wd = L["experts"][e]
-            xe = x[t]
-            out.index_add_(0, t, (ref.silu_mul(xe @ wg.t(), xe @ wu.t()) @ wd.t()) * w[t, j, None].to(x.dtype))
+            out.index_add_(0, t, self._mlp(x[t], wg, wu, wd) * w[t, j, None].to(x.dtype))
         if "shared" in L:
             wg, wu, wd = L["shared"]
-            out = out + torch.sigmoid(x @ L["shared_gate"].t()) * (ref.silu_mul(x @ wg.t(), x @ wu.t()) @ wd.t())
+            out = out + torch.sigmoid(x @ L["shared_gate"].t()) * self._mlp(x, wg, wu, wd)
         return out
 
     @torch.no_grad()

@@ -165,7 +165,15 @@ def test_hybrid_pipeline_matches_fp32_model(name):
     assert ops.read_and_clear_error(0) == 0
     d = rel_err(got, want)
     print(f"hybrid {name} kernel-vs-fp32: {d:.4f}")
-    assert d < 0.1
+    if not cfg.fp8:
+        assert d < 0.1
+        return
+    # fp8: as close to the exact model as an fp32 model that requantizes the
+    # weights and quantizes every fp8 GEMM input where the kernels do
+    emul = Q.Qwen35Reference(cfg, ckpt, device=DEV, head_rows=ids, emulate_kernels=True)
+    d_emul = rel_err(run(emul, torch.float32), want)
+    print(f"hybrid {name} emulated-vs-fp32: {d_emul:.4f}")
+    assert d < 1.5 * d_emul + 0.02, (d, d_emul)
 
 
 @pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.6-moe-gpu-tiny"])
