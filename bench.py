@@ -82,7 +82,7 @@ def main():
     from quail_b200.utils.synthetic import make_workload, rows_for_tokens
 
     cfg = MODEL_CONFIGS[args.model]
-    pipe = build_pipeline(cfg, device=dev, seed=0)
+    pipe = build_pipeline(cfg, device=dev, seed=0, max_tokens=args.chunk_tokens + 256)
     from quail_b200.planner.budgets import Budgets
     slots = Budgets.for_model(cfg, "b200", gpus=1).state_slots(cfg) if cfg.is_hybrid else 0
     arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=slots)

@@ -36,7 +36,7 @@ def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str,
 
 
 def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
-                   answer_ids=SYNTHETIC_TRUE_IDS + SYNTHETIC_FALSE_IDS):
+                   answer_ids=SYNTHETIC_TRUE_IDS + SYNTHETIC_FALSE_IDS, max_tokens: int = 16384 + 256):
     if ckpt is None:
         ckpt = random_checkpoint_on(cfg, device, seed)
     if cfg.is_hybrid:
@@ -44,7 +44,8 @@ def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
             from quail_b200.models.lfm2 import Lfm2Pipeline as Pipe
         else:
             from quail_b200.models.qwen3_5_gpu import Qwen35Pipeline as Pipe
-        pipe = Pipe(cfg, ckpt, device, head_rows=answer_ids)
+        kw = {"max_tokens": max_tokens} if cfg.is_moe else {}
+        pipe = Pipe(cfg, ckpt, device, head_rows=answer_ids, **kw)
         del ckpt
         torch.cuda.empty_cache() if torch.cuda.is_available() else None
         return pipe
