@@ -151,7 +151,7 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC,
+            "metric": METRIC if args.model == "qwen3-4b-fp8" else METRIC.replace("qwen3-4b-fp8", args.model),
             "value": round(toks_per_s, 1),
             "unit": "prompt tokens/s",
             "n_gpus": world,
@@ -164,11 +164,12 @@ def main():
             "baseline_value": BASELINE_TOKS_PER_GPU * world,
             "rows_per_second": round(rows_all / (ms_max / 1e3), 1),
             "fresh_tokens_per_second": round(fresh_all / (ms_max / 1e3), 1),
-            "dtype": "fp8 e4m3 weights+activations (128x128 / 1x128 block scales), bf16 KV and residual",
+            "dtype": ("fp8 e4m3 weights+activations (128x128 / 1x128 block scales), bf16 KV and residual"
+                      if cfg.fp8 else "bf16"),
             "data": "synthetic: random token-id bodies lognormal(median 180, sigma 0.6) clipped [16, 2048], "
                     "48-token shared template prefix, 40-token question suffix; random-init weights N(0, 0.02)",
-            "config": {"model": "qwen3-4b-fp8 (36 layers, hidden 2560, 32q/8kv heads, d128, SwiGLU 9728, "
-                                "vocab 151936)",
+            "config": {"model": ("qwen3-4b-fp8 (36 layers, hidden 2560, 32q/8kv heads, d128, SwiGLU 9728, "
+                                 "vocab 151936)" if args.model == "qwen3-4b-fp8" else args.model),
                        "global_batch": f"{args.chunk_tokens} tokens per rank per step",
                        "seq_len": "per row: 48 + body + 40", "parallelism": f"dp{world}",
                        "workload": "AI.IF filter, packed prefill chunks, yes/no readout",
