@@ -78,7 +78,7 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
                const torch::Tensor& dt_bias, const torch::Tensor& norm_w, const torch::Tensor& seqs,
                const torch::Tensor& state_io, torch::Tensor& conv_state, torch::Tensor& ssm_state, int64_t gi,
                int64_t Hk, int64_t Hv, int64_t DK, int64_t DV, double eps, torch::Tensor& conv_out,
-               torch::Tensor& o, torch::Tensor& y);
+               torch::Tensor& o, torch::Tensor& y, int64_t mode);
 void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                      const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& dseqs,
                      const torch::Tensor& page_list, double softmax_scale, torch::Tensor& out,

@@ -14,6 +14,8 @@
 //                  the reductions run over i inside a thread pair, so a token
 //                  costs one barrier. S is read from the source slot and written
 //                  to the destination slot.
+//                  (passes of one-token sequences and d_k < 128; the chunked
+//                  tensor-core form of the same recurrence is gdn_chunk.cu)
 //   gdn_gated_norm one warp per (token, value head): RMSNorm(o) * w * silu(z) -> bf16.
 //   short_conv     LFM2's gated short convolution: y = C * conv(B * x), one thread
 //                  per channel over a sequence's tokens, window in a state slot.
@@ -256,13 +258,18 @@ void short_conv(const torch::Tensor& bcx, const torch::Tensor& wconv, const torc
 }
 
 // ------------------------------------------------------------------ host side
+void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab, int b_col,
+                      int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk, const int* seqs,
+                      const int* sio, int S, float* ssm_state, int gi, int G, float* out, int dev,
+                      cudaStream_t st);
+
 // proj: bf16 [T, ld] = [qkv (C) | z (Hv*DV) | b (Hv) | a (Hv)] (the fused in-projection);
 // returns bf16 [T, Hv*DV] gated-norm output (the out_proj input).
 void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torch::Tensor& A_log,
                const torch::Tensor& dt_bias, const torch::Tensor& norm_w, const torch::Tensor& seqs,
                const torch::Tensor& state_io, torch::Tensor& conv_state, torch::Tensor& ssm_state, int64_t gi,
                int64_t Hk, int64_t Hv, int64_t DK, int64_t DV, double eps, torch::Tensor& conv_out,
-               torch::Tensor& o, torch::Tensor& y) {
+               torch::Tensor& o, torch::Tensor& y, int64_t mode) {
   TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.stride(1) == 1, "gdn: bf16 in-projection");
   const int T = proj.size(0), ld = proj.stride(0);
   const int C = 2 * Hk * DK + Hv * DV;
@@ -290,8 +297,18 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int b_col = C + Hv * DV, a_col = b_col + Hv;
   TORCH_CHECK(DV <= 128, "gdn: d_v <= 128");
+  // mode 0: the chunked tensor-core form when some sequence has several new
+  // tokens (T > S) and d_k = d_v = 128, else the per-token form; 1: per-token; 2: chunked
+  const bool chunked = DK == 128 && DV == 128 && (mode == 2 || (mode == 0 && T > S));
+  TORCH_CHECK(mode != 2 || chunked, "gdn: the chunked form needs d_k = d_v = 128");
+  if (chunked) {
+    launch_gdn_chunk(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
+                     reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
+                     A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, S,
+                     ssm_state.data_ptr<float>(), (int)gi, G, o.data_ptr<float>(), dev, st);
+  }
 #define QB_GDN_REC(DKK, PP)                                                                                     \
-  if (DK == DKK) {                                                                                              \
+  if (!chunked && DK == DKK) {                                                                                  \
     dim3 g2(S, Hv, 1);                                                                                           \
     gdn_recurrent_kernel<DKK, PP><<<g2, 128 * PP, 0, st>>>(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),        \
                                                       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), \

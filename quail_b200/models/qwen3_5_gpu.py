@@ -18,6 +18,8 @@ reference's Qwen3.5 pipeline over vLLM modules).
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from quail_b200.models.config import DecoderConfig
@@ -105,6 +107,8 @@ class Qwen35Pipeline:
         if cfg.has_sae:
             self.sae_w = ckpt["sae.W_enc"].to(device=dev, dtype=bf).contiguous()
             self.sae_b = ckpt["sae.b_enc"].to(device=dev, dtype=torch.float32).contiguous()
+        # Gated DeltaNet recurrence: 0 = chunked tensor-core form for prefill passes, 1 = per token
+        self.gdn_mode = int(os.environ.get("QB_GDN_MODE", "0"))
         self.ep = None
         if cfg.is_moe:
             from quail_b200.parallel.ep import EPState
@@ -183,7 +187,8 @@ class Qwen35Pipeline:
                 y = torch.empty(T, Hv * dv, dtype=torch.bfloat16, device=dev)
                 ops.count_launch(3)
                 C.gdn_layer(p, L["conv"], L["A_log"], L["dt_bias"], L["norm"], chunk.seqs, chunk.state_io,
-                            arena.states["conv"], arena.states["ssm"], gi, Hk, Hv, dk, dv, cfg.rms_eps, conv_out, o, y)
+                            arena.states["conv"], arena.states["ssm"], gi, Hk, Hv, dk, dv, cfg.rms_eps, conv_out, o, y,
+                            self.gdn_mode)
                 ops.gemm(y, L["wout"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 gi += 1
             else:
