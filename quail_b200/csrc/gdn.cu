@@ -262,6 +262,11 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
                       int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk, const int* seqs,
                       const int* sio, int S, float* ssm_state, int gi, int G, float* out, int dev,
                       cudaStream_t st);
+int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv);
+void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
+                            int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
+                            const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
+                            float* out, uint8_t* ws, int dev, cudaStream_t st);
 
 // proj: bf16 [T, ld] = [qkv (C) | z (Hv*DV) | b (Hv) | a (Hv)] (the fused in-projection);
 // returns bf16 [T, Hv*DV] gated-norm output (the out_proj input).
@@ -297,11 +302,20 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int b_col = C + Hv * DV, a_col = b_col + Hv;
   TORCH_CHECK(DV <= 128, "gdn: d_v <= 128");
-  // mode 0: the chunked tensor-core form when some sequence has several new
-  // tokens (T > S) and d_k = d_v = 128, else the per-token form; 1: per-token; 2: chunked
-  const bool chunked = DK == 128 && DV == 128 && (mode == 2 || (mode == 0 && T > S));
-  TORCH_CHECK(mode != 2 || chunked, "gdn: the chunked form needs d_k = d_v = 128");
-  if (chunked) {
+  // mode 0: the split chunked form when some sequence has several new tokens
+  // (T > S) and d_k = d_v = 128, else the per-token form; 1: per-token;
+  // 2: chunked, one kernel; 3: chunked, split (index + prep + scan)
+  const bool chunked = DK == 128 && DV == 128 && (mode == 2 || mode == 3 || (mode == 0 && T > S));
+  TORCH_CHECK(mode < 2 || chunked, "gdn: the chunked form needs d_k = d_v = 128");
+  if (chunked && mode != 2) {
+    // the workspace comes from PyTorch's caching allocator on the current stream
+    auto ws = at::empty({gdn_chunk_ws_bytes(T, S, Hv)}, proj.options().dtype(at::kByte));
+    launch_gdn_chunk_split(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
+                           reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
+                           A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, T, S,
+                           ssm_state.data_ptr<float>(), (int)gi, G, o.data_ptr<float>(), ws.data_ptr<uint8_t>(), dev,
+                           st);
+  } else if (chunked) {
     launch_gdn_chunk(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
                      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
                      A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, S,

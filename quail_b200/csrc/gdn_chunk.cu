@@ -388,6 +388,401 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(
   }
 }
 
+// ------------------------------------------------------------------ split form
+// The same algebra in two kernels, so the state-free work (gates, K K^T, Q K^T,
+// the triangular solve) runs in parallel over every chunk of the pass:
+//   gdn_chunk_index   the pass's chunk list (sequence, first token) and each
+//                     sequence's first chunk, by a block-wide scan
+//   gdn_chunk_prep    one CTA per (chunk, value head): writes the chunk's record
+//                     -W, U~ (bf16 [64][128]), M o QK^T (bf16 [64][64]), G (fp32 [64])
+//   gdn_chunk_scan    one CTA per (sequence, value head): walks the records with
+//                     the state: U = U~ + (-W) S0, O, S update (as above)
+constexpr int kRecW = 0;
+constexpr int kRecU = kRecW + kCh * kD * 2;
+constexpr int kRecM = kRecU + kCh * kD * 2;
+constexpr int kRecG = kRecM + kCh * kCh * 2;
+constexpr int kRecBytes = kRecG + kCh * 4;   // 41,216 B = 161 x 256
+static_assert(kRecBytes % 256 == 0, "records stay 256-byte aligned");
+
+// ws ints: [0] chunk count, [4, 4 + 2 maxc) the (sequence, first token) list,
+// then first[S]: each sequence's first chunk index
+__global__ void __launch_bounds__(256) gdn_chunk_index_kernel(const int* __restrict__ seqs, int S, int maxc,
+                                                              int* __restrict__ ws) {
+  __shared__ int part[256];
+  const int t = threadIdx.x, per = (S + 255) / 256;
+  const int a = min(S, t * per), b = min(S, a + per);
+  int cnt = 0;
+  for (int s = a; s < b; ++s) cnt += (seqs[s * kChSeqInts + 1] + kCh - 1) / kCh;
+  part[t] = cnt;
+  __syncthreads();
+  if (t < 32) {
+    // exclusive scan of 256 partial counts: 8 per lane, then across lanes
+    int v[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = part[t * 8 + i];
+      sum += v[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (t >= o) incl += y;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      part[t * 8 + i] = run;
+      run += v[i];
+    }
+    if (t == 31) ws[0] = incl;
+  }
+  __syncthreads();
+  int off = part[t];
+  int2* list = reinterpret_cast<int2*>(ws + 4);
+  int* first = ws + 4 + 2 * maxc;
+  for (int s = a; s < b; ++s) {
+    const int n = seqs[s * kChSeqInts + 1];
+    first[s] = off;
+    for (int c0 = 0; c0 < n; c0 += kCh) list[off++] = make_int2(s, c0);
+  }
+}
+
+struct GpSmem {
+  static constexpr int Q = 0;
+  static constexpr int K = Q + kCh * kP * 2;
+  static constexpr int A = K + kCh * kP * 2;
+  static constexpr int G = A + kCh * kPa * 4;
+  static constexpr int B = G + kCh * 4;
+  static constexpr int BYTES = B + kCh * 4;
+};
+
+__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
+    const float* __restrict__ conv_out, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
+    int b_col, int a_col, const float* __restrict__ A_log, const float* __restrict__ dt_bias, int Hv, int Hk,
+    const int* __restrict__ seqs, const int* __restrict__ ws, uint8_t* __restrict__ recs) {
+  const int ci = blockIdx.x, h = blockIdx.y;
+  if (ci >= ws[0]) return;
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* sA = reinterpret_cast<float*>(smem + GpSmem::A);
+  float* sG = reinterpret_cast<float*>(smem + GpSmem::G);
+  float* sB = reinterpret_cast<float*>(smem + GpSmem::B);
+  const uint32_t base = smem_u32(smem);
+  const uint32_t aQ = base + GpSmem::Q, aK = base + GpSmem::K;
+  constexpr int P2 = kP * 2;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+  const int2 e = reinterpret_cast<const int2*>(ws + 4)[ci];
+  const int s = e.x, c0 = e.y;
+  const int q0 = seqs[s * kChSeqInts], n = seqs[s * kChSeqInts + 1];
+  const int cn = min(kCh, n - c0);
+  const int hk = h / (Hv / Hk);
+  const int kofs = qk_channels / 2 + hk * kD, qofs = hk * kD, vofs = qk_channels + h * kD;
+  uint8_t* rec = recs + ((size_t)ci * Hv + h) * kRecBytes;
+
+  for (int idx = tid; idx < kCh * (kD / 4); idx += 256) {
+    const int row = idx >> 5, col = (idx & 31) * 4;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q;
+    if (row < cn) {
+      const float* r = conv_out + (size_t)(q0 + c0 + row) * C;
+      q = *reinterpret_cast<const float4*>(r + qofs + col);
+      k = *reinterpret_cast<const float4*>(r + kofs + col);
+    }
+    uint32_t* dq = reinterpret_cast<uint32_t*>(smem + GpSmem::Q + row * P2 + col * 2);
+    uint32_t* dk = reinterpret_cast<uint32_t*>(smem + GpSmem::K + row * P2 + col * 2);
+    dq[0] = gc_pack(q.x, q.y);
+    dq[1] = gc_pack(q.z, q.w);
+    dk[0] = gc_pack(k.x, k.y);
+    dk[1] = gc_pack(k.z, k.w);
+  }
+  if (tid < kCh) {
+    float gl = 0.f, beta = 0.f;
+    if (tid < cn) {
+      const size_t r = (size_t)(q0 + c0 + tid) * ldab;
+      const float a = __bfloat162float(ab[r + a_col + h]) + dt_bias[h];
+      const float sp = a > 20.f ? a : log1pf(__expf(a));  // softplus
+      gl = -__expf(A_log[h]) * sp;                         // log decay, <= 0
+      beta = 1.f / (1.f + __expf(-__bfloat162float(ab[r + b_col + h])));
+    }
+    sG[tid] = gl;
+    sB[tid] = beta;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float x0 = sG[2 * lane], x1 = sG[2 * lane + 1];
+    float p = x0 + x1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, p, o);
+      if (lane >= o) p += y;
+    }
+    const float excl = p - (x0 + x1);
+    sG[2 * lane] = excl + x0;
+    sG[2 * lane + 1] = excl + x0 + x1;
+    reinterpret_cast<float2*>(rec + kRecG)[lane] = make_float2(excl + x0, excl + x0 + x1);
+  }
+  __syncthreads();
+
+  {
+    const int mt = warp & 3, nh = warp >> 2;
+    float accP[4][4], accQ[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) accP[i][j] = accQ[i][j] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < kD; k0 += 16) {
+      uint32_t ak[4], aq[4];
+      gc_ldsm4(a_rows(aK, P2, 16 * mt, k0, lane), ak);
+      gc_ldsm4(a_rows(aQ, P2, 16 * mt, k0, lane), aq);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b[4];
+        gc_ldsm4(b_rows(aK, P2, 32 * nh + 16 * np, k0, lane), b);
+        gc_mma(accP[2 * np], ak, b[0], b[1]);
+        gc_mma(accP[2 * np + 1], ak, b[2], b[3]);
+        gc_mma(accQ[2 * np], aq, b[0], b[1]);
+        gc_mma(accQ[2 * np + 1], aq, b[2], b[3]);
+      }
+    }
+    uint32_t* Mrec = reinterpret_cast<uint32_t*>(rec + kRecM);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int i = 16 * mt + g + 8 * hf;
+        const int j = 32 * nh + 8 * nt + 2 * t4;
+        const float gi_ = sG[i], bi = sB[i];
+        const float d0 = j <= i ? __expf(gi_ - sG[j]) : 0.f;
+        const float d1 = j + 1 <= i ? __expf(gi_ - sG[j + 1]) : 0.f;
+        sA[i * kPa + j] = j < i ? bi * d0 * accP[nt][2 * hf] : 0.f;
+        sA[i * kPa + j + 1] = j + 1 < i ? bi * d1 * accP[nt][2 * hf + 1] : 0.f;
+        Mrec[(i * kCh + j) >> 1] = gc_pack(d0 * accQ[nt][2 * hf], d1 * accQ[nt][2 * hf + 1]);
+      }
+  }
+  __syncthreads();
+
+  {
+    const int col = tid;
+    const bool kside = col < kD;
+    const int gofs = kside ? kofs + col : vofs + (col - kD);
+    float x[kCh];
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) x[i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) {
+      float r = 0.f;
+      if (i < cn) r = sB[i] * (kside ? __expf(sG[i]) : 1.f) * conv_out[(size_t)(q0 + c0 + i) * C + gofs];
+      const float4* arow = reinterpret_cast<const float4*>(sA + i * kPa);
+#pragma unroll
+      for (int j4 = 0; j4 < (i + 3) / 4; ++j4) {
+        const float4 a = arow[j4];
+        r -= a.x * x[4 * j4] + a.y * x[4 * j4 + 1] + a.z * x[4 * j4 + 2] + a.w * x[4 * j4 + 3];
+      }
+      x[i] = r;
+    }
+    __nv_bfloat16* dstp = reinterpret_cast<__nv_bfloat16*>(rec + (kside ? kRecW : kRecU)) + (kside ? col : col - kD);
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) dstp[i * kD] = __float2bfloat16(kside ? -x[i] : x[i]);
+  }
+}
+
+struct GsSmem {
+  static constexpr int Q = 0;
+  static constexpr int K = Q + kCh * kP * 2;
+  static constexpr int S = K + kCh * kP * 2;
+  static constexpr int W = S + kD * kP * 2;
+  static constexpr int U = W + kCh * kP * 2;
+  static constexpr int Us = U + kCh * kP * 2;
+  static constexpr int M = Us + kCh * kP * 2;
+  static constexpr int G = M + kCh * kPm * 2;
+  static constexpr int BYTES = G + kCh * 4;
+};
+
+__global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
+    const float* __restrict__ conv_out, int C, int qk_channels, int Hv, int Hk, const int* __restrict__ seqs,
+    const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G, const int* __restrict__ ws,
+    int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* sG = reinterpret_cast<float*>(smem + GsSmem::G);
+  const uint32_t base = smem_u32(smem);
+  const uint32_t aQ = base + GsSmem::Q, aK = base + GsSmem::K, aS = base + GsSmem::S, aW = base + GsSmem::W;
+  const uint32_t aU = base + GsSmem::U, aUs = base + GsSmem::Us, aM = base + GsSmem::M;
+  constexpr int P2 = kP * 2, Pm2 = kPm * 2;
+
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+  const int hk = h / (Hv / Hk);
+  const int q0 = seqs[s * kChSeqInts], n = seqs[s * kChSeqInts + 1];
+  const int src = sio[2 * s], dst = sio[2 * s + 1];
+  const int first = ws[4 + 2 * maxc + s];
+  const size_t slot_stride = (size_t)G * Hv * kD * kD;
+  const size_t head_off = ((size_t)gi * Hv + h) * kD * kD;
+  const int kofs = qk_channels / 2 + hk * kD, qofs = hk * kD;
+
+  float Sacc[16][4];
+  const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int c = nt * 8 + 2 * t4;
+    if (src >= 0) {
+      const float* S0 = ssm_state + (size_t)src * slot_stride + head_off;
+      const float2 lo = *reinterpret_cast<const float2*>(S0 + (size_t)r_lo * kD + c);
+      const float2 hi = *reinterpret_cast<const float2*>(S0 + (size_t)r_hi * kD + c);
+      Sacc[nt][0] = lo.x; Sacc[nt][1] = lo.y; Sacc[nt][2] = hi.x; Sacc[nt][3] = hi.y;
+    } else {
+      Sacc[nt][0] = Sacc[nt][1] = Sacc[nt][2] = Sacc[nt][3] = 0.f;
+    }
+  }
+  uint32_t* sS32 = reinterpret_cast<uint32_t*>(smem + GsSmem::S);
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int c = nt * 8 + 2 * t4;
+    sS32[(r_lo * kP + c) >> 1] = gc_pack(Sacc[nt][0], Sacc[nt][1]);
+    sS32[(r_hi * kP + c) >> 1] = gc_pack(Sacc[nt][2], Sacc[nt][3]);
+  }
+  const int mt = warp & 3, nh = warp >> 2;
+
+  for (int c0 = 0, ci = first; c0 < n; c0 += kCh, ++ci) {
+    const int cn = min(kCh, n - c0);
+    const uint8_t* rec = recs + ((size_t)ci * Hv + h) * kRecBytes;
+    // q, k rows (bf16), the record's -W and M tiles, G
+    for (int idx = tid; idx < kCh * (kD / 4); idx += 256) {
+      const int row = idx >> 5, col = (idx & 31) * 4;
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q;
+      if (row < cn) {
+        const float* r = conv_out + (size_t)(q0 + c0 + row) * C;
+        q = *reinterpret_cast<const float4*>(r + qofs + col);
+        k = *reinterpret_cast<const float4*>(r + kofs + col);
+      }
+      uint32_t* dq = reinterpret_cast<uint32_t*>(smem + GsSmem::Q + row * P2 + col * 2);
+      uint32_t* dk = reinterpret_cast<uint32_t*>(smem + GsSmem::K + row * P2 + col * 2);
+      dq[0] = gc_pack(q.x, q.y);
+      dq[1] = gc_pack(q.z, q.w);
+      dk[0] = gc_pack(k.x, k.y);
+      dk[1] = gc_pack(k.z, k.w);
+    }
+    for (int idx = tid; idx < kCh * (kD / 8); idx += 256) {   // -W: 16 B per piece
+      const int row = idx >> 4, c8 = (idx & 15) * 8;
+      *reinterpret_cast<uint4*>(smem + GsSmem::W + row * P2 + c8 * 2) =
+          *reinterpret_cast<const uint4*>(rec + kRecW + (row * kD + c8) * 2);
+    }
+    for (int idx = tid; idx < kCh * (kCh / 8); idx += 256) {  // M
+      const int row = idx >> 3, c8 = (idx & 7) * 8;
+      *reinterpret_cast<uint4*>(smem + GsSmem::M + row * Pm2 + c8 * 2) =
+          *reinterpret_cast<const uint4*>(rec + kRecM + (row * kCh + c8) * 2);
+    }
+    if (tid < kCh) sG[tid] = reinterpret_cast<const float*>(rec + kRecG)[tid];
+    __syncthreads();
+
+    float accO[8][4];
+    {
+      float accU[8][4];
+      const uint32_t* Ut = reinterpret_cast<const uint32_t*>(rec + kRecU);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int c = 64 * nh + 8 * nt + 2 * t4;
+        const int i0 = 16 * mt + g;
+        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(Ut + ((i0 * kD + c) >> 1));
+        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(Ut + (((i0 + 8) * kD + c) >> 1));
+        accU[nt][0] = __low2float(lo);
+        accU[nt][1] = __high2float(lo);
+        accU[nt][2] = __low2float(hi);
+        accU[nt][3] = __high2float(hi);
+        accO[nt][0] = accO[nt][1] = accO[nt][2] = accO[nt][3] = 0.f;
+      }
+#pragma unroll
+      for (int k0 = 0; k0 < kD; k0 += 16) {
+        uint32_t aw[4], aq[4];
+        gc_ldsm4(a_rows(aW, P2, 16 * mt, k0, lane), aw);
+        gc_ldsm4(a_rows(aQ, P2, 16 * mt, k0, lane), aq);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t b[4];
+          gc_ldsm4t(b_cols(aS, P2, 64 * nh + 16 * np, k0, lane), b);
+          gc_mma(accU[2 * np], aw, b[0], b[1]);
+          gc_mma(accU[2 * np + 1], aw, b[2], b[3]);
+          gc_mma(accO[2 * np], aq, b[0], b[1]);
+          gc_mma(accO[2 * np + 1], aq, b[2], b[3]);
+        }
+      }
+      const float Gl = sG[kCh - 1];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int i = 16 * mt + g + 8 * hf;
+        const float gam = __expf(sG[i]), tail = __expf(Gl - sG[i]);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int c = 64 * nh + 8 * nt + 2 * t4;
+          const float u0 = accU[nt][2 * hf], u1 = accU[nt][2 * hf + 1];
+          *reinterpret_cast<uint32_t*>(smem + GsSmem::U + i * P2 + c * 2) = gc_pack(u0, u1);
+          *reinterpret_cast<uint32_t*>(smem + GsSmem::Us + i * P2 + c * 2) = gc_pack(tail * u0, tail * u1);
+          accO[nt][2 * hf] *= gam;
+          accO[nt][2 * hf + 1] *= gam;
+        }
+      }
+    }
+    __syncthreads();
+
+#pragma unroll
+    for (int k0 = 0; k0 < kCh; k0 += 16) {
+      uint32_t am[4];
+      gc_ldsm4(a_rows(aM, Pm2, 16 * mt, k0, lane), am);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b[4];
+        gc_ldsm4t(b_cols(aU, P2, 64 * nh + 16 * np, k0, lane), b);
+        gc_mma(accO[2 * np], am, b[0], b[1]);
+        gc_mma(accO[2 * np + 1], am, b[2], b[3]);
+      }
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int i = 16 * mt + g + 8 * hf;
+      if (i < cn) {
+        float* orow = out + (size_t)(q0 + c0 + i) * Hv * kD + h * kD;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int c = 64 * nh + 8 * nt + 2 * t4;
+          *reinterpret_cast<float2*>(orow + c) = make_float2(accO[nt][2 * hf], accO[nt][2 * hf + 1]);
+        }
+      }
+    }
+    {
+      const float gC = __expf(sG[kCh - 1]);
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) Sacc[nt][e] *= gC;
+#pragma unroll
+      for (int k0 = 0; k0 < kCh; k0 += 16) {
+        uint32_t ak[4];
+        gc_ldsm4t(a_cols(aK, P2, 16 * warp, k0, lane), ak);
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          uint32_t b[4];
+          gc_ldsm4t(b_cols(aUs, P2, 16 * np, k0, lane), b);
+          gc_mma(Sacc[2 * np], ak, b[0], b[1]);
+          gc_mma(Sacc[2 * np + 1], ak, b[2], b[3]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        const int c = nt * 8 + 2 * t4;
+        sS32[(r_lo * kP + c) >> 1] = gc_pack(Sacc[nt][0], Sacc[nt][1]);
+        sS32[(r_hi * kP + c) >> 1] = gc_pack(Sacc[nt][2], Sacc[nt][3]);
+      }
+    }
+    __syncthreads();
+  }
+  float* Sd = ssm_state + (size_t)dst * slot_stride + head_off;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int c = nt * 8 + 2 * t4;
+    *reinterpret_cast<float2*>(Sd + (size_t)r_lo * kD + c) = make_float2(Sacc[nt][0], Sacc[nt][1]);
+    *reinterpret_cast<float2*>(Sd + (size_t)r_hi * kD + c) = make_float2(Sacc[nt][2], Sacc[nt][3]);
+  }
+}
+
 }  // namespace
 
 // The chunked recurrence for one Gated DeltaNet layer (d_k = d_v = 128); the
@@ -405,6 +800,39 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
   dim3 grid(S, Hv);
   gdn_chunk_kernel<<<grid, 256, GcSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col, a_col, A_log,
                                                      dt_bias, Hv, Hk, seqs, sio, ssm_state, gi, G, out);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Bytes of the split form's workspace for a pass of T tokens in S sequences.
+int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv) {
+  const int64_t maxc = T / kCh + S + 1;
+  const int64_t ints = ((4 + 2 * maxc + S) * 4 + 255) / 256 * 256;
+  return ints + maxc * Hv * kRecBytes;
+}
+
+void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
+                            int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
+                            const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
+                            float* out, uint8_t* ws, int dev, cudaStream_t st) {
+  static bool configured[64] = {false};
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        GpSmem::BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        GsSmem::BYTES));
+    configured[dev] = true;
+  }
+  const int maxc = T / kCh + S + 1;
+  const int64_t ints = ((4 + 2 * (int64_t)maxc + S) * 4 + 255) / 256 * 256;
+  int* wsi = reinterpret_cast<int*>(ws);
+  uint8_t* recs = ws + ints;
+  gdn_chunk_index_kernel<<<1, 256, 0, st>>>(seqs, S, maxc, wsi);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col,
+                                                                     a_col, A_log, dt_bias, Hv, Hk, seqs, wsi, recs);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  gdn_chunk_scan_kernel<<<dim3(S, Hv), 256, GsSmem::BYTES, st>>>(conv_out, C, qk_channels, Hv, Hk, seqs, sio,
+                                                                  ssm_state, gi, G, wsi, maxc, recs, out);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

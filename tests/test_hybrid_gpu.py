@@ -80,10 +80,11 @@ def test_hybrid_qk_rope_kv():
     assert torch.equal(vc.view(-1, KH, D)[slots[ok].long()], v[ok])
 
 
-@pytest.mark.parametrize("dk,mode", [(128, 1), (64, 1), (128, 2)])
+@pytest.mark.parametrize("dk,mode", [(128, 1), (64, 1), (128, 2), (128, 3)])
 def test_gdn_layer_against_recurrence(dk, mode):
-    """mode 1: the per-token kernel (fp32 throughout); mode 2: the chunked tensor-core kernel
-    (bf16 operands, fp32 accumulation and state), sequences of 1 to 3 chunks."""
+    """mode 1: the per-token kernel (fp32 throughout); modes 2 and 3: the chunked tensor-core form
+    in one kernel and split in three (bf16 operands, fp32 accumulation and state), sequences of
+    1 to 3 chunks."""
     Hk, Hv, dv, W = 2, 4, dk, 4
     C = 2 * Hk * dk + Hv * dv
     lens = [5, 1, 70, 33] if mode == 1 else [5, 1, 150, 64, 33]
