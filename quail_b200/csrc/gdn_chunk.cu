@@ -394,34 +394,33 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(
 //   gdn_chunk_index   the pass's chunk list (sequence, first token) and each
 //                     sequence's first chunk, by a block-wide scan
 //   gdn_chunk_prep    one CTA per (chunk, value head): writes the chunk's record
-//                     -W, U~ (bf16 [64][128]), M o QK^T (bf16 [64][64]), G (fp32 [64])
+//                     -W, U~, q, k (bf16 [64][128]), M o QK^T (bf16 [64][64]), G (fp32 [64])
 //   gdn_chunk_scan    one CTA per (sequence, value head): walks the records with
-//                     the state: U = U~ + (-W) S0, O, S update (as above)
-constexpr int kRecW = 0;
-constexpr int kRecU = kRecW + kCh * kD * 2;
-constexpr int kRecM = kRecU + kCh * kD * 2;
-constexpr int kRecG = kRecM + kCh * kCh * 2;
-constexpr int kRecBytes = kRecG + kCh * 4;   // 41,216 B = 161 x 256
+//                     the state: U = U~ + (-W) S0, O, S update (as above); the
+//                     next record streams into shared memory (cp.async, two
+//                     buffers) while the current one is in the tensor cores
+constexpr int kRecW = 0;                      // bf16 [64][128] -W
+constexpr int kRecU = kRecW + kCh * kD * 2;   // bf16 [64][128] U~
+constexpr int kRecQ = kRecU + kCh * kD * 2;   // bf16 [64][128] q rows
+constexpr int kRecK = kRecQ + kCh * kD * 2;   // bf16 [64][128] k rows
+constexpr int kRecM = kRecK + kCh * kD * 2;   // bf16 [64][64] M o QK^T
+constexpr int kRecG = kRecM + kCh * kCh * 2;  // fp32 [64] G
+constexpr int kRecBytes = kRecG + kCh * 4;    // 73,984 B = 289 x 256
 static_assert(kRecBytes % 256 == 0, "records stay 256-byte aligned");
 
 // ws ints: [0] chunk count, [4, 4 + 2 maxc) the (sequence, first token) list,
-// then first[S]: each sequence's first chunk index
-__global__ void __launch_bounds__(256) gdn_chunk_index_kernel(const int* __restrict__ seqs, int S, int maxc,
-                                                              int* __restrict__ ws) {
-  __shared__ int part[256];
-  const int t = threadIdx.x, per = (S + 255) / 256;
-  const int a = min(S, t * per), b = min(S, a + per);
-  int cnt = 0;
-  for (int s = a; s < b; ++s) cnt += (seqs[s * kChSeqInts + 1] + kCh - 1) / kCh;
-  part[t] = cnt;
-  __syncthreads();
+// then first[S] (each sequence's first chunk index), then order[S]: the
+// sequences by chunk count, most first (the scan kernel's CTAs start the
+// longest sequences first, so short ones fill in behind them)
+__device__ __forceinline__ void gc_block_scan256(int* v, int* total) {
+  // exclusive scan of 256 shared ints by warp 0 (8 per lane)
+  const int t = threadIdx.x;
   if (t < 32) {
-    // exclusive scan of 256 partial counts: 8 per lane, then across lanes
-    int v[8], sum = 0;
+    int x[8], sum = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      v[i] = part[t * 8 + i];
-      sum += v[i];
+      x[i] = v[t * 8 + i];
+      sum += x[i];
     }
     int incl = sum;
 #pragma unroll
@@ -432,11 +431,36 @@ __global__ void __launch_bounds__(256) gdn_chunk_index_kernel(const int* __restr
     int run = incl - sum;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      part[t * 8 + i] = run;
-      run += v[i];
+      v[t * 8 + i] = run;
+      run += x[i];
     }
-    if (t == 31) ws[0] = incl;
+    if (t == 31 && total) *total = incl;
   }
+}
+
+__global__ void __launch_bounds__(256) gdn_chunk_index_kernel(const int* __restrict__ seqs, int S, int maxc,
+                                                              int* __restrict__ ws) {
+  __shared__ int part[256], hist[256];
+  const int t = threadIdx.x, per = (S + 255) / 256;
+  const int a = min(S, t * per), b = min(S, a + per);
+  hist[t] = 0;
+  __syncthreads();
+  int cnt = 0;
+  for (int s = a; s < b; ++s) {
+    const int c = (seqs[s * kChSeqInts + 1] + kCh - 1) / kCh;
+    cnt += c;
+    atomicAdd(&hist[255 - min(c, 255)], 1);
+  }
+  part[t] = cnt;
+  __syncthreads();
+  gc_block_scan256(hist, nullptr);
+  __syncthreads();
+  int* order = ws + 4 + 2 * maxc + S;
+  for (int s = a; s < b; ++s) {
+    const int c = (seqs[s * kChSeqInts + 1] + kCh - 1) / kCh;
+    order[atomicAdd(&hist[255 - min(c, 255)], 1)] = s;
+  }
+  gc_block_scan256(part, ws);
   __syncthreads();
   int off = part[t];
   int2* list = reinterpret_cast<int2*>(ws + 4);
@@ -451,7 +475,8 @@ __global__ void __launch_bounds__(256) gdn_chunk_index_kernel(const int* __restr
 struct GpSmem {
   static constexpr int Q = 0;
   static constexpr int K = Q + kCh * kP * 2;
-  static constexpr int A = K + kCh * kP * 2;
+  static constexpr int V = K + kCh * kP * 2;        // bf16 [64][kP]: the solve's right-hand side
+  static constexpr int A = V + kCh * kP * 2;
   static constexpr int G = A + kCh * kPa * 4;
   static constexpr int B = G + kCh * 4;
   static constexpr int BYTES = B + kCh * 4;
@@ -481,18 +506,24 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
 
   for (int idx = tid; idx < kCh * (kD / 4); idx += 256) {
     const int row = idx >> 5, col = (idx & 31) * 4;
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
     if (row < cn) {
       const float* r = conv_out + (size_t)(q0 + c0 + row) * C;
       q = *reinterpret_cast<const float4*>(r + qofs + col);
       k = *reinterpret_cast<const float4*>(r + kofs + col);
+      v = *reinterpret_cast<const float4*>(r + vofs + col);
     }
     uint32_t* dq = reinterpret_cast<uint32_t*>(smem + GpSmem::Q + row * P2 + col * 2);
     uint32_t* dk = reinterpret_cast<uint32_t*>(smem + GpSmem::K + row * P2 + col * 2);
+    uint32_t* dv = reinterpret_cast<uint32_t*>(smem + GpSmem::V + row * P2 + col * 2);
     dq[0] = gc_pack(q.x, q.y);
     dq[1] = gc_pack(q.z, q.w);
     dk[0] = gc_pack(k.x, k.y);
     dk[1] = gc_pack(k.z, k.w);
+    dv[0] = gc_pack(v.x, v.y);
+    dv[1] = gc_pack(v.z, v.w);
+    *reinterpret_cast<uint2*>(rec + kRecQ + (row * kD + col) * 2) = make_uint2(dq[0], dq[1]);
+    *reinterpret_cast<uint2*>(rec + kRecK + (row * kD + col) * 2) = make_uint2(dk[0], dk[1]);
   }
   if (tid < kCh) {
     float gl = 0.f, beta = 0.f;
@@ -564,14 +595,15 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
   {
     const int col = tid;
     const bool kside = col < kD;
-    const int gofs = kside ? kofs + col : vofs + (col - kD);
+    // the right-hand side from the staged bf16 rows (rows past the chunk are zeros)
+    const __nv_bfloat16* rhs =
+        reinterpret_cast<const __nv_bfloat16*>(smem + (kside ? GpSmem::K : GpSmem::V)) + (col & (kD - 1));
     float x[kCh];
 #pragma unroll
     for (int i = 0; i < kCh; ++i) x[i] = 0.f;
 #pragma unroll
     for (int i = 0; i < kCh; ++i) {
-      float r = 0.f;
-      if (i < cn) r = sB[i] * (kside ? __expf(sG[i]) : 1.f) * conv_out[(size_t)(q0 + c0 + i) * C + gofs];
+      float r = sB[i] * (kside ? __expf(sG[i]) : 1.f) * __bfloat162float(rhs[i * kP]);
       const float4* arow = reinterpret_cast<const float4*>(sA + i * kPa);
 #pragma unroll
       for (int j4 = 0; j4 < (i + 3) / 4; ++j4) {
@@ -587,37 +619,67 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
 }
 
 struct GsSmem {
+  // two buffers of one record's tiles (padded rows), then the state and U tiles
   static constexpr int Q = 0;
   static constexpr int K = Q + kCh * kP * 2;
-  static constexpr int S = K + kCh * kP * 2;
-  static constexpr int W = S + kD * kP * 2;
-  static constexpr int U = W + kCh * kP * 2;
-  static constexpr int Us = U + kCh * kP * 2;
-  static constexpr int M = Us + kCh * kP * 2;
+  static constexpr int W = K + kCh * kP * 2;
+  static constexpr int Ut = W + kCh * kP * 2;
+  static constexpr int M = Ut + kCh * kP * 2;
   static constexpr int G = M + kCh * kPm * 2;
-  static constexpr int BYTES = G + kCh * 4;
+  static constexpr int BUF = G + kCh * 4;            // 79,104 B
+  static constexpr int S = 2 * BUF;
+  static constexpr int U = S + kD * kP * 2;
+  static constexpr int Us = U + kCh * kP * 2;
+  static constexpr int BYTES = Us + kCh * kP * 2;    // 227,840 B
 };
 
+__device__ __forceinline__ void gc_cp16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void gc_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void gc_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// one record into buffer `buf`: the four [64][128] tiles, M and G (16 B pieces)
+__device__ __forceinline__ void gc_fetch_record(uint32_t sbuf, const uint8_t* rec, int tid) {
+  constexpr int P2 = kP * 2, Pm2 = kPm * 2;
+  for (int idx = tid; idx < 4 * kCh * 16; idx += 256) {
+    const int tile = idx >> 10, row = (idx >> 4) & 63, c16 = idx & 15;
+    const int src = tile == 0 ? kRecQ : tile == 1 ? kRecK : tile == 2 ? kRecW : kRecU;
+    const int dst = tile == 0 ? GsSmem::Q : tile == 1 ? GsSmem::K : tile == 2 ? GsSmem::W : GsSmem::Ut;
+    gc_cp16(sbuf + dst + row * P2 + c16 * 16, rec + src + row * kD * 2 + c16 * 16);
+  }
+  for (int idx = tid; idx < kCh * 8; idx += 256) {
+    const int row = idx >> 3, c16 = idx & 7;
+    gc_cp16(sbuf + GsSmem::M + row * Pm2 + c16 * 16, rec + kRecM + row * kCh * 2 + c16 * 16);
+  }
+  if (tid < 16) gc_cp16(sbuf + GsSmem::G + tid * 16, rec + kRecG + tid * 16);
+}
+
 __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
-    const float* __restrict__ conv_out, int C, int qk_channels, int Hv, int Hk, const int* __restrict__ seqs,
-    const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G, const int* __restrict__ ws,
-    int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out) {
+    int Hv, const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
+    const int* __restrict__ ws, int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float* sG = reinterpret_cast<float*>(smem + GsSmem::G);
   const uint32_t base = smem_u32(smem);
-  const uint32_t aQ = base + GsSmem::Q, aK = base + GsSmem::K, aS = base + GsSmem::S, aW = base + GsSmem::W;
-  const uint32_t aU = base + GsSmem::U, aUs = base + GsSmem::Us, aM = base + GsSmem::M;
+  const uint32_t aS = base + GsSmem::S, aU = base + GsSmem::U, aUs = base + GsSmem::Us;
   constexpr int P2 = kP * 2, Pm2 = kPm * 2;
 
-  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int S = gridDim.y, h = blockIdx.x, tid = threadIdx.x;
+  const int s = ws[4 + 2 * maxc + S + blockIdx.y];   // longest sequences first
   const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
-  const int hk = h / (Hv / Hk);
   const int q0 = seqs[s * kChSeqInts], n = seqs[s * kChSeqInts + 1];
   const int src = sio[2 * s], dst = sio[2 * s + 1];
   const int first = ws[4 + 2 * maxc + s];
+  const int nch = (n + kCh - 1) / kCh;
   const size_t slot_stride = (size_t)G * Hv * kD * kD;
   const size_t head_off = ((size_t)gi * Hv + h) * kD * kD;
-  const int kofs = qk_channels / 2 + hk * kD, qofs = hk * kD;
+  auto record = [&](int c) { return recs + ((size_t)(first + c) * Hv + h) * kRecBytes; };
+  if (nch > 0) {
+    gc_fetch_record(base, record(0), tid);
+    gc_commit();
+  }
 
   float Sacc[16][4];
   const int r_lo = 16 * warp + g, r_hi = r_lo + 8;
@@ -642,48 +704,31 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
   }
   const int mt = warp & 3, nh = warp >> 2;
 
-  for (int c0 = 0, ci = first; c0 < n; c0 += kCh, ++ci) {
-    const int cn = min(kCh, n - c0);
-    const uint8_t* rec = recs + ((size_t)ci * Hv + h) * kRecBytes;
-    // q, k rows (bf16), the record's -W and M tiles, G
-    for (int idx = tid; idx < kCh * (kD / 4); idx += 256) {
-      const int row = idx >> 5, col = (idx & 31) * 4;
-      float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q;
-      if (row < cn) {
-        const float* r = conv_out + (size_t)(q0 + c0 + row) * C;
-        q = *reinterpret_cast<const float4*>(r + qofs + col);
-        k = *reinterpret_cast<const float4*>(r + kofs + col);
-      }
-      uint32_t* dq = reinterpret_cast<uint32_t*>(smem + GsSmem::Q + row * P2 + col * 2);
-      uint32_t* dk = reinterpret_cast<uint32_t*>(smem + GsSmem::K + row * P2 + col * 2);
-      dq[0] = gc_pack(q.x, q.y);
-      dq[1] = gc_pack(q.z, q.w);
-      dk[0] = gc_pack(k.x, k.y);
-      dk[1] = gc_pack(k.z, k.w);
+  for (int c = 0; c < nch; ++c) {
+    const int c0 = c * kCh, cn = min(kCh, n - c0);
+    const uint32_t boff = (c & 1) * GsSmem::BUF;
+    if (c + 1 < nch) {
+      gc_fetch_record(base + (boff ^ GsSmem::BUF), record(c + 1), tid);
+      gc_commit();
+      gc_wait<1>();
+    } else {
+      gc_wait<0>();
     }
-    for (int idx = tid; idx < kCh * (kD / 8); idx += 256) {   // -W: 16 B per piece
-      const int row = idx >> 4, c8 = (idx & 15) * 8;
-      *reinterpret_cast<uint4*>(smem + GsSmem::W + row * P2 + c8 * 2) =
-          *reinterpret_cast<const uint4*>(rec + kRecW + (row * kD + c8) * 2);
-    }
-    for (int idx = tid; idx < kCh * (kCh / 8); idx += 256) {  // M
-      const int row = idx >> 3, c8 = (idx & 7) * 8;
-      *reinterpret_cast<uint4*>(smem + GsSmem::M + row * Pm2 + c8 * 2) =
-          *reinterpret_cast<const uint4*>(rec + kRecM + (row * kCh + c8) * 2);
-    }
-    if (tid < kCh) sG[tid] = reinterpret_cast<const float*>(rec + kRecG)[tid];
     __syncthreads();
+    const uint32_t aQ = base + boff + GsSmem::Q, aK = base + boff + GsSmem::K, aW = base + boff + GsSmem::W;
+    const uint32_t aM = base + boff + GsSmem::M;
+    const uint8_t* sUt = smem + boff + GsSmem::Ut;
+    const float* sG = reinterpret_cast<const float*>(smem + boff + GsSmem::G);
 
     float accO[8][4];
     {
       float accU[8][4];
-      const uint32_t* Ut = reinterpret_cast<const uint32_t*>(rec + kRecU);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        const int c = 64 * nh + 8 * nt + 2 * t4;
+        const int cc = 64 * nh + 8 * nt + 2 * t4;
         const int i0 = 16 * mt + g;
-        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(Ut + ((i0 * kD + c) >> 1));
-        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(Ut + (((i0 + 8) * kD + c) >> 1));
+        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(sUt + i0 * P2 + cc * 2);
+        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(sUt + (i0 + 8) * P2 + cc * 2);
         accU[nt][0] = __low2float(lo);
         accU[nt][1] = __high2float(lo);
         accU[nt][2] = __low2float(hi);
@@ -712,10 +757,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
         const float gam = __expf(sG[i]), tail = __expf(Gl - sG[i]);
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-          const int c = 64 * nh + 8 * nt + 2 * t4;
+          const int cc = 64 * nh + 8 * nt + 2 * t4;
           const float u0 = accU[nt][2 * hf], u1 = accU[nt][2 * hf + 1];
-          *reinterpret_cast<uint32_t*>(smem + GsSmem::U + i * P2 + c * 2) = gc_pack(u0, u1);
-          *reinterpret_cast<uint32_t*>(smem + GsSmem::Us + i * P2 + c * 2) = gc_pack(tail * u0, tail * u1);
+          *reinterpret_cast<uint32_t*>(smem + GsSmem::U + i * P2 + cc * 2) = gc_pack(u0, u1);
+          *reinterpret_cast<uint32_t*>(smem + GsSmem::Us + i * P2 + cc * 2) = gc_pack(tail * u0, tail * u1);
           accO[nt][2 * hf] *= gam;
           accO[nt][2 * hf + 1] *= gam;
         }
@@ -742,8 +787,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
         float* orow = out + (size_t)(q0 + c0 + i) * Hv * kD + h * kD;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-          const int c = 64 * nh + 8 * nt + 2 * t4;
-          *reinterpret_cast<float2*>(orow + c) = make_float2(accO[nt][2 * hf], accO[nt][2 * hf + 1]);
+          const int cc = 64 * nh + 8 * nt + 2 * t4;
+          *reinterpret_cast<float2*>(orow + cc) = make_float2(accO[nt][2 * hf], accO[nt][2 * hf + 1]);
         }
       }
     }
@@ -767,9 +812,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
       }
 #pragma unroll
       for (int nt = 0; nt < 16; ++nt) {
-        const int c = nt * 8 + 2 * t4;
-        sS32[(r_lo * kP + c) >> 1] = gc_pack(Sacc[nt][0], Sacc[nt][1]);
-        sS32[(r_hi * kP + c) >> 1] = gc_pack(Sacc[nt][2], Sacc[nt][3]);
+        const int cc = nt * 8 + 2 * t4;
+        sS32[(r_lo * kP + cc) >> 1] = gc_pack(Sacc[nt][0], Sacc[nt][1]);
+        sS32[(r_hi * kP + cc) >> 1] = gc_pack(Sacc[nt][2], Sacc[nt][3]);
       }
     }
     __syncthreads();
@@ -806,7 +851,7 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
 // Bytes of the split form's workspace for a pass of T tokens in S sequences.
 int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv) {
   const int64_t maxc = T / kCh + S + 1;
-  const int64_t ints = ((4 + 2 * maxc + S) * 4 + 255) / 256 * 256;
+  const int64_t ints = ((4 + 2 * maxc + 2 * S) * 4 + 255) / 256 * 256;
   return ints + maxc * Hv * kRecBytes;
 }
 
@@ -823,7 +868,7 @@ void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const
     configured[dev] = true;
   }
   const int maxc = T / kCh + S + 1;
-  const int64_t ints = ((4 + 2 * (int64_t)maxc + S) * 4 + 255) / 256 * 256;
+  const int64_t ints = ((4 + 2 * (int64_t)maxc + 2 * S) * 4 + 255) / 256 * 256;
   int* wsi = reinterpret_cast<int*>(ws);
   uint8_t* recs = ws + ints;
   gdn_chunk_index_kernel<<<1, 256, 0, st>>>(seqs, S, maxc, wsi);
@@ -831,8 +876,8 @@ void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const
   gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col,
                                                                      a_col, A_log, dt_bias, Hv, Hk, seqs, wsi, recs);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  gdn_chunk_scan_kernel<<<dim3(S, Hv), 256, GsSmem::BYTES, st>>>(conv_out, C, qk_channels, Hv, Hk, seqs, sio,
-                                                                  ssm_state, gi, G, wsi, maxc, recs, out);
+  gdn_chunk_scan_kernel<<<dim3(Hv, S), 256, GsSmem::BYTES, st>>>(Hv, seqs, sio, ssm_state, gi, G, wsi, maxc, recs,
+                                                                  out);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
