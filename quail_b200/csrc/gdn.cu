@@ -263,7 +263,8 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
                       const int* sio, int S, float* ssm_state, int gi, int G, float* out, int dev,
                       cudaStream_t st);
 int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv);
-void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
+void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, float* conv_state, float q_scale,
+                            float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
                             int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
                             const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
                             float* out, uint8_t* ws, int dev, cudaStream_t st);
@@ -292,30 +293,34 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
   const int* sq = seqs.data_ptr<int>();
   const int* sio = state_io.data_ptr<int>();
-  dim3 g1(S, (C + 127) / 128);
-  const float q_scale = (float)(1.0 / std::sqrt((double)DK));
-  TORCH_CHECK(W == 4, "gdn: conv width 4");
-  gdn_conv_kernel<4><<<g1, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, C,
-                                         (int)(2 * Hk * DK), (int)DK, wconv.data_ptr<float>(), sq, sio,
-                                         conv_state.data_ptr<float>(), (int)gi, G, q_scale,
-                                         conv_out.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int b_col = C + Hv * DV, a_col = b_col + Hv;
   TORCH_CHECK(DV <= 128, "gdn: d_v <= 128");
   // mode 0: the split chunked form when some sequence has several new tokens
   // (T > S) and d_k = d_v = 128, else the per-token form; 1: per-token;
   // 2: chunked, one kernel; 3: chunked, split (index + prep + scan)
-  const bool chunked = DK == 128 && DV == 128 && (mode == 2 || mode == 3 || (mode == 0 && T > S));
+  const bool chunked = DK == 128 && DV == 128 && ld % 4 == 0 && (mode == 2 || mode == 3 || (mode == 0 && T > S));
   TORCH_CHECK(mode < 2 || chunked, "gdn: the chunked form needs d_k = d_v = 128");
+  const float q_scale = (float)(1.0 / std::sqrt((double)DK));
+  TORCH_CHECK(W == 4, "gdn: conv width 4");
   if (chunked && mode != 2) {
-    // the workspace comes from PyTorch's caching allocator on the current stream
+    // the workspace comes from PyTorch's caching allocator on the current stream;
+    // the conv runs token-parallel over the same chunk list
     auto ws = at::empty({gdn_chunk_ws_bytes(T, S, Hv)}, proj.options().dtype(at::kByte));
-    launch_gdn_chunk_split(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
+    launch_gdn_chunk_split(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), wconv.data_ptr<float>(),
+                           conv_state.data_ptr<float>(), q_scale, conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
                            reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
                            A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, T, S,
                            ssm_state.data_ptr<float>(), (int)gi, G, o.data_ptr<float>(), ws.data_ptr<uint8_t>(), dev,
                            st);
-  } else if (chunked) {
+  } else {
+    dim3 g1(S, (C + 127) / 128);
+    gdn_conv_kernel<4><<<g1, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, C,
+                                           (int)(2 * Hk * DK), (int)DK, wconv.data_ptr<float>(), sq, sio,
+                                           conv_state.data_ptr<float>(), (int)gi, G, q_scale,
+                                           conv_out.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  if (chunked && mode == 2) {
     launch_gdn_chunk(conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
                      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
                      A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, S,

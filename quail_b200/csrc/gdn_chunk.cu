@@ -828,6 +828,91 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
   }
 }
 
+// ------------------------------------------------------------------ conv, token-parallel
+// The causal depthwise conv (width 4) + SiLU + q/k L2 norm, one warp per
+// (token, 128-channel block), 4 channels per lane: a token reads its own
+// input row and the 3 before it (the source slot's window before the
+// sequence's first token), so tokens are independent; a 128-channel block
+// of q or k is one head, so its norm is a warp reduction. CTAs walk the
+// chunk list (64 tokens each). The new windows are written afterwards by
+// gdn_conv_window (a sequence's source and destination slot may be the same).
+__global__ void __launch_bounds__(256) gdn_conv_chunk_kernel(
+    const __nv_bfloat16* __restrict__ mixed, int ldm, int C, int qk_channels, const float* __restrict__ wconv,
+    const int* __restrict__ seqs, const int* __restrict__ sio, const float* __restrict__ conv_state, int gi, int G,
+    float q_scale, const int* __restrict__ ws, float* __restrict__ out) {
+  const int ci = blockIdx.x;
+  if (ci >= ws[0]) return;
+  const int2 e = reinterpret_cast<const int2*>(ws + 4)[ci];
+  const int s = e.x, c0 = e.y;
+  const int q0 = seqs[s * kChSeqInts], n = seqs[s * kChSeqInts + 1];
+  const int cn = min(kCh, n - c0);
+  const int src = sio[2 * s];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cb = blockIdx.y * 128, ch = cb + lane * 4;
+  const bool is_qk = cb < qk_channels, is_q = cb < qk_channels / 2;
+  float w[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = *reinterpret_cast<const float4*>(wconv + (size_t)(ch + j) * 4);
+    w[j][0] = v.x; w[j][1] = v.y; w[j][2] = v.z; w[j][3] = v.w;
+  }
+  const float* win = src >= 0 ? conv_state + ((size_t)src * G + gi) * 3 * C : nullptr;
+  for (int tt = warp; tt < cn; tt += 8) {
+    const int t = c0 + tt;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int tap = 0; tap < 4; ++tap) {
+      const int pos = t - 3 + tap;
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (pos >= 0) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(mixed + (size_t)(q0 + pos) * ldm + ch);
+        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+        x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
+      } else if (win != nullptr) {
+        const float4 v = *reinterpret_cast<const float4*>(win + (size_t)(3 + pos) * C + ch);
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += w[j][tap] * x[j];
+    }
+    float y[4], ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      y[j] = acc[j] / (1.f + __expf(-acc[j]));   // SiLU
+      ss += y[j] * y[j];
+    }
+    if (is_qk) {
+      ss = warp_sum(ss);
+      const float r = rsqrtf(fmaxf(ss, 1e-12f)) * (is_q ? q_scale : 1.f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] *= r;
+    }
+    *reinterpret_cast<float4*>(out + (size_t)(q0 + t) * C + ch) = make_float4(y[0], y[1], y[2], y[3]);
+  }
+}
+
+// The destination window of each sequence: its last 3 inputs (older ones from
+// the source window when it has fewer than 3 new tokens). One thread per channel.
+__global__ void __launch_bounds__(128) gdn_conv_window_kernel(const __nv_bfloat16* __restrict__ mixed, int ldm,
+                                                              int C, const int* __restrict__ seqs,
+                                                              const int* __restrict__ sio,
+                                                              float* __restrict__ conv_state, int gi, int G) {
+  const int s = blockIdx.x, c = blockIdx.y * 128 + threadIdx.x;
+  if (c >= C) return;
+  const int q0 = seqs[s * kChSeqInts], n = seqs[s * kChSeqInts + 1];
+  const int src = sio[2 * s], dst = sio[2 * s + 1];
+  float v[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int pos = n - 3 + j;
+    v[j] = pos >= 0 ? __bfloat162float(mixed[(size_t)(q0 + pos) * ldm + c])
+                    : (src >= 0 ? conv_state[(((size_t)src * G + gi) * 3 + (3 + pos)) * C + c] : 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) conv_state[(((size_t)dst * G + gi) * 3 + j) * C + c] = v[j];
+}
+
 }  // namespace
 
 // The chunked recurrence for one Gated DeltaNet layer (d_k = d_v = 128); the
@@ -855,7 +940,8 @@ int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv) {
   return ints + maxc * Hv * kRecBytes;
 }
 
-void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
+void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, float* conv_state, float q_scale,
+                            float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
                             int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
                             const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
                             float* out, uint8_t* ws, int dev, cudaStream_t st) {
@@ -872,6 +958,11 @@ void launch_gdn_chunk_split(const float* conv_out, int C, int qk_channels, const
   int* wsi = reinterpret_cast<int*>(ws);
   uint8_t* recs = ws + ints;
   gdn_chunk_index_kernel<<<1, 256, 0, st>>>(seqs, S, maxc, wsi);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  gdn_conv_chunk_kernel<<<dim3(maxc, C / 128), 256, 0, st>>>(mixed, ldab, C, qk_channels, wconv, seqs, sio,
+                                                              conv_state, gi, G, q_scale, wsi, conv_out);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  gdn_conv_window_kernel<<<dim3(S, C / 128), 128, 0, st>>>(mixed, ldab, C, seqs, sio, conv_state, gi, G);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col,
                                                                      a_col, A_log, dt_bias, Hv, Hk, seqs, wsi, recs);
