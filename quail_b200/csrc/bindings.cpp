@@ -27,6 +27,8 @@ void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, con
 void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
              const c10::optional<torch::Tensor>& residual);
+void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
+                double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual);
 void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps, torch::Tensor& y8,
                       torch::Tensor& sf, int64_t T);
 void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch::Tensor& sf, int64_t T);
@@ -125,6 +127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b"), py::arg("sa"), py::arg("sb"), py::arg("sb_gran"), py::arg("epi"), py::arg("out"),
         py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
   m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
+  m.def("gemm_nvfp4", &qb::gemm_nvfp4, "tcgen05 NVFP4 GEMM: E2M1 operands, UE4M3 16-element block scales");
   m.def("rmsnorm_quant_mx", &qb::rmsnorm_quant_mx);
   m.def("quant_rows_mx", &qb::quant_rows_mx);
   m.def("row_argmax_lse", &qb::row_argmax_lse);

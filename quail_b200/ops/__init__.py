@@ -19,6 +19,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     final_norm_readout,
     gemm,
     gemm_mx,
+    gemm_nvfp4,
     sf_bytes,
     rmsnorm_quant_mx,
     quant_rows_mx,

@@ -105,6 +105,22 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     return out
 
 
+def gemm_nvfp4(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float, *,
+               epi: int = EPI_BF16, out: torch.Tensor | None = None, residual: torch.Tensor | None = None):
+    """D = alpha . A . B^T on the tcgen05 NVFP4 MMA (kind::mxf4nvf4, 16-value UE4M3 block scales).
+
+    A [M, K/2], B [N, K/2] packed E2M1 (uint8); sfa / sfb their block-scale
+    atoms (quail_b200.ops.quant.quantize_nvfp4); alpha the product of the two
+    global scales. EPI_BF16 or EPI_RESIDUAL (out = acc + residual).
+    """
+    M, N = a.shape[0], b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    count_launch()
+    native().gemm_nvfp4(a, sfa, b, sfb, float(alpha), epi, out, residual)
+    return out
+
+
 def rmsnorm_quant_mx(x: torch.Tensor, w: torch.Tensor, eps: float, *, out=None, out_sf=None, rows=None):
     """RMSNorm -> (e4m3 [T, H], UE8M0 scale bytes, one per 32 columns)."""
     T = x.shape[0] if rows is None else rows

@@ -164,3 +164,58 @@ def interleave_gate_up_mx(w: torch.Tensor, block: int = 128):
     q = torch.stack([qg.view(inter // 64, 64, K), qu.view(inter // 64, 64, K)], dim=1).reshape(I2, K)
     e = torch.stack([eg.view(inter // 64, 64, -1), eu.view(inter // 64, 64, -1)], dim=1).reshape(I2, -1)
     return q.contiguous(), pack_sf_atoms(e)
+
+
+# ---------------------------------------------------------------- NVFP4
+# E2M1 values by code (sign in bit 3): 0, 0.5, 1, 1.5, 2, 3, 4, 6
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+FP4_MAX = 6.0
+
+
+def _e2m1_codes(x: torch.Tensor) -> torch.Tensor:
+    """Round to the nearest E2M1 value (ties to the even code); 4-bit codes as uint8."""
+    grid = torch.tensor(E2M1_VALUES, device=x.device)
+    a = x.abs().clamp(max=FP4_MAX)
+    d = (a[..., None] - grid).abs()
+    best = d.min(dim=-1, keepdim=True).values
+    # among equally near values the even code (codes 0..7 in order of value)
+    cand = torch.where(d <= best + 1e-12, torch.arange(8, device=x.device), 99)
+    even = torch.where(cand % 2 == 0, cand, 99).min(dim=-1).values
+    code = torch.where(even < 99, even, cand.min(dim=-1).values)
+    return (code | ((x < 0) & (code > 0)).to(code.dtype) * 8).to(torch.uint8)
+
+
+def quantize_nvfp4(x: torch.Tensor, global_scale: float | None = None):
+    """[R, K] float -> (packed E2M1 [R, K/2] uint8, UE4M3 block-scale atoms, global scale).
+
+    One e4m3 scale per row and 16 values (amax / 6, divided by the global
+    scale so that it fits e4m3's range: global = amax(x) / (448 * 6)); two
+    codes per byte, the even element in the low nibble. Dequantized value =
+    E2M1 x block scale x global scale.
+    """
+    R, K = x.shape
+    assert K % 64 == 0
+    xf = x.float()
+    if global_scale is None:
+        global_scale = max(float(xf.abs().max()), 1e-12) / (FP8_MAX * FP4_MAX)
+    g = xf.view(R, K // 16, 16)
+    bs = (g.abs().amax(dim=2) / FP4_MAX / global_scale).clamp(max=FP8_MAX)
+    bs8 = bs.to(torch.float8_e4m3fn)
+    scale = bs8.float() * global_scale
+    q = torch.where(scale[..., None] > 0, g / scale[..., None].clamp(min=1e-30), torch.zeros_like(g))
+    codes = _e2m1_codes(q).view(R, K)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    return packed, pack_sf_atoms(bs8.view(torch.uint8)), global_scale
+
+
+def dequantize_nvfp4(packed: torch.Tensor, sf: torch.Tensor, global_scale: float, K: int) -> torch.Tensor:
+    """Inverse of quantize_nvfp4 -> fp32 [R, K]."""
+    R = packed.shape[0]
+    lo, hi = packed & 0xF, packed >> 4
+    codes = torch.stack([lo, hi], dim=-1).view(R, K).long()
+    vals = torch.tensor(E2M1_VALUES, device=packed.device)[codes & 7] * torch.where(codes >= 8, -1.0, 1.0)
+    KB = K // 16
+    Rp = -(-R // 128) * 128
+    e = sf[:(Rp // 128) * (KB // 4) * 512].view(Rp // 128, KB // 4, 32, 4, 4).permute(0, 3, 2, 1, 4)
+    bs = e.contiguous().view(Rp, KB)[:R].view(torch.float8_e4m3fn).float()
+    return vals * bs.repeat_interleave(16, dim=1) * global_scale

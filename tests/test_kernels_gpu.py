@@ -327,3 +327,24 @@ def test_sae_topk(R, F, keep):
     for r in range(R):
         sel = ids[r][pos[r]]
         assert sel.unique().numel() == sel.numel()
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 512, 512), (128, 272, 1024), (1000, 256, 256)])
+def test_gemm_nvfp4_matches_dequantized(M, N, K):
+    """The NVFP4 tcgen05 GEMM against fp32 matmul of the dequantized operands (same values:
+    only accumulation order and the bf16 output rounding differ), plain and residual epilogues."""
+    from quail_b200.ops.quant import dequantize_nvfp4, quantize_nvfp4
+    torch.manual_seed(M + N + K)
+    a = torch.randn(M, K, device="cuda")
+    b = torch.randn(N, K, device="cuda") * 0.1
+    pa, sa, ga = quantize_nvfp4(a)
+    pb, sb, gb = quantize_nvfp4(b)
+    want = dequantize_nvfp4(pa, sa, ga, K) @ dequantize_nvfp4(pb, sb, gb, K).t()
+    got = ops.gemm_nvfp4(pa, sa, pb, sb, ga * gb)
+    assert ops.read_and_clear_error(0) == 0
+    err = ((got.float() - want).norm() / want.norm()).item()
+    assert err < 1e-2, err
+    r = torch.randn(M, N, device="cuda").bfloat16()
+    got_r = ops.gemm_nvfp4(pa, sa, pb, sb, ga * gb, epi=ops.EPI_RESIDUAL, residual=r)
+    err_r = ((got_r.float() - (want + r.float())).norm() / (want + r.float()).norm()).item()
+    assert err_r < 1e-2, err_r
