@@ -28,7 +28,10 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
              const c10::optional<torch::Tensor>& residual);
 void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
-                double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual);
+                double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual,
+                const c10::optional<torch::Tensor>& row_scale);
+void nvfp4_quant_rows(const torch::Tensor& x, bool swiglu, torch::Tensor& q, torch::Tensor& sf,
+                      torch::Tensor& row_scale);
 void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps, torch::Tensor& y8,
                       torch::Tensor& sf, int64_t T);
 void quant_rows_mx(const torch::Tensor& x, bool swiglu, torch::Tensor& y8, torch::Tensor& sf, int64_t T);
@@ -128,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
   m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
   m.def("gemm_nvfp4", &qb::gemm_nvfp4, "tcgen05 NVFP4 GEMM: E2M1 operands, UE4M3 16-element block scales");
+  m.def("nvfp4_quant_rows", &qb::nvfp4_quant_rows, "bf16 rows (or SwiGLU of gate|up) -> NVFP4 + per-row scale");
   m.def("rmsnorm_quant_mx", &qb::rmsnorm_quant_mx);
   m.def("quant_rows_mx", &qb::quant_rows_mx);
   m.def("row_argmax_lse", &qb::row_argmax_lse);

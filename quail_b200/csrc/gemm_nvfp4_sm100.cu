@@ -32,6 +32,8 @@
 #include "gemm_sm100.h"
 #include "mx_common.cuh"
 
+#include <cuda_fp8.h>
+
 namespace qb {
 
 namespace {
@@ -49,6 +51,7 @@ constexpr int kF4SfbCol = kF4BN + 16;              // 4 steps x 8 columns
 struct F4Params {
   int M, N, K;
   float alpha;
+  const float* row_scale;   // optional per-row scale of A (dynamic activation quantization)
   __nv_bfloat16* D;
   int ldd;
   const __nv_bfloat16* R;
@@ -227,13 +230,14 @@ __global__ void __launch_bounds__(64 + kF4BN, 1)
       tc_fence_after();
       float acc[128];
       const uint32_t taddr = tmem_base + lane_base + (uint32_t)(h * 128);
+      const float scale = p.alpha * ((p.row_scale != nullptr && m < p.M) ? p.row_scale[m] : 1.f);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         QB_TMEM_LD32(taddr + c * 32, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[c * 32 + i] = __uint_as_float(r[i]) * p.alpha;
+        for (int i = 0; i < 32; ++i) acc[c * 32 + i] = __uint_as_float(r[i]) * scale;
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
@@ -266,6 +270,67 @@ __global__ void __launch_bounds__(64 + kF4BN, 1)
   }
 }
 
+// ------------------------------------------------------------------ activation quantization
+// One CTA per row: x (bf16 [T, K]; with swiglu, [T, 2K] = gate | up and the
+// value is silu(gate) * up) -> packed E2M1 [T, K/2], UE4M3 block-scale atoms
+// and the row's scale g = amax / (448 * 6): block scale = e4m3(amax_block / 6 / g),
+// code = E2M1(x / (block scale * g)), both by the hardware's round-to-nearest
+// conversions. The GEMM's epilogue multiplies by g (row_scale).
+__device__ __forceinline__ float f4_in(const __nv_bfloat16* row, int K, int j, bool swiglu) {
+  const float a = __bfloat162float(row[j]);
+  if (!swiglu) return a;
+  const float u = __bfloat162float(row[K + j]);
+  return a / (1.f + __expf(-a)) * u;
+}
+
+__device__ __forceinline__ uint8_t f4_pack2(float lo, float hi) {
+  // cvt packs its first source into the upper nibble
+  uint16_t r;
+  asm("{\n\t.reg .b8 b;\n\tcvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n\tcvt.u16.u8 %0, b;\n\t}"
+      : "=h"(r)
+      : "f"(hi), "f"(lo));
+  return (uint8_t)r;
+}
+
+__global__ void __launch_bounds__(256) nvfp4_quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
+                                                               int swiglu, uint8_t* __restrict__ q, int ldq,
+                                                               uint8_t* __restrict__ sf, float* __restrict__ row_scale) {
+  __shared__ float red[8];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const __nv_bfloat16* row = x + (size_t)t * ldx;
+  const int nb = K / 16;
+  float amax = 0.f;
+  for (int b = tid; b < nb; b += 256)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f4_in(row, K, b * 16 + i, swiglu)));
+  amax = warp_max(amax);
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+  const float g = fmaxf(amax, 1e-30f) / (448.f * 6.f);
+  if (tid == 0) row_scale[t] = g;
+  const float ig = 1.f / g;
+  for (int b = tid; b < nb; b += 256) {
+    float v[16], bmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = f4_in(row, K, b * 16 + i, swiglu);
+      bmax = fmaxf(bmax, fabsf(v[i]));
+    }
+    const __nv_fp8_e4m3 bs(bmax * (1.f / 6.f) * ig);
+    const float bsf = float(bs);
+    const float inv = bsf > 0.f ? 1.f / (bsf * g) : 0.f;
+    __align__(8) uint8_t out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = f4_pack2(v[2 * i] * inv, v[2 * i + 1] * inv);
+    *reinterpret_cast<uint2*>(q + (size_t)t * ldq + b * 8) = *reinterpret_cast<const uint2*>(out);
+    sf[((size_t)(t / 128) * (K / 64) + b / 4) * 512 + (t % 32) * 16 + ((t % 128) / 32) * 4 + (b % 4)] =
+        *reinterpret_cast<const uint8_t*>(&bs);
+  }
+}
+
 template <int EPI>
 void launch_f4(const CUtensorMap& ta, const CUtensorMap& tb, F4Params& p, cudaStream_t st, int dev) {
   auto kern = gemm_nvfp4_kernel<EPI>;
@@ -284,7 +349,8 @@ void launch_f4(const CUtensorMap& ta, const CUtensorMap& tb, F4Params& p, cudaSt
 // a: [M, K/2] packed E2M1 (uint8), sfa: its UE4M3 block-scale atoms; b: [N, K/2], sfb;
 // out bf16 [M, N] = alpha * a . b^T (+ residual with EPI_RESIDUAL).
 void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
-                double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual) {
+                double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual,
+                const c10::optional<torch::Tensor>& row_scale) {
   TORCH_CHECK(a.scalar_type() == at::kByte && b.scalar_type() == at::kByte, "gemm_nvfp4: packed E2M1 as uint8");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
               "gemm_nvfp4: shapes");
@@ -316,6 +382,10 @@ void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::T
   p.num_n_tiles = (N + kF4BN - 1) / kF4BN;
   p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldd = out.stride(0);
+  if (row_scale.has_value()) {
+    TORCH_CHECK(row_scale->scalar_type() == at::kFloat && row_scale->numel() >= M, "gemm_nvfp4: fp32 row scales");
+    p.row_scale = row_scale->data_ptr<float>();
+  }
   if (epi == kEpiResidual) {
     TORCH_CHECK(residual.has_value() && residual->scalar_type() == at::kBFloat16, "residual");
     p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
@@ -330,6 +400,32 @@ void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::T
     launch_f4<kEpiBf16>(ta, tb, p, st, dev);
   else
     launch_f4<kEpiResidual>(ta, tb, p, st, dev);
+}
+
+// x bf16 [T, K] (swiglu: [T, 2K] gate | up) -> q uint8 [T, K/2], sf atoms, row_scale fp32 [T]
+void nvfp4_quant_rows(const torch::Tensor& x, bool swiglu, torch::Tensor& q, torch::Tensor& sf,
+                      torch::Tensor& row_scale) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "nvfp4_quant_rows: bf16 rows");
+  const int T = x.size(0), K = swiglu ? x.size(1) / 2 : x.size(1);
+  TORCH_CHECK(K % 64 == 0, "nvfp4_quant_rows: K % 64 == 0");
+  TORCH_CHECK(q.scalar_type() == at::kByte && q.size(0) >= T && q.size(1) == K / 2 && q.stride(0) % 8 == 0,
+              "nvfp4_quant_rows: q [T, K/2]");
+  TORCH_CHECK(sf.scalar_type() == at::kByte && sf.numel() >= (int64_t)((T + 127) / 128) * (K / 64) * 512,
+              "nvfp4_quant_rows: scale atoms");
+  TORCH_CHECK(row_scale.scalar_type() == at::kFloat && row_scale.numel() >= T, "nvfp4_quant_rows: row scales");
+  if (T == 0) return;
+  const int dev = x.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  if (T % 128) {
+    // rows past T in the last 128-row atom block read as zero scales
+    const int64_t tail = (int64_t)(T / 128) * (K / 64) * 512;
+    C10_CUDA_CHECK(cudaMemsetAsync(sf.data_ptr<uint8_t>() + tail, 0, (size_t)(K / 64) * 512, st));
+  }
+  nvfp4_quant_rows_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), K,
+                                             swiglu ? 1 : 0, q.data_ptr<uint8_t>(), q.stride(0),
+                                             sf.data_ptr<uint8_t>(), row_scale.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace qb

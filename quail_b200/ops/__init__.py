@@ -20,6 +20,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     gemm,
     gemm_mx,
     gemm_nvfp4,
+    quant_rows_nvfp4,
     sf_bytes,
     rmsnorm_quant_mx,
     quant_rows_mx,

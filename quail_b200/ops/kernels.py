@@ -105,19 +105,34 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     return out
 
 
+def quant_rows_nvfp4(x: torch.Tensor, *, swiglu: bool = False):
+    """bf16 rows (or silu(gate) * up of [T, 2K] gate | up) -> (packed E2M1 [T, K/2], UE4M3 block-scale
+    atoms, fp32 per-row scale [T]) for gemm_nvfp4's A side."""
+    T = x.shape[0]
+    K = x.shape[1] // 2 if swiglu else x.shape[1]
+    q = torch.empty(T, K // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(-(-T // 128) * (K // 64) * 512, dtype=torch.uint8, device=x.device)
+    rs = torch.empty(T, dtype=torch.float32, device=x.device)
+    count_launch()
+    native().nvfp4_quant_rows(x, swiglu, q, sf, rs)
+    return q, sf, rs
+
+
 def gemm_nvfp4(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float, *,
-               epi: int = EPI_BF16, out: torch.Tensor | None = None, residual: torch.Tensor | None = None):
+               epi: int = EPI_BF16, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+               row_scale: torch.Tensor | None = None):
     """D = alpha . A . B^T on the tcgen05 NVFP4 MMA (kind::mxf4nvf4, 16-value UE4M3 block scales).
 
     A [M, K/2], B [N, K/2] packed E2M1 (uint8); sfa / sfb their block-scale
     atoms (quail_b200.ops.quant.quantize_nvfp4); alpha the product of the two
-    global scales. EPI_BF16 or EPI_RESIDUAL (out = acc + residual).
+    global scales, row_scale an optional per-row scale of A (quant_rows_nvfp4's).
+    EPI_BF16 or EPI_RESIDUAL (out = acc + residual).
     """
     M, N = a.shape[0], b.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
     count_launch()
-    native().gemm_nvfp4(a, sfa, b, sfb, float(alpha), epi, out, residual)
+    native().gemm_nvfp4(a, sfa, b, sfb, float(alpha), epi, out, residual, row_scale)
     return out
 
 

@@ -348,3 +348,28 @@ def test_gemm_nvfp4_matches_dequantized(M, N, K):
     got_r = ops.gemm_nvfp4(pa, sa, pb, sb, ga * gb, epi=ops.EPI_RESIDUAL, residual=r)
     err_r = ((got_r.float() - (want + r.float())).norm() / (want + r.float()).norm()).item()
     assert err_r < 1e-2, err_r
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_nvfp4_activation_quant_and_gemm(swiglu):
+    """Per-row dynamic NVFP4 quantization (plain rows and SwiGLU of gate | up): the codes
+    dequantize to within fp4 error of the input, and the GEMM with per-row scales equals the
+    fp32 matmul of the dequantized operands."""
+    from quail_b200.ops.quant import dequantize_nvfp4, quantize_nvfp4
+    torch.manual_seed(5)
+    T, K, N = 333, 1024, 512
+    x = (torch.randn(T, 2 * K if swiglu else K, device="cuda") * 3).bfloat16()
+    ref_x = x.float()
+    if swiglu:
+        ref_x = torch.nn.functional.silu(ref_x[:, :K]) * ref_x[:, K:]
+    q, sf, rs = ops.quant_rows_nvfp4(x, swiglu=swiglu)
+    xd = dequantize_nvfp4(q, sf, 1.0, K) * rs[:, None]
+    err_q = ((xd - ref_x).norm() / ref_x.norm()).item()
+    assert err_q < 0.15, err_q          # E2M1 with 16-value blocks: about 0.1 on Gaussian rows
+    w = torch.randn(N, K, device="cuda") * 0.05
+    pw, sw, gw = quantize_nvfp4(w)
+    want = xd @ dequantize_nvfp4(pw, sw, gw, K).t()
+    got = ops.gemm_nvfp4(q, sf, pw, sw, gw, row_scale=rs)
+    assert ops.read_and_clear_error(0) == 0
+    err = ((got.float() - want).norm() / want.norm()).item()
+    assert err < 1e-2, err
