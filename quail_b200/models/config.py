@@ -51,6 +51,7 @@ class DecoderConfig:
     # what the model answers with: "generative" (LM head), "reranker" (yes / no
     # logits of a Qwen3 reranker prompt, AI.SCORE only) or "decision" (an
     # option-scoring head over the backbone's rows, no text output)
+    mlp_fp4: bool = False            # MLP projections in NVFP4 (E2M1 + UE4M3 16-value blocks)
     role: str = "generative"
     prompt_layout: str = "ai-if"     # "ai-if" or "decision2-noul"
     decision_head_dim: int = 0
@@ -205,6 +206,9 @@ QWEN35_27B = QWEN35_4B.with_(name="qwen3.5-27b", layers=64, hidden=5120, num_q_h
                              intermediate=17408, tied_head=False, gdn_value_heads=48, layer_kinds=_Q35_KINDS * 16)
 QWEN35_27B_FP8 = QWEN35_27B.with_(name="qwen3.5-27b-fp8", weight_dtype="fp8")
 QWEN38_27B_FP8 = QWEN35_27B_FP8.with_(name="qwen3.8-27b-fp8")
+# the NVFP4 checkpoint: attention in fp8, MLP in NVFP4 (the reference spec's mlp_weight_precision = "fp4")
+QWEN38_27B_NVFP4 = QWEN38_27B_FP8.with_(name="qwen3.8-27b-nvfp4", mlp_fp4=True)
+QWEN35_GPU_TINY_NVFP4 = QWEN35_GPU_TINY.with_(name="qwen3.5-gpu-tiny-nvfp4", weight_dtype="fp8", mlp_fp4=True)
 # Qwen3.6-35B-A3B: the Qwen3.5 hybrid with 256 routed experts (top 8) and a shared expert
 # (the reference spec quail/specs/data/models/qwen3.6-35b-a3b-fp8.toml; HF Qwen3_5MoeSparseMoeBlock)
 QWEN36_35B_A3B = QWEN35_4B.with_(name="qwen3.6-35b-a3b-fp8", layers=40, hidden=2048, num_q_heads=16,
@@ -229,7 +233,8 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
                                QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY,
                                QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, QWEN35_27B_FP8, QWEN38_27B_FP8,
-                               QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY)}
+                               QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY, QWEN38_27B_NVFP4,
+                               QWEN35_GPU_TINY_NVFP4)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -264,6 +269,8 @@ MODEL_CONFIGS = {
     "qwen3.5-gpu-tiny-fp8": QWEN35_GPU_TINY_FP8,
     "qwen3.5-27b-fp8": QWEN35_27B_FP8,
     "qwen3.8-27b-fp8": QWEN38_27B_FP8,
+    "qwen3.8-27b-nvfp4": QWEN38_27B_NVFP4,
+    "qwen3.5-gpu-tiny-nvfp4": QWEN35_GPU_TINY_NVFP4,
     "qwen3.6-35b-a3b-fp8": QWEN36_35B_A3B,
     "qwen3.6-moe-gpu-tiny": QWEN36_MOE_GPU_TINY,
     "qwen3.6-moe-tiny": QWEN36_MOE_TINY,

@@ -106,6 +106,7 @@ class Qwen35Reference:
         # requantization, e4m3 + 1x32 scales on every fp8 GEMM input, and a
         # bf16 residual stream; the Gated DeltaNet projections stay as stored
         self.emulate = emulate_kernels and cfg.fp8
+        self.fp4 = self.emulate and cfg.mlp_fp4
 
         def dequantized(ck, name):
             if not self.emulate or ".linear_attn." in name or ck.get(name + ".weight_scale_inv") is None:
@@ -130,6 +131,15 @@ class Qwen35Reference:
                                    f(dequantized(ckpt, m + "shared_expert.up_proj")),
                                    f(dequantized(ckpt, m + "shared_expert.down_proj")))
                     L["shared_gate"] = f(ckpt[m + "shared_expert_gate.weight"])
+            elif self.fp4:
+                # the kernels' NVFP4 weights: gate | up quantized together, down alone
+                from quail_b200.models.weights import dequantized as plain
+                from quail_b200.ops.quant import dequantize_nvfp4, quantize_nvfp4
+                gu = torch.cat([plain(ckpt, p + "mlp.gate_proj"), plain(ckpt, p + "mlp.up_proj")]).to(device)
+                gu = dequantize_nvfp4(*quantize_nvfp4(gu), gu.shape[1])
+                wd = plain(ckpt, p + "mlp.down_proj").to(device)
+                L.update(wg=f(gu[:gu.shape[0] // 2]), wu=f(gu[gu.shape[0] // 2:]),
+                         wd=f(dequantize_nvfp4(*quantize_nvfp4(wd), wd.shape[1])))
             else:
                 L.update(wg=f(dequantized(ckpt, p + "mlp.gate_proj")), wu=f(dequantized(ckpt, p + "mlp.up_proj")),
                          wd=f(dequantized(ckpt, p + "mlp.down_proj")))
@@ -225,6 +235,12 @@ class Qwen35Reference:
         return dequantize_mx(*quantize_act_mx(x.bfloat16().float())).to(x.dtype)
 
     def _mlp(self, x, wg, wu, wd):
+        if self.fp4 and not self.cfg.is_moe:
+            from quail_b200.ops.quant import fake_nvfp4_rows
+            x4 = fake_nvfp4_rows(x.bfloat16().float())
+            gu = torch.cat([x4 @ wg.t(), x4 @ wu.t()], dim=1).bfloat16().float()
+            a = ref.silu_mul(gu[:, :wg.shape[0]], gu[:, wg.shape[0]:])
+            return fake_nvfp4_rows(a) @ wd.t()
         return self._q(ref.silu_mul(self._q(x) @ wg.t(), self._q(x) @ wu.t())) @ wd.t()
 
     # ------------------------------------------------------------ forward

@@ -42,7 +42,8 @@ class Qwen35Pipeline:
 
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None,
                  max_tokens: int = 16384):
-        from quail_b200.ops.quant import interleave_gate_up, interleave_gate_up_mx, quantize_weight_mx
+        from quail_b200.ops.quant import (interleave_gate_up, interleave_gate_up_mx, quantize_nvfp4,
+                                          quantize_weight_mx)
         assert cfg.is_hybrid
         self.cfg = cfg
         self.device = device
@@ -96,6 +97,13 @@ class Qwen35Pipeline:
                 self.layers.append(L)
                 continue
             gu = torch.cat([fp32(p + "mlp.gate_proj"), fp32(p + "mlp.up_proj")])
+            if cfg.mlp_fp4:
+                # NVFP4 MLP: gate | up rows (not interleaved: the SwiGLU runs in the
+                # activation quantizer), one global scale per weight
+                L["wgu4"] = quantize_nvfp4(gu)
+                L["wd4"] = quantize_nvfp4(fp32(p + "mlp.down_proj"))
+                self.layers.append(L)
+                continue
             if self.fp8:
                 L["wgu"], L["sgu"] = interleave_gate_up_mx(gu)
                 L["wd"], L["sd"] = quantize_weight_mx(fp32(p + "mlp.down_proj"))
@@ -215,6 +223,15 @@ class Qwen35Pipeline:
                 ai += 1
             if self.ep is not None:
                 self._moe_mlp(h, L)
+                continue
+            if "wgu4" in L:
+                x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+                q, sf, rs = ops.quant_rows_nvfp4(x)
+                wq, ws, wg = L["wgu4"]
+                gu = ops.gemm_nvfp4(q, sf, wq, ws, wg, row_scale=rs)
+                q, sf, rs = ops.quant_rows_nvfp4(gu, swiglu=True)
+                wq, ws, wg = L["wd4"]
+                ops.gemm_nvfp4(q, sf, wq, ws, wg, row_scale=rs, epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 continue
             if self.fp8:
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)

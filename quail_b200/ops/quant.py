@@ -219,3 +219,18 @@ def dequantize_nvfp4(packed: torch.Tensor, sf: torch.Tensor, global_scale: float
     e = sf[:(Rp // 128) * (KB // 4) * 512].view(Rp // 128, KB // 4, 32, 4, 4).permute(0, 3, 2, 1, 4)
     bs = e.contiguous().view(Rp, KB)[:R].view(torch.float8_e4m3fn).float()
     return vals * bs.repeat_interleave(16, dim=1) * global_scale
+
+
+def fake_nvfp4_rows(x: torch.Tensor) -> torch.Tensor:
+    """fp32 values of the per-row dynamic NVFP4 quantization of x [R, K] (the GPU quantizer's
+    rule: row scale amax / (448 * 6), e4m3 block scales of 16 values, E2M1 codes)."""
+    R, K = x.shape
+    xf = x.float()
+    g = (xf.abs().amax(dim=1, keepdim=True).clamp(min=1e-30) / (FP8_MAX * FP4_MAX))      # [R, 1]
+    blocks = xf.view(R, K // 16, 16)
+    bs = (blocks.abs().amax(dim=2) / FP4_MAX / g).to(torch.float8_e4m3fn).float()         # [R, K/16]
+    scale = bs * g
+    q = torch.where(scale[..., None] > 0, blocks / scale[..., None].clamp(min=1e-30), torch.zeros_like(blocks))
+    codes = _e2m1_codes(q).long()
+    vals = torch.tensor(E2M1_VALUES, device=x.device)[codes & 7] * torch.where(codes >= 8, -1.0, 1.0)
+    return (vals * scale[..., None]).view(R, K)

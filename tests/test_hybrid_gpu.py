@@ -134,7 +134,8 @@ def test_gdn_layer_against_recurrence(dk, mode):
         assert rel_err(y[a:a + n].view(n, Hv, dv), want_y) < 1e-2
 
 
-@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.5-gpu-tiny-fp8", "qwen3.6-moe-gpu-tiny"])
+@pytest.mark.parametrize("name", ["qwen3.5-gpu-tiny", "qwen3.5-gpu-tiny-fp8", "qwen3.6-moe-gpu-tiny",
+                                  "qwen3.5-gpu-tiny-nvfp4"])
 def test_hybrid_pipeline_matches_fp32_model(name):
     """bf16 and fp8 checkpoints (the fp8 one: attention and MLP on the block-scaled fp8 GEMM)
     against the fp32 model of the same (dequantized) weights."""
