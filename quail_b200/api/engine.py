@@ -224,7 +224,7 @@ class ModelEngine:
                 suffix = tok.encode(c.tail)
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
-                      offsets=offsets)
+                      offsets=offsets, copy=c.kind == "extract")
             if offsets:
                 pass
             elif c.kind in ("filter", "score"):

@@ -43,6 +43,7 @@ class SeqSpec:
     tag: object = None
     readout_rows: tuple | None = None  # offsets of new tokens to read (default: the last one)
     full: bool = False     # also read argmax and log-sum-exp over the whole vocabulary
+    topk: bool = False     # and the best few token ids with their logits
 
 
 @dataclass
@@ -62,6 +63,7 @@ class Chunk:
     host: dict | None = None   # numpy copies (tests, CPU reference)
     upload_bytes: int = 0
     full_readout: bool = False  # readout rows also need full-vocabulary argmax / log-sum-exp
+    topk: bool = False          # and the top-k token ids and logits (ops.READOUT_TOPK)
 
 
 class ChunkPacker:
@@ -91,7 +93,8 @@ class ChunkPacker:
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
                      final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2), readout_tags=tags,
                      num_seqs=len(specs), host=host, upload_bytes=int(flat.nbytes),
-                     full_readout=any(s.full and s.readout for s in specs))
+                     full_readout=any(s.full and s.readout for s in specs),
+                     topk=any(s.topk and s.readout for s in specs))
 
     def host_parts(self, specs: list[SeqSpec]) -> tuple[dict, list]:
         """The chunk's metadata as numpy arrays (keys of PARTS) and its readout tags.

@@ -52,7 +52,7 @@ class _Entry:
         self.out = None
         self.launches = 0
 
-    def chunk(self, full: bool) -> Chunk:
+    def chunk(self, full: bool, topk: bool = False) -> Chunk:
         v, o = {}, 0
         for k in PARTS:
             v[k] = self.buf[o:o + self.sizes[k]]
@@ -60,7 +60,7 @@ class _Entry:
         return Chunk(num_tokens=self.B, ids=v["ids"], positions=v["positions"], slots=v["slots"],
                      seqs=v["seqs"].view(-1, SEQ_INTS), tiles=v["tiles"].view(-1, 2), page_list=v["page_list"],
                      final_rows=v["final_rows"], dseqs=v["dseqs"], state_io=v["state_io"].view(-1, 2),
-                     num_seqs=self.B, full_readout=full)
+                     num_seqs=self.B, full_readout=full, topk=topk)
 
     def fill(self, host: dict) -> int:
         """Write a pass's metadata, padded to the bucket, into the staging image; returns its bytes."""
@@ -125,7 +125,7 @@ class DecodeGraphs:
                 return b
         return None
 
-    def run(self, host: dict, full: bool):
+    def run(self, host: dict, full: bool, topk: bool = False):
         """Run one decode pass from its host metadata; returns (readout rows [R, W], upload bytes)
         or None when the pass has no bucket (too many tokens)."""
         from quail_b200 import ops
@@ -138,17 +138,17 @@ class DecodeGraphs:
             self.entries.clear()
             self._rows_key = key
         pl_need = host["page_list"].size
-        e = self.entries.get((B, full))
+        e = self.entries.get((B, full, topk))
         if e is not None and pl_need > e.pl_cap:
             e = None
         if e is None:
             cap = 1 << max(10, int(np.ceil(np.log2(max(pl_need, 1)))) + 1)
             e = _Entry(B, cap, self.device)
-            self.entries[(B, full)] = e
+            self.entries[(B, full, topk)] = e
         nbytes = e.fill(host)
         R = host["final_rows"].size
         if e.graph is None:
-            chunk = e.chunk(full)
+            chunk = e.chunk(full, topk)
             out = self.model.forward_chunk(chunk, self.arena)      # eager: this pass's answer
             torch.cuda.current_stream().synchronize()
             n0 = ops.launch_count()

@@ -23,7 +23,9 @@ Readouts:
             position (the reference's label trie, label_stages.py)
   map       greedy decoding: each step appends the argmax token to the
             question's own pages until a stop token or max_tokens
-            (map_decoder.py); extract decodes the same way after the phrase cue
+            (map_decoder.py); extract decodes after the phrase cue with the
+            copy constraint: the best of the readout's top-k tokens that
+            continues a verbatim copy of the document (extract/copy.py)
   decision  a decision model's head scores the option rows against the last
             row (filter: Yes > No; score: sigmoid(Yes - No); classify: the
             best label), readout.py:633-728
@@ -45,6 +47,7 @@ from functools import partial
 import numpy as np
 
 from quail_b200.engine.stage_executor import StageExecutor, Task
+from quail_b200.ops.kernels import READOUT_TOPK as TOPK
 
 PREFIX_KEY = ("prefix",)
 
@@ -67,6 +70,9 @@ class Call:
     # decision models: rows read by the decision head, as distances before the
     # last row (one per option, then 0); empty = an LM-head readout
     offsets: tuple = ()
+    # extract: every generated token continues a verbatim copy of the row's document
+    # (the readout carries the best few tokens; the best one the copy allows wins)
+    copy: bool = False
 
 
 @dataclass
@@ -90,6 +96,7 @@ class RegionRun:
         self._next = [0] * len(docs)          # next call index to submit per row
         self._pending = [0] * len(docs)       # calls in flight per row
         self._label_parts: dict = {}
+        self._copies: dict = {}               # (row, call) -> document positions a copy may continue at
         # columns after the answer rows in a full readout: argmax, lse
         self.nans = answer_width
 
@@ -204,13 +211,20 @@ class RegionRun:
     def _decode_step(self, r, ci, row, generated):
         """One greedy step of row r's call ci; `generated` is the row's token list (appended in place)."""
         call = self.calls[ci]
-        arg_col = self.nans if self.nans is not None else len(row) - 2
-        tok = int(round(float(row.numpy()[arg_col] if hasattr(row, "numpy") else row[arg_col])))
+        vals = row.numpy() if hasattr(row, "numpy") else np.asarray(row)
+        arg_col = self.nans if self.nans is not None else (len(vals) - 2 - (2 * TOPK if call.copy else 0))
+        if call.copy:
+            tok = self._copy_choice(r, ci, vals, arg_col, generated)
+        else:
+            tok = int(round(float(vals[arg_col])))
         stop = tok in call.stop_ids
         if not stop:
             generated.append(tok)
+        if tok < 0:
+            stop = True
         if stop or len(generated) >= call.max_tokens:
             self.results[r].values[call.name] = generated
+            self._copies.pop((r, ci), None)
             self._finish_call(r, ci)
             return
         key, reads, pos, own_len = self._question(r, ci)
@@ -218,10 +232,36 @@ class RegionRun:
         self.fresh_tokens += 1
         self.ex.submit_continuation(Task(key=key, tokens=[tok], pos_start=pos + own_len + n_prev, reads=reads,
                                          readout=True, full_readout=True, own_prefix=own_len + n_prev,
-                                         free_after=False, on_done=partial(self._decode_next, r, ci, generated)))
+                                         free_after=False, topk=call.copy,
+                                         on_done=partial(self._decode_next, r, ci, generated)))
 
     def _decode_next(self, r, ci, generated, task, row):
         self._decode_step(r, ci, row, generated)
+
+    def _copy_choice(self, r, ci, vals, arg_col, generated) -> int:
+        """The next token of a copy-constrained extraction: the best-ranked readout candidate
+        that continues a verbatim copy of the document (any document token to start), or a
+        stop token; when no candidate qualifies, the phrase ends.
+
+        The copy state is the set of document positions that can follow the phrase so far
+        (the reference's copy-constrained extraction: executor/extract/copy.py).
+        """
+        call = self.calls[ci]
+        doc = self.docs[r]
+        state = self._copies.get((r, ci))
+        if state is None:
+            state = np.arange(len(doc))               # nothing copied yet: any position starts
+        cand = vals[arg_col + 2:arg_col + 2 + TOPK].astype(np.int64)
+        allowed = doc[state[state < len(doc)]]
+        for t in cand:
+            t = int(t)
+            if t in call.stop_ids:
+                return t
+            hit = state[(state < len(doc)) & (allowed == t)]
+            if hit.size:
+                self._copies[(r, ci)] = hit + 1
+                return t
+        return call.stop_ids[0] if call.stop_ids else -1
 
     # ------------------------------------------------------------ scheduling
     def _finish_call(self, r: int, ci: int) -> None:
@@ -273,7 +313,7 @@ class RegionRun:
         key, reads, pos, own_len = self._question(r, ci)
         self.fresh_tokens += len(call.suffix)
         self.ex.submit(Task(key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
-                            full_readout=self._needs_full(call), reserve_tokens=self._reserve(call),
+                            full_readout=self._needs_full(call), reserve_tokens=self._reserve(call), topk=call.copy,
                             readout_rows=self._pooled_rows(call, len(call.suffix)),
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
 
@@ -289,6 +329,7 @@ class RegionRun:
             self._pending[r] = 1
             self.ex.submit(Task(key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
                                 full_readout=self._needs_full(first), reserve_tokens=self._reserve(first),
+                                topk=first.copy,
                                 readout_rows=self._pooled_rows(first, len(toks)),
                                 on_done=lambda t, row, r=r: self._answered(r, 0, row), free_after=False))
 

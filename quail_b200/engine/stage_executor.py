@@ -57,6 +57,7 @@ class Task:
     tag: object = None
     readout_rows: tuple | None = None                # offsets read out (default: the last token)
     full_readout: bool = False                       # also argmax / log-sum-exp over the vocabulary
+    topk: bool = False                               # and the top-k token ids and logits
     reserve_tokens: int = 0                          # decode headroom allocated with the key's pages
     got_rows: list = field(default_factory=list)     # readout rows of the pieces already collected
 
@@ -150,7 +151,7 @@ class StageExecutor:
             cont.popleft()
             rows = tuple(task.readout_rows) if task.readout and task.readout_rows is not None else None
             specs.append(SeqSpec(task.reads, task.key, task.own_prefix, task.tokens, task.pos_start, task.readout,
-                                 task, rows, task.full_readout))
+                                 task, rows, task.full_readout, task.topk))
             task.done = n
             room -= n
         deferred: list[Task] = []
@@ -203,7 +204,7 @@ class StageExecutor:
             specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix + task.done,
                                  tokens=task.tokens[task.done:task.done + piece],
                                  pos_start=task.pos_start + task.done, readout=readout, tag=task,
-                                 readout_rows=rows if readout else None, full=task.full_readout))
+                                 readout_rows=rows if readout else None, full=task.full_readout, topk=task.topk))
             task.done += piece
             room -= piece
             if not last:
@@ -229,7 +230,8 @@ class StageExecutor:
         res = None
         if self.graphs is not None and self.graphs.eligible(specs):
             host, _ = self.packer.host_parts(specs)
-            res = self.graphs.run(host, any(s.full and s.readout for s in specs))
+            res = self.graphs.run(host, any(s.full and s.readout for s in specs),
+                                  any(s.topk and s.readout for s in specs))
         if res is not None:
             logits, nbytes = res
             chunk = _Replayed(num_tokens=len(specs), upload_bytes=nbytes)

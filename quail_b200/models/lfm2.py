@@ -129,7 +129,7 @@ class Lfm2Reference:
         if not getattr(chunk, "full_readout", False):
             return ans
         full = (normed @ self.head.t()).float()
-        return torch.cat([ans, full.argmax(dim=1).float()[:, None], torch.logsumexp(full, dim=1)[:, None]], dim=1)
+        return ref.head_readout(full, ans, getattr(chunk, "topk", False))
 
 
 class Lfm2Pipeline:
@@ -229,5 +229,4 @@ class Lfm2Pipeline:
         normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
         ans = ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows,
                                      normed=normed)
-        arg, lse = ops.row_argmax_lse(ops.gemm(normed, self.head_bf16()))
-        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)
+        return ops.head_readout(normed, self.head_bf16(), ans, getattr(chunk, "topk", False))

@@ -160,8 +160,7 @@ class Qwen3Pipeline:
         R = chunk.final_rows.numel()
         normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
         ans = ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows, normed=normed)
-        arg, lse = ops.row_argmax_lse(ops.gemm(normed, w.head_bf16()))
-        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)
+        return ops.head_readout(normed, w.head_bf16(), ans, getattr(chunk, "topk", False))
 
 
 class Qwen3Reference:
@@ -298,6 +297,4 @@ class Qwen3Reference:
         if not getattr(chunk, "full_readout", False):
             return ans
         full = (normed @ self.head.t()).float()
-        arg = full.argmax(dim=1).float()
-        lse = torch.logsumexp(full, dim=1)
-        return torch.cat([ans, arg[:, None], lse[:, None]], dim=1)
+        return ref.head_readout(full, ans, getattr(chunk, "topk", False))

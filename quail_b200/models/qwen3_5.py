@@ -289,4 +289,4 @@ class Qwen35Reference:
         if not getattr(chunk, "full_readout", False):
             return ans
         full = (normed @ self.head.t()).float()
-        return torch.cat([ans, full.argmax(dim=1).float()[:, None], torch.logsumexp(full, dim=1)[:, None]], dim=1)
+        return ref.head_readout(full, ans, getattr(chunk, "topk", False))

@@ -256,5 +256,4 @@ class Qwen35Pipeline:
         normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
         ans = ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows,
                                      normed=normed)
-        arg, lse = ops.row_argmax_lse(ops.gemm(normed, self.head_bf16()))
-        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)
+        return ops.head_readout(normed, self.head_bf16(), ans, getattr(chunk, "topk", False))

@@ -187,5 +187,4 @@ class Qwen3MoePipeline:
         R = chunk.final_rows.numel()
         normed = torch.empty(R, cfg.hidden, dtype=torch.bfloat16, device=h.device)
         ans = ops.final_norm_readout(h, chunk.final_rows, w.final_norm, cfg.rms_eps, w.answer_rows, normed=normed)
-        arg, lse = ops.row_argmax_lse(ops.gemm(normed, w.head_bf16()))
-        return torch.cat([ans, arg.float()[:, None], lse[:, None]], dim=1)
+        return ops.head_readout(normed, w.head_bf16(), ans, getattr(chunk, "topk", False))

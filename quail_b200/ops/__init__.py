@@ -20,6 +20,8 @@ from quail_b200.ops.kernels import (  # noqa: F401
     gemm,
     gemm_mx,
     gemm_nvfp4,
+    head_readout,
+    READOUT_TOPK,
     quant_rows_nvfp4,
     sf_bytes,
     rmsnorm_quant_mx,

@@ -330,6 +330,21 @@ def row_argmax_lse(logits: torch.Tensor):
     return arg, lse
 
 
+READOUT_TOPK = 8   # candidates per row of a top-k readout (copy-constrained extraction)
+
+
+def head_readout(normed: torch.Tensor, head: torch.Tensor, ans: torch.Tensor, topk: bool = False):
+    """Full-vocabulary readout of final-normed rows: [answer logits | argmax | log-sum-exp],
+    then with `topk` the READOUT_TOPK best token ids and their logits."""
+    logits = gemm(normed, head)
+    arg, lse = row_argmax_lse(logits)
+    cols = [ans, arg.float()[:, None], lse[:, None]]
+    if topk:
+        v, i = torch.topk(logits, READOUT_TOPK, dim=1)
+        cols += [i.float(), v.float()]
+    return torch.cat(cols, dim=1)
+
+
 def read_and_clear_error(device: int = 0) -> int:
     """Synchronize and return (then clear) the kernels' bounded-wait error code."""
     return int(native().read_and_clear_error(device))

@@ -112,3 +112,12 @@ def sae_features(x: torch.Tensor, w_enc: torch.Tensor, b_enc: torch.Tensor, keep
     v = v.clamp(min=0.0)
     i = torch.where(v > 0, i, torch.zeros_like(i))
     return torch.cat([i.float(), v], dim=1)
+
+
+def head_readout(full: torch.Tensor, ans: torch.Tensor, topk: bool = False, k: int = 8) -> torch.Tensor:
+    """fp32 statement of ops.head_readout from full-vocabulary logits [R, V]."""
+    cols = [ans, full.argmax(dim=1).float()[:, None], torch.logsumexp(full, dim=1)[:, None]]
+    if topk:
+        v, i = torch.topk(full, k, dim=1)
+        cols += [i.float(), v.float()]
+    return torch.cat(cols, dim=1)

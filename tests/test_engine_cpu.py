@@ -165,3 +165,57 @@ def test_decode_headroom_under_memory_pressure(pages):
         assert g[0] == (3 + 1) % 500 and g[1] == (g[0] + 1) % 500
     assert ex.pool.free_pages == pages
     ex.pool.check()
+
+
+def test_copy_constrained_choice():
+    """The copy state: the best candidate that continues a verbatim copy of the document wins,
+    a stop token ends the phrase, and no qualifying candidate ends it too."""
+    from quail_b200.engine.region import Call, RegionRun
+    from quail_b200.ops.kernels import READOUT_TOPK as K
+
+    class _Ex:
+        pass
+    doc = np.array([5, 6, 7, 5, 9], dtype=np.int32)
+    call = Call(kind="extract", suffix=np.zeros(1, np.int32), stop_ids=(99,), copy=True, max_tokens=8)
+    run = RegionRun(_Ex(), np.zeros(0, np.int32), [doc], [call], answer_width=2)
+
+    def row(cands):
+        c = list(cands) + [0] * (K - len(cands))
+        return np.array([0.0, 0.0, 0.0, 0.0] + c + [0.0] * K, dtype=np.float32)   # 2 answers, arg, lse
+    assert run._copy_choice(0, 0, row([3, 5]), 2, []) == 5          # 3 is not in the document
+    assert run._copy_choice(0, 0, row([7, 6, 9]), 2, []) == 6       # after 5: 6 or 9 continue, 7 does not
+    assert run._copy_choice(0, 0, row([5, 7]), 2, []) == 7          # after 5 6: only 7
+    assert run._copy_choice(0, 0, row([1, 2]), 2, []) == 99         # nothing continues: the phrase ends
+    run._copies.clear()
+    assert run._copy_choice(0, 0, row([99, 5]), 2, []) == 99        # a stop token wins when ranked first
+
+
+def test_extract_phrases_are_document_copies():
+    """AI.EXTRACT on the fp32 model: every extracted phrase's tokens are a contiguous run of the
+    row's document tokens (or empty)."""
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    from quail_b200.api import prompts as P
+    cfg = quail.EngineConfig(model="qwen3-tiny", device="cpu", chunk_tokens=256)
+    bodies = ["the order arrived late and the box was broken", "great service, thanks", "refund please"]
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": [0, 1, 2], "body": bodies}))
+        eng = s.engine()
+        from quail_b200.engine.region import RegionRun
+        seen = []
+        orig = RegionRun._decode_step
+
+        def spy(self, r, ci, row, generated):
+            orig(self, r, ci, row, generated)
+            seen.append((r, list(generated), self.docs[r].tolist()))
+        RegionRun._decode_step = spy
+        try:
+            s.sql("SELECT id, AI.EXTRACT(body, ['What went wrong?']) AS e FROM t").collect()
+        finally:
+            RegionRun._decode_step = orig
+        assert seen
+        for r, gen, doc in seen:
+            n = len(gen)
+            assert n == 0 or any(doc[i:i + n] == gen for i in range(len(doc) - n + 1)), (gen, doc)
+    del P, eng

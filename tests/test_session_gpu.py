@@ -70,3 +70,13 @@ def test_decision_model_on_the_kernels():
     np.testing.assert_allclose(a, b, atol=0.03)
     agree = np.mean(np.array(got.column("c").to_pylist()) == np.array(want.column("c").to_pylist()))
     assert agree >= 0.9
+
+
+def test_extract_copies_from_the_document(session):
+    """AI.EXTRACT on the kernels with the copy constraint (top-k readout): every phrase is a
+    verbatim piece of its row's document (or null when nothing was copied)."""
+    t = session.sql("SELECT id, body, AI.EXTRACT(body, ['What is it about?']) AS e FROM t WHERE id < 12 "
+                    "ORDER BY id").collect()
+    for body, e in zip(t.column("body").to_pylist(), t.column("e").to_pylist()):
+        for phrase in e:
+            assert phrase is None or phrase.strip() in body, (phrase, body)
