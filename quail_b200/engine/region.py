@@ -50,6 +50,7 @@ from quail_b200.engine.stage_executor import StageExecutor, Task
 from quail_b200.ops.kernels import READOUT_TOPK as TOPK
 
 PREFIX_KEY = ("prefix",)
+DRAFT_TOKENS = 8          # document tokens drafted per pass once a copy has one continuation
 
 
 @dataclass
@@ -97,6 +98,7 @@ class RegionRun:
         self._pending = [0] * len(docs)       # calls in flight per row
         self._label_parts: dict = {}
         self._copies: dict = {}               # (row, call) -> document positions a copy may continue at
+        self.drafted = 0                      # draft tokens accepted (copy-constrained extraction)
         # columns after the answer rows in a full readout: argmax, lse
         self.nans = answer_width
 
@@ -208,20 +210,31 @@ class RegionRun:
             res.values[call.name + "#probs"] = [x / z for x in e]
         self._finish_call(r, ci)
 
-    def _decode_step(self, r, ci, row, generated):
-        """One greedy step of row r's call ci; `generated` is the row's token list (appended in place)."""
+    def _decode_step(self, r, ci, row, generated, draft=()):
+        """One decode step of row r's call ci; `generated` is the row's token list (appended in place).
+
+        `row` holds one readout row, or with a draft one per drafted position: the
+        draft's tokens are kept while the step's choice (greedy, or the copy
+        constraint's) agrees with them, and the first disagreeing choice (or the
+        choice after the whole draft) is the step's new token.
+        """
         call = self.calls[ci]
-        vals = row.numpy() if hasattr(row, "numpy") else np.asarray(row)
-        arg_col = self.nans if self.nans is not None else (len(vals) - 2 - (2 * TOPK if call.copy else 0))
-        if call.copy:
-            tok = self._copy_choice(r, ci, vals, arg_col, generated)
-        else:
-            tok = int(round(float(vals[arg_col])))
-        stop = tok in call.stop_ids
+        vals = np.asarray(row.numpy() if hasattr(row, "numpy") else row)
+        rows = vals.reshape(-1, vals.shape[-1])
+        arg_col = self.nans if self.nans is not None else (rows.shape[1] - 2 - (2 * TOPK if call.copy else 0))
+        tok = -1
+        for jrow in range(rows.shape[0]):
+            tok = (self._copy_choice(r, ci, rows[jrow], arg_col, generated) if call.copy
+                   else int(round(float(rows[jrow][arg_col]))))
+            if (jrow < len(draft) and tok == draft[jrow] and tok not in call.stop_ids
+                    and len(generated) + 1 < call.max_tokens):
+                generated.append(tok)
+                self.drafted += 1
+                continue
+            break
+        stop = tok < 0 or tok in call.stop_ids
         if not stop:
             generated.append(tok)
-        if tok < 0:
-            stop = True
         if stop or len(generated) >= call.max_tokens:
             self.results[r].values[call.name] = generated
             self._copies.pop((r, ci), None)
@@ -229,14 +242,27 @@ class RegionRun:
             return
         key, reads, pos, own_len = self._question(r, ci)
         n_prev = len(generated) - 1
-        self.fresh_tokens += 1
-        self.ex.submit_continuation(Task(key=key, tokens=[tok], pos_start=pos + own_len + n_prev, reads=reads,
+        nxt = self._draft(r, ci, call.max_tokens - len(generated)) if call.copy else ()
+        self.fresh_tokens += 1 + len(nxt)
+        self.ex.submit_continuation(Task(key=key, tokens=[tok, *nxt], pos_start=pos + own_len + n_prev, reads=reads,
                                          readout=True, full_readout=True, own_prefix=own_len + n_prev,
                                          free_after=False, topk=call.copy,
-                                         on_done=partial(self._decode_next, r, ci, generated)))
+                                         readout_rows=tuple(range(1 + len(nxt))) if nxt else None,
+                                         on_done=partial(self._decode_next, r, ci, generated, nxt)))
 
-    def _decode_next(self, r, ci, generated, task, row):
-        self._decode_step(r, ci, row, generated)
+    def _decode_next(self, r, ci, generated, draft, task, row):
+        self._decode_step(r, ci, row, generated, draft)
+
+    def _draft(self, r, ci, room: int) -> tuple:
+        """Document-copy draft: when the copy so far continues at one document position only,
+        the next few document tokens, to verify in one pass (reference: extract/candidates.py)."""
+        state = self._copies.get((r, ci))
+        doc = self.docs[r]
+        if state is None or state.size != 1 or state[0] >= len(doc):
+            return ()
+        p = int(state[0])
+        n = min(DRAFT_TOKENS, room, len(doc) - p)
+        return tuple(int(t) for t in doc[p:p + n]) if n > 0 else ()
 
     def _copy_choice(self, r, ci, vals, arg_col, generated) -> int:
         """The next token of a copy-constrained extraction: the best-ranked readout candidate

@@ -219,3 +219,72 @@ def test_extract_phrases_are_document_copies():
             n = len(gen)
             assert n == 0 or any(doc[i:i + n] == gen for i in range(len(doc) - n + 1)), (gen, doc)
     del P, eng
+
+
+def test_extract_drafts_match_token_by_token_decoding():
+    """Document-copy drafts change how many passes an extraction takes, not what it extracts:
+    the same region with drafts off gives the same phrases."""
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    from quail_b200.engine import region as R
+    cfg = quail.EngineConfig(model="qwen3-tiny", device="cpu", chunk_tokens=256)
+    bodies = ["the order arrived late and the box was broken", "great service, thanks a lot", "refund please now"]
+    q = "SELECT id, AI.EXTRACT(body, ['What went wrong?', 'Who?']) AS e FROM t ORDER BY id"
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": [0, 1, 2], "body": bodies}))
+        with_drafts = s.sql(q).collect().column("e").to_pylist()
+        keep = R.DRAFT_TOKENS
+        R.DRAFT_TOKENS = 0
+        try:
+            without = s.sql(q).collect().column("e").to_pylist()
+        finally:
+            R.DRAFT_TOKENS = keep
+    assert with_drafts == without
+
+
+class _CopyModel:
+    """A stand-in model that always predicts the current token + 1 (then a stop token): on a
+    document of consecutive ids it copies the document, which exercises the drafts."""
+
+    def __init__(self, stop):
+        self.stop = stop
+
+    def set_answer_rows(self, ids):
+        pass
+
+    def forward_chunk(self, chunk, arena):
+        from quail_b200.ops.kernels import READOUT_TOPK as K
+        ids = chunk.ids[chunk.final_rows.long()].float()
+        R = ids.shape[0]
+        out = torch.zeros(R, 1 + 2 + 2 * K)
+        out[:, 1] = ids + 1                                   # argmax
+        out[:, 3] = ids + 1                                   # top-1
+        out[:, 4] = float(self.stop)                          # top-2: the stop token
+        out[:, 3 + K] = 5.0
+        out[:, 4 + K] = 4.0
+        return out
+
+
+@pytest.mark.parametrize("drafts", [0, 8])
+def test_copy_drafts_accept_whole_runs(drafts):
+    from quail_b200.engine import region as R
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.engine.stage_executor import StageExecutor
+    doc = np.arange(10, 31, dtype=np.int32)                   # 21 consecutive ids
+    arena = KVArena(1, 64, 16, 1, 8, device="cpu", dtype=torch.float32)
+    ex = StageExecutor(_CopyModel(stop=99), arena, 256)
+    call = R.Call(kind="extract", suffix=np.array([9], dtype=np.int32), stop_ids=(99,), copy=True, max_tokens=30,
+                  name="e")
+    keep = R.DRAFT_TOKENS
+    R.DRAFT_TOKENS = drafts
+    try:
+        run = R.RegionRun(ex, np.array([1, 2], dtype=np.int32), [doc], [call], answer_width=1)
+        res = run.run()
+    finally:
+        R.DRAFT_TOKENS = keep
+    assert res[0].values["e"] == list(range(10, 31))
+    if drafts:
+        assert run.drafted > 0 and ex.stats.passes <= 6
+    else:
+        assert run.drafted == 0 and ex.stats.passes >= 21
