@@ -89,13 +89,17 @@ class ExecutorStats:
 
 class StageExecutor:
     def __init__(self, model, arena, chunk_tokens: int, *, min_piece: int = 64, gpu_timing: bool = False,
-                 max_seqs: int | None = None):
+                 max_seqs: int | None = None, cont_cap: int = 512):
         self.model = model
         self.arena = arena
         self.pool = arena.pool
         self.chunk_tokens = chunk_tokens
         self.min_piece = min_piece
         self.max_seqs = max_seqs
+        # continuations (decode steps) per pass: with more decoding rows than this they
+        # split into groups that alternate, so the host builds one group's next step
+        # while the GPU runs the other's (a step depends on the previous one's token)
+        self.cont_cap = cont_cap
         self.device = arena.device
         self.packer = ChunkPacker(self.pool, self.device)
         self.queue: deque[Task] = deque()
@@ -138,7 +142,8 @@ class StageExecutor:
         # continuations first: each is one or a few tokens of a resident key
         cont, pool = self.cont, self.pool
         max_seqs = self.max_seqs if self.max_seqs is not None else 1 << 30
-        while cont and room > 0 and len(specs) < max_seqs:
+        cap = min(max_seqs, self.cont_cap)
+        while cont and room > 0 and len(specs) < cap:
             task = cont[0]
             n = len(task.tokens)
             total = task.own_prefix + n
