@@ -267,8 +267,7 @@ void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, floa
                             float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
                             int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
                             const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
-                            float* out, uint8_t* ws, const __nv_bfloat16* norm_w, float eps, __nv_bfloat16* y,
-                            int dev, cudaStream_t st);
+                            float* out, uint8_t* ws, int dev, cudaStream_t st);
 
 // proj: bf16 [T, ld] = [qkv (C) | z (Hv*DV) | b (Hv) | a (Hv)] (the fused in-projection);
 // returns bf16 [T, Hv*DV] gated-norm output (the out_proj input).
@@ -311,10 +310,8 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
                            conv_state.data_ptr<float>(), q_scale, conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
                            reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,
                            A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hv, (int)Hk, sq, sio, T, S,
-                           ssm_state.data_ptr<float>(), (int)gi, G, o.data_ptr<float>(), ws.data_ptr<uint8_t>(),
-                           reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr()), (float)eps,
-                           reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), dev, st);
-    return;   // the scan wrote the gated norm's output y directly
+                           ssm_state.data_ptr<float>(), (int)gi, G, o.data_ptr<float>(), ws.data_ptr<uint8_t>(), dev,
+                           st);
   } else {
     dim3 g1(S, (C + 127) / 128);
     gdn_conv_kernel<4><<<g1, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, C,

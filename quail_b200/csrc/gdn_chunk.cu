@@ -660,9 +660,7 @@ __device__ __forceinline__ void gc_fetch_record(uint32_t sbuf, const uint8_t* re
 
 __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
     int Hv, const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
-    const int* __restrict__ ws, int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out,
-    const __nv_bfloat16* __restrict__ z, int ldz, int z_col, const __nv_bfloat16* __restrict__ norm_w, float eps,
-    __nv_bfloat16* __restrict__ y) {
+    const int* __restrict__ ws, int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out) {
   extern __shared__ __align__(16) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
   const uint32_t aS = base + GsSmem::S, aU = base + GsSmem::U, aUs = base + GsSmem::Us;
@@ -782,50 +780,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
         gc_mma(accO[2 * np + 1], am, b[2], b[3]);
       }
     }
-    if (y == nullptr) {
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int i = 16 * mt + g + 8 * hf;
-        if (i < cn) {
-          float* orow = out + (size_t)(q0 + c0 + i) * Hv * kD + h * kD;
+    for (int hf = 0; hf < 2; ++hf) {
+      const int i = 16 * mt + g + 8 * hf;
+      if (i < cn) {
+        float* orow = out + (size_t)(q0 + c0 + i) * Hv * kD + h * kD;
 #pragma unroll
-          for (int nt = 0; nt < 8; ++nt) {
-            const int cc = 64 * nh + 8 * nt + 2 * t4;
-            *reinterpret_cast<float2*>(orow + cc) = make_float2(accO[nt][2 * hf], accO[nt][2 * hf + 1]);
-          }
-        }
-      }
-    } else {
-      // gated RMSNorm of each output row over its 128 values, here: the row's two
-      // 64-column halves live in two warps, so their squares meet in shared memory
-      float* sRed = reinterpret_cast<float*>(smem + GsSmem::BYTES);
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float ss = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) ss += accO[nt][2 * hf] * accO[nt][2 * hf] + accO[nt][2 * hf + 1] * accO[nt][2 * hf + 1];
-        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-        if (t4 == 0) sRed[(16 * mt + g + 8 * hf) * 2 + nh] = ss;
-      }
-      __syncthreads();
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int i = 16 * mt + g + 8 * hf;
-        if (i < cn) {
-          const float r = rsqrtf((sRed[i * 2] + sRed[i * 2 + 1]) * (1.f / kD) + eps);
-          const size_t t = (size_t)(q0 + c0 + i);
-          const __nv_bfloat16* zr = z + t * ldz + z_col + h * kD;
-          __nv_bfloat16* yr = y + t * Hv * kD + h * kD;
-#pragma unroll
-          for (int nt = 0; nt < 8; ++nt) {
-            const int cc = 64 * nh + 8 * nt + 2 * t4;
-            const float2 zz = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zr + cc));
-            const float2 ww = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(norm_w + cc));
-            const float v0 = accO[nt][2 * hf] * r * ww.x * (zz.x / (1.f + __expf(-zz.x)));
-            const float v1 = accO[nt][2 * hf + 1] * r * ww.y * (zz.y / (1.f + __expf(-zz.y)));
-            *reinterpret_cast<__nv_bfloat162*>(yr + cc) = __floats2bfloat162_rn(v0, v1);
-          }
+        for (int nt = 0; nt < 8; ++nt) {
+          const int cc = 64 * nh + 8 * nt + 2 * t4;
+          *reinterpret_cast<float2*>(orow + cc) = make_float2(accO[nt][2 * hf], accO[nt][2 * hf + 1]);
         }
       }
     }
@@ -981,14 +944,13 @@ void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, floa
                             float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
                             int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
                             const int* seqs, const int* sio, int T, int S, float* ssm_state, int gi, int G,
-                            float* out, uint8_t* ws, const __nv_bfloat16* norm_w, float eps, __nv_bfloat16* y,
-                            int dev, cudaStream_t st) {
+                            float* out, uint8_t* ws, int dev, cudaStream_t st) {
   static bool configured[64] = {false};
   if (!configured[dev]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         GpSmem::BYTES));
     C10_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        GsSmem::BYTES + kCh * 2 * 4));
+                                        GsSmem::BYTES));
     configured[dev] = true;
   }
   const int maxc = T / kCh + S + 1;
@@ -1005,8 +967,8 @@ void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, floa
   gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col,
                                                                      a_col, A_log, dt_bias, Hv, Hk, seqs, wsi, recs);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  gdn_chunk_scan_kernel<<<dim3(Hv, S), 256, GsSmem::BYTES + kCh * 2 * 4, st>>>(
-      Hv, seqs, sio, ssm_state, gi, G, wsi, maxc, recs, out, ab, ldab, C, norm_w, eps, y);
+  gdn_chunk_scan_kernel<<<dim3(Hv, S), 256, GsSmem::BYTES, st>>>(Hv, seqs, sio, ssm_state, gi, G, wsi, maxc, recs,
+                                                                  out);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

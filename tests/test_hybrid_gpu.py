@@ -126,8 +126,7 @@ def test_gdn_layer_against_recurrence(dk, mode):
         rep = Hv // Hk
         out = Q.delta_rule(qq.repeat_interleave(rep, 1), kk.repeat_interleave(rep, 1), vv, g[a:a + n],
                            beta[a:a + n], S)
-        if mode != 3:   # the split form writes only y (its scan applies the gated norm)
-            assert rel_err(o[a:a + n].view(n, Hv, dv), out) < tol, (i, rel_err(o[a:a + n].view(n, Hv, dv), out))
+        assert rel_err(o[a:a + n].view(n, Hv, dv), out) < tol, (i, rel_err(o[a:a + n].view(n, Hv, dv), out))
         assert rel_err(conv_state[dst, gi], win) < 1e-5
         assert rel_err(ssm_state[dst, gi], S) < tol, (i, rel_err(ssm_state[dst, gi], S))
         z = pf[a:a + n, C:C + Hv * dv].view(n, Hv, dv)
