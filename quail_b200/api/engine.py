@@ -247,7 +247,12 @@ class ModelEngine:
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
         run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer),
                         decision=getattr(self.model, "decision", None))
-        results = run.run()
+        from quail_b200.utils import progress
+        kinds = ", ".join(sorted({c.kind for c in calls}))
+        with progress.count(f"{kinds} over {len(uniq)} documents", len(uniq), " docs") as bar:
+            run.progress = bar
+            results = run.run()
+        progress.say(f"{ex.stats.passes - passes0} passes, {ex.stats.tokens - tok0} fresh tokens", detail=True)
         if self.on_gpu:
             from quail_b200 import ops
             err = ops.read_and_clear_error(self.device.index)

@@ -99,6 +99,7 @@ class RegionRun:
         self._label_parts: dict = {}
         self._copies: dict = {}               # (row, call) -> document positions a copy may continue at
         self.drafted = 0                      # draft tokens accepted (copy-constrained extraction)
+        self.progress = None                  # utils.progress.Count advanced as each row finishes
         # columns after the answer rows in a full readout: argmax, lse
         self.nans = answer_width
 
@@ -305,6 +306,8 @@ class RegionRun:
         ci = self._next[r]
         if not res.kept or ci >= len(self.calls):
             self.ex.free(("doc", r))
+            if self.progress is not None:
+                self.progress.advance()
             return
         # a filter runs alone; non-filter calls up to the next filter run side by side
         batch = [ci]

@@ -40,6 +40,8 @@ def main():
     ap.add_argument("--socket", required=True)
     ap.add_argument("--index", type=int, required=True)
     args = ap.parse_args()
+    from quail_b200.utils.progress import set_gpu_index
+    set_gpu_index(args.index)
     from quail_b200 import _native
     import os
     if os.environ.get("QB_FAULT") == f"noconnect:{args.index}":
