@@ -41,6 +41,7 @@ or a filter dropped it.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from functools import partial
 
@@ -50,6 +51,15 @@ from quail_b200.engine.stage_executor import StageExecutor, Task
 from quail_b200.ops.kernels import READOUT_TOPK as TOPK
 
 PREFIX_KEY = ("prefix",)
+# QUAIL_EXTRACT_TRACE=<path>: one JSON line per copy-constrained choice (row, step, the readout's
+# candidates, the chosen token, how many document positions the copy can continue at)
+_EXTRACT_TRACE = os.environ.get("QUAIL_EXTRACT_TRACE")
+
+
+def _trace_extract(rec: dict) -> None:
+    import json
+    with open(_EXTRACT_TRACE, "a", encoding="utf-8") as f:
+        f.write(json.dumps(rec) + "\n")
 DRAFT_TOKENS = 8          # document tokens drafted per pass once a copy has one continuation
 
 
@@ -280,15 +290,21 @@ class RegionRun:
             state = np.arange(len(doc))               # nothing copied yet: any position starts
         cand = vals[arg_col + 2:arg_col + 2 + TOPK].astype(np.int64)
         allowed = doc[state[state < len(doc)]]
+        choice, kept = (call.stop_ids[0] if call.stop_ids else -1), 0
         for t in cand:
             t = int(t)
             if t in call.stop_ids:
-                return t
+                choice = t
+                break
             hit = state[(state < len(doc)) & (allowed == t)]
             if hit.size:
                 self._copies[(r, ci)] = hit + 1
-                return t
-        return call.stop_ids[0] if call.stop_ids else -1
+                choice, kept = t, int(hit.size)
+                break
+        if _EXTRACT_TRACE:
+            _trace_extract({"row": int(r), "call": self.calls[ci].name, "step": len(generated),
+                            "candidates": [int(t) for t in cand], "chosen": int(choice), "positions": kept})
+        return choice
 
     # ------------------------------------------------------------ scheduling
     def _finish_call(self, r: int, ci: int) -> None:

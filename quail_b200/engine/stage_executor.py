@@ -23,6 +23,8 @@ prefill pieces, Borrowing) and readout.py (async readouts drained in order).
 
 from __future__ import annotations
 
+import os
+
 import time
 from collections import deque
 from dataclasses import dataclass, field
@@ -110,6 +112,8 @@ class StageExecutor:
         self.stats = ExecutorStats()
         self.gpu_timing = gpu_timing and self.device.type == "cuda"
         self.graphs = None        # engine.graphs.DecodeGraphs once enable_graphs() is called
+        # QB_NVTX=1: one NVTX range per forward pass (named by pass index and sequence count)
+        self.nvtx = self.device.type == "cuda" and os.environ.get("QB_NVTX") == "1"
         self._inflight: deque = deque()
         self.should_stop: Callable | None = None   # checked between passes (cancel / timeout)
 
@@ -228,6 +232,15 @@ class StageExecutor:
             self.graphs = DecodeGraphs(self.model, self.arena, self.device)
 
     def _launch(self, specs: list[SeqSpec]):
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(f"pass {self.stats.passes}: {len(specs)} seqs")
+        try:
+            self._launch_inner(specs)
+        finally:
+            if self.nvtx:
+                torch.cuda.nvtx.range_pop()
+
+    def _launch_inner(self, specs: list[SeqSpec]):
         ev0 = ev1 = None
         if self.gpu_timing:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

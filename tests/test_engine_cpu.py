@@ -288,3 +288,24 @@ def test_copy_drafts_accept_whole_runs(drafts):
         assert run.drafted > 0 and ex.stats.passes <= 6
     else:
         assert run.drafted == 0 and ex.stats.passes >= 21
+
+
+def test_extract_trace_lines(tmp_path, monkeypatch):
+    """QUAIL_EXTRACT_TRACE writes one JSON line per copy-constrained choice."""
+    import json
+
+    from quail_b200.engine import region as R
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.engine.stage_executor import StageExecutor
+    path = tmp_path / "extract.jsonl"
+    monkeypatch.setattr(R, "_EXTRACT_TRACE", str(path))
+    doc = np.arange(10, 16, dtype=np.int32)
+    arena = KVArena(1, 64, 16, 1, 8, device="cpu", dtype=torch.float32)
+    ex = StageExecutor(_CopyModel(stop=99), arena, 256)
+    call = R.Call(kind="extract", suffix=np.array([9], dtype=np.int32), stop_ids=(99,), copy=True, max_tokens=30,
+                  name="e")
+    run = R.RegionRun(ex, np.array([1, 2], dtype=np.int32), [doc], [call], answer_width=1)
+    assert run.run()[0].values["e"] == list(range(10, 16))
+    recs = [json.loads(ln) for ln in path.read_text().splitlines()]
+    assert recs[0]["step"] == 0 and recs[0]["chosen"] == 10 and recs[0]["positions"] == 1
+    assert recs[-1]["chosen"] == 99
