@@ -74,4 +74,20 @@ def check_config(config: EngineConfig):
     if config.attention not in (None, "tree", "unified"):
         raise RefusalError(Refusal(reasons=("attention is 'tree', 'unified' or None",),
                                    constraint="unsupported_backend_configuration"))
+    # what each split of a model over several GPUs runs on (backends/quail/backend.py:18-88 is the
+    # reference's supports(): device, architecture, gpus)
+    if config.parallel not in ("dp", "tp", "ep"):
+        raise RefusalError(Refusal(reasons=(f"parallel is 'dp', 'tp' or 'ep', not {config.parallel!r}",),
+                                   constraint="unsupported_backend_configuration"))
+    if config.parallel == "tp" and (model.is_hybrid or model.is_moe or model.role != "generative"):
+        raise RefusalError(Refusal(reasons=(f"tensor parallelism runs dense Qwen3 decoders, not {model.name!r}",),
+                                   constraint="unsupported_backend_configuration"))
+    if config.parallel == "ep" and not model.is_moe:
+        raise RefusalError(Refusal(reasons=(f"expert parallelism needs a mixture-of-experts model, not {model.name!r}",),
+                                   constraint="unsupported_backend_configuration"))
+    if config.parallel != "dp" and config.gpus > 1:
+        raise RefusalError(Refusal(
+            reasons=(f"a session splits work over GPUs by data parallelism; {config.parallel} runs through "
+                     f"quail_b200.utils.bench_tp / bench_moe",),
+            constraint="unsupported_backend_configuration"))
     return model

@@ -179,3 +179,18 @@ def test_results_do_not_depend_on_chunk_size():
             s.register("t", t)
             outs.append(s.sql("SELECT id, AI.SCORE(PROMPT('Good? {0}', body)) AS s FROM t ORDER BY id").collect())
     assert np.allclose(outs[0].column("s").to_pylist(), outs[1].column("s").to_pylist(), atol=1e-5)
+
+
+def test_parallel_refusals():
+    import pytest as _pytest
+
+    from quail_b200.api.config import EngineConfig, RefusalError, check_config
+    assert check_config(EngineConfig(model="qwen3-tiny", device="cpu")).name == "qwen3-tiny"
+    with _pytest.raises(RefusalError, match="tensor parallelism runs dense Qwen3"):
+        check_config(EngineConfig(model="qwen3.5-tiny", device="cpu", parallel="tp"))
+    with _pytest.raises(RefusalError, match="expert parallelism needs"):
+        check_config(EngineConfig(model="qwen3-tiny", device="cpu", parallel="ep"))
+    with _pytest.raises(RefusalError, match="data parallelism"):
+        check_config(EngineConfig(model="qwen3-moe-gpu-tiny", device="cpu", parallel="ep", gpus=2))
+    with _pytest.raises(RefusalError, match="parallel is"):
+        check_config(EngineConfig(model="qwen3-tiny", device="cpu", parallel="pp"))
