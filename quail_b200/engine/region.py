@@ -192,7 +192,7 @@ class RegionRun:
             lab = np.asarray(call.labels[li], dtype=np.int32)
             toks = lab[:-1]
             self.fresh_tokens += len(toks)
-            self.ex.submit(Task(key=("lab", r, ci, li), tokens=toks, pos_start=pos + own_len,
+            self.ex.submit(Task(np_rows=True, key=("lab", r, ci, li), tokens=toks, pos_start=pos + own_len,
                                 reads=reads + [(key, own_len)], readout=True,
                                 readout_rows=tuple(range(len(toks))), full_readout=True,
                                 on_done=lambda t, rows, r=r, ci=ci, li=li: self._label_rows(r, ci, li, rows)))
@@ -255,7 +255,7 @@ class RegionRun:
         n_prev = len(generated) - 1
         nxt = self._draft(r, ci, call.max_tokens - len(generated)) if call.copy else ()
         self.fresh_tokens += 1 + len(nxt)
-        self.ex.submit_continuation(Task(key=key, tokens=[tok, *nxt], pos_start=pos + own_len + n_prev, reads=reads,
+        self.ex.submit_continuation(Task(np_rows=True, key=key, tokens=[tok, *nxt], pos_start=pos + own_len + n_prev, reads=reads,
                                          readout=True, full_readout=True, own_prefix=own_len + n_prev,
                                          free_after=False, topk=call.copy,
                                          readout_rows=tuple(range(1 + len(nxt))) if nxt else None,
@@ -357,7 +357,7 @@ class RegionRun:
         call = self.calls[ci]
         key, reads, pos, own_len = self._question(r, ci)
         self.fresh_tokens += len(call.suffix)
-        self.ex.submit(Task(key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
+        self.ex.submit(Task(np_rows=True, key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
                             full_readout=self._needs_full(call), reserve_tokens=self._reserve(call), topk=call.copy,
                             readout_rows=self._pooled_rows(call, len(call.suffix)),
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
@@ -365,14 +365,14 @@ class RegionRun:
     def submit_all(self) -> None:
         P = len(self.prefix)
         self.fresh_tokens += P
-        self.ex.submit(Task(key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
+        self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
         first = self.calls[0]
         for r, doc in enumerate(self.docs):
             toks = np.concatenate([doc, first.suffix])
             self.fresh_tokens += len(toks)
             self._next[r] = 1
             self._pending[r] = 1
-            self.ex.submit(Task(key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
+            self.ex.submit(Task(np_rows=True, key=("doc", r), tokens=toks, pos_start=P, reads=[(PREFIX_KEY, P)], readout=True,
                                 full_readout=self._needs_full(first), reserve_tokens=self._reserve(first),
                                 topk=first.copy,
                                 readout_rows=self._pooled_rows(first, len(toks)),

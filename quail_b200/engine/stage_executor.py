@@ -62,6 +62,7 @@ class Task:
     topk: bool = False                               # and the top-k token ids and logits
     reserve_tokens: int = 0                          # decode headroom allocated with the key's pages
     got_rows: list = field(default_factory=list)     # readout rows of the pieces already collected
+    np_rows: bool = False                            # on_done gets numpy rows (views of the pass's host copy)
 
     @property
     def remaining(self) -> int:
@@ -283,13 +284,15 @@ class StageExecutor:
         if ev0 is not None:
             self.stats.gpu_ms += ev0.elapsed_time(ev1)
         r = 0
+        hnp = host.numpy() if hasattr(host, "numpy") else host   # one view for the whole pass
         for s in specs:
             task: Task = s.tag
             last = s.own_start + len(s.tokens) == task.own_prefix + len(task.tokens)
             row = None
             if s.readout:
                 k = len(s.readout_rows) if s.readout_rows is not None else 1
-                row = host[r] if s.readout_rows is None else host[r:r + k]
+                src = hnp if task.np_rows else host
+                row = src[r] if s.readout_rows is None else src[r:r + k]
                 r += k
                 self.stats.readouts += 1
             if task.readout_rows is not None and task.readout:
