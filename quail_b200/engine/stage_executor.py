@@ -109,6 +109,7 @@ class StageExecutor:
         # continuations of resident keys (decode steps, label continuations):
         # admitted before new work, they need at most a page-list extension
         self.cont: deque[Task] = deque()
+        self.follow: deque[Task] = deque()   # new keys that read a resident document (follow-up questions)
         self.written: dict = {}     # key -> tokens written by launched chunks
         self.stats = ExecutorStats()
         self.gpu_timing = gpu_timing and self.device.type == "cuda"
@@ -126,6 +127,8 @@ class StageExecutor:
                 f"task {task.key!r} needs {need} pages; the arena has {self.pool.num_pages}")
         if task.own_prefix > 0 and self.pool.resident(task.key):
             self.cont.append(task)
+        elif len(task.reads) > 1:
+            self.follow.append(task)   # reads a document as well as the prefix: a follow-up
         else:
             self.queue.append(task)
 
@@ -164,13 +167,18 @@ class StageExecutor:
                                  task, rows, task.full_readout, task.topk))
             task.done = n
             room -= n
-        deferred: list[Task] = []
         scanned = 0
         no_new = False
-        while self.queue and room > 0 and scanned < 4096:
+        stop = False
+        # follow-ups (questions about resident documents) before new documents: they free
+        # their documents' pages when answered, so under memory pressure the rows in flight
+        # finish first instead of new documents taking the pages they need
+        for dq in (self.follow, self.queue):
+          deferred: list[Task] = []
+          while dq and room > 0 and scanned < 4096 and not stop:
             if self.max_seqs is not None and len(specs) >= self.max_seqs:
                 break
-            task = self.queue.popleft()
+            task = dq.popleft()
             scanned += 1
             if not self._readable(task):
                 deferred.append(task)
@@ -199,10 +207,12 @@ class StageExecutor:
                     self.pool.evict_retained(self.pool.pages_needed(total))
                     if self.pool.grow(task.key, total) is None:
                         deferred.append(task)
+                        stop = True
                         break
             piece = min(task.remaining, room)
             if piece < task.remaining and piece < self.min_piece and specs:
                 deferred.append(task)
+                stop = True
                 break
             last = piece == task.remaining
             rows = None
@@ -219,10 +229,11 @@ class StageExecutor:
             room -= piece
             if not last:
                 deferred.append(task)  # the rest goes in a later chunk
+                stop = True
                 break
-        # deferred tasks go back to the head in their original order
-        for t in reversed(deferred):
-            self.queue.appendleft(t)
+          # deferred tasks go back to the head of their queue in their original order
+          for t in reversed(deferred):
+              dq.appendleft(t)
         return specs
 
     # ------------------------------------------------------------ run
@@ -323,22 +334,28 @@ class StageExecutor:
 
     def run(self) -> ExecutorStats:
         t0 = time.perf_counter()
-        while self.queue or self.cont or self._inflight:
+        while self.pending() or self._inflight:
             if self.should_stop is not None and self.should_stop():
                 self.abort()
                 raise QueryCancelled("the query was stopped")
             if not self.step():
-                if self.queue or self.cont:
+                if self.pending():
+                    head = (self.follow or self.queue or self.cont)[0]
                     raise ArenaFullError(
-                        f"{len(self.queue)} tasks cannot be admitted: {self.pool.free_pages} free pages; "
-                        f"head {self.queue[0].key!r} reads {self.queue[0].reads}")
+                        f"{len(self.follow) + len(self.queue)} tasks cannot be admitted: {self.pool.free_pages} "
+                        f"free pages; head {head.key!r} reads {head.reads}")
                 break
         self.stats.wall_s += time.perf_counter() - t0
         return self.stats
 
+    def pending(self) -> bool:
+        """Tasks waiting for admission (new documents, follow-ups, continuations)."""
+        return bool(self.queue or self.follow or self.cont)
+
     def abort(self) -> None:
         """Drop queued work, wait for in-flight passes, release every resident key."""
         self.queue.clear()
+        self.follow.clear()
         self.cont.clear()
         while self._inflight:
             _, _, _, done, _, _ = self._inflight.popleft()

@@ -311,11 +311,11 @@ def run_lockstep(executor, pipe, cpu_group) -> None:
     t0 = time.perf_counter()
     flag = torch.zeros(1, dtype=torch.int32)
     while True:
-        flag[0] = 1 if (ex.queue or ex.cont or ex._inflight) else 0
+        flag[0] = 1 if (ex.pending() or ex._inflight) else 0
         dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=cpu_group)
         if int(flag[0]) == 0:
             break
-        specs = ex._admit() if (ex.queue or ex.cont) else []
+        specs = ex._admit() if ex.pending() else []
         if specs:
             ex._launch(specs)
             while len(ex._inflight) > 1:
@@ -324,6 +324,6 @@ def run_lockstep(executor, pipe, cpu_group) -> None:
             pipe.idle_pass()
             if ex._inflight:
                 ex._collect_one()
-    if ex.queue or ex.cont:
-        raise RuntimeError(f"{len(ex.queue) + len(ex.cont)} tasks were never admitted")
+    if ex.pending():
+        raise RuntimeError(f"{len(ex.queue) + len(ex.follow) + len(ex.cont)} tasks were never admitted")
     ex.stats.wall_s += time.perf_counter() - t0
