@@ -187,14 +187,34 @@ __global__ void gdn_gated_norm_kernel(const float* __restrict__ o, const __nv_bf
   if (idx >= T * Hv) return;
   const int t = idx / Hv, h = idx % Hv;
   const float* row = o + (size_t)t * Hv * DV + h * DV;
+  const __nv_bfloat16* zr = z + (size_t)t * ldz + z_col + h * DV;
+  __nv_bfloat16* yr = y + (size_t)t * Hv * DV + h * DV;
+  if (DV == 128 && ((ldz | z_col) & 3) == 0) {
+    // 4 values per lane: one float4 of o, 8 bytes of z and of y
+    const float4 v = *reinterpret_cast<const float4*>(row + lane * 4);
+    const float r = rsqrtf(warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) / DV + eps);
+    const uint2 zraw = *reinterpret_cast<const uint2*>(zr + lane * 4);
+    const uint2 wraw = *reinterpret_cast<const uint2*>(w + lane * 4);
+    const float2 z01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zraw.x));
+    const float2 z23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zraw.y));
+    const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wraw.x));
+    const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wraw.y));
+    auto g = [](float zz) { return zz / (1.f + __expf(-zz)); };
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x * r * w01.x * g(z01.x), v.y * r * w01.y * g(z01.y));
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v.z * r * w23.x * g(z23.x), v.w * r * w23.y * g(z23.y));
+    uint2 out;
+    out.x = *reinterpret_cast<const uint32_t*>(&a);
+    out.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(yr + lane * 4) = out;
+    return;
+  }
   float ss = 0.f;
   for (int d = lane; d < DV; d += 32) ss += row[d] * row[d];
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / DV + eps);
   for (int d = lane; d < DV; d += 32) {
-    const float zz = __bfloat162float(z[(size_t)t * ldz + z_col + h * DV + d]);
-    const float v = row[d] * r * __bfloat162float(w[d]) * (zz / (1.f + __expf(-zz)));
-    y[(size_t)t * Hv * DV + h * DV + d] = __float2bfloat16(v);
+    const float zz = __bfloat162float(zr[d]);
+    yr[d] = __float2bfloat16(row[d] * r * __bfloat162float(w[d]) * (zz / (1.f + __expf(-zz))));
   }
 }
 

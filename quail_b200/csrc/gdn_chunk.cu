@@ -857,24 +857,39 @@ __global__ void __launch_bounds__(256) gdn_conv_chunk_kernel(
     w[j][0] = v.x; w[j][1] = v.y; w[j][2] = v.z; w[j][3] = v.w;
   }
   const float* win = src >= 0 ? conv_state + ((size_t)src * G + gi) * 3 * C : nullptr;
-  for (int tt = warp; tt < cn; tt += 8) {
+  // input row `pos` of the sequence (the source window before its first token)
+  auto load_in = [&](int pos, float* x) {
+    x[0] = x[1] = x[2] = x[3] = 0.f;
+    if (pos >= 0) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(mixed + (size_t)(q0 + pos) * ldm + ch);
+      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+      x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
+    } else if (win != nullptr) {
+      const float4 v = *reinterpret_cast<const float4*>(win + (size_t)(3 + pos) * C + ch);
+      x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    }
+  };
+  // each warp takes 8 consecutive tokens and slides the 4-row window over them,
+  // loading one new input row per token
+  const int t_lo = warp * 8, t_hi = min(cn, t_lo + 8);
+  float hist[3][4];
+  if (t_lo < t_hi)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) load_in(c0 + t_lo - 3 + k, hist[k]);
+  for (int tt = t_lo; tt < t_hi; ++tt) {
     const int t = c0 + tt;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float cur[4];
+    load_in(t, cur);
+    float acc[4];
 #pragma unroll
-    for (int tap = 0; tap < 4; ++tap) {
-      const int pos = t - 3 + tap;
-      float x[4] = {0.f, 0.f, 0.f, 0.f};
-      if (pos >= 0) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(mixed + (size_t)(q0 + pos) * ldm + ch);
-        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
-      } else if (win != nullptr) {
-        const float4 v = *reinterpret_cast<const float4*>(win + (size_t)(3 + pos) * C + ch);
-        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
-      }
+    for (int j = 0; j < 4; ++j)
+      acc[j] = w[j][0] * hist[0][j] + w[j][1] * hist[1][j] + w[j][2] * hist[2][j] + w[j][3] * cur[j];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] += w[j][tap] * x[j];
+    for (int j = 0; j < 4; ++j) {
+      hist[0][j] = hist[1][j];
+      hist[1][j] = hist[2][j];
+      hist[2][j] = cur[j];
     }
     float y[4], ss = 0.f;
 #pragma unroll
