@@ -282,7 +282,7 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
                       int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk, const int* seqs,
                       const int* sio, int S, float* ssm_state, int gi, int G, float* out, int dev,
                       cudaStream_t st);
-int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv);
+int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv, int64_t C);
 void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, float* conv_state, float q_scale,
                             float* conv_out, int C, int qk_channels, const __nv_bfloat16* ab, int ldab,
                             int b_col, int a_col, const float* A_log, const float* dt_bias, int Hv, int Hk,
@@ -325,7 +325,7 @@ void gdn_layer(const torch::Tensor& proj, const torch::Tensor& wconv, const torc
   if (chunked && mode != 2) {
     // the workspace comes from PyTorch's caching allocator on the current stream;
     // the conv runs token-parallel over the same chunk list
-    auto ws = at::empty({gdn_chunk_ws_bytes(T, S, Hv)}, proj.options().dtype(at::kByte));
+    auto ws = at::empty({gdn_chunk_ws_bytes(T, S, Hv, C)}, proj.options().dtype(at::kByte));
     launch_gdn_chunk_split(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), wconv.data_ptr<float>(),
                            conv_state.data_ptr<float>(), q_scale, conv_out.data_ptr<float>(), C, (int)(2 * Hk * DK),
                            reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), ld, b_col, a_col,

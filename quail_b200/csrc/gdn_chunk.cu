@@ -393,19 +393,19 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(
 // the triangular solve) runs in parallel over every chunk of the pass:
 //   gdn_chunk_index   the pass's chunk list (sequence, first token) and each
 //                     sequence's first chunk, by a block-wide scan
+//   gdn_conv_chunk    the causal conv, token-parallel, into a bf16 [T, C] buffer
+//                     that the two kernels below read (q, k, v rows)
 //   gdn_chunk_prep    one CTA per (chunk, value head): writes the chunk's record
-//                     -W, U~, q, k (bf16 [64][128]), M o QK^T (bf16 [64][64]), G (fp32 [64])
+//                     -W, U~ (bf16 [64][128]), M o QK^T (bf16 [64][64]), G (fp32 [64])
 //   gdn_chunk_scan    one CTA per (sequence, value head): walks the records with
 //                     the state: U = U~ + (-W) S0, O, S update (as above); the
 //                     next record streams into shared memory (cp.async, two
 //                     buffers) while the current one is in the tensor cores
 constexpr int kRecW = 0;                      // bf16 [64][128] -W
 constexpr int kRecU = kRecW + kCh * kD * 2;   // bf16 [64][128] U~
-constexpr int kRecQ = kRecU + kCh * kD * 2;   // bf16 [64][128] q rows
-constexpr int kRecK = kRecQ + kCh * kD * 2;   // bf16 [64][128] k rows
-constexpr int kRecM = kRecK + kCh * kD * 2;   // bf16 [64][64] M o QK^T
+constexpr int kRecM = kRecU + kCh * kD * 2;   // bf16 [64][64] M o QK^T
 constexpr int kRecG = kRecM + kCh * kCh * 2;  // fp32 [64] G
-constexpr int kRecBytes = kRecG + kCh * 4;    // 73,984 B = 289 x 256
+constexpr int kRecBytes = kRecG + kCh * 4;    // 41,216 B = 161 x 256
 static_assert(kRecBytes % 256 == 0, "records stay 256-byte aligned");
 
 // ws ints: [0] chunk count, [4, 4 + 2 maxc) the (sequence, first token) list,
@@ -483,7 +483,7 @@ struct GpSmem {
 };
 
 __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
-    const float* __restrict__ conv_out, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
+    const __nv_bfloat16* __restrict__ cv, int C, int qk_channels, const __nv_bfloat16* __restrict__ ab, int ldab,
     int b_col, int a_col, const float* __restrict__ A_log, const float* __restrict__ dt_bias, int Hv, int Hk,
     const int* __restrict__ seqs, const int* __restrict__ ws, uint8_t* __restrict__ recs) {
   const int ci = blockIdx.x, h = blockIdx.y;
@@ -504,26 +504,18 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
   const int kofs = qk_channels / 2 + hk * kD, qofs = hk * kD, vofs = qk_channels + h * kD;
   uint8_t* rec = recs + ((size_t)ci * Hv + h) * kRecBytes;
 
-  for (int idx = tid; idx < kCh * (kD / 4); idx += 256) {
-    const int row = idx >> 5, col = (idx & 31) * 4;
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
+  for (int idx = tid; idx < kCh * (kD / 8); idx += 256) {
+    const int row = idx >> 4, col = (idx & 15) * 8;
+    uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q;
     if (row < cn) {
-      const float* r = conv_out + (size_t)(q0 + c0 + row) * C;
-      q = *reinterpret_cast<const float4*>(r + qofs + col);
-      k = *reinterpret_cast<const float4*>(r + kofs + col);
-      v = *reinterpret_cast<const float4*>(r + vofs + col);
+      const __nv_bfloat16* r = cv + (size_t)(q0 + c0 + row) * C;
+      q = *reinterpret_cast<const uint4*>(r + qofs + col);
+      k = *reinterpret_cast<const uint4*>(r + kofs + col);
+      v = *reinterpret_cast<const uint4*>(r + vofs + col);
     }
-    uint32_t* dq = reinterpret_cast<uint32_t*>(smem + GpSmem::Q + row * P2 + col * 2);
-    uint32_t* dk = reinterpret_cast<uint32_t*>(smem + GpSmem::K + row * P2 + col * 2);
-    uint32_t* dv = reinterpret_cast<uint32_t*>(smem + GpSmem::V + row * P2 + col * 2);
-    dq[0] = gc_pack(q.x, q.y);
-    dq[1] = gc_pack(q.z, q.w);
-    dk[0] = gc_pack(k.x, k.y);
-    dk[1] = gc_pack(k.z, k.w);
-    dv[0] = gc_pack(v.x, v.y);
-    dv[1] = gc_pack(v.z, v.w);
-    *reinterpret_cast<uint2*>(rec + kRecQ + (row * kD + col) * 2) = make_uint2(dq[0], dq[1]);
-    *reinterpret_cast<uint2*>(rec + kRecK + (row * kD + col) * 2) = make_uint2(dk[0], dk[1]);
+    *reinterpret_cast<uint4*>(smem + GpSmem::Q + row * P2 + col * 2) = q;
+    *reinterpret_cast<uint4*>(smem + GpSmem::K + row * P2 + col * 2) = k;
+    *reinterpret_cast<uint4*>(smem + GpSmem::V + row * P2 + col * 2) = v;
   }
   if (tid < kCh) {
     float gl = 0.f, beta = 0.f;
@@ -642,13 +634,26 @@ __device__ __forceinline__ void gc_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// one record into buffer `buf`: the four [64][128] tiles, M and G (16 B pieces)
-__device__ __forceinline__ void gc_fetch_record(uint32_t sbuf, const uint8_t* rec, int tid) {
+__device__ __forceinline__ void gc_cp16z(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+// one chunk into buffer `buf`: its q and k rows from the bf16 conv buffer (rows
+// past the chunk's end zero-filled), the record's -W and U~ tiles, M and G (16 B pieces)
+__device__ __forceinline__ void gc_fetch_record(uint32_t sbuf, const uint8_t* rec, const __nv_bfloat16* qrows,
+                                                const __nv_bfloat16* krows, int C, int cn, int tid) {
   constexpr int P2 = kP * 2, Pm2 = kPm * 2;
-  for (int idx = tid; idx < 4 * kCh * 16; idx += 256) {
+  for (int idx = tid; idx < 2 * kCh * 16; idx += 256) {
     const int tile = idx >> 10, row = (idx >> 4) & 63, c16 = idx & 15;
-    const int src = tile == 0 ? kRecQ : tile == 1 ? kRecK : tile == 2 ? kRecW : kRecU;
-    const int dst = tile == 0 ? GsSmem::Q : tile == 1 ? GsSmem::K : tile == 2 ? GsSmem::W : GsSmem::Ut;
+    const bool valid = row < cn;
+    const __nv_bfloat16* src = (tile == 0 ? qrows : krows) + (size_t)(valid ? row : 0) * C + c16 * 8;
+    gc_cp16z(sbuf + (tile == 0 ? GsSmem::Q : GsSmem::K) + row * P2 + c16 * 16, src, valid);
+  }
+  for (int idx = tid; idx < 2 * kCh * 16; idx += 256) {
+    const int tile = idx >> 10, row = (idx >> 4) & 63, c16 = idx & 15;
+    const int src = tile == 0 ? kRecW : kRecU;
+    const int dst = tile == 0 ? GsSmem::W : GsSmem::Ut;
     gc_cp16(sbuf + dst + row * P2 + c16 * 16, rec + src + row * kD * 2 + c16 * 16);
   }
   for (int idx = tid; idx < kCh * 8; idx += 256) {
@@ -659,8 +664,9 @@ __device__ __forceinline__ void gc_fetch_record(uint32_t sbuf, const uint8_t* re
 }
 
 __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
-    int Hv, const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi, int G,
-    const int* __restrict__ ws, int maxc, const uint8_t* __restrict__ recs, float* __restrict__ out) {
+    int Hv, int Hk, const int* __restrict__ seqs, const int* __restrict__ sio, float* __restrict__ ssm_state, int gi,
+    int G, const int* __restrict__ ws, int maxc, const uint8_t* __restrict__ recs, const __nv_bfloat16* __restrict__ cv,
+    int C, int qk_channels, float* __restrict__ out) {
   extern __shared__ __align__(16) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
   const uint32_t aS = base + GsSmem::S, aU = base + GsSmem::U, aUs = base + GsSmem::Us;
@@ -676,8 +682,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
   const size_t slot_stride = (size_t)G * Hv * kD * kD;
   const size_t head_off = ((size_t)gi * Hv + h) * kD * kD;
   auto record = [&](int c) { return recs + ((size_t)(first + c) * Hv + h) * kRecBytes; };
+  const int hk = h / (Hv / Hk);
+  const __nv_bfloat16* qbase = cv + (size_t)q0 * C + hk * kD;
+  const __nv_bfloat16* kbase = cv + (size_t)q0 * C + qk_channels / 2 + hk * kD;
+  auto fetch = [&](uint32_t sbuf, int c) {
+    gc_fetch_record(sbuf, record(c), qbase + (size_t)c * kCh * C, kbase + (size_t)c * kCh * C, C,
+                    min(kCh, n - c * kCh), tid);
+  };
   if (nch > 0) {
-    gc_fetch_record(base, record(0), tid);
+    fetch(base, 0);
     gc_commit();
   }
 
@@ -708,7 +721,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
     const int c0 = c * kCh, cn = min(kCh, n - c0);
     const uint32_t boff = (c & 1) * GsSmem::BUF;
     if (c + 1 < nch) {
-      gc_fetch_record(base + (boff ^ GsSmem::BUF), record(c + 1), tid);
+      fetch(base + (boff ^ GsSmem::BUF), c + 1);
       gc_commit();
       gc_wait<1>();
     } else {
@@ -839,7 +852,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
 __global__ void __launch_bounds__(256) gdn_conv_chunk_kernel(
     const __nv_bfloat16* __restrict__ mixed, int ldm, int C, int qk_channels, const float* __restrict__ wconv,
     const int* __restrict__ seqs, const int* __restrict__ sio, const float* __restrict__ conv_state, int gi, int G,
-    float q_scale, const int* __restrict__ ws, float* __restrict__ out) {
+    float q_scale, const int* __restrict__ ws, __nv_bfloat16* __restrict__ out) {
   const int ci = blockIdx.x;
   if (ci >= ws[0]) return;
   const int2 e = reinterpret_cast<const int2*>(ws + 4)[ci];
@@ -903,7 +916,7 @@ __global__ void __launch_bounds__(256) gdn_conv_chunk_kernel(
 #pragma unroll
       for (int j = 0; j < 4; ++j) y[j] *= r;
     }
-    *reinterpret_cast<float4*>(out + (size_t)(q0 + t) * C + ch) = make_float4(y[0], y[1], y[2], y[3]);
+    *reinterpret_cast<uint2*>(out + (size_t)(q0 + t) * C + ch) = make_uint2(gc_pack(y[0], y[1]), gc_pack(y[2], y[3]));
   }
 }
 
@@ -949,10 +962,11 @@ void launch_gdn_chunk(const float* conv_out, int C, int qk_channels, const __nv_
 }
 
 // Bytes of the split form's workspace for a pass of T tokens in S sequences.
-int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv) {
+int64_t gdn_chunk_ws_bytes(int64_t T, int64_t S, int64_t Hv, int64_t C) {
   const int64_t maxc = T / kCh + S + 1;
   const int64_t ints = ((4 + 2 * maxc + 2 * S) * 4 + 255) / 256 * 256;
-  return ints + maxc * Hv * kRecBytes;
+  const int64_t cvb = (T * C * 2 + 255) / 256 * 256;
+  return ints + cvb + maxc * Hv * kRecBytes;
 }
 
 void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, float* conv_state, float q_scale,
@@ -971,19 +985,20 @@ void launch_gdn_chunk_split(const __nv_bfloat16* mixed, const float* wconv, floa
   const int maxc = T / kCh + S + 1;
   const int64_t ints = ((4 + 2 * (int64_t)maxc + 2 * S) * 4 + 255) / 256 * 256;
   int* wsi = reinterpret_cast<int*>(ws);
-  uint8_t* recs = ws + ints;
+  __nv_bfloat16* cv = reinterpret_cast<__nv_bfloat16*>(ws + ints);
+  uint8_t* recs = ws + ints + ((int64_t)T * C * 2 + 255) / 256 * 256;
   gdn_chunk_index_kernel<<<1, 256, 0, st>>>(seqs, S, maxc, wsi);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   gdn_conv_chunk_kernel<<<dim3(maxc, C / 128), 256, 0, st>>>(mixed, ldab, C, qk_channels, wconv, seqs, sio,
-                                                              conv_state, gi, G, q_scale, wsi, conv_out);
+                                                              conv_state, gi, G, q_scale, wsi, cv);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   gdn_conv_window_kernel<<<dim3(S, C / 128), 128, 0, st>>>(mixed, ldab, C, seqs, sio, conv_state, gi, G);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(conv_out, C, qk_channels, ab, ldab, b_col,
+  gdn_chunk_prep_kernel<<<dim3(maxc, Hv), 256, GpSmem::BYTES, st>>>(cv, C, qk_channels, ab, ldab, b_col,
                                                                      a_col, A_log, dt_bias, Hv, Hk, seqs, wsi, recs);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  gdn_chunk_scan_kernel<<<dim3(Hv, S), 256, GsSmem::BYTES, st>>>(Hv, seqs, sio, ssm_state, gi, G, wsi, maxc, recs,
-                                                                  out);
+  gdn_chunk_scan_kernel<<<dim3(Hv, S), 256, GsSmem::BYTES, st>>>(Hv, Hk, seqs, sio, ssm_state, gi, G, wsi, maxc,
+                                                                  recs, cv, C, qk_channels, out);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
