@@ -6,7 +6,10 @@ hash_join ..., crates/quail-planner/src/physical/nodes.rs:168-349) and prints
 estimated times per node (explain.rs). This planner derives the same node
 sequence from the syntax tree in the order the executor runs it (relational
 conjuncts first, the guarded AI.IF chain, then projection calls) and prices
-each model node with the roofline of `Budgets.pass_seconds`.
+each model node with the roofline of `Budgets.pass_seconds`: prefill of the
+document and question tokens, plus one pass per generated token for AI.MAP /
+AI.EXTRACT; an AI filter keeps its options' 'selectivity' share of the rows
+(one half without one).
 """
 
 from __future__ import annotations
@@ -76,7 +79,38 @@ def _expr_text(e) -> str:
         return e["name"] + "(" + ", ".join(_expr_text(a) for a in e.get("args", []) if isinstance(a, dict)) + ")"
     if t == "binary":
         return f"{_expr_text(e['left'])} {e['op']} {_expr_text(e['right'])}"
+    if t == "array":
+        return "[" + ", ".join(_expr_text(i) for i in e.get("items", [])) + "]"
+    if t == "object":
+        return "{" + ", ".join(f"{k!r}: {_expr_text(v)}" for k, v in e.get("items", [])) + "}"
     return t
+
+
+def _selectivity(call) -> float:
+    """The share of rows an AI filter keeps: its options' 'selectivity', else one half."""
+    from quail_b200.sql.executor import literal_value
+    args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
+    if len(args) > 1:
+        try:
+            v = literal_value(args[1])
+            if isinstance(v, dict) and isinstance(v.get("selectivity"), (int, float)):
+                return min(max(float(v["selectivity"]), 0.0), 1.0)
+        except Exception:  # noqa: BLE001 - a non-literal option prices at the default
+            pass
+    return 0.5
+
+
+def _decode_tokens(call) -> int:
+    """Tokens a decoding call generates per row at most (AI.MAP's max_tokens, AI.EXTRACT's 64 per question)."""
+    from quail_b200.sql.executor import MAP_DEFAULT_TOKENS, literal_value
+    args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
+    if call["name"] == "AI.MAP":
+        v = literal_value(args[2]) if len(args) > 2 else MAP_DEFAULT_TOKENS
+        return int(v) if isinstance(v, int) else MAP_DEFAULT_TOKENS
+    if call["name"] in ("AI.EXTRACT", "AI.EXTRACT_SPAN"):
+        qs = literal_value(args[1]) if len(args) > 1 else []
+        return 64 * (1 if isinstance(qs, str) else max(len(qs), 1))
+    return 0
 
 
 def plan_query(tree: dict, session) -> Plan:
@@ -135,13 +169,18 @@ def _plan_select(node, session, budgets) -> PlanNode:
                     secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / max(session.config.gpus, 1)
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
                                children=[cur] if cur else [])
-                rows = rows * 0.5 if rows is not None else None
+                rows = rows * _selectivity(n) if rows is not None else None
     for it in node["items"]:
         for n in walk(it["expr"]):
             if is_model_call(n):
                 secs = None
                 if rows is not None:
-                    secs = budgets.pass_seconds(int(rows * tail_tokens), mean_doc_tokens) / max(session.config.gpus, 1)
+                    secs = budgets.pass_seconds(int(rows * tail_tokens), mean_doc_tokens)
+                    steps = _decode_tokens(n)
+                    if steps:
+                        # greedy decode: one token per row per step over the row's context
+                        secs += steps * budgets.pass_seconds(max(int(rows), 1), mean_doc_tokens + steps / 2)
+                    secs /= max(session.config.gpus, 1)
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
                                children=[cur] if cur else [])
     if node.get("group_by") is not None:

@@ -29,6 +29,8 @@ QUERIES = {
             "WHERE AI.IF(PROMPT('Is {0} about a sequel?', r.body))",
     "aggregate": "SELECT stars, COUNT(*) AS n FROM reviews WHERE AI.IF(PROMPT('Is it sarcastic? {0}', body)) "
                  "GROUP BY stars ORDER BY stars",
+    "selectivity": "SELECT id, AI.SCORE(PROMPT('Is it positive? {0}', body)) AS s FROM reviews "
+                   "WHERE AI.IF(PROMPT('Is it about acting? {0}', body), {'selectivity': 0.25})",
     "cte": "WITH good AS (SELECT id, body FROM reviews WHERE stars >= 4) "
            "SELECT id, AI.SCORE(PROMPT('Would they rewatch? {0}', body)) AS s FROM good",
 }
