@@ -124,6 +124,39 @@ def plan_query(tree: dict, session) -> Plan:
     return Plan(root=_plan_select(node, session, budgets), settings=settings)
 
 
+def _doc_column(call):
+    """The column a call reads as its document (a plain column or PROMPT's one argument), or None."""
+    args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
+    if not args:
+        return None
+    d = args[0]
+    if d.get("type") == "call" and d.get("name") == "PROMPT" and len(d.get("args", [])) == 2:
+        d = d["args"][1]
+    return d.get("name") if d.get("type") == "column" else None
+
+
+def _mean_doc_tokens(call, ref, session, default: float = 300.0) -> float:
+    """Mean document length in tokens from a sample of the scanned column: token-id lists by
+    their length, text at about 4 characters per token; `default` when it cannot tell."""
+    col = _doc_column(call)
+    if col is None or ref is None or ref.get("type") != "table":
+        return default
+    try:
+        from quail_b200.catalog.providers import ScanRequest
+        for k, p in session.catalog.items():
+            if k.lower() != ref["name"].lower():
+                continue
+            name = next((c for c in p.columns if c.lower() == col.lower()), None)
+            if name is None:
+                return default
+            vals = p.scan(ScanRequest(columns=(name,), limit=256)).read_all().column(0).to_pylist()
+            lens = [len(v) / (4.0 if isinstance(v, str) else 1.0) for v in vals if v is not None]
+            return max(sum(lens) / len(lens), 1.0) if lens else default
+    except Exception:  # noqa: BLE001 - statistics are best effort
+        return default
+    return default
+
+
 def _rows_of(ref, session) -> float | None:
     if ref.get("type") != "table":
         return None
@@ -155,7 +188,7 @@ def _plan_select(node, session, budgets) -> PlanNode:
             r2 = right.rows
             rows = rows * r2 if rows is not None and r2 is not None and kind == "AiJoin" else rows
             cur = PlanNode(kind, j["kind"], rows=rows, children=[cur, right])
-    mean_doc_tokens = 300.0
+    base_ref = node["from"][0] if node.get("from") and not node.get("joins") else None
     tail_tokens = 60.0
     for c in conjuncts(node.get("where")):
         if not has_model_call(c):
@@ -164,6 +197,7 @@ def _plan_select(node, session, budgets) -> PlanNode:
         for n in walk(c):
             if is_model_call(n):
                 secs = None
+                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session)
                 if rows is not None:
                     tokens = rows * (mean_doc_tokens + tail_tokens)
                     secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / max(session.config.gpus, 1)
@@ -174,6 +208,7 @@ def _plan_select(node, session, budgets) -> PlanNode:
         for n in walk(it["expr"]):
             if is_model_call(n):
                 secs = None
+                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session)
                 if rows is not None:
                     secs = budgets.pass_seconds(int(rows * tail_tokens), mean_doc_tokens)
                     steps = _decode_tokens(n)
