@@ -28,7 +28,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKS_PER_GPU = 17_000.0   # H100 SXM, qwen3-4b-fp8 prompt tok/s per GPU
+BASELINE_TOKS_PER_GPU = 17_000.0   # H100 SXM, qwen3-4b-fp8 prompt tok/s per GPU (the published reference number)
 METRIC = "AI-function rows/sec & prefill tok/s per box (AI.IF, qwen3-4b-fp8), device-timed"
 
 

@@ -136,7 +136,7 @@ QWEN3_32B = DecoderConfig(name="qwen3-32b", layers=64, hidden=5120, num_q_heads=
 QWEN3_30B_A3B = DecoderConfig(name="qwen3-30b-a3b", layers=48, hidden=2048, num_q_heads=32,
                               num_kv_heads=4, head_dim=128, intermediate=6144, num_experts=128,
                               top_k=8, moe_intermediate=768)
-# BASELINE config 1: the CPU plumbing model (fp32, tiny)
+# the CPU plumbing model (fp32, tiny)
 QWEN3_TINY = DecoderConfig(name="qwen3-tiny", layers=2, hidden=256, num_q_heads=4, num_kv_heads=2,
                            head_dim=64, intermediate=768, weight_dtype="bf16")
 # the smallest model the GPU kernels take (head_dim 128, hidden multiple of 256)
