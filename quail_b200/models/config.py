@@ -199,6 +199,7 @@ DECISION_TINY = QWEN3_TINY.with_(name="decision-tiny", role="decision", prompt_l
 DECISION_GPU_TINY = QWEN3_GPU_TINY.with_(name="decision-gpu-tiny", role="decision", prompt_layout="decision2-noul",
                                          decision_head_dim=128, weight_dtype="bf16")
 RERANKER_TINY = QWEN3_TINY.with_(name="reranker-tiny", role="reranker", weight_dtype="bf16")
+RERANKER_GPU_TINY = QWEN3_GPU_TINY.with_(name="reranker-gpu-tiny", role="reranker", weight_dtype="bf16")
 QWEN35_9B = QWEN35_4B.with_(name="qwen3.5-9b", hidden=4096, intermediate=12288, tied_head=False)
 QWEN35_4B_FP8 = QWEN35_4B.with_(name="qwen3.5-4b-fp8", weight_dtype="fp8")
 QWEN35_GPU_TINY_FP8 = QWEN35_GPU_TINY.with_(name="qwen3.5-gpu-tiny-fp8", weight_dtype="fp8")
@@ -232,7 +233,7 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
                                QWEN35_2B_SAE, QWEN35_SAE_TINY, DECISION_TINY, DECISION_GPU_TINY, RERANKER_TINY,
-                               QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, QWEN35_27B_FP8, QWEN38_27B_FP8,
+                               QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, RERANKER_GPU_TINY, QWEN35_27B_FP8, QWEN38_27B_FP8,
                                QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY, QWEN38_27B_NVFP4,
                                QWEN35_GPU_TINY_NVFP4)}
 
@@ -265,6 +266,7 @@ MODEL_CONFIGS = {
     "decision-tiny": DECISION_TINY,
     "decision-gpu-tiny": DECISION_GPU_TINY,
     "reranker-tiny": RERANKER_TINY,
+    "reranker-gpu-tiny": RERANKER_GPU_TINY,
     "qwen3.5-4b-fp8": QWEN35_4B_FP8,
     "qwen3.5-gpu-tiny-fp8": QWEN35_GPU_TINY_FP8,
     "qwen3.5-27b-fp8": QWEN35_27B_FP8,

@@ -80,3 +80,31 @@ def test_extract_copies_from_the_document(session):
     for body, e in zip(t.column("body").to_pylist(), t.column("e").to_pylist()):
         for phrase in e:
             assert phrase is None or phrase.strip() in body, (phrase, body)
+
+
+def test_reranker_model_on_the_kernels():
+    """A Qwen3 reranker on the bf16 kernels against the same weights in the fp32 reference
+    model: AI.SCORE = sigmoid(yes - no) of its chat prompt, to bf16 accuracy."""
+    import torch
+    from quail_b200.api.engine import ModelEngine
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.models.build import random_checkpoint_on
+    from quail_b200.models.qwen3 import Qwen3Reference
+    rng = np.random.default_rng(2)
+    words = ["refund", "late", "broken", "great", "thanks", "order"]
+    bodies = [" ".join(rng.choice(words, size=int(rng.integers(3, 30)))) for _ in range(12)]
+    q = "SELECT id, AI.SCORE(PROMPT('Does {0} ask for a refund?', body)) AS s FROM t ORDER BY id"
+    cfg = quail.EngineConfig(model="reranker-gpu-tiny", device="b200", chunk_tokens=2048)
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": list(range(12)), "body": bodies}))
+        got = s.sql(q).collect()
+        eng = s.engine()
+        m = eng.cfg
+        ref_model = Qwen3Reference(m, random_checkpoint_on(m, eng.device, seed=0), device=eng.device)
+        arena = KVArena(m.layers, 4096, 16, m.num_kv_heads, m.head_dim, device=eng.device, dtype=torch.float32)
+        s._engine = ModelEngine.from_replica(cfg, ref_model, arena, tokenizer=eng.tokenizer)
+        want = s.sql(q).collect()
+        s._engine = eng
+    a, b = np.array(got.column("s").to_pylist()), np.array(want.column("s").to_pylist())
+    assert np.all((a >= 0) & (a <= 1))
+    np.testing.assert_allclose(a, b, atol=0.03)
