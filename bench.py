@@ -42,6 +42,9 @@ def parse():
     ap.add_argument("--chunk-tokens", type=int, default=16384)
     ap.add_argument("--pages", type=int, default=1024)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-pass", action="store_true",
+                    help="after the timed steps, run one more pass between cudaProfilerStart/Stop "
+                         "(for `ncu --profile-from-start off`); it is not timed")
     return ap.parse_args()
 
 
@@ -125,6 +128,12 @@ def main():
     err = ops.read_and_clear_error(local)
     if err:
         raise RuntimeError(f"kernel error code {err}")
+    if args.profile_pass:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ex.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     # drain the rest of this workload (not timed) so the arena is clean
     while ex.step():
         pass
@@ -164,7 +173,9 @@ def main():
             "baseline_value": BASELINE_TOKS_PER_GPU * world,
             "rows_per_second": round(rows_all / (ms_max / 1e3), 1),
             "fresh_tokens_per_second": round(fresh_all / (ms_max / 1e3), 1),
-            "dtype": ("fp8 e4m3 weights+activations (128x128 / 1x128 block scales), bf16 KV and residual"
+            "dtype": ("fp8 e4m3 weights+activations, MX block scaling on the tensor cores: UE8M0 (power-of-two) "
+                      "scales per 1x32 activation group and per 128x128 weight block (checkpoint fp32 "
+                      "128x128 weight_scale_inv requantized to UE8M0 at load); bf16 KV cache and residual"
                       if cfg.fp8 else "bf16"),
             "data": "synthetic: random token-id bodies lognormal(median 180, sigma 0.6) clipped [16, 2048], "
                     "48-token shared template prefix, 40-token question suffix; random-init weights N(0, 0.02)",

@@ -29,7 +29,6 @@ constexpr int kStages = 4;
 constexpr int kSmem = kStages * (128 * 128 + kBN * 128) + 1024 + 256 + 4096;
 
 struct DeviceSetup {
-  bool done = false;
   bool ok = false;
   uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
   int sms = 0;
@@ -57,8 +56,8 @@ DeviceSetup* setup_current_device() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceSetup& s = g_setup[dev];
-  if (s.done) return s.ok ? &s : nullptr;
-  s.done = true;
+  if (s.ok) return &s;
+  // a failed set-up is not remembered: the next call on this device tries again
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
   s.scratch = static_cast<uint8_t*>(p);
@@ -109,7 +108,11 @@ extern "C" int qb_gemm_fp8_noalloc(const void* a, int64_t lda, const float* a_sc
 
   // the status word must start at zero on every call
   if (cudaMemsetAsync(status, 0, sizeof(int), stream) != cudaSuccess) return QB_NOALLOC_LAUNCH_FAILED;
-  if (M == 0) return QB_NOALLOC_OK;
+  if (M == 0) {
+    // nothing to compute; the caller still gets the status word it asked for
+    if (status_out) *status_out = 0;
+    return QB_NOALLOC_OK;
+  }
 
   const int n = M * G;
   transpose_scales_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a_scale, sa, M, G);

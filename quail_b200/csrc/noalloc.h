@@ -49,7 +49,9 @@ extern "C" {
 //
 // The first call on a device looks up the scratch array's device address
 // (cudaGetSymbolAddress) with that device current and sets the kernel's
-// shared-memory limit; make that first call before any stream capture.
+// shared-memory limit; make that first call before any stream capture. If
+// that set-up fails (QB_NOALLOC_SETUP_FAILED), nothing is remembered and
+// the next call on the device tries it again.
 // Every call reuses the same scratch array: it clears the status word,
 // then overwrites the scales, so two calls whose work overlaps on the GPU
 // (different streams, or different host threads on one device) race on
@@ -57,7 +59,8 @@ extern "C" {
 //
 // status_out: NULL to return right after enqueueing; otherwise the call
 // synchronizes `stream`, stores the kernel's status word there (0 = ok) and
-// returns QB_NOALLOC_KERNEL_TIMEOUT if it is not zero.
+// returns QB_NOALLOC_KERNEL_TIMEOUT if it is not zero. With M == 0 nothing
+// is launched and *status_out is set to 0.
 int qb_gemm_fp8_noalloc(const void* a, int64_t lda, const float* a_scale, const void* b, int64_t ldb,
                         const float* b_scale, void* d, int64_t ldd, int M, int N, int K, cudaStream_t stream,
                         int* status_out);

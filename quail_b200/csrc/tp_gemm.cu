@@ -6,11 +6,14 @@
 // output columns (QKV, gate_up) or by input columns (o_proj, down).
 //
 //   AG -> GEMM (QKV, gate_up): every rank's normalized e4m3 shard and its MX
-//     scale atoms sit at their own rows of a symmetric buffer. The GEMM CTA
-//     has two gather warps that copy peer shards, one 128-row m-tile at a
-//     time, from the peer's buffer into the same rows of the local one with
-//     plain P2P loads (each remote tile crosses NVLink once), then release a
-//     per-m-tile ready word. The TMA producer starts with the local shard's
+//     scale atoms sit at their own rows of a symmetric buffer. In each GEMM
+//     CTA one elected thread of the gather warps copies peer shards, one
+//     128-row m-tile at a time, into the same rows of the local buffer: a
+//     non-multicast cp.async.bulk load brings an 8 KB piece from the peer's
+//     memory into shared memory (two pieces in flight), a cp.async.bulk store
+//     writes it to local memory (each remote tile crosses NVLink once), and
+//     after the last store of the m-tile lands it releases a per-m-tile
+//     ready word. The TMA producer starts with the local shard's
 //     m-tiles and waits (bounded) on the ready word of each remote m-tile
 //     before its first TMA load. Peers announce their shard with a ready flag
 //     (written by the norm kernel that produced it).
@@ -21,9 +24,9 @@
 //     the slots into its residual rows, applies RMSNorm and writes the e4m3 +
 //     MX scales of its shard for the next AG -> GEMM, then raises its flag.
 //
-// TMA loads here read only this GPU's memory, each CTA its own tiles; peer
-// memory is read by ld.global / written by st.global in the gather warps and
-// the RS epilogue. Every wait on a peer has a clock budget and sets an error
+// TMA tensor loads here read only this GPU's memory, each CTA its own tiles;
+// peer memory is read by the gather thread's bulk copies (never with
+// .multicast::cluster) and written by st.global in the RS epilogue. Every wait on a peer has a clock budget and sets an error
 // code instead of hanging.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>

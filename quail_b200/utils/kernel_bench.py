@@ -143,8 +143,56 @@ def run_attention(model: str, tokens: int, iters: int = 10) -> dict:
     ms_tc = _timeit(lambda: ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list,
                                                      ref.softmax_scale(128)), iters, flush=flush)
     assert ops.read_and_clear_error(0) == 0
-    return {"case": "prefill_attention", "tokens": chunk.num_tokens, "mma_sync_ms": ms,
-            "mma_sync_useful_tflops": flops / ms / 1e9, "tcgen05_ms": ms_tc, "tcgen05_useful_tflops": flops / ms_tc / 1e9}
+    row = {"case": "prefill_attention", "tokens": chunk.num_tokens, "mma_sync_ms": ms,
+           "mma_sync_useful_tflops": flops / ms / 1e9, "tcgen05_ms": ms_tc,
+           "tcgen05_useful_tflops": flops / ms_tc / 1e9}
+    row.update(_fa4_bar(cfg, chunk, q, kc, vc, flops, iters, flush))
+    return row
+
+
+def _fa4_bar(cfg, chunk, q, kc, vc, flops, iters, flush) -> dict:
+    """The library bar on the same shapes: FA4 (CuTe DSL, sm100) as the reference calls it on B200.
+
+    Each packed row is one varlen sequence whose keys are the 48 shared prefix
+    tokens followed by its own tokens, contiguous (the prefix copied in front
+    of every row); queries are the row's own tokens, causal with the
+    bottom-right alignment, so the work equals the paged kernel's.
+    """
+    try:
+        from vllm.vllm_flash_attn import flash_attn_varlen_func
+    except Exception as exc:  # noqa: BLE001
+        return {"fa4_error": f"import: {str(exc)[:160]}"}
+    seqs = chunk.seqs.cpu().tolist()
+    P = kc.shape[1]
+    pl = chunk.page_list.cpu()
+    kk, vv, cuq, cuk = [], [], [0], [0]
+    for sd in seqs:
+        q_len, nseg = sd[1], sd[2]
+        ks, vs = [], []
+        for i in range(nseg):
+            ln, off = sd[4 + i], sd[8 + i]
+            pages = pl[off: off + (ln + P - 1) // P].to(kc.device)
+            ks.append(kc[pages].reshape(-1, kc.shape[2], kc.shape[3])[:ln])
+            vs.append(vc[pages].reshape(-1, vc.shape[2], vc.shape[3])[:ln])
+        k1, v1 = torch.cat(ks), torch.cat(vs)
+        kk.append(k1)
+        vv.append(v1)
+        cuq.append(cuq[-1] + q_len)
+        cuk.append(cuk[-1] + k1.shape[0])
+    k_all, v_all = torch.cat(kk).contiguous(), torch.cat(vv).contiguous()
+    cu_q = torch.tensor(cuq, dtype=torch.int32, device=q.device)
+    cu_k = torch.tensor(cuk, dtype=torch.int32, device=q.device)
+    max_q = max(b - a for a, b in zip(cuq, cuq[1:]))
+    max_k = max(b - a for a, b in zip(cuk, cuk[1:]))
+    qq = q[: cuq[-1]].contiguous()
+    from quail_b200.ops import reference as ref
+    try:
+        fn = lambda: flash_attn_varlen_func(qq, k_all, v_all, max_q, cu_q, max_k, cu_seqlens_k=cu_k,  # noqa: E731
+                                            softmax_scale=ref.softmax_scale(128), causal=True, fa_version=4)
+        ms = _timeit(fn, iters, flush=flush)
+    except Exception as exc:  # noqa: BLE001
+        return {"fa4_error": f"call: {str(exc)[:200]}"}
+    return {"fa4_ms": ms, "fa4_useful_tflops": flops / ms / 1e9}
 
 
 def main():

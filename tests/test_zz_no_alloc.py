@@ -17,6 +17,7 @@ import pytest
 import torch
 
 from quail_b200 import ops
+from quail_b200.ops.quant import dequantize_act, dequantize_weight
 
 pytestmark = pytest.mark.gpu
 
@@ -66,6 +67,18 @@ def test_noalloc_gemm_matches_the_torch_entry_point_on_two_calls():
         rc, st = _call(fn, a8, sa.t().contiguous(), b8, sb, out)
         assert rc == 0 and st == 0, (rc, st)
         assert _rel(out, want) < 5e-3
+        # and directly against the fp32 product of the dequantized operands
+        a32 = dequantize_act(a8, sa)
+        b32 = dequantize_weight(b8, sb)
+        assert _rel(out, a32 @ b32.t()) < 1e-2
+
+
+def test_noalloc_gemm_with_no_rows_reports_its_status():
+    fn = _lib()
+    a8, sa, b8, sb = _case(128, 256, 256, 2)
+    out = torch.empty(8, 256, device="cuda", dtype=torch.bfloat16)[:0]   # a real (non-null) pointer
+    rc, st = _call(fn, a8[:0], sa.t().contiguous()[:0], b8, sb, out)
+    assert rc == 0 and st == 0
 
 
 def test_noalloc_gemm_rejects_a_call_beyond_its_scratch():
