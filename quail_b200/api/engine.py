@@ -41,6 +41,10 @@ class CallSpec:
     pooling: str = "last"     # features: "last" or "max"
     segments: list | None = None   # tail tokenized piece by piece (decision prompts); joins to `tail`
     read: list = field(default_factory=list)   # segments whose last token the decision head reads
+    drops: bool = True        # filter: FALSE drops the row from the region (WHERE); else a value only
+    # demand guard (quail_b200.sql.guards): the call is asked on an input row only where
+    # this formula is TRUE; its `ai` leaves name earlier calls of the same list
+    guard: dict | None = None
 
 
 @dataclass
@@ -169,14 +173,19 @@ class ModelEngine:
 
     def run_region(self, preamble: str, docs: list, calls: list[CallSpec]) -> RegionOutput:
         from quail_b200.engine.region import Call, RegionRun
+        from quail_b200.sql import guards as G
         tok = self.tokenizer
-        # one read per distinct document
-        keys, uniq, where = {}, [], []
-        for t in self.tokenize_docs(docs):
+        # one read per distinct document (and, with guards, per distinct guard inputs)
+        guarded = [c.guard for c in calls if c.guard is not None]
+        keys, uniq, where, rep = {}, [], [], []
+        for i, t in enumerate(self.tokenize_docs(docs)):
             k = t.tobytes()
+            if guarded:
+                k = (k, tuple(G.signature(g, i) for g in guarded))
             if k not in keys:
                 keys[k] = len(uniq)
                 uniq.append(t)
+                rep.append(i)
             where.append(keys[k])
         if self.cfg.role == "reranker":
             # a Qwen3 reranker answers "yes" or "no" (lowering.rs:549-551)
@@ -224,7 +233,12 @@ class ModelEngine:
                 suffix = tok.encode(c.tail)
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
-                      offsets=offsets, copy=c.kind == "extract")
+                      offsets=offsets, copy=c.kind == "extract", drops=c.drops)
+            if c.guard is not None:
+                deps = G.calls_of(c.guard)
+                rc.after = tuple(j for j, o in enumerate(calls) if o.name in deps)
+                rc.when = (lambda r, vals, g=c.guard:
+                           G.asks(g, rep[r], self._sql_values(calls, vals, G.calls_of(g))))
             if offsets:
                 pass
             elif c.kind in ("filter", "score"):
@@ -270,6 +284,19 @@ class ModelEngine:
         stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
                  "documents": len(uniq), "rows": len(docs), "asked": run.asked}
         return RegionOutput(values=values, stats=stats)
+
+    def _sql_values(self, calls: list[CallSpec], raw: dict, names) -> dict:
+        """The SQL values of a row's answers so far (labels, decoded text), for guard tests."""
+        out = {}
+        for c in calls:
+            if c.name in names and c.name in raw:
+                v = raw[c.name]
+                if c.kind == "classify":
+                    v = c.labels[v]
+                elif c.kind in ("map", "extract"):
+                    v = self.tokenizer.decode(v)
+                out[c.name] = v
+        return out
 
     def close(self):
         self.executor = None

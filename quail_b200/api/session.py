@@ -85,8 +85,31 @@ class Query:
         return t if limit is None else t.slice(0, limit)
 
     def execute_stream(self, batch_rows: int = 65_536, limit: int | None = None):
-        t = self.collect(limit)
-        return pa.RecordBatchReader.from_batches(t.schema, t.to_batches(max_chunksize=batch_rows))
+        """The rows as a RecordBatchReader that yields each slice's rows once its region finished.
+
+        A query that can run slice by slice (no aggregate, DISTINCT, or ORDER BY on a
+        model answer) sends its first rows to the model in a small slice and
+        doubles the slice each time, so rows arrive while later ones are asked; a
+        limit stops asking once enough rows came through. Other queries return
+        their rows when the whole query finished (reference: crates/quail/src/lib.rs:376).
+        """
+        from quail_b200.sql.executor import Executor
+        if batch_rows < 1:
+            raise ValueError(f"batch_rows={batch_rows}: at least one row per batch")
+        if limit is not None and limit < 0:
+            raise ValueError(f"limit={limit}: a row limit cannot be negative")
+        s = self.session
+        engine = s.engine() if s._needs_model(self.tree) else None
+        ex = Executor(s.catalog, engine, settings=s.settings)
+        parts = ex.stream(self.tree, batch_rows, limit)
+        first = next(parts)
+
+        def batches():
+            yield from first.to_batches(max_chunksize=batch_rows)
+            for part in parts:
+                yield from part.cast(first.schema).to_batches(max_chunksize=batch_rows)
+
+        return pa.RecordBatchReader.from_batches(first.schema, batches())
 
     def submit(self, **options):
         raise RuntimeError("submit() sends a query to a Quail server; this session has no endpoint")

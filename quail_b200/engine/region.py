@@ -84,6 +84,13 @@ class Call:
     # extract: every generated token continues a verbatim copy of the row's document
     # (the readout carries the best few tokens; the best one the copy allows wins)
     copy: bool = False
+    # filter: a FALSE answer drops the row, so no later call is asked (a WHERE
+    # conjunct); False keeps the row and only records the value (a projection)
+    drops: bool = True
+    # demand guard: when(row, answers so far) decides whether the call is asked on
+    # the row at all (None: always); `after` lists the earlier calls it reads
+    when: object = None
+    after: tuple = ()
 
 
 @dataclass
@@ -120,7 +127,8 @@ class RegionRun:
         doc_len = len(self.docs[r])
         if ci == 0:
             return ("doc", r), [(PREFIX_KEY, P)], P, doc_len + len(self.calls[0].suffix)
-        return ("q", r, ci), [(PREFIX_KEY, P), (("doc", r), doc_len)], P + doc_len, len(self.calls[ci].suffix)
+        reads = [(PREFIX_KEY, P), (("doc", r), doc_len)] if doc_len else [(PREFIX_KEY, P)]
+        return ("q", r, ci), reads, P + doc_len, len(self.calls[ci].suffix)
 
     def _full_cols(self, row):
         na = self.nans if self.nans is not None else len(row) - 2
@@ -141,7 +149,7 @@ class RegionRun:
         if call.kind == "filter":
             keep = bool(scores[1] > scores[0])
             res.values[call.name] = keep
-            if not keep:
+            if not keep and call.drops:
                 res.kept = False
         elif call.kind == "score":
             res.values[call.name] = 1.0 / (1.0 + math.exp(-(float(scores[1]) - float(scores[0]))))
@@ -162,7 +170,7 @@ class RegionRun:
         if call.kind == "filter":
             keep = self._margin(call, row) > 0
             res.values[call.name] = bool(keep)
-            if not keep:
+            if not keep and call.drops:
                 res.kept = False
             self._finish_call(r, ci)
         elif call.kind == "score":
@@ -317,25 +325,41 @@ class RegionRun:
         if self._pending[r] == 0:
             self._advance(r)
 
+    @staticmethod
+    def _barrier(call: Call) -> bool:
+        return call.kind == "filter" and call.drops
+
+    def _asks(self, r: int, ci: int) -> bool:
+        when = self.calls[ci].when
+        return when is None or bool(when(r, self.results[r].values))
+
     def _advance(self, r: int) -> None:
         res = self.results[r]
-        ci = self._next[r]
-        if not res.kept or ci >= len(self.calls):
-            self.ex.free(("doc", r))
-            if self.progress is not None:
-                self.progress.advance()
+        while True:
+            ci = self._next[r]
+            if not res.kept or ci >= len(self.calls):
+                if self.ex.pool.resident(("doc", r)):
+                    self.ex.free(("doc", r))
+                if self.progress is not None:
+                    self.progress.advance()
+                return
+            # a dropping filter runs alone; other calls up to the next one run side by
+            # side, except a call whose guard reads an answer of the same batch
+            batch = [ci]
+            if not self._barrier(self.calls[ci]):
+                j = ci + 1
+                while (j < len(self.calls) and not self._barrier(self.calls[j])
+                       and not set(self.calls[j].after) & set(batch)):
+                    batch.append(j)
+                    j += 1
+            self._next[r] = batch[-1] + 1
+            ask = [c for c in batch if self._asks(r, c)]
+            if not ask:
+                continue
+            self._pending[r] = len(ask)
+            for c in ask:
+                self._submit_question(r, c)
             return
-        # a filter runs alone; non-filter calls up to the next filter run side by side
-        batch = [ci]
-        if self.calls[ci].kind != "filter":
-            j = ci + 1
-            while j < len(self.calls) and self.calls[j].kind != "filter":
-                batch.append(j)
-                j += 1
-        self._next[r] = batch[-1] + 1
-        self._pending[r] = len(batch)
-        for c in batch:
-            self._submit_question(r, c)
 
     @staticmethod
     def _pooled_rows(call: Call, n: int):
@@ -368,6 +392,19 @@ class RegionRun:
         self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
         first = self.calls[0]
         for r, doc in enumerate(self.docs):
+            if not self._asks(r, 0):
+                # the first call is not asked on this row: its document alone, then the rest
+                self._next[r] = 1
+                self._pending[r] = 1
+                if len(doc) == 0:
+                    self._pending[r] = 0
+                    self._advance(r)
+                    continue
+                self.fresh_tokens += len(doc)
+                self.ex.submit(Task(np_rows=True, key=("doc", r), tokens=doc, pos_start=P,
+                                    reads=[(PREFIX_KEY, P)], free_after=False,
+                                    on_done=lambda t, row, r=r: self._doc_only(r)))
+                continue
             toks = np.concatenate([doc, first.suffix])
             self.fresh_tokens += len(toks)
             self._next[r] = 1
@@ -377,6 +414,10 @@ class RegionRun:
                                 topk=first.copy,
                                 readout_rows=self._pooled_rows(first, len(toks)),
                                 on_done=lambda t, row, r=r: self._answered(r, 0, row), free_after=False))
+
+    def _doc_only(self, r: int) -> None:
+        self._pending[r] = 0
+        self._advance(r)
 
     def run(self):
         self.submit_all()

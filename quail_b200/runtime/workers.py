@@ -217,13 +217,19 @@ class WorkerPool:
         shards = [[] for _ in range(self.n)]
         for i, d in enumerate(docs):
             shards[shard_of(d, self.n)].append(i)
+        from quail_b200.sql import guards as G
         paths, msgs = [], []
         for w in range(self.n):
             t = docs_table([docs[i] for i in shards[w]])
             name = f"qb-{os.getpid()}-{self._region}-{w}"
             path = _native.shm_write(name, table_bytes(t))
             paths.append(path)
-            msgs.append({"region": {"preamble": preamble, "path": path, "calls": [asdict(c) for c in calls]}})
+            shard_calls = []
+            for c in calls:
+                d = asdict(c)
+                d["guard"] = G.take(c.guard, shards[w])   # per-row guard inputs of this shard's rows
+                shard_calls.append(d)
+            msgs.append({"region": {"preamble": preamble, "path": path, "calls": shard_calls}})
         try:
             replies = self._all(None, msgs)
         finally:

@@ -16,9 +16,20 @@ limits). AI calls are the reference's logical rules in small
   evaluated once per row, and identical documents once per table
   (`ModelEngine.run_region` deduplicates).
 
-A call inside an expression the rules cannot split (an OR of AI calls, a
-CASE) is evaluated on every row that reaches that operator, then the
-expression is computed from its values.
+- demand (`quail_b200.sql.guards`): a call under a CASE branch, the right
+  side of AND / OR, IFF or COALESCE is asked only on the rows whose guard
+  holds (CASE guards and OR guards, crates/quail-datafusion/src/rules/
+  guards.rs, or_guards.rs); all of one document's calls share a region,
+  the guarded ones after the calls their guards read;
+- fetch (rules/derive/fetch.rs): with LIMIT (and no ORDER BY, or one on
+  plain columns, which is applied first) the rows go to the model in
+  slices, and no further slice is asked once LIMIT rows came through;
+- streaming (crates/quail/src/lib.rs:376 sql_stream): `Executor.stream`
+  yields each slice's rows as its region finishes.
+
+`SET quail.pushdown = false` turns demand and fetch off: every call is then
+asked on every row that reaches its operator (the transcript tests compare
+both ways: same rows, fewer questions with the rules on).
 """
 
 from __future__ import annotations
@@ -189,6 +200,8 @@ class BoundCall:
     descriptions: list = field(default_factory=list)  # classify: per-label descriptions
     segments: list | None = None                     # decision prompts: the tail's segments
     read: list = field(default_factory=list)         # decision prompts: segments the head reads
+    drops: bool = True                               # filter: FALSE drops the row (WHERE chains)
+    guard: dict | None = None                        # demand guard (quail_b200.sql.guards)
 
 
 def _options(node) -> dict:
@@ -369,6 +382,8 @@ class Executor:
         self.ctes: dict = {}
         self.report = {"regions": [], "asked": 0, "fresh_tokens": 0, "passes": 0, "evaluated_documents": 0}
         self.ai_values: dict = {}   # (call key) -> Arrow array aligned with the relation being evaluated
+        flag = self.settings.get("quail.pushdown", self.settings.get("pushdown", True))
+        self.pushdown = str(flag).lower() not in ("false", "off", "0", "no")
 
     # ------------------------------------------------------------ entry
     def run(self, tree: dict) -> pa.Table:
@@ -489,6 +504,10 @@ class Executor:
         ai = [c for c in conjuncts(where) if has_model_call(c)]
         for c in plain:
             rel = rel.filter(_as_mask(self.eval(c, rel)))
+        return self.apply_ai_conjuncts(rel, ai)
+
+    def apply_ai_conjuncts(self, rel: Relation, ai: list) -> Relation:
+        """WHERE conjuncts holding model calls, on the rows the plain conjuncts kept."""
         if not ai:
             return rel
         # AI.IF conjuncts: a guarded chain; others evaluated on the survivors
@@ -533,59 +552,107 @@ class Executor:
         return rel.filter(pa.array(keep))
 
     def compute_ai(self, rel: Relation, exprs: list) -> None:
-        """Evaluate every model call inside `exprs` on all rows of `rel` (merged per prompt)."""
-        calls = {}
+        """Evaluate the model calls inside `exprs` on `rel`, each on the rows its guard asks for.
+
+        Calls reading the same document under the same instruction share a
+        region. A guarded call comes after the calls its guard reads: in the
+        same region (the guard is tested per row between the questions) or,
+        for a call of another region, once that region's answers are in.
+        """
+        from quail_b200.sql import guards as G
+        demand = G.Demand(self, rel, enabled=self.pushdown)
         for e in exprs:
-            for n in walk(e):
-                if is_model_call(n):
-                    k = node_key(n)
-                    if k not in calls and k not in self.ai_values:
-                        calls[k] = bind_call(n, self.turn, self.model)
-        if not calls:
+            demand.visit(e)
+        todo = {k: v for k, v in demand.guards.items() if k not in self.ai_values}
+        if not todo:
             return
-        groups = {}
-        for c in calls.values():
-            groups.setdefault((c.preamble, node_key(c.doc_expr)), []).append(c)
-        for (_, _), cs in groups.items():
-            docs = _to_pylist(self.eval(cs[0].doc_expr, rel)) if rel.num_rows else []
-            expanded = []
-            for c in cs:
-                if c.kind == "extract":
-                    for qi, q in enumerate(c.questions):
-                        bp = P.bind_extract_prompt(q, self.turn)
-                        expanded.append(BoundCall(key=f"{c.key}#{qi}", kind="extract", preamble=bp.preamble,
-                                                  tail=bp.tail, doc_expr=c.doc_expr, max_tokens=c.max_tokens))
-                else:
-                    expanded.append(c)
-            vals = self._engine_region(cs[0].preamble, docs, expanded) if docs else []
-            for c in cs:
-                if c.kind == "extract":
-                    out = []
-                    for r, v in enumerate(vals):
-                        answers = [_clean_phrase(v.get(f"{c.key}#{qi}")) for qi in range(len(c.questions))]
-                        if c.span:
-                            doc = "" if docs[r] is None else str(docs[r])
-                            answers = [_span(doc, a) for a in answers]
-                        out.append(answers)
-                    self.ai_values[c.key] = pa.array(out)
-                elif c.kind == "classify" and c.probabilities:
-                    self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], pa.string())
-                    self.ai_values[c.key + "#probs"] = pa.array([v.get(c.key + "#probs") for v in vals])
-                elif c.kind == "features":
-                    self.ai_values[c.key] = pa.array(
-                        [None if v.get(c.key) is None else [{"feature": f, "strength": x} for f, x in v[c.key]]
-                         for v in vals], FEATURE_LIST)
-                else:
-                    typ = {"filter": pa.bool_(), "score": pa.float64(), "classify": pa.string(),
-                           "map": pa.string()}[c.kind]
-                    self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], typ)
+        bound = {}
+        for k, (node, guard) in todo.items():
+            b = bind_call(node, self.turn, self.model)
+            b.drops = False
+            b.guard = None if guard["op"] == "true" else guard
+            bound[k] = b
+        n = rel.num_rows
+        remaining = list(bound)
+        while remaining:
+            groups: dict = {}
+            for k in remaining:
+                b = bound[k]
+                groups.setdefault((b.preamble, node_key(b.doc_expr)), []).append(k)
+            ran = False
+            for keys in groups.values():
+                deps = set().union(*(G.calls_of(bound[k].guard) for k in keys))
+                if (deps - set(keys)) & set(remaining):
+                    continue          # a guard reads a call another region still has to answer
+                known = {d: _to_pylist(self.ai_values[d]) for d in deps - set(keys) if d in self.ai_values}
+                for k in keys:
+                    bound[k].guard = G.fold(bound[k].guard, known, n)
+                self._run_group(rel, _in_dependency_order(keys, bound))
+                remaining = [k for k in remaining if k not in keys]
+                ran = True
+            if not ran:
+                # guards that read each other across regions: ask those calls everywhere
+                for k in remaining:
+                    bound[k].guard = None
+
+    def _run_group(self, rel: Relation, cs: list[BoundCall]) -> None:
+        """One region: the calls `cs` (dependency order) over the rows any of them may be asked on."""
+        from quail_b200.sql import guards as G
+        n = rel.num_rows
+        rows = [r for r in range(n) if any(c.guard is None or G.may_ask(c.guard, r) for c in cs)]
+        docs_all = _to_pylist(self.eval(cs[0].doc_expr, rel)) if n else []
+        if not isinstance(docs_all, list):
+            docs_all = [docs_all] * n
+        docs = [docs_all[r] for r in rows]
+        expanded = []
+        for c in cs:
+            guard = None if c.guard is None else G.take(c.guard, rows)
+            if c.kind == "extract":
+                for qi, q in enumerate(c.questions):
+                    bp = P.bind_extract_prompt(q, self.turn)
+                    expanded.append(BoundCall(key=f"{c.key}#{qi}", kind="extract", preamble=bp.preamble,
+                                              tail=bp.tail, doc_expr=c.doc_expr, max_tokens=c.max_tokens,
+                                              drops=False, guard=guard))
+            else:
+                expanded.append(BoundCall(**{**c.__dict__, "guard": guard}))
+        got = self._engine_region(cs[0].preamble, docs, expanded) if docs else []
+        vals = [{} for _ in range(n)]
+        for j, r in enumerate(rows):
+            vals[r] = got[j]
+        for c in cs:
+            if c.kind == "extract":
+                out = []
+                for r, v in enumerate(vals):
+                    if f"{c.key}#0" not in v:
+                        out.append(None)
+                        continue
+                    answers = [_clean_phrase(v.get(f"{c.key}#{qi}")) for qi in range(len(c.questions))]
+                    if c.span:
+                        doc = "" if docs_all[r] is None else str(docs_all[r])
+                        answers = [_span(doc, a) for a in answers]
+                    out.append(answers)
+                self.ai_values[c.key] = pa.array(out, pa.list_(pa.struct([("start", pa.int64()), ("end", pa.int64())]))
+                                                 if c.span else pa.list_(pa.string()))
+            elif c.kind == "classify" and c.probabilities:
+                self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], pa.string())
+                self.ai_values[c.key + "#probs"] = pa.array([v.get(c.key + "#probs") for v in vals],
+                                                            pa.list_(pa.float64()))
+            elif c.kind == "features":
+                self.ai_values[c.key] = pa.array(
+                    [None if v.get(c.key) is None else [{"feature": f, "strength": x} for f, x in v[c.key]]
+                     for v in vals], FEATURE_LIST)
+            else:
+                typ = {"filter": pa.bool_(), "score": pa.float64(), "classify": pa.string(),
+                       "map": pa.string()}[c.kind]
+                self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], typ)
 
     def _engine_region(self, preamble: str, docs: list, calls: list[BoundCall]) -> list[dict]:
         if self.engine is None:
             raise QueryError("this query needs a model; the session has none")
         from quail_b200.api.engine import CallSpec
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
-                          probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read)
+                          probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read,
+                          drops=c.drops, guard=c.guard)
                  for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self.report["regions"].append(out.stats)
@@ -596,6 +663,143 @@ class Executor:
 
     # ------------------------------------------------------------ SELECT
     def select(self, node) -> pa.Table:
+        plan = self._slice_plan(node)
+        if plan is not None:
+            parts = list(self.select_slices(node, plan))
+            return pa.concat_tables(parts) if len(parts) > 1 else parts[0]
+        return self._select_whole(node)
+
+    # ------------------------------------------------------------ fetch demand and streaming
+    def _slice_plan(self, node):
+        """How a SELECT can run slice by slice, or None when it needs all its rows at once.
+
+        It can when it has no aggregate, GROUP BY, HAVING or DISTINCT, and its
+        ORDER BY keys (if any) read no model call: the rows are then sorted
+        before any model call, so each slice's output is final.
+        """
+        if "from" not in node or node.get("distinct") or node.get("having") or node.get("group_by"):
+            return None
+        items = node["items"]
+        if any(is_aggregate(n) for it in items for n in walk(it["expr"])):
+            return None
+        order = []
+        for o in node.get("order_by", []):
+            e = o["expr"]
+            if e.get("type") == "literal" and e.get("kind") == "int":
+                e = items[int(e["value"]) - 1]["expr"]
+            elif e.get("type") == "column" and e.get("table") is None:
+                for it in items:
+                    if (it.get("alias") or "").lower() == e["name"].lower():
+                        e = it["expr"]
+                        break
+            if e.get("type") == "star" or has_model_call(e):
+                return None
+            order.append((e, o["desc"]))
+        off = int(literal_value(node["offset"])) if node.get("offset") else 0
+        lim = int(literal_value(node["limit"])) if node.get("limit") is not None else None
+        return {"order": order, "offset": off, "limit": lim}
+
+    def _filter_selectivity(self, ai: list) -> float:
+        est = 1.0
+        for c in ai:
+            inner = c["args"][0] if c.get("type") == "call" and c["name"] == "HINT" else c
+            sel = None
+            if is_model_call(inner) and inner["name"] in ("AI.IF", "AI_FILTER"):
+                sel = bind_call(inner, self.turn, self.model).selectivity
+            est *= 0.5 if sel is None else max(float(sel), 0.01)
+        return est
+
+    def select_slices(self, node, plan: dict, *, stream_rows: int | None = None, extra_limit: int | None = None):
+        """Run a sliceable SELECT; yield its output a slice of input rows at a time.
+
+        With a LIMIT (or `extra_limit`) and demand rules on, rows go to the
+        model in slices sized from the pass rate seen so far, and no slice is
+        asked once enough rows came through (the fetch demand). With
+        `stream_rows`, slices start at that many rows and double, so the first
+        rows come back early. Otherwise one slice holds every row.
+        """
+        rel = self.from_clause(node)
+        where = node.get("where")
+        plain = [c for c in conjuncts(where) if not has_model_call(c)]
+        ai = [c for c in conjuncts(where) if has_model_call(c)]
+        for c in plain:
+            rel = rel.filter(_as_mask(self.eval(c, rel)))
+        if plan["order"]:
+            tmp = rel.table
+            keys = []
+            for k, (e, desc) in enumerate(plan["order"]):
+                tmp = tmp.append_column(f"__order{k}", _as_array(self.eval(e, rel), rel.num_rows))
+                keys.append((f"__order{k}", "descending" if desc else "ascending"))
+            rel = rel.take(pc.sort_indices(tmp, sort_keys=keys, null_placement="at_end"))
+        off, lim = plan["offset"], plan["limit"]
+        if extra_limit is not None:
+            lim = extra_limit if lim is None else min(lim, extra_limit)
+        need = None if lim is None else off + lim
+        n = rel.num_rows
+        fetch = self.pushdown and need is not None and bool(ai) or stream_rows is not None
+        sel = self._filter_selectivity(ai)
+        start = emitted = tried = passed = 0
+        first = True
+        size_hint = stream_rows
+        while first or (start < n and (need is None or emitted < need)):
+            size = n - start
+            if fetch and need is not None and self.pushdown and ai:
+                rate = (passed + 1) / (tried + 2) if tried else sel
+                size = min(size, max(32, int(-(-(need - emitted) * 1.25 // max(rate, 0.02)))))
+            if stream_rows is not None:
+                size = min(size, size_hint)
+                size_hint *= 2
+            part = rel.take(pa.array(np.arange(start, start + size, dtype=np.int64))) if size < n else rel
+            start += size
+            kept = self.apply_ai_conjuncts(part, ai)
+            tried += part.num_rows
+            passed += kept.num_rows
+            out = self._project(kept, node)
+            lo, hi = emitted, emitted + out.num_rows
+            emitted = hi
+            a = max(off - lo, 0)
+            b = out.num_rows if need is None else max(min(need - lo, out.num_rows), 0)
+            if first or b > a:
+                yield out.slice(a, max(b - a, 0))
+            first = False
+            if need is not None and emitted >= need:
+                break
+
+    def _project(self, rel: Relation, node) -> pa.Table:
+        """The SELECT list of a non-aggregating query over `rel` (its model calls asked on demand)."""
+        items = node["items"]
+        self.ai_values = {}
+        self.compute_ai(rel, [it["expr"] for it in items])
+        names, arrays = [], []
+        for it in items:
+            e = it["expr"]
+            if e.get("type") == "star":
+                for i, (q, n) in enumerate(rel.cols):
+                    if e.get("table") is None or (q or "").lower() == e["table"].lower():
+                        if n.startswith("__"):
+                            continue
+                        names.append(n)
+                        arrays.append(rel.column(i))
+                continue
+            names.append(it.get("alias") or expr_name(e))
+            arrays.append(_as_array(self.eval(e, rel), rel.num_rows))
+        self.ai_values = {}
+        return pa.Table.from_arrays(arrays, names=_dedupe(names))
+
+    def stream(self, tree: dict, batch_rows: int = 65_536, limit: int | None = None):
+        """Yield the query's rows as tables, each slice's as soon as its region finishes.
+
+        The first table may be empty; it always comes, so the caller has the schema.
+        """
+        node = tree
+        plan = self._slice_plan(node) if node.get("type") == "select" and not node.get("with") else None
+        if plan is None:
+            out = self.run(tree)
+            yield out if limit is None else out.slice(0, limit)
+            return
+        yield from self.select_slices(node, plan, stream_rows=min(batch_rows, 1024), extra_limit=limit)
+
+    def _select_whole(self, node) -> pa.Table:
         rel = self.from_clause(node)
         if node.get("where"):
             rel = self.apply_where(rel, node["where"])
@@ -892,6 +1096,23 @@ class Executor:
 
 
 # ---------------------------------------------------------------- small helpers
+
+def _in_dependency_order(keys: list, bound: dict) -> list:
+    """The calls of one region, each after the calls its guard reads (otherwise as found)."""
+    from quail_b200.sql import guards as G
+    out, placed = [], set()
+    pending = list(keys)
+    while pending:
+        for k in pending:
+            if G.calls_of(bound[k].guard) & set(pending) - {k} <= placed:
+                break
+        else:
+            k = pending[0]            # a cycle cannot come from the rules; keep the order found
+        out.append(bound[k])
+        placed.add(k)
+        pending.remove(k)
+    return out
+
 
 def _as_array(v, n):
     if isinstance(v, pa.Scalar):

@@ -194,3 +194,47 @@ def test_parallel_refusals():
         check_config(EngineConfig(model="qwen3-moe-gpu-tiny", device="cpu", parallel="ep", gpus=2))
     with _pytest.raises(RefusalError, match="parallel is"):
         check_config(EngineConfig(model="qwen3-tiny", device="cpu", parallel="pp"))
+
+
+def _both_ways(session, q):
+    on = session.sql(q).run()
+    session.settings["quail.pushdown"] = "false"
+    try:
+        off = session.sql(q).run()
+    finally:
+        session.settings.pop("quail.pushdown")
+    return on, off
+
+
+def test_case_guard_on_the_model_asks_only_where_the_filter_holds(session):
+    f = "AI.IF(PROMPT('Does the review discuss the ending? {0}', body))"
+    sc = "AI.SCORE(PROMPT('Is the review positive? {0}', body))"
+    q = f"SELECT id, {f} AS f, CASE WHEN {f} THEN {sc} END AS s FROM reviews ORDER BY id"
+    on, off = _both_ways(session, q)
+    assert on.table.column("f").to_pylist() == off.table.column("f").to_pylist()
+    for keep, a, b in zip(on.table.column("f").to_pylist(), on.table.column("s").to_pylist(),
+                          off.table.column("s").to_pylist()):
+        if keep:
+            assert abs(a - b) < 1e-4
+        else:
+            assert a is None and b is None
+    assert on.report["asked"] < off.report["asked"]
+
+
+def test_a_first_call_left_out_on_a_row_still_reads_the_document(session):
+    # the guarded call comes first in the region: rows it skips prefill the document alone,
+    # then the unguarded call reads it as a follow-up question
+    s1 = "AI.SCORE(PROMPT('Is the review positive? {0}', body))"
+    s2 = "AI.SCORE(PROMPT('Is the review about money? {0}', body))"
+    q = f"SELECT id, CASE WHEN grp = 1 THEN {s1} END AS a, {s2} AS b FROM reviews ORDER BY id"
+    on, off = _both_ways(session, q)
+    ta, tb = on.table, off.table
+    for g, a_on, a_off, b_on, b_off in zip(ta.column("id").to_pylist(), ta.column("a").to_pylist(),
+                                           tb.column("a").to_pylist(), ta.column("b").to_pylist(),
+                                           tb.column("b").to_pylist()):
+        assert abs(b_on - b_off) < 1e-4
+        if g % 3 == 1:
+            assert abs(a_on - a_off) < 1e-4
+        else:
+            assert a_on is None
+    assert on.report["asked"] < off.report["asked"]

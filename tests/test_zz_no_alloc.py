@@ -76,9 +76,14 @@ def test_noalloc_gemm_matches_the_torch_entry_point_on_two_calls():
 def test_noalloc_gemm_with_no_rows_reports_its_status():
     fn = _lib()
     a8, sa, b8, sb = _case(128, 256, 256, 2)
-    out = torch.empty(8, 256, device="cuda", dtype=torch.bfloat16)[:0]   # a real (non-null) pointer
-    rc, st = _call(fn, a8[:0], sa.t().contiguous()[:0], b8, sb, out)
-    assert rc == 0 and st == 0
+    sa_rows = sa.t().contiguous()
+    out = torch.empty(128, 256, device="cuda", dtype=torch.bfloat16)
+    st = ctypes.c_int(-7)
+    # M = 0 with valid pointers: nothing runs, and the status word asked for is still written
+    rc = fn(a8.data_ptr(), a8.stride(0), sa_rows.data_ptr(), b8.data_ptr(), b8.stride(0), sb.data_ptr(),
+            out.data_ptr(), out.stride(0), 0, 256, 256, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+            ctypes.byref(st))
+    assert rc == 0 and st.value == 0
 
 
 def test_noalloc_gemm_rejects_a_call_beyond_its_scratch():
