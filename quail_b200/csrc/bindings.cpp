@@ -24,6 +24,14 @@ void prefill_attention(const torch::Tensor& q, const torch::Tensor& k_cache, con
                        const torch::Tensor& seqs, const torch::Tensor& tiles, const torch::Tensor& page_list,
                        double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_scale);
 
+void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b,
+                      const torch::Tensor& sfb, const torch::Tensor& positions, const torch::Tensor& slots,
+                      const torch::Tensor& qn, const torch::Tensor& kn, const torch::Tensor& cos_sin,
+                      torch::Tensor& q_out, torch::Tensor& k_cache, torch::Tensor& v_cache, int64_t QH, int64_t KH,
+                      double eps, bool norm_qk);
+void prefill_attention_tc2(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
+                           const torch::Tensor& seqs, const torch::Tensor& blocks, const torch::Tensor& page_list,
+                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
 void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
              const c10::optional<torch::Tensor>& residual);
@@ -130,6 +138,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b"), py::arg("sa"), py::arg("sb"), py::arg("sb_gran"), py::arg("epi"), py::arg("out"),
         py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
   m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
+  m.def("prefill_attention_tc2", &qb::prefill_attention_tc2,
+        "persistent tcgen05 prefill attention: TMA loader, MMA warp, two ping-pong softmax warpgroups");
+  m.def("gemm_mx_qkv_rope", &qb::gemm_mx_qkv_rope,
+        "MX fp8 QKV projection with q/k RMSNorm, NeoX RoPE and the paged KV write in the epilogue");
   m.def("gemm_nvfp4", &qb::gemm_nvfp4, "tcgen05 NVFP4 GEMM: E2M1 operands, UE4M3 16-element block scales");
   m.def("nvfp4_quant_rows", &qb::nvfp4_quant_rows, "bf16 rows (or SwiGLU of gate|up) -> NVFP4 + per-row scale");
   m.def("rmsnorm_quant_mx", &qb::rmsnorm_quant_mx);

@@ -8,6 +8,7 @@ enum Epi : int {
   kEpiResidual = 1,    // D = acc + R (bf16; R may alias D)
   kEpiSwigluFp8 = 2,   // Y = e4m3(silu(g) * u), one fp32 scale per 128 outputs
   kEpiSwigluBf16 = 3,  // D = silu(g) * u (bf16)
+  kEpiQkvRope = 4,     // per 128-column head: q/k RMSNorm + NeoX RoPE; q -> q_out, k/v -> paged cache
 };
 
 }  // namespace qb

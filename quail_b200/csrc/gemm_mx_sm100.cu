@@ -44,6 +44,17 @@ struct MxParams {
   const uint8_t* sfb;  // [ceil(N/128)][K/128][512]
   int* err;
   int num_m_tiles, num_n_tiles;
+  // kEpiQkvRope: the columns are QH q heads, KH k heads, KH v heads of 128
+  int QH, KH, norm_qk;
+  float eps;
+  const int* positions;          // [M] rotary position of each token
+  const int* slots;              // [M] arena row of each token (< 0: not stored)
+  const __nv_bfloat16* qn;       // [128] q RMSNorm weight
+  const __nv_bfloat16* kn;       // [128] k RMSNorm weight
+  const float* cos_sin;          // [max_pos, 128]: cos[64] | sin[64]
+  __nv_bfloat16* q_out;          // [M, QH, 128]
+  __nv_bfloat16* k_cache;        // [slots, KH, 128]
+  __nv_bfloat16* v_cache;
 };
 
 template <int EPI>
@@ -202,7 +213,53 @@ __global__ void __launch_bounds__(64 + kMxBN, 1)
       tc_fence_before();
       mbar_arrive(acc_empty);
       if (m >= p.M) continue;
-      if constexpr (EPI == kEpiBf16 || EPI == kEpiResidual) {
+      if constexpr (EPI == kEpiQkvRope) {
+        // this thread's row of one head: per-head RMSNorm and NeoX RoPE of q and k in
+        // fp32, then q to q_out and k / v straight into the token's arena row
+        if (n0 >= p.N) continue;
+        const int hd = n0 >> 7;
+        if (hd < p.QH + p.KH) {
+          if (p.norm_qk) {
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) ss = fmaf(acc[i], acc[i], ss);
+            const float rinv = rsqrtf(ss * (1.f / 128.f) + p.eps);
+            const __nv_bfloat16* wn = hd < p.QH ? p.qn : p.kn;
+#pragma unroll
+            for (int j = 0; j < 128; j += 8) {
+              float w8[8];
+              ld_bf16x8f(wn + j, w8);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[j + i] = acc[j + i] * rinv * w8[i];
+            }
+          }
+          const float* cs = p.cos_sin + (size_t)p.positions[m] * 128;
+#pragma unroll
+          for (int i = 0; i < 64; i += 4) {
+            const float4 c = __ldg(reinterpret_cast<const float4*>(cs + i));
+            const float4 sn = __ldg(reinterpret_cast<const float4*>(cs + 64 + i));
+            const float cc[4] = {c.x, c.y, c.z, c.w}, ss4[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float x = acc[i + k], y = acc[i + 64 + k];
+              acc[i + k] = x * cc[k] - y * ss4[k];
+              acc[i + 64 + k] = y * cc[k] + x * ss4[k];
+            }
+          }
+        }
+        __nv_bfloat16* dst;
+        if (hd < p.QH) {
+          dst = p.q_out + ((size_t)m * p.QH + hd) * 128;
+        } else {
+          const int slot = p.slots[m];
+          if (slot < 0) continue;
+          const bool is_k = hd < p.QH + p.KH;
+          const int kvh = is_k ? hd - p.QH : hd - p.QH - p.KH;
+          dst = (is_k ? p.k_cache : p.v_cache) + ((size_t)slot * p.KH + kvh) * 128;
+        }
+#pragma unroll
+        for (int j = 0; j < 128; j += 8) st_bf16x8(dst + j, &acc[j]);
+      } else if constexpr (EPI == kEpiBf16 || EPI == kEpiResidual) {
         __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + n0;
 #pragma unroll
         for (int j = 0; j < 128; j += 8) {
@@ -337,12 +394,78 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   switch (epi) {
+    case kEpiQkvRope: TORCH_CHECK(false, "gemm_mx: the QKV epilogue is gemm_mx_qkv_rope"); break;
     case kEpiBf16: launch_mx<kEpiBf16>(ta, tb, p, st, dev); break;
     case kEpiResidual: launch_mx<kEpiResidual>(ta, tb, p, st, dev); break;
     case kEpiSwigluFp8: launch_mx<kEpiSwigluFp8>(ta, tb, p, st, dev); break;
     case kEpiSwigluBf16: launch_mx<kEpiSwigluBf16>(ta, tb, p, st, dev); break;
     default: TORCH_CHECK(false, "gemm_mx: unknown epilogue ", epi);
   }
+}
+
+// The QKV projection with K4 fused into its epilogue: x [M, K] e4m3 times
+// wqkv [(QH + 2 KH) * 128, K] e4m3; per head of 128 columns the epilogue
+// applies q / k RMSNorm (norm_qk) and NeoX RoPE at positions[m], writes q to
+// q_out [M, QH, 128] and k / v to row slots[m] of the paged caches
+// [*, KH, 128] (slots < 0 are not stored). Replaces a bf16 qkv round trip
+// through memory and the separate qk_norm_rope_kv launch.
+void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b,
+                      const torch::Tensor& sfb, const torch::Tensor& positions, const torch::Tensor& slots,
+                      const torch::Tensor& qn, const torch::Tensor& kn, const torch::Tensor& cos_sin,
+                      torch::Tensor& q_out, torch::Tensor& k_cache, torch::Tensor& v_cache, int64_t QH, int64_t KH,
+                      double eps, bool norm_qk) {
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "qkv_rope: e4m3");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
+              "qkv_rope: shapes");
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(K % 128 == 0 && N == (QH + 2 * KH) * 128 && N % kMxBN == 0, "qkv_rope: N = (QH + 2 KH) * 128");
+  TORCH_CHECK(sfa.numel() >= (int64_t)((M + 127) / 128) * (K / 128) * 512 &&
+                  sfb.numel() >= (int64_t)((N + 127) / 128) * (K / 128) * 512,
+              "qkv_rope: scale bytes");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt && positions.numel() >= M &&
+                  slots.numel() >= M,
+              "qkv_rope: int32 positions / slots per row");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 128 && cos_sin.is_contiguous(),
+              "qkv_rope: cos_sin [max_pos, 128] fp32");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() >= (int64_t)M * QH * 128 &&
+                  q_out.scalar_type() == at::kBFloat16,
+              "qkv_rope: q_out [M, QH, 128] bf16");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(-1) == 128 &&
+                  k_cache.size(-2) == KH && k_cache.scalar_type() == at::kBFloat16,
+              "qkv_rope: caches [*, KH, 128] bf16");
+  TORCH_CHECK(qn.scalar_type() == at::kBFloat16 && kn.scalar_type() == at::kBFloat16 && qn.numel() == 128 &&
+                  kn.numel() == 128,
+              "qkv_rope: bf16 norm weights of 128");
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  if (M == 0) return;
+  MxParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.sfa = sfa.data_ptr<uint8_t>();
+  p.sfb = sfb.data_ptr<uint8_t>();
+  p.err = device_error_word(dev);
+  p.num_m_tiles = (M + 127) / 128;
+  p.num_n_tiles = N / kMxBN;
+  p.QH = (int)QH;
+  p.KH = (int)KH;
+  p.norm_qk = norm_qk ? 1 : 0;
+  p.eps = (float)eps;
+  p.positions = positions.data_ptr<int>();
+  p.slots = slots.data_ptr<int>();
+  p.qn = reinterpret_cast<const __nv_bfloat16*>(qn.data_ptr());
+  p.kn = reinterpret_cast<const __nv_bfloat16*>(kn.data_ptr());
+  p.cos_sin = cos_sin.data_ptr<float>();
+  p.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a.stride(0), 128, 128,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  launch_mx<kEpiQkvRope>(ta, tb, p, st, dev);
 }
 
 }  // namespace qb

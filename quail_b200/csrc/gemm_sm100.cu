@@ -71,6 +71,25 @@ CUtensorMap make_tmap_2d(const void* ptr, CUtensorMapDataType dtype, int elem_by
   return m;
 }
 
+// 3-D bf16 tensor map, 128-byte swizzle: dims {d0, d1, d2} (d0 contiguous),
+// byte strides of dims 1 and 2, box {box0, box1, box2} (box0 * 2 bytes = 128).
+CUtensorMap make_tmap_3d_bf16(const void* ptr, int64_t d0, int64_t d1, int64_t d2, int64_t stride1_bytes,
+                              int64_t stride2_bytes, int box0, int box1, int box2) {
+  CUtensorMap m;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(stride1_bytes % 16 == 0 && stride2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  TORCH_CHECK(box0 * 2 == 128, "128-byte swizzle: the inner box is 64 bf16");
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)stride1_bytes, (cuuint64_t)stride2_bytes};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, (cuuint32_t)box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed: ", (int)r);
+  return m;
+}
+
 int num_sms(int dev) {
   static int cached[64] = {0};
   if (!cached[dev]) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);

@@ -6,6 +6,8 @@ sequences, plus the metadata the kernels read:
   ids, positions, slots   [T] int32  token id, absolute position, KV slot (page*P + offset; -1 = none)
   seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
   tiles                   [n, 2]     (sequence, first query token) per 32-token prefill-attention tile
+  blocks                  [m, 2]     the same per 64-token block of the persistent attention kernel,
+                                     the blocks reading the most keys first
   dseqs                   [d]        sequences with one new token (decode attention: one CTA per KV head)
   state_io                [S, 2]     hybrid models: state slot each sequence starts from (-1 = zeros), slot it ends in
   page_list               [*]        page ids of every segment, segments point into it
@@ -26,7 +28,8 @@ import torch
 MAX_SEGMENTS = 4
 SEQ_INTS = 12
 # the metadata arrays in upload order
-PARTS = ("ids", "positions", "slots", "seqs", "tiles", "page_list", "final_rows", "dseqs", "state_io")
+PARTS = ("ids", "positions", "slots", "seqs", "tiles", "page_list", "final_rows", "dseqs", "state_io",
+         "blocks")
 ATTN_BLOCK_Q = 32
 
 
@@ -59,6 +62,7 @@ class Chunk:
     readout_tags: list = field(default_factory=list)
     dseqs: torch.Tensor | None = None
     state_io: torch.Tensor | None = None
+    blocks: torch.Tensor | None = None
     num_seqs: int = 0
     host: dict | None = None   # numpy copies (tests, CPU reference)
     upload_bytes: int = 0
@@ -91,7 +95,8 @@ class ChunkPacker:
             o += sz
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
-                     final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2), readout_tags=tags,
+                     final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2),
+                     blocks=views[9].view(-1, 2), readout_tags=tags,
                      num_seqs=len(specs), host=host, upload_bytes=int(flat.nbytes),
                      full_readout=any(s.full and s.readout for s in specs),
                      topk=any(s.topk and s.readout for s in specs))
@@ -113,6 +118,7 @@ class ChunkPacker:
         page_list: list[int] = []
         seg_cache: dict = {}
         tiles: list[int] = []
+        blocks: list[tuple] = []      # (keys read, sequence, first token)
         dseqs: list[int] = []
         final_rows: list[int] = []
         tags: list = []
@@ -161,6 +167,9 @@ class ChunkPacker:
             else:
                 for q0 in range(0, n, ATTN_BLOCK_Q):
                     tiles += (si, q0)
+                before = sum(ln for _, ln in reads)
+                for q0 in range(0, n, 2 * ATTN_BLOCK_Q):
+                    blocks.append((before + j0 + min(n, q0 + 2 * ATTN_BLOCK_Q), si, q0))
             if s.readout:
                 if s.readout_rows is None:
                     final_rows.append(q + n - 1)
@@ -175,7 +184,9 @@ class ChunkPacker:
                 "slots": np.asarray(slots, dtype=i32), "seqs": np.asarray(seqs, dtype=i32).reshape(S, SEQ_INTS),
                 "tiles": np.asarray(tiles, dtype=i32).reshape(-1, 2), "page_list": np.asarray(page_list, dtype=i32),
                 "final_rows": np.asarray(final_rows, dtype=i32), "dseqs": np.asarray(dseqs, dtype=i32),
-                "state_io": sio}
+                "state_io": sio,
+                "blocks": np.asarray([(b[1], b[2]) for b in sorted(blocks, key=lambda b: -b[0])],
+                                     dtype=i32).reshape(-1, 2)}
         return host, tags
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:

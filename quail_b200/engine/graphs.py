@@ -43,7 +43,8 @@ class _Entry:
         self.B = B
         self.pl_cap = pl_cap
         self.sizes = {"ids": B, "positions": B, "slots": B, "seqs": B * SEQ_INTS, "tiles": 0,
-                      "page_list": pl_cap + 1, "final_rows": B, "dseqs": B, "state_io": 2 * B}
+                      "page_list": pl_cap + 1, "final_rows": B, "dseqs": B, "state_io": 2 * B,
+                      "blocks": 0}
         self.total = sum(self.sizes.values())
         self.buf = torch.zeros(self.total, dtype=torch.int32, device=device)
         self.stage = torch.empty(self.total, dtype=torch.int32, pin_memory=True)
@@ -60,7 +61,7 @@ class _Entry:
         return Chunk(num_tokens=self.B, ids=v["ids"], positions=v["positions"], slots=v["slots"],
                      seqs=v["seqs"].view(-1, SEQ_INTS), tiles=v["tiles"].view(-1, 2), page_list=v["page_list"],
                      final_rows=v["final_rows"], dseqs=v["dseqs"], state_io=v["state_io"].view(-1, 2),
-                     num_seqs=self.B, full_readout=full, topk=topk)
+                     blocks=v["blocks"].view(-1, 2), num_seqs=self.B, full_readout=full, topk=topk)
 
     def fill(self, host: dict) -> int:
         """Write a pass's metadata, padded to the bucket, into the staging image; returns its bytes."""
@@ -71,7 +72,7 @@ class _Entry:
             "slots": np.full(B, -1, np.int32), "seqs": np.zeros((B, SEQ_INTS), np.int32),
             "tiles": np.zeros(0, np.int32), "page_list": np.zeros(self.pl_cap + 1, np.int32),
             "final_rows": np.arange(B, dtype=np.int32), "dseqs": np.arange(B, dtype=np.int32),
-            "state_io": np.full((B, 2), -1, np.int32),
+            "state_io": np.full((B, 2), -1, np.int32), "blocks": np.zeros(0, np.int32),
         }
         for k in ("ids", "positions", "slots"):
             img[k][:T] = host[k]

@@ -121,12 +121,14 @@ class Qwen3Pipeline:
             kc, vc = arena.layer(li)
             if fp8:
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln1"], cfg.rms_eps)
-                qkv = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
+                # K1 + K4: QKV GEMM whose epilogue norms, rotates and writes K/V to the arena
+                q = ops.gemm_mx_qkv_rope(x8, xs, L["wqkv"], L["sqkv"], chunk.positions, chunk.slots, L["qn"],
+                                         L["kn"], w.cos_sin, kc, vc, cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
             else:
                 x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
                 qkv = ops.gemm(x, L["wqkv"])
-            q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
-                                    cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
+                q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
+                                        cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
             if fp8 and self.tc_attention:
                 o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
                 ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)

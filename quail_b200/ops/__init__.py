@@ -32,6 +32,8 @@ from quail_b200.ops.kernels import (  # noqa: F401
     native,
     prefill_attention,
     prefill_attention_tc,
+    prefill_attention_tc2,
+    gemm_mx_qkv_rope,
     qk_norm_rope_kv,
     quant_rows,
     read_and_clear_error,

@@ -105,6 +105,20 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     return out
 
 
+def gemm_mx_qkv_rope(x8, xs, wqkv, sqkv, positions, slots, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache,
+                     num_q_heads: int, num_kv_heads: int, eps: float, *, norm_qk: bool = True, q_out=None):
+    """The fp8 QKV projection with per-head q/k RMSNorm, NeoX RoPE and the paged KV write
+    fused into its epilogue (K1 + K4 in one kernel). Returns q [T, QH, 128] bf16."""
+    C = native()
+    T = x8.shape[0]
+    if q_out is None:
+        q_out = torch.empty(T, num_q_heads, 128, dtype=torch.bfloat16, device=x8.device)
+    count_launch()
+    C.gemm_mx_qkv_rope(x8, xs, wqkv, sqkv, positions, slots, q_norm_w, k_norm_w, cos_sin, q_out, k_cache, v_cache,
+                       num_q_heads, num_kv_heads, eps, norm_qk)
+    return q_out
+
+
 def quant_rows_nvfp4(x: torch.Tensor, *, swiglu: bool = False):
     """bf16 rows (or silu(gate) * up of [T, 2K] gate | up) -> (packed E2M1 [T, K/2], UE4M3 block-scale
     atoms, fp32 per-row scale [T]) for gemm_nvfp4's A side."""
@@ -270,6 +284,26 @@ def decode_attention(q, k_cache, v_cache, seqs, dseqs, page_list, softmax_scale:
     native().decode_attention(q, k_cache, v_cache, seqs, dseqs, page_list, softmax_scale, out, out_scale)
 
 
+def prefill_attention_tc2(q, k_cache, v_cache, seqs, blocks, page_list, softmax_scale: float, *,
+                          fp8_out: bool = True, out=None, out_scale=None):
+    """The persistent tcgen05 attention (csrc/attention_tc2.cu) over 64-token query blocks.
+
+    blocks [m, 2] int32: (sequence, first query token) per 64-token block
+    (`ops.reference.attention_tiles(seqs, 64)` or a chunk's `blocks`); pages
+    hold a multiple of 64 tokens. Returns bf16 [T, QH*128], or with fp8_out
+    (e4m3, UE8M0 scale bytes in the MX atom layout).
+    """
+    T, QH = q.shape[0], q.shape[1]
+    if out is None:
+        out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if fp8_out else torch.bfloat16, device=q.device)
+    if fp8_out and out_scale is None:
+        out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+    count_launch()
+    native().prefill_attention_tc2(q, k_cache, v_cache, seqs, blocks, page_list, softmax_scale, out,
+                                   out_scale if fp8_out else None)
+    return (out, out_scale) if fp8_out else out
+
+
 def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: bool, tc: bool,
                     out=None, out_scale=None):
     """Attention of every query row of a packed chunk.
@@ -285,7 +319,11 @@ def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: boo
     if mx and out_scale is None:
         out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
     if chunk.tiles.shape[0] > 0:
-        if tc:
+        blocks = getattr(chunk, "blocks", None)
+        if tc and blocks is not None and k_cache.shape[1] % 64 == 0:
+            prefill_attention_tc2(q, k_cache, v_cache, chunk.seqs, blocks, chunk.page_list, softmax_scale,
+                                  fp8_out=mx, out=out, out_scale=out_scale)
+        elif tc:
             prefill_attention_tc(q, k_cache, v_cache, chunk.seqs, chunk.tiles, chunk.page_list, softmax_scale,
                                  fp8_out=mx, out=out, out_scale=out_scale)
         else:

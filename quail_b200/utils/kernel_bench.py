@@ -142,10 +142,13 @@ def run_attention(model: str, tokens: int, iters: int = 10) -> dict:
                                                ref.softmax_scale(128), fp8_out=True, mx=True), iters, flush=flush)
     ms_tc = _timeit(lambda: ops.prefill_attention_tc(q, kc, vc, chunk.seqs, chunk.tiles, chunk.page_list,
                                                      ref.softmax_scale(128)), iters, flush=flush)
+    ms_p = _timeit(lambda: ops.prefill_attention_tc2(q, kc, vc, chunk.seqs, chunk.blocks, chunk.page_list,
+                                                     ref.softmax_scale(128)), iters, flush=flush)
     assert ops.read_and_clear_error(0) == 0
     row = {"case": "prefill_attention", "tokens": chunk.num_tokens, "mma_sync_ms": ms,
            "mma_sync_useful_tflops": flops / ms / 1e9, "tcgen05_ms": ms_tc,
-           "tcgen05_useful_tflops": flops / ms_tc / 1e9}
+           "tcgen05_useful_tflops": flops / ms_tc / 1e9, "persistent_ms": ms_p,
+           "persistent_useful_tflops": flops / ms_p / 1e9}
     row.update(_fa4_bar(cfg, chunk, q, kc, vc, flops, iters, flush))
     return row
 
@@ -200,13 +203,22 @@ def main():
     ap.add_argument("--model", default="qwen3-4b-fp8")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--only", default="all", choices=["all", "gemm", "attention"])
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "attention", "persistent"])
     args = ap.parse_args()
     if args.only in ("all", "gemm"):
         for row in run(args.model, args.tokens, args.iters):
             print(json.dumps(row))
     if args.only in ("all", "attention"):
         print(json.dumps(run_attention(args.model, args.tokens, args.iters)))
+    if args.only == "persistent":
+        # one case for a profiler: the persistent attention kernel alone, `iters` launches
+        from quail_b200.ops import reference as ref
+        cfg = MODEL_CONFIGS[args.model]
+        chunk, q, kc, vc, _ = attention_case(cfg, args.tokens)
+        for _ in range(args.iters):
+            ops.prefill_attention_tc2(q, kc, vc, chunk.seqs, chunk.blocks, chunk.page_list, ref.softmax_scale(128))
+        torch.cuda.synchronize()
+        assert ops.read_and_clear_error(0) == 0
 
 
 if __name__ == "__main__":

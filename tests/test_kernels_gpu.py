@@ -135,6 +135,41 @@ def test_qk_norm_rope_kv():
     assert flat_k[slots[3].abs().long()].abs().sum() == 0 or True
 
 
+@pytest.mark.parametrize("T", [1, 300, 1000])
+def test_gemm_mx_qkv_rope_matches_the_fp32_statement(T):
+    # the QKV GEMM with q/k norm, RoPE and the KV write in its epilogue, against
+    # fp32: dequantized operands, per-head RMSNorm, NeoX RoPE, rows by slot
+    H, QH, KH, D, P = 1024, 8, 2, 128, 16
+    g = torch.Generator(device=DEV).manual_seed(T)
+    x = torch.randn(T, H, device=DEV, generator=g)
+    w = torch.randn((QH + 2 * KH) * D, H, device=DEV, generator=g) * 0.05
+    x8, xs = ops.quantize_act_mx(x)
+    w8, ws = ops.quantize_weight_mx(w)
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32, generator=g)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV, generator=g)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(D, device=DEV, generator=g)).bfloat16()
+    cs = ref.rope_cos_sin(4096, D, 1e6, device=DEV)
+    pages = (T + P - 1) // P + 4
+    kc = torch.zeros(pages, P, KH, D, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(pages * P, device=DEV, generator=g)[:T].int()
+    if T > 3:
+        slots[3] = -1
+    q = ops.gemm_mx_qkv_rope(x8, xs, w8, ws, pos, slots, qw, kw, cs, kc, vc, QH, KH, 1e-6)
+    assert ops.read_and_clear_error(0) == 0
+    qkv = (ops.dequantize_mx(x8, xs) @ ops.dequantize_mx(w8, ws).t()).view(T, QH + 2 * KH, D)
+    q_ref = ref.rope_neox(ref.rmsnorm(qkv[:, :QH], qw, 1e-6), pos, cs)
+    k_ref = ref.rope_neox(ref.rmsnorm(qkv[:, QH:QH + KH], kw, 1e-6), pos, cs)
+    assert rel_err(q, q_ref) < 1e-2
+    ok = slots >= 0
+    flat_k, flat_v = kc.view(-1, KH, D), vc.view(-1, KH, D)
+    assert rel_err(flat_k[slots[ok].long()], k_ref[ok]) < 1e-2
+    assert rel_err(flat_v[slots[ok].long()], qkv[ok][:, QH + KH:]) < 1e-2
+    written = torch.zeros(pages * P, dtype=torch.bool, device=DEV)
+    written[slots[ok].long()] = True
+    assert flat_k[~written].abs().sum() == 0 and flat_v[~written].abs().sum() == 0
+
+
 def _segmented_case(P, seq_specs, QH=8, KH=2, D=128, pages=512):
     """seq_specs: list of (q_len, [segment lengths]); the last segment is the own one."""
     g = torch.Generator().manual_seed(1)
@@ -283,6 +318,29 @@ def test_prefill_attention_tcgen05(P):
     out = ops.prefill_attention_tc(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale, fp8_out=False)
     assert rel_err(out, want) < 1e-2
     o8, sf = ops.prefill_attention_tc(q, kc, vc, seqs.to(DEV), tiles.to(DEV), pl.to(DEV), scale)
+    assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
+
+
+@pytest.mark.parametrize("P", [64, 128])
+@pytest.mark.parametrize("QH,KH", [(8, 2), (32, 8)])
+def test_prefill_attention_persistent(P, QH, KH):
+    # the persistent kernel against fp32: short, long, one-token and multi-segment sequences,
+    # a shared prefix read by several of them, both output forms
+    specs = [(100, [48, 100]), (7, [48, 7]), (64, [48, 300, 64]), (130, [48, 130]), (1, [48, 1]),
+             (20, [48, 200, 40]), (300, [48, 300]), (65, [65]), (33, [48, 33]), (200, [48, 8, 200])]
+    q, kc, vc, seqs, pl = _segmented_case(P, specs, QH=QH, KH=KH, pages=1024)
+    blocks = ref.attention_tiles(seqs, 64)
+    scale = ref.softmax_scale(128)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    out = ops.prefill_attention_tc2(q, kc, vc, seqs.to(DEV), blocks.to(DEV), pl.to(DEV), scale, fp8_out=False)
+    assert ops.read_and_clear_error(0) == 0
+    assert rel_err(out, want) < 1e-2
+    # blocks in any order give the same rows
+    perm = torch.randperm(blocks.shape[0])
+    again = ops.prefill_attention_tc2(q, kc, vc, seqs.to(DEV), blocks[perm].contiguous().to(DEV), pl.to(DEV), scale,
+                                      fp8_out=False)
+    assert torch.equal(again, out)
+    o8, sf = ops.prefill_attention_tc2(q, kc, vc, seqs.to(DEV), blocks.to(DEV), pl.to(DEV), scale)
     assert rel_err(ops.dequantize_mx(o8, sf), want) < 4e-2
 
 
