@@ -108,6 +108,9 @@ class ModelEngine:
     def _build(self, pages: int | None):
         from quail_b200.engine.arena import KVArena
         from quail_b200.engine.stage_executor import StageExecutor
+        if self.cfg.is_moe and not self.cfg.is_hybrid:
+            self._build_moe(pages)
+            return
         ckpt = self._checkpoint()
         if self.cfg.is_hybrid:
             if self.cfg.arch == "lfm2":
@@ -148,6 +151,33 @@ class ModelEngine:
         if self.on_gpu and os.environ.get("QB_GRAPHS", "1") != "0":
             # decode passes (AI.MAP / AI.EXTRACT steps) replay captured CUDA graphs
             self.executor.enable_graphs()
+
+    def _build_moe(self, pages: int | None):
+        """A Qwen3-MoE copy on this GPU (all experts): the routed-expert kernels of the
+        expert-parallel path with local buffers; 16-token KV pages (decode-heavy AI.MAP)."""
+        from quail_b200.api.config import Refusal, RefusalError
+        from quail_b200.engine.arena import KVArena
+        from quail_b200.engine.stage_executor import StageExecutor
+        from quail_b200.models.qwen3_moe import Qwen3MoePipeline, Qwen3MoeWeights
+        if not self.on_gpu:
+            raise RefusalError(Refusal(reasons=(f"{self.cfg.name} runs on the GPU kernels only",),
+                                       constraint="unsupported_backend_configuration"))
+        ckpt = None
+        if self.config.weights:
+            from quail_b200.models.weights import load_checkpoint
+            ckpt = load_checkpoint(self.config.weights, device=self.device)
+        weights = Qwen3MoeWeights(self.cfg, ckpt, self.device, head_rows=range(8), seed=self.config.seed)
+        del ckpt
+        self.model = Qwen3MoePipeline(self.cfg, weights, max_tokens=self.chunk_tokens + 256)
+        torch.cuda.empty_cache()
+        page_tokens = int(self.config.extra.get("page_tokens", 16))
+        if pages is None:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            per_page = self.cfg.layers * 2 * page_tokens * self.cfg.num_kv_heads * self.cfg.head_dim * 2
+            pages = max(64, int(free * 0.7) // per_page)
+        self.arena = KVArena(self.cfg.layers, pages, page_tokens, self.cfg.num_kv_heads, self.cfg.head_dim,
+                             device=self.device)
+        self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens, gpu_timing=self.config.gpu_timing)
 
     def _set_answer_rows(self, ids):
         w = getattr(self.model, "w", None)
@@ -284,6 +314,39 @@ class ModelEngine:
         stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
                  "documents": len(uniq), "rows": len(docs), "asked": run.asked}
         return RegionOutput(values=values, stats=stats)
+
+    def run_pairs(self, preamble: str, anchors: list, pairs: list, call: CallSpec) -> RegionOutput:
+        """An AI join's region: anchor documents (each prefilled once) and (anchor index, other
+        document) pairs; `call` (AI.IF or AI.SCORE) is asked once per pair. Values per pair."""
+        from quail_b200.engine.region import Call, PairRun
+        tok = self.tokenizer
+        true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
+        false_ids = tok.answer_ids(P.FALSE_SPELLINGS)
+        both = set(true_ids) & set(false_ids)
+        answer = [i for i in true_ids if i not in both] + [i for i in false_ids if i not in both]
+        nt = len([i for i in true_ids if i not in both])
+        self._set_answer_rows(answer)
+        rc = Call(kind=call.kind, suffix=tok.encode(call.tail), name=call.name,
+                  true_cols=list(range(nt)), false_cols=list(range(nt, len(answer))))
+        a_tok = self.tokenize_docs(list(anchors))
+        o_tok = self.tokenize_docs([t for _, t in pairs])
+        ex = self.executor
+        passes0, tok0 = ex.stats.passes, ex.stats.tokens
+        run = PairRun(ex, tok.encode(preamble), a_tok, [(i, o) for (i, _), o in zip(pairs, o_tok)], rc,
+                      answer_width=len(answer))
+        from quail_b200.utils import progress
+        with progress.count(f"join over {len(anchors)} anchors", len(pairs), " pairs") as bar:
+            run.progress = bar
+            values = run.run()
+        if self.on_gpu:
+            from quail_b200 import ops
+            err = ops.read_and_clear_error(self.device.index)
+            if err:
+                raise RuntimeError(f"a kernel's bounded wait ran out (code {err})")
+        stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
+                 "documents": sum(1 for a in a_tok if len(a)), "rows": len(pairs), "asked": run.asked,
+                 "pairs": len(pairs)}
+        return RegionOutput(values=[{call.name: v} for v in values], stats=stats)
 
     def _sql_values(self, calls: list[CallSpec], raw: dict, names) -> dict:
         """The SQL values of a row's answers so far (labels, decoded text), for guard tests."""

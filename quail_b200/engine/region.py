@@ -448,3 +448,67 @@ def feature_list(rows) -> list:
     ids, st = ids[first], st[first]
     by = np.lexsort((ids, -st))              # strongest first, lower id on ties
     return [(int(i), float(v)) for i, v in zip(ids[by], st[by])]
+
+
+class PairRun:
+    """An AI join's questions: every (anchor document, other document) pair, asked once.
+
+    Each anchor document is prefilled once, after the shared prefix; each pair
+    is one follow-up task that reads the prefix and its anchor's pages and
+    computes only its own tokens (the other document, then the call's
+    question), with its answer read at the last token. An anchor's pages are
+    freed when its last pair is answered. This is the reference's join
+    operator with pair lists (quail/backends/quail/executor/operators/
+    join.py:47-739): the anchor side's KV is shared by all of its pairs.
+    """
+
+    def __init__(self, executor: StageExecutor, prefix: np.ndarray, anchors: list, pairs: list, call: Call,
+                 answer_width: int | None = None):
+        self.ex = executor
+        self.prefix = np.asarray(prefix, dtype=np.int32)
+        self.anchors = [np.asarray(a, dtype=np.int32) for a in anchors]
+        self.pairs = [(int(i), np.asarray(t, dtype=np.int32)) for i, t in pairs]
+        self.call = call
+        self.values: list = [None] * len(self.pairs)
+        self.asked = 0
+        self.fresh_tokens = 0
+        self._left = [0] * len(self.anchors)
+        for i, _ in self.pairs:
+            self._left[i] += 1
+        self.progress = None
+
+    def _answered(self, j: int, row) -> None:
+        call = self.call
+        margin = RegionRun._margin(call, row)
+        self.values[j] = bool(margin > 0) if call.kind == "filter" else 1.0 / (1.0 + math.exp(-margin))
+        self.asked += 1
+        self.ex.free(("pair", j))
+        i = self.pairs[j][0]
+        self._left[i] -= 1
+        if self._left[i] == 0 and self.ex.pool.resident(("anc", i)):
+            self.ex.free(("anc", i))
+        if self.progress is not None:
+            self.progress.advance()
+
+    def run(self) -> list:
+        if self.call.kind not in ("filter", "score"):
+            raise ValueError(f"an AI join asks filter or score questions, not {self.call.kind}")
+        P = len(self.prefix)
+        self.fresh_tokens += P
+        self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
+        for i, a in enumerate(self.anchors):
+            if self._left[i] and len(a):
+                self.fresh_tokens += len(a)
+                self.ex.submit(Task(np_rows=True, key=("anc", i), tokens=a, pos_start=P, reads=[(PREFIX_KEY, P)],
+                                    free_after=False))
+        for j, (i, toks) in enumerate(self.pairs):
+            a_len = len(self.anchors[i])
+            own = np.concatenate([toks, self.call.suffix]).astype(np.int32)
+            reads = [(PREFIX_KEY, P)] + ([(("anc", i), a_len)] if a_len else [])
+            self.fresh_tokens += len(own)
+            self.ex.submit(Task(np_rows=True, key=("pair", j), tokens=own, pos_start=P + a_len, reads=reads,
+                                readout=True, free_after=False,
+                                on_done=lambda t, row, j=j: self._answered(j, row)))
+        self.ex.run()
+        self.ex.free(PREFIX_KEY)
+        return self.values

@@ -86,17 +86,27 @@ def _expr_text(e) -> str:
     return t
 
 
-def _selectivity(call) -> float:
-    """The share of rows an AI filter keeps: its options' 'selectivity', else one half."""
+def _options_of(call) -> dict:
+    """A call's options object: its second positional argument or its named `options`."""
     from quail_b200.sql.executor import literal_value
     args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
-    if len(args) > 1:
-        try:
-            v = literal_value(args[1])
-            if isinstance(v, dict) and isinstance(v.get("selectivity"), (int, float)):
-                return min(max(float(v["selectivity"]), 0.0), 1.0)
-        except Exception:  # noqa: BLE001 - a non-literal option prices at the default
-            pass
+    named = {a["name"].lower(): a["value"] for a in call.get("args", [])
+             if isinstance(a, dict) and a.get("type") == "named_arg"}
+    node = args[1] if len(args) > 1 else named.get("options")
+    if node is None:
+        return {}
+    try:
+        v = literal_value(node)
+    except Exception:  # noqa: BLE001 - a non-literal option prices at the defaults
+        return {}
+    return v if isinstance(v, dict) else {}
+
+
+def _selectivity(call) -> float:
+    """The share of rows an AI filter keeps: its options' 'selectivity', else one half."""
+    v = _options_of(call).get("selectivity")
+    if isinstance(v, (int, float)):
+        return min(max(float(v), 0.0), 1.0)
     return 0.5
 
 
@@ -135,12 +145,26 @@ def _doc_column(call):
     return d.get("name") if d.get("type") == "column" else None
 
 
-def _mean_doc_tokens(call, ref, session, default: float = 300.0) -> float:
+def _mean_doc_tokens(call, ref, session, default: float = 300.0, cache: dict | None = None) -> float:
     """Mean document length in tokens from a sample of the scanned column: token-id lists by
-    their length, text at about 4 characters per token; `default` when it cannot tell."""
-    col = _doc_column(call)
+    their length, text at about 4 characters per token; `default` when it cannot tell.
+    `cache` keeps one sample per (table, column) for the whole plan."""
+    return _column_mean_tokens(ref, _doc_column(call), session, default, cache)
+
+
+def _column_mean_tokens(ref, col, session, default: float = 300.0, cache: dict | None = None) -> float:
     if col is None or ref is None or ref.get("type") != "table":
         return default
+    key = (ref["name"].lower(), col.lower())
+    if cache is not None and key in cache:
+        return cache[key]
+    value = _sample_mean_tokens(ref, col, session, default)
+    if cache is not None:
+        cache[key] = value
+    return value
+
+
+def _sample_mean_tokens(ref, col, session, default: float) -> float:
     try:
         from quail_b200.catalog.providers import ScanRequest
         for k, p in session.catalog.items():
@@ -178,6 +202,9 @@ def _plan_select(node, session, budgets) -> PlanNode:
         return PlanNode(node.get("type", "?"))
     cur = None
     rows = None
+    cache: dict = {}
+    gpus = max(session.config.gpus, 1)
+    tail_tokens = 60.0
     if node.get("from"):
         ref = node["from"][0]
         rows = _rows_of(ref, session)
@@ -186,21 +213,30 @@ def _plan_select(node, session, budgets) -> PlanNode:
             right = PlanNode("quail.scan", j["table"].get("name", "subquery"), rows=_rows_of(j["table"], session))
             kind = "AiJoin" if has_model_call(j.get("on")) else "HashJoin"
             r2 = right.rows
+            left_rows = rows
             rows = rows * r2 if rows is not None and r2 is not None and kind == "AiJoin" else rows
-            cur = PlanNode(kind, j["kind"], rows=rows, children=[cur, right])
+            detail, secs = j["kind"], None
+            if kind == "AiJoin":
+                detail, secs = _ai_join(j, ref, left_rows, r2, session, budgets, cache, tail_tokens)
+            cur = PlanNode(kind, detail, rows=rows, seconds=secs, children=[cur, right])
     base_ref = node["from"][0] if node.get("from") and not node.get("joins") else None
-    tail_tokens = 60.0
     for c in conjuncts(node.get("where")):
         if not has_model_call(c):
             cur = PlanNode("Filter", _expr_text(c), rows=rows, children=[cur] if cur else [])
-    for c in conjuncts(node.get("where")):
+    # AI filters in the order the executor asks them (planner.search.order_filters)
+    ai_conj = [c for c in conjuncts(node.get("where")) if has_model_call(c)]
+    ai_conj = _ordered_filters(ai_conj, session)
+    doc_read = set()
+    for c in ai_conj:
         for n in walk(c):
             if is_model_call(n):
                 secs = None
-                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session)
+                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session, cache=cache)
                 if rows is not None:
-                    tokens = rows * (mean_doc_tokens + tail_tokens)
-                    secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / max(session.config.gpus, 1)
+                    first = _doc_column(n) not in doc_read
+                    tokens = rows * ((mean_doc_tokens if first else 0.0) + tail_tokens)
+                    secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / gpus
+                doc_read.add(_doc_column(n))
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
                                children=[cur] if cur else [])
                 rows = rows * _selectivity(n) if rows is not None else None
@@ -208,14 +244,17 @@ def _plan_select(node, session, budgets) -> PlanNode:
         for n in walk(it["expr"]):
             if is_model_call(n):
                 secs = None
-                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session)
+                mean_doc_tokens = _mean_doc_tokens(n, base_ref, session, cache=cache)
                 if rows is not None:
-                    secs = budgets.pass_seconds(int(rows * tail_tokens), mean_doc_tokens)
+                    # a document no earlier model call read is prefilled here
+                    fresh = tail_tokens + (0.0 if _doc_column(n) in doc_read else mean_doc_tokens)
+                    doc_read.add(_doc_column(n))
+                    secs = budgets.pass_seconds(int(rows * fresh), mean_doc_tokens)
                     steps = _decode_tokens(n)
                     if steps:
                         # greedy decode: one token per row per step over the row's context
                         secs += steps * budgets.pass_seconds(max(int(rows), 1), mean_doc_tokens + steps / 2)
-                    secs /= max(session.config.gpus, 1)
+                    secs /= gpus
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
                                children=[cur] if cur else [])
     if node.get("group_by") is not None:
@@ -228,3 +267,64 @@ def _plan_select(node, session, budgets) -> PlanNode:
     if node.get("limit") is not None:
         cur = PlanNode("Limit", _expr_text(node["limit"]), children=[cur])
     return cur
+
+
+def _ordered_filters(ai_conj: list, session) -> list:
+    """WHERE conjuncts with model calls: AI.IF ones in the executor's cost order, then the rest."""
+    from quail_b200.planner.search import doc_tokens, order_filters
+    from quail_b200.sql.executor import bind_call
+    filters, others = [], []
+    for c in ai_conj:
+        inner = c["args"][0] if c.get("type") == "call" and c.get("name") == "HINT" else c
+        (filters if is_model_call(inner) and inner["name"] in ("AI.IF", "AI_FILTER") else others).append(c)
+    if len(filters) < 2:
+        return filters + others
+    try:
+        from quail_b200.api import prompts as P
+        model = P.prompt_model(session.model_cfg) if session.model_cfg is not None else P.PromptModel()
+        bound = [bind_call(c["args"][0] if c.get("name") == "HINT" else c, model.turn, model) for c in filters]
+        order = order_filters([doc_tokens(b.tail) for b in bound],
+                              [b.selectivity if b.selectivity is not None else 0.5 for b in bound])
+    except Exception:  # noqa: BLE001 - a call the binder refuses keeps the written order
+        return filters + others
+    return [filters[i] for i in order] + others
+
+
+def _ai_join(j, left_ref, left_rows, right_rows, session, budgets, cache, tail_tokens):
+    """Detail and cost of an AI join: its anchor side (planner.search) and the pair prefill."""
+    on = j.get("on")
+    call = next((n for n in walk(on) if is_model_call(n)), None)
+    if call is None:
+        return j["kind"], None
+    args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
+    prompt = args[0] if args else None
+    if not (prompt and prompt.get("type") == "call" and prompt.get("name") == "PROMPT"
+            and len(prompt.get("args", [])) == 3):
+        return j["kind"], None
+    a, b = prompt["args"][1], prompt["args"][2]
+    right_ref = j["table"]
+
+    def side_of(e):
+        q = e.get("table") if e.get("type") == "column" else None
+        if q is not None and q.lower() in ((right_ref.get("alias") or right_ref.get("name") or "").lower(),):
+            return "R"
+        return "L"
+    lexpr, rexpr = (a, b) if side_of(a) == "L" else (b, a)
+    lm = _column_mean_tokens(left_ref, lexpr.get("name") if lexpr.get("type") == "column" else None, session,
+                             cache=cache)
+    rm = _column_mean_tokens(right_ref, rexpr.get("name") if rexpr.get("type") == "column" else None, session,
+                             cache=cache)
+    if left_rows is None or right_rows is None:
+        return f"{j['kind']}, anchor by cost at run time", None
+    pairs = left_rows * right_rows
+    asked = _options_of(call).get("anchor")
+    cost_l = left_rows * lm + pairs * (rm + tail_tokens)
+    cost_r = right_rows * rm + pairs * (lm + tail_tokens)
+    if asked is not None:
+        anchor = "left" if str(asked).lower() in ("left", "l", "0", "first") else "right"
+    else:
+        anchor = "left" if cost_l <= cost_r else "right"
+    tokens = cost_l if anchor == "left" else cost_r
+    secs = budgets.pass_seconds(int(tokens), (lm + rm) / 2) / max(session.config.gpus, 1)
+    expr = _expr_text(lexpr if anchor == "left" else rexpr)
+    return f"{j['kind']}, anchor={anchor} ({expr}), pairs={pairs:.0f}", secs

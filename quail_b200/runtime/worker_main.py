@@ -4,6 +4,7 @@
 
 Messages (JSON frames): {"boot": config} -> {"ready": true, "boot_s": s};
 {"region": {"preamble", "path", "calls"}} -> {"values": [...], "stats": {...}};
+{"pairs": {"preamble", "anchors", "pairs", "call"}} (an AI join's pairs) -> the same;
 {"shutdown": true} -> exit. A failure answers {"error": traceback} and the
 worker keeps serving (the reference's WorkerEnd.fail, worker.py:410).
 """
@@ -61,11 +62,16 @@ def main():
                 return
             if "boot" in msg:
                 from quail_b200.api.config import EngineConfig
+                from quail_b200.runtime.groups import build_group_engine, group_env
                 cfg = dict(msg["boot"])
-                cfg["gpus"] = 1
                 t0 = time.perf_counter()
-                from quail_b200.api.engine import ModelEngine
-                engine = ModelEngine(EngineConfig(**cfg))
+                grp = group_env()
+                if grp is not None:
+                    engine = build_group_engine(EngineConfig(**cfg), *grp)
+                else:
+                    from quail_b200.api.engine import ModelEngine
+                    cfg["gpus"] = 1
+                    engine = ModelEngine(EngineConfig(**cfg))
                 reply = {"ready": True, "boot_s": time.perf_counter() - t0}
             elif "region" in msg:
                 import pyarrow as pa
@@ -77,9 +83,29 @@ def main():
                 table = pa.ipc.open_stream(pa.py_buffer(memoryview(mapped))).read_all()
                 docs = table.column("doc").to_pylist()
                 calls = [CallSpec(**c) for c in r["calls"]]
-                out = engine.run_region(r["preamble"], docs, calls) if docs else None
+                # a rank of a multi-GPU copy runs even with no rows: its peers wait for its passes
+                grouped = getattr(engine, "group", None) is not None
+                out = engine.run_region(r["preamble"], docs, calls) if docs or grouped else None
                 reply = {"values": out.values if out else [], "stats": out.stats if out else {}}
                 del table, mapped
+            elif "pairs" in msg:
+                import pyarrow as pa
+
+                from quail_b200.api.engine import CallSpec
+                r = msg["pairs"]
+                tabs = []
+                for key in ("anchors", "pairs"):
+                    mapped = _native.MappedFile(r[key])
+                    tabs.append(pa.ipc.open_stream(pa.py_buffer(memoryview(mapped))).read_all())
+                    del mapped
+                anchors = tabs[0].column("doc").to_pylist()
+                pairs = list(zip(tabs[1].column("anchor").to_pylist(), tabs[1].column("doc").to_pylist()))
+                grouped = getattr(engine, "group", None) is not None
+                if pairs or grouped:
+                    out = engine.run_pairs(r["preamble"], anchors, pairs, CallSpec(**r["call"]))
+                    reply = {"values": out.values, "stats": out.stats}
+                else:
+                    reply = {"values": [], "stats": {}}
             else:
                 reply = {"error": f"unknown message {sorted(msg)}"}
         except Exception:  # noqa: BLE001 - the traceback goes back to the session

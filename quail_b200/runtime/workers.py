@@ -13,6 +13,13 @@ run_region / revive / interrupt, 120 s connect patience), stages.rs
 Failure handling, host side only: a worker that exits or closes its socket
 fails the region with its traceback; the next region revives (kills and
 re-spawns) every worker, which reloads the model.
+
+Copies larger than one GPU (`parallel="tp"` / `"ep"`, quail_b200.runtime.groups):
+the workers of one copy see all of its GPUs and join one process group at
+boot. tp: rows are sharded over copies and every rank of a copy gets its
+copy's rows (rank 0's answers are kept); ep: every rank gets its own rows
+and the ranks of a copy step in lockstep, so a rank with no rows still runs
+(its experts serve the others).
 """
 
 from __future__ import annotations
@@ -90,10 +97,14 @@ class WorkerPool:
     """`gpus` worker processes behind the session; same run_region as ModelEngine."""
 
     def __init__(self, config, python: str | None = None, boot: bool = True):
-        from quail_b200.api.config import check_config
+        from quail_b200.api.config import check_config, group_size
         self.config = config
         self.cfg = check_config(config)   # the decoder config (roles, prompt layout) the workers serve
         self.n = config.gpus
+        # tp / ep: `group` workers form one model copy (rank = index % group)
+        self.group = group_size(config)
+        self.mode = config.parallel if self.group > 1 else "dp"
+        self.copies = self.n // self.group
         self.python = python or sys.executable
         self.dir = tempfile.mkdtemp(prefix=f"qb-{os.getpid()}-")
         self.sock = os.path.join(self.dir, "s")
@@ -108,9 +119,15 @@ class WorkerPool:
     # ------------------------------------------------------------ lifecycle
     def _spawn(self):
         pids = []
+        ports = [_free_port() for _ in range(self.copies)] if self.group > 1 else []
         for i in range(self.n):
             env = [f"QB_WORKER_INDEX={i}"]
-            if self.config.device != "cpu":
+            if self.group > 1:
+                copy, rank = divmod(i, self.group)
+                gpus = ",".join(str(copy * self.group + k) for k in range(self.group))
+                env += [f"CUDA_VISIBLE_DEVICES={gpus}", f"QB_GROUP_RANK={rank}", f"QB_GROUP_SIZE={self.group}",
+                        f"QB_GROUP_PORT={ports[copy]}", "MASTER_ADDR=127.0.0.1"]
+            elif self.config.device != "cpu":
                 env.append(f"CUDA_VISIBLE_DEVICES={i}")
             argv = [self.python, "-m", "quail_b200.runtime.worker_main", "--socket", self.sock, "--index", str(i)]
             pids.append(_native.spawn(argv, env))
@@ -215,8 +232,15 @@ class WorkerPool:
             self.revive()
         self._region += 1
         shards = [[] for _ in range(self.n)]
-        for i, d in enumerate(docs):
-            shards[shard_of(d, self.n)].append(i)
+        if self.mode == "tp":
+            # rows go to copies; every rank of a copy runs its copy's rows
+            for i, d in enumerate(docs):
+                c = shard_of(d, self.copies)
+                for r in range(self.group):
+                    shards[c * self.group + r].append(i)
+        else:
+            for i, d in enumerate(docs):
+                shards[shard_of(d, self.n)].append(i)
         from quail_b200.sql import guards as G
         paths, msgs = [], []
         for w in range(self.n):
@@ -239,16 +263,73 @@ class WorkerPool:
         stats = {"passes": 0, "fresh_tokens": 0, "documents": 0, "rows": len(docs), "asked": 0,
                  "per_worker": []}
         for w, rep in enumerate(replies):
+            stats["per_worker"].append(rep["stats"])
+            if self.mode == "tp" and w % self.group:
+                continue              # the other ranks of a tp copy computed the same answers
             for j, i in enumerate(shards[w]):
                 values[i] = rep["values"][j]
             for k in ("passes", "fresh_tokens", "documents", "asked"):
                 stats[k] += rep["stats"].get(k, 0)
+        return RegionOutput(values=values, stats=stats)
+
+    def run_pairs(self, preamble: str, anchors: list, pairs: list, call):
+        """An AI join's pairs: each anchor (with all of its pairs) goes to one copy."""
+        from dataclasses import asdict
+
+        from quail_b200.api.engine import RegionOutput
+        if not self.alive():
+            self.revive()
+        self._region += 1
+        n_shards = self.copies if self.mode == "tp" else self.n
+        owner = [shard_of(a, n_shards) for a in anchors]
+        per = [[] for _ in range(n_shards)]
+        for j, (i, _) in enumerate(pairs):
+            per[owner[i]].append(j)
+        paths, msgs = [], []
+        for w in range(self.n):
+            sh = w // self.group if self.mode == "tp" else w
+            js = per[sh]
+            local = {}
+            for j in js:
+                local.setdefault(pairs[j][0], len(local))
+            a_tab = docs_table([anchors[i] for i in local] or [""])
+            p_tab = pa.table({"anchor": pa.array([local[pairs[j][0]] for j in js], pa.int32()),
+                              "doc": pa.array([pairs[j][1] for j in js], pa.string())})
+            base = f"qb-{os.getpid()}-{self._region}-{w}"
+            pa_path = _native.shm_write(base + "a", table_bytes(a_tab))
+            pp_path = _native.shm_write(base + "p", table_bytes(p_tab))
+            paths += [pa_path, pp_path]
+            msgs.append({"pairs": {"preamble": preamble, "anchors": pa_path, "pairs": pp_path,
+                                   "call": asdict(call)}})
+        try:
+            replies = self._all(None, msgs)
+        finally:
+            for p in paths:
+                _native.unlink_path(p)
+        values = [None] * len(pairs)
+        stats = {"passes": 0, "fresh_tokens": 0, "documents": 0, "rows": len(pairs), "asked": 0, "per_worker": []}
+        for w, rep in enumerate(replies):
             stats["per_worker"].append(rep["stats"])
+            if self.mode == "tp" and w % self.group:
+                continue
+            sh = w // self.group if self.mode == "tp" else w
+            for k, j in enumerate(per[sh]):
+                values[j] = rep["values"][k]
+            for k in ("passes", "fresh_tokens", "documents", "asked"):
+                stats[k] += rep["stats"].get(k, 0)
         return RegionOutput(values=values, stats=stats)
 
     @property
     def chunk_tokens(self):
         return self.config.chunk_tokens
+
+
+def _free_port() -> int:
+    """A TCP port on 127.0.0.1 that is free now (a tp / ep copy's rendezvous)."""
+    import socket
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
 
 
 def content_hash(b: bytes) -> str:

@@ -470,11 +470,113 @@ class Executor:
             if kind != "inner":
                 raise QueryError(f"{kind.upper()} JOIN needs an equality condition")
             rel = self._cross(left, right)
-        for c in rest:
-            if kind != "inner":
-                raise QueryError("an outer join's ON may only hold equalities")
-            rel = self.apply_where(rel, c)
+        if rest and kind != "inner":
+            raise QueryError("an outer join's ON may only hold equalities")
+        # plain conditions first, then the model's: an AI condition over one column of each
+        # side runs as pairs that share the anchor side's document KV
+        for c in [c for c in rest if not has_model_call(c)] + [c for c in rest if has_model_call(c)]:
+            pair = self._pair_call(c, left, right) if has_model_call(c) else None
+            if pair is not None:
+                rel = self._pair_filter(rel, *pair)
+            else:
+                rel = self.apply_where(rel, c)
         return rel
+
+    # ------------------------------------------------------------ AI join on pairs
+    def _side(self, e, left: Relation, right: Relation) -> str | None:
+        """'L' or 'R' when every column of `e` belongs to that side only, else None."""
+        sides = set()
+        for n in walk(e):
+            if n.get("type") == "column":
+                in_l = in_r = True
+                try:
+                    left.resolve(n.get("table"), n["name"])
+                except QueryError:
+                    in_l = False
+                try:
+                    right.resolve(n.get("table"), n["name"])
+                except QueryError:
+                    in_r = False
+                if in_l == in_r:
+                    return None
+                sides.add("L" if in_l else "R")
+        return sides.pop() if len(sides) == 1 else None
+
+    def _pair_call(self, c, left: Relation, right: Relation):
+        """(call node, template, left expr, right expr, left placeholder) of an AI.IF over one
+        document of each side, or None."""
+        inner = c["args"][0] if c.get("type") == "call" and c["name"] == "HINT" else c
+        if not (is_model_call(inner) and inner["name"] in ("AI.IF", "AI_FILTER")):
+            return None
+        if self.model.role in ("reranker", "decision"):
+            return None
+        args = [a for a in inner["args"] if a.get("type") != "named_arg"]
+        if not args or args[0].get("type") != "call" or args[0]["name"] != "PROMPT":
+            return None
+        pargs = args[0]["args"]
+        if len(pargs) != 3 or pargs[0].get("type") != "literal":
+            return None
+        s0, s1 = self._side(pargs[1], left, right), self._side(pargs[2], left, right)
+        if {s0, s1} != {"L", "R"}:
+            return None
+        lexpr, rexpr = (pargs[1], pargs[2]) if s0 == "L" else (pargs[2], pargs[1])
+        return inner, pargs[0]["value"], lexpr, rexpr, 0 if s0 == "L" else 1
+
+    def _pair_filter(self, rel: Relation, node, template: str, lexpr, rexpr, lpos: int) -> Relation:
+        """Keep the joined rows whose pair the model answers TRUE, asking each distinct pair once.
+
+        The anchor side (the one whose documents are prefilled once and read by
+        all of their pairs) is the one that makes the pair questions cheaper
+        (`planner.search.choose_anchor`); with demand rules off every pair gets
+        its own copy of its anchor document (the same prompt tokens, no sharing).
+        """
+        from quail_b200.planner.search import choose_anchor
+        if rel.num_rows == 0:
+            return rel
+        ldocs = [None if v is None else str(v) for v in _as_array(self.eval(lexpr, rel), rel.num_rows).to_pylist()]
+        rdocs = [None if v is None else str(v) for v in _as_array(self.eval(rexpr, rel), rel.num_rows).to_pylist()]
+        P.check_placeholders(template, 2)
+        question = re.sub(r"\{(\d+)\}", lambda m: f"DOCUMENT {int(m.group(1)) + 1}", template).strip()
+        opts = _options(node["args"][1]) if len([a for a in node["args"] if a.get("type") != "named_arg"]) > 1 \
+            else {}
+        side = choose_anchor(ldocs, rdocs, opts.get("anchor"))
+        self.report.setdefault("joins", []).append({"anchor": "left" if side == "L" else "right"})
+        anc_docs, oth_docs = (ldocs, rdocs) if side == "L" else (rdocs, ldocs)
+        anc_pos = lpos if side == "L" else 1 - lpos
+        anc_label, oth_label = f"DOCUMENT {anc_pos + 1}:\n", f"\n\nDOCUMENT {2 - anc_pos}:\n"
+        tail = P.JOIN_QUESTION_SEP + P.TASK_INSTRUCTION + question + P.ANSWER_CUE + self.turn.suffix
+        anchors, where, pairs, pair_of = [], {}, [], {}
+        keys = []
+        for r in range(rel.num_rows):
+            a = anc_label + (anc_docs[r] or "")
+            o = oth_label + (oth_docs[r] or "")
+            if self.pushdown:
+                k = (a, o)
+                if k in pair_of:            # a repeated pair is asked once
+                    keys.append(pair_of[k])
+                    continue
+                if a not in where:
+                    where[a] = len(anchors)
+                    anchors.append(a)
+                ai = where[a]
+            else:
+                ai = len(anchors)
+                anchors.append(a)
+                k = (ai, o)
+            pair_of[k] = len(pairs)
+            keys.append(len(pairs))
+            pairs.append((ai, o))
+        from quail_b200.api.engine import CallSpec
+        spec = CallSpec(kind="filter", tail=tail, name=node_key(node))
+        if self.engine is None:
+            raise QueryError("this query needs a model; the session has none")
+        out = self.engine.run_pairs(self.turn.prefix, anchors, pairs, spec)
+        self.report["regions"].append(out.stats)
+        for k in ("asked", "fresh_tokens", "passes"):
+            self.report[k] += out.stats.get(k, 0)
+        self.report["evaluated_documents"] += out.stats.get("documents", 0)
+        keep = [bool(out.values[keys[r]].get(spec.name)) for r in range(rel.num_rows)]
+        return rel.filter(pa.array(keep))
 
     def _cross(self, left: Relation, right: Relation) -> Relation:
         n, m = left.num_rows, right.num_rows
@@ -522,10 +624,11 @@ class Executor:
             else:
                 others.append(c)
         if filters:
+            from quail_b200.planner.search import doc_tokens, order_filters
             bound = [bind_call(f, self.turn, self.model) for f in filters]
-            # the most selective hinted filter first
-            order = sorted(range(len(bound)), key=lambda i: bound[i].selectivity if bound[i].selectivity is not None
-                           else 1.0)
+            # cheapest-per-row-removed first: question tokens / (1 - hinted selectivity)
+            order = order_filters([doc_tokens(b.tail) for b in bound],
+                                  [b.selectivity if b.selectivity is not None else 0.5 for b in bound])
             rel = self.run_filters(rel, [bound[i] for i in order])
         for c in others:
             self.compute_ai(rel, [c])

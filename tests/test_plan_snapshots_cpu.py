@@ -31,6 +31,11 @@ QUERIES = {
                  "GROUP BY stars ORDER BY stars",
     "selectivity": "SELECT id, AI.SCORE(PROMPT('Is it positive? {0}', body)) AS s FROM reviews "
                    "WHERE AI.IF(PROMPT('Is it about acting? {0}', body), {'selectivity': 0.25})",
+    "ai_join_anchor": "SELECT r.id, m.title FROM reviews r JOIN movies m "
+                      "ON AI.IF(PROMPT('Is {0} a review of the film {1}?', r.body, m.title))",
+    "cost_order": "SELECT id FROM reviews WHERE AI.IF(PROMPT('Is this a long and detailed review that discusses "
+                  "the acting, the music and the plot of the film at length? {0}', body), {'selectivity': 0.5}) "
+                  "AND AI.IF(PROMPT('Is it funny? {0}', body), {'selectivity': 0.5})",
     "cte": "WITH good AS (SELECT id, body FROM reviews WHERE stars >= 4) "
            "SELECT id, AI.SCORE(PROMPT('Would they rewatch? {0}', body)) AS s FROM good",
 }
