@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "gemm_sm100.h"
 #include "mx_common.cuh"
+#include "tile_order.cuh"
 
 namespace qb {
 
@@ -44,6 +45,7 @@ struct MxParams {
   const uint8_t* sfb;  // [ceil(N/128)][K/128][512]
   int* err;
   int num_m_tiles, num_n_tiles;
+  int n_fast;                    // tile order (gemm_sm100_kernel.cuh: tile_coords)
   // kEpiQkvRope: the columns are QH q heads, KH k heads, KH v heads of 128
   int QH, KH, norm_qk;
   float eps;
@@ -112,7 +114,8 @@ __global__ void __launch_bounds__(64 + kMxBN, 1)
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+        int tm, tn;
+        tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
         const int nchunks = min(BN / 128, sfb_chunks - tn * (BN / 128));
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
@@ -193,7 +196,8 @@ __global__ void __launch_bounds__(64 + kMxBN, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+      int tm, tn;
+        tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
       const int m = tm * BM + row;
       const int n0 = tn * BN + h * 128;
       if (!mbar_wait(acc_full, aphase, p.err, kErrTimeoutEpilogue)) break;
@@ -367,6 +371,7 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
   p.sfb = sfb.data_ptr<uint8_t>();
   p.err = device_error_word(dev);
   p.num_m_tiles = (M + 127) / 128;
+  p.n_fast = M > N ? 1 : 0;
   p.num_n_tiles = (N + kMxBN - 1) / kMxBN;
   if (epi == kEpiSwigluFp8) {
     TORCH_CHECK(N % kMxBN == 0, "SwiGLU: N must be a multiple of 256");
@@ -448,6 +453,7 @@ void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const to
   p.sfb = sfb.data_ptr<uint8_t>();
   p.err = device_error_word(dev);
   p.num_m_tiles = (M + 127) / 128;
+  p.n_fast = M > N ? 1 : 0;
   p.num_n_tiles = N / kMxBN;
   p.QH = (int)QH;
   p.KH = (int)KH;

@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "gemm_sm100.h"
 #include "mx_common.cuh"
+#include "tile_order.cuh"
 
 #include <cuda_fp8.h>
 
@@ -60,6 +61,7 @@ struct F4Params {
   const uint8_t* sfb;   // [ceil(N/128)][K/64][512]
   int* err;
   int num_m_tiles, num_n_tiles;
+  int n_fast;   // tile order (gemm_sm100_kernel.cuh: tile_coords)
 };
 
 __device__ __forceinline__ void umma_nvfp4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -133,7 +135,8 @@ __global__ void __launch_bounds__(64 + kF4BN, 1)
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+        int tm, tn;
+        tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
         const int nchunks = min(BN / 128, sfb_chunks - tn * (BN / 128));
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
@@ -222,7 +225,8 @@ __global__ void __launch_bounds__(64 + kF4BN, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int tm = t % p.num_m_tiles, tn = t / p.num_m_tiles;
+      int tm, tn;
+        tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
       const int m = tm * BM + row;
       const int n0 = tn * BN + h * 128;
       if (!mbar_wait(acc_full, aphase, p.err, kErrTimeoutEpilogue)) break;
@@ -379,6 +383,7 @@ void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::T
   p.sfb = sfb.data_ptr<uint8_t>();
   p.err = device_error_word(dev);
   p.num_m_tiles = (M + 127) / 128;
+  p.n_fast = M > N ? 1 : 0;
   p.num_n_tiles = (N + kF4BN - 1) / kF4BN;
   p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldd = out.stride(0);

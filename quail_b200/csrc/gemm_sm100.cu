@@ -143,6 +143,7 @@ void gemm_sm100(const torch::Tensor& a, const torch::Tensor& b, const c10::optio
   TORCH_CHECK(BN == 128 || BN == 256, "gemm_sm100: BN is 128 or 256");
   p.num_m_tiles = (M + 127) / 128;
   p.num_n_tiles = (N + BN - 1) / BN;
+  p.n_fast = M > N ? 1 : 0;
   if (epi == kEpiSwigluFp8 || epi == kEpiSwigluBf16) TORCH_CHECK(N % BN == 0, "SwiGLU: N must be a multiple of BN");
 
   if (epi == kEpiSwigluFp8) {

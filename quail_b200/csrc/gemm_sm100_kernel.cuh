@@ -6,6 +6,8 @@
 #include "common.cuh"
 #include "gemm_epi.h"
 
+#include "tile_order.cuh"
+
 namespace qb {
 
 struct GemmParams {
@@ -24,13 +26,8 @@ struct GemmParams {
   int sb_gran;
   int* err;
   int num_m_tiles, num_n_tiles;
+  int n_fast;   // tile order: 0 = m fastest (consecutive CTAs share a B tile), 1 = n fastest
 };
-
-__device__ __forceinline__ void tile_coords(int t, int num_m_tiles, int& tm, int& tn) {
-  // column-major raster: consecutive CTAs share one B tile, A stays in L2
-  tm = t % num_m_tiles;
-  tn = t / num_m_tiles;
-}
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -118,7 +115,7 @@ __global__ void __launch_bounds__(64 + BN, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, p.num_m_tiles, tm, tn);
+        tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
             ok = false;
@@ -216,7 +213,7 @@ __global__ void __launch_bounds__(64 + BN, 1)
     int tile_count = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_count) {
       int tm, tn;
-      tile_coords(t, p.num_m_tiles, tm, tn);
+      tile_coords(t, p.num_m_tiles, p.num_n_tiles, p.n_fast, tm, tn);
       const int m = tm * BM + row;
       const int n0 = tn * BN + h * 128;  // first of this thread's 128 columns
       bool ok = true;
@@ -300,8 +297,9 @@ __global__ void __launch_bounds__(64 + BN, 1)
             __threadfence_block();
             xf[(par * 2 + h) * 128 + row] = tile_count + 1;
             const long long t0 = clock64();
+            const long long budget = wait_budget(p.err);
             while (xf[(par * 2 + (h ^ 1)) * 128 + row] != tile_count + 1) {
-              if (clock64() - t0 > kWaitBudgetCycles) {
+              if (clock64() - t0 > budget) {
                 atomicCAS(p.err, 0, kErrTimeoutEpilogue);
                 break;
               }
