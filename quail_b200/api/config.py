@@ -4,9 +4,12 @@ Same fields as the reference's EngineConfig (quail/api/config.py:21-42):
 `model` and `device` name the weights and the hardware, `gpus` counts model
 copies on one host (1, 2, 4 or 8), `gpu_timing` records a CUDA event pair
 per forward chunk, `canvas_draws` and `attention` are kept for API parity.
-Two additions: `weights`, a directory of HF safetensors to load instead of
-random-init weights of the named architecture, and `parallel`, how a model
-larger than one GPU is split ("tp" or "ep") when gpus > 1.
+Additions: `weights`, a directory of HF safetensors to load instead of
+random-init weights of the named architecture; `parallel`, how each model
+copy spreads over GPUs ("dp": one GPU per copy; "tp": tensor-parallel
+copies; "ep": expert-parallel copies of a mixture-of-experts model); and
+`group_gpus`, the GPUs of one tp / ep copy (default: all `gpus`, one copy).
+Rows are sharded over the copies either way.
 """
 
 from __future__ import annotations
@@ -45,6 +48,7 @@ class EngineConfig:
     attention: str | None = None
     weights: str | None = None
     parallel: str = "dp"
+    group_gpus: int | None = None   # GPUs per tp / ep model copy (None: every GPU, one copy)
     chunk_tokens: int | None = None
     tokenizer: str | None = None   # a tokenizer.json (or its directory), or "words" / "bytes"
     seed: int = 0
@@ -85,9 +89,30 @@ def check_config(config: EngineConfig):
     if config.parallel == "ep" and not model.is_moe:
         raise RefusalError(Refusal(reasons=(f"expert parallelism needs a mixture-of-experts model, not {model.name!r}",),
                                    constraint="unsupported_backend_configuration"))
-    if config.parallel != "dp" and config.gpus > 1:
-        raise RefusalError(Refusal(
-            reasons=(f"a session splits work over GPUs by data parallelism; {config.parallel} runs through "
-                     f"quail_b200.utils.bench_tp / bench_moe",),
-            constraint="unsupported_backend_configuration"))
+    if config.parallel != "dp":
+        g = group_size(config)
+        if config.device == "cpu" and config.gpus > 1:
+            raise RefusalError(Refusal(reasons=(f"{config.parallel} copies run on GPUs, not the CPU",),
+                                       constraint="unsupported_backend_configuration"))
+        if g not in (1, 2, 4, 8) or config.gpus % g:
+            raise RefusalError(Refusal(
+                reasons=(f"group_gpus={g} must be 1, 2, 4 or 8 and divide gpus={config.gpus}",),
+                constraint="unsupported_backend_configuration"))
+        if config.parallel == "tp" and (model.num_q_heads % g or model.num_kv_heads % g
+                                        or model.intermediate % (g * 128)):
+            raise RefusalError(Refusal(
+                reasons=(f"{model.name} does not split over {g} GPUs: its q heads ({model.num_q_heads}), kv heads "
+                         f"({model.num_kv_heads}) and MLP width / 128 ({model.intermediate // 128}) must divide",),
+                constraint="unsupported_backend_configuration"))
+        if config.parallel == "ep" and model.num_experts % g:
+            raise RefusalError(Refusal(
+                reasons=(f"{model.num_experts} experts do not split over {g} GPUs",),
+                constraint="unsupported_backend_configuration"))
     return model
+
+
+def group_size(config: EngineConfig) -> int:
+    """GPUs of one model copy: 1 for data parallelism, else group_gpus (default: all gpus)."""
+    if config.parallel == "dp":
+        return 1
+    return config.group_gpus or config.gpus

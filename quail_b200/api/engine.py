@@ -201,7 +201,19 @@ class ModelEngine:
                 out[i] = ids
         return [self.tokenize_doc(d) if o is None else o for d, o in zip(docs, out)]
 
-    def run_region(self, preamble: str, docs: list, calls: list[CallSpec]) -> RegionOutput:
+    def run_region(self, preamble: str, docs: list, calls: list[CallSpec], *, on_rows=None,
+                   stop=None) -> RegionOutput:
+        """Ask `calls` over `docs`; values per input row.
+
+        on_rows(rows, values): called as each distinct document's chain finishes, with the
+        input rows that share it and their SQL values (streamed answers).
+        stop(): checked between forward passes; True ends the region early, and the rows
+        not finished by then come back with no values (stats["stopped"] is set).
+        """
+        return self._run_region(preamble, docs, calls, on_rows, stop)
+
+    def _run_region(self, preamble: str, docs: list, calls: list[CallSpec], on_rows, stop) -> RegionOutput:
+        from quail_b200.engine.stage_executor import QueryCancelled
         from quail_b200.engine.region import Call, RegionRun
         from quail_b200.sql import guards as G
         tok = self.tokenizer
@@ -286,31 +298,62 @@ class ModelEngine:
             answer = [0]
         self._set_answer_rows(answer)
         ex = self.executor
-        stop = getattr(self, "interrupt", None)
-        ex.should_stop = stop.is_set if stop is not None else None
+        interrupt = getattr(self, "interrupt", None)
+        stopped = [False]
+
+        def asked_stop():
+            # latched: a stop hook that answers True once is not asked again
+            if stop is not None and not stopped[0]:
+                stopped[0] = bool(stop())
+            return stopped[0]
+        checks = [f for f in (interrupt.is_set if interrupt is not None else None,
+                              asked_stop if stop is not None else None) if f is not None]
+        ex.should_stop = (lambda: any(f() for f in checks)) if checks else None
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
         run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer),
                         decision=getattr(self.model, "decision", None))
+        rows_of: dict = {}
+        for i, u in enumerate(where):
+            rows_of.setdefault(u, []).append(i)
+
+        def sql_values(u):
+            v = dict(run.results[u].values)
+            for c in calls:
+                if c.kind in ("map", "extract") and c.name in v:
+                    v[c.name] = tok.decode(v[c.name])
+                if c.kind == "classify" and c.name in v:
+                    v[c.name] = c.labels[v[c.name]]
+            return v
+
+        finished: set = set()
+
+        def finish(u):
+            finished.add(u)
+            if on_rows is not None:
+                on_rows(rows_of[u], sql_values(u))
+        run.on_finish = finish
         from quail_b200.utils import progress
         kinds = ", ".join(sorted({c.kind for c in calls}))
         with progress.count(f"{kinds} over {len(uniq)} documents", len(uniq), " docs") as bar:
             run.progress = bar
-            results = run.run()
+            try:
+                results = run.run()
+            except QueryCancelled:
+                if not stopped[0] or (interrupt is not None and interrupt.is_set()):
+                    raise
+                # stopped on request: the rows finished so far keep their answers
+                values = [sql_values(u) if u in finished else {} for u in where]
+                return RegionOutput(values=values, stats={
+                    "passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
+                    "documents": len(finished), "rows": len(docs), "asked": run.asked, "stopped": True})
         progress.say(f"{ex.stats.passes - passes0} passes, {ex.stats.tokens - tok0} fresh tokens", detail=True)
         if self.on_gpu:
             from quail_b200 import ops
             err = ops.read_and_clear_error(self.device.index)
             if err:
                 raise RuntimeError(f"a kernel's bounded wait ran out (code {err})")
-        values = []
-        for u in where:
-            v = dict(results[u].values)
-            for c in calls:
-                if c.kind in ("map", "extract") and c.name in v:
-                    v[c.name] = tok.decode(v[c.name])
-                if c.kind == "classify" and c.name in v:
-                    v[c.name] = c.labels[v[c.name]]
-            values.append(v)
+        values = [sql_values(u) for u in where]
+        del results
         stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
                  "documents": len(uniq), "rows": len(docs), "asked": run.asked}
         return RegionOutput(values=values, stats=stats)

@@ -181,6 +181,31 @@ class Session:
                 self._engine = ModelEngine(self.config)
         return self._engine
 
+    def interrupt(self) -> None:
+        """Stop the model work of this session now: a running query fails, and queries fail at
+        once until resume() (crates/quail/src/lib.rs:265-273). Worker processes are killed and
+        come back, models reloaded, on the first query after resume()."""
+        eng = self._engine
+        if eng is None:
+            return
+        if hasattr(eng, "interrupt") and callable(eng.interrupt):
+            eng.interrupt()
+        else:
+            import threading
+            flag = getattr(eng, "interrupt", None)
+            if not isinstance(flag, threading.Event):
+                eng.interrupt = threading.Event()
+            eng.interrupt.set()
+
+    def resume(self) -> None:
+        eng = self._engine
+        if eng is None:
+            return
+        if hasattr(eng, "resume"):
+            eng.resume()
+        elif getattr(eng, "interrupt", None) is not None:
+            eng.interrupt.clear()
+
     def close(self) -> None:
         if self._engine is not None:
             self._engine.close()

@@ -110,9 +110,10 @@ int* device_error_word(int dev) {
   std::lock_guard<std::mutex> lk(g_err_mu);
   if (!g_err[dev]) {
     c10::cuda::CUDAGuard guard(dev);
+    // 16 bytes: the error code (int) and, at byte 8, the wait budget (int64, 0 = default)
     int* p = nullptr;
-    C10_CUDA_CHECK(cudaMalloc(&p, sizeof(int)));
-    C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+    C10_CUDA_CHECK(cudaMalloc(&p, 16));
+    C10_CUDA_CHECK(cudaMemset(p, 0, 16));
     g_err[dev] = p;
   }
   return g_err[dev];
@@ -128,6 +129,16 @@ int64_t read_and_clear_error(int64_t dev) {
   C10_CUDA_CHECK(cudaMemcpy(&h, p, sizeof(int), cudaMemcpyDeviceToHost));
   if (h) C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
   return h;
+}
+
+// Sets the spin budget (clock cycles) of every bounded wait on the device;
+// 0 or below restores the default. Takes effect for kernels launched after it.
+void set_wait_budget(int64_t dev, int64_t cycles) {
+  int* p = device_error_word((int)dev);
+  c10::cuda::CUDAGuard guard((int)dev);
+  long long v = cycles > 0 ? cycles : 0;
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  C10_CUDA_CHECK(cudaMemcpy(p + 2, &v, sizeof(v), cudaMemcpyHostToDevice));
 }
 
 }  // namespace qb
@@ -163,6 +174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_and_clear_error", &qb::read_and_clear_error);
   m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");
   m.def("tp_gemm_rs", &qb::tp_gemm_rs, "MX GEMM -> reduce-scatter fused: epilogue pushes tiles to owner ranks");
+  m.def("set_wait_budget", &qb::set_wait_budget, "spin budget (cycles) of the kernels' bounded waits; 0 = default");
   m.def("tp_reduce_norm", &qb::tp_reduce_norm, "sum RS slots + residual, RMSNorm, MX quant into the AG buffer");
   m.def("moe_route", &qb::moe_route, "MoE router: softmax, top-k, renormalized weights, per-expert slots");
   m.def("moe_plan_ints", &qb::moe_plan_ints);

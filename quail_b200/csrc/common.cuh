@@ -19,6 +19,16 @@ namespace qb {
 // about two seconds at the B200's boost clock
 constexpr long long kWaitBudgetCycles = 4000000000LL;
 
+// The error word every kernel gets (`err`) sits in a 16-byte device block:
+// int 0 is the error code, the int64 at byte 8 the spin budget in clock
+// cycles (0 or below: kWaitBudgetCycles). The host sets it with
+// set_wait_budget (tests make a wait run out in a millisecond).
+__device__ __forceinline__ long long wait_budget(const int* err) {
+  if (err == nullptr) return kWaitBudgetCycles;
+  const long long b = *reinterpret_cast<const volatile long long*>(err + 2);
+  return b > 0 ? b : kWaitBudgetCycles;
+}
+
 enum ErrorCode : int {
   kOk = 0,
   kErrTimeoutProducer = 1,
@@ -85,9 +95,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const long long start = clock64();
+  const long long budget = wait_budget(err);
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
-    if (clock64() - start > kWaitBudgetCycles) {
+    if (clock64() - start > budget) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

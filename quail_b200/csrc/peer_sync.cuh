@@ -31,10 +31,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 template <bool SYS>
 __device__ __forceinline__ bool wait_word(const uint32_t* p, uint32_t want, int* err) {
   const long long t0 = clock64();
+  const long long budget = wait_budget(err);
   while (true) {
     const uint32_t v = SYS ? ld_acquire_sys(p) : ld_acquire_gpu(p);
     if ((int32_t)(v - want) >= 0) return true;
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       atomicCAS(err, 0, kErrTimeoutPeer);
       return false;
     }

@@ -117,6 +117,7 @@ class RegionRun:
         self._copies: dict = {}               # (row, call) -> document positions a copy may continue at
         self.drafted = 0                      # draft tokens accepted (copy-constrained extraction)
         self.progress = None                  # utils.progress.Count advanced as each row finishes
+        self.on_finish = None                 # on_finish(r): row r's chain is done (streamed answers)
         # columns after the answer rows in a full readout: argmax, lse
         self.nans = answer_width
 
@@ -342,6 +343,8 @@ class RegionRun:
                     self.ex.free(("doc", r))
                 if self.progress is not None:
                     self.progress.advance()
+                if self.on_finish is not None:
+                    self.on_finish(r)
                 return
             # a dropping filter runs alone; other calls up to the next one run side by
             # side, except a call whose guard reads an answer of the same batch

@@ -142,6 +142,10 @@ QWEN3_TINY = DecoderConfig(name="qwen3-tiny", layers=2, hidden=256, num_q_heads=
 # the smallest model the GPU kernels take (head_dim 128, hidden multiple of 256)
 QWEN3_GPU_TINY = DecoderConfig(name="qwen3-gpu-tiny", layers=2, hidden=1024, num_q_heads=8,
                                num_kv_heads=4, head_dim=128, intermediate=1024)
+# the flagship layer sequence at the smallest size: fp8 MX GEMMs, the fused QKV epilogue and
+# the tcgen05 attention (4 q heads per KV head, as Qwen3-4B / 8B / 32B)
+QWEN3_GPU_TINY_GQA4 = DecoderConfig(name="qwen3-gpu-tiny-gqa4", layers=2, hidden=1024, num_q_heads=8,
+                                    num_kv_heads=2, head_dim=128, intermediate=1024)
 # the smallest MoE the GPU kernels take: 16 experts, top-4, expert width 256
 QWEN3_MOE_GPU_TINY = DecoderConfig(name="qwen3-moe-gpu-tiny", layers=2, hidden=1024, num_q_heads=8,
                                    num_kv_heads=2, head_dim=128, intermediate=1024, num_experts=16, top_k=4,
@@ -229,6 +233,7 @@ QWEN35_2B_SAE = QWEN35_4B.with_(name="qwen3.5-2b-sae", layers=12, hidden=2048, n
 QWEN35_SAE_TINY = QWEN35_TINY.with_(name="qwen3.5-sae-tiny", sae_features=256, sae_keep=8)
 
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
+                               QWEN3_GPU_TINY_GQA4,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
                                QWEN35_4B, QWEN35_TINY, QWEN35_GPU_TINY, LFM2_2_6B, LFM2_TINY, LFM2_GPU_TINY,
                                QWEN3_06B, QWEN3_RERANKER_06B, QWEN3_RERANKER_4B, DECISION2_06B, QWEN35_9B, QWEN35_27B,
@@ -246,6 +251,7 @@ MODEL_CONFIGS = {
     "qwen3-30b-a3b-fp8": QWEN3_30B_A3B,
     "qwen3-tiny": QWEN3_TINY,
     "qwen3-gpu-tiny": QWEN3_GPU_TINY,
+    "qwen3-gpu-tiny-gqa4": QWEN3_GPU_TINY_GQA4,
     "qwen3-moe-gpu-tiny": QWEN3_MOE_GPU_TINY,
     "qwen3-4b-sae-bf16": QWEN3_4B_SAE,
     "qwen3-sae-tiny": QWEN3_SAE_TINY,

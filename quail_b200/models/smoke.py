@@ -1,4 +1,9 @@
-"""One tiny packed-prefill forward + yes/no readout of the flagship pipeline on cuda:0."""
+"""One tiny packed-prefill forward + yes/no readout of the flagship pipeline on cuda:0.
+
+The model is the flagship's layer sequence at the smallest size (fp8 MX GEMMs,
+the QKV epilogue with q/k norm + RoPE + KV write, the persistent tcgen05
+attention with 4 q heads per KV head).
+"""
 
 from __future__ import annotations
 
@@ -12,11 +17,11 @@ def run_smoke() -> None:
     from quail_b200.engine.region import Call, RegionRun
     from quail_b200.engine.stage_executor import StageExecutor
     from quail_b200.models.build import build_pipeline
-    from quail_b200.models.config import QWEN3_GPU_TINY
+    from quail_b200.models.config import QWEN3_GPU_TINY_GQA4
 
     assert torch.cuda.is_available(), "smoke needs a GPU"
     ops.native()
-    cfg = QWEN3_GPU_TINY
+    cfg = QWEN3_GPU_TINY_GQA4
     dev = torch.device("cuda", 0)
     pipe = build_pipeline(cfg, device=dev, seed=0, answer_ids=(1, 2, 3, 4))
     arena = KVArena(cfg.layers, 64, 128, cfg.num_kv_heads, cfg.head_dim, device=dev)

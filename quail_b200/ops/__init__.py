@@ -37,6 +37,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     qk_norm_rope_kv,
     quant_rows,
     read_and_clear_error,
+    set_wait_budget,
     rmsnorm_quant,
     sae_features,
     row_argmax_lse,

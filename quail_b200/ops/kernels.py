@@ -383,6 +383,12 @@ def head_readout(normed: torch.Tensor, head: torch.Tensor, ans: torch.Tensor, to
     return torch.cat(cols, dim=1)
 
 
+def set_wait_budget(cycles: int, device: int = 0) -> None:
+    """Spin budget, in clock cycles, of every bounded wait in the kernels on `device`
+    (0 restores the default of about two seconds)."""
+    native().set_wait_budget(device, int(cycles))
+
+
 def read_and_clear_error(device: int = 0) -> int:
     """Synchronize and return (then clear) the kernels' bounded-wait error code."""
     return int(native().read_and_clear_error(device))

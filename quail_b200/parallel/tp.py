@@ -295,8 +295,16 @@ class TPQwen3:
         rows = chunk.final_rows.long()
         mine = (rows >= r * rpr) & (rows < (r + 1) * rpr)
         local = torch.where(mine, rows - r * rpr, torch.zeros_like(rows)).int()
-        logits = ops.final_norm_readout(h, local, self.final_norm, cfg.rms_eps, self.answer_rows)
+        if getattr(chunk, "full_readout", False):
+            # AI.CLASSIFY / MAP rows: answer rows plus the full-vocabulary argmax and log-sum-exp
+            # of this rank's rows (the head is replicated); the other ranks' rows are zero
+            normed = torch.empty(rows.numel(), H, dtype=torch.bfloat16, device=dev)
+            ans = ops.final_norm_readout(h, local, self.final_norm, cfg.rms_eps, self.answer_rows, normed=normed)
+            logits = ops.head_readout(normed, self.head, ans, getattr(chunk, "topk", False))
+        else:
+            logits = ops.final_norm_readout(h, local, self.final_norm, cfg.rms_eps, self.answer_rows)
         logits = logits * mine[:, None].float()
+        # each row is owned by one rank: the sum hands every rank every row's readout
         dist.all_reduce(logits, group=st.group)
         return logits
 

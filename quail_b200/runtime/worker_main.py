@@ -5,6 +5,8 @@
 Messages (JSON frames): {"boot": config} -> {"ready": true, "boot_s": s};
 {"region": {"preamble", "path", "calls"}} -> {"values": [...], "stats": {...}};
 {"pairs": {"preamble", "anchors", "pairs", "call"}} (an AI join's pairs) -> the same;
+during a region the worker may also send {"event": ...} frames and {"ask": ...}
+frames that the session answers (`_Channel`);
 {"shutdown": true} -> exit. A failure answers {"error": traceback} and the
 worker keeps serving (the reference's WorkerEnd.fail, worker.py:410).
 """
@@ -34,6 +36,57 @@ def _inject_fault(index: int) -> None:
         raise RuntimeError(f"injected failure in worker {index}")
     if kind == "exit":
         os._exit(3)
+
+
+class _Channel:
+    """The worker's side of a region's ask channel (the reference's Connection::call,
+    crates/quail/src/workers.rs:184-213).
+
+    While a region runs, the worker may send frames before its reply:
+    {"event": {"kind": "answers", "rows": [[row, values], ...]}} with the rows
+    whose questions are all answered, and {"event": {"kind": "progress", ...}};
+    neither expects an answer. With `ask_every_s`, it also asks
+    {"ask": {"kind": "continue", "done": n}} at most that often, between forward
+    passes, and waits for {"answer": {"stop": bool}}: a host whose LIMIT is
+    met, or whose query was cancelled, answers stop and the region ends with
+    the rows finished so far.
+    """
+
+    def __init__(self, fd, events: bool, ask_every_s):
+        self.fd = fd
+        self.events = bool(events)
+        self.asks = ask_every_s is not None
+        self.every = float(ask_every_s or 0.0)
+        self.rows: list = []
+        self.done = 0
+        self.last = time.monotonic()
+
+    def _send(self, obj) -> None:
+        from quail_b200 import _native
+        _native.send_frame(self.fd, json.dumps(obj).encode(), -1)
+
+    def on_rows(self, rows, values) -> None:
+        for i in rows:
+            self.rows.append([i, values])
+        self.done += len(rows)
+        if len(self.rows) >= 64 or time.monotonic() - self.last > 0.2:
+            self.flush()
+
+    def flush(self) -> None:
+        if self.events and self.rows:
+            self._send({"event": {"kind": "answers", "rows": self.rows}})
+            self._send({"event": {"kind": "progress", "rows_done": self.done}})
+            self.rows = []
+        self.last = time.monotonic()
+
+    def should_stop(self) -> bool:
+        from quail_b200 import _native
+        if time.monotonic() - self.last < self.every:
+            return False
+        self.flush()
+        self._send({"ask": {"kind": "continue", "done": self.done}})
+        reply = json.loads(_native.recv_frame(self.fd, 1 << 20, 120_000))
+        return bool(reply.get("answer", {}).get("stop", False))
 
 
 def main():
@@ -85,7 +138,11 @@ def main():
                 calls = [CallSpec(**c) for c in r["calls"]]
                 # a rank of a multi-GPU copy runs even with no rows: its peers wait for its passes
                 grouped = getattr(engine, "group", None) is not None
-                out = engine.run_region(r["preamble"], docs, calls) if docs or grouped else None
+                chan = _Channel(fd, r.get("events", False), r.get("ask_every_s"))
+                out = (engine.run_region(r["preamble"], docs, calls, on_rows=chan.on_rows if chan.events else None,
+                                         stop=chan.should_stop if chan.asks else None)
+                       if docs or grouped else None)
+                chan.flush()
                 reply = {"values": out.values if out else [], "stats": out.stats if out else {}}
                 del table, mapped
             elif "pairs" in msg:

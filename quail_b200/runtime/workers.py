@@ -78,9 +78,21 @@ class Worker:
     def __init__(self, index: int, pid: int, fd: int):
         self.index, self.pid, self.fd = index, pid, fd
 
-    def call(self, msg: dict, timeout_ms: int = -1) -> dict:
+    def call(self, msg: dict, timeout_ms: int = -1, on_event=None, on_ask=None) -> dict:
+        """Send `msg` and return the reply; frames before it are events (to `on_event`)
+        or asks (answered with on_ask(ask), by default "go on")."""
         _native.send_frame(self.fd, json.dumps(msg).encode(), timeout_ms)
-        return self.receive(timeout_ms)
+        while True:
+            reply = self.receive(timeout_ms)
+            if "event" in reply:
+                if on_event is not None:
+                    on_event(self.index, reply["event"])
+                continue
+            if "ask" in reply:
+                answer = on_ask(self.index, reply["ask"]) if on_ask is not None else {"stop": False}
+                _native.send_frame(self.fd, json.dumps({"answer": answer}).encode(), timeout_ms)
+                continue
+            return reply
 
     def receive(self, timeout_ms: int = -1) -> dict:
         try:
@@ -112,6 +124,8 @@ class WorkerPool:
         self.workers: list[Worker] = []
         self._region = 0
         self.tokenizer = None
+        self._interrupted = False
+        self.ask_every_s = 0.25   # how often a worker asks whether to go on (regions with a stop hook)
         self._spawn()
         if boot:
             self.boot()
@@ -179,8 +193,14 @@ class WorkerPool:
         self.boot()
 
     def interrupt(self):
-        """Stop every worker now; the next region revives them."""
+        """Stop every worker now (the reference's Interrupter, workers.rs:687-711): running
+        regions fail, and regions fail at once until resume()."""
+        self._interrupted = True
         self._kill_all([w.pid for w in self.workers])
+
+    def resume(self):
+        """Accept regions again; the next one revives (re-spawns and boots) the workers."""
+        self._interrupted = False
 
     def close(self):
         for w in self.workers:
@@ -203,14 +223,14 @@ class WorkerPool:
         except OSError:
             pass
 
-    def _all(self, msg: dict, per_worker: list | None = None) -> list:
+    def _all(self, msg: dict, per_worker: list | None = None, on_event=None, on_ask=None) -> list:
         """Send to every worker (or per_worker messages), then gather every reply in order."""
         errors, replies = [], [None] * self.n
 
         def one(i):
             try:
                 m = per_worker[i] if per_worker is not None else msg
-                replies[i] = self.workers[i].call(m)
+                replies[i] = self.workers[i].call(m, on_event=on_event, on_ask=on_ask)
             except Exception as exc:  # noqa: BLE001 - every worker is told to finish; errors re-raised below
                 errors.append(exc)
 
@@ -224,10 +244,15 @@ class WorkerPool:
         return replies
 
     # ------------------------------------------------------------ regions
-    def run_region(self, preamble: str, docs: list, calls: list):
+    def run_region(self, preamble: str, docs: list, calls: list, *, on_rows=None, stop=None):
+        """Same contract as ModelEngine.run_region. on_rows(rows, values) receives each worker's
+        finished rows while the region runs (session row numbers); stop() is asked by every
+        worker about every `ask_every_s` and ends the region on all of them."""
         from dataclasses import asdict
 
         from quail_b200.api.engine import RegionOutput
+        if self._interrupted:
+            raise WorkerError("the session was interrupted; call resume() before the next query")
         if not self.alive():
             self.revive()
         self._region += 1
@@ -253,9 +278,24 @@ class WorkerPool:
                 d = asdict(c)
                 d["guard"] = G.take(c.guard, shards[w])   # per-row guard inputs of this shard's rows
                 shard_calls.append(d)
-            msgs.append({"region": {"preamble": preamble, "path": path, "calls": shard_calls}})
+            region = {"preamble": preamble, "path": path, "calls": shard_calls}
+            if on_rows is not None:
+                region["events"] = True
+            if stop is not None:
+                region["ask_every_s"] = self.ask_every_s
+            msgs.append({"region": region})
+
+        def on_event(w, ev):
+            if ev.get("kind") == "answers" and on_rows is not None:
+                if self.mode == "tp" and w % self.group:
+                    return
+                for j, values in ev["rows"]:
+                    on_rows([shards[w][j]], values)
+
+        def on_ask(w, ask):
+            return {"stop": bool(stop())} if stop is not None else {"stop": False}
         try:
-            replies = self._all(None, msgs)
+            replies = self._all(None, msgs, on_event=on_event, on_ask=on_ask)
         finally:
             for p in paths:
                 _native.unlink_path(p)

@@ -5,7 +5,9 @@
 
 All ranks run the same packed chunks (rows lognormal(median 400, sigma 0.6)
 clipped to [16, 4096], a 48-token shared prefix); one step is one forward
-pass. Device-timed with CUDA events over exactly K steps, max over ranks.
+pass. --query if_classify adds AI.CLASSIFY (4 labels) on the rows AI.IF keeps:
+its questions read the document's pages and need full-vocabulary readouts,
+so the timed passes mix new documents with classify follow-ups. Device-timed with CUDA events over exactly K steps, max over ranks.
 --comm fused: the in-kernel AG->GEMM / GEMM->RS paths; --comm nccl: the
 same GEMMs with NCCL all-gather / reduce-scatter between them (baseline).
 """
@@ -17,6 +19,7 @@ import json
 import os
 from datetime import timedelta
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -29,6 +32,9 @@ def main():
     ap.add_argument("--chunk-tokens", type=int, default=32768)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--query", default="if", choices=["if", "if_classify"],
+                    help="if: AI.IF alone; if_classify: AI.IF, then AI.CLASSIFY into 4 labels (1-3 seeded token "
+                         "ids each) on the rows it keeps (BASELINE config 4)")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -46,7 +52,14 @@ def main():
     cfg = MODEL_CONFIGS[args.model]
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
-    model = TPQwen3(cfg, dist.group.WORLD, seed=0, max_tokens=args.chunk_tokens + 4096, answer_ids=range(8),
+    rng = np.random.default_rng(11)
+    labels = [[int(x) for x in rng.integers(1000, 100000, int(rng.integers(1, 4)))] for _ in range(4)]
+    answer = list(range(8))
+    for lab in labels:
+        for t in lab:
+            if t not in answer:
+                answer.append(t)
+    model = TPQwen3(cfg, dist.group.WORLD, seed=0, max_tokens=args.chunk_tokens + 4096, answer_ids=answer,
                     comm=args.comm)
     pages = 2 * (args.chunk_tokens // 128) + 512
     arena = KVArena(cfg.layers, pages, 128, cfg.num_kv_heads // world, 128, device=dev)
@@ -55,7 +68,12 @@ def main():
                        hi=4096, seed=7)  # the same rows on every rank
     ex = StageExecutor(model, arena, args.chunk_tokens)
     call = Call(kind="filter", suffix=wl.suffix, true_cols=[0, 1, 2, 3], false_cols=[4, 5, 6, 7], name="if")
-    run = RegionRun(ex, wl.prefix, wl.bodies, [call])
+    calls = [call]
+    if args.query == "if_classify":
+        suffix2 = np.random.default_rng(12).integers(0, cfg.vocab, 56).astype(np.int32)
+        calls.append(Call(kind="classify", suffix=suffix2, name="kind", labels=[np.asarray(x, np.int32) for x in labels],
+                          label_cols=[[answer.index(t) for t in lab] for lab in labels]))
+    run = RegionRun(ex, wl.prefix, wl.bodies, calls, answer_width=len(answer))
     run.submit_all()
     ex.step()
     for _ in range(args.warmup):
@@ -80,7 +98,8 @@ def main():
     ms_max = float(t[0])
     if rank == 0:
         prompt = fresh + rows * len(wl.prefix)
-        print(json.dumps({"metric": "AI.IF prefill tok/s, qwen3-32b-fp8 tensor-parallel", "comm": args.comm,
+        print(json.dumps({"metric": f"AI.{'IF + AI.CLASSIFY' if args.query == 'if_classify' else 'IF'} prefill "
+                                    f"tok/s, qwen3-32b-fp8 tensor-parallel", "comm": args.comm, "query": args.query,
                           "tp": world, "layers": cfg.layers, "value": round(prompt / (ms_max / 1e3), 1),
                           "unit": "prompt tokens/s", "rows_per_second": round(rows / (ms_max / 1e3), 1),
                           "fresh_tokens_per_second": round(fresh / (ms_max / 1e3), 1),

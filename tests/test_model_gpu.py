@@ -12,7 +12,7 @@ import torch
 from quail_b200 import ops
 from quail_b200.engine.arena import KVArena
 from quail_b200.engine.stage_executor import StageExecutor, Task
-from quail_b200.models.config import QWEN3_GPU_TINY
+from quail_b200.models.config import QWEN3_GPU_TINY, QWEN3_GPU_TINY_GQA4
 from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Reference, Qwen3Weights
 from quail_b200.models.weights import random_checkpoint
 
@@ -35,9 +35,13 @@ def _dist(a, b):
     return ((a - b).norm() / b.norm()).item()
 
 
-@pytest.mark.parametrize("weight_dtype,layers", [("fp8", 1), ("fp8", 2), ("bf16", 2)])
-def test_pipeline_matches_fp32_model(weight_dtype, layers):
-    cfg = QWEN3_GPU_TINY.with_(weight_dtype=weight_dtype, vocab=4096, max_position=8192, layers=layers)
+@pytest.mark.parametrize("base,weight_dtype,layers", [(QWEN3_GPU_TINY, "fp8", 1), (QWEN3_GPU_TINY, "fp8", 2),
+                                                      (QWEN3_GPU_TINY, "bf16", 2), (QWEN3_GPU_TINY_GQA4, "fp8", 2),
+                                                      (QWEN3_GPU_TINY_GQA4, "bf16", 2)])
+def test_pipeline_matches_fp32_model(base, weight_dtype, layers):
+    # QWEN3_GPU_TINY_GQA4 runs the flagship layer sequence: MX fp8 GEMMs, the QKV epilogue with
+    # norm + RoPE + KV write, and the persistent tcgen05 attention (4 q heads per KV head)
+    cfg = base.with_(weight_dtype=weight_dtype, vocab=4096, max_position=8192, layers=layers)
     ckpt = random_checkpoint(cfg, seed=7, device="cuda")
     ids = list(range(16))
     pipe = Qwen3Pipeline(cfg, Qwen3Weights(cfg, ckpt, "cuda", head_rows=ids))
@@ -53,7 +57,7 @@ def test_pipeline_matches_fp32_model(weight_dtype, layers):
     assert ops.read_and_clear_error(0) == 0
     d_kernel = _dist(got, want)
     d_emul = _dist(close, want)
-    print(f"{weight_dtype} L={layers}: kernel-vs-exact {d_kernel:.4f} emulated-vs-exact {d_emul:.4f} "
+    print(f"{cfg.name} {weight_dtype} L={layers}: kernel-vs-exact {d_kernel:.4f} emulated-vs-exact {d_emul:.4f} "
           f"kernel-vs-emulated {_dist(got, close):.4f}")
     # the kernels are as close to the exact fp32 model as an fp32 model that
     # rounds and quantizes at the same points

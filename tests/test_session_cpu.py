@@ -190,8 +190,15 @@ def test_parallel_refusals():
         check_config(EngineConfig(model="qwen3.5-tiny", device="cpu", parallel="tp"))
     with _pytest.raises(RefusalError, match="expert parallelism needs"):
         check_config(EngineConfig(model="qwen3-tiny", device="cpu", parallel="ep"))
-    with _pytest.raises(RefusalError, match="data parallelism"):
+    with _pytest.raises(RefusalError, match="run on GPUs"):
         check_config(EngineConfig(model="qwen3-moe-gpu-tiny", device="cpu", parallel="ep", gpus=2))
+    with _pytest.raises(RefusalError, match="does not split over 4 GPUs"):
+        check_config(EngineConfig(model="qwen3-tiny", device="b200", parallel="tp", gpus=4))
+    with _pytest.raises(RefusalError, match="divide gpus"):
+        check_config(EngineConfig(model="qwen3-32b-fp8", device="b200", parallel="tp", gpus=4, group_gpus=8))
+    # a TP=8 copy of the 32B model, and two TP=4 copies, are accepted
+    assert check_config(EngineConfig(model="qwen3-32b-fp8", device="b200", parallel="tp", gpus=8)).layers == 64
+    assert check_config(EngineConfig(model="qwen3-32b-fp8", device="b200", parallel="tp", gpus=8, group_gpus=4))
     with _pytest.raises(RefusalError, match="parallel is"):
         check_config(EngineConfig(model="qwen3-tiny", device="cpu", parallel="pp"))
 

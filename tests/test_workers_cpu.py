@@ -109,3 +109,77 @@ def test_an_oversized_frame_is_refused_before_allocation():
     _native.close_fd(fd)
     _native.close_fd(lfd)
     os.unlink(path)
+
+
+def _many(n=40):
+    rng = np.random.default_rng(9)
+    words = ["alpha", "beta", "gamma", "delta", "omega", "sigma", "kappa"]
+    return [" ".join(rng.choice(words, size=int(rng.integers(20, 60)))) for _ in range(n)]
+
+
+def test_workers_stream_answers_over_the_ask_channel():
+    bp = bind_prompt("Short? {0}")
+    docs = _many()
+    got = {}
+
+    def on_rows(rows, values):
+        for r in rows:
+            assert r not in got          # each row arrives once
+            got[r] = values
+    pool = WorkerPool(_cfg(2))
+    try:
+        out = pool.run_region(bp.preamble, docs, [CallSpec(kind="filter", tail=bp.tail, name="f")], on_rows=on_rows)
+    finally:
+        pool.close()
+    assert sorted(got) == list(range(len(docs)))
+    assert all(got[r] == out.values[r] for r in got)
+
+
+def test_a_stop_answer_ends_the_region_with_the_rows_finished_so_far():
+    bp = bind_prompt("Short? {0}")
+    docs = _many()
+    asked, seen = [], []
+
+    def stop():
+        # the fetch demand of a LIMIT: enough rows came back, stop asking
+        asked.append(1)
+        return len(seen) >= 5
+    pool = WorkerPool(quail.EngineConfig(model="qwen3-tiny", device="cpu", gpus=2, chunk_tokens=128))
+    pool.ask_every_s = 0.0               # ask between every two passes
+    try:
+        full = pool.run_region(bp.preamble, docs, [CallSpec(kind="filter", tail=bp.tail, name="f")])
+        part = pool.run_region(bp.preamble, docs, [CallSpec(kind="filter", tail=bp.tail, name="f")], stop=stop,
+                               on_rows=lambda rows, v: seen.extend(rows))
+    finally:
+        pool.close()
+    assert asked
+    done = [i for i, v in enumerate(part.values) if v]
+    assert 0 < len(done) < len(docs)
+    assert all(part.values[i] == full.values[i] for i in done)
+    assert part.stats["asked"] < full.stats["asked"]
+
+
+def test_interrupt_fails_regions_until_resume():
+    pool = WorkerPool(_cfg(2))
+    try:
+        _region(pool)
+        pool.interrupt()
+        with pytest.raises(WorkerError, match="interrupted"):
+            _region(pool)
+        pool.resume()
+        out = _region(pool)                # the workers are revived and the models reloaded
+        assert len(out.values) == 20
+    finally:
+        pool.close()
+
+
+def test_session_interrupt_and_resume_on_one_engine():
+    from quail_b200.engine.stage_executor import QueryCancelled
+    with quail.Session(config=_cfg(1)) as s:
+        s.register("t", _table())
+        s.sql(QUERY).collect()
+        s.interrupt()
+        with pytest.raises(QueryCancelled):
+            s.sql(QUERY).collect()
+        s.resume()
+        assert s.sql(QUERY).collect().num_rows >= 0
