@@ -96,7 +96,7 @@ def main():
     # ---------------------------------------------------------------- device-timed steps
     steps_total = args.warmup + args.steps + 2
     wl = make_workload(rows_for_tokens(steps_total * args.chunk_tokens * 1.1), seed=1000 + rank)
-    ex = StageExecutor(pipe, arena, args.chunk_tokens)
+    ex = StageExecutor(pipe, arena, args.chunk_tokens, gpu_timing=True)
     run = RegionRun(ex, wl.prefix, wl.bodies, [call(wl.suffix)])
     run.submit_all()
     ex.step()  # the shared prefix pass
@@ -108,6 +108,7 @@ def main():
     torch.cuda.synchronize()
     sampler = ClockSampler(local).start()
     tok0, passes0 = ex.stats.tokens, ex.stats.passes
+    gpu0 = ex.stats.gpu_ms
     launches0 = ops.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # readouts of the last warm-up pass are collected inside the first timed step
@@ -121,6 +122,9 @@ def main():
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
+    # device time inside the passes' forward calls (event pairs around each pass): the rest of
+    # the timed region is the GPU waiting for the host
+    busy_ms = ex.stats.gpu_ms - gpu0
     launches = ops.launch_count() - launches0
     fresh = ex.stats.tokens - tok0
     # rows whose last token ran in the timed passes
@@ -186,6 +190,7 @@ def main():
                        "workload": "AI.IF filter, packed prefill chunks, yes/no readout",
                        "l2": "inputs larger than L2 (4.4 GB of weights streamed every step)"},
             "gpu_launches": launches,
+            "forward_ms_per_step": round(busy_ms / args.steps, 3),
             "clocks": clocks,
         }
         if e2e is not None:

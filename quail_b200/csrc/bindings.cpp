@@ -28,13 +28,17 @@ void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const to
                       const torch::Tensor& sfb, const torch::Tensor& positions, const torch::Tensor& slots,
                       const torch::Tensor& qn, const torch::Tensor& kn, const torch::Tensor& cos_sin,
                       torch::Tensor& q_out, torch::Tensor& k_cache, torch::Tensor& v_cache, int64_t QH, int64_t KH,
-                      double eps, bool norm_qk);
+                      double eps, bool norm_qk, const c10::optional<torch::Tensor>& row_ss);
 void prefill_attention_tc2(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                            const torch::Tensor& seqs, const torch::Tensor& blocks, const torch::Tensor& page_list,
                            double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
 void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
-             const c10::optional<torch::Tensor>& residual);
+             const c10::optional<torch::Tensor>& residual, const c10::optional<torch::Tensor>& row_ss,
+             double ss_eps, const c10::optional<torch::Tensor>& xq, const c10::optional<torch::Tensor>& xq_sf,
+             const c10::optional<torch::Tensor>& ss_out);
+void quant_mx_ss(const torch::Tensor& x, torch::Tensor& y8, torch::Tensor& sf, torch::Tensor& ss, int64_t T);
+void row_rinv(const torch::Tensor& parts, int64_t K, double eps, torch::Tensor& out);
 void gemm_nvfp4(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
                 double alpha, int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& residual,
                 const c10::optional<torch::Tensor>& row_scale);
@@ -149,6 +153,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b"), py::arg("sa"), py::arg("sb"), py::arg("sb_gran"), py::arg("epi"), py::arg("out"),
         py::arg("out_scale"), py::arg("residual"), py::arg("bn"));
   m.def("gemm_mx", &qb::gemm_mx, "tcgen05 fp8 GEMM with UE8M0 block scales (kind::mxf8f6f4.block_scale)");
+  m.def("row_rinv", &qb::row_rinv, "1 / rms per row from partial sums of squares");
+  m.def("quant_mx_ss", &qb::quant_mx_ss, "bf16 rows -> MX e4m3 (no normalization) + per-row sum of squares");
   m.def("prefill_attention_tc2", &qb::prefill_attention_tc2,
         "persistent tcgen05 prefill attention: TMA loader, MMA warp, two ping-pong softmax warpgroups");
   m.def("gemm_mx_qkv_rope", &qb::gemm_mx_qkv_rope,

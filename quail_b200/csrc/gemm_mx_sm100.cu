@@ -57,6 +57,20 @@ struct MxParams {
   __nv_bfloat16* q_out;          // [M, QH, 128]
   __nv_bfloat16* k_cache;        // [slots, KH, 128]
   __nv_bfloat16* v_cache;
+  // kEpiResidualMx: the new residual rows (as stored, bf16) also go out as e4m3
+  // with UE8M0 scales per 32 columns (xq [M, N], xq_sf atoms with K = N), and
+  // each thread's 128-column partial sum of squares goes to ss_out[m, n / 128]
+  // (no atomics: a fixed order of summation, so reruns are bitwise equal): the
+  // next GEMM's input without a normalization pass
+  uint8_t* xq;
+  uint8_t* xq_sf;
+  float* ss_out;
+  // any epilogue: with row_ss ([M, ss_parts] partial sums), rows are first scaled
+  // by 1 / rms = rsqrt(sum(row_ss[m, :]) * inv_k + ss_eps): the RMSNorm of the A
+  // rows, whose weight is folded into B
+  const float* row_ss;
+  int ss_parts;
+  float inv_k, ss_eps;
 };
 
 template <int EPI>
@@ -217,7 +231,63 @@ __global__ void __launch_bounds__(64 + kMxBN, 1)
       tc_fence_before();
       mbar_arrive(acc_empty);
       if (m >= p.M) continue;
-      if constexpr (EPI == kEpiQkvRope) {
+      if constexpr (EPI != kEpiResidual && EPI != kEpiResidualMx) {
+        if (p.row_ss != nullptr) {
+          // ss_parts == 0: row_ss already holds 1 / rms per row (row_rinv below)
+          float rinv;
+          if (p.ss_parts == 0) {
+            rinv = p.row_ss[m];
+          } else {
+            float ss = 0.f;
+            for (int j = 0; j < p.ss_parts; ++j) ss += p.row_ss[(size_t)m * p.ss_parts + j];
+            rinv = rsqrtf(ss * p.inv_k + p.ss_eps);
+          }
+#pragma unroll
+          for (int i = 0; i < 128; ++i) acc[i] *= rinv;
+        }
+      }
+      if constexpr (EPI == kEpiResidualMx) {
+        // residual add, bf16 store, then the stored row as MX e4m3 and its sum of squares
+        if (n0 >= p.N) continue;
+        __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + n0;
+        uint32_t word = 0;
+        float ss = 0.f;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float rv[8];
+            ld_bf16x8f(p.R + (size_t)m * p.ldr + n0 + g * 32 + j, rv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              v[j + i] = __bfloat162float(__float2bfloat16(acc[g * 32 + j + i] + rv[i]));
+            st_bf16x8(dst + g * 32 + j, &v[j]);
+          }
+          float amax = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            amax = fmaxf(amax, fabsf(v[i]));
+            ss = fmaf(v[i], v[i], ss);
+          }
+          const uint8_t e = ue8m0_of(amax);
+          const float inv = ue8m0_inv(e);
+          word |= (uint32_t)e << (8 * g);
+          uint8_t* xd = p.xq + (size_t)m * p.N + n0 + g * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 16) {
+            __align__(16) __nv_fp8x4_e4m3 pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              pk[i] = __nv_fp8x4_e4m3(make_float4(v[j + 4 * i] * inv, v[j + 4 * i + 1] * inv, v[j + 4 * i + 2] * inv,
+                                                  v[j + 4 * i + 3] * inv));
+            *reinterpret_cast<uint4*>(xd + j) = *reinterpret_cast<const uint4*>(pk);
+          }
+        }
+        *reinterpret_cast<uint32_t*>(p.xq_sf + ((size_t)(m / 128) * (p.N / 128) + n0 / 128) * 512 + (m % 32) * 16 +
+                                     ((m % 128) / 32) * 4) = word;
+        p.ss_out[(size_t)m * (p.N / 128) + n0 / 128] = ss;
+      } else if constexpr (EPI == kEpiQkvRope) {
         // this thread's row of one head: per-head RMSNorm and NeoX RoPE of q and k in
         // fp32, then q to q_out and k / v straight into the token's arena row
         if (n0 >= p.N) continue;
@@ -348,7 +418,9 @@ static void launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, MxParams& p,
 // a: [M, K] e4m3, sfa: MX scale bytes of a; b: [N, K] e4m3, sfb: of b.
 void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
-             const c10::optional<torch::Tensor>& residual) {
+             const c10::optional<torch::Tensor>& residual, const c10::optional<torch::Tensor>& row_ss,
+             double ss_eps, const c10::optional<torch::Tensor>& xq, const c10::optional<torch::Tensor>& xq_sf,
+             const c10::optional<torch::Tensor>& ss_out) {
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "gemm_mx: e4m3");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
               "gemm_mx: shapes");
@@ -389,10 +461,32 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
     p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
     p.ldd = out.stride(0);
   }
-  if (epi == kEpiResidual) {
+  if (epi == kEpiResidual || epi == kEpiResidualMx) {
     TORCH_CHECK(residual.has_value() && residual->scalar_type() == at::kBFloat16, "residual");
     p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     p.ldr = residual->stride(0);
+  }
+  if (epi == kEpiResidualMx) {
+    TORCH_CHECK(N % 128 == 0, "kEpiResidualMx: N must be a multiple of 128");
+    TORCH_CHECK(xq.has_value() && xq->scalar_type() == at::kFloat8_e4m3fn && xq->is_contiguous() &&
+                    xq->size(0) >= M && xq->size(1) == N,
+                "kEpiResidualMx: xq [M, N] e4m3");
+    TORCH_CHECK(xq_sf.has_value() && xq_sf->numel() >= (int64_t)((M + 127) / 128) * (N / 128) * 512,
+                "kEpiResidualMx: xq scale bytes");
+    TORCH_CHECK(ss_out.has_value() && ss_out->scalar_type() == at::kFloat && ss_out->numel() >= (int64_t)M * (N / 128),
+                "kEpiResidualMx: ss_out [M, N / 128] fp32 partial sums of squares");
+    p.xq = reinterpret_cast<uint8_t*>(xq->data_ptr());
+    p.xq_sf = xq_sf->data_ptr<uint8_t>();
+    p.ss_out = ss_out->data_ptr<float>();
+  }
+  if (row_ss.has_value()) {
+    TORCH_CHECK(row_ss->scalar_type() == at::kFloat && row_ss->size(0) >= M && row_ss->is_contiguous() &&
+                    row_ss->dim() <= 2,
+                "row_ss: [M, parts] partial sums of squares, or [M] 1 / rms");
+    p.row_ss = row_ss->data_ptr<float>();
+    p.ss_parts = row_ss->dim() == 2 ? (int)row_ss->size(1) : 0;
+    p.inv_k = 1.f / (float)K;
+    p.ss_eps = (float)ss_eps;
   }
   CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a.stride(0), 128, 128,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -402,6 +496,7 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
     case kEpiQkvRope: TORCH_CHECK(false, "gemm_mx: the QKV epilogue is gemm_mx_qkv_rope"); break;
     case kEpiBf16: launch_mx<kEpiBf16>(ta, tb, p, st, dev); break;
     case kEpiResidual: launch_mx<kEpiResidual>(ta, tb, p, st, dev); break;
+    case kEpiResidualMx: launch_mx<kEpiResidualMx>(ta, tb, p, st, dev); break;
     case kEpiSwigluFp8: launch_mx<kEpiSwigluFp8>(ta, tb, p, st, dev); break;
     case kEpiSwigluBf16: launch_mx<kEpiSwigluBf16>(ta, tb, p, st, dev); break;
     default: TORCH_CHECK(false, "gemm_mx: unknown epilogue ", epi);
@@ -418,7 +513,7 @@ void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const to
                       const torch::Tensor& sfb, const torch::Tensor& positions, const torch::Tensor& slots,
                       const torch::Tensor& qn, const torch::Tensor& kn, const torch::Tensor& cos_sin,
                       torch::Tensor& q_out, torch::Tensor& k_cache, torch::Tensor& v_cache, int64_t QH, int64_t KH,
-                      double eps, bool norm_qk) {
+                      double eps, bool norm_qk, const c10::optional<torch::Tensor>& row_ss) {
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "qkv_rope: e4m3");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
               "qkv_rope: shapes");
@@ -467,11 +562,45 @@ void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const to
   p.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
   p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
   p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  if (row_ss.has_value()) {
+    TORCH_CHECK(row_ss->scalar_type() == at::kFloat && row_ss->size(0) >= M && row_ss->is_contiguous() &&
+                    row_ss->dim() <= 2,
+                "row_ss: [M, parts] partial sums of squares, or [M] 1 / rms");
+    p.row_ss = row_ss->data_ptr<float>();
+    p.ss_parts = row_ss->dim() == 2 ? (int)row_ss->size(1) : 0;
+    p.inv_k = 1.f / (float)K;
+    p.ss_eps = (float)eps;
+  }
   CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, a.stride(0), 128, 128,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, b.stride(0), 128, kMxBN,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   launch_mx<kEpiQkvRope>(ta, tb, p, st, dev);
+}
+
+// 1 / rms per row from the partial sums of squares a kEpiResidualMx epilogue
+// wrote ([M, parts], summed in a fixed order): one float per row for the
+// epilogues of the GEMMs that read those rows.
+__global__ void row_rinv_kernel(const float* __restrict__ parts, int n_parts, int M, float inv_k, float eps,
+                                float* __restrict__ out) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float ss = 0.f;
+  for (int j = 0; j < n_parts; ++j) ss += parts[(size_t)m * n_parts + j];
+  out[m] = rsqrtf(ss * inv_k + eps);
+}
+
+void row_rinv(const torch::Tensor& parts, int64_t K, double eps, torch::Tensor& out) {
+  TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.dim() == 2 && parts.is_contiguous(), "parts [M, n] fp32");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.numel() >= parts.size(0), "out [M] fp32");
+  const int M = parts.size(0);
+  if (M == 0) return;
+  const int dev = parts.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
+  row_rinv_kernel<<<(M + 255) / 256, 256, 0, st>>>(parts.data_ptr<float>(), (int)parts.size(1), M, 1.f / (float)K,
+                                                   (float)eps, out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace qb

@@ -83,11 +83,14 @@ __device__ __forceinline__ size_t sf_atom_offset(int m, int j, int kst) {
   return ((size_t)(m >> 7) * kst + (j >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (j & 3);
 }
 
-template <int H, bool FP8, bool MX = false>
+// RAW (with MX): no normalization; the row is quantized as it is and its sum
+// of squares goes to ss_out[row] (the GEMM that consumes it applies 1/rms).
+template <int H, bool FP8, bool MX = false, bool RAW = false>
 __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                      const __nv_bfloat16* __restrict__ w, float eps,
                                      uint8_t* __restrict__ y8, float* __restrict__ ys, int ldys,
-                                     __nv_bfloat16* __restrict__ ybf, int ldy, int T) {
+                                     __nv_bfloat16* __restrict__ ybf, int ldy, int T,
+                                     float* __restrict__ ss_out = nullptr) {
   constexpr int SLABS = H / 256;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -102,13 +105,18 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int ld
     for (int i = 0; i < 8; ++i) ss += v[s][i] * v[s][i];
   }
   ss = warp_sum(ss);
+  if constexpr (RAW) {
+    if (lane == 0) ss_out[warp] = ss;
+  }
   const float rinv = rsqrtf(ss / H + eps);
 #pragma unroll
   for (int s = 0; s < SLABS; ++s) {
-    float wv[8];
-    ld_bf16x8(w + s * 256 + lane * 8, wv);
+    if constexpr (!RAW) {
+      float wv[8];
+      ld_bf16x8(w + s * 256 + lane * 8, wv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[s][i] = v[s][i] * rinv * wv[i];
+      for (int i = 0; i < 8; ++i) v[s][i] = v[s][i] * rinv * wv[i];
+    }
     if constexpr (FP8 && MX) {
       // one UE8M0 scale per 32 columns (4 lanes)
       float amax = 0.f;
@@ -421,6 +429,37 @@ void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, c
   QB_NORM_CASE(5120)
 #undef QB_NORM_CASE
   TORCH_CHECK(false, "rmsnorm_quant: unsupported hidden size ", H);
+}
+
+// x: [T, H] bf16 -> e4m3 [T, H] + UE8M0 scale bytes of x itself (no normalization) and
+// ss [T, 1] fp32, the sum of squares of each row: the input of a GEMM that applies the
+// row's 1/rms in its epilogue (the norm weight folded into its B operand).
+void quant_mx_ss(const torch::Tensor& x, torch::Tensor& y8, torch::Tensor& sf, torch::Tensor& ss, int64_t T) {
+  const int H = x.size(1);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "quant_mx_ss: bf16 rows");
+  TORCH_CHECK(y8.is_contiguous() && y8.size(1) == H && y8.size(0) >= T, "quant_mx_ss output");
+  TORCH_CHECK(sf.scalar_type() == at::kByte && sf.numel() >= (T + 127) / 128 * (H / 128) * 512, "scale bytes");
+  TORCH_CHECK(ss.scalar_type() == at::kFloat && ss.numel() >= T, "ss: fp32 per row");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(x.get_device());
+  const int threads = 256, blocks = (int)((T * 32 + threads - 1) / threads);
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto yp = reinterpret_cast<uint8_t*>(y8.data_ptr());
+  auto sp = reinterpret_cast<float*>(sf.data_ptr());
+#define QB_QSS_CASE(HH)                                                                                        \
+  if (H == HH) {                                                                                               \
+    rmsnorm_quant_kernel<HH, true, true, true><<<blocks, threads, 0, cur_stream(x)>>>(                         \
+        xp, x.stride(0), nullptr, 0.f, yp, sp, 0, nullptr, 0, (int)T, ss.data_ptr<float>());                   \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                            \
+    return;                                                                                                    \
+  }
+  QB_QSS_CASE(1024)
+  QB_QSS_CASE(2048)
+  QB_QSS_CASE(2560)
+  QB_QSS_CASE(4096)
+  QB_QSS_CASE(5120)
+#undef QB_QSS_CASE
+  TORCH_CHECK(false, "quant_mx_ss: unsupported hidden size ", H);
 }
 
 // x: [T, H] bf16 -> e4m3 [T, H] + UE8M0 scale bytes (MX atom layout, one per 32 columns)

@@ -9,6 +9,12 @@ against the retained answer rows of the LM head:
             rmsnorm+quant -> gate_up GEMM (+SwiGLU+quant) -> down GEMM (+residual)] x L
         -> gather readout rows -> final norm -> answer-row logits
 
+fp8 models fold those steps: the QKV epilogue does q/k norm, RoPE and the KV
+write; the o / down GEMMs that update the residual also write it as MX e4m3
+with per-row sums of squares, and the GEMM that reads it applies the row's
+1 / rms (the RMSNorm weights are folded into the QKV and gate_up weights at
+load), so no separate norm pass reads the residual stream.
+
 The reference drives vLLM modules with its own loop
 (quail/backends/quail/executor/models/qwen3.py:15-135, Engine primitives in
 attention.py:432-1573); here every step is one of our kernels.
@@ -56,10 +62,13 @@ class Qwen3Weights:
                 # projection is requantized once at load with the same blocks
                 deq = lambda n: dequantize_weight(ckpt[n + ".weight"].to(device),  # noqa: E731
                                                   ckpt[n + ".weight_scale_inv"].to(device))
-                L["wqkv"], L["sqkv"] = quantize_weight_mx(torch.cat([deq(n) for n in names]))
+                # the RMSNorm weights fold into the K columns of the projections they feed:
+                # (x / rms(x) * w) . W^T = (x . (W diag(w))^T) / rms(x), and the GEMMs apply 1 / rms
+                ln1, ln2 = L["ln1"].float()[None, :], L["ln2"].float()[None, :]
+                L["wqkv"], L["sqkv"] = quantize_weight_mx(torch.cat([deq(n) for n in names]) * ln1)
                 L["wo"], L["so"] = quantize_weight_mx(deq(p + "self_attn.o_proj"))
                 L["wgu"], L["sgu"] = interleave_gate_up_mx(torch.cat([deq(p + "mlp.gate_proj"),
-                                                                      deq(p + "mlp.up_proj")]))
+                                                                      deq(p + "mlp.up_proj")]) * ln2)
                 L["wd"], L["sd"] = quantize_weight_mx(deq(p + "mlp.down_proj"))
             else:
                 L["wqkv"] = torch.cat([ckpt[n + ".weight"].to(bf) for n in names]).to(device).contiguous()
@@ -117,38 +126,48 @@ class Qwen3Pipeline:
         dev = w.device
         h = ops.embed_gather(chunk.ids, w.embed)  # residual stream, bf16 [T, H]
         fp8 = cfg.fp8
+        H = cfg.hidden
+        if fp8:
+            # the residual stream's RMSNorms run inside the GEMMs: the GEMM that writes h also
+            # writes it as MX e4m3 with per-128-column sums of squares, and the next GEMM
+            # scales its rows by 1 / rms (the norm weights are folded into its weights)
+            x8, xs, ss = ops.quant_mx_ss(h)
+        n_layers = len(w.layers)
         for li, L in enumerate(w.layers):
             kc, vc = arena.layer(li)
             if fp8:
-                x8, xs = ops.rmsnorm_quant_mx(h, L["ln1"], cfg.rms_eps)
                 # K1 + K4: QKV GEMM whose epilogue norms, rotates and writes K/V to the arena
                 q = ops.gemm_mx_qkv_rope(x8, xs, L["wqkv"], L["sqkv"], chunk.positions, chunk.slots, L["qn"],
-                                         L["kn"], w.cos_sin, kc, vc, cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
-            else:
-                x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
-                qkv = ops.gemm(x, L["wqkv"])
-                q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
-                                        cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
-            if fp8 and self.tc_attention:
-                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
-                ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-                x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
-                a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
-                ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                                         L["kn"], w.cos_sin, kc, vc, cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps,
+                                         row_ss=ops.row_rinv(ss, H, cfg.rms_eps))
+                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=self.tc_attention)
+                x8 = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
+                xs = torch.empty(ops.sf_bytes(T, H), dtype=torch.uint8, device=dev)
+                ss = torch.empty(T, H // 128, dtype=torch.float32, device=dev)
+                ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL_MX, out=h, residual=h, xq=x8, xq_sf=xs,
+                            ss_out=ss)
+                # one 1 / rms per row for the whole gate_up GEMM (its epilogue then reads one float)
+                a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8,
+                                      row_ss=ops.row_rinv(ss, H, cfg.rms_eps), eps=cfg.rms_eps)
+                if li == n_layers - 1:
+                    ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                    continue
+                x8 = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
+                xs = torch.empty(ops.sf_bytes(T, H), dtype=torch.uint8, device=dev)
+                ss = torch.empty(T, H // 128, dtype=torch.float32, device=dev)
+                ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL_MX, out=h, residual=h, xq=x8, xq_sf=xs,
+                            ss_out=ss)
                 continue
-            if fp8:
-                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=False)
-                ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-                x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
-                a8, as_ = ops.gemm_mx(x8, xs, L["wgu"], L["sgu"], epi=ops.EPI_SWIGLU_FP8)
-                ops.gemm_mx(a8, as_, L["wd"], L["sd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-            else:
-                o = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=False, tc=self.tc_attention)
-                ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-                x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
-                a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
-                ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-        del T, dev
+            x = ops.rmsnorm_quant(h, L["ln1"], cfg.rms_eps, fp8=False)
+            qkv = ops.gemm(x, L["wqkv"])
+            q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
+                                    cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
+            o = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=False, tc=self.tc_attention)
+            ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+            x = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+            a = ops.gemm(x, L["wgu"], epi=ops.EPI_SWIGLU_BF16)
+            ops.gemm(a, L["wd"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+        del T, dev, H
         if cfg.has_sae:
             # resid_post of the last loaded layer -> packed SAE features per readout row
             return ops.sae_features(h.index_select(0, chunk.final_rows.long()), w.sae_w, w.sae_b, cfg.sae_keep)

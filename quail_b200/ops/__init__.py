@@ -34,6 +34,9 @@ from quail_b200.ops.kernels import (  # noqa: F401
     prefill_attention_tc,
     prefill_attention_tc2,
     gemm_mx_qkv_rope,
+    quant_mx_ss,
+    row_rinv,
+    EPI_RESIDUAL_MX,
     qk_norm_rope_kv,
     quant_rows,
     read_and_clear_error,

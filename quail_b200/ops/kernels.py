@@ -29,6 +29,7 @@ EPI_BF16 = 0
 EPI_RESIDUAL = 1
 EPI_SWIGLU_FP8 = 2
 EPI_SWIGLU_BF16 = 3
+EPI_RESIDUAL_MX = 5
 
 
 def kernels_available() -> bool:
@@ -82,12 +83,20 @@ def sf_bytes(rows: int, K: int) -> int:
 
 def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, *, epi: int = EPI_BF16,
             out: torch.Tensor | None = None, out_sf: torch.Tensor | None = None,
-            residual: torch.Tensor | None = None):
+            residual: torch.Tensor | None = None, row_ss: torch.Tensor | None = None, eps: float = 1e-6,
+            xq: torch.Tensor | None = None, xq_sf: torch.Tensor | None = None, ss_out: torch.Tensor | None = None):
     """D = A . B^T with UE8M0 block scales on the tcgen05 block-scaled MMA.
 
     A [M, K], B [N, K] e4m3; sfa / sfb their scale bytes in the MX atom
     layout (quail_b200.ops.quant.pack_sf_atoms). EPI_SWIGLU_FP8 returns
     (e4m3 [M, N/2], its scale bytes) ready to be the next GEMM's A.
+
+    row_ss [M, parts] (partial sums of squares of A's unnormalized rows): the
+    rows are RMS-normalized in the epilogue (rsqrt(sum / K + eps)), for an A
+    that came out of EPI_RESIDUAL_MX or quant_mx_ss and a B with the norm
+    weight folded in. EPI_RESIDUAL_MX: out = acc + residual (bf16), and out as
+    e4m3 + MX scales into xq / xq_sf, with each row's sums of squares per 128
+    columns into ss_out [M, N / 128].
     """
     C = native()
     M, N = a.shape[0], b.shape[0]
@@ -97,16 +106,39 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
             out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
         if out_sf is None:
             out_sf = torch.empty(sf_bytes(M, N // 2), dtype=torch.uint8, device=a.device)
-        C.gemm_mx(a, sfa, b, sfb, epi, out, out_sf, None)
+        C.gemm_mx(a, sfa, b, sfb, epi, out, out_sf, None, row_ss, eps, None, None, None)
         return out, out_sf
     if out is None:
         out = torch.empty(M, N // 2 if epi == EPI_SWIGLU_BF16 else N, dtype=torch.bfloat16, device=a.device)
-    C.gemm_mx(a, sfa, b, sfb, epi, out, None, residual)
+    C.gemm_mx(a, sfa, b, sfb, epi, out, None, residual, row_ss, eps, xq, xq_sf, ss_out)
     return out
 
 
+def row_rinv(parts: torch.Tensor, K: int, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """1 / rms per row, [M] fp32, from [M, n] partial sums of squares over K columns."""
+    if out is None:
+        out = torch.empty(parts.shape[0], dtype=torch.float32, device=parts.device)
+    count_launch()
+    native().row_rinv(parts, K, eps, out)
+    return out
+
+
+def quant_mx_ss(x: torch.Tensor, *, out=None, out_sf=None, ss=None, rows: int | None = None):
+    """bf16 rows -> (e4m3 rows, MX scale bytes, per-row sum of squares): a GEMM input whose
+    RMSNorm the GEMM applies (gemm_mx(row_ss=...))."""
+    T = x.shape[0] if rows is None else rows
+    H = x.shape[1]
+    out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device) if out is None else out
+    out_sf = torch.empty(sf_bytes(T, H), dtype=torch.uint8, device=x.device) if out_sf is None else out_sf
+    ss = torch.empty(T, 1, dtype=torch.float32, device=x.device) if ss is None else ss
+    count_launch()
+    native().quant_mx_ss(x, out, out_sf, ss, T)
+    return out, out_sf, ss
+
+
 def gemm_mx_qkv_rope(x8, xs, wqkv, sqkv, positions, slots, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache,
-                     num_q_heads: int, num_kv_heads: int, eps: float, *, norm_qk: bool = True, q_out=None):
+                     num_q_heads: int, num_kv_heads: int, eps: float, *, norm_qk: bool = True, q_out=None,
+                     row_ss=None):
     """The fp8 QKV projection with per-head q/k RMSNorm, NeoX RoPE and the paged KV write
     fused into its epilogue (K1 + K4 in one kernel). Returns q [T, QH, 128] bf16."""
     C = native()
@@ -115,7 +147,7 @@ def gemm_mx_qkv_rope(x8, xs, wqkv, sqkv, positions, slots, q_norm_w, k_norm_w, c
         q_out = torch.empty(T, num_q_heads, 128, dtype=torch.bfloat16, device=x8.device)
     count_launch()
     C.gemm_mx_qkv_rope(x8, xs, wqkv, sqkv, positions, slots, q_norm_w, k_norm_w, cos_sin, q_out, k_cache, v_cache,
-                       num_q_heads, num_kv_heads, eps, norm_qk)
+                       num_q_heads, num_kv_heads, eps, norm_qk, row_ss)
     return q_out
 
 

@@ -43,6 +43,13 @@ def test_pipeline_matches_fp32_model(base, weight_dtype, layers):
     # norm + RoPE + KV write, and the persistent tcgen05 attention (4 q heads per KV head)
     cfg = base.with_(weight_dtype=weight_dtype, vocab=4096, max_position=8192, layers=layers)
     ckpt = random_checkpoint(cfg, seed=7, device="cuda")
+    # non-trivial RMSNorm weights (random init leaves them at one): the fp8 pipeline folds
+    # them into the projections it feeds, which this makes visible
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for k in list(ckpt):
+        if k.endswith("layernorm.weight") or k == "model.norm.weight":
+            ckpt[k] = (ckpt[k].float() * (1 + 0.3 * torch.randn(ckpt[k].shape, generator=g, device="cuda"))).to(
+                ckpt[k].dtype)
     ids = list(range(16))
     pipe = Qwen3Pipeline(cfg, Qwen3Weights(cfg, ckpt, "cuda", head_rows=ids))
     exact = Qwen3Reference(cfg, ckpt, device="cuda", head_rows=ids)
