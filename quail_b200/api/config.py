@@ -55,16 +55,25 @@ class EngineConfig:
     extra: dict = field(default_factory=dict)
 
 
-def resolve_model(name: str):
+def resolve_model(name: str, registry=None):
     from quail_b200.models.config import MODEL_CONFIGS
+    if registry is not None:
+        found = registry.model(name)
+        if found is not None:
+            return found
     if name in MODEL_CONFIGS:
         return MODEL_CONFIGS[name]
-    return Refusal(reasons=(f"unknown model {name!r}; registered models: {sorted(MODEL_CONFIGS)}",),
+    names = registry.model_names() if registry is not None else sorted(MODEL_CONFIGS)
+    return Refusal(reasons=(f"unknown model {name!r}; registered models: {names}",),
                    constraint="unknown_model", needed=1, available=0, unit="specs")
 
 
-def check_config(config: EngineConfig):
-    model = resolve_model(config.model)
+def check_config(config: EngineConfig, registry=None):
+    """The decoder config a session runs, or a RefusalError naming what cannot run.
+
+    `registry` (quail_b200.extensions.ExtensionRegistry) adds models to the built-in ones.
+    """
+    model = resolve_model(config.model, registry)
     if isinstance(model, Refusal):
         raise RefusalError(model)
     if config.device not in DEVICES:

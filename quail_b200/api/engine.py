@@ -72,9 +72,9 @@ class ModelEngine:
         self.executor = StageExecutor(model, arena, self.chunk_tokens, gpu_timing=config.gpu_timing)
         return self
 
-    def __init__(self, config: EngineConfig, device_index: int = 0, pages: int | None = None):
+    def __init__(self, config: EngineConfig, device_index: int = 0, pages: int | None = None, registry=None):
         self.config = config
-        self.cfg = check_config(config)
+        self.cfg = check_config(config, registry)
         self.on_gpu = config.device != "cpu"
         if self.on_gpu:
             if not torch.cuda.is_available():

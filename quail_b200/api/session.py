@@ -42,12 +42,17 @@ class QueryResult:
 
 
 class Query:
-    def __init__(self, session: "Session", text: str, dialect: str = "snowflake"):
+    def __init__(self, session: "Session", text: str, dialect: str | None = None):
+        from quail_b200.api.dialects import SQLDialect, to_parser_sql
         from quail_b200.sql.executor import parse
         self.session = session
         self.text = text
-        self.dialect = dialect
-        self.tree = parse(text)  # syntax errors surface here, before any model work
+        if dialect is None:
+            dialect = session.settings.get("datafusion.sql_parser.dialect", "snowflake")
+        self.dialect = SQLDialect.of(dialect).value
+        self.tree = parse(to_parser_sql(text, self.dialect))  # syntax errors surface here, before model work
+        if session.registry is not None:
+            self.tree = session.registry.apply_rules(self.tree)
 
     def plan(self):
         from quail_b200.planner.plan import plan_query
@@ -119,11 +124,11 @@ class Session:
     def __init__(self, config: EngineConfig | None = None, *, tokenizer=None, registry=None,
                  endpoint: str | None = None, token: str | None = None):
         self.config = config
-        self.model_cfg = check_config(config) if config is not None else None
+        self.registry = registry     # quail_b200.extensions.ExtensionRegistry: extra models, devices, rules
+        self.model_cfg = check_config(config, registry) if config is not None else None
         self.catalog: dict = {}
         self.settings: dict = {}
         self.tokenizer_path = tokenizer
-        self.registry = registry
         self._engine = None
         self._remote = None
         if endpoint is not None:
@@ -150,10 +155,11 @@ class Session:
         self.catalog.pop(name, None)
 
     # ------------------------------------------------------------ queries
-    def sql(self, text: str, dialect: str = "snowflake"):
+    def sql(self, text: str, dialect: str | None = None):
+        """A query in `dialect` (quail_b200.SQLDialect: 'snowflake', the default, or 'bq')."""
         if self._remote is not None:
             from quail_b200.server.client import RemoteQuery
-            return RemoteQuery(self, text, dialect)
+            return RemoteQuery(self, text, dialect or "snowflake")
         return Query(self, text, dialect)
 
     def get_run(self, query_id: str):
@@ -175,10 +181,10 @@ class Session:
         if self._engine is None:
             if self.config.gpus > 1:
                 from quail_b200.runtime.workers import WorkerPool
-                self._engine = WorkerPool(self.config)
+                self._engine = WorkerPool(self.config, registry=self.registry)
             else:
                 from quail_b200.api.engine import ModelEngine
-                self._engine = ModelEngine(self.config)
+                self._engine = ModelEngine(self.config, registry=self.registry)
         return self._engine
 
     def interrupt(self) -> None:

@@ -62,8 +62,9 @@ class Budgets:
     gpus: int = 1
 
     @classmethod
-    def for_model(cls, cfg, device_name: str, gpus: int = 1, chunk_tokens: int | None = None) -> "Budgets":
-        dev = DEVICES[device_name]
+    def for_model(cls, cfg, device_name: str, gpus: int = 1, chunk_tokens: int | None = None,
+                  registry=None) -> "Budgets":
+        dev = (registry.device(device_name) if registry is not None else None) or DEVICES[device_name]
         chunk = chunk_tokens or DEFAULT_CHUNK_TOKENS
         chunk = min(chunk, kernel_index_cap(cfg))
         free = dev.mem_bytes * POOL_FRACTION - weight_bytes(cfg)

@@ -127,7 +127,8 @@ def plan_query(tree: dict, session) -> Plan:
     from quail_b200.planner.budgets import Budgets
     cfg = session.model_cfg
     budgets = Budgets.for_model(cfg, session.config.device, gpus=session.config.gpus,
-                                chunk_tokens=session.config.chunk_tokens)
+                                chunk_tokens=session.config.chunk_tokens,
+                                registry=getattr(session, "registry", None))
     settings = {"model": session.config.model, "device": session.config.device, "gpus": session.config.gpus,
                 "chunk_tokens": budgets.chunk_tokens, "compute_knee": budgets.compute_knee()}
     node = tree["query"] if tree.get("type") == "explain" else tree

@@ -1,8 +1,8 @@
 """Device specs: the peaks the cost model prices work against.
 
-B200 numbers: nominal dense peaks (bf16 2.25, fp8 4.5, fp4 9 PFLOP/s),
-8 TB/s HBM3e, 180 GB; the reference's spec has the same
-(quail/specs/data/devices/b200.toml:2-8). `measured_b200()` swaps in the
+Read from the TOML device specs (quail_b200/specs/data/devices: b200,
+h100-sxm, l40s, rtx-pro-6000-blackwell-server; the reference's spec format).
+B200: nominal dense peaks (bf16 2.25, fp8 4.5, fp4 9 PFLOP/s), 8 TB/s HBM3e. `measured_b200()` swaps in the
 pool's measured copy bandwidth and cuBLAS bf16 throughput when the
 driver-written MEASURED_PEAKS.json sits at the repository root.
 """
@@ -25,15 +25,19 @@ class DeviceSpec:
     page_tokens: int = 128
     usd_per_hour: float = 0.0
     sms: int = 0
+    fp32_flops: float = 0.0
+    cuda_name: str = ""
 
 
-DEVICES = {
-    "b200": DeviceSpec("b200", mem_bytes=183_359 * 2**20, hbm_bw=8e12, fp8_flops=4.5e15, bf16_flops=2.25e15,
-                       fp4_flops=9e15, page_tokens=128, usd_per_hour=6.2496, sms=148),
-    "h100-sxm": DeviceSpec("h100-sxm", mem_bytes=85_520_809_984, hbm_bw=3.35e12, fp8_flops=1.629e15,
-                           bf16_flops=0.857e15, page_tokens=16),
-    "cpu": DeviceSpec("cpu", mem_bytes=8 << 30, hbm_bw=50e9, fp8_flops=1e12, bf16_flops=1e12, page_tokens=16),
-}
+def _devices() -> dict:
+    """The TOML device specs (quail_b200/specs/data/devices) plus the host CPU."""
+    from quail_b200.specs.loading import builtin_devices
+    out = builtin_devices()
+    out["cpu"] = DeviceSpec("cpu", mem_bytes=8 << 30, hbm_bw=50e9, fp8_flops=1e12, bf16_flops=1e12, page_tokens=16)
+    return out
+
+
+DEVICES = _devices()
 
 
 def measured_b200(path: str | None = None) -> DeviceSpec:

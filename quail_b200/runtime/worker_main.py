@@ -118,13 +118,22 @@ def main():
                 from quail_b200.runtime.groups import build_group_engine, group_env
                 cfg = dict(msg["boot"])
                 t0 = time.perf_counter()
+                registry = None
+                if "decoder" in msg:
+                    # a model the session's extension registry added
+                    from quail_b200.extensions import built_in_registry
+                    from quail_b200.models.config import DecoderConfig
+                    registry = built_in_registry()
+                    d = dict(msg["decoder"])
+                    d["layer_kinds"] = tuple(d.get("layer_kinds") or ())
+                    registry.register_model(cfg["model"], DecoderConfig(**d))
                 grp = group_env()
                 if grp is not None:
                     engine = build_group_engine(EngineConfig(**cfg), *grp)
                 else:
                     from quail_b200.api.engine import ModelEngine
                     cfg["gpus"] = 1
-                    engine = ModelEngine(EngineConfig(**cfg))
+                    engine = ModelEngine(EngineConfig(**cfg), registry=registry)
                 reply = {"ready": True, "boot_s": time.perf_counter() - t0}
             elif "region" in msg:
                 import pyarrow as pa

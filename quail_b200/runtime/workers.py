@@ -108,10 +108,12 @@ class Worker:
 class WorkerPool:
     """`gpus` worker processes behind the session; same run_region as ModelEngine."""
 
-    def __init__(self, config, python: str | None = None, boot: bool = True):
+    def __init__(self, config, python: str | None = None, boot: bool = True, registry=None):
         from quail_b200.api.config import check_config, group_size
         self.config = config
-        self.cfg = check_config(config)   # the decoder config (roles, prompt layout) the workers serve
+        self.cfg = check_config(config, registry)   # the decoder config (roles, prompt layout) the workers serve
+        # a model only the session's registry knows travels to the workers as its config
+        self._decoder = None if registry is None or registry.model(config.model) is None else self.cfg
         self.n = config.gpus
         # tp / ep: `group` workers form one model copy (rank = index % group)
         self.group = group_size(config)
@@ -175,11 +177,14 @@ class WorkerPool:
                 time.sleep(0.01)
 
     def boot(self):
-        replies = self._all({"boot": _config_dict(self.config)})
+        msg = {"boot": _config_dict(self.config)}
+        if self._decoder is not None:
+            from dataclasses import asdict
+            msg["decoder"] = asdict(self._decoder)
+        replies = self._all(msg)
         self.boot_s = max(r.get("boot_s", 0.0) for r in replies)
         from quail_b200.api.tokenizer import load_tokenizer
-        from quail_b200.api.config import check_config
-        self.tokenizer = load_tokenizer(self.config.tokenizer or self.config.weights, check_config(self.config).vocab)
+        self.tokenizer = load_tokenizer(self.config.tokenizer or self.config.weights, self.cfg.vocab)
 
     def alive(self) -> bool:
         return all(_native.poll_exit(w.pid) == -1 for w in self.workers)

@@ -645,7 +645,7 @@ class Executor:
             groups.setdefault((c.preamble, node_key(c.doc_expr)), []).append(c)
         keep = np.ones(rel.num_rows, dtype=bool)
         for (_, _), cs in groups.items():
-            docs = _to_pylist(self.eval(cs[0].doc_expr, rel))
+            docs = _documents(self.eval(cs[0].doc_expr, rel), rel.num_rows)
             idx = np.nonzero(keep)[0]
             vals = self._engine_region(cs[0].preamble, [docs[i] for i in idx], cs)
             for j, i in enumerate(idx):
@@ -703,9 +703,7 @@ class Executor:
         from quail_b200.sql import guards as G
         n = rel.num_rows
         rows = [r for r in range(n) if any(c.guard is None or G.may_ask(c.guard, r) for c in cs)]
-        docs_all = _to_pylist(self.eval(cs[0].doc_expr, rel)) if n else []
-        if not isinstance(docs_all, list):
-            docs_all = [docs_all] * n
+        docs_all = _documents(self.eval(cs[0].doc_expr, rel), n) if n else []
         docs = [docs_all[r] for r in rows]
         expanded = []
         for c in cs:
@@ -1290,6 +1288,20 @@ def _distinct(t: pa.Table) -> pa.Table:
         key = json.dumps(r, default=str)
         rows.setdefault(key, i)
     return t.take(pa.array(sorted(rows.values())))
+
+
+def _documents(v, n: int) -> list:
+    """Each row's document: a string, or for a list<int> column (token ids) a numpy view of
+    the row's ids (no Python list per row: the engine takes arrays as they are)."""
+    if isinstance(v, pa.Scalar):
+        return [v.as_py()] * n
+    arr = v.combine_chunks() if isinstance(v, pa.ChunkedArray) else v
+    if pa.types.is_list(arr.type) or pa.types.is_large_list(arr.type):
+        if pa.types.is_integer(arr.type.value_type) and arr.null_count == 0:
+            flat = arr.values.to_numpy(zero_copy_only=False).astype(np.int32, copy=False)
+            offs = arr.offsets.to_numpy()
+            return [flat[offs[i]:offs[i + 1]] for i in range(len(arr))]
+    return arr.to_pylist()
 
 
 def _to_pylist(v):

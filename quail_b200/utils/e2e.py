@@ -4,7 +4,8 @@ The timed region is one `Session.sql(...).run()` of
 
     SELECT id FROM docs WHERE AI.IF(PROMPT('<16-word instruction> {0}', body))
 
-over a registered table of synthetic token-id bodies: SQL parsing and
+over a registered table of synthetic token-id bodies (by default the
+configuration's 200,000 rows, sharded over the ranks): SQL parsing and
 planning, prompt tokenization, chunk packing on the host, each chunk's
 host->device copy from pinned memory, the forward passes, and the
 device->host copy of every chunk's answers, wall-clock with a device
@@ -30,9 +31,19 @@ def run_e2e(pipe, arena, cfg, args, rank: int, world: int, dev) -> dict:
     from quail_b200.api.engine import ModelEngine
     from quail_b200.utils.synthetic import make_workload, rows_for_tokens
 
-    wl = make_workload(rows_for_tokens(args.steps * args.chunk_tokens), seed=2000 + rank)
+    total = getattr(args, "e2e_rows", None)
+    if total:
+        # the configuration's table, sharded over the ranks (each rank its 1/N of the rows)
+        rows = total // world + (1 if rank < total % world else 0)
+    else:
+        rows = rows_for_tokens(args.steps * args.chunk_tokens)
+    wl = make_workload(rows, seed=2000 + rank)
+    lens = np.fromiter((len(b) for b in wl.bodies), dtype=np.int64, count=len(wl.bodies))
+    offsets = np.zeros(len(lens) + 1, dtype=np.int32)
+    np.cumsum(lens, out=offsets[1:])
+    flat = np.concatenate(wl.bodies) if wl.bodies else np.zeros(0, np.int32)
     table = pa.table({"id": np.arange(wl.rows, dtype=np.int64),
-                      "body": pa.array([b.tolist() for b in wl.bodies], pa.list_(pa.int32()))})
+                      "body": pa.ListArray.from_arrays(pa.array(offsets), pa.array(flat, pa.int32()))})
     config = quail.EngineConfig(model=args.model, device="b200", chunk_tokens=args.chunk_tokens, tokenizer="words")
     session = quail.Session(config=config)
     engine = ModelEngine.from_replica(config, pipe, arena)
@@ -63,4 +74,5 @@ def run_e2e(pipe, arena, cfg, args, rank: int, world: int, dev) -> dict:
     return {"value": round(prompt / wall, 1), "unit": "prompt tokens/s", "rows_per_second": round(rows / wall, 1),
             "h2d_bytes_per_step": int(h2d / max(passes, 1)), "d2h_bytes_per_step": int(d2h / max(passes, 1)),
             "rows": int(rows), "kept_rows": int(kept), "passes": int(passes), "wall_s": round(wall, 3),
+            "table_rows": int(total) if total else int(rows),
             "api": "quail_b200.Session.sql(\"SELECT id FROM docs WHERE AI.IF(PROMPT(...))\").run()"}
