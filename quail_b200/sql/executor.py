@@ -720,6 +720,10 @@ class Executor:
         vals = [{} for _ in range(n)]
         for j, r in enumerate(rows):
             vals[r] = got[j]
+        self._store(cs, vals, docs_all)
+
+    def _store(self, cs: list[BoundCall], vals: list[dict], docs_all: list) -> None:
+        """Typed Arrow values of calls `cs` from per-row answer dicts (None where not asked)."""
         for c in cs:
             if c.kind == "extract":
                 out = []
@@ -852,10 +856,14 @@ class Executor:
                 size_hint *= 2
             part = rel.take(pa.array(np.arange(start, start + size, dtype=np.int64))) if size < n else rel
             start += size
-            kept = self.apply_ai_conjuncts(part, ai)
+            fused = self._filters_with_riders(part, ai, node)
+            if fused is not None:
+                kept, pre = fused
+            else:
+                kept, pre = self.apply_ai_conjuncts(part, ai), None
             tried += part.num_rows
             passed += kept.num_rows
-            out = self._project(kept, node)
+            out = self._project(kept, node, pre)
             lo, hi = emitted, emitted + out.num_rows
             emitted = hi
             a = max(off - lo, 0)
@@ -866,10 +874,62 @@ class Executor:
             if need is not None and emitted >= need:
                 break
 
-    def _project(self, rel: Relation, node) -> pa.Table:
-        """The SELECT list of a non-aggregating query over `rel` (its model calls asked on demand)."""
-        items = node["items"]
+    def _filters_with_riders(self, rel: Relation, ai: list, node):
+        """WHERE AI.IF chain and the SELECT list's calls on the same document in one region.
+
+        When every model conjunct is an AI.IF over one document (one instruction
+        layout), the projection's calls on that document ride in the same region:
+        asked as follow-up questions right after the filters kept the row, while
+        its document's KV is still resident (the reference runs a chain's
+        operators in the same passes, quail/backends/quail/executor/region.py).
+        Returns (kept rows, their projection values) or None when it does not apply.
+        """
+        from quail_b200.planner.search import doc_tokens, order_filters
+        from quail_b200.sql import guards as G
+        if not ai or rel.num_rows == 0:
+            return None
+        filters = []
+        for c in ai:
+            inner = c["args"][0] if c.get("type") == "call" and c["name"] == "HINT" else c
+            if not (is_model_call(inner) and inner["name"] in ("AI.IF", "AI_FILTER")):
+                return None
+            filters.append(bind_call(inner, self.turn, self.model))
+        key = (filters[0].preamble, node_key(filters[0].doc_expr))
+        if any((f.preamble, node_key(f.doc_expr)) != key for f in filters):
+            return None
+        demand = G.Demand(self, rel, enabled=self.pushdown)
+        for it in node["items"]:
+            demand.visit(it["expr"])
+        riders = {}
+        for k, (call_node, guard) in demand.guards.items():
+            b = bind_call(call_node, self.turn, self.model)
+            if (b.preamble, node_key(b.doc_expr)) != key or b.kind == "extract":
+                continue
+            b.drops = False
+            b.guard = None if guard["op"] == "true" else guard
+            riders[k] = b
+        riders = {k: b for k, b in riders.items() if G.calls_of(b.guard) <= set(riders)}
+        if not riders:
+            return None
+        order = order_filters([doc_tokens(b.tail) for b in filters],
+                              [b.selectivity if b.selectivity is not None else 0.5 for b in filters])
+        chain = [filters[i] for i in order] + _in_dependency_order(list(riders), riders)
+        docs = _documents(self.eval(filters[0].doc_expr, rel), rel.num_rows)
+        vals = self._engine_region(key[0], docs, chain)
+        keep = [all(v.get(f.key, False) for f in filters) for v in vals]
+        idx = [i for i, k in enumerate(keep) if k]
+        kept = rel.filter(pa.array(keep))
+        saved = self.ai_values
         self.ai_values = {}
+        self._store(list(riders.values()), [vals[i] for i in idx], [docs[i] for i in idx])
+        pre, self.ai_values = self.ai_values, saved
+        return kept, pre
+
+    def _project(self, rel: Relation, node, pre: dict | None = None) -> pa.Table:
+        """The SELECT list of a non-aggregating query over `rel` (its model calls asked on demand;
+        `pre` holds values some calls already got, aligned with `rel`)."""
+        items = node["items"]
+        self.ai_values = dict(pre or {})
         self.compute_ai(rel, [it["expr"] for it in items])
         names, arrays = [], []
         for it in items:

@@ -245,3 +245,17 @@ def test_a_first_call_left_out_on_a_row_still_reads_the_document(session):
         else:
             assert a_on is None
     assert on.report["asked"] < off.report["asked"]
+
+
+def test_projection_calls_ride_in_the_filter_region(session):
+    # the WHERE filter and the SELECT list's calls on the same document run as one region:
+    # the document is prefilled once, and the score is asked only where the filter kept the row
+    q = ("SELECT id, AI.SCORE(PROMPT('Is the review positive? {0}', body)) AS s FROM reviews "
+         "WHERE AI.IF(PROMPT('Does the review discuss the ending? {0}', body)) ORDER BY id")
+    res = session.sql(q).run()
+    assert len(res.report["regions"]) == 1
+    kept = res.table.num_rows
+    assert res.report["asked"] == 24 + kept
+    alone = session.sql("SELECT id FROM reviews WHERE AI.IF(PROMPT('Does the review discuss the ending? {0}', "
+                        "body)) ORDER BY id").collect()
+    assert res.table.column("id").to_pylist() == alone.column("id").to_pylist()
