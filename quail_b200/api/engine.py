@@ -70,6 +70,8 @@ class ModelEngine:
         self.model = model
         self.arena = arena
         self.executor = StageExecutor(model, arena, self.chunk_tokens, gpu_timing=config.gpu_timing)
+        self.retention = bool(config.extra.get("retention", True))
+        self._retained_keys = set()
         return self
 
     def __init__(self, config: EngineConfig, device_index: int = 0, pages: int | None = None, registry=None):
@@ -87,6 +89,9 @@ class ModelEngine:
         from quail_b200.planner.budgets import Budgets
         self.budgets = Budgets.for_model(self.cfg, config.device, gpus=1)
         self.chunk_tokens = config.chunk_tokens or self.budgets.chunk_tokens
+        # keep finished documents' KV for later regions (evicted first under memory pressure)
+        self.retention = bool(config.extra.get("retention", True))
+        self._retained_keys = set()
         self._build(pages)
 
     # ------------------------------------------------------------ model
@@ -310,8 +315,18 @@ class ModelEngine:
                               asked_stop if stop is not None else None) if f is not None]
         ex.should_stop = (lambda: any(f() for f in checks)) if checks else None
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
-        run = RegionRun(ex, tok.encode(preamble), uniq, rcalls, answer_width=len(answer),
+        reused0, replays0 = ex.stats.reused, ex.stats.replays
+        prefix_ids = tok.encode(preamble)
+        run = RegionRun(ex, prefix_ids, uniq, rcalls, answer_width=len(answer),
                         decision=getattr(self.model, "decision", None))
+        if self.retention:
+            # document KV stays in the arena for later regions with the same instruction prefix
+            import hashlib
+            ph = hashlib.blake2b(np.asarray(prefix_ids, np.int32).tobytes(), digest_size=8).hexdigest()
+            keys = [("ret", ph, hashlib.blake2b(u.tobytes(), digest_size=12).hexdigest()) for u in uniq]
+            run.retain_key = lambda r: keys[r]
+            run.retained_earlier = frozenset(self._retained_keys)
+            self._retained_keys.update(keys)
         rows_of: dict = {}
         for i, u in enumerate(where):
             rows_of.setdefault(u, []).append(i)
@@ -355,7 +370,8 @@ class ModelEngine:
         values = [sql_values(u) for u in where]
         del results
         stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
-                 "documents": len(uniq), "rows": len(docs), "asked": run.asked}
+                 "documents": len(uniq), "rows": len(docs), "asked": run.asked,
+                 "reused_documents": ex.stats.reused - reused0, "replays": ex.stats.replays - replays0}
         return RegionOutput(values=values, stats=stats)
 
     def run_pairs(self, preamble: str, anchors: list, pairs: list, call: CallSpec) -> RegionOutput:

@@ -147,6 +147,28 @@ class PagePool:
         if pages is not None:
             self._drop(pages)
 
+    def rewind(self, key, tokens: int) -> None:
+        """Trim a resident key back to its first `tokens` tokens and release the pages past them
+        (pages a reader still holds stay held until it is freed)."""
+        have = self.owned[key]
+        keep = self.pages_needed(tokens)
+        if keep < len(have):
+            self._drop(have[keep:])
+            del have[keep:]
+        self.tokens[key] = min(self.tokens[key], tokens)
+
+    def adopt(self, old, new) -> None:
+        """Give a resident key's pages, holds and state slot to a new key (no longer retained)."""
+        if new in self.owned:
+            raise KeyError(f"{new!r} already resident")
+        self.owned[new] = self.owned.pop(old)
+        self.tokens[new] = self.tokens.pop(old)
+        self.borrows[new] = self.borrows.pop(old, [])
+        if old in self.slot_of:
+            self.slot_of[new] = self.slot_of.pop(old)
+            self.slot_borrows[new] = self.slot_borrows.pop(old, [])
+        self.retained.pop(old, None)
+
     def retain(self, key) -> None:
         self.retained[key] = None
         self.retained.move_to_end(key)

@@ -118,6 +118,11 @@ class RegionRun:
         self.drafted = 0                      # draft tokens accepted (copy-constrained extraction)
         self.progress = None                  # utils.progress.Count advanced as each row finishes
         self.on_finish = None                 # on_finish(r): row r's chain is done (streamed answers)
+        # retention across regions: retain_key(r) names row r's document KV for later regions (None:
+        # free it); a document found retained is not prefilled again, one whose KV was evicted
+        # is recomputed (a replay)
+        self.retain_key = None
+        self._resident_doc = [False] * len(docs)
         # columns after the answer rows in a full readout: argmax, lse
         self.nans = answer_width
 
@@ -126,7 +131,7 @@ class RegionRun:
         """(own key, reads, position of the first own token, own length) of call ci's question."""
         P = len(self.prefix)
         doc_len = len(self.docs[r])
-        if ci == 0:
+        if ci == 0 and not self._resident_doc[r]:
             return ("doc", r), [(PREFIX_KEY, P)], P, doc_len + len(self.calls[0].suffix)
         reads = [(PREFIX_KEY, P), (("doc", r), doc_len)] if doc_len else [(PREFIX_KEY, P)]
         return ("q", r, ci), reads, P + doc_len, len(self.calls[ci].suffix)
@@ -317,8 +322,12 @@ class RegionRun:
 
     # ------------------------------------------------------------ scheduling
     def _finish_call(self, r: int, ci: int) -> None:
-        if ci > 0:
+        if ci > 0 or self._resident_doc[r]:
             self.ex.free(("q", r, ci))
+        elif self.calls[0].kind in ("map", "extract") and len(self.calls) > 1 and not self.ex.pool.state_slots:
+            # KV rewind: the first call decoded into the document's own pages; the later
+            # questions read only the document, so its generated tokens' pages go back
+            self.ex.rewind(("doc", r), len(self.docs[r]))
         for li in range(len(self.calls[ci].labels)):
             if self.ex.pool.resident(("lab", r, ci, li)):
                 self.ex.free(("lab", r, ci, li))
@@ -340,7 +349,12 @@ class RegionRun:
             ci = self._next[r]
             if not res.kept or ci >= len(self.calls):
                 if self.ex.pool.resident(("doc", r)):
-                    self.ex.free(("doc", r))
+                    keep = self.retain_key(r) if self.retain_key is not None else None
+                    if keep is not None and not self.ex.pool.state_slots and len(self.docs[r]):
+                        self.ex.rewind(("doc", r), len(self.docs[r]))
+                        self.ex.retain(("doc", r), keep)
+                    else:
+                        self.ex.free(("doc", r))
                 if self.progress is not None:
                     self.progress.advance()
                 if self.on_finish is not None:
@@ -394,7 +408,24 @@ class RegionRun:
         self.fresh_tokens += P
         self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
         first = self.calls[0]
+        pinned, cap = 0, self.ex.pool.num_pages // 2
         for r, doc in enumerate(self.docs):
+            if self.retain_key is not None and len(doc) and not self.ex.pool.state_slots:
+                rk = self.retain_key(r)
+                if rk is not None and self.ex.pool.resident(rk):
+                    need = self.ex.pool.pages_needed(len(doc))
+                    if pinned + need <= cap and self.ex.claim(rk, ("doc", r)):
+                        # this document's KV is already in the arena: only its questions run
+                        pinned += need
+                        self._resident_doc[r] = True
+                        self.ex.stats.reused += 1
+                        self._next[r] = 0
+                        self._pending[r] = 0
+                        self._advance(r)
+                        continue
+                elif rk is not None and rk in self.retained_earlier:
+                    # retained by an earlier region, evicted since: computed again
+                    self.ex.stats.replays += 1
             if not self._asks(r, 0):
                 # the first call is not asked on this row: its document alone, then the rest
                 self._next[r] = 1
@@ -421,6 +452,8 @@ class RegionRun:
     def _doc_only(self, r: int) -> None:
         self._pending[r] = 0
         self._advance(r)
+
+    retained_earlier: frozenset = frozenset()   # keys earlier regions retained (to count replays)
 
     def run(self):
         self.submit_all()

@@ -88,6 +88,9 @@ class ExecutorStats:
     h2d_bytes: int = 0
     d2h_bytes: int = 0
     wall_s: float = 0.0
+    evictions: int = 0          # retained keys freed to make room
+    reused: int = 0             # documents a region found retained (no prefill)
+    replays: int = 0            # documents a region recomputed because their retained KV was evicted
 
 
 class StageExecutor:
@@ -140,6 +143,34 @@ class StageExecutor:
         self.pool.free_key(key)
         self.written.pop(key, None)
 
+    def rewind(self, key, tokens: int) -> None:
+        """Trim a key to its first `tokens` tokens (KV rewind: a decode's own tokens dropped once
+        no one reads them), releasing the pages past them."""
+        self.pool.rewind(key, tokens)
+        if key in self.written:
+            self.written[key] = min(self.written[key], tokens)
+
+    def retain(self, key, as_key) -> None:
+        """Keep a finished key's KV under `as_key` for a later region; it is evicted (freed) first
+        when the arena runs short, and a region that needs it then recomputes it."""
+        self.pool.adopt(key, as_key)
+        self.written[as_key] = self.written.pop(key, self.pool.tokens[as_key])
+        self.pool.retain(as_key)
+
+    def claim(self, retained_key, key) -> bool:
+        """Take a retained key's KV for `key` (pinned again: not evictable); False if it was evicted."""
+        if not self.pool.resident(retained_key):
+            self.written.pop(retained_key, None)
+            return False
+        self.pool.adopt(retained_key, key)
+        self.written[key] = self.written.pop(retained_key, self.pool.tokens[key])
+        return True
+
+    def _evict(self, pages: int) -> None:
+        for key in self.pool.evict_retained(pages):
+            self.written.pop(key, None)
+            self.stats.evictions += 1
+
     # ------------------------------------------------------------ admission
     def _readable(self, task: Task) -> bool:
         return all(self.written.get(k, -1) >= n for k, n in task.reads)
@@ -158,7 +189,7 @@ class StageExecutor:
             if n > room:
                 break
             if pool.tokens[task.key] < total and pool.grow(task.key, total) is None:
-                pool.evict_retained(pool.pages_needed(total))
+                self._evict(pool.pages_needed(total))
                 if pool.grow(task.key, total) is None:
                     break
             cont.popleft()
@@ -191,7 +222,7 @@ class StageExecutor:
                 cap = total + task.reserve_tokens
                 pages = self.pool.alloc(task.key, total, cap)
                 if pages is None:
-                    self.pool.evict_retained(self.pool.pages_needed(cap))
+                    self._evict(self.pool.pages_needed(cap))
                     pages = self.pool.alloc(task.key, total, cap)
                 if pages is None:
                     # keep new work in FIFO order under memory pressure, but
@@ -204,7 +235,7 @@ class StageExecutor:
             elif self.pool.tokens[task.key] < total:
                 # a continuation (decode step, prefill piece) of a resident key
                 if self.pool.grow(task.key, total) is None:
-                    self.pool.evict_retained(self.pool.pages_needed(total))
+                    self._evict(self.pool.pages_needed(total))
                     if self.pool.grow(task.key, total) is None:
                         deferred.append(task)
                         stop = True

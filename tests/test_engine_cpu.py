@@ -309,3 +309,73 @@ def test_extract_trace_lines(tmp_path, monkeypatch):
     recs = [json.loads(ln) for ln in path.read_text().splitlines()]
     assert recs[0]["step"] == 0 and recs[0]["chosen"] == 10 and recs[0]["positions"] == 1
     assert recs[-1]["chosen"] == 99
+
+
+def _score_engine(pages=None, retention=True):
+    import quail_b200 as quail
+    from quail_b200.api.engine import ModelEngine
+    cfg = quail.EngineConfig(model="qwen3-tiny", device="cpu", chunk_tokens=96,
+                             extra={"retention": retention})
+    return ModelEngine(cfg, pages=pages)
+
+
+def _score(engine, question, docs):
+    from quail_b200.api.engine import CallSpec
+    from quail_b200.api.prompts import bind_prompt
+    bp = bind_prompt(question + " {0}")
+    out = engine.run_region(bp.preamble, docs, [CallSpec(kind="score", tail=bp.tail, name="s")])
+    return [v["s"] for v in out.values], out.stats
+
+
+def _docs(n=14, seed=4):
+    rng = np.random.default_rng(seed)
+    words = ["alpha", "beta", "gamma", "delta", "omega", "kappa"]
+    return [" ".join(rng.choice(words, size=int(rng.integers(10, 40)))) for _ in range(n)]
+
+
+def test_retained_documents_are_read_again_without_a_prefill():
+    docs = _docs()
+    plain = _score_engine(retention=False)
+    want1, _ = _score(plain, "Is it greek?", docs)
+    want2, _ = _score(plain, "Is it long?", docs)
+    eng = _score_engine()
+    got1, st1 = _score(eng, "Is it greek?", docs)
+    got2, st2 = _score(eng, "Is it long?", docs)
+    assert st1["reused_documents"] == 0
+    assert st2["reused_documents"] == len(docs) and st2["replays"] == 0
+    assert st2["fresh_tokens"] < st1["fresh_tokens"]
+    np.testing.assert_allclose(got1, want1, atol=1e-5)
+    np.testing.assert_allclose(got2, want2, atol=1e-5)
+    eng.arena.pool.check()
+
+
+def test_evicted_documents_are_replayed_on_a_tiny_arena():
+    docs = _docs(30, seed=5)
+    plain = _score_engine(retention=False)
+    want, _ = _score(plain, "Is it long?", docs)
+    eng = _score_engine(pages=40)                   # far less than the 30 documents' pages
+    _score(eng, "Is it greek?", docs)
+    got, st = _score(eng, "Is it long?", docs)
+    assert st["replays"] > 0 and st["reused_documents"] + st["replays"] == len(docs)
+    np.testing.assert_allclose(got, want, atol=1e-5)
+    eng.arena.pool.check()
+
+
+def test_rewind_releases_a_first_decode_before_later_questions():
+    from quail_b200.api.engine import CallSpec
+    from quail_b200.api.prompts import bind_map_prompt, bind_prompt
+    docs = _docs(8, seed=6)
+    bm = bind_map_prompt("Name one word.")
+    bs = bind_prompt("Is it greek? {0}")
+    calls = [CallSpec(kind="map", tail=bm.tail, name="m", max_tokens=6), CallSpec(kind="score", tail=bs.tail, name="s")]
+    eng = _score_engine(retention=False)
+    out = eng.run_region(bm.preamble, docs, calls)
+    # the same follow-up after a first question that generates nothing reads the same KV
+    alone = _score_engine(retention=False)
+    first = CallSpec(kind="score", tail=bm.tail, name="x")
+    want_s = [v["s"] for v in alone.run_region(bm.preamble, docs, [first, calls[1]]).values]
+    want_m = alone.run_region(bm.preamble, docs, calls[:1]).values
+    np.testing.assert_allclose([v["s"] for v in out.values], want_s, atol=1e-5)
+    assert [v["m"] for v in out.values] == [v["m"] for v in want_m]
+    eng.arena.pool.check()
+    assert not eng.arena.pool.owned                  # every key released at the end
