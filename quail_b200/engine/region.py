@@ -409,8 +409,10 @@ class RegionRun:
         self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
         first = self.calls[0]
         pinned, cap = 0, self.ex.pool.num_pages // 2
+        # a first call that reads every own token (max-pooled features) needs the document computed
+        reusable = not (first.kind == "features" and first.pooling == "max")
         for r, doc in enumerate(self.docs):
-            if self.retain_key is not None and len(doc) and not self.ex.pool.state_slots:
+            if self.retain_key is not None and reusable and len(doc) and not self.ex.pool.state_slots:
                 rk = self.retain_key(r)
                 if rk is not None and self.ex.pool.resident(rk):
                     need = self.ex.pool.pages_needed(len(doc))

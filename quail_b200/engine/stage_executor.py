@@ -153,6 +153,8 @@ class StageExecutor:
     def retain(self, key, as_key) -> None:
         """Keep a finished key's KV under `as_key` for a later region; it is evicted (freed) first
         when the arena runs short, and a region that needs it then recomputes it."""
+        if self.pool.resident(as_key):
+            self.free(as_key)          # an older copy of the same document's KV
         self.pool.adopt(key, as_key)
         self.written[as_key] = self.written.pop(key, self.pool.tokens[as_key])
         self.pool.retain(as_key)
