@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--chunk-tokens", type=int, default=16384)
     ap.add_argument("--pages", type=int, default=1024)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-rows", type=int, default=200_000,
+                    help="rows of the end-to-end query's table over all ranks (the configuration's 200k)")
     ap.add_argument("--profile-pass", action="store_true",
                     help="after the timed steps, run one more pass between cudaProfilerStart/Stop "
                          "(for `ncu --profile-from-start off`); it is not timed")

@@ -41,6 +41,7 @@ class CallSpec:
     pooling: str = "last"     # features: "last" or "max"
     segments: list | None = None   # tail tokenized piece by piece (decision prompts); joins to `tail`
     read: list = field(default_factory=list)   # segments whose last token the decision head reads
+    letters: list = field(default_factory=list)  # lettered prompts: option i's answer letter (slot_lm)
     drops: bool = True        # filter: FALSE drops the row from the region (WHERE); else a value only
     # demand guard (quail_b200.sql.guards): the call is asked on an input row only where
     # this formula is TRUE; its `ai` leaves name earlier calls of the same list
@@ -106,7 +107,7 @@ class ModelEngine:
 
     def _attach_head(self, ckpt) -> None:
         """A decision model's option-scoring head, kept in fp32 beside the backbone."""
-        if self.cfg.role == "decision":
+        if self.cfg.decision_head:
             from quail_b200.models.decision import DecisionHead, head_tensors
             self.model.decision = DecisionHead(head_tensors(ckpt), self.device)
 
@@ -257,11 +258,14 @@ class ModelEngine:
                        else f"{self.cfg.name} serves AI.SAE_FEATURES only")
                 raise RefusalError(Refusal(reasons=(why,), constraint="unsupported_function"))
         decision = self.cfg.role == "decision"
+        lettered = self.cfg.readout == "slot_lm"
         for c in calls:
             why = None
-            if decision and c.segments is None:
+            if lettered and not c.letters:
+                why = f"{c.kind} is not a call {self.cfg.name!r} answers: it answers with an option letter"
+            elif decision and not lettered and c.segments is None:
                 why = f"{c.kind} is not a call {self.cfg.name!r} answers: its head scores listed options"
-            elif not decision and c.segments is not None:
+            elif not decision and (c.segments is not None or c.letters):
                 why = f"an option-scoring prompt needs a decision model, not {self.cfg.name!r}"
             elif self.cfg.role == "reranker" and c.kind != "score":
                 why = "a reranker model can only be used with AI.SCORE"
@@ -286,7 +290,21 @@ class ModelEngine:
                 rc.after = tuple(j for j, o in enumerate(calls) if o.name in deps)
                 rc.when = (lambda r, vals, g=c.guard:
                            G.asks(g, rep[r], self._sql_values(calls, vals, G.calls_of(g))))
-            if offsets:
+            if c.letters:
+                # the slot_lm readout: the LM head's logit of each option's letter at the last row
+                ids = []
+                for code in c.letters:
+                    t = tok.encode(code)
+                    if len(t) != 1:
+                        raise RefusalError(Refusal(
+                            reasons=(f"option code {code!r} is not one token of this tokenizer",),
+                            constraint="unsupported_function"))
+                    ids.append(int(t[0]))
+                if c.kind in ("filter", "score"):
+                    rc.true_cols, rc.false_cols = [col(ids[0])], [col(ids[1])]
+                else:
+                    rc.letter_cols = [col(i) for i in ids]
+            elif offsets:
                 pass
             elif c.kind in ("filter", "score"):
                 rc.true_cols = [col(i) for i in true_ids]
@@ -317,8 +335,15 @@ class ModelEngine:
         passes0, tok0 = ex.stats.passes, ex.stats.tokens
         reused0, replays0 = ex.stats.reused, ex.stats.replays
         prefix_ids = tok.encode(preamble)
-        run = RegionRun(ex, prefix_ids, uniq, rcalls, answer_width=len(answer),
-                        decision=getattr(self.model, "decision", None))
+        if self.cfg.bidirectional:
+            # document-isolated: the preamble and the layout's close are part of every document's block
+            close = (tok.encode(P.MAMMOTH_DOCUMENT_CLOSE) if self.cfg.prompt_layout == "mammoth"
+                     else np.zeros(0, np.int32))
+            blocks = [np.concatenate([prefix_ids, u, close]).astype(np.int32) for u in uniq]
+            run = RegionRun(ex, np.zeros(0, np.int32), blocks, rcalls, answer_width=len(answer), isolated=True)
+        else:
+            run = RegionRun(ex, prefix_ids, uniq, rcalls, answer_width=len(answer),
+                            decision=getattr(self.model, "decision", None))
         if self.retention:
             # document KV stays in the arena for later regions with the same instruction prefix
             import hashlib
@@ -377,7 +402,11 @@ class ModelEngine:
     def run_pairs(self, preamble: str, anchors: list, pairs: list, call: CallSpec) -> RegionOutput:
         """An AI join's region: anchor documents (each prefilled once) and (anchor index, other
         document) pairs; `call` (AI.IF or AI.SCORE) is asked once per pair. Values per pair."""
+        from quail_b200.api.config import Refusal, RefusalError
         from quail_b200.engine.region import Call, PairRun
+        if self.cfg.role != "generative":
+            raise RefusalError(Refusal(reasons=(f"an AI join's pair questions need a generative model, not "
+                                                f"{self.cfg.name!r}",), constraint="unsupported_function"))
         tok = self.tokenizer
         true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
         false_ids = tok.answer_ids(P.FALSE_SPELLINGS)

@@ -207,6 +207,30 @@ RERANKER_SYSTEM = ("You are an expert at text analysis. Judge whether the Docume
 RERANKER_INSTRUCTION = "Judge whether the document meets the requirements in the query."
 
 
+# Base Labs' mammoth-1 / elephant-1 layout (crates/quail-planner/src/prompts.rs:131-140 and
+# 191-201): the system turn and the document in a state block, then the question with lettered
+# options and an answer line. A filter asks yes / no as options A and B. These strings are the
+# checkpoints' interface, so they are the reference's, character for character.
+MAMMOTH_DOCUMENT_LABEL = "<state>\n"
+MAMMOTH_DOCUMENT_CLOSE = "\n</state>\n\n"
+MAMMOTH_QUESTION_LABEL = "Question: "
+MAMMOTH_OPTIONS_LABEL = "\n\nOptions:"
+MAMMOTH_CLOSING = "\n\nAnswer with one letter: {letters}."
+MAMMOTH_LABEL_CLOSING = "\n\nAnswer with one label: {letters}."
+MAMMOTH_FILTER_END = ("\n\nOptions:\nA. yes: the statement is true / the answer is yes"
+                      "\nB. no: the statement is false / the answer is no\n\nAnswer with one letter: A, B.")
+MAMMOTH_EMPTY_QUESTION = "Which option applies to the state?"
+MAX_LETTERS = 255          # the most options one coded prompt lists
+
+
+def code_candidates(n: int) -> list[str]:
+    """The first n option codes: A to Z, then AA, AB, ... ZZ."""
+    import string
+    upper = list(string.ascii_uppercase)
+    codes = upper + [a + b for a in upper for b in upper]
+    return codes[:n]
+
+
 @dataclass(frozen=True)
 class PromptModel:
     """What the binder needs to know of a model: its role, prompt layout and chat turn."""
@@ -221,6 +245,8 @@ def prompt_model(cfg) -> PromptModel:
     """The prompt model of a decoder config: rerankers and decision models bring their own text."""
     role = getattr(cfg, "role", "generative")
     turn = Turn(prefix="", suffix="") if role in ("reranker", "decision") else Turn()
+    if getattr(cfg, "turn_prefix", None) is not None:
+        turn = Turn(prefix=cfg.turn_prefix, suffix=turn.suffix)
     return PromptModel(role=role, layout=getattr(cfg, "prompt_layout", "ai-if"), turn=turn,
                        name=getattr(cfg, "name", ""))
 
@@ -275,6 +301,50 @@ def bind_decision_choice_prompt(template: str | None, labels: list[str], descrip
     return SegmentedPrompt(kind="classify", template=template or "", preamble=turn.prefix + DECISION2_DOCUMENT_LABEL,
                            tail="".join(segments), question=question, labels=list(labels),
                            descriptions=descriptions, segments=segments, read=list(range(1, len(labels) + 1)))
+
+
+@dataclass
+class LetteredPrompt(BoundPrompt):
+    """A prompt answered by the LM head's logits of option letters at its last row (the
+    slot_lm readout): option i is `letters[i]`; a filter's options are yes (A), then no (B)."""
+
+    letters: list = field(default_factory=list)
+
+
+def bind_mammoth_prompt(template: str, kind: str, turn: Turn = Turn(prefix="", suffix="")) -> LetteredPrompt:
+    """AI.IF / AI.SCORE in the mammoth layout: the question, then options A (yes) and B (no)."""
+    base = bind_prompt(template, 1, turn)
+    question = base.question or MAMMOTH_EMPTY_QUESTION
+    tail = MAMMOTH_QUESTION_LABEL + question + MAMMOTH_FILTER_END + turn.suffix
+    return LetteredPrompt(kind=kind, template=template, preamble=turn.prefix + MAMMOTH_DOCUMENT_LABEL, tail=tail,
+                          question=question, letters=["A", "B"])
+
+
+def bind_mammoth_choice_prompt(template: str | None, labels: list[str], descriptions: list[str] | None = None,
+                               task_description: str = "",
+                               turn: Turn = Turn(prefix="", suffix="")) -> LetteredPrompt:
+    """AI.CLASSIFY in the mammoth layout: one coded line per label, then the answer line
+    (prompts.rs choice_segments: a two-letter code asks for "one label")."""
+    if len(labels) > MAX_LETTERS:
+        raise PromptError(f"a coded prompt takes at most {MAX_LETTERS} options, got {len(labels)}")
+    if template:
+        question, rest = split_frame(template)
+        question = (question + ("\n\n" + rest.strip() if rest.strip() else "")).strip()
+    else:
+        question = ""
+    if task_description:
+        question = f"{question}\n{task_description}" if question else task_description
+    question = question or MAMMOTH_EMPTY_QUESTION
+    descriptions = list(descriptions or [])
+    letters = code_candidates(len(labels))
+    lines = "".join(f"\n{code}. {label}: {descriptions[i]}" if i < len(descriptions) and descriptions[i]
+                    else f"\n{code}. {label}" for i, (code, label) in enumerate(zip(letters, labels)))
+    closing = MAMMOTH_LABEL_CLOSING if any(len(c) > 1 for c in letters) else MAMMOTH_CLOSING
+    tail = (MAMMOTH_QUESTION_LABEL + question + MAMMOTH_OPTIONS_LABEL + lines
+            + closing.replace("{letters}", ", ".join(letters)) + turn.suffix)
+    return LetteredPrompt(kind="classify", template=template or "", preamble=turn.prefix + MAMMOTH_DOCUMENT_LABEL,
+                          tail=tail, question=question, labels=list(labels), descriptions=descriptions,
+                          letters=letters)
 
 
 def reranker_text(query: str, document: str) -> str:

@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(HPB * 64)
   const int kvh = head0 / (QH / KH);
   const int* sd = seqs + seq * kSeqDescInts;
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
+  const bool bidir = (sd[3] & 1) != 0;   // own segment read both ways (document-isolated block)
   int seg_len[kMaxSeg], seg_off[kMaxSeg];
 #pragma unroll
   for (int i = 0; i < kMaxSeg; ++i) {
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(HPB * 64)
 #pragma unroll
   for (int i = 0; i < kMaxSeg; ++i) {
     int visible = seg_len[i];
-    if (i == nseg - 1) visible = min(visible, max_pos + 1);
+    if (i == nseg - 1 && !bidir) visible = min(visible, max_pos + 1);
     seg_tiles[i] = i < nseg ? (visible + BKV - 1) / BKV : 0;
   }
   int total_tiles = 0;
@@ -220,7 +221,7 @@ __global__ void __launch_bounds__(HPB * 64)
 #pragma unroll
     for (int i = 1; i < kMaxSeg; ++i)
       if (s == i) slen = seg_len[i];
-    const bool causal = (s == nseg - 1);
+    const bool causal = (s == nseg - 1) && !bidir;
 
     const uint32_t kb = sK0 + buf * BKV * 256, vb = sV0 + buf * BKV * 256;
     float sacc[8][4];

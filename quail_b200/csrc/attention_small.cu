@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
   }
   const int* sd = seqs + seq * kSmSeqInts;
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
+  const bool bidir = (sd[3] & 1) != 0;   // own segment read both ways (document-isolated block)
   if (q0 >= q_len) return;
   const int kvh = blockIdx.y, h0 = kvh * G;
   int seg_len[kSmMaxSeg], seg_off[kSmMaxSeg], seg_blocks[kSmMaxSeg];
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
 #pragma unroll
   for (int i = 0; i < kSmMaxSeg; ++i) {
     int vis = seg_len[i];
-    if (i == nseg - 1) vis = min(vis, first_pos + rows_tok);
+    if (i == nseg - 1 && !bidir) vis = min(vis, first_pos + rows_tok);
     seg_blocks[i] = i < nseg ? (vis + kSmBk - 1) / kSmBk : 0;
     total += seg_blocks[i];
   }
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
 #pragma unroll
     for (int i = 1; i < kSmMaxSeg; ++i)
       if (s_idx == i) slen = seg_len[i];
-    const bool own = s_idx == nseg - 1;
+    const bool own = s_idx == nseg - 1 && !bidir;
     const uint32_t ks = sbase + (st * 2 + 0) * SM::kBuf, vs = sbase + (st * 2 + 1) * SM::kBuf;
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll

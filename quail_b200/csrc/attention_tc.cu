@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(160, 2)
   const int kvh = head0 / (QH / KH);
   const int* sd = seqs + seq * kSeqInts;
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
+  const bool bidir = (sd[3] & 1) != 0;   // own segment read both ways (document-isolated block)
   int seg_len[kMaxSegTc], seg_off[kMaxSegTc], seg_tiles[kMaxSegTc];
 #pragma unroll
   for (int i = 0; i < kMaxSegTc; ++i) {
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(160, 2)
 #pragma unroll
   for (int i = 0; i < kMaxSegTc; ++i) {
     int visible = seg_len[i];
-    if (i == nseg - 1) visible = min(visible, max_pos + 1);
+    if (i == nseg - 1 && !bidir) visible = min(visible, max_pos + 1);
     seg_tiles[i] = i < nseg ? (visible + kTcBkv - 1) / kTcBkv : 0;
     total += seg_tiles[i];
   }
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(160, 2)
 #pragma unroll
       for (int i = 1; i < kMaxSegTc; ++i)
         if (s == i) slen = seg_len[i];
-      const bool causal = (s == nseg - 1);
+      const bool causal = (s == nseg - 1) && !bidir;
       if (!mbar_wait(s_full, ph, err, kErrTimeoutEpilogue)) {
         ok = false;
         break;

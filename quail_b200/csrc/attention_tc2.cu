@@ -102,6 +102,7 @@ __device__ __forceinline__ uint8_t ue8m0_att(float amax) {
 // The geometry of one work item, computed alike by every role.
 struct Item {
   int q_start, q_len, nseg, own_len, q0, head0, kvh;
+  bool bidir;       // own segment read both ways (a document-isolated block)
   int seg_len[kMaxSeg], seg_off[kMaxSeg];
   int rows[2];      // valid query tokens of tiles A and B (0..32)
   int n[2];         // K/V tiles each tile reads
@@ -119,6 +120,7 @@ __device__ __forceinline__ void load_item(Item& it, int item, const int* __restr
   it.q_start = sd[0];
   it.q_len = sd[1];
   it.nseg = sd[2];
+  it.bidir = (sd[3] & 1) != 0;
 #pragma unroll
   for (int i = 0; i < kMaxSeg; ++i) {
     it.seg_len[i] = i < it.nseg ? sd[4 + i] : 0;
@@ -141,7 +143,7 @@ __device__ __forceinline__ void load_item(Item& it, int item, const int* __restr
       it.n[t] = 0;
     } else {
       const int max_pos = it.own_len - it.q_len + first + it.rows[t] - 1;  // own-segment position
-      const int visible = min(it.own_len, max_pos + 1);
+      const int visible = it.bidir ? it.own_len : min(it.own_len, max_pos + 1);
       it.n[t] = before + (visible + kBkv - 1) / kBkv;
     }
     it.nmax = max(it.nmax, it.n[t]);
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s == i) slen = it.seg_len[i];
         const int j0 = tt * kBkv;
         int lim = slen - j0;
-        if (s == it.nseg - 1) lim = min(lim, pos - j0 + 1);
+        if (s == it.nseg - 1 && !it.bidir) lim = min(lim, pos - j0 + 1);
         if (!valid) lim = 0;
         float tmax = -INFINITY;
 #pragma unroll

@@ -4,7 +4,8 @@ A chunk is the unit the GPU runs: up to `chunk_tokens` new tokens from many
 sequences, plus the metadata the kernels read:
 
   ids, positions, slots   [T] int32  token id, absolute position, KV slot (page*P + offset; -1 = none)
-  seqs                    [S, 12]    q_start, q_len, nseg, 0, seg_len[4], seg_off[4]
+  seqs                    [S, 12]    q_start, q_len, nseg, flags (bit 0: own segment both ways),
+                                     seg_len[4], seg_off[4]
   tiles                   [n, 2]     (sequence, first query token) per 32-token prefill-attention tile
   blocks                  [m, 2]     the same per 64-token block of the persistent attention kernel,
                                      the blocks reading the most keys first
@@ -47,6 +48,7 @@ class SeqSpec:
     readout_rows: tuple | None = None  # offsets of new tokens to read (default: the last one)
     full: bool = False     # also read argmax and log-sum-exp over the whole vocabulary
     topk: bool = False     # and the best few token ids with their logits
+    bidirectional: bool = False  # every own token reads every own token (a document-isolated block)
 
 
 @dataclass
@@ -141,7 +143,8 @@ class ChunkPacker:
                 ids.extend(toks.tolist() if hasattr(toks, "tolist") else toks)
                 pos.extend(range(s.pos_start, s.pos_start + n))
                 slots.extend(own[j // P] * P + j % P for j in range(j0, j0 + n))
-            row = [q, n, nr + 1, 0, 0, 0, 0, 0, 0, 0, 0, 0]
+            # int 3: flags; bit 0 = the own segment is read both ways (no causal mask)
+            row = [q, n, nr + 1, 1 if s.bidirectional else 0, 0, 0, 0, 0, 0, 0, 0, 0]
             if slots_on:
                 # continue the key's own state, else start from the last segment it reads
                 dst = slot_of[s.own_key]

@@ -29,6 +29,10 @@ Readouts:
   decision  a decision model's head scores the option rows against the last
             row (filter: Yes > No; score: sigmoid(Yes - No); classify: the
             best label), readout.py:633-728
+  letters   a lettered prompt (slot_lm readout): the LM head's logits of the
+            option letters at the last row (filter: A (yes) > B (no); score:
+            sigmoid(A - B); classify: the option with the largest letter logit),
+            readout.py:558-620
   features  SAE features of the residual stream (a model with an SAE returns
             packed [feature ids | strengths] rows): the last token's, or
             with max pooling each feature's largest strength over the row's
@@ -36,6 +40,13 @@ Readouts:
 
 The document's pages stay resident until the row's last call has answered
 or a filter dropped it.
+
+Document-isolated models (`isolated`): the shared instruction prefix is part
+of every document's block (its KV depends on the document, which the block's
+tokens read both ways), so there is no shared prefix task; each document is
+one bidirectional task, and every call, the first included, is a follow-up
+whose own tokens read the block and each other both ways (the reference's
+"document_isolated" mask, attention.py:371-375, planning.rs:241-250).
 """
 
 from __future__ import annotations
@@ -91,6 +102,9 @@ class Call:
     # the row at all (None: always); `after` lists the earlier calls it reads
     when: object = None
     after: tuple = ()
+    # lettered classify (slot_lm readout): the answer column of each option's letter; the
+    # answer is the option whose letter has the largest logit at the last row
+    letter_cols: list = field(default_factory=list)
 
 
 @dataclass
@@ -101,8 +115,10 @@ class RowResult:
 
 class RegionRun:
     def __init__(self, executor: StageExecutor, prefix: np.ndarray, docs: list, calls: list[Call],
-                 doc_ids: list | None = None, answer_width: int | None = None, decision=None):
+                 doc_ids: list | None = None, answer_width: int | None = None, decision=None,
+                 isolated: bool = False):
         self.ex = executor
+        self.isolated = isolated              # document-isolated blocks (docs already hold the prefix)
         self.decision = decision              # models.decision.DecisionHead of a decision model
         self.prefix = np.asarray(prefix, dtype=np.int32)
         self.docs = [np.asarray(d, dtype=np.int32) for d in docs]
@@ -134,6 +150,8 @@ class RegionRun:
         if ci == 0 and not self._resident_doc[r]:
             return ("doc", r), [(PREFIX_KEY, P)], P, doc_len + len(self.calls[0].suffix)
         reads = [(PREFIX_KEY, P), (("doc", r), doc_len)] if doc_len else [(PREFIX_KEY, P)]
+        if self.isolated:
+            reads = [(("doc", r), doc_len)]
         return ("q", r, ci), reads, P + doc_len, len(self.calls[ci].suffix)
 
     def _full_cols(self, row):
@@ -181,6 +199,13 @@ class RegionRun:
             self._finish_call(r, ci)
         elif call.kind == "score":
             res.values[call.name] = 1.0 / (1.0 + math.exp(-self._margin(call, row)))
+            self._finish_call(r, ci)
+        elif call.kind == "classify" and call.letter_cols:
+            scores = np.asarray([float(row[c]) for c in call.letter_cols], dtype=np.float64)
+            res.values[call.name] = int(np.argmax(scores))
+            if call.probabilities:
+                e = np.exp(scores - scores.max())
+                res.values[call.name + "#probs"] = [float(x) for x in e / e.sum()]
             self._finish_call(r, ci)
         elif call.kind == "classify":
             self._classify_first(r, ci, row)
@@ -392,7 +417,7 @@ class RegionRun:
         return call.max_tokens if call.kind in ("map", "extract") else 0
 
     def _needs_full(self, call: Call) -> bool:
-        return call.kind in ("classify", "map", "extract") and not call.offsets
+        return call.kind in ("classify", "map", "extract") and not call.offsets and not call.letter_cols
 
     def _submit_question(self, r: int, ci: int) -> None:
         call = self.calls[ci]
@@ -400,10 +425,31 @@ class RegionRun:
         self.fresh_tokens += len(call.suffix)
         self.ex.submit(Task(np_rows=True, key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
                             full_readout=self._needs_full(call), reserve_tokens=self._reserve(call), topk=call.copy,
-                            readout_rows=self._pooled_rows(call, len(call.suffix)),
+                            readout_rows=self._pooled_rows(call, len(call.suffix)), bidirectional=self.isolated,
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
 
+    def _submit_isolated(self) -> None:
+        """Every document as one block read both ways; then its calls, all as follow-ups."""
+        for r, doc in enumerate(self.docs):
+            self._resident_doc[r] = True
+            self._next[r] = 0
+            if self.retain_key is not None and not self.ex.pool.state_slots:
+                rk = self.retain_key(r)
+                if rk is not None and self.ex.pool.resident(rk) and self.ex.claim(rk, ("doc", r)):
+                    self.ex.stats.reused += 1
+                    self._advance(r)
+                    continue
+                if rk is not None and rk in self.retained_earlier:
+                    self.ex.stats.replays += 1
+            self._pending[r] = 1
+            self.fresh_tokens += len(doc)
+            self.ex.submit(Task(np_rows=True, key=("doc", r), tokens=doc, pos_start=0, reads=[], free_after=False,
+                                bidirectional=True, on_done=lambda t, row, r=r: self._doc_only(r)))
+
     def submit_all(self) -> None:
+        if self.isolated:
+            self._submit_isolated()
+            return
         P = len(self.prefix)
         self.fresh_tokens += P
         self.ex.submit(Task(np_rows=True, key=PREFIX_KEY, tokens=self.prefix, pos_start=0, free_after=False))
@@ -460,7 +506,8 @@ class RegionRun:
     def run(self):
         self.submit_all()
         self.ex.run()
-        self.ex.free(PREFIX_KEY)
+        if self.ex.pool.resident(PREFIX_KEY):
+            self.ex.free(PREFIX_KEY)
         return self.results
 
 

@@ -63,6 +63,9 @@ class Task:
     reserve_tokens: int = 0                          # decode headroom allocated with the key's pages
     got_rows: list = field(default_factory=list)     # readout rows of the pieces already collected
     np_rows: bool = False                            # on_done gets numpy rows (views of the pass's host copy)
+    # a document-isolated block: its own tokens read each other both ways, so it runs in one
+    # pass (never split into prefill pieces)
+    bidirectional: bool = False
 
     @property
     def remaining(self) -> int:
@@ -243,6 +246,14 @@ class StageExecutor:
                         stop = True
                         break
             piece = min(task.remaining, room)
+            if task.bidirectional and piece < task.remaining:
+                if task.remaining > self.chunk_tokens:
+                    raise OversizedDocumentError(
+                        f"a document-isolated block of {task.remaining} tokens does not fit one pass of "
+                        f"{self.chunk_tokens} tokens")
+                deferred.append(task)
+                stop = True
+                break
             if piece < task.remaining and piece < self.min_piece and specs:
                 deferred.append(task)
                 stop = True
@@ -257,7 +268,8 @@ class StageExecutor:
             specs.append(SeqSpec(reads=list(task.reads), own_key=task.key, own_start=task.own_prefix + task.done,
                                  tokens=task.tokens[task.done:task.done + piece],
                                  pos_start=task.pos_start + task.done, readout=readout, tag=task,
-                                 readout_rows=rows if readout else None, full=task.full_readout, topk=task.topk))
+                                 readout_rows=rows if readout else None, full=task.full_readout, topk=task.topk,
+                                 bidirectional=task.bidirectional))
             task.done += piece
             room -= piece
             if not last:

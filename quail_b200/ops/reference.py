@@ -72,6 +72,8 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
         qpos = causal_from + own_len - q_len + torch.arange(q_len)
         kpos = torch.arange(L)
         mask = kpos[None, :] <= qpos[:, None]
+        if int(seqs[s, 3]) & 1:       # own segment read both ways (document-isolated block)
+            mask = torch.ones_like(mask)
         scores = scores.masked_fill(~mask.to(scores.device)[None], float("-inf"))
         p = torch.softmax(scores, dim=-1)
         o = torch.einsum("hqk,khd->qhd", p, v)

@@ -206,6 +206,8 @@ def _plan_select(node, session, budgets) -> PlanNode:
     cache: dict = {}
     gpus = max(session.config.gpus, 1)
     tail_tokens = 60.0
+    # a document-isolated model prefills its system turn with every document (no shared prefix KV)
+    block_tokens = 48.0 if getattr(getattr(session, "model_cfg", None), "bidirectional", False) else 0.0
     if node.get("from"):
         ref = node["from"][0]
         rows = _rows_of(ref, session)
@@ -235,7 +237,7 @@ def _plan_select(node, session, budgets) -> PlanNode:
                 mean_doc_tokens = _mean_doc_tokens(n, base_ref, session, cache=cache)
                 if rows is not None:
                     first = _doc_column(n) not in doc_read
-                    tokens = rows * ((mean_doc_tokens if first else 0.0) + tail_tokens)
+                    tokens = rows * ((mean_doc_tokens + block_tokens if first else 0.0) + tail_tokens)
                     secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / gpus
                 doc_read.add(_doc_column(n))
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
@@ -248,7 +250,7 @@ def _plan_select(node, session, budgets) -> PlanNode:
                 mean_doc_tokens = _mean_doc_tokens(n, base_ref, session, cache=cache)
                 if rows is not None:
                     # a document no earlier model call read is prefilled here
-                    fresh = tail_tokens + (0.0 if _doc_column(n) in doc_read else mean_doc_tokens)
+                    fresh = tail_tokens + (0.0 if _doc_column(n) in doc_read else mean_doc_tokens + block_tokens)
                     doc_read.add(_doc_column(n))
                     secs = budgets.pass_seconds(int(rows * fresh), mean_doc_tokens)
                     steps = _decode_tokens(n)

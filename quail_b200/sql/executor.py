@@ -200,6 +200,7 @@ class BoundCall:
     descriptions: list = field(default_factory=list)  # classify: per-label descriptions
     segments: list | None = None                     # decision prompts: the tail's segments
     read: list = field(default_factory=list)         # decision prompts: segments the head reads
+    letters: list = field(default_factory=list)      # lettered prompts: option i's answer letter
     drops: bool = True                               # filter: FALSE drops the row (WHERE chains)
     guard: dict | None = None                        # demand guard (quail_b200.sql.guards)
 
@@ -272,12 +273,17 @@ def bind_role_call(node, model: P.PromptModel) -> BoundCall:
             raise QueryError("AI.SCORE on a reranker reads one document")
         bp = P.bind_reranker_prompt(template)
         return BoundCall(key=key, kind="score", preamble=bp.preamble, tail=bp.tail, doc_expr=doc)
+    lettered = model.layout == "mammoth"
     if name in ("AI.IF", "AI_FILTER", "AI.SCORE"):
         if not args:
             raise QueryError(f"{name} takes a prompt")
         template, doc, _ = _prompt_parts(args[0])
         opts = _options(args[1] if len(args) > 1 else named.get("options"))
         kind = "score" if name == "AI.SCORE" else "filter"
+        if lettered:
+            bp = P.bind_mammoth_prompt(template, kind, model.turn)
+            return BoundCall(key=key, kind=kind, preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                             selectivity=opts.get("selectivity"), letters=bp.letters)
         bp = P.bind_decision_prompt(template, kind, model.turn)
         return BoundCall(key=key, kind=kind, preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
                          selectivity=opts.get("selectivity"), segments=bp.segments, read=bp.read)
@@ -285,6 +291,14 @@ def bind_role_call(node, model: P.PromptModel) -> BoundCall:
         call = bind_call(node, model.turn)
         opts = _options(args[2] if len(args) > 2 else named.get("options"))
         template, _, _ = _prompt_parts(args[0])
+        if lettered:
+            try:
+                bp = P.bind_mammoth_choice_prompt(template if template != "{0}" else None, call.labels,
+                                                  call.descriptions, opts.get("task_description", ""), model.turn)
+            except P.PromptError as exc:
+                raise QueryError(str(exc)) from None
+            call.preamble, call.tail, call.letters = bp.preamble, bp.tail, bp.letters
+            return call
         bp = P.bind_decision_choice_prompt(template if template != "{0}" else None, call.labels,
                                            call.descriptions, opts.get("task_description", ""), model.turn)
         call.preamble, call.tail, call.segments, call.read = bp.preamble, bp.tail, bp.segments, bp.read
@@ -757,7 +771,7 @@ class Executor:
         from quail_b200.api.engine import CallSpec
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
                           probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read,
-                          drops=c.drops, guard=c.guard)
+                          letters=c.letters, drops=c.drops, guard=c.guard)
                  for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self.report["regions"].append(out.stats)

@@ -254,3 +254,38 @@ def test_lfm2_pipeline_matches_fp32_model():
     d = rel_err(got, want)
     print(f"lfm2 kernel-vs-fp32: {d:.4f}")
     assert d < 0.1
+
+
+def test_document_isolated_model_on_the_kernels():
+    """mammoth-1's shape at the smallest size: the Qwen3.5 kernels with the document block and
+    each question read both ways, answered by option-letter logits, against the fp32 model of the
+    same weights (same SQL; scores to bf16 accuracy)."""
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    from quail_b200.api.engine import ModelEngine
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.models.build import random_checkpoint_on
+    rng = np.random.default_rng(3)
+    words = ["refund", "late", "broken", "great", "thanks", "order", "invoice", "parcel"]
+    bodies = [" ".join(rng.choice(words, size=int(rng.integers(3, 60)))) for _ in range(12)]
+    q = ("SELECT id, AI.SCORE(PROMPT('Is {0} a refund request?', body)) AS s, "
+         "AI.CLASSIFY(body, ['billing', 'shipping', 'praise']) AS c FROM t ORDER BY id")
+    cfg = quail.EngineConfig(model="mammoth-gpu-tiny", device="b200", chunk_tokens=2048)
+    with quail.Session(config=cfg) as s:
+        s.register("t", pa.table({"id": list(range(12)), "body": bodies}))
+        got = s.sql(q).collect()
+        eng = s.engine()
+        m = eng.cfg
+        ref_model = Q.Qwen35Reference(m, random_checkpoint_on(m, eng.device, seed=0), device=eng.device)
+        arena = KVArena.for_model(m, 2048, 16, device=eng.device, dtype=torch.float32, state_slots=64)
+        s._engine = ModelEngine.from_replica(cfg, ref_model, arena, tokenizer=eng.tokenizer)
+        want = s.sql(q).collect()
+        s._engine = eng
+    a, b = np.array(got.column("s").to_pylist()), np.array(want.column("s").to_pylist())
+    da, db = np.log(a / (1 - a)), np.log(b / (1 - b))
+    spread = db.max() - db.min()
+    assert spread > 1e-3, f"the reference scores do not separate the rows: {db}"
+    assert np.abs(da - db).max() < 0.2 * spread, (da, db)
+    agree = np.mean(np.array(got.column("c").to_pylist()) == np.array(want.column("c").to_pylist()))
+    assert agree >= 0.8

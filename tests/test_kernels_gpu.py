@@ -431,3 +431,43 @@ def test_nvfp4_activation_quant_and_gemm(swiglu):
     assert ops.read_and_clear_error(0) == 0
     err = ((got.float() - want).norm() / want.norm()).item()
     assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("P", [64, 128])
+def test_bidirectional_own_segment_in_every_prefill_kernel(P):
+    # document-isolated blocks: flag bit 0 of a sequence makes its own segment read both ways
+    # (a document block alone; a question reading its block and itself); the others stay causal
+    specs = [(100, [100]), (7, [300, 7]), (130, [48, 130]), (65, [65]), (200, [200]), (33, [64, 33])]
+    q, kc, vc, seqs, pl = _segmented_case(P, specs, QH=8, KH=2, pages=1024)
+    seqs[[0, 1, 3, 4], 3] = 1
+    scale = ref.softmax_scale(128)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    causal = seqs.clone()
+    causal[:, 3] = 0
+    assert rel_err(ref.segmented_attention(q, kc, vc, causal, pl, scale), want) > 0.05  # the flag matters
+    sd, pld = seqs.to(DEV), pl.to(DEV)
+    tiles = ref.attention_tiles(seqs).to(DEV)
+    out = ops.prefill_attention(q, kc, vc, sd, tiles, pld, scale)
+    assert rel_err(out, want) < 1e-2
+    out = ops.prefill_attention_tc(q, kc, vc, sd, tiles, pld, scale, fp8_out=False)
+    assert rel_err(out, want) < 1e-2
+    blocks = ref.attention_tiles(seqs, 64).to(DEV)
+    out = ops.prefill_attention_tc2(q, kc, vc, sd, blocks, pld, scale, fp8_out=False)
+    assert ops.read_and_clear_error(0) == 0
+    assert rel_err(out, want) < 1e-2
+
+
+@pytest.mark.parametrize("D", [256, 128])
+def test_bidirectional_own_segment_in_the_small_tile_kernel(D):
+    specs = [(100, [100]), (7, [300, 7]), (130, [48, 130]), (17, [17]), (40, [200, 40])]
+    QH, KH = 4, 2
+    q, kc, vc, seqs, pl = _segmented_case(16, specs, QH=QH, KH=KH, D=D, pages=2048)
+    seqs[[0, 1, 3], 3] = 1
+    scale = ref.softmax_scale(D)
+    want = ref.segmented_attention(q, kc, vc, seqs, pl, scale)
+    T = q.shape[0]
+    tiles = ref.attention_tiles(seqs).to(DEV)
+    dseqs = torch.zeros(0, dtype=torch.int32, device=DEV)
+    out = torch.empty(T, QH * D, dtype=torch.bfloat16, device=DEV)
+    ops.native().small_attention(q, kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out, None, 0)
+    assert rel_err(out.view(T, QH, D), want.view(T, QH, D)) < 1e-2
