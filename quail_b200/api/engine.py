@@ -18,6 +18,7 @@ the arena, bind answer rows), executor/runtime.py and executor/region.py.
 from __future__ import annotations
 
 import os
+import time
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -185,6 +186,31 @@ class ModelEngine:
                              device=self.device)
         self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens, gpu_timing=self.config.gpu_timing)
 
+    # ------------------------------------------------------------ metrics
+    def _snapshot(self) -> dict:
+        """Executor counters at a region's start (its metrics are the differences)."""
+        st = self.executor.stats
+        if self.on_gpu:
+            torch.cuda.reset_peak_memory_stats(self.device)
+        return {"passes": st.passes, "tokens": st.tokens, "cached": st.cached, "reused": st.reused,
+                "replays": st.replays, "evictions": st.evictions, "gpu_ms": st.gpu_ms, "t": time.perf_counter()}
+
+    def _metrics(self, snap: dict, documents: int, rows: int, asked: int, **extra) -> dict:
+        """A region's measured metrics: the reference's per-node set (crates/quail/src/report.rs:24-39;
+        every count adds across workers, peak_gpu_bytes takes the largest)."""
+        st = self.executor.stats
+        hits = st.reused - snap["reused"]
+        out = {"passes": st.passes - snap["passes"], "fresh_tokens": st.tokens - snap["tokens"],
+               "documents": documents, "rows": rows, "asked": asked,
+               "wall_s": time.perf_counter() - snap["t"], "input_rows": rows,
+               "cached_tokens": st.cached - snap["cached"], "kv_hits": hits, "kv_misses": max(documents - hits, 0),
+               "kv_removals": st.evictions - snap["evictions"], "kv_recomputations": st.replays - snap["replays"],
+               "peak_gpu_bytes": int(torch.cuda.max_memory_allocated(self.device)) if self.on_gpu else 0,
+               "gpu_s": (st.gpu_ms - snap["gpu_ms"]) / 1e3, "chunks": st.passes - snap["passes"],
+               "reused_documents": hits, "replays": st.replays - snap["replays"]}
+        out.update(extra)
+        return out
+
     def _set_answer_rows(self, ids):
         w = getattr(self.model, "w", None)
         (w if w is not None and hasattr(w, "set_answer_rows") else self.model).set_answer_rows(ids)
@@ -332,8 +358,7 @@ class ModelEngine:
         checks = [f for f in (interrupt.is_set if interrupt is not None else None,
                               asked_stop if stop is not None else None) if f is not None]
         ex.should_stop = (lambda: any(f() for f in checks)) if checks else None
-        passes0, tok0 = ex.stats.passes, ex.stats.tokens
-        reused0, replays0 = ex.stats.reused, ex.stats.replays
+        snap = self._snapshot()
         prefix_ids = tok.encode(preamble)
         if self.cfg.bidirectional:
             # document-isolated: the preamble and the layout's close are part of every document's block
@@ -383,10 +408,10 @@ class ModelEngine:
                     raise
                 # stopped on request: the rows finished so far keep their answers
                 values = [sql_values(u) if u in finished else {} for u in where]
-                return RegionOutput(values=values, stats={
-                    "passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
-                    "documents": len(finished), "rows": len(docs), "asked": run.asked, "stopped": True})
-        progress.say(f"{ex.stats.passes - passes0} passes, {ex.stats.tokens - tok0} fresh tokens", detail=True)
+                return RegionOutput(values=values, stats=self._metrics(snap, len(finished), len(docs), run.asked,
+                                                                         stopped=True))
+        progress.say(f"{ex.stats.passes - snap['passes']} passes, {ex.stats.tokens - snap['tokens']} fresh tokens",
+                     detail=True)
         if self.on_gpu:
             from quail_b200 import ops
             err = ops.read_and_clear_error(self.device.index)
@@ -394,9 +419,8 @@ class ModelEngine:
                 raise RuntimeError(f"a kernel's bounded wait ran out (code {err})")
         values = [sql_values(u) for u in where]
         del results
-        stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
-                 "documents": len(uniq), "rows": len(docs), "asked": run.asked,
-                 "reused_documents": ex.stats.reused - reused0, "replays": ex.stats.replays - replays0}
+        stats = self._metrics(snap, len(uniq), len(docs), run.asked,
+                              output_rows=sum(1 for u in where if run.results[u].kept))
         return RegionOutput(values=values, stats=stats)
 
     def run_pairs(self, preamble: str, anchors: list, pairs: list, call: CallSpec) -> RegionOutput:
@@ -419,7 +443,7 @@ class ModelEngine:
         a_tok = self.tokenize_docs(list(anchors))
         o_tok = self.tokenize_docs([t for _, t in pairs])
         ex = self.executor
-        passes0, tok0 = ex.stats.passes, ex.stats.tokens
+        snap = self._snapshot()
         run = PairRun(ex, tok.encode(preamble), a_tok, [(i, o) for (i, _), o in zip(pairs, o_tok)], rc,
                       answer_width=len(answer))
         from quail_b200.utils import progress
@@ -431,9 +455,8 @@ class ModelEngine:
             err = ops.read_and_clear_error(self.device.index)
             if err:
                 raise RuntimeError(f"a kernel's bounded wait ran out (code {err})")
-        stats = {"passes": ex.stats.passes - passes0, "fresh_tokens": ex.stats.tokens - tok0,
-                 "documents": sum(1 for a in a_tok if len(a)), "rows": len(pairs), "asked": run.asked,
-                 "pairs": len(pairs)}
+        stats = self._metrics(snap, sum(1 for a in a_tok if len(a)), len(pairs), run.asked, pairs=len(pairs),
+                              evaluated_document_pairs=len(pairs))
         return RegionOutput(values=[{call.name: v} for v in values], stats=stats)
 
     def _sql_values(self, calls: list[CallSpec], raw: dict, names) -> dict:

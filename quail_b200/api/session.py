@@ -41,6 +41,26 @@ class QueryResult:
         return f"QueryResult({self.table.num_rows} rows, {self.report.get('wall_s', 0):.3f} s)"
 
 
+def _finish_report(rep: dict, session, wall: float) -> None:
+    """Whole-query metrics (crates/quail/src/report.rs:355-380): the nodes' summed counts,
+    the largest GPU peak in GiB, and the price of the GPU time at the device's hourly rate."""
+    from quail_b200.runtime.report import totals
+    nodes = rep.setdefault("node_metrics", {})
+    tot = totals(nodes)
+    rep["cached_tokens"] = tot["cached_tokens"]
+    rep["evaluated_document_pairs"] = tot["evaluated_document_pairs"]
+    rep["peak_gib"] = tot["peak_gpu_bytes"] / 2 ** 30
+    price = None
+    cfg = session.config
+    if cfg is not None:
+        from quail_b200.planner.specs import DEVICES
+        dev = DEVICES.get(cfg.device)
+        if dev is not None and dev.usd_per_hour:
+            price = dev.usd_per_hour
+    rep["usd_per_query"] = (wall / 3600.0 * max(cfg.gpus, 1) * price) if price else None
+    nodes["output"] = {"output_rows": rep.get("output_rows", 0), "wall_s": wall}
+
+
 class Query:
     def __init__(self, session: "Session", text: str, dialect: str | None = None):
         from quail_b200.api.dialects import SQLDialect, to_parser_sql
@@ -83,6 +103,7 @@ class Query:
         rep = dict(ex.report)
         rep.update(wall_s=wall, boot_s=boot, output_rows=table.num_rows)
         rep["documents_per_second"] = rep["evaluated_documents"] / wall if wall > 0 else 0.0
+        _finish_report(rep, s, wall)
         return QueryResult(table=table, report=rep, plan=self.plan().explain())
 
     def collect(self, limit: int | None = None) -> pa.Table:

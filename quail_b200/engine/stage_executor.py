@@ -94,6 +94,23 @@ class ExecutorStats:
     evictions: int = 0          # retained keys freed to make room
     reused: int = 0             # documents a region found retained (no prefill)
     replays: int = 0            # documents a region recomputed because their retained KV was evicted
+    cached: int = 0             # prompt tokens tasks read from resident KV instead of computing them
+
+
+ANSWER_ADMISSION_ENV = "QUAIL_ANSWER_ADMISSION"
+ANSWER_ADMISSION_MODES = ("headroom=0", "headroom")
+HEADROOM_TRACE_ENV = "QUAIL_HEADROOM_TRACE"
+
+
+def answer_admission_mode() -> str:
+    """How a task's decode headroom counts at admission (the reference's QUAIL_ANSWER_ADMISSION,
+    quail/backends/quail/executor/stage_executor.py:27-50): "headroom" (default) admits a
+    task when its prompt and its answer's headroom fit; "headroom=0" when its prompt fits
+    (a decode step then grows the key's pages, evicting retained KV if it must)."""
+    mode = os.environ.get(ANSWER_ADMISSION_ENV, "headroom")
+    if mode not in ANSWER_ADMISSION_MODES:
+        raise ValueError(f"{ANSWER_ADMISSION_ENV}={mode!r}; expected one of {', '.join(ANSWER_ADMISSION_MODES)}")
+    return mode
 
 
 class StageExecutor:
@@ -124,6 +141,12 @@ class StageExecutor:
         self.nvtx = self.device.type == "cuda" and os.environ.get("QB_NVTX") == "1"
         self._inflight: deque = deque()
         self.should_stop: Callable | None = None   # checked between passes (cancel / timeout)
+        self.answer_headroom = answer_admission_mode() == "headroom"
+        # QUAIL_HEADROOM_TRACE=<dir>: each run writes its arena occupancy per pass there
+        # (seconds since the run began, pass, new tokens, free / held pages, keys held, retained
+        # keys, and the device memory allocated when the pass launched)
+        self.trace_dir = os.environ.get(HEADROOM_TRACE_ENV) or None
+        self.trace: list = []
 
     # ------------------------------------------------------------ submission
     def submit(self, task: Task) -> None:
@@ -224,7 +247,7 @@ class StageExecutor:
                 if no_new:
                     deferred.append(task)
                     continue
-                cap = total + task.reserve_tokens
+                cap = total + (task.reserve_tokens if self.answer_headroom else 0)
                 pages = self.pool.alloc(task.key, total, cap)
                 if pages is None:
                     self._evict(self.pool.pages_needed(cap))
@@ -258,6 +281,8 @@ class StageExecutor:
                 deferred.append(task)
                 stop = True
                 break
+            if task.done == 0:
+                self.stats.cached += sum(n for _, n in task.reads)
             last = piece == task.remaining
             rows = None
             readout = task.readout and last
@@ -331,6 +356,12 @@ class StageExecutor:
         self.stats.h2d_bytes += chunk.upload_bytes
         if logits is not None:
             self.stats.d2h_bytes += logits.numel() * logits.element_size()
+        if self.trace_dir is not None:
+            pool = self.pool
+            mem = torch.cuda.memory_allocated(self.device) if self.device.type == "cuda" else 0
+            self.trace.append([round(time.perf_counter() - self._t_run, 6), self.stats.passes, chunk.num_tokens,
+                               pool.free_pages, pool.num_pages - pool.free_pages, len(pool.owned),
+                               len(getattr(pool, "retained", ()) or ()), int(mem)])
         self._inflight.append((specs, chunk, host, done, ev0, ev1))
 
     def _collect_one(self):
@@ -379,6 +410,27 @@ class StageExecutor:
 
     def run(self) -> ExecutorStats:
         t0 = time.perf_counter()
+        self._t_run = t0
+        self.trace = []
+        try:
+            return self._run(t0)
+        finally:
+            if self.trace_dir is not None and self.trace:
+                self._write_trace()
+
+    def _write_trace(self) -> None:
+        import json
+        os.makedirs(self.trace_dir, exist_ok=True)
+        n = len([f for f in os.listdir(self.trace_dir) if f.startswith(f"headroom-{os.getpid()}-")])
+        path = os.path.join(self.trace_dir, f"headroom-{os.getpid()}-{n}.json")
+        with open(path, "w", encoding="utf-8") as f:
+            json.dump({"columns": ["t_s", "pass", "tokens", "free_pages", "held_pages", "keys", "retained",
+                                   "gpu_bytes"],
+                       "num_pages": self.pool.num_pages, "page_tokens": self.pool.page_tokens,
+                       "answer_admission": "headroom" if self.answer_headroom else "headroom=0",
+                       "samples": self.trace}, f)
+
+    def _run(self, t0: float) -> ExecutorStats:
         while self.pending() or self._inflight:
             if self.should_stop is not None and self.should_stop():
                 self.abort()

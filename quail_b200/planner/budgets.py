@@ -54,6 +54,19 @@ def kernel_index_cap(cfg) -> int:
     return INT32_MAX // widest
 
 
+KV_POOL_TOKENS_ENV = "QUAIL_KV_POOL_TOKENS"
+
+
+def kv_pool_cap_tokens():
+    """The KV pool cap QUAIL_KV_POOL_TOKENS sets, in tokens, or None."""
+    import os
+    v = os.environ.get(KV_POOL_TOKENS_ENV, "").strip()
+    try:
+        return int(v) if v else None
+    except ValueError:
+        raise ValueError(f"{KV_POOL_TOKENS_ENV}={v!r} is not a token count") from None
+
+
 @dataclass
 class Budgets:
     cfg: object
@@ -100,7 +113,13 @@ class Budgets:
             raise MemoryError(f"the arena holds {pages} pages; a chunk of {self.chunk_tokens} tokens needs {need}")
         # enough for eight chunks in flight and retained documents; more
         # only costs start-up time zeroing memory nothing reads
-        return min(pages, 8 * (self.chunk_tokens // page_tokens) + 256)
+        pages = min(pages, 8 * (self.chunk_tokens // page_tokens) + 256)
+        cap = kv_pool_cap_tokens()
+        if cap is not None:
+            # an experiment's cap on the KV pool (the reference's QUAIL_KV_POOL_TOKENS,
+            # crates/quail-planner/src/cost/budgets.rs:287-320)
+            pages = min(pages, max(cap // page_tokens, 1))
+        return pages
 
     def compute_knee(self) -> int:
         wb = 1.0 if self.cfg.fp8 else 2.0

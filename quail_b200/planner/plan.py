@@ -65,8 +65,17 @@ class Plan:
         return "\n".join(lines)
 
     def explain_measured(self, report: dict) -> str:
-        keys = ("wall_s", "boot_s", "fresh_tokens", "evaluated_documents", "passes", "asked", "output_rows")
-        return "measured: " + ", ".join(f"{k}={report.get(k)}" for k in keys if k in report)
+        keys = ("wall_s", "boot_s", "fresh_tokens", "cached_tokens", "evaluated_documents", "passes", "asked",
+                "output_rows", "peak_gib", "usd_per_query")
+        lines = ["measured: " + ", ".join(f"{k}={_short(report.get(k))}" for k in keys if k in report)]
+        for node, m in report.get("node_metrics", {}).items():
+            shown = ", ".join(f"{k}={_short(v)}" for k, v in m.items() if v)
+            lines.append(f"  {node}: {shown}")
+        return "\n".join(lines)
+
+
+def _short(v):
+    return f"{v:.4g}" if isinstance(v, float) else v
 
 
 def _expr_text(e) -> str:

@@ -304,17 +304,15 @@ class WorkerPool:
         finally:
             for p in paths:
                 _native.unlink_path(p)
+        from quail_b200.runtime.report import merge_worker_stats
         values = [None] * len(docs)
-        stats = {"passes": 0, "fresh_tokens": 0, "documents": 0, "rows": len(docs), "asked": 0,
-                 "per_worker": []}
+        counted = [not (self.mode == "tp" and w % self.group) for w in range(len(replies))]
         for w, rep in enumerate(replies):
-            stats["per_worker"].append(rep["stats"])
-            if self.mode == "tp" and w % self.group:
+            if not counted[w]:
                 continue              # the other ranks of a tp copy computed the same answers
             for j, i in enumerate(shards[w]):
                 values[i] = rep["values"][j]
-            for k in ("passes", "fresh_tokens", "documents", "asked"):
-                stats[k] += rep["stats"].get(k, 0)
+        stats = merge_worker_stats([rep["stats"] for rep in replies], counted, len(docs))
         return RegionOutput(values=values, stats=stats)
 
     def run_pairs(self, preamble: str, anchors: list, pairs: list, call):
@@ -351,17 +349,16 @@ class WorkerPool:
         finally:
             for p in paths:
                 _native.unlink_path(p)
+        from quail_b200.runtime.report import merge_worker_stats
         values = [None] * len(pairs)
-        stats = {"passes": 0, "fresh_tokens": 0, "documents": 0, "rows": len(pairs), "asked": 0, "per_worker": []}
+        counted = [not (self.mode == "tp" and w % self.group) for w in range(len(replies))]
         for w, rep in enumerate(replies):
-            stats["per_worker"].append(rep["stats"])
-            if self.mode == "tp" and w % self.group:
+            if not counted[w]:
                 continue
             sh = w // self.group if self.mode == "tp" else w
             for k, j in enumerate(per[sh]):
                 values[j] = rep["values"][k]
-            for k in ("passes", "fresh_tokens", "documents", "asked"):
-                stats[k] += rep["stats"].get(k, 0)
+        stats = merge_worker_stats([rep["stats"] for rep in replies], counted, len(pairs))
         return RegionOutput(values=values, stats=stats)
 
     @property

@@ -585,10 +585,7 @@ class Executor:
         if self.engine is None:
             raise QueryError("this query needs a model; the session has none")
         out = self.engine.run_pairs(self.turn.prefix, anchors, pairs, spec)
-        self.report["regions"].append(out.stats)
-        for k in ("asked", "fresh_tokens", "passes"):
-            self.report[k] += out.stats.get(k, 0)
-        self.report["evaluated_documents"] += out.stats.get("documents", 0)
+        self._record(out.stats, "quail.ai_join")
         keep = [bool(out.values[keys[r]].get(spec.name)) for r in range(rel.num_rows)]
         return rel.filter(pa.array(keep))
 
@@ -774,11 +771,18 @@ class Executor:
                           letters=c.letters, drops=c.drops, guard=c.guard)
                  for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
-        self.report["regions"].append(out.stats)
-        for k in ("asked", "fresh_tokens", "passes"):
-            self.report[k] += out.stats.get(k, 0)
-        self.report["evaluated_documents"] += out.stats.get("documents", 0)
+        self._record(out.stats, "quail.region[" + ",".join(c.kind for c in calls) + "]")
         return out.values
+
+    def _record(self, stats: dict, kind: str) -> None:
+        """A model region's stats into the query report: totals, and its metrics under a node id."""
+        from quail_b200.runtime.report import node_metrics
+        self.report["regions"].append(stats)
+        for k in ("asked", "fresh_tokens", "passes"):
+            self.report[k] += stats.get(k, 0)
+        self.report["evaluated_documents"] += stats.get("documents", 0)
+        nodes = self.report.setdefault("node_metrics", {})
+        nodes[f"{len(nodes)}:{kind}"] = node_metrics(stats)
 
     # ------------------------------------------------------------ SELECT
     def select(self, node) -> pa.Table:
