@@ -123,13 +123,13 @@ class Budgets:
 
     def compute_knee(self) -> int:
         wb = 1.0 if self.cfg.fp8 else 2.0
-        peak = self.device.fp8_flops if self.cfg.fp8 else self.device.bf16_flops
+        peak = self.device.gemm_flops(self.cfg.fp8)
         return int(peak * wb / (2 * self.device.hbm_bw))
 
     def pass_seconds(self, tokens: int, context_tokens: float = 0.0) -> float:
         """Roofline time of one pass of `tokens` new tokens (max of compute and weight reads)."""
         cfg, dev = self.cfg, self.device
-        peak = dev.fp8_flops if cfg.fp8 else dev.bf16_flops
+        peak = dev.gemm_flops(cfg.fp8)
         flops = 2.0 * cfg.dense_params_per_token() * tokens
         flops += 4.0 * cfg.layers * cfg.q_dim * context_tokens * tokens
         bytes_ = weight_bytes(cfg) + tokens * activation_bytes_per_token(cfg) * cfg.layers * 2

@@ -27,6 +27,15 @@ class DeviceSpec:
     sms: int = 0
     fp32_flops: float = 0.0
     cuda_name: str = ""
+    # measured burst matmul rates (quail_b200.calibrate), 0 = use the nominal peaks
+    mamf_fp8_flops: float = 0.0
+    mamf_bf16_flops: float = 0.0
+
+    def gemm_flops(self, fp8: bool) -> float:
+        """The rate GEMM work is priced at: the calibrated MAMF where measured, else the peak."""
+        if fp8:
+            return self.mamf_fp8_flops or self.fp8_flops
+        return self.mamf_bf16_flops or self.bf16_flops
 
 
 def _devices() -> dict:
