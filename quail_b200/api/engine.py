@@ -115,6 +115,19 @@ class ModelEngine:
     def _build(self, pages: int | None):
         from quail_b200.engine.arena import KVArena
         from quail_b200.engine.stage_executor import StageExecutor
+        if self.cfg.set_attention:
+            # set attention (LFM3 / d1): whole passes with no KV kept; the pipeline holds
+            # its own scratch pages
+            from quail_b200.models.lfm3 import Lfm3Pipeline, Lfm3Reference
+            ckpt = self._checkpoint()
+            if self.on_gpu:
+                self.model = Lfm3Pipeline(self.cfg, ckpt, self.device, max_tokens=self.chunk_tokens)
+            else:
+                self.model = Lfm3Reference(self.cfg, ckpt, device="cpu")
+            del ckpt
+            self.arena = None
+            self.executor = None
+            return
         if self.cfg.is_moe and not self.cfg.is_hybrid:
             self._build_moe(pages)
             return
@@ -244,8 +257,129 @@ class ModelEngine:
         """
         return self._run_region(preamble, docs, calls, on_rows, stop)
 
+    def _run_set_region(self, preamble: str, docs: list, calls: list[CallSpec], on_rows, stop) -> RegionOutput:
+        """A region on a set-attention model: pass groups of questions over each document
+        (engine/set_passes.py); no KV is kept between passes."""
+        from quail_b200.api.config import Refusal, RefusalError
+        from quail_b200.engine import set_passes as SP
+        from quail_b200.sql import guards as G
+        cfg, tok = self.cfg, self.tokenizer
+        t0 = time.perf_counter()
+        keys, uniq, where, rep = {}, [], [], []
+        guarded = [c.guard for c in calls if c.guard is not None]
+        for i, t in enumerate(self.tokenize_docs(docs)):
+            k = t.tobytes()
+            if guarded:
+                k = (k, tuple(G.signature(g, i) for g in guarded))
+            if k not in keys:
+                keys[k] = len(uniq)
+                uniq.append(t)
+                rep.append(i)
+            where.append(keys[k])
+        yes_sp, no_sp = cfg.answer_spellings or (P.TRUE_SPELLINGS, P.FALSE_SPELLINGS)
+        yes, no = tok.answer_ids(list(yes_sp)), tok.answer_ids(list(no_sp))
+        end_slot = len(tok.encode("\nend:"))     # the start slot's row, counted back from the end slot
+        qs = []
+        for c in calls:
+            body = np.asarray(tok.encode(c.tail), dtype=np.int32)
+            if c.kind in ("filter", "score"):
+                q = SP.SetQuestion("yes_no" if c.kind == "filter" else "score", body, c.name, yes=yes, no=no)
+            elif c.kind == "classify":
+                codes = c.letters or P.code_candidates(len(c.labels))
+                q = SP.SetQuestion("choice", body, c.name, options=[[int(tok.encode(x)[0])] for x in codes])
+            elif c.kind == "extract":
+                q = SP.SetQuestion("read", body, c.name, slots=(end_slot, 0))
+            else:
+                raise RefusalError(Refusal(reasons=(f"{c.kind} decodes text, which the set-attention model "
+                                                    f"{cfg.name!r} does not",), constraint="unsupported_function"))
+            q.drops = c.drops
+            if c.guard is not None:
+                deps = G.calls_of(c.guard)
+                q.after = tuple(j for j, o in enumerate(calls) if o.name in deps)
+                q.when = (lambda r, vals, g=c.guard: G.asks(g, rep[r], self._sql_values(calls, vals, G.calls_of(g))))
+            qs.append(q)
+        # pass groups: a dropping filter closes its group; a call reading an answer of the
+        # current group opens the next one
+        groups, cur = [], []
+        for j, q in enumerate(qs):
+            if cur and set(q.after) & set(cur):
+                groups.append(cur)
+                cur = []
+            cur.append(j)
+            if q.kind == "yes_no" and q.drops:
+                groups.append(cur)
+                cur = []
+        if cur:
+            groups.append(cur)
+        head = tok.encode(preamble)
+        header = np.asarray(tok.encode(SP.D1_HEADER), dtype=np.int32)
+        states = [np.concatenate([head, u, header]).astype(np.int32) for u in uniq]
+        spans = [(len(head), len(u)) for u in uniq]
+        region = SP.SetRegion(self.model, self._head_for_set(), self.chunk_tokens, cfg.set_size, header,
+                              cfg.answer_temperature, cfg.read_span_tokens, cfg.read_found)
+        values = [dict() for _ in uniq]
+        kept = [True] * len(uniq)
+        stopped = False
+        for g in groups:
+            if stop is not None and stop():
+                stopped = True
+                break
+            # documents by the calls of this group their guards ask
+            by_calls: dict = {}
+            for d in range(len(uniq)):
+                if not kept[d]:
+                    continue
+                ask = tuple(j for j in g if qs[j].when is None or qs[j].when(d, values[d]))
+                if ask:
+                    by_calls.setdefault(ask, []).append(d)
+            for ask, who in by_calls.items():
+                sub = [qs[j] for j in ask]
+                got = region.ask(states, spans, sub, who)
+                for d in who:
+                    for k, j in enumerate(ask):
+                        ans, extra = got[(d, k)]
+                        c = calls[j]
+                        if c.kind == "classify":
+                            values[d][c.name] = ans
+                            if c.probabilities:
+                                values[d][c.name + "#probs"] = [float(x) for x in extra]
+                        elif c.kind == "extract":
+                            values[d][c.name] = (None if ans is None
+                                                 else tok.decode(uniq[d][ans[0]:ans[1] + 1]).strip() or None)
+                        else:
+                            values[d][c.name] = ans
+                            if c.kind == "filter" and c.drops and not ans:
+                                kept[d] = False
+        out_vals = []
+        for u in where:
+            v = dict(values[u])
+            for c in calls:
+                if c.kind == "classify" and c.name in v:
+                    v[c.name] = c.labels[v[c.name]]
+            out_vals.append(v)
+        if on_rows is not None:
+            rows_of: dict = {}
+            for i, u in enumerate(where):
+                rows_of.setdefault(u, []).append(i)
+            for u, rows in rows_of.items():
+                on_rows(rows, out_vals[rows[0]])
+        st = region.stats
+        stats = {"passes": st["chunks"], "fresh_tokens": st["fresh_tokens"], "documents": len(uniq),
+                 "rows": len(docs), "asked": st["asked"], "set_passes": st["passes"], "chunks": st["chunks"],
+                 "input_rows": len(docs), "kv_misses": len(uniq), "wall_s": time.perf_counter() - t0,
+                 "output_rows": sum(1 for u in where if kept[u])}
+        if stopped:
+            stats["stopped"] = True
+        return RegionOutput(values=out_vals, stats=stats)
+
+    def _head_for_set(self):
+        m = self.model
+        return m.head
+
     def _run_region(self, preamble: str, docs: list, calls: list[CallSpec], on_rows, stop) -> RegionOutput:
         from quail_b200.engine.stage_executor import QueryCancelled
+        if self.cfg.set_attention:
+            return self._run_set_region(preamble, docs, calls, on_rows, stop)
         from quail_b200.engine.region import Call, RegionRun
         from quail_b200.sql import guards as G
         tok = self.tokenizer
@@ -428,9 +562,9 @@ class ModelEngine:
         document) pairs; `call` (AI.IF or AI.SCORE) is asked once per pair. Values per pair."""
         from quail_b200.api.config import Refusal, RefusalError
         from quail_b200.engine.region import Call, PairRun
-        if self.cfg.role != "generative":
-            raise RefusalError(Refusal(reasons=(f"an AI join's pair questions need a generative model, not "
-                                                f"{self.cfg.name!r}",), constraint="unsupported_function"))
+        if self.cfg.role != "generative" or self.cfg.set_attention:
+            raise RefusalError(Refusal(reasons=(f"an AI join's pair questions need a generative model that keeps "
+                                                f"KV, not {self.cfg.name!r}",), constraint="unsupported_function"))
         tok = self.tokenizer
         true_ids = tok.answer_ids(P.TRUE_SPELLINGS)
         false_ids = tok.answer_ids(P.FALSE_SPELLINGS)

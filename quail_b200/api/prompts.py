@@ -223,6 +223,17 @@ MAMMOTH_EMPTY_QUESTION = "Which option applies to the state?"
 MAX_LETTERS = 255          # the most options one coded prompt lists
 
 
+# LiquidAI d1 layout (crates/quail-planner/src/prompts.rs:174-189): the document with no label,
+# then "QUESTION:" blocks; the answer instructions, the option lines "<code> <text>", and the
+# read slots are the checkpoint's interface, so they are the reference's
+D1_QUESTION_SEPARATOR = "\n\n\n"
+D1_QUESTION_LABEL = "QUESTION:\n"
+D1_YES_NO_END = "\n\nReply with yes or no only."
+D1_OPTION_END = "\n\nReply with the option code only."
+D1_READ_END = "\n\nRead the text from the state, or nothing if it is absent."
+D1_READ_SLOTS = "start:\nend:"
+
+
 def code_candidates(n: int) -> list[str]:
     """The first n option codes: A to Z, then AA, AB, ... ZZ."""
     import string
@@ -247,6 +258,8 @@ def prompt_model(cfg) -> PromptModel:
     turn = Turn(prefix="", suffix="") if role in ("reranker", "decision") else Turn()
     if getattr(cfg, "turn_prefix", None) is not None:
         turn = Turn(prefix=cfg.turn_prefix, suffix=turn.suffix)
+    if getattr(cfg, "turn_suffix", None) is not None:
+        turn = Turn(prefix=turn.prefix, suffix=cfg.turn_suffix)
     return PromptModel(role=role, layout=getattr(cfg, "prompt_layout", "ai-if"), turn=turn,
                        name=getattr(cfg, "name", ""))
 
@@ -345,6 +358,49 @@ def bind_mammoth_choice_prompt(template: str | None, labels: list[str], descript
     return LetteredPrompt(kind="classify", template=template or "", preamble=turn.prefix + MAMMOTH_DOCUMENT_LABEL,
                           tail=tail, question=question, labels=list(labels), descriptions=descriptions,
                           letters=letters)
+
+
+def option_codes(labels: list[str]) -> list[str]:
+    """A coded prompt's option codes: the labels themselves when every one is a single letter,
+    else A, B, ... (prompts.rs option_codes)."""
+    stripped = [str(x).strip() for x in labels]
+    if stripped and all(len(x) == 1 and x.isalpha() for x in stripped):
+        return stripped
+    return code_candidates(len(labels))
+
+
+def bind_d1_prompt(template: str, kind: str, turn: Turn = Turn(prefix="", suffix="")) -> LetteredPrompt:
+    """AI.IF / AI.SCORE for a set-attention model: the question body after its header."""
+    base = bind_prompt(template, 1, turn)
+    return LetteredPrompt(kind=kind, template=template, preamble=turn.prefix,
+                          tail=base.question + D1_YES_NO_END + turn.suffix, question=base.question)
+
+
+def bind_d1_choice_prompt(template: str | None, labels: list[str], descriptions: list[str] | None = None,
+                          task_description: str = "", turn: Turn = Turn(prefix="", suffix="")) -> LetteredPrompt:
+    """AI.CLASSIFY for a set-attention model: the question, one "<code> <text>" line per option."""
+    if template:
+        question, rest = split_frame(template)
+        question = (question + ("\n\n" + rest.strip() if rest.strip() else "")).strip()
+    else:
+        question = ""
+    if task_description:
+        question = f"{question}\n{task_description}" if question else task_description
+    descriptions = list(descriptions or [])
+    codes = option_codes(labels)
+    lines = "\n".join(f"{code} {descriptions[i] if i < len(descriptions) and descriptions[i] else str(lab).replace('_', ' ')}"
+                      for i, (code, lab) in enumerate(zip(codes, labels)))
+    tail = question + "\n\nOptions:\n" + lines + D1_OPTION_END + turn.suffix
+    return LetteredPrompt(kind="classify", template=template or "", preamble=turn.prefix, tail=tail,
+                          question=question, labels=list(labels), descriptions=descriptions, letters=codes)
+
+
+def bind_d1_read_prompt(question: str, turn: Turn = Turn(prefix="", suffix="")) -> BoundPrompt:
+    """AI.EXTRACT for a set-attention model: a pointer read, answered at the two slot rows."""
+    if not question.strip():
+        raise PromptError("AI.EXTRACT needs a question with at least one word")
+    return BoundPrompt(kind="extract", template="{0}", preamble=turn.prefix,
+                       tail=question + D1_READ_END + turn.suffix + D1_READ_SLOTS, question=question)
 
 
 def reranker_text(query: str, document: str) -> str:

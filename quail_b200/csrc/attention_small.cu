@@ -99,6 +99,9 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
   const int* sd = seqs + seq * kSmSeqInts;
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
   const bool bidir = (sd[3] & 1) != 0;   // own segment read both ways (document-isolated block)
+  // bits 8..23: a sliding window over the own segment (a row at own position p reads own keys
+  // p - win + 1 .. p); 0 = none. Earlier segments are read whole.
+  const int win = bidir ? 0 : ((sd[3] >> 8) & 0xffff);
   if (q0 >= q_len) return;
   const int kvh = blockIdx.y, h0 = kvh * G;
   int seg_len[kSmMaxSeg], seg_off[kSmMaxSeg], seg_blocks[kSmMaxSeg];
@@ -110,12 +113,15 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
   const int own_len = seg_len[nseg - 1];
   const int rows_tok = min(TOK, q_len - q0);
   const int first_pos = own_len - q_len + q0;       // own-segment position of the tile's first token
+  // own-segment key blocks wholly below the first row's window are skipped
+  const int own_skip = win > 0 ? max(0, first_pos - win + 1) / kSmBk : 0;
   int total = 0;
 #pragma unroll
   for (int i = 0; i < kSmMaxSeg; ++i) {
     int vis = seg_len[i];
     if (i == nseg - 1 && !bidir) vis = min(vis, first_pos + rows_tok);
     seg_blocks[i] = i < nseg ? (vis + kSmBk - 1) / kSmBk : 0;
+    if (i == nseg - 1) seg_blocks[i] = max(0, seg_blocks[i] - own_skip);
     total += seg_blocks[i];
   }
   const size_t row_stride = (size_t)KH * D;
@@ -148,6 +154,7 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
         bb -= seg_blocks[i];
         s = i + 1;
       }
+    if (s == nseg - 1) bb += own_skip;
   };
   auto load_block = [&](int b, int st) {
     int s, bb;
@@ -217,7 +224,7 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
       for (int i = 0; i < 4; ++i) {
         const int jj = bb * kSmBk + n * 8 + t4 * 2 + (i & 1);
         const int lim = (i >> 1) ? lim1 : lim0;
-        const bool vis = jj < slen && (!own || jj <= lim);
+        const bool vis = jj < slen && (!own || (jj <= lim && (win == 0 || jj > lim - win)));
         s[n][i] = vis ? s[n][i] * scale_log2 : -INFINITY;
         mx[i >> 1] = fmaxf(mx[i >> 1], s[n][i]);
       }
@@ -279,7 +286,12 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
       const size_t row = (size_t)q_start + q0 + tr;
       const float il = half ? il1 : il0;
       float v0 = oacc[n][half * 2] * il, v1 = oacc[n][half * 2 + 1] * il;
-      if (gate != nullptr) {
+      if (gate != nullptr && gate_hstride < 0) {
+        // one gate value per (row, head)
+        const float gs = 1.f / (1.f + __expf(-__bfloat162float(gate[row * ld_gate + h0 + hr])));
+        v0 *= gs;
+        v1 *= gs;
+      } else if (gate != nullptr) {
         const __nv_bfloat16* gp = gate + row * ld_gate + (size_t)(h0 + hr) * gate_hstride + col;
         v0 *= 1.f / (1.f + __expf(-__bfloat162float(gp[0])));
         v1 *= 1.f / (1.f + __expf(-__bfloat162float(gp[1])));

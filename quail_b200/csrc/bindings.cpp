@@ -10,6 +10,9 @@
 namespace qb {
 
 void embed_gather(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out);
+void post_norm_add_norm(const torch::Tensor& y, torch::Tensor& h, const torch::Tensor& wpost,
+                        const c10::optional<torch::Tensor>& wnext, const c10::optional<torch::Tensor>& x, double eps);
+void kv_copy_rows(torch::Tensor& k_cache, torch::Tensor& v_cache, const torch::Tensor& src, const torch::Tensor& dst);
 void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, const c10::optional<torch::Tensor>& y8,
                    const c10::optional<torch::Tensor>& ys, const c10::optional<torch::Tensor>& ybf, int64_t T);
 void quant_rows(const torch::Tensor& x, bool swiglu, const c10::optional<torch::Tensor>& y8,
@@ -165,6 +168,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_rows_mx", &qb::quant_rows_mx);
   m.def("row_argmax_lse", &qb::row_argmax_lse);
   m.def("embed_gather", &qb::embed_gather);
+  m.def("post_norm_add_norm", &qb::post_norm_add_norm, "LFM3 sandwich norm: h += norm(y) * w; x = norm(h) * w_next");
+  m.def("kv_copy_rows", &qb::kv_copy_rows, "copy K and V rows between arena slots");
   m.def("rmsnorm_quant", &qb::rmsnorm_quant);
   m.def("quant_rows", &qb::quant_rows);
   m.def("qk_norm_rope_kv", &qb::qk_norm_rope_kv);

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(128) short_conv_kernel(const __nv_bfloat16* __
     win[W - 2] = bx;
     y[(size_t)(q0 + t) * H + c] = __float2bfloat16(__bfloat162float(row[H + c]) * acc);
   }
+  if (dst < 0) return;   // no state kept (whole-sequence passes)
 #pragma unroll
   for (int j = 0; j < W - 1; ++j) state[(((size_t)dst * NL + li) * (W - 1) + j) * H + c] = win[j];
 }
@@ -263,17 +264,19 @@ void short_conv(const torch::Tensor& bcx, const torch::Tensor& wconv, const torc
   c10::cuda::CUDAGuard guard(dev);
   cudaStream_t st = at::cuda::getCurrentCUDAStream(dev);
   dim3 grid(S, (H + 127) / 128);
-  TORCH_CHECK(W == 3 || W == 4, "short_conv: width 3 or 4");
+  TORCH_CHECK(W == 3 || W == 4 || W == 7, "short_conv: width 3, 4 or 7");
+#define QB_SHORT_CONV(WW)                                                                                    \
+  short_conv_kernel<WW><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(bcx.data_ptr()),       \
+                                              (int)bcx.stride(0), H, wconv.data_ptr<float>(), seqs.data_ptr<int>(), \
+                                              state_io.data_ptr<int>(), state.data_ptr<float>(), (int)li,   \
+                                              (int)state.size(1), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()))
   if (W == 3)
-    short_conv_kernel<3><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(bcx.data_ptr()),
-                                                (int)bcx.stride(0), H, wconv.data_ptr<float>(), seqs.data_ptr<int>(),
-                                                state_io.data_ptr<int>(), state.data_ptr<float>(), (int)li,
-                                                (int)state.size(1), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    QB_SHORT_CONV(3);
+  else if (W == 4)
+    QB_SHORT_CONV(4);
   else
-    short_conv_kernel<4><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(bcx.data_ptr()),
-                                                (int)bcx.stride(0), H, wconv.data_ptr<float>(), seqs.data_ptr<int>(),
-                                                state_io.data_ptr<int>(), state.data_ptr<float>(), (int)li,
-                                                (int)state.size(1), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()));
+    QB_SHORT_CONV(7);
+#undef QB_SHORT_CONV
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

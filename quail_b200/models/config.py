@@ -63,6 +63,16 @@ class DecoderConfig:
     # (recurrent layers stay causal), so a document's KV serves its own questions only
     attention_mask: str = "causal"
     turn_prefix: str | None = None   # the chat text before every prompt (None: the role's default)
+    turn_suffix: str | None = None   # the chat text after every question (None: the role's default)
+    # set attention (LFM3 / d1, attention_mask="set"): a pass is a document and up to
+    # `set_size` questions, recomputed per pass with no KV kept
+    set_size: int = 0
+    sliding_window: int = 0          # "swa" layers: each token reads the last `sliding_window` tokens
+    rotary_pairs: float = 1.0        # full-attention layers rotate this share of the frequency pairs
+    answer_temperature: float = 1.0  # divides an option / yes-no margin before the softmax / sigmoid
+    read_span_tokens: int = 0        # the longest span a pointer read returns
+    read_found: tuple = ()           # a pointer read's (raw, calibrated) P(found) knots
+    answer_spellings: tuple = ()     # (true spellings, false spellings) read at a yes / no slot
 
     @property
     def bidirectional(self) -> bool:
@@ -103,7 +113,11 @@ class DecoderConfig:
     @property
     def attn_layers(self) -> list:
         """Indices of the layers with a KV cache."""
-        return [i for i in range(self.layers) if self.kind(i) == "attn"]
+        return [i for i in range(self.layers) if self.kind(i) in ("attn", "swa")]
+
+    @property
+    def set_attention(self) -> bool:
+        return self.attention_mask == "set"
 
     @property
     def gdn_layers(self) -> list:
@@ -265,6 +279,27 @@ MAMMOTH_TINY = QWEN35_TINY.with_(name="mammoth-tiny", **_ISOLATED)
 MAMMOTH_GPU_TINY = QWEN35_GPU_TINY.with_(name="mammoth-gpu-tiny", **_ISOLATED)
 ISOLATED_DENSE_TINY = QWEN3_TINY.with_(name="isolated-dense-tiny", **_ISOLATED)
 
+# LiquidAI d1-2B (LFM3): short convolutions (7 taps) between attention layers that alternate
+# full attention (half the frequency pairs rotated) and a 256-token sliding window; sandwich
+# norms; a sigmoid gate per attention head; set attention (the reference spec
+# quail/specs/data/models/d1-2b-bf16.toml)
+_D1_KINDS = ("conv", "conv") + ("attn", "conv", "swa", "conv") * 5 + ("attn", "conv")
+D1_TURN_PREFIX = "<|startoftext|><|im_start|>user\n"
+D1_TURN_SUFFIX = "<|im_end|>\n<|im_start|>assistant\n<think></think>"
+D1_2B = DecoderConfig(name="d1-2b", layers=24, hidden=2048, num_q_heads=16, num_kv_heads=4, head_dim=128,
+                      intermediate=7680, vocab=128_000, tied_head=True, weight_dtype="bf16", arch="lfm3",
+                      layer_kinds=_D1_KINDS, conv_width=7, rms_eps=1e-5, max_position=128_000,
+                      attention_mask="set", set_size=16, sliding_window=256, rotary_pairs=0.5,
+                      answer_temperature=1.337398453966105, read_span_tokens=512, prompt_layout="d1",
+                      turn_prefix=D1_TURN_PREFIX, turn_suffix=D1_TURN_SUFFIX,
+                      answer_spellings=(("yes", "Yes", "YES"), ("no", "No", "NO")))
+D1_TINY = D1_2B.with_(name="d1-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2, head_dim=64,
+                      intermediate=512, vocab=151_936, layer_kinds=("conv", "attn", "conv", "swa"), set_size=4,
+                      sliding_window=16, read_span_tokens=32, max_position=40_960)
+D1_GPU_TINY = D1_2B.with_(name="d1-gpu-tiny", layers=4, hidden=1024, num_q_heads=8, num_kv_heads=2, head_dim=128,
+                          intermediate=1024, vocab=4096, layer_kinds=("conv", "attn", "conv", "swa"), set_size=4,
+                          sliding_window=64, read_span_tokens=64, max_position=8192)
+
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
                                QWEN3_GPU_TINY_GQA4,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
@@ -274,7 +309,7 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, RERANKER_GPU_TINY, QWEN35_27B_FP8, QWEN38_27B_FP8,
                                QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY, QWEN38_27B_NVFP4,
                                QWEN35_GPU_TINY_NVFP4, MAMMOTH_1, ELEPHANT_1, MAMMOTH_TINY, MAMMOTH_GPU_TINY,
-                               ISOLATED_DENSE_TINY)}
+                               ISOLATED_DENSE_TINY, D1_2B, D1_TINY, D1_GPU_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -321,4 +356,7 @@ MODEL_CONFIGS = {
     "mammoth-tiny": MAMMOTH_TINY,
     "mammoth-gpu-tiny": MAMMOTH_GPU_TINY,
     "isolated-dense-tiny": ISOLATED_DENSE_TINY,
+    "d1-2b-bf16": D1_2B,
+    "d1-tiny": D1_TINY,
+    "d1-gpu-tiny": D1_GPU_TINY,
 }

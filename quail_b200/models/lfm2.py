@@ -205,11 +205,11 @@ class Lfm2Pipeline:
                 p = ops.gemm(x, L["wqkv"])
                 kc, vc = arena.layer(ai)
                 q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=self.device)
-                ops.count_launch(1 + int(chunk.tiles.shape[0] > 0) + int(chunk.dseqs.numel() > 0))
+                ops.count_launch(1)
                 C.hybrid_qk_rope_kv(p, QH, KH, False, chunk.positions, L["qn"], L["kn"], False, self.cos_sin,
                                     chunk.slots, kc, vc, q, cfg.rms_eps)
                 o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=self.device)
-                C.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
+                ops.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
                                   None, 0)
                 ops.gemm(o, L["wo"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
                 ai += 1

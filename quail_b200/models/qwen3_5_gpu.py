@@ -212,8 +212,7 @@ class Qwen35Pipeline:
                                     cfg.norm_offset, self.cos_sin, chunk.slots, kc, vc, q, cfg.rms_eps)
                 o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=dev)
                 gate = p[:, D:] if cfg.attn_output_gate else None
-                ops.count_launch(int(chunk.tiles.shape[0] > 0) + int(chunk.dseqs.numel() > 0))
-                C.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
+                ops.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
                                   gate, 2 * D)
                 if self.fp8:
                     o8, os_ = ops.quant_rows_mx(o)

@@ -72,6 +72,9 @@ def iter_random_layer(cfg: DecoderConfig, i: int, gen: torch.Generator, device="
     if cfg.arch == "lfm2":
         yield from _iter_lfm2_layer(cfg, i, gen, device, dtype)
         return
+    if cfg.arch == "lfm3":
+        yield from _iter_lfm3_layer(cfg, i, gen, device, dtype)
+        return
     p = layer_prefix(i)
     H = cfg.hidden
     # zero-centered norms (scale 1 + w) start at 0; plain ones at 1
@@ -119,6 +122,28 @@ def _iter_lfm2_layer(cfg: DecoderConfig, i: int, gen, device, dtype):
         yield p + "self_attn.k_layernorm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
         for name, shape in (("q_proj", (cfg.q_dim, H)), ("k_proj", (cfg.kv_dim, H)), ("v_proj", (cfg.kv_dim, H)),
                             ("out_proj", (H, cfg.q_dim))):
+            yield from _emit_proj(p + "self_attn." + name, shape, cfg, gen, device, dtype).items()
+    for name, shape in (("w1", (cfg.intermediate, H)), ("w3", (cfg.intermediate, H)), ("w2", (H, cfg.intermediate))):
+        yield from _emit_proj(p + "feed_forward." + name, shape, cfg, gen, device, dtype).items()
+
+
+def _iter_lfm3_layer(cfg: DecoderConfig, i: int, gen, device, dtype):
+    """An LFM3 layer in HF names: sandwich norms (operator_norm, post_operator_norm, ffn_norm,
+    post_ffn_norm), conv.{in_proj, conv, out_proj} or self_attn.{q,k,v,gate,o}_proj + q/k_norm,
+    feed_forward.w1 (gate), w3 (up), w2 (down). The post norms start at one like the others."""
+    p = layer_prefix(i)
+    H = cfg.hidden
+    for name in ("operator_norm", "post_operator_norm", "ffn_norm", "post_ffn_norm"):
+        yield p + name + ".weight", torch.ones(H, device=device, dtype=dtype)
+    if cfg.kind(i) == "conv":
+        yield from _emit_proj(p + "conv.in_proj", (3 * H, H), cfg, gen, device, dtype).items()
+        yield p + "conv.conv.weight", _rand((H, 1, cfg.conv_width), 0.3, gen, device, dtype)
+        yield from _emit_proj(p + "conv.out_proj", (H, H), cfg, gen, device, dtype).items()
+    else:
+        yield p + "self_attn.q_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+        yield p + "self_attn.k_norm.weight", torch.ones(cfg.head_dim, device=device, dtype=dtype)
+        for name, shape in (("q_proj", (cfg.q_dim, H)), ("k_proj", (cfg.kv_dim, H)), ("v_proj", (cfg.kv_dim, H)),
+                            ("gate_proj", (cfg.num_q_heads, H)), ("o_proj", (H, cfg.q_dim))):
             yield from _emit_proj(p + "self_attn." + name, shape, cfg, gen, device, dtype).items()
     for name, shape in (("w1", (cfg.intermediate, H)), ("w3", (cfg.intermediate, H)), ("w2", (H, cfg.intermediate))):
         yield from _emit_proj(p + "feed_forward." + name, shape, cfg, gen, device, dtype).items()
@@ -174,7 +199,7 @@ def random_sae(cfg: DecoderConfig, gen: torch.Generator, device="cpu") -> dict[s
 
 
 def final_norm_name(cfg: DecoderConfig) -> str:
-    return "model.embedding_norm.weight" if cfg.arch == "lfm2" else "model.norm.weight"
+    return "model.embedding_norm.weight" if cfg.arch in ("lfm2", "lfm3") else "model.norm.weight"
 
 
 def head_weight(ckpt: dict[str, torch.Tensor], cfg: DecoderConfig) -> torch.Tensor:

@@ -44,6 +44,10 @@ from quail_b200.ops.kernels import (  # noqa: F401
     rmsnorm_quant,
     sae_features,
     row_argmax_lse,
+    small_attention,
+    SMALL_ATTENTION_SHAPES,
+    post_norm_add_norm,
+    kv_copy_rows,
 )
 from quail_b200.ops.quant import (  # noqa: F401
     FP8_MAX,

@@ -336,6 +336,43 @@ def prefill_attention_tc2(q, k_cache, v_cache, seqs, blocks, page_list, softmax_
     return (out, out_scale) if fp8_out else out
 
 
+# (head_dim, q heads per KV head) pairs the small-tile attention kernel is built for
+SMALL_ATTENTION_SHAPES = frozenset({(64, 2), (64, 4), (128, 4), (256, 2), (256, 4), (256, 6), (256, 8)})
+
+
+def small_attention(q, k_cache, v_cache, seqs, tiles, dseqs, page_list, softmax_scale: float, out,
+                    gate=None, gate_hstride: int = 0):
+    """Small-tile paged attention (mma.sync) for head_dim 64 / 128 / 256, optional sigmoid gate.
+
+    The shape is checked here, before the native call: only the (head_dim, group) pairs the
+    kernel is instantiated for run.
+    """
+    D, G = q.shape[2], q.shape[1] // k_cache.shape[2]
+    if (D, G) not in SMALL_ATTENTION_SHAPES:
+        raise ValueError(f"small_attention: head_dim {D} with {G} q heads per KV head is not built; "
+                         f"built: {sorted(SMALL_ATTENTION_SHAPES)}")
+    count_launch(int(tiles.shape[0] > 0) + int(dseqs.numel() > 0))
+    native().small_attention(q, k_cache, v_cache, seqs, tiles, dseqs, page_list, softmax_scale, out, gate,
+                             gate_hstride)
+    return out
+
+
+def post_norm_add_norm(y: torch.Tensor, h: torch.Tensor, w_post: torch.Tensor, w_next=None, eps: float = 1e-5):
+    """A sandwich-normed block's residual add: h += RMSNorm(y) * w_post in place; then, with
+    w_next, the next block's input RMSNorm(h) * w_next (bf16 [T, H]), else None."""
+    x = torch.empty_like(h) if w_next is not None else None
+    count_launch()
+    native().post_norm_add_norm(y, h, w_post, w_next, x, eps)
+    return x
+
+
+def kv_copy_rows(k_cache: torch.Tensor, v_cache: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Copy the K and V rows of arena slots `src` to slots `dst` (int32, one per row)."""
+    if src.numel():
+        count_launch()
+        native().kv_copy_rows(k_cache, v_cache, src, dst)
+
+
 def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: bool, tc: bool,
                     out=None, out_scale=None):
     """Attention of every query row of a packed chunk.

@@ -42,7 +42,11 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 
 def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                         seqs: torch.Tensor, page_list: torch.Tensor, scale: float) -> torch.Tensor:
-    """fp32 oracle of csrc/attention.cu: [T, QH, D] -> [T, QH * D]."""
+    """fp32 oracle of csrc/attention.cu: [T, QH, D] -> [T, QH * D].
+
+    seqs[s, 3] holds flags: bit 0, the own segment is read both ways; bits 8..23, a
+    sliding window over the own segment (0: none).
+    """
     T, QH, D = q.shape
     P, KH = k_cache.shape[1], k_cache.shape[2]
     out = torch.zeros(T, QH * D, dtype=torch.float32, device=q.device)
@@ -72,8 +76,12 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
         qpos = causal_from + own_len - q_len + torch.arange(q_len)
         kpos = torch.arange(L)
         mask = kpos[None, :] <= qpos[:, None]
-        if int(seqs[s, 3]) & 1:       # own segment read both ways (document-isolated block)
+        flags = int(seqs[s, 3])
+        win = (flags >> 8) & 0xFFFF
+        if flags & 1:                 # own segment read both ways (document-isolated block)
             mask = torch.ones_like(mask)
+        elif win:                     # a sliding window over the own segment; earlier segments whole
+            mask &= (kpos[None, :] < causal_from) | (kpos[None, :] > qpos[:, None] - win)
         scores = scores.masked_fill(~mask.to(scores.device)[None], float("-inf"))
         p = torch.softmax(scores, dim=-1)
         o = torch.einsum("hqk,khd->qhd", p, v)

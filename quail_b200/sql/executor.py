@@ -306,7 +306,48 @@ def bind_role_call(node, model: P.PromptModel) -> BoundCall:
     return bind_call(node, model.turn)
 
 
+def bind_set_call(node, model: P.PromptModel) -> BoundCall:
+    """An AI call for a set-attention model (the d1 layout): yes / no questions, option codes
+    and pointer reads, asked in passes over each document; nothing decodes text
+    (crates/quail-planner/src/prompts.rs:174-189, 940-990)."""
+    name = node["name"]
+    args = [a for a in node["args"] if a.get("type") != "named_arg"]
+    named = {a["name"].lower(): a["value"] for a in node["args"] if a.get("type") == "named_arg"}
+    key = node_key(node)
+    if name in ("AI.MAP", "AI.SAE_FEATURES"):
+        _refuse(f"{name} needs text decoding or features, which the set-attention model {model.name!r} does not "
+                f"give", f"unsupported_{name[3:].lower()}_query")
+    if name in ("AI.IF", "AI_FILTER", "AI.SCORE"):
+        if not args:
+            raise QueryError(f"{name} takes a prompt")
+        template, doc, _ = _prompt_parts(args[0])
+        opts = _options(args[1] if len(args) > 1 else named.get("options"))
+        kind = "score" if name == "AI.SCORE" else "filter"
+        bp = P.bind_d1_prompt(template, kind, model.turn)
+        return BoundCall(key=key, kind=kind, preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                         selectivity=opts.get("selectivity"))
+    if name == "AI.CLASSIFY":
+        call = bind_call(node, model.turn)
+        opts = _options(args[2] if len(args) > 2 else named.get("options"))
+        template, _, _ = _prompt_parts(args[0])
+        bp = P.bind_d1_choice_prompt(template if template != "{0}" else None, call.labels, call.descriptions,
+                                     opts.get("task_description", ""), model.turn)
+        call.preamble, call.tail, call.letters = bp.preamble, bp.tail, bp.letters
+        return call
+    if name in ("AI.EXTRACT", "AI.EXTRACT_SPAN"):
+        call = bind_call(node, model.turn)
+        try:
+            bp = P.bind_d1_read_prompt(call.questions[0], model.turn)
+        except P.PromptError as exc:
+            raise QueryError(str(exc)) from None
+        call.preamble, call.tail = bp.preamble, bp.tail
+        return call
+    return bind_call(node, model.turn)
+
+
 def bind_call(node, turn: P.Turn, model: P.PromptModel | None = None) -> BoundCall:
+    if model is not None and model.layout == "d1":
+        return bind_set_call(node, model)
     if model is not None and model.role in ("reranker", "decision"):
         return bind_role_call(node, model)
     name = node["name"]
@@ -721,7 +762,8 @@ class Executor:
             guard = None if c.guard is None else G.take(c.guard, rows)
             if c.kind == "extract":
                 for qi, q in enumerate(c.questions):
-                    bp = P.bind_extract_prompt(q, self.turn)
+                    bp = (P.bind_d1_read_prompt(q, self.turn) if self.model.layout == "d1"
+                          else P.bind_extract_prompt(q, self.turn))
                     expanded.append(BoundCall(key=f"{c.key}#{qi}", kind="extract", preamble=bp.preamble,
                                               tail=bp.tail, doc_expr=c.doc_expr, max_tokens=c.max_tokens,
                                               drops=False, guard=guard))

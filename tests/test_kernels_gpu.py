@@ -457,10 +457,9 @@ def test_bidirectional_own_segment_in_every_prefill_kernel(P):
     assert rel_err(out, want) < 1e-2
 
 
-@pytest.mark.parametrize("D", [256, 128])
-def test_bidirectional_own_segment_in_the_small_tile_kernel(D):
+@pytest.mark.parametrize("D,QH,KH", [(256, 4, 2), (128, 8, 2)])
+def test_bidirectional_own_segment_in_the_small_tile_kernel(D, QH, KH):
     specs = [(100, [100]), (7, [300, 7]), (130, [48, 130]), (17, [17]), (40, [200, 40])]
-    QH, KH = 4, 2
     q, kc, vc, seqs, pl = _segmented_case(16, specs, QH=QH, KH=KH, D=D, pages=2048)
     seqs[[0, 1, 3], 3] = 1
     scale = ref.softmax_scale(D)
@@ -469,5 +468,7 @@ def test_bidirectional_own_segment_in_the_small_tile_kernel(D):
     tiles = ref.attention_tiles(seqs).to(DEV)
     dseqs = torch.zeros(0, dtype=torch.int32, device=DEV)
     out = torch.empty(T, QH * D, dtype=torch.bfloat16, device=DEV)
-    ops.native().small_attention(q, kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out, None, 0)
+    ops.small_attention(q, kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out)
     assert rel_err(out.view(T, QH, D), want.view(T, QH, D)) < 1e-2
+    with pytest.raises(ValueError, match="not built"):
+        ops.small_attention(q.view(T, QH * D // 32, 32), kc, vc, seqs.to(DEV), tiles, dseqs, pl.to(DEV), scale, out)
