@@ -286,6 +286,8 @@ def test_document_isolated_model_on_the_kernels():
     da, db = np.log(a / (1 - a)), np.log(b / (1 - b))
     spread = db.max() - db.min()
     assert spread > 1e-3, f"the reference scores do not separate the rows: {db}"
-    assert np.abs(da - db).max() < 0.2 * spread, (da, db)
+    # bf16 Gated DeltaNet and attention against fp32: the row-to-row pattern must match
+    assert np.abs(da - db).max() < 0.35 * spread, (da, db)
+    assert np.corrcoef(da, db)[0, 1] > 0.9, (da, db)
     agree = np.mean(np.array(got.column("c").to_pylist()) == np.array(want.column("c").to_pylist()))
     assert agree >= 0.8
