@@ -71,7 +71,8 @@ class ModelEngine:
         self.chunk_tokens = config.chunk_tokens or self.budgets.chunk_tokens
         self.model = model
         self.arena = arena
-        self.executor = StageExecutor(model, arena, self.chunk_tokens, gpu_timing=config.gpu_timing)
+        self.executor = StageExecutor(model, arena, self.chunk_tokens, gpu_timing=config.gpu_timing,
+                                      attention=self._attention_path())
         self.retention = bool(config.extra.get("retention", True))
         self._retained_keys = set()
         return self
@@ -151,7 +152,7 @@ class ModelEngine:
             self.arena = KVArena.for_model(self.cfg, n_pages, page_tokens, device=self.device, dtype=dtype,
                                            state_slots=self.budgets.state_slots(self.cfg))
             self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
-                                          gpu_timing=self.config.gpu_timing)
+                                          gpu_timing=self.config.gpu_timing, attention=self._attention_path())
             return
         if self.on_gpu:
             from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights
@@ -167,7 +168,7 @@ class ModelEngine:
         self.arena = KVArena(self.cfg.layers, n_pages, page_tokens, self.cfg.num_kv_heads, self.cfg.head_dim,
                              device=self.device, dtype=dtype)
         self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
-                                      gpu_timing=self.config.gpu_timing)
+                                      gpu_timing=self.config.gpu_timing, attention=self._attention_path())
         if self.on_gpu and os.environ.get("QB_GRAPHS", "1") != "0":
             # decode passes (AI.MAP / AI.EXTRACT steps) replay captured CUDA graphs
             self.executor.enable_graphs()
@@ -223,6 +224,11 @@ class ModelEngine:
                "reused_documents": hits, "replays": st.replays - snap["replays"]}
         out.update(extra)
         return out
+
+    def _attention_path(self) -> str:
+        """EngineConfig.attention: "tree" or "unified" as asked; None lets each chunk choose by
+        the cost rule (engine/chunk.py: tree_saves)."""
+        return {"tree": "tree", "unified": "unified"}.get(self.config.attention, "auto")
 
     def _set_answer_rows(self, ids):
         w = getattr(self.model, "w", None)

@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const __grid_constant__ CUtensorMap tmV, const int* __restrict__ seqs,
                             const int* __restrict__ blocks, int n_items, const int* __restrict__ page_list,
                             int page_tokens, int QH, int KH, float scale_log2, __nv_bfloat16* __restrict__ o,
-                            int ldo, uint8_t* __restrict__ o8, uint8_t* __restrict__ osf, int* err) {
+                            int ldo, uint8_t* __restrict__ o8, uint8_t* __restrict__ osf, float* __restrict__ lse,
+                            int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -528,6 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint32_t*>(osf + ((t_out >> 7) * QH + head) * 512 + (t_out & 31) * 16 +
                                        ((t_out & 127) >> 5) * 4) = word;
       }
+      // the row's log-sum-exp (natural log) for a merge with another read of the same rows
+      if (lse != nullptr && valid)
+        lse[t_out * QH + head] = l > 0.f ? (m_ref + __log2f(l)) * 0.69314718055994531f : -INFINITY;
       tc_fence_before();
       mbar_arrive(&o_free[t]);
     }
@@ -552,7 +556,7 @@ int* device_error_word(int dev);
 template <int MODE>
 static void launch_tc2(int grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                        const int* seqs, const int* blocks, int n_items, const int* pl, int P, int QH, int KH, float sl2,
-                       __nv_bfloat16* o, int ldo, uint8_t* o8, uint8_t* osf, int* err, int dev) {
+                       __nv_bfloat16* o, int ldo, uint8_t* o8, uint8_t* osf, float* lse, int* err, int dev) {
   static bool configured[64] = {false};
   if (!configured[dev]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(prefill_attn_tc2_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -560,15 +564,17 @@ static void launch_tc2(int grid, cudaStream_t st, const CUtensorMap& tq, const C
     configured[dev] = true;
   }
   prefill_attn_tc2_kernel<MODE><<<grid, kThreads, kSmem, st>>>(tq, tk, tv, seqs, blocks, n_items, pl, P, QH, KH, sl2,
-                                                                o, ldo, o8, osf, err);
+                                                                o, ldo, o8, osf, lse, err);
 }
 
 // q [T, QH, 128] bf16; caches [pages, P, KH, 128] bf16 (P a multiple of 64, a
 // power of two); seqs [S, 12]; blocks [n, 2] int32 (sequence, first token of a
-// 64-token block); out bf16 [T, QH*128] or e4m3 with out_sf scale bytes.
+// 64-token block); out bf16 [T, QH*128] or e4m3 with out_sf scale bytes; with a bf16 out,
+// `lse` [T, QH] fp32 receives each row's log-sum-exp (rows no block covers are not written).
 void prefill_attention_tc2(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                            const torch::Tensor& seqs, const torch::Tensor& blocks, const torch::Tensor& page_list,
-                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf) {
+                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
+                           const c10::optional<torch::Tensor>& lse) {
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous() && q.scalar_type() == at::kBFloat16,
               "q: [T, QH, 128] bf16");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == 128 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
@@ -593,18 +599,25 @@ void prefill_attention_tc2(const torch::Tensor& q, const torch::Tensor& k_cache,
   const int grid = std::min(n_items, num_sms(dev));
   const float sl2 = (float)(softmax_scale * 1.4426950408889634);
   int* err = device_error_word(dev);
+  float* lse_p = nullptr;
+  if (lse.has_value()) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "a log-sum-exp output goes with a bf16 out");
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->is_contiguous() && lse->numel() >= (int64_t)T * QH,
+                "lse: fp32 [T, QH]");
+    lse_p = lse->data_ptr<float>();
+  }
   if (out.scalar_type() == at::kFloat8_e4m3fn) {
     TORCH_CHECK(out_sf.has_value() && out_sf->scalar_type() == at::kByte &&
                     out_sf->numel() >= (int64_t)((T + 127) / 128) * QH * 512,
                 "e4m3 output needs its MX scale bytes");
     launch_tc2<2>(grid, st, tq, tk, tv, seqs.data_ptr<int>(), blocks.data_ptr<int>(), n_items,
                   page_list.data_ptr<int>(), P, QH, KH, sl2, nullptr, out.stride(0),
-                  reinterpret_cast<uint8_t*>(out.data_ptr()), out_sf->data_ptr<uint8_t>(), err, dev);
+                  reinterpret_cast<uint8_t*>(out.data_ptr()), out_sf->data_ptr<uint8_t>(), nullptr, err, dev);
   } else {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 or e4m3 output");
     launch_tc2<0>(grid, st, tq, tk, tv, seqs.data_ptr<int>(), blocks.data_ptr<int>(), n_items,
                   page_list.data_ptr<int>(), P, QH, KH, sl2, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                  out.stride(0), nullptr, nullptr, err, dev);
+                  out.stride(0), nullptr, nullptr, lse_p, err, dev);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

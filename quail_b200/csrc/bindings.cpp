@@ -13,6 +13,9 @@ void embed_gather(const torch::Tensor& ids, const torch::Tensor& table, torch::T
 void post_norm_add_norm(const torch::Tensor& y, torch::Tensor& h, const torch::Tensor& wpost,
                         const c10::optional<torch::Tensor>& wnext, const c10::optional<torch::Tensor>& x, double eps);
 void kv_copy_rows(torch::Tensor& k_cache, torch::Tensor& v_cache, const torch::Tensor& src, const torch::Tensor& dst);
+void attention_merge(const torch::Tensor& o_a, const torch::Tensor& lse_a, const torch::Tensor& o_b,
+                     const torch::Tensor& lse_b, const torch::Tensor& source, int64_t QH, torch::Tensor& out,
+                     const c10::optional<torch::Tensor>& out_sf);
 void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, const c10::optional<torch::Tensor>& y8,
                    const c10::optional<torch::Tensor>& ys, const c10::optional<torch::Tensor>& ybf, int64_t T);
 void quant_rows(const torch::Tensor& x, bool swiglu, const c10::optional<torch::Tensor>& y8,
@@ -34,7 +37,8 @@ void gemm_mx_qkv_rope(const torch::Tensor& a, const torch::Tensor& sfa, const to
                       double eps, bool norm_qk, const c10::optional<torch::Tensor>& row_ss);
 void prefill_attention_tc2(const torch::Tensor& q, const torch::Tensor& k_cache, const torch::Tensor& v_cache,
                            const torch::Tensor& seqs, const torch::Tensor& blocks, const torch::Tensor& page_list,
-                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf);
+                           double softmax_scale, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
+                           const c10::optional<torch::Tensor>& lse);
 void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tensor& b, const torch::Tensor& sfb,
              int64_t epi, torch::Tensor& out, const c10::optional<torch::Tensor>& out_sf,
              const c10::optional<torch::Tensor>& residual, const c10::optional<torch::Tensor>& row_ss,
@@ -170,6 +174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_gather", &qb::embed_gather);
   m.def("post_norm_add_norm", &qb::post_norm_add_norm, "LFM3 sandwich norm: h += norm(y) * w; x = norm(h) * w_next");
   m.def("kv_copy_rows", &qb::kv_copy_rows, "copy K and V rows between arena slots");
+  m.def("attention_merge", &qb::attention_merge, "merge two attention reads of the same rows by log-sum-exp");
   m.def("rmsnorm_quant", &qb::rmsnorm_quant);
   m.def("quant_rows", &qb::quant_rows);
   m.def("qk_norm_rope_kv", &qb::qk_norm_rope_kv);

@@ -17,6 +17,17 @@ sequences, plus the metadata the kernels read:
 The host packs it with numpy into one pinned int32 buffer and ships it with
 a single H2D copy (reference: chunk.py pack_chunk + InputStaging, which
 stage per-field pinned buffers).
+
+The tree path (`ChunkPacker(tree=...)`): when several prefill sequences of a
+chunk read the same resident segment first (the shared instruction prefix, a
+join anchor), `Chunk.tree` also holds
+  seqs_a   [S, 12]  the sequences without that stacked segment (every row's own reads)
+  seqs_b   [G, 12]  one sequence per stacked segment: its readers' rows, stacked, read it whole
+  blocks_a / blocks_b  the persistent attention kernel's blocks of each table
+  rows     [R]      the chunk rows stacked into seqs_b's query rows, in order
+  source   [T]      each chunk row's stacked row, -1 for none
+and the attention runs as two reads merged by their log-sum-exps
+(ops.attention_merge); `chunk.seqs` stays the unified table.
 """
 
 from __future__ import annotations
@@ -70,12 +81,35 @@ class Chunk:
     upload_bytes: int = 0
     full_readout: bool = False  # readout rows also need full-vocabulary argmax / log-sum-exp
     topk: bool = False          # and the top-k token ids and logits (ops.READOUT_TOPK)
+    tree: dict | None = None    # the tree path's tables (module docstring), None: unified
+
+
+TREE_BLOCK = 64        # query rows per block of the persistent attention kernel
+
+
+def tree_saves(reader_rows: list, shared_tokens: int) -> bool:
+    """The tree path's cost rule (the reference's cheaper_attention_path, cost/budgets.rs:537-562,
+    restated for this kernel): the unified path reads the shared keys once per 64-row block of
+    every reader, the tree path once per 64-row block of the stacked readers plus a merge pass;
+    stack when that saves at least a quarter of the shared-key tiles and 16 tiles."""
+    kv_tiles = -(-shared_tokens // TREE_BLOCK)
+    unified = sum(-(-n // TREE_BLOCK) for n in reader_rows) * kv_tiles
+    stacked = -(-sum(reader_rows) // TREE_BLOCK) * kv_tiles
+    return unified - stacked >= max(16, unified // 4)
 
 
 class ChunkPacker:
-    """Packs SeqSpecs against a PagePool into a Chunk on `device`."""
+    """Packs SeqSpecs against a PagePool into a Chunk on `device`.
 
-    def __init__(self, pool, device, pin: bool = True, split_decode: bool = True):
+    tree: "unified" (never stack), "tree" (stack every shared first segment read by two or
+    more prefill sequences) or "auto" (stack where `tree_saves` says so)."""
+
+    def __init__(self, pool, device, pin: bool = True, split_decode: bool = True, tree: str = "unified",
+                 tree_min_tokens: int = 64):
+        if tree not in ("unified", "tree", "auto"):
+            raise ValueError(f"attention path is 'unified', 'tree' or 'auto', not {tree!r}")
+        self.tree = tree
+        self.tree_min_tokens = tree_min_tokens
         self.pool = pool
         # one-token sequences go to the decode attention kernel instead of prefill tiles
         self.split_decode = split_decode
@@ -95,11 +129,27 @@ class ChunkPacker:
         for sz in sizes:
             views.append(dev[o:o + sz])
             o += sz
+        tree = self.tree_parts(specs, host) if self.tree != "unified" and n_tok else None
+        tree_dev = None
+        up = int(flat.nbytes)
+        if tree is not None:
+            keys = ("seqs_a", "seqs_b", "blocks_a", "blocks_b", "rows", "source")
+            tflat = np.concatenate([tree[k].reshape(-1) for k in keys])
+            tdev = self._upload_plain(tflat)
+            tree_dev, o = {}, 0
+            for k in keys:
+                n = tree[k].size
+                v = tdev[o:o + n]
+                tree_dev[k] = v.view(-1, SEQ_INTS) if k.startswith("seqs") else (
+                    v.view(-1, 2) if k.startswith("blocks") else v)
+                o += n
+            up += int(tflat.nbytes)
+            host["tree"] = tree
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
                      final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2),
-                     blocks=views[9].view(-1, 2), readout_tags=tags,
-                     num_seqs=len(specs), host=host, upload_bytes=int(flat.nbytes),
+                     blocks=views[9].view(-1, 2), readout_tags=tags, tree=tree_dev,
+                     num_seqs=len(specs), host=host, upload_bytes=up,
                      full_readout=any(s.full and s.readout for s in specs),
                      topk=any(s.topk and s.readout for s in specs))
 
@@ -191,6 +241,84 @@ class ChunkPacker:
                 "blocks": np.asarray([(b[1], b[2]) for b in sorted(blocks, key=lambda b: -b[0])],
                                      dtype=i32).reshape(-1, 2)}
         return host, tags
+
+    def tree_parts(self, specs: list[SeqSpec], host: dict) -> dict | None:
+        """The tree path's tables for this chunk, or None when nothing is worth stacking."""
+        seqs = host["seqs"]
+        decode = set(host["dseqs"].tolist())
+        # each prefill sequence stacks at most one earlier segment: the longest one that another
+        # sequence of the chunk reads too (a shared prefix, a join anchor)
+        count: dict = {}
+        for si, s in enumerate(specs):
+            if si not in decode and not s.bidirectional:
+                for r in s.reads:
+                    if r[1] >= self.tree_min_tokens:
+                        count[r] = count.get(r, 0) + 1
+        groups: dict = {}
+        for si, s in enumerate(specs):
+            if si in decode or s.bidirectional:
+                continue
+            best = None
+            for i, r in enumerate(s.reads):
+                if count.get(r, 0) >= 2 and (best is None or r[1] > s.reads[best][1]):
+                    best = i
+            if best is not None:
+                groups.setdefault(s.reads[best], []).append((si, best))
+        chosen = []
+        for (key, ln), members in groups.items():
+            if len(members) < 2:
+                continue
+            rows = [int(seqs[si, 1]) for si, _ in members]
+            if self.tree == "auto" and not tree_saves(rows, ln):
+                continue
+            chosen.append((ln, members))
+        if not chosen:
+            return None
+        T = host["ids"].size
+        a = seqs.copy()
+        b_rows, b_seqs, stacked = [], [], 0
+        source = np.full(T, -1, dtype=np.int32)
+        for ln, members in chosen:
+            start = stacked
+            for si, seg in members:
+                # drop segment `seg` from the sequence's table (the own segment stays last)
+                nseg = int(a[si, 2])
+                lens = [int(x) for i, x in enumerate(seqs[si, 4:4 + nseg]) if i != seg]
+                offs = [int(x) for i, x in enumerate(seqs[si, 8:8 + nseg]) if i != seg]
+                a[si, 4:8] = 0
+                a[si, 8:12] = 0
+                a[si, 4:4 + nseg - 1] = lens
+                a[si, 8:8 + nseg - 1] = offs
+                a[si, 2] = nseg - 1
+                q0, n = int(seqs[si, 0]), int(seqs[si, 1])
+                r = np.arange(q0, q0 + n, dtype=np.int32)
+                b_rows.append(r)
+                source[r] = np.arange(stacked, stacked + n, dtype=np.int32)
+                stacked += n
+            si0, seg0 = members[0]
+            # the stacked rows read the shared segment whole (bit 0: both ways)
+            b_seqs.append([start, stacked - start, 1, 1, ln, 0, 0, 0, int(seqs[si0, 8 + seg0]), 0, 0, 0])
+        seqs_b = np.asarray(b_seqs, dtype=np.int32).reshape(-1, SEQ_INTS)
+
+        def blocks_of(tab, skip):
+            out = []
+            for si in range(tab.shape[0]):
+                if si in skip:
+                    continue
+                n, nseg = int(tab[si, 1]), int(tab[si, 2])
+                keys = int(tab[si, 4:4 + nseg].sum())
+                for q0 in range(0, n, TREE_BLOCK):
+                    out.append((keys, si, q0))
+            out.sort(key=lambda x: -x[0])
+            return np.asarray([(x[1], x[2]) for x in out], dtype=np.int32).reshape(-1, 2)
+        return {"seqs_a": a, "seqs_b": seqs_b, "blocks_a": blocks_of(a, decode), "blocks_b": blocks_of(seqs_b, ()),
+                "rows": np.concatenate(b_rows).astype(np.int32), "source": source}
+
+    def _upload_plain(self, flat: np.ndarray) -> torch.Tensor:
+        src = torch.from_numpy(np.ascontiguousarray(flat))
+        if self.device.type != "cuda":
+            return src.clone()
+        return src.pin_memory().to(self.device, non_blocking=True) if self.pin else src.to(self.device)
 
     def _upload(self, flat: np.ndarray) -> torch.Tensor:
         src = torch.from_numpy(flat)

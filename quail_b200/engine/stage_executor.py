@@ -95,6 +95,7 @@ class ExecutorStats:
     reused: int = 0             # documents a region found retained (no prefill)
     replays: int = 0            # documents a region recomputed because their retained KV was evicted
     cached: int = 0             # prompt tokens tasks read from resident KV instead of computing them
+    tree_passes: int = 0        # passes whose attention ran the tree path (stacked shared segments)
 
 
 ANSWER_ADMISSION_ENV = "QUAIL_ANSWER_ADMISSION"
@@ -115,7 +116,7 @@ def answer_admission_mode() -> str:
 
 class StageExecutor:
     def __init__(self, model, arena, chunk_tokens: int, *, min_piece: int = 64, gpu_timing: bool = False,
-                 max_seqs: int | None = None, cont_cap: int = 512):
+                 max_seqs: int | None = None, cont_cap: int = 512, attention: str = "unified"):
         self.model = model
         self.arena = arena
         self.pool = arena.pool
@@ -127,7 +128,8 @@ class StageExecutor:
         # while the GPU runs the other's (a step depends on the previous one's token)
         self.cont_cap = cont_cap
         self.device = arena.device
-        self.packer = ChunkPacker(self.pool, self.device)
+        # the attention path: "unified", "tree" (stack readers of a shared first segment) or "auto"
+        self.packer = ChunkPacker(self.pool, self.device, tree=attention)
         self.queue: deque[Task] = deque()
         # continuations of resident keys (decode steps, label continuations):
         # admitted before new work, they need at most a page-list extension
@@ -337,6 +339,8 @@ class StageExecutor:
             chunk = _Replayed(num_tokens=len(specs), upload_bytes=nbytes)
         else:
             chunk = self.packer.pack(specs)
+            if getattr(chunk, "tree", None) is not None:
+                self.stats.tree_passes += 1
             logits = self.model.forward_chunk(chunk, self.arena)
         if self.gpu_timing:
             ev1.record()

@@ -276,7 +276,12 @@ class Qwen3Reference:
             slots = chunk.slots[ok].long()
             kc.view(-1, KH, D)[slots] = self._bf(k[ok]).to(kc.dtype)
             vc.view(-1, KH, D)[slots] = self._bf(v[ok]).to(vc.dtype)
-            o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(h.dtype)
+            tree = getattr(chunk, "tree", None)
+            if tree is not None:
+                # the tree path: two reads merged by their log-sum-exps (the same sum, reordered)
+                o = ref.tree_attention(q, kc, vc, chunk.seqs, chunk.page_list, tree, self.scale).to(h.dtype)
+            else:
+                o = ref.segmented_attention(q, kc, vc, chunk.seqs, chunk.page_list, self.scale).to(h.dtype)
             o = self._q(o) if self.cfg.fp8 else self._bf(o)
             h = self._bf(h + o @ L["wo"].t())
             x = self._q(self._bf(ref.rmsnorm(h, L["ln2"], cfg.rms_eps)))

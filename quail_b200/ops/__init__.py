@@ -48,6 +48,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     SMALL_ATTENTION_SHAPES,
     post_norm_add_norm,
     kv_copy_rows,
+    attention_merge,
 )
 from quail_b200.ops.quant import (  # noqa: F401
     FP8_MAX,

@@ -317,22 +317,44 @@ def decode_attention(q, k_cache, v_cache, seqs, dseqs, page_list, softmax_scale:
 
 
 def prefill_attention_tc2(q, k_cache, v_cache, seqs, blocks, page_list, softmax_scale: float, *,
-                          fp8_out: bool = True, out=None, out_scale=None):
+                          fp8_out: bool = True, out=None, out_scale=None, lse=None):
     """The persistent tcgen05 attention (csrc/attention_tc2.cu) over 64-token query blocks.
 
     blocks [m, 2] int32: (sequence, first query token) per 64-token block
     (`ops.reference.attention_tiles(seqs, 64)` or a chunk's `blocks`); pages
     hold a multiple of 64 tokens. Returns bf16 [T, QH*128], or with fp8_out
-    (e4m3, UE8M0 scale bytes in the MX atom layout).
+    (e4m3, UE8M0 scale bytes in the MX atom layout). With a bf16 out, `lse`
+    (fp32 [T, QH]) receives each row's log-sum-exp for a later merge.
     """
     T, QH = q.shape[0], q.shape[1]
     if out is None:
         out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if fp8_out else torch.bfloat16, device=q.device)
     if fp8_out and out_scale is None:
         out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+    if lse is not None and fp8_out:
+        raise ValueError("a log-sum-exp output goes with a bf16 attention output")
     count_launch()
     native().prefill_attention_tc2(q, k_cache, v_cache, seqs, blocks, page_list, softmax_scale, out,
-                                   out_scale if fp8_out else None)
+                                   out_scale if fp8_out else None, lse)
+    return (out, out_scale) if fp8_out else out
+
+
+def attention_merge(o_a, lse_a, o_b, lse_b, source, *, fp8_out: bool = True, out=None, out_scale=None):
+    """Merge two attention reads of the same rows over disjoint key sets (csrc/attention_merge.cu).
+
+    o_a bf16 [T, QH*D], lse_a fp32 [T, QH]: every row's read of one key set; o_b / lse_b
+    [R, ...]: reads of another key set by some rows, `source` int32 [T] naming each row's
+    row of o_b (-1: none). out = (o_a e^lse_a + o_b e^lse_b) / (e^lse_a + e^lse_b), as bf16
+    or as e4m3 with UE8M0 scales per 32 columns in the MX atom layout (the next GEMM's input).
+    """
+    T, W = o_a.shape
+    QH = lse_a.shape[1]
+    if out is None:
+        out = torch.empty(T, W, dtype=torch.float8_e4m3fn if fp8_out else torch.bfloat16, device=o_a.device)
+    if fp8_out and out_scale is None:
+        out_scale = torch.empty(sf_bytes(T, W), dtype=torch.uint8, device=o_a.device)
+    count_launch()
+    native().attention_merge(o_a, lse_a, o_b, lse_b, source, QH, out, out_scale if fp8_out else None)
     return (out, out_scale) if fp8_out else out
 
 
@@ -387,6 +409,9 @@ def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: boo
         out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn if mx else torch.bfloat16, device=q.device)
     if mx and out_scale is None:
         out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+    tree = getattr(chunk, "tree", None)
+    if tree is not None and tc and k_cache.shape[1] % 64 == 0 and chunk.tiles.shape[0] > 0:
+        return _tree_attention(q, k_cache, v_cache, chunk, tree, softmax_scale, mx=mx, out=out, out_scale=out_scale)
     if chunk.tiles.shape[0] > 0:
         blocks = getattr(chunk, "blocks", None)
         if tc and blocks is not None and k_cache.shape[1] % 64 == 0:
@@ -403,6 +428,35 @@ def chunk_attention(q, k_cache, v_cache, chunk, softmax_scale: float, *, mx: boo
         decode_attention(q, k_cache, v_cache, chunk.seqs, dseqs, chunk.page_list, softmax_scale, out,
                          out_scale if mx else None)
     return (out, out_scale) if mx else out
+
+
+def _tree_attention(q, k_cache, v_cache, chunk, tree, softmax_scale, *, mx, out, out_scale):
+    """The tree path of a chunk (engine/chunk.py): every row's own reads (persistent kernel,
+    bf16 + log-sum-exp), the stacked readers' read of their shared segments (same kernel over
+    the gathered rows), one-token rows on the decode kernel, then the merge (+ MX quantization)."""
+    T, QH = q.shape[0], q.shape[1]
+    o_a = torch.empty(T, QH * 128, dtype=torch.bfloat16, device=q.device)
+    lse_a = torch.empty(T, QH, dtype=torch.float32, device=q.device)
+    prefill_attention_tc2(q, k_cache, v_cache, tree["seqs_a"], tree["blocks_a"], chunk.page_list, softmax_scale,
+                          fp8_out=False, out=o_a, lse=lse_a)
+    dseqs = getattr(chunk, "dseqs", None)
+    if dseqs is not None and dseqs.numel() > 0:
+        decode_attention(q, k_cache, v_cache, chunk.seqs, dseqs, chunk.page_list, softmax_scale, o_a, None)
+    rows = tree["rows"]
+    qb = q.index_select(0, rows.long())
+    o_b = torch.empty(rows.numel(), QH * 128, dtype=torch.bfloat16, device=q.device)
+    lse_b = torch.empty(rows.numel(), QH, dtype=torch.float32, device=q.device)
+    prefill_attention_tc2(qb, k_cache, v_cache, tree["seqs_b"], tree["blocks_b"], chunk.page_list, softmax_scale,
+                          fp8_out=False, out=o_b, lse=lse_b)
+    if mx:
+        if out is None:
+            out = torch.empty(T, QH * 128, dtype=torch.float8_e4m3fn, device=q.device)
+        if out_scale is None:
+            out_scale = torch.empty(sf_bytes(T, QH * 128), dtype=torch.uint8, device=q.device)
+        attention_merge(o_a, lse_a, o_b, lse_b, tree["source"], fp8_out=True, out=out, out_scale=out_scale)
+        return out, out_scale
+    out = attention_merge(o_a, lse_a, o_b, lse_b, tree["source"], fp8_out=False, out=out)
+    return out
 
 
 def sae_features(x: torch.Tensor, w_enc: torch.Tensor, b_enc: torch.Tensor, keep: int) -> torch.Tensor:

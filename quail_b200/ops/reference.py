@@ -89,6 +89,81 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     return out
 
 
+def segmented_attention_lse(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            seqs: torch.Tensor, page_list: torch.Tensor, scale: float):
+    """segmented_attention plus each covered row's log-sum-exp: ([T, QH * D], [T, QH]);
+    rows no sequence covers get out 0 and lse -inf."""
+    T, QH, D = q.shape
+    P, KH = k_cache.shape[1], k_cache.shape[2]
+    out = torch.zeros(T, QH * D, dtype=torch.float32, device=q.device)
+    lse = torch.full((T, QH), float("-inf"), dtype=torch.float32, device=q.device)
+    seqs = seqs.cpu()
+    pl = page_list.cpu()
+    for s in range(seqs.shape[0]):
+        q_start, q_len, nseg = (int(v) for v in seqs[s, :3])
+        ks, vs, before = [], [], 0
+        for i in range(nseg):
+            ln, off = int(seqs[s, 4 + i]), int(seqs[s, 8 + i])
+            idx = torch.arange(ln)
+            slots = (pl[off + idx // P] * P + idx % P).to(k_cache.device)
+            ks.append(k_cache.reshape(-1, KH, D)[slots].float())
+            vs.append(v_cache.reshape(-1, KH, D)[slots].float())
+            if i < nseg - 1:
+                before += ln
+        k, v = torch.cat(ks), torch.cat(vs)
+        L = k.shape[0]
+        qs = q[q_start:q_start + q_len].float()
+        k = k.repeat_interleave(QH // KH, dim=1)
+        v = v.repeat_interleave(QH // KH, dim=1)
+        sc = torch.einsum("qhd,khd->hqk", qs, k) * scale
+        qpos = L - q_len + torch.arange(q_len)
+        kpos = torch.arange(L)
+        mask = kpos[None, :] <= qpos[:, None]
+        if int(seqs[s, 3]) & 1:
+            mask = torch.ones_like(mask)
+        sc = sc.masked_fill(~mask.to(sc.device)[None], float("-inf"))
+        l_ = torch.logsumexp(sc, dim=-1)                       # [QH, q_len]
+        p = torch.exp(sc - l_[..., None]).nan_to_num(0.0)
+        out[q_start:q_start + q_len] = torch.einsum("hqk,khd->qhd", p, v).reshape(q_len, QH * D)
+        lse[q_start:q_start + q_len] = l_.t()
+    return out, lse
+
+
+def merge_lse(o_a: torch.Tensor, lse_a: torch.Tensor, o_b: torch.Tensor, lse_b: torch.Tensor,
+              source: torch.Tensor) -> torch.Tensor:
+    """fp32 statement of csrc/attention_merge.cu: rows with source >= 0 merge o_a with o_b[source]
+    by their log-sum-exps; the others keep o_a."""
+    T, W = o_a.shape
+    QH = lse_a.shape[1]
+    D = W // QH
+    out = o_a.float().clone().view(T, QH, D)
+    rows = (source >= 0).nonzero().flatten()
+    if rows.numel():
+        src = source[rows].long()
+        la, lb = lse_a[rows].float(), lse_b[src].float()
+        m = torch.maximum(la, lb)
+        wa, wb = torch.exp(la - m).nan_to_num(0.0), torch.exp(lb - m).nan_to_num(0.0)
+        z = (wa + wb).clamp(min=1e-30)
+        a = o_a.float().view(T, QH, D)[rows]
+        b = o_b.float().view(-1, QH, D)[src]
+        out[rows] = (a * wa[..., None] + b * wb[..., None]) / z[..., None]
+    return out.view(T, W)
+
+
+def tree_attention(q, k_cache, v_cache, seqs, page_list, tree: dict, scale: float) -> torch.Tensor:
+    """The tree path in fp32: each row's read without the stacked shared segment (seqs_a), the
+    stacked readers' read of the shared segments (seqs_b over rows q[rows]), merged."""
+    o_a, lse_a = segmented_attention_lse(q, k_cache, v_cache, tree["seqs_a"], page_list, scale)
+    qb = q[tree["rows"].long()]
+    o_b, lse_b = segmented_attention_lse(qb, k_cache, v_cache, tree["seqs_b"], page_list, scale)
+    # rows the tree tables do not cover (one-token sequences) read as in the unified path
+    uncovered = torch.isinf(lse_a).all(dim=1) & (tree["source"].cpu() < 0).to(lse_a.device)
+    if bool(uncovered.any()):
+        full = segmented_attention(q, k_cache, v_cache, seqs, page_list, scale)
+        o_a[uncovered] = full[uncovered]
+    return merge_lse(o_a, lse_a, o_b, lse_b, tree["source"].to(o_a.device))
+
+
 def attention_tiles(seqs: torch.Tensor, block_q: int = 32) -> torch.Tensor:
     """[n_tiles, 2] int32 (sequence, first query row) covering every query row."""
     rows = []
