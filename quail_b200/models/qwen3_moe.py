@@ -152,15 +152,17 @@ class Qwen3MoePipeline:
         h = ops.embed_gather(chunk.ids, w.embed)
         x8, xs = ops.rmsnorm_quant_mx(h, w.layers[0]["ln1"], cfg.rms_eps)
         n = len(w.layers)
+        tm = self.ep.timer
         for li, L in enumerate(w.layers):
             kc, vc = arena.layer(li)
-            qkv = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
-            q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
-                                    cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
-            o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
-            ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
-            x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
-            xb = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
+            with tm("attention block (qkv, rope, attention, o_proj, norms)"):
+                qkv = ops.gemm_mx(x8, xs, L["wqkv"], L["sqkv"])
+                q = ops.qk_norm_rope_kv(qkv, chunk.positions, L["qn"], L["kn"], w.cos_sin, chunk.slots, kc, vc,
+                                        cfg.num_q_heads, cfg.num_kv_heads, cfg.rms_eps)
+                o8, os_ = ops.chunk_attention(q, kc, vc, chunk, self.scale, mx=True, tc=True)
+                ops.gemm_mx(o8, os_, L["wo"], L["so"], epi=ops.EPI_RESIDUAL, out=h, residual=h)
+                x8, xs = ops.rmsnorm_quant_mx(h, L["ln2"], cfg.rms_eps)
+                xb = ops.rmsnorm_quant(h, L["ln2"], cfg.rms_eps, fp8=False)
             nxt = w.layers[li + 1]["ln1"] if li + 1 < n else None
             r = self.ep.forward(x8, xs, xb, h, L, next_norm=nxt, eps=cfg.rms_eps)
             if r is not None:

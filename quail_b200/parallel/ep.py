@@ -42,6 +42,8 @@ class EPState:
         self.cfg = cfg
         self.device = torch.device(device)
         self.group = group
+        from quail_b200.utils.op_timer import OpTimer
+        self.timer = OpTimer()       # QB_OP_TIMING=1: device ms per MoE step (route, plan, dispatch + gate_up, ...)
         self.W = dist.get_world_size(group) if group is not None else 1
         self.rank = dist.get_rank(group) if group is not None else 0
         E, K, H, I = cfg.num_experts, cfg.top_k, cfg.hidden, cfg.moe_intermediate
@@ -154,30 +156,37 @@ class EPState:
         E, K = self.E, self.K
         self.epoch += 1
         ops.count_launch(5)
-        if M > 0:
-            logits = ops.gemm(xb, L["router"], bn=128)
-            ops.count_launch(1)
-            C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
-        else:
-            # a rank without tokens this step still serves its experts to the others
-            x8 = self.recv_a()[:0]
-        C.moe_plan(self.counts, self.peer("counts_all") if self.W > 1 else [],
-                   self.peer("cflag") if self.W > 1 else [], self.counts_all(), self.cflag(),
-                   self.plan, self.cum, self.rank, E, self.t_cap, self.epoch)
-        C.moe_sort(self.ids, self.pos, M * K, self.plan, E, self.src_list)
-        C.moe_gate_up(x8, xsf, self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
-                      self.peer("recv_a"), self.peer("recv_sf"), self.peer("recv_meta"), self.peer("recv_count"),
-                      self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
-        C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, self.recv_meta(), L["wd"], L["sd"],
-                   self.peer("comb"), self.peer("comb_counter"))
+        tm = self.timer
+        with tm("route"):
+            if M > 0:
+                logits = ops.gemm(xb, L["router"], bn=128)
+                ops.count_launch(1)
+                C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+            else:
+                # a rank without tokens this step still serves its experts to the others
+                x8 = self.recv_a()[:0]
+        with tm("plan (count exchange)"):
+            C.moe_plan(self.counts, self.peer("counts_all") if self.W > 1 else [],
+                       self.peer("cflag") if self.W > 1 else [], self.counts_all(), self.cflag(),
+                       self.plan, self.cum, self.rank, E, self.t_cap, self.epoch)
+            C.moe_sort(self.ids, self.pos, M * K, self.plan, E, self.src_list)
+        with tm("dispatch + gate_up"):
+            C.moe_gate_up(x8, xsf, self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
+                          self.peer("recv_a"), self.peer("recv_sf"), self.peer("recv_meta"),
+                          self.peer("recv_count"), self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"],
+                          L["sgu"], self.y, self.ysf)
+        with tm("down + combine push"):
+            C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, self.recv_meta(), L["wd"], L["sd"],
+                       self.peer("comb"), self.peer("comb_counter"))
         self.comb_units = (self.comb_units + M * K * (self.H // 128)) & 0xFFFFFFFF
         want = self.comb_units  # compared modulo 2^32 on the device
-        if next_norm is None:
-            C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, None, eps, None, None)
-            return None
-        y8 = torch.empty(M, self.H, dtype=torch.float8_e4m3fn, device=h.device)
-        ysf = torch.empty(ops.sf_bytes(M, self.H), dtype=torch.uint8, device=h.device)
-        C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, next_norm, eps, y8, ysf)
+        with tm("combine + norm"):
+            if next_norm is None:
+                C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, None, eps, None, None)
+                return None
+            y8 = torch.empty(M, self.H, dtype=torch.float8_e4m3fn, device=h.device)
+            ysf = torch.empty(ops.sf_bytes(M, self.H), dtype=torch.uint8, device=h.device)
+            C.moe_combine(self.comb(M), M, K, self.comb_counter(), want, h, next_norm, eps, y8, ysf)
         return y8, ysf
 
     # ------------------------------------------------------------ NCCL baseline
@@ -204,13 +213,17 @@ class EPState:
             self._nb = {"out": torch.empty(self.R_cap, H, dtype=torch.bfloat16, device=dev),
                         "ctr": torch.zeros(8, dtype=torch.int32, device=dev)}
         self.epoch += 1
-        if M > 0:
-            logits = ops.gemm(xb, L["router"], bn=128)
-            C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
-            ops.count_launch(1)
-            ids = self.ids[:M * K].long()
-        else:
-            ids = torch.zeros(0, dtype=torch.long, device=dev)
+        tm = self.timer
+        with tm("route"):
+            if M > 0:
+                logits = ops.gemm(xb, L["router"], bn=128)
+                C.moe_route(logits, E, K, self.ids, self.wts, self.pos, self.counts)
+                ops.count_launch(1)
+                ids = self.ids[:M * K].long()
+            else:
+                ids = torch.zeros(0, dtype=torch.long, device=dev)
+        sp = tm("counts all-to-all + host split sizes + rows all-to-all + layout")
+        sp.__enter__()
         self.counts.zero_()
         order = torch.argsort(ids, stable=True)
         cnt_e = torch.bincount(ids, minlength=E).to(torch.int32)
@@ -265,30 +278,35 @@ class EPState:
             pv[tofs + self.t_cap:tofs + self.t_cap + len(tiles)] = t[:, 1]
             pv[tofs + 2 * self.t_cap:tofs + 2 * self.t_cap + len(tiles)] = t[:, 2]
         self.plan.copy_(pv, non_blocking=False)
+        sp.__exit__(None, None, None)
         ops.count_launch(2)
         e8 = x8[:0] if M > 0 else self.recv_a()[:0]
-        C.moe_gate_up(e8, self.recv_sf(), self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
-                      self.peer("recv_a")[self.rank:self.rank + 1] * W, self.peer("recv_sf")[:1] * W,
-                      self.peer("recv_meta")[:1] * W, self.peer("recv_count")[:1] * W,
-                      self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
+        with tm("gate_up"):
+            C.moe_gate_up(e8, self.recv_sf(), self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
+                          self.peer("recv_a")[self.rank:self.rank + 1] * W, self.peer("recv_sf")[:1] * W,
+                          self.peer("recv_meta")[:1] * W, self.peer("recv_count")[:1] * W,
+                          self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
         out = self._nb["out"]
-        C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, meta, L["wd"], L["sd"],
-                   [out.data_ptr()] * W, [self._nb["ctr"].data_ptr()] * W)
+        with tm("down"):
+            C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, meta, L["wd"], L["sd"],
+                       [out.data_ptr()] * W, [self._nb["ctr"].data_ptr()] * W)
         back = torch.empty(M * K, H, dtype=torch.bfloat16, device=dev)
-        dist.all_to_all_single(back, out[:n_recv], output_split_sizes=send_sizes, input_split_sizes=recv_sizes,
-                               group=g)
+        with tm("outputs all-to-all"):
+            dist.all_to_all_single(back, out[:n_recv], output_split_sizes=send_sizes,
+                                   input_split_sizes=recv_sizes, group=g)
         if M == 0:
             return None
-        items = torch.empty_like(back)
-        items[order] = back       # rows come back weighted by the expert owner's epilogue
-        zero = self._nb["ctr"][4:5]
-        ops.count_launch(1)
-        if next_norm is None:
-            C.moe_combine(items, M, K, zero, 0, h, None, eps, None, None)
-            return None
-        y8 = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
-        ysf = torch.empty(ops.sf_bytes(M, H), dtype=torch.uint8, device=dev)
-        C.moe_combine(items, M, K, zero, 0, h, next_norm, eps, y8, ysf)
+        with tm("combine + norm"):
+            items = torch.empty_like(back)
+            items[order] = back       # rows come back weighted by the expert owner's epilogue
+            zero = self._nb["ctr"][4:5]
+            ops.count_launch(1)
+            if next_norm is None:
+                C.moe_combine(items, M, K, zero, 0, h, None, eps, None, None)
+                return None
+            y8 = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+            ysf = torch.empty(ops.sf_bytes(M, H), dtype=torch.uint8, device=dev)
+            C.moe_combine(items, M, K, zero, 0, h, next_norm, eps, y8, ysf)
         return y8, ysf
 
 

@@ -98,6 +98,7 @@ def main():
     if world > 1:
         dist.barrier()
     wl, ex, run = region(args.rows, 1000 + rank)
+    pipe.ep.timer.reset()
     sampler = ClockSampler(local).start()
     launches0 = ops.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -107,6 +108,7 @@ def main():
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = s.elapsed_time(e)
+    ops_ms = pipe.ep.timer.summary()   # QB_OP_TIMING=1: device ms per MoE step over the timed region (this rank)
     launches = ops.launch_count() - launches0
     err = ops.read_and_clear_error(local)
     gen = sum(len(r.values.get("map", [])) for r in run.results)
@@ -131,6 +133,7 @@ def main():
             "rows": int(t[1]), "generated_tokens": int(t[3]), "passes_max": int(mx[4]) if world > 1 else int(t[4]),
             "seconds": round(sec, 3), "max_new": args.max_new, "page_tokens": args.page_tokens,
             "chunk_tokens": args.chunk_tokens, "gpu_launches": launches, "kernel_error": err_max,
+            **({"op_ms_rank0": ops_ms} if ops_ms else {}),
             "clocks": clocks,
         }), flush=True)
     if world > 1:
