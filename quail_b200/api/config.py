@@ -79,7 +79,7 @@ def check_config(config: EngineConfig, registry=None):
     if config.device not in DEVICES:
         raise RefusalError(Refusal(reasons=(f"unknown device {config.device!r}; devices: {list(DEVICES)}",),
                                    constraint="unknown_device"))
-    if config.backend != "quail":
+    if config.backend != "quail" and (registry is None or registry.backend(config.backend) is None):
         raise RefusalError(Refusal(reasons=(f"unknown backend {config.backend!r}",), constraint="unknown_backend"))
     if config.gpus not in (1, 2, 4, 8):
         raise RefusalError(Refusal(reasons=(f"gpus must be 1, 2, 4 or 8, not {config.gpus}",),

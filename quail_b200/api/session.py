@@ -200,6 +200,12 @@ class Session:
     def engine(self):
         """The model engine (started on first use: weights loaded, arena sized)."""
         if self._engine is None:
+            factory = (self.registry.backend(self.config.backend)
+                       if self.config.backend != "quail" and self.registry is not None else None)
+            if factory is not None:
+                # a comparison backend (quail_b200.baselines): the same SQL, another engine
+                self._engine = factory(self.config, self.registry)
+                return self._engine
             if self.config.gpus > 1:
                 from quail_b200.runtime.workers import WorkerPool
                 self._engine = WorkerPool(self.config, registry=self.registry)

@@ -26,6 +26,7 @@ class ExtensionRegistry:
         self.models: dict = {}
         self.devices: dict = {}
         self.rules: dict[str, Callable[[dict], dict]] = {}
+        self.backends: dict[str, Callable] = {}
 
     # models ---------------------------------------------------------
     def register_model(self, name: str, config) -> None:
@@ -54,6 +55,19 @@ class ExtensionRegistry:
         if name in self.devices:
             return self.devices[name]
         return self.parent.device(name) if self.parent is not None else None
+
+    # backends -------------------------------------------------------
+    def register_backend(self, name: str, factory: Callable) -> None:
+        """An engine other than this one's (factory(config, registry) -> an object with run_region),
+        named by EngineConfig.backend; `quail_b200.baselines.register_baselines` adds "vllm"."""
+        if name == "quail" or name in self.backends:
+            raise ValueError(f"backend {name!r} is already registered")
+        self.backends[name] = factory
+
+    def backend(self, name: str):
+        if name in self.backends:
+            return self.backends[name]
+        return self.parent.backend(name) if self.parent is not None else None
 
     # logical rules --------------------------------------------------
     def register_rule(self, name: str, rule: Callable[[dict], dict]) -> None:
