@@ -113,6 +113,23 @@ class ModelEngine:
             from quail_b200.models.decision import DecisionHead, head_tensors
             self.model.decision = DecisionHead(head_tensors(ckpt), self.device)
 
+    images = None       # engine.images.ImageStore of a model with a vision tower
+    vision = None       # its vision tower (models/vision.py)
+
+    def _attach_vision(self, ckpt) -> None:
+        """A Qwen3.5 model's vision tower and the store of its regions' images."""
+        if not self.cfg.has_vision:
+            return
+        from quail_b200.engine.images import ImageStore
+        if self.on_gpu:
+            from quail_b200.models.vision import VisionPipeline
+            self.vision = VisionPipeline(self.cfg, ckpt, self.device)
+        else:
+            from quail_b200.models.vision import VisionReference
+            self.vision = VisionReference(self.cfg, ckpt, device="cpu")
+        self.images = ImageStore(self.cfg, int(self.config.extra.get("image_longest", 1024)))
+        self.model.images = self.images
+
     def _build(self, pages: int | None):
         from quail_b200.engine.arena import KVArena
         from quail_b200.engine.stage_executor import StageExecutor
@@ -147,12 +164,15 @@ class ModelEngine:
                 self.model = CpuModel(self.cfg, ckpt, device="cpu")
                 page_tokens, dtype = 16, torch.float32
             self._attach_head(ckpt)
+            self._attach_vision(ckpt)
             del ckpt
             n_pages = pages or self.budgets.arena_pages(page_tokens)
             self.arena = KVArena.for_model(self.cfg, n_pages, page_tokens, device=self.device, dtype=dtype,
                                            state_slots=self.budgets.state_slots(self.cfg))
             self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
                                           gpu_timing=self.config.gpu_timing, attention=self._attention_path())
+            if self.images is not None:
+                self.executor.packer.images = self.images
             return
         if self.on_gpu:
             from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights
@@ -238,6 +258,13 @@ class ModelEngine:
     def tokenize_doc(self, doc) -> np.ndarray:
         if isinstance(doc, np.ndarray):
             return doc.astype(np.int32)
+        if isinstance(doc, (bytes, bytearray, memoryview)):
+            # an image document (AI.IMAGE): the vision tower reads it
+            if self.images is None:
+                from quail_b200.api.config import Refusal, RefusalError
+                raise RefusalError(Refusal(reasons=(f"{self.cfg.name!r} has no vision tower to read an image",),
+                                           constraint="unsupported_function"))
+            return self.images.add(bytes(doc))
         if isinstance(doc, (list, tuple)) and (not doc or isinstance(doc[0], (int, np.integer))):
             return np.asarray(doc, dtype=np.int32)
         return self.tokenizer.encode("" if doc is None else str(doc))
@@ -392,7 +419,12 @@ class ModelEngine:
         # one read per distinct document (and, with guards, per distinct guard inputs)
         guarded = [c.guard for c in calls if c.guard is not None]
         keys, uniq, where, rep = {}, [], [], []
-        for i, t in enumerate(self.tokenize_docs(docs)):
+        if self.images is not None:
+            self.images.clear()
+        toks = self.tokenize_docs(docs)
+        if self.images is not None:
+            self.images.encode(self.vision)
+        for i, t in enumerate(toks):
             k = t.tobytes()
             if guarded:
                 k = (k, tuple(G.signature(g, i) for g in guarded))

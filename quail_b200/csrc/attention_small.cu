@@ -351,8 +351,10 @@ void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const
                            QH, KH, sl2, out, gp, ldg, (int)gate_hstride, dev);                                    \
     return;                                                                                                       \
   }
+  QB_SMALL(64, 1)
   QB_SMALL(64, 2)
   QB_SMALL(64, 4)
+  QB_SMALL(128, 1)
   QB_SMALL(128, 4)
   QB_SMALL(256, 2)
   QB_SMALL(256, 4)
@@ -374,7 +376,7 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
                                          const __nv_bfloat16* __restrict__ kw, int offset,
                                          const float* __restrict__ cos_sin, int rd, const int* __restrict__ slots,
                                          __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
-                                         __nv_bfloat16* __restrict__ q_out, int T, float eps) {
+                                         __nv_bfloat16* __restrict__ q_out, int T, float eps, int sec_h, int sec_w) {
   constexpr int E = D / 32;
   const int lane = threadIdx.x & 31;
   const int widx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -408,12 +410,19 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
       x[e] = x[e] * r * wv;
     }
     const int half = rd / 2;
-    const int pos = positions[t];
     const int xorl = half / E;  // lanes between a dim and its partner
+    // sec_h / sec_w > 0: interleaved multimodal RoPE, positions [T, 3] (time, height, width);
+    // frequency pair p follows height when p % 3 == 1 and p < 3 sec_h, width when p % 3 == 2
+    // and p < 3 sec_w, else time
+    const bool mrope = sec_h > 0 || sec_w > 0;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const float partner = __shfl_xor_sync(0xffffffffu, x[e], xorl);
       const int i = lane * E + e;
+      const int pr = i < half ? i : i - half;
+      int stream = 0;
+      if (mrope) stream = (pr % 3 == 1 && pr < 3 * sec_h) ? 1 : ((pr % 3 == 2 && pr < 3 * sec_w) ? 2 : 0);
+      const int pos = mrope ? positions[(size_t)t * 3 + stream] : positions[t];
       if (i < half) {
         const float c = cos_sin[(size_t)pos * rd + i], sn = cos_sin[(size_t)pos * rd + half + i];
         x[e] = x[e] * c - partner * sn;
@@ -440,11 +449,13 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
 void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated, const torch::Tensor& positions,
                        const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
                        const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
-                       torch::Tensor& q_out, double eps) {
+                       torch::Tensor& q_out, double eps, int64_t sec_h, int64_t sec_w) {
   const int T = proj.size(0), D = k_cache.size(3), rd = cos_sin.size(1);
   TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.stride(1) == 1, "proj bf16");
   TORCH_CHECK(q_out.is_contiguous() && q_out.size(2) == D, "q_out [T, QH, D]");
   TORCH_CHECK(rd <= D && rd % 2 == 0 && ((rd / 2) % (D / 32)) == 0, "rotary dims");
+  TORCH_CHECK((sec_h == 0 && sec_w == 0) ? positions.dim() == 1 : (positions.dim() == 2 && positions.size(1) == 3),
+              "positions: [T], or [T, 3] (time, height, width) with multimodal RoPE sections");
   if (T == 0) return;
   const int dev = proj.get_device();
   c10::cuda::CUDAGuard guard(dev);
@@ -458,7 +469,7 @@ void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool g
         reinterpret_cast<const __nv_bfloat16*>(kw.data_ptr()), offset ? 1 : 0, cos_sin.data_ptr<float>(), rd,  \
         slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),                          \
         reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-        T, (float)eps);                                                                                         \
+        T, (float)eps, (int)sec_h, (int)sec_w);                                                                 \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                             \
     return;                                                                                                     \
   }

@@ -110,7 +110,7 @@ void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const
 void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated, const torch::Tensor& positions,
                        const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
                        const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
-                       torch::Tensor& q_out, double eps);
+                       torch::Tensor& q_out, double eps, int64_t sec_h, int64_t sec_w);
 void short_conv(const torch::Tensor& bcx, const torch::Tensor& wconv, const torch::Tensor& seqs,
                 const torch::Tensor& state_io, torch::Tensor& state, int64_t li, torch::Tensor& y);
 

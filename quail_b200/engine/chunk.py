@@ -82,6 +82,7 @@ class Chunk:
     full_readout: bool = False  # readout rows also need full-vocabulary argmax / log-sum-exp
     topk: bool = False          # and the top-k token ids and logits (ops.READOUT_TOPK)
     tree: dict | None = None    # the tree path's tables (module docstring), None: unified
+    rope3: torch.Tensor | None = None   # [T, 3] rotary (time, height, width) positions of a model with images
 
 
 TREE_BLOCK = 64        # query rows per block of the persistent attention kernel
@@ -108,6 +109,11 @@ class ChunkPacker:
                  tree_min_tokens: int = 64):
         if tree not in ("unified", "tree", "auto"):
             raise ValueError(f"attention path is 'unified', 'tree' or 'auto', not {tree!r}")
+        # a model with a vision tower: the engine's ImageStore; each chunk then carries the
+        # multimodal rotary positions of its tokens, and `rope_shift` what each key's image
+        # tokens moved its rotary positions behind its KV positions
+        self.images = None
+        self.rope_shift: dict = {}
         self.tree = tree
         self.tree_min_tokens = tree_min_tokens
         self.pool = pool
@@ -129,6 +135,11 @@ class ChunkPacker:
         for sz in sizes:
             views.append(dev[o:o + sz])
             o += sz
+        rope3 = None
+        if self.images is not None and n_tok:
+            r3 = self.rope3_parts(specs)
+            host["rope3"] = r3
+            rope3 = self._upload_plain(r3.reshape(-1)).view(-1, 3)
         tree = self.tree_parts(specs, host) if self.tree != "unified" and n_tok else None
         tree_dev = None
         up = int(flat.nbytes)
@@ -148,7 +159,7 @@ class ChunkPacker:
         return Chunk(num_tokens=n_tok, ids=views[0], positions=views[1], slots=views[2],
                      seqs=views[3].view(-1, SEQ_INTS), tiles=views[4].view(-1, 2), page_list=views[5],
                      final_rows=views[6], dseqs=views[7], state_io=views[8].view(-1, 2),
-                     blocks=views[9].view(-1, 2), readout_tags=tags, tree=tree_dev,
+                     blocks=views[9].view(-1, 2), readout_tags=tags, tree=tree_dev, rope3=rope3,
                      num_seqs=len(specs), host=host, upload_bytes=up,
                      full_readout=any(s.full and s.readout for s in specs),
                      topk=any(s.topk and s.readout for s in specs))
@@ -241,6 +252,19 @@ class ChunkPacker:
                 "blocks": np.asarray([(b[1], b[2]) for b in sorted(blocks, key=lambda b: -b[0])],
                                      dtype=i32).reshape(-1, 2)}
         return host, tags
+
+    def rope3_parts(self, specs: list[SeqSpec]) -> np.ndarray:
+        """[T, 3] int32 rotary positions of the chunk's tokens (engine/images.py)."""
+        parts = []
+        for s in specs:
+            shift = sum(self.rope_shift.get(k, 0) for k, _ in s.reads)
+            if s.own_start > 0:
+                shift = self.rope_shift.get(s.own_key, shift)
+            n = len(s.tokens)
+            r3, shift = self.images.rope_positions(s.tokens, np.arange(s.pos_start, s.pos_start + n), shift)
+            self.rope_shift[s.own_key] = shift
+            parts.append(r3)
+        return np.concatenate(parts).astype(np.int32)
 
     def tree_parts(self, specs: list[SeqSpec], host: dict) -> dict | None:
         """The tree path's tables for this chunk, or None when nothing is worth stacking."""

@@ -29,6 +29,9 @@ def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str,
                                  * cfg.init_std).bfloat16()
     from quail_b200.models.weights import random_sae
     out.update(random_sae(cfg, gen, device))
+    if cfg.has_vision:
+        from quail_b200.models.vision import random_vision
+        out.update(random_vision(cfg, gen, device))
     if cfg.decision_head:
         from quail_b200.models.decision import random_decision_head
         out.update(random_decision_head(cfg.hidden, cfg.decision_head_dim, gen, device))

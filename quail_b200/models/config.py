@@ -73,6 +73,20 @@ class DecoderConfig:
     read_span_tokens: int = 0        # the longest span a pointer read returns
     read_found: tuple = ()           # a pointer read's (raw, calibrated) P(found) knots
     answer_spellings: tuple = ()     # (true spellings, false spellings) read at a yes / no slot
+    # vision tower (Qwen3.5): a ViT over 16-pixel patches (2 frames per patch for a still image),
+    # 2x2 patches merged into one LM token; 0 layers = text only. The LM reads image tokens with
+    # interleaved multimodal RoPE over (time, height, width) position streams.
+    vision_depth: int = 0
+    vision_hidden: int = 0
+    vision_heads: int = 0
+    vision_intermediate: int = 0
+    vision_patch: int = 16
+    vision_merge: int = 2
+    vision_temporal: int = 2
+    vision_pos_embeddings: int = 2304
+    mrope_sections: tuple = (11, 11, 10)   # rotary frequency pairs per (t, h, w) stream, interleaved
+    vision_start_id: int = 248_053
+    vision_end_id: int = 248_054
 
     @property
     def bidirectional(self) -> bool:
@@ -114,6 +128,10 @@ class DecoderConfig:
     def attn_layers(self) -> list:
         """Indices of the layers with a KV cache."""
         return [i for i in range(self.layers) if self.kind(i) in ("attn", "swa")]
+
+    @property
+    def has_vision(self) -> bool:
+        return self.vision_depth > 0
 
     @property
     def set_attention(self) -> bool:
@@ -200,6 +218,9 @@ QWEN35_4B = DecoderConfig(name="qwen3.5-4b", layers=32, hidden=2560, num_q_heads
                           gdn_key_heads=16,
                           gdn_value_heads=32, gdn_key_dim=128, gdn_value_dim=128, conv_width=4,
                           max_position=262_144)
+# Qwen3.5's vision tower (Hugging Face Qwen3_5VisionConfig defaults: 27 layers, width 1152, 16 heads)
+_Q35_VISION = dict(vision_depth=27, vision_hidden=1152, vision_heads=16, vision_intermediate=4304)
+QWEN35_VL_4B = QWEN35_4B.with_(name="qwen3.5-4b-vl", **_Q35_VISION)
 QWEN35_TINY = QWEN35_4B.with_(name="qwen3.5-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2,
                               head_dim=64, intermediate=512, vocab=151_936, gdn_key_heads=2, gdn_value_heads=4,
                               gdn_key_dim=32, gdn_value_dim=32, layer_kinds=_Q35_KINDS, max_position=40_960)
@@ -300,6 +321,14 @@ D1_GPU_TINY = D1_2B.with_(name="d1-gpu-tiny", layers=4, hidden=1024, num_q_heads
                           intermediate=1024, vocab=4096, layer_kinds=("conv", "attn", "conv", "swa"), set_size=4,
                           sliding_window=64, read_span_tokens=64, max_position=8192)
 
+# the smallest hybrids with a vision tower (the CPU model, the GPU kernels' shapes)
+QWEN35_VL_TINY = QWEN35_TINY.with_(name="qwen3.5-vl-tiny", vision_depth=2, vision_hidden=96, vision_heads=4,
+                                   vision_intermediate=192, vision_pos_embeddings=64, mrope_sections=(3, 3, 2),
+                                   vision_start_id=151_933, vision_end_id=151_934)
+QWEN35_VL_GPU_TINY = QWEN35_GPU_TINY.with_(name="qwen3.5-vl-gpu-tiny", vision_depth=2, vision_hidden=256,
+                                           vision_heads=4, vision_intermediate=512, vision_pos_embeddings=256,
+                                           vision_start_id=4093, vision_end_id=4094)
+
 CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWEN3_TINY, QWEN3_GPU_TINY,
                                QWEN3_GPU_TINY_GQA4,
                                QWEN3_MOE_GPU_TINY, QWEN3_4B_SAE, QWEN3_SAE_TINY, QWEN3_GPU_SAE_TINY,
@@ -309,7 +338,8 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                QWEN35_4B_FP8, QWEN35_GPU_TINY_FP8, RERANKER_GPU_TINY, QWEN35_27B_FP8, QWEN38_27B_FP8,
                                QWEN36_35B_A3B, QWEN36_MOE_GPU_TINY, QWEN36_MOE_TINY, QWEN38_27B_NVFP4,
                                QWEN35_GPU_TINY_NVFP4, MAMMOTH_1, ELEPHANT_1, MAMMOTH_TINY, MAMMOTH_GPU_TINY,
-                               ISOLATED_DENSE_TINY, D1_2B, D1_TINY, D1_GPU_TINY)}
+                               ISOLATED_DENSE_TINY, D1_2B, D1_TINY, D1_GPU_TINY, QWEN35_VL_4B, QWEN35_VL_TINY,
+                               QWEN35_VL_GPU_TINY)}
 
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
@@ -358,5 +388,8 @@ MODEL_CONFIGS = {
     "isolated-dense-tiny": ISOLATED_DENSE_TINY,
     "d1-2b-bf16": D1_2B,
     "d1-tiny": D1_TINY,
+    "qwen3.5-4b-vl-bf16": QWEN35_VL_4B,
+    "qwen3.5-vl-tiny": QWEN35_VL_TINY,
+    "qwen3.5-vl-gpu-tiny": QWEN35_VL_GPU_TINY,
     "d1-gpu-tiny": D1_GPU_TINY,
 }

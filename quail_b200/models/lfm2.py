@@ -207,7 +207,7 @@ class Lfm2Pipeline:
                 q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=self.device)
                 ops.count_launch(1)
                 C.hybrid_qk_rope_kv(p, QH, KH, False, chunk.positions, L["qn"], L["kn"], False, self.cos_sin,
-                                    chunk.slots, kc, vc, q, cfg.rms_eps)
+                                    chunk.slots, kc, vc, q, cfg.rms_eps, 0, 0)
                 o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=self.device)
                 ops.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,
                                   None, 0)

@@ -298,7 +298,7 @@ class Lfm3Pipeline:
                 q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=dev)
                 ops.count_launch()
                 C.hybrid_qk_rope_kv(p, QH, KH, False, pos_d, L["qn"], L["kn"], False, self.tables[kind], slots_d,
-                                    kc, vc, q, cfg.rms_eps)
+                                    kc, vc, q, cfg.rms_eps, 0, 0)
                 if kind == "attn":
                     ops.kv_copy_rows(kc, vc, src_d, dst_d)
                 o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=dev)

@@ -45,12 +45,30 @@ def rmsnorm_offset(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor
     return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())
 
 
-def rope_partial(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, rotary_dim: int) -> torch.Tensor:
-    """NeoX RoPE on the first `rotary_dim` dims of each head; the rest pass through."""
+def rope_partial(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, rotary_dim: int,
+                 sections=None) -> torch.Tensor:
+    """NeoX RoPE on the first `rotary_dim` dims of each head; the rest pass through. [T, 3]
+    positions (with `sections`) rotate by interleaved multimodal RoPE (ops.reference.rope_neox_3d)."""
+    def rot(y):
+        if positions.dim() == 2:
+            return ref.rope_neox_3d(y, positions, cos_sin, sections)
+        return ref.rope_neox(y, positions, cos_sin)
     if rotary_dim == x.shape[-1]:
-        return ref.rope_neox(x, positions, cos_sin)
-    rot = ref.rope_neox(x[..., :rotary_dim], positions, cos_sin)
-    return torch.cat([rot, x[..., rotary_dim:]], dim=-1)
+        return rot(x)
+    return torch.cat([rot(x[..., :rotary_dim]), x[..., rotary_dim:]], dim=-1)
+
+
+def image_embeddings(ids: torch.Tensor, embed: torch.Tensor, images) -> torch.Tensor:
+    """Token embeddings; ids at or above the image token base take their rows of the region's
+    vision-tower output (`images`: engine.images.ImageStore) instead of the text table."""
+    from quail_b200.engine.images import IMAGE_TOKEN_BASE
+    ids = ids.long()
+    img = ids >= IMAGE_TOKEN_BASE
+    h = embed[torch.where(img, torch.zeros_like(ids), ids)]
+    if images is not None and bool(img.any()):
+        table = images.table(h.device, h.dtype)
+        h[img] = table[ids[img] - IMAGE_TOKEN_BASE]
+    return h
 
 
 def gdn_gates(a: torch.Tensor, b: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor):
@@ -216,8 +234,12 @@ class Qwen35Reference:
         q, gate = (qg[..., :D], qg[..., D:]) if cfg.attn_output_gate else (qg, None)
         k = (x @ L["wk"].t()).view(T, KH, D)
         v = (x @ L["wv"].t()).view(T, KH, D)
-        q = rope_partial(rmsnorm_offset(q, L["qn"], cfg.rms_eps), chunk.positions, self.cos_sin, cfg.rotary_dim)
-        k = rope_partial(rmsnorm_offset(k, L["kn"], cfg.rms_eps), chunk.positions, self.cos_sin, cfg.rotary_dim)
+        rope3 = getattr(chunk, "rope3", None)
+        pos = rope3 if rope3 is not None else chunk.positions
+        q = rope_partial(rmsnorm_offset(q, L["qn"], cfg.rms_eps), pos, self.cos_sin, cfg.rotary_dim,
+                         cfg.mrope_sections)
+        k = rope_partial(rmsnorm_offset(k, L["kn"], cfg.rms_eps), pos, self.cos_sin, cfg.rotary_dim,
+                         cfg.mrope_sections)
         ok = chunk.slots >= 0
         slots = chunk.slots[ok].long()
         kc.view(-1, KH, D)[slots] = k[ok].to(kc.dtype)
@@ -244,10 +266,12 @@ class Qwen35Reference:
         return self._q(ref.silu_mul(self._q(x) @ wg.t(), self._q(x) @ wu.t())) @ wd.t()
 
     # ------------------------------------------------------------ forward
+    images = None           # engine.images.ImageStore of a model with a vision tower
+
     @torch.no_grad()
     def hidden_chunk(self, chunk, arena) -> torch.Tensor:
         cfg = self.cfg
-        h = self.embed[chunk.ids.long()]
+        h = image_embeddings(chunk.ids, self.embed, self.images) if cfg.has_vision else self.embed[chunk.ids.long()]
         gi = ai = 0
         for i, L in enumerate(self.layers):
             x = rmsnorm_offset(h, L["ln1"], cfg.rms_eps)

@@ -40,6 +40,8 @@ def _pad_rows(w: torch.Tensor, multiple: int = 16) -> torch.Tensor:
 class Qwen35Pipeline:
     """Forward pass of a packed chunk of a Qwen3.5 hybrid on the GPU kernels."""
 
+    images = None           # engine.images.ImageStore of a model with a vision tower
+
     def __init__(self, cfg: DecoderConfig, ckpt: dict[str, torch.Tensor], device, head_rows=None,
                  max_tokens: int = 16384):
         from quail_b200.ops.quant import (interleave_gate_up, interleave_gate_up_mx, quantize_nvfp4,
@@ -184,7 +186,11 @@ class Qwen35Pipeline:
         dev = self.device
         QH, KH, D = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim
         Hk, Hv, dk, dv = cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_key_dim, cfg.gdn_value_dim
-        h = ops.embed_gather(chunk.ids, self.embed)
+        if self.cfg.has_vision and self.images is not None and getattr(chunk, "rope3", None) is not None:
+            from quail_b200.models.qwen3_5 import image_embeddings
+            h = image_embeddings(chunk.ids, self.embed, self.images).contiguous()
+        else:
+            h = ops.embed_gather(chunk.ids, self.embed)
         gi = ai = 0
         for i, L in enumerate(self.layers):
             if cfg.kind(i) == "gdn":
@@ -208,8 +214,11 @@ class Qwen35Pipeline:
                 kc, vc = arena.layer(ai)
                 q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=dev)
                 ops.count_launch(1)
-                C.hybrid_qk_rope_kv(p, QH, KH, cfg.attn_output_gate, chunk.positions, L["qn"], L["kn"],
-                                    cfg.norm_offset, self.cos_sin, chunk.slots, kc, vc, q, cfg.rms_eps)
+                rope3 = getattr(chunk, "rope3", None)
+                sec = cfg.mrope_sections if rope3 is not None else (0, 0, 0)
+                C.hybrid_qk_rope_kv(p, QH, KH, cfg.attn_output_gate, rope3 if rope3 is not None else chunk.positions,
+                                    L["qn"], L["kn"], cfg.norm_offset, self.cos_sin, chunk.slots, kc, vc, q,
+                                    cfg.rms_eps, sec[1], sec[2])
                 o = torch.empty(T, QH * D, dtype=torch.bfloat16, device=dev)
                 gate = p[:, D:] if cfg.attn_output_gate else None
                 ops.small_attention(q, kc, vc, chunk.seqs, chunk.tiles, chunk.dseqs, chunk.page_list, self.scale, o,

@@ -179,6 +179,9 @@ def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=tor
     if not cfg.tied_head:
         out["lm_head.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)
     out.update(random_sae(cfg, gen, device))
+    if cfg.has_vision:
+        from quail_b200.models.vision import random_vision
+        out.update(random_vision(cfg, gen, device))
     if cfg.decision_head:
         from quail_b200.models.decision import random_decision_head
         out.update(random_decision_head(cfg.hidden, cfg.decision_head_dim, gen, device))

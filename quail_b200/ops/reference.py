@@ -36,6 +36,30 @@ def rope_neox(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
 
 
+def mrope_streams(pairs: int, sections) -> torch.Tensor:
+    """[pairs] position stream (0 time, 1 height, 2 width) of each rotary frequency pair under
+    interleaved multimodal RoPE: pair p follows height when p % 3 == 1 and p < 3 * sections[1],
+    width when p % 3 == 2 and p < 3 * sections[2], else time."""
+    p = torch.arange(pairs)
+    s = torch.zeros(pairs, dtype=torch.long)
+    s[(p % 3 == 1) & (p < 3 * sections[1])] = 1
+    s[(p % 3 == 2) & (p < 3 * sections[2])] = 2
+    return s
+
+
+def rope_neox_3d(x: torch.Tensor, pos3: torch.Tensor, cos_sin: torch.Tensor, sections) -> torch.Tensor:
+    """rope_neox with [T, 3] positions: each frequency pair rotates by its stream's position."""
+    D = x.shape[-1]
+    half = D // 2
+    streams = mrope_streams(half, sections).to(pos3.device)
+    rows = pos3.long()[:, streams]                               # [T, half] table row per pair
+    cols = torch.arange(half, device=pos3.device)
+    cos = cos_sin[rows, cols[None, :]][:, None, :]
+    sin = cos_sin[rows, half + cols[None, :]][:, None, :]
+    x1, x2 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return F.silu(gate.float()) * up.float()
 

@@ -68,7 +68,7 @@ def test_hybrid_qk_rope_kv():
     slots = torch.randperm(128, device=DEV)[:T].int()
     slots[3] = -1
     q = torch.empty(T, QH, D, dtype=torch.bfloat16, device=DEV)
-    ops.native().hybrid_qk_rope_kv(proj, QH, KH, True, pos, qw, kw, True, cs, slots, kc, vc, q, 1e-6)
+    ops.native().hybrid_qk_rope_kv(proj, QH, KH, True, pos, qw, kw, True, cs, slots, kc, vc, q, 1e-6, 0, 0)
     qg = proj[:, :QH * 2 * D].view(T, QH, 2 * D)
     want_q = Q.rope_partial(Q.rmsnorm_offset(qg[..., :D], qw, 1e-6), pos, cs, rd)
     assert rel_err(q, want_q) < 1e-2
