@@ -74,8 +74,8 @@ def position_table(cfg: DecoderConfig, table: torch.Tensor, gh: int, gw: int) ->
     """The learned square position table bilinearly resampled to a gh x gw patch grid, in patch
     order (merged-token blocks, as patches_of)."""
     side = int(round(math.sqrt(table.shape[0])))
-    hs = torch.linspace(0, side - 1, gh, dtype=torch.float64)
-    ws = torch.linspace(0, side - 1, gw, dtype=torch.float64)
+    hs = torch.linspace(0, side - 1, gh, dtype=torch.float64, device=table.device)
+    ws = torch.linspace(0, side - 1, gw, dtype=torch.float64, device=table.device)
     h0, w0 = hs.floor().long(), ws.floor().long()
     h1, w1 = (h0 + 1).clamp(max=side - 1), (w0 + 1).clamp(max=side - 1)
     dh, dw = (hs - h0).float(), (ws - w0).float()
