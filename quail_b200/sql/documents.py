@@ -6,7 +6,9 @@ image.rs). AI.PARSE_DOCUMENT here reads the text a PDF stores: it inflates
 the content streams and collects the strings shown by Tj / TJ / ' / "
 operators between BT and ET. AI.IMAGE shrinks an image (PNG / JPEG bytes) so
 its longer side is at most `longest_edge` pixels and returns PNG bytes.
-AI.PDF_PAGES needs a PDF rasterizer and is refused here.
+AI.PDF_PAGES(pdf [, longest_edge [, first [, last]]]) draws each page as a PNG
+(`sql/pdf_render.py`) and returns list<struct<page int32, image binary>>, one
+entry per page, for UNNEST and a vision model.
 """
 
 from __future__ import annotations
@@ -102,6 +104,17 @@ def call(name: str, args: list, n: int):
     if name == "AI.IMAGE":
         edges = col(args[1])
         return pa.array([image(x, e) for x, e in zip(col(args[0]), edges)], pa.binary())
+    if name == "AI.PDF_PAGES":
+        from quail_b200.sql.pdf_render import DEFAULT_LONGEST_EDGE, pdf_pages
+        pdfs = col(args[0])
+        edges = col(args[1]) if len(args) > 1 else [DEFAULT_LONGEST_EDGE] * n
+        firsts = col(args[2]) if len(args) > 2 else [1] * n
+        lasts = col(args[3]) if len(args) > 3 else [None] * n
+        out = [pdf_pages(d, int(e or DEFAULT_LONGEST_EDGE), int(f or 1), None if la is None else int(la))
+               for d, e, f, la in zip(pdfs, edges, firsts, lasts)]
+        return pa.array(out, PDF_PAGES_TYPE)
     from quail_b200.api.config import Refusal, RefusalError
-    raise RefusalError(Refusal(reasons=(f"{name} needs a PDF rasterizer, which this build does not have",),
-                               constraint="unsupported_function"))
+    raise RefusalError(Refusal(reasons=(f"unknown document function {name}",), constraint="unsupported_function"))
+
+
+PDF_PAGES_TYPE = pa.list_(pa.struct([("page", pa.int32()), ("image", pa.binary())]))

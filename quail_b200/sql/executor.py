@@ -48,6 +48,8 @@ from quail_b200.api import prompts as P
 FEATURE_LIST = pa.list_(pa.struct([("feature", pa.int32()), ("strength", pa.float32())]))
 
 CPU_AI_FUNCTIONS = ("AI.PARSE_DOCUMENT", "AI.PDF_PAGES", "AI.IMAGE")
+# Snowflake spellings of the document functions
+CPU_ALIASES = {"AI_PARSE_DOCUMENT": "AI.PARSE_DOCUMENT", "AI_PDF_PAGES": "AI.PDF_PAGES", "AI_IMAGE": "AI.IMAGE"}
 MODEL_AI_FUNCTIONS = ("AI.IF", "AI_FILTER", "AI.SCORE", "AI.CLASSIFY", "AI.EXTRACT", "AI.EXTRACT_SPAN",
                       "AI.MAP", "AI.SAE_FEATURES")
 AGGREGATES = ("COUNT", "SUM", "AVG", "MIN", "MAX", "ARRAY_AGG", "ANY_VALUE")
@@ -992,8 +994,17 @@ class Executor:
         self.ai_values = dict(pre or {})
         self.compute_ai(rel, [it["expr"] for it in items])
         names, arrays = [], []
+        unnest = None
         for it in items:
             e = it["expr"]
+            if e.get("type") == "call" and e.get("name") == "UNNEST":
+                # one row per element of the list; the other items repeat per row
+                if unnest is not None or len(e.get("args", [])) != 1:
+                    raise QueryError("a SELECT list takes one UNNEST of one list")
+                unnest = len(arrays)
+                names.append(it.get("alias") or "unnest")
+                arrays.append(_as_array(self.eval(e["args"][0], rel), rel.num_rows))
+                continue
             if e.get("type") == "star":
                 for i, (q, n) in enumerate(rel.cols):
                     if e.get("table") is None or (q or "").lower() == e["table"].lower():
@@ -1005,6 +1016,14 @@ class Executor:
             names.append(it.get("alias") or expr_name(e))
             arrays.append(_as_array(self.eval(e, rel), rel.num_rows))
         self.ai_values = {}
+        if unnest is not None:
+            lst = arrays[unnest]
+            if isinstance(lst, pa.ChunkedArray):
+                lst = lst.combine_chunks()
+            if not pa.types.is_list(lst.type) and not pa.types.is_large_list(lst.type):
+                raise QueryError(f"UNNEST takes a list, not {lst.type}")
+            parents = pc.list_parent_indices(lst)
+            arrays = [pc.list_flatten(lst) if i == unnest else pc.take(a, parents) for i, a in enumerate(arrays)]
         return pa.Table.from_arrays(arrays, names=_dedupe(names))
 
     def stream(self, tree: dict, batch_rows: int = 65_536, limit: int | None = None):
@@ -1289,10 +1308,13 @@ class Executor:
             return self.eval(e["args"][0], rel)
         if name == "PROMPT":
             raise QueryError("PROMPT is the input of an AI function, not a value")
+        name = CPU_ALIASES.get(name, name)
         if name in CPU_AI_FUNCTIONS:
             from quail_b200.sql import documents
             args = [self.eval(a, rel) for a in e["args"]]
             return documents.call(name, args, rel.num_rows)
+        if name == "UNNEST":
+            raise QueryError("UNNEST expands a list into rows: it is an item of a SELECT list")
         args = [self.eval(a, rel) for a in e["args"] if a.get("type") != "named_arg"]
         fns = {
             "UPPER": lambda a: pc.utf8_upper(a[0]), "LOWER": lambda a: pc.utf8_lower(a[0]),
