@@ -269,12 +269,20 @@ class ModelEngine:
             return np.asarray(doc, dtype=np.int32)
         return self.tokenizer.encode("" if doc is None else str(doc))
 
+    token_store = None      # engine.token_store.TokenStore shared by a session's queries
+
     def tokenize_docs(self, docs: list) -> list[np.ndarray]:
-        """Token ids of every document; text goes through the tokenizer in one batch when it has one."""
+        """Token ids of every document; text goes through the tokenizer in one batch when it has
+        one, and through the session's token store when the engine has one."""
         batch = getattr(self.tokenizer, "encode_batch", None)
         texts = [i for i, d in enumerate(docs) if d is None or isinstance(d, str)]
         out = [None] * len(docs)
-        if batch is not None and len(texts) > 1:
+        if texts and self.token_store is not None:
+            enc = batch if batch is not None else (lambda xs: [self.tokenizer.encode(x) for x in xs])
+            for i, ids in zip(texts, self.token_store.encode_all(["" if docs[i] is None else docs[i]
+                                                                  for i in texts], enc)):
+                out[i] = ids
+        elif batch is not None and len(texts) > 1:
             for i, ids in zip(texts, batch(["" if docs[i] is None else docs[i] for i in texts])):
                 out[i] = ids
         return [self.tokenize_doc(d) if o is None else o for d, o in zip(docs, out)]

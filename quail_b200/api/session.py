@@ -16,6 +16,7 @@ work (fresh tokens, documents, passes, wall time) and the plan text. With
 
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -211,7 +212,11 @@ class Session:
                 self._engine = WorkerPool(self.config, registry=self.registry)
             else:
                 from quail_b200.api.engine import ModelEngine
+                from quail_b200.engine.token_store import TokenStore
                 self._engine = ModelEngine(self.config, registry=self.registry)
+                # documents tokenized once per session (QUAIL_TOKEN_STORE_TOKENS caps it)
+                cap = int(os.environ.get("QUAIL_TOKEN_STORE_TOKENS", "200000000"))
+                self._engine.token_store = TokenStore(cap) if cap > 0 else None
         return self._engine
 
     def interrupt(self) -> None:

@@ -447,7 +447,20 @@ class Executor:
         t = tree.get("type")
         if t == "explain":
             raise QueryError("EXPLAIN is answered by Query.explain()")
+        self.check_similar(tree)
         return self.query(tree)
+
+    def check_similar(self, tree: dict) -> None:
+        """Refuse calls written the same but for case, whitespace or punctuation; warn of calls a
+        typo apart (sql/similar.py)."""
+        from quail_b200.sql import similar
+        calls = [n for n in walk(tree) if is_model_call(n)]
+        for kind, a, b in similar.similar_calls(calls):
+            if kind == "spelling":
+                raise QueryError(similar.message(kind, a, b))
+            self.report.setdefault("warnings", []).append(similar.message(kind, a, b))
+            from quail_b200.utils import progress
+            progress.say(similar.message(kind, a, b))
 
     def query(self, node) -> pa.Table:
         saved = dict(self.ctes)

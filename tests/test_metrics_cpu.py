@@ -96,3 +96,19 @@ def test_kv_pool_cap_and_answer_admission_flags(monkeypatch, tmp_path):
         assert trace["samples"] and all(s[3] + s[4] == 64 for s in trace["samples"])
     # the admission rule changes when work starts, never the answers
     assert got["headroom"] == got["headroom=0"]
+
+
+def test_documents_are_tokenized_once_per_session():
+    with _session() as s:
+        s.sql("SELECT id FROM r WHERE AI.IF(PROMPT('Is {0} short?', body))").collect()
+        store = s.engine().token_store
+        misses = store.misses
+        assert misses == 5 and store.hits == 0          # five distinct bodies
+        s.sql("SELECT id, AI.SCORE(PROMPT('Is {0} long?', body)) AS p FROM r").collect()
+        assert store.misses == misses and store.hits >= 5
+        assert store.mean_tokens(["great music", "bad ending"]) > 0
+    from quail_b200.engine.token_store import TokenStore
+    small = TokenStore(capacity_tokens=3)
+    small.put("a", [1, 2])
+    small.put("b", [3, 4])
+    assert small.get("a") is None and len(small) == 1   # the oldest went out

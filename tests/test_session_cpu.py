@@ -259,3 +259,17 @@ def test_projection_calls_ride_in_the_filter_region(session):
     alone = session.sql("SELECT id FROM reviews WHERE AI.IF(PROMPT('Does the review discuss the ending? {0}', "
                         "body)) ORDER BY id").collect()
     assert res.table.column("id").to_pylist() == alone.column("id").to_pylist()
+
+
+def test_calls_written_almost_the_same(session):
+    from quail_b200.sql.similar import likeness
+    assert likeness("Is {0} rude?", "is {0} rude") == "spelling"
+    assert likeness("Is the review about the ending? {0}", "Is the reveiw about the ending? {0}") == "typo"
+    assert likeness("Is it from 2027? {0}", "Is it from 2028? {0}") is None
+    assert likeness("Is {0} long?", "Is {0} short?") is None
+    with pytest.raises(Exception, match="case, whitespace or punctuation"):
+        session.sql("SELECT id FROM reviews WHERE AI.IF(PROMPT('Is {0} rude?', body)) "
+                    "AND AI.IF(PROMPT('is {0} rude', body))").collect()
+    res = session.sql("SELECT id, AI.SCORE(PROMPT('Is the review about the ending? {0}', body)) AS a, "
+                      "AI.SCORE(PROMPT('Is the reveiw about the ending? {0}', body)) AS b FROM reviews").run()
+    assert any("a few letters" in w for w in res.report["warnings"])
