@@ -173,6 +173,11 @@ class ModelEngine:
                                           gpu_timing=self.config.gpu_timing, attention=self._attention_path())
             if self.images is not None:
                 self.executor.packer.images = self.images
+            elif self.on_gpu and getattr(self.model, "ep", None) is None and os.environ.get("QB_GRAPHS", "1") != "0":
+                # the token mixers' decode step reads its state slots from device metadata, so a
+                # decode pass of a hybrid is one graph too (not with images: their rotary positions
+                # are host-computed per pass; not with routed experts: their plan syncs the host)
+                self.executor.enable_graphs()
             return
         if self.on_gpu:
             from quail_b200.models.qwen3 import Qwen3Pipeline, Qwen3Weights

@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const __nv_bfloat16* __re
     }
     if (live) out[(size_t)(q0 + t) * C + c] = y;
   }
-  if (live)
+  if (live && dst >= 0)   // dst < 0: the state is not kept (a padding row of a replayed decode pass)
 #pragma unroll
     for (int j = 0; j < W - 1; ++j) conv_state[(((size_t)dst * G + gi) * (W - 1) + j) * C + c] = win[j];
 }
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(128 * PARTS) gdn_recurrent_kernel(
     if (live && part == 0) out[(size_t)(q0 + t) * Hv * DV + h * DV + j] = o;
     __syncthreads();
   }
-  if (live)
+  if (live && dst >= 0)
 #pragma unroll
     for (int i = 0; i < ROWS; ++i)
       ssm_state[(size_t)dst * slot_stride + head_off + (size_t)(r0 + i) * DV + j] = S[i];

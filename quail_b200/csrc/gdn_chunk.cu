@@ -379,6 +379,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(
     }
     __syncthreads();
   }
+  if (dst < 0) return;   // the state is not kept
   float* Sd = ssm_state + (size_t)dst * slot_stride + head_off;
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
@@ -832,6 +833,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(
     }
     __syncthreads();
   }
+  if (dst < 0) return;   // the state is not kept
   float* Sd = ssm_state + (size_t)dst * slot_stride + head_off;
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
@@ -937,6 +939,7 @@ __global__ void __launch_bounds__(128) gdn_conv_window_kernel(const __nv_bfloat1
     v[j] = pos >= 0 ? __bfloat162float(mixed[(size_t)(q0 + pos) * ldm + c])
                     : (src >= 0 ? conv_state[(((size_t)src * G + gi) * 3 + (3 + pos)) * C + c] : 0.f);
   }
+  if (dst < 0) return;   // the state is not kept
 #pragma unroll
   for (int j = 0; j < 3; ++j) conv_state[(((size_t)dst * G + gi) * 3 + j) * C + c] = v[j];
 }

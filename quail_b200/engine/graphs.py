@@ -11,8 +11,9 @@ token count (buckets 8, 16, 32, 64, 128, 256, 512, 1024):
     final rows, dseqs), so the captured kernels read fixed addresses;
   * a pass fills the buffer's host image (its real rows, then padding rows:
     token 0, no KV slot (-1, the write is skipped), one own segment of one
-    token on the arena's page 0, read and discarded), copies it with one
-    H2D copy and replays the graph;
+    token on the arena's page 0, read and discarded, and for hybrid models
+    no state slot (state_io -1, -1: it starts from zeros and its state is
+    not written back)), copies it with one H2D copy and replays the graph;
   * the first pass of a bucket runs eagerly (its result is the pass's) and
     then captures; a page list longer than the bucket's capacity recaptures
     with twice the capacity; new answer rows (another query) drop the graphs.
@@ -85,6 +86,9 @@ class _Entry:
         pad[:, 8] = self.pl_cap         # on the page at the last page-list entry (page 0)
         img["page_list"][:pl.size] = pl
         img["final_rows"][:host["final_rows"].size] = host["final_rows"]
+        if "state_io" in host:
+            # hybrid models: real rows carry their state slots; padding starts from zeros and keeps nothing
+            img["state_io"][:T] = np.asarray(host["state_io"]).reshape(-1, 2)[:T]
         flat = np.concatenate([img[k].reshape(-1) for k in PARTS])
         if self.copy_done is not None:
             self.copy_done.synchronize()

@@ -40,3 +40,25 @@ def test_graph_replays_match_eager(model):
     assert ops.read_and_clear_error(0) == 0
     assert all(len(g) == 12 for g in graphed)
     assert graphed == eager
+
+
+@pytest.mark.parametrize("model", ["qwen3.5-gpu-tiny", "lfm2-gpu-tiny"])
+def test_hybrid_graph_replays_match_eager(model):
+    """Hybrids: the token mixers' decode step reads and writes its state slots through the
+    graph's state_io rows; padding rows start from zeros and write no state."""
+    from quail_b200 import ops
+    from quail_b200.engine.arena import KVArena
+    from quail_b200.models.build import build_pipeline
+    from quail_b200.models.config import MODEL_CONFIGS
+    cfg = MODEL_CONFIGS[model]
+    dev = torch.device("cuda", 0)
+    pipe = build_pipeline(cfg, dev, answer_ids=list(range(8)))
+
+    def arena():
+        return KVArena.for_model(cfg, 512, 128, device=dev, dtype=torch.bfloat16, state_slots=96)
+    eager, _ = _run(pipe, arena(), False, rows=37)
+    graphed, ex = _run(pipe, arena(), True, rows=37)
+    assert ex.graphs.captures >= 1 and ex.graphs.replays >= 1
+    assert ops.read_and_clear_error(0) == 0
+    assert all(len(g) == 12 for g in graphed)
+    assert graphed == eager
