@@ -47,6 +47,11 @@ class CallSpec:
     # demand guard (quail_b200.sql.guards): the call is asked on an input row only where
     # this formula is TRUE; its `ai` leaves name earlier calls of the same list
     guard: dict | None = None
+    # map: decide(text so far) -> "true" | "not_true" | "undecided" for the WHERE test of the
+    # answer alone (quail_b200.sql.partial); the answer stops once it is decided NOT TRUE, or
+    # decided TRUE when `stop_when_true` (nothing else reads the answer)
+    stop: object = None
+    stop_when_true: bool = False
 
 
 @dataclass
@@ -496,6 +501,8 @@ class ModelEngine:
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
                       offsets=offsets, copy=c.kind == "extract", drops=c.drops)
+            if c.stop is not None and c.kind == "map":
+                rc.stop_test = (lambda r, gen, c=c: self._stop_decision(c, gen))
             if c.guard is not None:
                 deps = G.calls_of(c.guard)
                 rc.after = tuple(j for j, o in enumerate(calls) if o.name in deps)
@@ -606,6 +613,8 @@ class ModelEngine:
         del results
         stats = self._metrics(snap, len(uniq), len(docs), run.asked,
                               output_rows=sum(1 for u in where if run.results[u].kept))
+        if run.stopped_early:
+            stats["stopped_early"] = run.stopped_early
         return RegionOutput(values=values, stats=stats)
 
     def run_pairs(self, preamble: str, anchors: list, pairs: list, call: CallSpec) -> RegionOutput:
@@ -643,6 +652,12 @@ class ModelEngine:
         stats = self._metrics(snap, sum(1 for a in a_tok if len(a)), len(pairs), run.asked, pairs=len(pairs),
                               evaluated_document_pairs=len(pairs))
         return RegionOutput(values=[{call.name: v} for v in values], stats=stats)
+
+    def _stop_decision(self, c: CallSpec, generated) -> str:
+        """"stop" once call c's WHERE test is decided on the answer's text so far."""
+        from quail_b200.sql.partial import NOT_TRUE, TRUE, partial_text
+        d = c.stop(partial_text(self.tokenizer.decode(generated)))
+        return "stop" if d == NOT_TRUE or (d == TRUE and c.stop_when_true) else "continue"
 
     def _sql_values(self, calls: list[CallSpec], raw: dict, names) -> dict:
         """The SQL values of a row's answers so far (labels, decoded text), for guard tests."""

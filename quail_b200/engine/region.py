@@ -105,6 +105,9 @@ class Call:
     # lettered classify (slot_lm readout): the answer column of each option's letter; the
     # answer is the option whose letter has the largest logit at the last row
     letter_cols: list = field(default_factory=list)
+    # map: stop_test(row, tokens so far) -> "continue" | "stop": the answer ends early once a
+    # test of it is decided on its text so far (quail_b200.sql.partial)
+    stop_test: object = None
 
 
 @dataclass
@@ -127,6 +130,7 @@ class RegionRun:
         self.results = [RowResult() for _ in docs]
         self.asked = 0
         self.fresh_tokens = 0
+        self.stopped_early = 0                # answers ended once their test was decided
         self._next = [0] * len(docs)          # next call index to submit per row
         self._pending = [0] * len(docs)       # calls in flight per row
         self._label_parts: dict = {}
@@ -285,6 +289,10 @@ class RegionRun:
         stop = tok < 0 or tok in call.stop_ids
         if not stop:
             generated.append(tok)
+            if (call.stop_test is not None and len(generated) < call.max_tokens
+                    and call.stop_test(r, generated) == "stop"):
+                stop = True
+                self.stopped_early += 1
         if stop or len(generated) >= call.max_tokens:
             self.results[r].values[call.name] = generated
             self._copies.pop((r, ci), None)

@@ -205,6 +205,7 @@ class BoundCall:
     letters: list = field(default_factory=list)      # lettered prompts: option i's answer letter
     drops: bool = True                               # filter: FALSE drops the row (WHERE chains)
     guard: dict | None = None                        # demand guard (quail_b200.sql.guards)
+    stop: dict | None = None                         # map: WHERE test decided on partial answers
 
 
 def _options(node) -> dict:
@@ -448,6 +449,11 @@ class Executor:
         if t == "explain":
             raise QueryError("EXPLAIN is answered by Query.explain()")
         self.check_similar(tree)
+        # how often each model call is written in the whole statement (answer stops read it)
+        self.call_counts: dict = {}
+        for n in walk(tree):
+            if is_model_call(n):
+                self.call_counts[node_key(n)] = self.call_counts.get(node_key(n), 0) + 1
         return self.query(tree)
 
     def check_similar(self, tree: dict) -> None:
@@ -698,10 +704,26 @@ class Executor:
                                   [b.selectivity if b.selectivity is not None else 0.5 for b in bound])
             rel = self.run_filters(rel, [bound[i] for i in order])
         for c in others:
-            self.compute_ai(rel, [c])
+            self.compute_ai(rel, [c], stops=self._answer_stops(c))
             rel = rel.filter(_as_mask(self.eval(c, rel)))
             self.ai_values = {}
         return rel
+
+    def _answer_stops(self, conjunct) -> dict:
+        """The early stop of an AI.MAP answer that `conjunct` tests alone (quail_b200.sql.partial):
+        {call key: {"test": conjunct, "when_true": nothing else reads the answer}}."""
+        from quail_b200.sql import partial
+        if not self.pushdown:
+            return {}
+        calls = {node_key(n): n for n in walk(conjunct) if is_model_call(n)}
+        if len(calls) != 1:
+            return {}
+        (key, call), = calls.items()
+        if call["name"] != "AI.MAP" or not partial.reads_answer_alone(conjunct, key, node_key):
+            return {}
+        here = sum(1 for n in walk(conjunct) if is_model_call(n) and node_key(n) == key)
+        total = getattr(self, "call_counts", {}).get(key)
+        return {key: {"test": conjunct, "when_true": total is not None and total == here}}
 
     def run_filters(self, rel: Relation, calls: list[BoundCall]) -> Relation:
         """AI.IF calls as one guarded chain over the relation's documents."""
@@ -721,7 +743,7 @@ class Executor:
                         keep[i] = False
         return rel.filter(pa.array(keep))
 
-    def compute_ai(self, rel: Relation, exprs: list) -> None:
+    def compute_ai(self, rel: Relation, exprs: list, stops: dict | None = None) -> None:
         """Evaluate the model calls inside `exprs` on `rel`, each on the rows its guard asks for.
 
         Calls reading the same document under the same instruction share a
@@ -741,6 +763,7 @@ class Executor:
             b = bind_call(node, self.turn, self.model)
             b.drops = False
             b.guard = None if guard["op"] == "true" else guard
+            b.stop = (stops or {}).get(k)
             bound[k] = b
         n = rel.num_rows
         remaining = list(bound)
@@ -823,9 +846,14 @@ class Executor:
         if self.engine is None:
             raise QueryError("this query needs a model; the session has none")
         from quail_b200.api.engine import CallSpec
+        from quail_b200.sql import partial
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
                           probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read,
-                          letters=c.letters, drops=c.drops, guard=c.guard)
+                          letters=c.letters, drops=c.drops, guard=c.guard,
+                          stop=None if c.stop is None else (
+                              lambda text, c=c: partial.decide(c.stop["test"], c.key, partial.Completions(text),
+                                                               node_key)),
+                          stop_when_true=bool(c.stop and c.stop["when_true"]))
                  for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self._record(out.stats, "quail.region[" + ",".join(c.kind for c in calls) + "]")
@@ -837,6 +865,8 @@ class Executor:
         self.report["regions"].append(stats)
         for k in ("asked", "fresh_tokens", "passes"):
             self.report[k] += stats.get(k, 0)
+        if stats.get("stopped_early"):
+            self.report["stopped_early"] = self.report.get("stopped_early", 0) + stats["stopped_early"]
         self.report["evaluated_documents"] += stats.get("documents", 0)
         nodes = self.report.setdefault("node_metrics", {})
         nodes[f"{len(nodes)}:{kind}"] = node_metrics(stats)
@@ -1337,6 +1367,8 @@ class Executor:
             "FLOOR": lambda a: pc.floor(a[0]), "CEIL": lambda a: pc.ceil(a[0]),
             "COALESCE": lambda a: pc.coalesce(*a), "CONCAT": lambda a: pc.binary_join_element_wise(*[_str(x) for x in a], ""),
             "SUBSTR": lambda a: _substr(a), "SUBSTRING": lambda a: _substr(a),
+            "LEFT": lambda a: pc.utf8_slice_codeunits(a[0], 0, max(int(a[1].as_py()), 0)),
+            "CHARACTER_LENGTH": lambda a: pc.utf8_length(a[0]),
             "STARTS_WITH": lambda a: pc.starts_with(a[0], a[1].as_py()),
             "CONTAINS": lambda a: pc.match_substring(a[0], a[1].as_py()),
             "REGEXP_LIKE": lambda a: pc.match_substring_regex(a[0], a[1].as_py()),
