@@ -440,6 +440,8 @@ class Executor:
         self.ctes: dict = {}
         self.report = {"regions": [], "asked": 0, "fresh_tokens": 0, "passes": 0, "evaluated_documents": 0}
         self.ai_values: dict = {}   # (call key) -> Arrow array aligned with the relation being evaluated
+        self.carried = ({}, {})     # WHERE answers and their asked rows, aligned with the rows it kept
+        self.asked_rows: dict = {}  # (call key) -> bool array: rows of ai_values[key] the call was asked on
         flag = self.settings.get("quail.pushdown", self.settings.get("pushdown", True))
         self.pushdown = str(flag).lower() not in ("false", "off", "0", "no")
 
@@ -703,10 +705,21 @@ class Executor:
             order = order_filters([doc_tokens(b.tail) for b in bound],
                                   [b.selectivity if b.selectivity is not None else 0.5 for b in bound])
             rel = self.run_filters(rel, [bound[i] for i in order])
+        carry: dict = {}
+        carry_asked: dict = {}
         for c in others:
+            self.ai_values, self.asked_rows = dict(carry), dict(carry_asked)
             self.compute_ai(rel, [c], stops=self._answer_stops(c))
-            rel = rel.filter(_as_mask(self.eval(c, rel)))
-            self.ai_values = {}
+            mask = _as_mask(self.eval(c, rel))
+            rel = rel.filter(mask)
+            # the answers stay with the rows they belong to, with the rows each call was asked
+            # on, so a later conjunct or the SELECT list reading the same call asks it only
+            # where it was not asked yet
+            keep = np.asarray(mask.to_pylist() if hasattr(mask, "to_pylist") else mask, dtype=bool)
+            carry = {k: v.filter(mask) for k, v in self.ai_values.items()}
+            carry_asked = {k: a[keep] for k, a in self.asked_rows.items() if k in carry}
+            self.ai_values, self.asked_rows = {}, {}
+        self.carried = (carry, carry_asked)
         return rel
 
     def _answer_stops(self, conjunct) -> dict:
@@ -755,6 +768,9 @@ class Executor:
         demand = G.Demand(self, rel, enabled=self.pushdown)
         for e in exprs:
             demand.visit(e)
+        for k, (node, guard) in demand.guards.items():
+            if k in self.ai_values:
+                self._fill_unasked(rel, k, node, guard)
         todo = {k: v for k, v in demand.guards.items() if k not in self.ai_values}
         if not todo:
             return
@@ -788,6 +804,38 @@ class Executor:
                 for k in remaining:
                     bound[k].guard = None
 
+    def _fill_unasked(self, rel: Relation, k: str, node, guard) -> None:
+        """A call some earlier clause asked on part of `rel`'s rows (under its own guard): ask it
+        on the rows it skipped that `guard` may now need, and merge those answers in."""
+        from quail_b200.sql import guards as G
+        asked = self.asked_rows.get(k)
+        if asked is None or asked.all():
+            return
+        g = None if guard["op"] == "true" else guard
+        if g is not None:
+            deps = G.calls_of(g)
+            g = G.fold(g, {d: _to_pylist(self.ai_values[d]) for d in deps if d in self.ai_values}, rel.num_rows)
+        miss = [r for r in np.nonzero(~asked)[0].tolist() if g is None or G.may_ask(g, r)]
+        if not miss:
+            return
+        saved, saved_asked = self.ai_values, self.asked_rows
+        self.ai_values, self.asked_rows = {}, {}
+        b = bind_call(node, self.turn, self.model)
+        b.drops = False
+        self._run_group(rel.take(pa.array(miss, pa.int64())), [b])
+        got = self.ai_values
+        self.ai_values, self.asked_rows = saved, saved_asked
+        for key in (k, k + "#probs"):
+            if key not in got or key not in self.ai_values:
+                continue
+            merged = self.ai_values[key].to_pylist()
+            for j, r in enumerate(miss):
+                merged[r] = got[key][j].as_py()
+            self.ai_values[key] = pa.array(merged, self.ai_values[key].type)
+        asked = asked.copy()
+        asked[miss] = True
+        self.asked_rows[k] = asked
+
     def _run_group(self, rel: Relation, cs: list[BoundCall]) -> None:
         """One region: the calls `cs` (dependency order) over the rows any of them may be asked on."""
         from quail_b200.sql import guards as G
@@ -816,6 +864,8 @@ class Executor:
     def _store(self, cs: list[BoundCall], vals: list[dict], docs_all: list) -> None:
         """Typed Arrow values of calls `cs` from per-row answer dicts (None where not asked)."""
         for c in cs:
+            first = f"{c.key}#0" if c.kind == "extract" else c.key
+            self.asked_rows[c.key] = np.array([first in v for v in vals], dtype=bool)
             if c.kind == "extract":
                 out = []
                 for r, v in enumerate(vals):
@@ -962,13 +1012,16 @@ class Executor:
             part = rel.take(pa.array(np.arange(start, start + size, dtype=np.int64))) if size < n else rel
             start += size
             fused = self._filters_with_riders(part, ai, node)
+            pre_asked = None
             if fused is not None:
                 kept, pre = fused
             else:
-                kept, pre = self.apply_ai_conjuncts(part, ai), None
+                self.carried = ({}, {})
+                kept = self.apply_ai_conjuncts(part, ai)
+                (pre, pre_asked), self.carried = self.carried, ({}, {})
             tried += part.num_rows
             passed += kept.num_rows
-            out = self._project(kept, node, pre)
+            out = self._project(kept, node, pre, pre_asked)
             lo, hi = emitted, emitted + out.num_rows
             emitted = hi
             a = max(off - lo, 0)
@@ -1030,11 +1083,12 @@ class Executor:
         pre, self.ai_values = self.ai_values, saved
         return kept, pre
 
-    def _project(self, rel: Relation, node, pre: dict | None = None) -> pa.Table:
+    def _project(self, rel: Relation, node, pre: dict | None = None, pre_asked: dict | None = None) -> pa.Table:
         """The SELECT list of a non-aggregating query over `rel` (its model calls asked on demand;
         `pre` holds values some calls already got, aligned with `rel`)."""
         items = node["items"]
         self.ai_values = dict(pre or {})
+        self.asked_rows = dict(pre_asked or {})
         self.compute_ai(rel, [it["expr"] for it in items])
         names, arrays = [], []
         unnest = None
@@ -1084,13 +1138,15 @@ class Executor:
 
     def _select_whole(self, node) -> pa.Table:
         rel = self.from_clause(node)
+        self.carried = ({}, {})
         if node.get("where"):
             rel = self.apply_where(rel, node["where"])
         items = node["items"]
         group_by = node.get("group_by")
         aggregated = group_by is not None or any(is_aggregate(n) for it in items for n in walk(it["expr"]))
-        # AI calls in the projection / ORDER BY / HAVING run on the surviving rows
-        self.ai_values = {}
+        # AI calls in the projection / ORDER BY / HAVING run on the surviving rows (answers the
+        # WHERE already got are read, not asked again)
+        (self.ai_values, self.asked_rows), self.carried = self.carried, ({}, {})
         ai_exprs = [it["expr"] for it in items] + [o["expr"] for o in node.get("order_by", [])]
         if node.get("having"):
             ai_exprs.append(node["having"])
