@@ -197,6 +197,7 @@ class BoundCall:
     probabilities: bool = False
     selectivity: float | None = None
     questions: list = field(default_factory=list)   # extract: one call per question
+    fields: list | None = None                       # extract: struct field names ({'name': question} form)
     span: bool = False
     pooling: str = "last"                            # features
     descriptions: list = field(default_factory=list)  # classify: per-label descriptions
@@ -403,10 +404,21 @@ def bind_call(node, turn: P.Turn, model: P.PromptModel | None = None) -> BoundCa
             raise QueryError(f"{name} takes an input and a list of questions")
         _, doc, _ = _prompt_parts(args[0])
         qs = literal_value(args[1])
-        qs = [qs] if isinstance(qs, str) else list(qs)
+        fields = None
+        if isinstance(qs, dict):
+            # {'field': 'question', ...}: a struct with one field per question
+            if not qs or not all(isinstance(k, str) and k for k in qs):
+                raise QueryError(f"{name} questions must map field names to questions")
+            fields, qs = list(qs), [str(v) for v in qs.values()]
+        elif isinstance(qs, str):
+            qs = [qs]
+        elif isinstance(qs, list) and qs:
+            qs = [str(q) for q in qs]
+        else:
+            raise QueryError(f"{name} takes an object from field names to questions")
         bp = P.bind_extract_prompt(qs[0], turn)
         return BoundCall(key=key, kind="extract", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, questions=qs,
-                         span=name == "AI.EXTRACT_SPAN", max_tokens=64)
+                         fields=fields, span=name == "AI.EXTRACT_SPAN", max_tokens=64)
     if name == "AI.SAE_FEATURES":
         opts = _options(args[1]) if len(args) == 2 else {}
         pooling = opts.get("pooling")
@@ -708,6 +720,12 @@ class Executor:
         carry: dict = {}
         carry_asked: dict = {}
         for c in others:
+            pre = self._substring_precheck(rel, c)
+            if pre is not None:
+                rel = rel.filter(pre)
+                keep = np.asarray(pre.to_pylist(), dtype=bool)
+                carry = {k: v.filter(pre) for k, v in carry.items()}
+                carry_asked = {k: a[keep] for k, a in carry_asked.items()}
             self.ai_values, self.asked_rows = dict(carry), dict(carry_asked)
             self.compute_ai(rel, [c], stops=self._answer_stops(c))
             mask = _as_mask(self.eval(c, rel))
@@ -721,6 +739,53 @@ class Executor:
             self.ai_values, self.asked_rows = {}, {}
         self.carried = (carry, carry_asked)
         return rel
+
+    def _substring_precheck(self, rel: Relation, conjunct):
+        """Rows whose document can give an extraction answer passing `conjunct`, or None.
+
+        AI.EXTRACT copies each answer from its document, so an answer that must match a LIKE
+        pattern needs a document containing the pattern's literal text: the longest run between
+        wildcards, then that run's longest word (case and whitespace are where a decoded answer
+        may differ from its document). `answer['f'] LIKE '%2027%'` then asks the model only on
+        documents that contain '2027' (case-insensitively); the test itself still runs.
+        Reference: crates/quail-datafusion/src/rules/substring.rs.
+        """
+        if not self.pushdown or rel.num_rows == 0 or conjunct.get("type") != "like" or conjunct.get("negated"):
+            return None
+        arg = conjunct["arg"]
+        if arg.get("type") == "subscript":
+            arg = arg["arg"]
+        if not (is_model_call(arg) and arg["name"] == "AI.EXTRACT"):
+            return None
+        try:
+            pat = literal_value(conjunct["pattern"])
+        except QueryError:
+            return None
+        if not isinstance(pat, str):
+            return None
+        runs, cur, i = [], "", 0
+        while i < len(pat):
+            ch = pat[i]
+            if ch == "\\" and i + 1 < len(pat):
+                cur += pat[i + 1]
+                i += 2
+                continue
+            if ch in "%_":
+                runs.append(cur)
+                cur = ""
+            else:
+                cur += ch
+            i += 1
+        runs.append(cur)
+        words = max(runs, key=len).split()
+        need = max(words, key=len) if words else ""
+        if not need:
+            return None
+        b = bind_call(arg, self.turn, self.model)
+        docs = _as_array(self.eval(b.doc_expr, rel), rel.num_rows)
+        if not pa.types.is_string(docs.type) and not pa.types.is_large_string(docs.type):
+            return None
+        return pc.fill_null(pc.match_substring(docs, need, ignore_case=True), False)
 
     def _answer_stops(self, conjunct) -> dict:
         """The early stop of an AI.MAP answer that `conjunct` tests alone (quail_b200.sql.partial):
@@ -876,9 +941,10 @@ class Executor:
                     if c.span:
                         doc = "" if docs_all[r] is None else str(docs_all[r])
                         answers = [_span(doc, a) for a in answers]
-                    out.append(answers)
-                self.ai_values[c.key] = pa.array(out, pa.list_(pa.struct([("start", pa.int64()), ("end", pa.int64())]))
-                                                 if c.span else pa.list_(pa.string()))
+                    out.append(answers if c.fields is None else dict(zip(c.fields, answers)))
+                item = pa.struct([("start", pa.int64()), ("end", pa.int64())]) if c.span else pa.string()
+                typ = pa.list_(item) if c.fields is None else pa.struct([(f, item) for f in c.fields])
+                self.ai_values[c.key] = pa.array(out, typ)
             elif c.kind == "classify" and c.probabilities:
                 self.ai_values[c.key] = pa.array([v.get(c.key) for v in vals], pa.string())
                 self.ai_values[c.key + "#probs"] = pa.array([v.get(c.key + "#probs") for v in vals],
