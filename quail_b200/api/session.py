@@ -36,6 +36,7 @@ class QueryResult:
         return self.table
 
     def explain(self) -> str:
+        """The plan with its estimates and, below, what the run measured."""
         return self.plan
 
     def __repr__(self) -> str:
@@ -105,7 +106,9 @@ class Query:
         rep.update(wall_s=wall, boot_s=boot, output_rows=table.num_rows)
         rep["documents_per_second"] = rep["evaluated_documents"] / wall if wall > 0 else 0.0
         _finish_report(rep, s, wall)
-        return QueryResult(table=table, report=rep, plan=self.plan().explain())
+        plan = self.plan()
+        text = plan.explain() if self.tree.get("type") == "set" else plan.explain() + "\n" + plan.explain_measured(rep)
+        return QueryResult(table=table, report=rep, plan=text)
 
     def collect(self, limit: int | None = None) -> pa.Table:
         t = self.run().table

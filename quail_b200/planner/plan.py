@@ -30,12 +30,16 @@ class PlanNode:
     rows: float | None = None
     seconds: float | None = None
     children: list = field(default_factory=list)
+    # what the physical section shows: the table alias an AI node reads, its prompt, its
+    # selectivity (and whether it was assumed), a scan's token counts (planner/explain.py)
+    info: dict = field(default_factory=dict)
 
 
 @dataclass
 class Plan:
     root: PlanNode
     settings: dict = field(default_factory=dict)
+    envelope: dict = field(default_factory=dict)
 
     def nodes(self):
         out, stack = [], [self.root]
@@ -46,6 +50,11 @@ class Plan:
         return out
 
     def explain(self, verbose: bool = False) -> str:
+        """The logical plan, then the physical plan with the planner's estimates."""
+        from quail_b200.planner.explain import render
+        return render(self, verbose=verbose)
+
+    def logical(self, verbose: bool = False) -> str:
         lines = []
 
         def rec(n: PlanNode, depth: int):
@@ -65,13 +74,15 @@ class Plan:
         return "\n".join(lines)
 
     def explain_measured(self, report: dict) -> str:
+        """The physical plan's measured side after a run (rows, pass share, time, fresh tokens per
+        model region), then the run's totals."""
+        from quail_b200.planner.explain import render_measured
+        return render_measured(self, report)
+
+    def measured_totals(self, report: dict) -> str:
         keys = ("wall_s", "boot_s", "fresh_tokens", "cached_tokens", "evaluated_documents", "passes", "asked",
-                "output_rows", "peak_gib", "usd_per_query")
-        lines = ["measured: " + ", ".join(f"{k}={_short(report.get(k))}" for k in keys if k in report)]
-        for node, m in report.get("node_metrics", {}).items():
-            shown = ", ".join(f"{k}={_short(v)}" for k, v in m.items() if v)
-            lines.append(f"  {node}: {shown}")
-        return "\n".join(lines)
+                "output_rows", "stopped_early", "peak_gib", "usd_per_query")
+        return "totals: " + ", ".join(f"{k}={_short(report.get(k))}" for k in keys if k in report)
 
 
 def _short(v):
@@ -141,7 +152,38 @@ def plan_query(tree: dict, session) -> Plan:
     settings = {"model": session.config.model, "device": session.config.device, "gpus": session.config.gpus,
                 "chunk_tokens": budgets.chunk_tokens, "compute_knee": budgets.compute_knee()}
     node = tree["query"] if tree.get("type") == "explain" else tree
-    return Plan(root=_plan_select(node, session, budgets), settings=settings)
+    plan = Plan(root=_plan_select(node, session, budgets), settings=settings)
+    plan.envelope = _envelope(session, budgets)
+    return plan
+
+
+def _envelope(session, budgets) -> dict:
+    """The physical plan's header: backend, model, GPUs, memory budgets, architecture, kernels."""
+    cfg = session.model_cfg
+    cpu = session.config.device == "cpu"
+    out = {"backend": "quail_b200", "model": session.config.model, "gpus": max(session.config.gpus, 1),
+           "chunk_tokens": budgets.chunk_tokens, "kv": "fp32" if cpu else "bf16"}
+    if cfg is None:
+        return out
+    try:
+        page = 128 if session.config.device != "cpu" else 16
+        out["admission_tokens"] = budgets.arena_pages(page) * page
+    except Exception:  # noqa: BLE001 - a budget that does not fit is the executor's refusal, not explain's
+        out["admission_tokens"] = None
+    out["architecture"] = f"{cfg.arch} ({cfg.layers} layers)"
+    weights = "nvfp4" if getattr(cfg, "mlp_fp4", False) else ("fp8" if getattr(cfg, "fp8", False) else "bf16")
+    out["weights"] = weights
+    gemm = {"fp8": "MX fp8 tcgen05 GEMM (1x32 UE8M0 activation scales)", "bf16": "bf16 tcgen05 GEMM",
+            "nvfp4": "NVFP4 tcgen05 GEMM (attention fp8)"}[weights]
+    attn = ("small-tile paged attention (head_dim %d)" % cfg.head_dim if cfg.is_hybrid or cfg.head_dim != 128
+            else "persistent tcgen05 attention (TMEM accumulators)")
+    out["kernels"] = f"linear layers: {gemm}; attention: {attn}"
+    if cpu:
+        out["kernels"] = "the fp32 statement of the model on the CPU (no GPU kernels)"
+    elif cfg.is_hybrid:
+        out["kernels"] += "; token mixers: " + ("gated delta rule (chunked)" if cfg.arch != "lfm2"
+                                                 else "short convolution")
+    return out
 
 
 def _doc_column(call):
@@ -217,20 +259,26 @@ def _plan_select(node, session, budgets) -> PlanNode:
     tail_tokens = 60.0
     # a document-isolated model prefills its system turn with every document (no shared prefix KV)
     block_tokens = 48.0 if getattr(getattr(session, "model_cfg", None), "bidirectional", False) else 0.0
+    scans = {}
     if node.get("from"):
         ref = node["from"][0]
         rows = _rows_of(ref, session)
-        cur = PlanNode("quail.scan", ref.get("name", "subquery"), rows=rows)
+        cur = PlanNode("quail.scan", ref.get("name", "subquery"), rows=rows, info=_scan_info(ref))
+        scans[cur.info["alias"].lower()] = cur
         for j in node.get("joins", []):
-            right = PlanNode("quail.scan", j["table"].get("name", "subquery"), rows=_rows_of(j["table"], session))
+            right = PlanNode("quail.scan", j["table"].get("name", "subquery"), rows=_rows_of(j["table"], session),
+                             info=_scan_info(j["table"]))
+            scans[right.info["alias"].lower()] = right
             kind = "AiJoin" if has_model_call(j.get("on")) else "HashJoin"
             r2 = right.rows
             left_rows = rows
             rows = rows * r2 if rows is not None and r2 is not None and kind == "AiJoin" else rows
-            detail, secs = j["kind"], None
+            detail, secs, jinfo = j["kind"], None, {"join": j["kind"]}
             if kind == "AiJoin":
                 detail, secs = _ai_join(j, ref, left_rows, r2, session, budgets, cache, tail_tokens)
-            cur = PlanNode(kind, detail, rows=rows, seconds=secs, children=[cur, right])
+                call = next(n for n in walk(j.get("on")) if is_model_call(n))
+                jinfo = {**_call_info(call, rows, None), "join": j["kind"], "detail": detail}
+            cur = PlanNode(kind, detail, rows=rows, seconds=secs, children=[cur, right], info=jinfo)
     base_ref = node["from"][0] if node.get("from") and not node.get("joins") else None
     for c in conjuncts(node.get("where")):
         if not has_model_call(c):
@@ -250,7 +298,8 @@ def _plan_select(node, session, budgets) -> PlanNode:
                     secs = budgets.pass_seconds(int(tokens), mean_doc_tokens / 2) / gpus
                 doc_read.add(_doc_column(n))
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
-                               children=[cur] if cur else [])
+                               children=[cur] if cur else [], info=_call_info(n, rows, base_ref))
+                _note_scan(scans, cur.info, rows, mean_doc_tokens)
                 rows = rows * _selectivity(n) if rows is not None else None
     for it in node["items"]:
         for n in walk(it["expr"]):
@@ -268,7 +317,8 @@ def _plan_select(node, session, budgets) -> PlanNode:
                         secs += steps * budgets.pass_seconds(max(int(rows), 1), mean_doc_tokens + steps / 2)
                     secs /= gpus
                 cur = PlanNode(NODE_OF[n["name"]], _expr_text(n)[:80], rows=rows, seconds=secs,
-                               children=[cur] if cur else [])
+                               children=[cur] if cur else [], info=_call_info(n, rows, base_ref))
+                _note_scan(scans, cur.info, rows, mean_doc_tokens)
     if node.get("group_by") is not None:
         cur = PlanNode("Aggregate", ", ".join(_expr_text(g) for g in node["group_by"]), children=[cur] if cur else [])
     cur = PlanNode("Projection", ", ".join(it.get("alias") or _expr_text(it["expr"]) for it in node["items"])[:120],
@@ -279,6 +329,61 @@ def _plan_select(node, session, budgets) -> PlanNode:
     if node.get("limit") is not None:
         cur = PlanNode("Limit", _expr_text(node["limit"]), children=[cur])
     return cur
+
+
+def _scan_info(ref) -> dict:
+    name = ref.get("name", "subquery")
+    return {"table": name, "alias": ref.get("alias") or name}
+
+
+def _note_scan(scans: dict, info: dict, rows, mean_doc_tokens: float) -> None:
+    """The scan an AI node reads gets its document token counts (first reader's column)."""
+    scan = scans.get((info.get("alias") or "").lower()) or (next(iter(scans.values())) if len(scans) == 1 else None)
+    if scan is None or "mean_document_tokens" in scan.info:
+        return
+    scan.info["mean_document_tokens"] = mean_doc_tokens
+    if scan.rows is not None:
+        scan.info["tokens"] = scan.rows * mean_doc_tokens
+
+
+def _call_info(call, rows, base_ref) -> dict:
+    """What the physical section shows of an AI node: the alias of the table it reads, its
+    prompt (the PROMPT template, an instruction or the questions), its input rows and, for a
+    filter, its selectivity and whether the planner assumed it."""
+    from quail_b200.sql.executor import literal_value
+    args = [a for a in call.get("args", []) if isinstance(a, dict) and a.get("type") != "named_arg"]
+    info = {"kind": call["name"], "rows_in": rows}
+    d = args[0] if args else {}
+    cols = [n for n in walk(d) if n.get("type") == "column"]
+    alias = next((c.get("table") for c in cols if c.get("table")), None)
+    if alias is None and base_ref is not None:
+        alias = base_ref.get("alias") or base_ref.get("name")
+    info["alias"] = alias or ""
+    prompt = None
+    if d.get("type") == "call" and d.get("name") == "PROMPT" and d.get("args"):
+        try:
+            prompt = literal_value(d["args"][0])
+        except Exception:  # noqa: BLE001 - a computed template shows as written
+            prompt = None
+    try:
+        second = literal_value(args[1]) if len(args) > 1 else None
+    except Exception:  # noqa: BLE001 - options that are not constants
+        second = None
+    if call["name"] in ("AI.IF", "AI_FILTER"):
+        v = _options_of(call).get("selectivity")
+        info["selectivity"] = _selectivity(call)
+        info["assumed"] = not isinstance(v, (int, float))
+    elif call["name"] == "AI.CLASSIFY" and isinstance(second, list):
+        info["labels"] = len(second)
+    elif call["name"] == "AI.MAP":
+        prompt = prompt or (second if isinstance(second, str) else None)
+        info["max_tokens"] = _decode_tokens(call)
+    elif call["name"] in ("AI.EXTRACT", "AI.EXTRACT_SPAN"):
+        qs = second if isinstance(second, (list, dict)) else [second]
+        info["questions"] = len(qs)
+        prompt = prompt or (", ".join(str(q) for q in (qs.values() if isinstance(qs, dict) else qs)))
+    info["prompt"] = prompt if prompt is not None else "{0}"
+    return info
 
 
 def _ordered_filters(ai_conj: list, session) -> list:
