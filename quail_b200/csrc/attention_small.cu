@@ -1,5 +1,5 @@
-// Paged segmented attention for any head_dim up to 256 (hybrid models' gated
-// attention: head_dim 256, partial RoPE, sigmoid output gate).
+// Paged segmented attention for head_dim 64 to 512 (hybrid models' gated attention: head_dim
+// 256, partial RoPE, sigmoid output gate; Gemma 4's global layers: head_dim 512).
 //
 // One CTA per (16 query rows, KV head): the rows are TOK = 16 / G tokens x the
 // G = QH / KH query heads of the KV head (rows past TOK x G idle when G does not
@@ -100,21 +100,27 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
   const int q_start = sd[0], q_len = sd[1], nseg = sd[2];
   const bool bidir = (sd[3] & 1) != 0;   // own segment read both ways (document-isolated block)
   // bits 8..23: a sliding window over the own segment (a row at own position p reads own keys
-  // p - win + 1 .. p); 0 = none. Earlier segments are read whole.
-  const int win = bidir ? 0 : ((sd[3] >> 8) & 0xffff);
+  // p - win + 1 .. p); 0 = none. Earlier segments are read whole unless bit 24 is set: then the
+  // window spans the whole sequence (its segments hold consecutive positions), and with the
+  // own segment read both ways it bounds only the earlier segments (a diffusion canvas)
+  const bool win_all = ((sd[3] >> 24) & 1) != 0;
+  const int win = (bidir && !win_all) ? 0 : ((sd[3] >> 8) & 0xffff);
   if (q0 >= q_len) return;
   const int kvh = blockIdx.y, h0 = kvh * G;
-  int seg_len[kSmMaxSeg], seg_off[kSmMaxSeg], seg_blocks[kSmMaxSeg];
+  int seg_len[kSmMaxSeg], seg_off[kSmMaxSeg], seg_blocks[kSmMaxSeg], seg_start[kSmMaxSeg];
+  int own_start = 0;
 #pragma unroll
   for (int i = 0; i < kSmMaxSeg; ++i) {
     seg_len[i] = i < nseg ? sd[4 + i] : 0;
     seg_off[i] = i < nseg ? sd[8 + i] : 0;
+    seg_start[i] = own_start;                        // position of the segment's first key
+    if (i < nseg - 1) own_start += seg_len[i];
   }
   const int own_len = seg_len[nseg - 1];
   const int rows_tok = min(TOK, q_len - q0);
   const int first_pos = own_len - q_len + q0;       // own-segment position of the tile's first token
   // own-segment key blocks wholly below the first row's window are skipped
-  const int own_skip = win > 0 ? max(0, first_pos - win + 1) / kSmBk : 0;
+  const int own_skip = (win > 0 && !bidir) ? max(0, first_pos - win + 1) / kSmBk : 0;
   int total = 0;
 #pragma unroll
   for (int i = 0; i < kSmMaxSeg; ++i) {
@@ -198,11 +204,16 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
     __syncthreads();
     int s_idx, bb;
     locate(b, s_idx, bb);
-    int slen = seg_len[0];
+    int slen = seg_len[0], kstart = 0;
 #pragma unroll
     for (int i = 1; i < kSmMaxSeg; ++i)
-      if (s_idx == i) slen = seg_len[i];
+      if (s_idx == i) {
+        slen = seg_len[i];
+        kstart = seg_start[i];
+      }
     const bool own = s_idx == nseg - 1 && !bidir;
+    // an earlier segment under a whole-sequence window: keys at or below row position - win drop
+    const bool far = win_all && win > 0 && s_idx != nseg - 1;
     const uint32_t ks = sbase + (st * 2 + 0) * SM::kBuf, vs = sbase + (st * 2 + 1) * SM::kBuf;
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -224,7 +235,8 @@ __global__ void __launch_bounds__(128) small_attn_kernel(
       for (int i = 0; i < 4; ++i) {
         const int jj = bb * kSmBk + n * 8 + t4 * 2 + (i & 1);
         const int lim = (i >> 1) ? lim1 : lim0;
-        const bool vis = jj < slen && (!own || (jj <= lim && (win == 0 || jj > lim - win)));
+        const bool vis = jj < slen && (!own || (jj <= lim && (win == 0 || jj > lim - win))) &&
+                         (!far || kstart + jj > own_start + lim - win);
         s[n][i] = vis ? s[n][i] * scale_log2 : -INFINITY;
         mx[i >> 1] = fmaxf(mx[i >> 1], s[n][i]);
       }
@@ -360,6 +372,7 @@ void small_attention(const torch::Tensor& q, const torch::Tensor& k_cache, const
   QB_SMALL(256, 4)
   QB_SMALL(256, 6)
   QB_SMALL(256, 8)
+  QB_SMALL(512, 8)
 #undef QB_SMALL
   TORCH_CHECK(false, "small_attention: unsupported head_dim / group ", D, " / ", G);
 }

@@ -87,7 +87,8 @@ void moe_gate_up(const torch::Tensor& x8, const torch::Tensor& xsf, const torch:
                  int64_t tcap, const std::vector<int64_t>& recv_a_peer, const std::vector<int64_t>& recv_sf_peer,
                  const std::vector<int64_t>& recv_meta_peer, const std::vector<int64_t>& recv_count_peer,
                  const torch::Tensor& recv_a, const torch::Tensor& recv_sf, const torch::Tensor& recv_count,
-                 const torch::Tensor& w_gu, const torch::Tensor& s_gu, torch::Tensor& y, torch::Tensor& ysf);
+                 const torch::Tensor& w_gu, const torch::Tensor& s_gu, torch::Tensor& y, torch::Tensor& ysf,
+                 int64_t act);
 void moe_down(const torch::Tensor& y, const torch::Tensor& ysf, const torch::Tensor& plan, int64_t E, int64_t tcap,
               const torch::Tensor& recv_meta, const torch::Tensor& w_d, const torch::Tensor& s_d,
               const std::vector<int64_t>& comb_peer, const std::vector<int64_t>& comb_counter_peer);

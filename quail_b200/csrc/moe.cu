@@ -332,6 +332,7 @@ struct MoeGemmParams {
   __nv_bfloat16* comb_peer[kMoeMaxRanks];
   uint32_t* comb_counter_peer[kMoeMaxRanks];
   int* err;
+  int act;               // gate activation: 0 SiLU (SwiGLU), 1 GELU tanh form (GeGLU)
 };
 
 constexpr int kMoeWarps = 12;  // producer, MMA, 8 epilogue, 2 dispatch
@@ -539,8 +540,13 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
       {
         // gate = acc[0..63], up = acc[64..127] of outputs out0 .. out0+63
         const int out0 = tn * (BN / 2) + h * 64;
+        if (p.act == 1) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i] = silu_f(acc[i]) * acc[64 + i];
+          for (int i = 0; i < 64; ++i) acc[i] = gelu_tanh_f(acc[i]) * acc[64 + i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) acc[i] = silu_f(acc[i]) * acc[64 + i];
+        }
         uint8_t e[2];
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
@@ -788,7 +794,8 @@ void moe_gate_up(const torch::Tensor& x8, const torch::Tensor& xsf, const torch:
                  int64_t tcap, const std::vector<int64_t>& recv_a_peer, const std::vector<int64_t>& recv_sf_peer,
                  const std::vector<int64_t>& recv_meta_peer, const std::vector<int64_t>& recv_count_peer,
                  const torch::Tensor& recv_a, const torch::Tensor& recv_sf, const torch::Tensor& recv_count,
-                 const torch::Tensor& w_gu, const torch::Tensor& s_gu, torch::Tensor& y, torch::Tensor& ysf) {
+                 const torch::Tensor& w_gu, const torch::Tensor& s_gu, torch::Tensor& y, torch::Tensor& ysf,
+                 int64_t act) {
   const int W = (int)recv_a_peer.size();
   const int H = x8.size(1), N = w_gu.size(0) / (E / W), Rcap = recv_a.size(0);
   TORCH_CHECK(W >= 1 && W <= kMoeMaxRanks && E % W == 0, "moe_gate_up: ranks");
@@ -809,6 +816,7 @@ void moe_gate_up(const torch::Tensor& x8, const torch::Tensor& xsf, const torch:
   p.E = (int)E;
   p.Epr = (int)E / W;
   p.tcap = (int)tcap;
+  p.act = (int)act;
   p.plan = i32(plan);
   p.x8 = reinterpret_cast<const uint8_t*>(x8.data_ptr());
   p.xsf = xsf.data_ptr<uint8_t>();

@@ -58,6 +58,11 @@ __device__ __forceinline__ uint8_t ue8m0_of(float amax) {
 __device__ __forceinline__ float ue8m0_inv(uint8_t e) { return __uint_as_float((uint32_t)(254 - e) << 23); }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// GELU, tanh form (Hendrycks and Gimpel, "Gaussian Error Linear Units", 2016, eq. for the
+// tanh approximation): 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
 
 __device__ __forceinline__ void st_bf16x8(__nv_bfloat16* dst, const float* v) {
   __align__(16) __nv_bfloat162 h[4];

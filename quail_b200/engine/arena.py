@@ -213,14 +213,25 @@ class KVArena:
     """Device K/V pools with a PagePool."""
 
     def __init__(self, num_layers: int, num_pages: int, page_tokens: int, kv_heads: int, head_dim: int,
-                 device="cuda", dtype=torch.bfloat16, state_slots: int = 0, state_shapes: dict | None = None):
+                 device="cuda", dtype=torch.bfloat16, state_slots: int = 0, state_shapes: dict | None = None,
+                 layer_geoms: list | None = None):
         self.num_layers = num_layers
         self.page_tokens = page_tokens
         self.kv_heads = kv_heads
         self.head_dim = head_dim
         self.device = torch.device(device)
-        self.kv = torch.zeros(num_layers, 2, num_pages, page_tokens, kv_heads, head_dim, device=device,
-                              dtype=dtype)
+        # layers of another (KV heads, head_dim) (Gemma 4's global layers) get a pool tensor of
+        # their own, addressed by the same page ids
+        geoms = list(layer_geoms) if layer_geoms else [(kv_heads, head_dim)] * num_layers
+        assert len(geoms) == num_layers
+        self._where = []
+        count: dict = {}
+        for g in geoms:
+            self._where.append((g, count.get(g, 0)))
+            count[g] = count.get(g, 0) + 1
+        self.groups = {g: torch.zeros(n, 2, num_pages, page_tokens, g[0], g[1], device=device, dtype=dtype)
+                       for g, n in count.items()}
+        self.kv = self.groups.get((kv_heads, head_dim), next(iter(self.groups.values())))
         self.pool = PagePool(num_pages, page_tokens, state_slots)
         # recurrent states of hybrid models: name -> [slots, *shape] fp32 (e.g. conv window, delta-rule state)
         self.states = {name: torch.zeros(state_slots, *shape, device=device, dtype=torch.float32)
@@ -240,15 +251,19 @@ class KVArena:
             if cfg.conv_layers:
                 shapes["sconv"] = (len(cfg.conv_layers), cfg.conv_width - 1, cfg.hidden)
             state_slots = state_slots or 64
+        geoms = [cfg.attn_geometry(i) for i in cfg.attn_layers] if getattr(cfg, "gemma4", False) else None
         return cls(len(cfg.attn_layers), num_pages, page_tokens, cfg.num_kv_heads, cfg.head_dim, device=device,
-                   dtype=dtype, state_slots=state_slots if cfg.is_hybrid else 0, state_shapes=shapes)
+                   dtype=dtype, state_slots=state_slots if cfg.is_hybrid else 0, state_shapes=shapes,
+                   layer_geoms=geoms)
 
     @property
     def num_pages(self) -> int:
         return self.pool.num_pages
 
     def layer(self, i: int):
-        return self.kv[i, 0], self.kv[i, 1]
+        g, j = self._where[i]
+        t = self.groups[g]
+        return t[j, 0], t[j, 1]
 
     @staticmethod
     def bytes_per_page(num_layers, page_tokens, kv_heads, head_dim, elem_bytes=2) -> int:

@@ -87,6 +87,19 @@ class DecoderConfig:
     mrope_sections: tuple = (11, 11, 10)   # rotary frequency pairs per (t, h, w) stream, interleaved
     vision_start_id: int = 248_053
     vision_end_id: int = 248_054
+    # Gemma 4 layers (DiffusionGemma): "attn" layers are the global ones, with their own head
+    # geometry, rotary base and rotated share; "swa" layers slide over `sliding_window` tokens
+    full_kv_heads: int = 0
+    full_head_dim: int = 0
+    full_rope_theta: float = 0.0
+    full_rotary_pairs: float = 1.0
+    k_eq_v: bool = False             # global layers: the values are the key projection (before k_norm)
+    attn_scale: float = 0.0          # softmax scale (0: 1 / sqrt(head_dim))
+    hidden_act: str = "silu"         # "silu" (SwiGLU) or "gelu_tanh" (GeGLU)
+    embed_scale: float = 1.0         # embeddings are multiplied by this (Gemma: sqrt(hidden))
+    final_softcap: float = 0.0       # logits -> c * tanh(logits / c) when > 0
+    canvas_tokens: int = 0           # diffusion canvas rows after each question (0: none)
+    canvas_seed: int = 0
 
     @property
     def bidirectional(self) -> bool:
@@ -115,7 +128,9 @@ class DecoderConfig:
 
     @property
     def is_hybrid(self) -> bool:
-        return any(k != "attn" for k in self.layer_kinds)
+        """Layers besides plain attention (Gated DeltaNet, short convolutions; Gemma 4's sliding
+        layers are attention with a window and do not count)."""
+        return not self.gemma4 and any(k != "attn" for k in self.layer_kinds)
 
     @property
     def conv_layers(self) -> list:
@@ -128,6 +143,21 @@ class DecoderConfig:
     def attn_layers(self) -> list:
         """Indices of the layers with a KV cache."""
         return [i for i in range(self.layers) if self.kind(i) in ("attn", "swa")]
+
+    @property
+    def gemma4(self) -> bool:
+        return self.arch == "gemma4"
+
+    def attn_geometry(self, i: int) -> tuple:
+        """(KV heads, head_dim) of layer i's KV cache: Gemma 4's global layers have their own."""
+        if self.gemma4 and self.kind(i) == "attn":
+            return self.full_kv_heads, self.full_head_dim
+        return self.num_kv_heads, self.head_dim
+
+    @property
+    def kv_dims(self) -> list:
+        """KV elements per token of each attention layer (K or V alone)."""
+        return [h * d for h, d in (self.attn_geometry(i) for i in self.attn_layers)]
 
     @property
     def has_vision(self) -> bool:
@@ -167,6 +197,8 @@ class DecoderConfig:
         return self.layers * (attn + mlp)
 
     def kv_bytes_per_token(self) -> int:
+        if self.gemma4:
+            return 2 * sum(self.kv_dims) * 2
         return self.layers * 2 * self.kv_dim * 2
 
     def with_(self, **kw) -> "DecoderConfig":
@@ -341,6 +373,32 @@ CONFIGS = {c.name: c for c in (QWEN3_4B, QWEN3_8B, QWEN3_32B, QWEN3_30B_A3B, QWE
                                ISOLATED_DENSE_TINY, D1_2B, D1_TINY, D1_GPU_TINY, QWEN35_VL_4B, QWEN35_VL_TINY,
                                QWEN35_VL_GPU_TINY)}
 
+# DiffusionGemma (Gemma 4 MoE backbone, one-step canvas readout): 25 sliding-window layers over
+# 1024 tokens with 256-wide heads, every sixth layer global with 512-wide heads and two KV heads
+# whose values are the keys' projection; a dense GeGLU MLP beside 128 experts (top 8)
+_DG_KINDS = tuple("attn" if (i + 1) % 6 == 0 else "swa" for i in range(30))
+DIFFUSION_GEMMA_26B = DecoderConfig(
+    name="diffusion-gemma-26b-a4b-fp8", layers=30, hidden=2816, num_q_heads=16, num_kv_heads=8, head_dim=256,
+    intermediate=2112, vocab=262_144, rope_theta=10_000.0, rms_eps=1e-6, tied_head=True, weight_dtype="fp8",
+    num_experts=128, top_k=8, moe_intermediate=704, max_position=131_072, layer_kinds=_DG_KINDS, arch="gemma4",
+    sliding_window=1024, full_kv_heads=2, full_head_dim=512, full_rope_theta=1_000_000.0, full_rotary_pairs=0.25,
+    k_eq_v=True, attn_scale=1.0, hidden_act="gelu_tanh", embed_scale=2816 ** 0.5, final_softcap=30.0,
+    canvas_tokens=1, canvas_seed=20_260_514,
+    turn_prefix="<bos><|turn>system\nYou are an expert at text analysis<turn|>\n<|turn>user\n",
+    turn_suffix="<turn|>\n<|turn>model\n<|channel>thought\n<channel|>")
+# the CPU model (fp32; checked against Hugging Face's Gemma4TextModel) and the GPU kernels' shapes
+DIFFUSION_GEMMA_TINY = DIFFUSION_GEMMA_26B.with_(
+    name="diffusion-gemma-tiny", layers=4, hidden=256, num_q_heads=4, num_kv_heads=2, head_dim=64,
+    intermediate=256, vocab=151_936, num_experts=8, top_k=2, moe_intermediate=64, max_position=40_960,
+    layer_kinds=("swa", "attn", "swa", "attn"), sliding_window=16, full_kv_heads=1, full_head_dim=128,
+    embed_scale=256 ** 0.5, weight_dtype="bf16")
+DIFFUSION_GEMMA_GPU_TINY = DIFFUSION_GEMMA_26B.with_(
+    name="diffusion-gemma-gpu-tiny", layers=4, hidden=1024, num_q_heads=8, num_kv_heads=4, head_dim=256,
+    intermediate=512, vocab=4096, num_experts=16, top_k=4, moe_intermediate=256, max_position=8192,
+    layer_kinds=("swa", "attn", "swa", "attn"), sliding_window=64, full_kv_heads=1, full_head_dim=512,
+    embed_scale=1024 ** 0.5, weight_dtype="bf16")
+CONFIGS.update({c.name: c for c in (DIFFUSION_GEMMA_26B, DIFFUSION_GEMMA_TINY, DIFFUSION_GEMMA_GPU_TINY)})
+
 # model spec names (as in EngineConfig.model) -> decoder config
 MODEL_CONFIGS = {
     "qwen3-4b-fp8": QWEN3_4B,
@@ -392,4 +450,7 @@ MODEL_CONFIGS = {
     "qwen3.5-vl-tiny": QWEN35_VL_TINY,
     "qwen3.5-vl-gpu-tiny": QWEN35_VL_GPU_TINY,
     "d1-gpu-tiny": D1_GPU_TINY,
+    "diffusion-gemma-26b-a4b-fp8": DIFFUSION_GEMMA_26B,
+    "diffusion-gemma-tiny": DIFFUSION_GEMMA_TINY,
+    "diffusion-gemma-gpu-tiny": DIFFUSION_GEMMA_GPU_TINY,
 }

@@ -360,7 +360,7 @@ def attention_merge(o_a, lse_a, o_b, lse_b, source, *, fp8_out: bool = True, out
 
 # (head_dim, q heads per KV head) pairs the small-tile attention kernel is built for
 SMALL_ATTENTION_SHAPES = frozenset({(64, 1), (64, 2), (64, 4), (128, 1), (128, 4), (256, 2), (256, 4), (256, 6),
-                                    (256, 8)})
+                                    (256, 8), (512, 8)})
 
 
 def small_attention(q, k_cache, v_cache, seqs, tiles, dseqs, page_list, softmax_scale: float, out,

@@ -69,7 +69,8 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     """fp32 oracle of csrc/attention.cu: [T, QH, D] -> [T, QH * D].
 
     seqs[s, 3] holds flags: bit 0, the own segment is read both ways; bits 8..23, a
-    sliding window over the own segment (0: none).
+    sliding window over the own segment (0: none); bit 24, the window spans every segment
+    (with bit 0 it bounds only the earlier segments).
     """
     T, QH, D = q.shape
     P, KH = k_cache.shape[1], k_cache.shape[2]
@@ -102,8 +103,13 @@ def segmented_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
         mask = kpos[None, :] <= qpos[:, None]
         flags = int(seqs[s, 3])
         win = (flags >> 8) & 0xFFFF
-        if flags & 1:                 # own segment read both ways (document-isolated block)
+        win_all = bool(flags & (1 << 24))
+        if flags & 1:                 # own segment read both ways (document-isolated block, canvas)
             mask = torch.ones_like(mask)
+            if win and win_all:
+                mask &= (kpos[None, :] >= causal_from) | (kpos[None, :] > qpos[:, None] - win)
+        elif win and win_all:         # a sliding window over the whole sequence
+            mask &= kpos[None, :] > qpos[:, None] - win
         elif win:                     # a sliding window over the own segment; earlier segments whole
             mask &= (kpos[None, :] < causal_from) | (kpos[None, :] > qpos[:, None] - win)
         scores = scores.masked_fill(~mask.to(scores.device)[None], float("-inf"))

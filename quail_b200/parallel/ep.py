@@ -94,6 +94,7 @@ class EPState:
             self.buf = torch.zeros(total, dtype=torch.uint8, device=dev)
             self.peers = [self.buf.data_ptr()]
         self.comm = "fused"     # "nccl": the NCCL all-to-all baseline (forward_nccl)
+        self.act = 1 if getattr(cfg, "hidden_act", "silu") == "gelu_tanh" else 0   # experts' gate activation
         self.epoch = 0          # MoE layers run so far (count-exchange flags carry it)
         self.comb_units = 0     # cumulative (row, 128-column) units this rank expects in its combine buffer
         if self.W > 1:
@@ -174,7 +175,7 @@ class EPState:
             C.moe_gate_up(x8, xsf, self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
                           self.peer("recv_a"), self.peer("recv_sf"), self.peer("recv_meta"),
                           self.peer("recv_count"), self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"],
-                          L["sgu"], self.y, self.ysf)
+                          L["sgu"], self.y, self.ysf, self.act)
         with tm("down + combine push"):
             C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, self.recv_meta(), L["wd"], L["sd"],
                        self.peer("comb"), self.peer("comb_counter"))
@@ -285,7 +286,7 @@ class EPState:
             C.moe_gate_up(e8, self.recv_sf(), self.src_list, self.wts, self.plan, self.rank, E, K, self.t_cap,
                           self.peer("recv_a")[self.rank:self.rank + 1] * W, self.peer("recv_sf")[:1] * W,
                           self.peer("recv_meta")[:1] * W, self.peer("recv_count")[:1] * W,
-                          self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf)
+                          self.recv_a(), self.recv_sf(), self.recv_count(), L["wgu"], L["sgu"], self.y, self.ysf, self.act)
         out = self._nb["out"]
         with tm("down"):
             C.moe_down(self.y, self.ysf, self.plan, E, self.t_cap, meta, L["wd"], L["sd"],

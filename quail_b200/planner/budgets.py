@@ -103,7 +103,7 @@ class Budgets:
         cfg = self.cfg
         free = (self.device.mem_bytes * POOL_FRACTION - weight_bytes(cfg)
                 - ACT_RESERVE_CHUNKS * self.chunk_tokens * activation_bytes_per_token(cfg))
-        page_bytes = len(cfg.attn_layers) * 2 * page_tokens * cfg.kv_dim * 2
+        page_bytes = 2 * page_tokens * sum(cfg.kv_dims) * 2
         if self.device.name == "cpu":
             free = min(free, 2 << 30)
         pages = int(free // page_bytes)
