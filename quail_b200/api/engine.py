@@ -151,6 +151,23 @@ class ModelEngine:
             self.arena = None
             self.executor = None
             return
+        if self.cfg.gemma4:
+            # DiffusionGemma: KV pages in two geometries (sliding and global layers), the routed
+            # experts on the grouped MX GEMMs; answers at the canvas row after each question
+            from quail_b200.models.gemma4 import DiffusionGemmaPipeline, DiffusionGemmaReference
+            ckpt = self._checkpoint()
+            if self.on_gpu:
+                self.model = DiffusionGemmaPipeline(self.cfg, ckpt, self.device, max_tokens=self.chunk_tokens + 256)
+                page_tokens, dtype = 128, torch.bfloat16
+            else:
+                self.model = DiffusionGemmaReference(self.cfg, ckpt, device="cpu")
+                page_tokens, dtype = 16, torch.float32
+            del ckpt
+            n_pages = pages or self.budgets.arena_pages(page_tokens)
+            self.arena = KVArena.for_model(self.cfg, n_pages, page_tokens, device=self.device, dtype=dtype)
+            self.executor = StageExecutor(self.model, self.arena, self.chunk_tokens,
+                                          gpu_timing=self.config.gpu_timing, attention="unified")
+            return
         if self.cfg.is_moe and not self.cfg.is_hybrid:
             self._build_moe(pages)
             return
@@ -475,13 +492,19 @@ class ModelEngine:
                 raise RefusalError(Refusal(reasons=(why,), constraint="unsupported_function"))
         decision = self.cfg.role == "decision"
         lettered = self.cfg.readout == "slot_lm"
+        canvas = self.cfg.canvas_tokens > 0
         for c in calls:
             why = None
             if lettered and not c.letters:
                 why = f"{c.kind} is not a call {self.cfg.name!r} answers: it answers with an option letter"
+            elif canvas and c.kind in ("map", "extract", "features"):
+                why = (f"{c.kind} needs a model that decodes token by token; {self.cfg.name!r} answers in one "
+                       f"denoising step at its canvas row")
+            elif canvas and c.kind == "classify" and not c.letters:
+                why = f"{self.cfg.name!r} classifies under the letters rule (a letter per label)"
             elif decision and not lettered and c.segments is None:
                 why = f"{c.kind} is not a call {self.cfg.name!r} answers: its head scores listed options"
-            elif not decision and (c.segments is not None or c.letters):
+            elif not decision and not canvas and (c.segments is not None or c.letters):
                 why = f"an option-scoring prompt needs a decision model, not {self.cfg.name!r}"
             elif self.cfg.role == "reranker" and c.kind != "score":
                 why = "a reranker model can only be used with AI.SCORE"
@@ -498,6 +521,10 @@ class ModelEngine:
                 offsets = tuple(sum(lens[i + 1:]) for i in c.read) + (0,)
             else:
                 suffix = tok.encode(c.tail)
+            if canvas:
+                # the canvas row after the question: the answer is read there
+                from quail_b200.models.gemma4 import canvas_ids
+                suffix = np.concatenate([suffix, canvas_ids(self.cfg)]).astype(np.int32)
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
                       offsets=offsets, copy=c.kind == "extract", drops=c.drops)
@@ -622,7 +649,7 @@ class ModelEngine:
         document) pairs; `call` (AI.IF or AI.SCORE) is asked once per pair. Values per pair."""
         from quail_b200.api.config import Refusal, RefusalError
         from quail_b200.engine.region import Call, PairRun
-        if self.cfg.role != "generative" or self.cfg.set_attention:
+        if self.cfg.role != "generative" or self.cfg.set_attention or self.cfg.canvas_tokens:
             raise RefusalError(Refusal(reasons=(f"an AI join's pair questions need a generative model that keeps "
                                                 f"KV, not {self.cfg.name!r}",), constraint="unsupported_function"))
         tok = self.tokenizer

@@ -24,6 +24,7 @@ JOIN_QUESTION_SEP = "\n\n"
 TASK_INSTRUCTION = "Evaluate TRUE or FALSE for the following question: "
 ANSWER_CUE = "\nANSWER:"
 CLASSIFY_INSTRUCTION = "Answer with exactly one of the categories below for the following question: "
+LETTERS_INSTRUCTION = "Answer with the letter of exactly one of the categories below for the following question: "
 CATEGORIES_HEADER = "\n\nCategories:"
 CHOICE_QUESTION = "Which option best fits the context?"
 EXTRACT_QUESTION_LABEL = "\n\nQuestion: "
@@ -322,6 +323,32 @@ class LetteredPrompt(BoundPrompt):
     slot_lm readout): option i is `letters[i]`; a filter's options are yes (A), then no (B)."""
 
     letters: list = field(default_factory=list)
+
+
+def letter_candidates() -> list[str]:
+    """Option letters for the letters rule: A to Z, a to z, then AA to ZZ."""
+    import string
+    upper = list(string.ascii_uppercase)
+    return upper + list(string.ascii_lowercase) + [a + b for a in upper for b in upper]
+
+
+def bind_letters_classify_prompt(template: str | None, labels: list[str], descriptions: list[str] | None = None,
+                                 task_description: str = "", turn: Turn = Turn()) -> LetteredPrompt:
+    """AI.CLASSIFY under the letters rule (a canvas model reads one row): the categories
+    listed as "- <letter>: <label> (<description>)", answered by the logit of a letter."""
+    if len(labels) > MAX_LETTERS:
+        raise PromptError(f"a lettered prompt takes at most {MAX_LETTERS} options, got {len(labels)}")
+    base = bind_classify_prompt(template, labels, descriptions, task_description, turn)
+    letters = letter_candidates()[:len(labels)]
+    lines = []
+    for i, (letter, label) in enumerate(zip(letters, labels)):
+        d = descriptions[i] if descriptions and i < len(descriptions) and descriptions[i] else ""
+        lines.append(f"- {letter}: {label}" + (f" ({d})" if d else ""))
+    tail = (JOIN_QUESTION_SEP + LETTERS_INSTRUCTION + base.question + CATEGORIES_HEADER + "\n" + "\n".join(lines)
+            + ANSWER_CUE + turn.suffix)
+    return LetteredPrompt(kind="classify", template=template or "", preamble=base.preamble, tail=tail,
+                          question=base.question, labels=list(labels), descriptions=list(descriptions or []),
+                          letters=letters)
 
 
 def bind_mammoth_prompt(template: str, kind: str, turn: Turn = Turn(prefix="", suffix="")) -> LetteredPrompt:

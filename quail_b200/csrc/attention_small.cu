@@ -389,7 +389,8 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
                                          const __nv_bfloat16* __restrict__ kw, int offset,
                                          const float* __restrict__ cos_sin, int rd, const int* __restrict__ slots,
                                          __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
-                                         __nv_bfloat16* __restrict__ q_out, int T, float eps, int sec_h, int sec_w) {
+                                         __nv_bfloat16* __restrict__ q_out, int T, float eps, int sec_h, int sec_w,
+                                         int vmode) {
   constexpr int E = D / 32;
   const int lane = threadIdx.x & 31;
   const int widx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -405,12 +406,25 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
   } else if (h < QH + KH) {
     src = proj + (size_t)t * ldp + (size_t)QH * qstride + (size_t)(h - QH) * D;
     w = kw;
+  } else if (vmode == 2) {
+    // the values are the key projection (Gemma 4's global layers)
+    src = proj + (size_t)t * ldp + (size_t)QH * qstride + (size_t)(h - QH - KH) * D;
   } else {
     src = proj + (size_t)t * ldp + (size_t)QH * qstride + (size_t)KH * D + (size_t)(h - QH - KH) * D;
   }
   float x[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[lane * E + e]);
+  if (w == nullptr && vmode != 0) {
+    // vmode 1 / 2: the values are RMS-normalized per head, with no weight
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / D + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] *= r;
+  }
   if (w != nullptr) {
     float ss = 0.f;
 #pragma unroll
@@ -459,10 +473,11 @@ __global__ void hybrid_qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ proj,
   for (int e = 0; e < E; ++e) dst[lane * E + e] = __float2bfloat16(x[e]);
 }
 
-void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated, const torch::Tensor& positions,
-                       const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
-                       const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
-                       torch::Tensor& q_out, double eps, int64_t sec_h, int64_t sec_w) {
+static void qk_rope_kv_impl(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated,
+                            const torch::Tensor& positions, const torch::Tensor& qw, const torch::Tensor& kw,
+                            bool offset, const torch::Tensor& cos_sin, const torch::Tensor& slots,
+                            torch::Tensor& k_cache, torch::Tensor& v_cache, torch::Tensor& q_out, double eps,
+                            int64_t sec_h, int64_t sec_w, int vmode) {
   const int T = proj.size(0), D = k_cache.size(3), rd = cos_sin.size(1);
   TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.stride(1) == 1, "proj bf16");
   TORCH_CHECK(q_out.is_contiguous() && q_out.size(2) == D, "q_out [T, QH, D]");
@@ -482,15 +497,36 @@ void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool g
         reinterpret_cast<const __nv_bfloat16*>(kw.data_ptr()), offset ? 1 : 0, cos_sin.data_ptr<float>(), rd,  \
         slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),                          \
         reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-        T, (float)eps, (int)sec_h, (int)sec_w);                                                                 \
+        T, (float)eps, (int)sec_h, (int)sec_w, vmode);                                                          \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                             \
     return;                                                                                                     \
   }
   QB_HQR(64)
   QB_HQR(128)
   QB_HQR(256)
+  QB_HQR(512)
 #undef QB_HQR
-  TORCH_CHECK(false, "hybrid_qk_rope_kv: head_dim 64, 128 or 256");
+  TORCH_CHECK(false, "hybrid_qk_rope_kv: head_dim 64, 128, 256 or 512");
+}
+
+void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool gated, const torch::Tensor& positions,
+                       const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
+                       const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
+                       torch::Tensor& q_out, double eps, int64_t sec_h, int64_t sec_w) {
+  qk_rope_kv_impl(proj, QH, KH, gated, positions, qw, kw, offset, cos_sin, slots, k_cache, v_cache, q_out, eps,
+                  sec_h, sec_w, 0);
+}
+
+// Gemma 4: q/k per-head RMSNorm (weights) + RoPE over the whole head (a table whose unrotated
+// pairs hold cos 1, sin 0), values RMS-normalized without a weight; vmode 1: proj is
+// [q | k | v], vmode 2: [q | k] and the values are the key projection.
+void qkv_norm_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, const torch::Tensor& positions,
+                      const torch::Tensor& qw, const torch::Tensor& kw, const torch::Tensor& cos_sin,
+                      const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
+                      torch::Tensor& q_out, double eps, int64_t vmode) {
+  TORCH_CHECK(vmode == 1 || vmode == 2, "qkv_norm_rope_kv: vmode 1 (own values) or 2 (values = keys)");
+  qk_rope_kv_impl(proj, QH, KH, false, positions, qw, kw, false, cos_sin, slots, k_cache, v_cache, q_out, eps, 0, 0,
+                  (int)vmode);
 }
 
 }  // namespace qb

@@ -112,6 +112,10 @@ void hybrid_qk_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, bool g
                        const torch::Tensor& qw, const torch::Tensor& kw, bool offset, const torch::Tensor& cos_sin,
                        const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
                        torch::Tensor& q_out, double eps, int64_t sec_h, int64_t sec_w);
+void qkv_norm_rope_kv(const torch::Tensor& proj, int64_t QH, int64_t KH, const torch::Tensor& positions,
+                      const torch::Tensor& qw, const torch::Tensor& kw, const torch::Tensor& cos_sin,
+                      const torch::Tensor& slots, torch::Tensor& k_cache, torch::Tensor& v_cache,
+                      torch::Tensor& q_out, double eps, int64_t vmode);
 void short_conv(const torch::Tensor& bcx, const torch::Tensor& wconv, const torch::Tensor& seqs,
                 const torch::Tensor& state_io, torch::Tensor& state, int64_t li, torch::Tensor& y);
 
@@ -187,6 +191,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_layer", &qb::gdn_layer, "Gated DeltaNet: causal conv + L2 norm, delta-rule recurrence, gated RMSNorm");
   m.def("small_attention", &qb::small_attention, "paged attention for any head_dim <= 256, optional sigmoid gate");
   m.def("hybrid_qk_rope_kv", &qb::hybrid_qk_rope_kv, "q/k RMSNorm + partial RoPE + KV write of gated attention");
+  m.def("qkv_norm_rope_kv", &qb::qkv_norm_rope_kv,
+        "Gemma 4 attention inputs: q/k RMSNorm + RoPE, values RMS-normalized (own or the key projection), KV write");
   m.def("short_conv", &qb::short_conv, "LFM2 gated short convolution with per-key state slots");
   m.def("read_and_clear_error", &qb::read_and_clear_error);
   m.def("tp_ag_gemm", &qb::tp_ag_gemm, "all-gather -> MX GEMM fused over NVLink peer memory");

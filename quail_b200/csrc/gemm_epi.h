@@ -10,6 +10,7 @@ enum Epi : int {
   kEpiSwigluBf16 = 3,  // D = silu(g) * u (bf16)
   kEpiQkvRope = 4,     // per 128-column head: q/k RMSNorm + NeoX RoPE; q -> q_out, k/v -> paged cache
   kEpiResidualMx = 5,  // D = acc + R (bf16), and D as e4m3 + UE8M0 per 32 columns, row sums of squares
+  kEpiGegluBf16 = 6,   // D = gelu_tanh(g) * u (bf16), gate/up interleaved as for SwiGLU
 };
 
 }  // namespace qb

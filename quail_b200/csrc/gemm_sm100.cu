@@ -144,7 +144,8 @@ void gemm_sm100(const torch::Tensor& a, const torch::Tensor& b, const c10::optio
   p.num_m_tiles = (M + 127) / 128;
   p.num_n_tiles = (N + BN - 1) / BN;
   p.n_fast = M > N ? 1 : 0;
-  if (epi == kEpiSwigluFp8 || epi == kEpiSwigluBf16) TORCH_CHECK(N % BN == 0, "SwiGLU: N must be a multiple of BN");
+  if (epi == kEpiSwigluFp8 || epi == kEpiSwigluBf16 || epi == kEpiGegluBf16)
+    TORCH_CHECK(N % BN == 0, "SwiGLU / GeGLU: N must be a multiple of BN");
 
   if (epi == kEpiSwigluFp8) {
     TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.size(0) == M && out.size(1) == N / 2,
@@ -157,7 +158,7 @@ void gemm_sm100(const torch::Tensor& a, const torch::Tensor& b, const c10::optio
     TORCH_CHECK(out_scale->size(0) == N / 256 && out_scale->size(1) >= M, "SwiGLU fp8 scale shape");
   } else {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1, "bf16 output expected");
-    const int want_n = (epi == kEpiSwigluBf16) ? N / 2 : N;
+    const int want_n = (epi == kEpiSwigluBf16 || epi == kEpiGegluBf16) ? N / 2 : N;
     TORCH_CHECK(out.size(0) == M && out.size(1) == want_n, "gemm_sm100: output shape");
     TORCH_CHECK(out.stride(0) % 8 == 0, "gemm_sm100: output row stride must be a multiple of 8");
     p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -206,6 +207,7 @@ void gemm_sm100(const torch::Tensor& a, const torch::Tensor& b, const c10::optio
   QB_GEMM_CASE(256, false, kEpiBf16, 4)
   QB_GEMM_CASE(256, false, kEpiResidual, 4)
   QB_GEMM_CASE(256, false, kEpiSwigluBf16, 4)
+  QB_GEMM_CASE(256, false, kEpiGegluBf16, 4)
   QB_GEMM_CASE(128, false, kEpiBf16, 6)
   QB_GEMM_CASE(128, false, kEpiResidual, 6)
 #undef QB_GEMM_CASE

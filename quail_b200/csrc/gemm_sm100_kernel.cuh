@@ -30,6 +30,10 @@ struct GemmParams {
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// GELU, tanh form (Hendrycks and Gimpel 2016): 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh(float x) {
+  return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
 
 __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
   __align__(16) __nv_bfloat162 h[4];
@@ -268,17 +272,21 @@ __global__ void __launch_bounds__(64 + BN, 1)
               }
             }
           }
-        } else if constexpr (EPI == kEpiSwigluBf16 || EPI == kEpiSwigluFp8) {
+        } else if constexpr (EPI == kEpiSwigluBf16 || EPI == kEpiSwigluFp8 || EPI == kEpiGegluBf16) {
           // this thread holds gate (acc[0..63]) and up (acc[64..127]) of
           // outputs 64h .. 64h+63 of output tile tn (128 outputs per tile)
           float amax = 0.f;
 #pragma unroll
           for (int i = 0; i < 64; ++i) {
-            acc[i] = silu(acc[i]) * acc[64 + i];
+            if constexpr (EPI == kEpiGegluBf16) {
+              acc[i] = gelu_tanh(acc[i]) * acc[64 + i];
+            } else {
+              acc[i] = silu(acc[i]) * acc[64 + i];
+            }
             amax = fmaxf(amax, fabsf(acc[i]));
           }
           const int out0 = tn * (BN / 2) + h * 64;
-          if constexpr (EPI == kEpiSwigluBf16) {
+          if constexpr (EPI == kEpiSwigluBf16 || EPI == kEpiGegluBf16) {
             if (m < p.M && out0 < p.N / 2) {
               __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + out0;
 #pragma unroll

@@ -15,6 +15,9 @@ SYNTHETIC_FALSE_IDS = (30351, 4049, 4049 + 1, 30351 + 1)
 
 def random_checkpoint_on(cfg: DecoderConfig, device, seed: int = 0) -> dict[str, torch.Tensor]:
     """Random-init weights in checkpoint format, generated layer by layer on `device`."""
+    if cfg.gemma4:
+        from quail_b200.models.gemma4 import random_gemma4
+        return random_gemma4(cfg, seed=seed, device=device, dtype=torch.bfloat16)
     gen = torch.Generator(device=device).manual_seed(seed)
     out: dict[str, torch.Tensor] = {}
     out["model.embed_tokens.weight"] = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device)
@@ -42,6 +45,11 @@ def build_pipeline(cfg: DecoderConfig, device="cuda", seed: int = 0, ckpt=None,
                    answer_ids=SYNTHETIC_TRUE_IDS + SYNTHETIC_FALSE_IDS, max_tokens: int = 16384 + 256):
     if ckpt is None:
         ckpt = random_checkpoint_on(cfg, device, seed)
+    if cfg.gemma4:
+        from quail_b200.models.gemma4 import DiffusionGemmaPipeline
+        pipe = DiffusionGemmaPipeline(cfg, ckpt, device, head_rows=answer_ids, max_tokens=max_tokens)
+        del ckpt
+        return pipe
     if cfg.is_hybrid:
         if cfg.arch == "lfm2":
             from quail_b200.models.lfm2 import Lfm2Pipeline as Pipe

@@ -383,7 +383,7 @@ DIFFUSION_GEMMA_26B = DecoderConfig(
     num_experts=128, top_k=8, moe_intermediate=704, max_position=131_072, layer_kinds=_DG_KINDS, arch="gemma4",
     sliding_window=1024, full_kv_heads=2, full_head_dim=512, full_rope_theta=1_000_000.0, full_rotary_pairs=0.25,
     k_eq_v=True, attn_scale=1.0, hidden_act="gelu_tanh", embed_scale=2816 ** 0.5, final_softcap=30.0,
-    canvas_tokens=1, canvas_seed=20_260_514,
+    canvas_tokens=1, canvas_seed=20_260_514, prompt_layout="letters",
     turn_prefix="<bos><|turn>system\nYou are an expert at text analysis<turn|>\n<|turn>user\n",
     turn_suffix="<turn|>\n<|turn>model\n<|channel>thought\n<channel|>")
 # the CPU model (fp32; checked against Hugging Face's Gemma4TextModel) and the GPU kernels' shapes

@@ -278,3 +278,165 @@ def hf_config(cfg: DecoderConfig):
         rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": cfg.rope_theta},
                          "full_attention": {"rope_type": "proportional", "rope_theta": cfg.full_rope_theta,
                                             "partial_rotary_factor": cfg.full_rotary_pairs}})
+
+
+def _pad_rows(w: torch.Tensor, rows: int) -> torch.Tensor:
+    return w if w.shape[0] == rows else torch.cat([w, w.new_zeros(rows - w.shape[0], *w.shape[1:])])
+
+
+def _pad_cols(w: torch.Tensor, cols: int) -> torch.Tensor:
+    return w if w.shape[1] == cols else torch.cat([w, w.new_zeros(w.shape[0], cols - w.shape[1])], dim=1)
+
+
+class DiffusionGemmaPipeline:
+    """The forward pass of a packed chunk on the GPU kernels.
+
+    Per layer: RMSNorm kernel -> QKV GEMM (bf16 tcgen05) -> q/k RMSNorm + RoPE + value
+    RMSNorm + KV write (one kernel; the global layers' values are the key projection) ->
+    small-tile paged attention (head_dim 256 with the sliding window over every segment, or
+    512) -> o_proj GEMM -> post-norm residual add fused with the next RMSNorm -> GeGLU MLP (the
+    GEMM's GeGLU epilogue, then down) and, in MoE layers, the routed experts on the grouped MX
+    GEMMs (GELU gate activation, per-expert scales folded into the down rows) -> the two branch
+    norms -> post-norm residual add with the layer scalar folded into its weight.
+    Dense widths are padded to multiples of 128 with zero rows (exact: gelu(0) * 0 = 0).
+    """
+
+    def __init__(self, cfg: DecoderConfig, ckpt: dict, device, head_rows=None, max_tokens: int = 16384 + 256):
+        from quail_b200.ops.quant import interleave_gate_up, interleave_gate_up_mx, quantize_weight_mx
+        assert cfg.gemma4
+        self.cfg = cfg
+        self.device = dev = torch.device(device)
+        bf = torch.bfloat16
+
+        def t(name, dtype=bf):
+            return ckpt[name].to(device=dev, dtype=dtype).contiguous()
+        self.embed = t("model.embed_tokens.weight")
+        self.final_norm = t("model.norm.weight")
+        self.canvas_norm = t(SELF_CONDITIONING_NORM)
+        H = cfg.hidden
+        I_pad = -(-cfg.intermediate // 128) * 128
+        self.layers = []
+        for i in range(cfg.layers):
+            p, a = layer_prefix(i), layer_prefix(i) + "self_attn."
+            kh, d = cfg.attn_geometry(i)
+            full = cfg.kind(i) == "attn"
+            scalar = float(ckpt[p + "layer_scalar"].float().reshape(-1)[0])
+            L = {"ln_in": t(p + "input_layernorm.weight"), "ln_post_attn": t(p + "post_attention_layernorm.weight"),
+                 "ln_pre_ffn": t(p + "pre_feedforward_layernorm.weight"),
+                 # the layer scalar multiplies the residual and the branch's norm alike
+                 "ln_post_ffn": (ckpt[p + "post_feedforward_layernorm.weight"].float() * scalar).to(dev, bf),
+                 "scalar": scalar, "qn": t(a + "q_norm.weight"), "kn": t(a + "k_norm.weight"),
+                 "wo": t(a + "o_proj.weight"), "kh": kh, "d": d, "full": full}
+            parts = [ckpt[a + "q_proj.weight"], ckpt[a + "k_proj.weight"]]
+            L["vmode"] = 2 if a + "v_proj.weight" not in ckpt else 1
+            if L["vmode"] == 1:
+                parts.append(ckpt[a + "v_proj.weight"])
+            L["wqkv"] = torch.cat([w.to(dev, bf) for w in parts]).contiguous()
+            g = _pad_rows(ckpt[p + "mlp.gate_proj.weight"].to(dev, torch.float32), I_pad)
+            u = _pad_rows(ckpt[p + "mlp.up_proj.weight"].to(dev, torch.float32), I_pad)
+            L["wgu"] = interleave_gate_up(torch.cat([g, u]).to(bf)).contiguous()
+            L["wd"] = _pad_cols(ckpt[p + "mlp.down_proj.weight"].to(dev, torch.float32), I_pad).to(bf).contiguous()
+            if cfg.is_moe:
+                L.update(ln_post_ffn1=t(p + "post_feedforward_layernorm_1.weight"),
+                         ln_post_ffn2=t(p + "post_feedforward_layernorm_2.weight"),
+                         ln_pre_ffn2=t(p + "pre_feedforward_layernorm_2.weight"),
+                         router_in=(ckpt[p + "router.scale"].float() * H ** -0.5).to(dev, bf))
+                L["moe"] = self._experts(ckpt, p, interleave_gate_up_mx, quantize_weight_mx)
+            self.layers.append(L)
+        self.ep = None
+        if cfg.is_moe:
+            from quail_b200.parallel.ep import EPState
+            self.ep = EPState(cfg.with_(moe_intermediate=self._ie_pad), max_tokens, dev, None)
+        self.rope_swa = rope_table(cfg.max_position, cfg.head_dim, cfg.rope_theta, 1.0, dev)
+        self.rope_full = rope_table(cfg.max_position, cfg.full_head_dim, cfg.full_rope_theta, cfg.full_rotary_pairs,
+                                    dev)
+        self.scale = cfg.attn_scale or ref.softmax_scale(cfg.head_dim)
+        self.head = self.embed
+        self.answer_rows = None
+        if head_rows is not None:
+            self.set_answer_rows(head_rows)
+
+    def _experts(self, ckpt, p, interleave_gate_up_mx, quantize_weight_mx) -> dict:
+        """Router (bf16) and the experts in the grouped GEMMs' MX layout: the expert width padded
+        to a multiple of 128, each expert's per_expert_scale folded into its down rows."""
+        cfg, dev = self.cfg, self.device
+        Ie = cfg.moe_intermediate
+        self._ie_pad = -(-Ie // 128) * 128
+        gu = ckpt[p + "experts.gate_up_proj"].to(dev, torch.float32)
+        down = ckpt[p + "experts.down_proj"].to(dev, torch.float32)
+        s = ckpt[p + "router.per_expert_scale"].to(dev, torch.float32)
+        gq, gs, dq, ds = [], [], [], []
+        for e in range(cfg.num_experts):
+            g = _pad_rows(gu[e, :Ie], self._ie_pad)
+            u = _pad_rows(gu[e, Ie:], self._ie_pad)
+            q, sc = interleave_gate_up_mx(torch.cat([g, u]))
+            gq.append(q)
+            gs.append(sc)
+            q, sc = quantize_weight_mx(_pad_cols(down[e] * s[e], self._ie_pad))
+            dq.append(q)
+            ds.append(sc)
+        return {"router": ckpt[p + "router.proj.weight"].to(dev, torch.bfloat16).contiguous(),
+                "wgu": torch.cat(gq).contiguous(), "sgu": torch.cat(gs).contiguous(),
+                "wd": torch.cat(dq).contiguous(), "sd": torch.cat(ds).contiguous()}
+
+    def set_answer_rows(self, token_ids) -> None:
+        ids = torch.as_tensor(list(token_ids), dtype=torch.long)
+        self.answer_rows = self.head.index_select(0, ids.to(self.head.device)).contiguous()
+        self.answer_ids = ids
+
+    def head_bf16(self) -> torch.Tensor:
+        return self.head
+
+    @torch.no_grad()
+    def forward_hidden(self, chunk, arena) -> torch.Tensor:
+        from quail_b200 import ops
+        C = ops.native()
+        cfg, dev = self.cfg, self.device
+        eps = cfg.rms_eps
+        T = chunk.num_tokens
+        ids = chunk.ids
+        canvas = ids >= CANVAS_TOKEN_BASE
+        h = ops.embed_gather(torch.where(canvas, ids - CANVAS_TOKEN_BASE, ids), self.embed)
+        h.mul_(cfg.embed_scale)
+        h = torch.where(canvas[:, None], ops.rmsnorm_quant(h, self.canvas_norm, eps, fp8=False), h)
+        seqs_w = window_seqs(chunk.seqs, cfg.sliding_window)
+        x = ops.rmsnorm_quant(h, self.layers[0]["ln_in"], eps, fp8=False)
+        for i, L in enumerate(self.layers):
+            kh, d = L["kh"], L["d"]
+            QH = cfg.num_q_heads
+            p = ops.gemm(x, L["wqkv"])
+            kc, vc = arena.layer(i)
+            q = torch.empty(T, QH, d, dtype=torch.bfloat16, device=dev)
+            ops.count_launch(1)
+            C.qkv_norm_rope_kv(p, QH, kh, chunk.positions, L["qn"], L["kn"],
+                               self.rope_full if L["full"] else self.rope_swa, chunk.slots, kc, vc, q, eps, L["vmode"])
+            o = torch.empty(T, QH * d, dtype=torch.bfloat16, device=dev)
+            ops.small_attention(q, kc, vc, chunk.seqs if L["full"] else seqs_w, chunk.tiles, chunk.dseqs,
+                                chunk.page_list, self.scale, o, None, 0)
+            a = ops.gemm(o, L["wo"])
+            x = ops.post_norm_add_norm(a, h, L["ln_post_attn"], L["ln_pre_ffn"], eps)
+            dense = ops.gemm(ops.gemm(x, L["wgu"], epi=ops.EPI_GEGLU_BF16), L["wd"])
+            if cfg.is_moe:
+                xb = ops.rmsnorm_quant(h, L["router_in"], eps, fp8=False)
+                x8, xs = ops.rmsnorm_quant_mx(h, L["ln_pre_ffn2"], eps)
+                routed = torch.zeros_like(h)
+                self.ep.forward(x8, xs, xb, routed, L["moe"], next_norm=None, eps=eps)
+                both = torch.zeros_like(h)
+                ops.post_norm_add_norm(dense, both, L["ln_post_ffn1"], None, eps)
+                ops.post_norm_add_norm(routed, both, L["ln_post_ffn2"], None, eps)
+                dense = both
+            h.mul_(L["scalar"])
+            nxt = self.layers[i + 1]["ln_in"] if i + 1 < len(self.layers) else None
+            x = ops.post_norm_add_norm(dense, h, L["ln_post_ffn"], nxt, eps)
+        return h
+
+    @torch.no_grad()
+    def forward_chunk(self, chunk, arena) -> torch.Tensor:
+        from quail_b200 import ops
+        cfg = self.cfg
+        if getattr(chunk, "full_readout", False):
+            raise ValueError("a canvas model answers at its canvas row; it does not decode")
+        h = self.forward_hidden(chunk, arena)
+        ans = ops.final_norm_readout(h, chunk.final_rows, self.final_norm, cfg.rms_eps, self.answer_rows)
+        c = cfg.final_softcap
+        return c * torch.tanh(ans / c) if c > 0 else ans

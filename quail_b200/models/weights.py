@@ -169,6 +169,9 @@ def _iter_gdn(cfg: DecoderConfig, p: str, gen: torch.Generator, device, dtype):
 def random_checkpoint(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
                       layers: range | None = None) -> dict[str, torch.Tensor]:
     """A whole random-init checkpoint dict in HF names."""
+    if cfg.gemma4:
+        from quail_b200.models.gemma4 import random_gemma4
+        return random_gemma4(cfg, seed=seed, device=device, dtype=dtype)
     gen = torch.Generator(device=device).manual_seed(seed)
     out: dict[str, torch.Tensor] = {}
     out["model.embed_tokens.weight"] = _rand((cfg.vocab, cfg.hidden), cfg.init_std, gen, device, dtype)

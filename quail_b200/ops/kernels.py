@@ -29,6 +29,7 @@ EPI_BF16 = 0
 EPI_RESIDUAL = 1
 EPI_SWIGLU_FP8 = 2
 EPI_SWIGLU_BF16 = 3
+EPI_GEGLU_BF16 = 6
 EPI_RESIDUAL_MX = 5
 
 
@@ -56,7 +57,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
     [ceil(N/sb_gran), K/128]. Epilogues: EPI_BF16 -> [M, N] bf16;
     EPI_RESIDUAL -> out = acc + residual (out may be the residual itself);
     EPI_SWIGLU_BF16 -> [M, N/2] bf16 of silu(gate) * up over a gate/up
-    interleaved B; EPI_SWIGLU_FP8 -> ([M, N/2] e4m3, [N/256, M] scales).
+    interleaved B (EPI_GEGLU_BF16: gelu_tanh(gate) * up; bf16 operands only);
+    EPI_SWIGLU_FP8 -> ([M, N/2] e4m3, [N/256, M] scales).
     """
     C = native()
     M, N = a.shape[0], b.shape[0]
@@ -69,7 +71,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, sa: torch.Tensor | None = None,
         C.gemm(a, b, sa, sb, sb_gran, epi, out, out_scale, None, bn)
         return out, out_scale
     if out is None:
-        width = N // 2 if epi == EPI_SWIGLU_BF16 else N
+        width = N // 2 if epi in (EPI_SWIGLU_BF16, EPI_GEGLU_BF16) else N
         out = torch.empty(M, width, dtype=torch.bfloat16, device=a.device)
     count_launch()
     C.gemm(a, b, sa, sb, sb_gran, epi, out, None, residual, bn)

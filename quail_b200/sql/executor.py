@@ -385,6 +385,16 @@ def bind_call(node, turn: P.Turn, model: P.PromptModel | None = None) -> BoundCa
         if len(set(labels)) != len(labels):
             raise QueryError("AI.CLASSIFY categories must be distinct")
         opts = _options(args[2] if len(args) > 2 else named.get("options"))
+        if model is not None and model.layout == "letters":
+            # a canvas model reads one row: the labels are listed under letters, answered by a letter
+            try:
+                bp = P.bind_letters_classify_prompt(template if template != "{0}" else None, labels, descriptions,
+                                                    opts.get("task_description", ""), turn)
+            except P.PromptError as exc:
+                raise QueryError(str(exc)) from None
+            return BoundCall(key=key, kind="classify", preamble=bp.preamble, tail=bp.tail, doc_expr=doc,
+                             labels=labels, probabilities=bool(opts.get("probabilities", False)),
+                             descriptions=descriptions, letters=bp.letters)
         bp = P.bind_classify_prompt(template if template != "{0}" else None, labels, descriptions,
                                     opts.get("task_description", ""), turn)
         return BoundCall(key=key, kind="classify", preamble=bp.preamble, tail=bp.tail, doc_expr=doc, labels=labels,

@@ -131,3 +131,71 @@ def test_sliding_window_reaches_into_earlier_segments():
         s = q[t, 0] @ keys[lo:pos + 1].t()
         want = torch.softmax(s, 0) @ vals[lo:pos + 1]
         assert torch.allclose(got[t], want, atol=1e-5)
+
+
+DOCS = ["the plot was thin", "a great cast and music", "the ending surprised me", "long and slow"]
+
+
+@pytest.fixture(scope="module")
+def engine():
+    from quail_b200.api.config import EngineConfig
+    from quail_b200.api.engine import ModelEngine
+    return ModelEngine(EngineConfig(model="diffusion-gemma-tiny", device="cpu", chunk_tokens=256))
+
+
+def _canvas_logits(eng, bp, doc, ids):
+    """The statement's logits of `ids` at the canvas row of the whole prompt, asked alone."""
+    tok = eng.tokenizer
+    toks = np.concatenate([tok.encode(bp.preamble), tok.encode(doc), tok.encode(bp.tail), G.canvas_ids(CFG)])
+    eng.model.set_answer_rows(ids)
+    return _alone(eng.model, toks)
+
+
+def test_scores_are_read_at_the_canvas_row(engine):
+    from quail_b200.api import prompts as P
+    from quail_b200.api.engine import CallSpec
+    tok = engine.tokenizer
+    bp = P.bind_prompt("Is {0} about a film?", 1, P.prompt_model(CFG).turn)
+    assert bp.preamble.startswith("<bos><|turn>system\n") and bp.tail.endswith("<channel|>")
+    out = engine.run_region(bp.preamble, DOCS, [CallSpec(kind="score", tail=bp.tail, name="s")])
+    t_ids, f_ids = tok.answer_ids(P.TRUE_SPELLINGS), tok.answer_ids(P.FALSE_SPELLINGS)
+    both = set(t_ids) & set(f_ids)
+    t_ids = [i for i in t_ids if i not in both]
+    f_ids = [i for i in f_ids if i not in both]
+    for doc, v in zip(DOCS, out.values):
+        row = _canvas_logits(engine, bp, doc, t_ids + f_ids)
+        margin = float(row[:len(t_ids)].max() - row[len(t_ids):].max())
+        assert v["s"] == pytest.approx(1.0 / (1.0 + np.exp(-margin)), abs=1e-4)
+
+
+def test_classify_is_the_best_letter_at_the_canvas_row(engine):
+    from quail_b200.api import prompts as P
+    from quail_b200.api.engine import CallSpec
+    labels = ["praise", "complaint", "question"]
+    bp = P.bind_letters_classify_prompt(None, labels, turn=P.prompt_model(CFG).turn)
+    assert bp.letters == ["A", "B", "C"] and "- B: complaint" in bp.tail
+    out = engine.run_region(bp.preamble, DOCS, [CallSpec(kind="classify", tail=bp.tail, name="k", labels=labels,
+                                                         letters=bp.letters)])
+    ids = [int(engine.tokenizer.encode(x)[0]) for x in bp.letters]
+    for doc, v in zip(DOCS, out.values):
+        row = _canvas_logits(engine, bp, doc, ids)
+        assert v["k"] == labels[int(row.argmax())]
+
+
+def test_sql_on_the_canvas_model():
+    import pyarrow as pa
+
+    import quail_b200 as quail
+    from quail_b200.api.config import RefusalError
+    cfg = quail.EngineConfig(model="diffusion-gemma-tiny", device="cpu", chunk_tokens=256)
+    with quail.Session(config=cfg) as s:
+        s.register("r", quail.DocumentProvider.from_table(pa.table({"id": [0, 1, 2], "body": DOCS[:3]}),
+                                                          id_col="id"))
+        rows = s.sql("SELECT id, AI.CLASSIFY(body, ['praise', 'complaint']) AS k, "
+                     "AI.SCORE(PROMPT('Is {0} long?', body)) AS sc FROM r ORDER BY id").collect().to_pylist()
+        assert [r["k"] in ("praise", "complaint") for r in rows] == [True] * 3
+        assert all(0.0 < r["sc"] < 1.0 for r in rows)
+        for q in ("SELECT AI.MAP(body, 'Summarize.') FROM r",
+                  "SELECT AI.EXTRACT(body, {'who': 'Who?'}) FROM r"):
+            with pytest.raises(RefusalError, match="one denoising step"):
+                s.sql(q).collect()
