@@ -346,7 +346,8 @@ class DiffusionGemmaPipeline:
         self.ep = None
         if cfg.is_moe:
             from quail_b200.parallel.ep import EPState
-            self.ep = EPState(cfg.with_(moe_intermediate=self._ie_pad), max_tokens, dev, None)
+            # the experts always run on the grouped MX (fp8) GEMMs
+            self.ep = EPState(cfg.with_(moe_intermediate=self._ie_pad, weight_dtype="fp8"), max_tokens, dev, None)
         self.rope_swa = rope_table(cfg.max_position, cfg.head_dim, cfg.rope_theta, 1.0, dev)
         self.rope_full = rope_table(cfg.max_position, cfg.full_head_dim, cfg.full_rope_theta, cfg.full_rotary_pairs,
                                     dev)
