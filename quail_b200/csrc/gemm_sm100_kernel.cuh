@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(64 + BN, 1)
             }
           }
         } else {
-          // SwiGLU to bf16 (bf16 models): gate chunk c, up chunk c + 2
+          // SwiGLU / GeGLU to bf16 (bf16 models): gate chunk c, up chunk c + 2
           const int out0 = tn * (BN / 2) + h * 64;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -373,7 +373,14 @@ __global__ void __launch_bounds__(64 + BN, 1)
             if (m < p.M && out0 < p.N / 2) {
               float v[32];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = silu(__uint_as_float(g[i])) * __uint_as_float(u[i]);
+              for (int i = 0; i < 32; ++i) {
+                const float gv = __uint_as_float(g[i]);
+                if constexpr (EPI == kEpiGegluBf16) {
+                  v[i] = gelu_tanh(gv) * __uint_as_float(u[i]);
+                } else {
+                  v[i] = silu(gv) * __uint_as_float(u[i]);
+                }
+              }
               __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + out0 + c * 32;
 #pragma unroll
               for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, &v[j]);

@@ -105,8 +105,11 @@ def random_gemma4(cfg: DecoderConfig, seed: int = 0, device="cpu", dtype=torch.b
         if not (full and cfg.k_eq_v):
             out[a + "v_proj.weight"] = _rand((kh * d, H), std, gen, device, dtype)
         out[a + "o_proj.weight"] = _rand((H, cfg.num_q_heads * d), std, gen, device, dtype)
-        out[a + "q_norm.weight"] = 1.0 + _rand((d,), 0.1, gen, device, dtype)
-        out[a + "k_norm.weight"] = 1.0 + _rand((d,), 0.1, gen, device, dtype)
+        # the softmax scale is 1: q/k norm weights near d**-0.25 keep q . k near unit variance, as
+        # trained checkpoints' small norm weights do (unit weights would make every softmax one-hot)
+        qk = d ** -0.25
+        out[a + "q_norm.weight"] = qk * (1.0 + _rand((d,), 0.1, gen, device, torch.float32)).to(dtype)
+        out[a + "k_norm.weight"] = qk * (1.0 + _rand((d,), 0.1, gen, device, torch.float32)).to(dtype)
         I = cfg.intermediate
         out[p + "mlp.gate_proj.weight"] = _rand((I, H), std, gen, device, dtype)
         out[p + "mlp.up_proj.weight"] = _rand((I, H), std, gen, device, dtype)

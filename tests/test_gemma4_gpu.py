@@ -83,7 +83,7 @@ def test_sql_on_the_gpu_canvas_model():
     import pyarrow as pa
 
     import quail_b200 as quail
-    cfg = quail.EngineConfig(model="diffusion-gemma-gpu-tiny", device="cuda")
+    cfg = quail.EngineConfig(model="diffusion-gemma-gpu-tiny", device="b200")
     bodies = [" ".join(["word"] * n) for n in (5, 40, 200, 17)]
     with quail.Session(config=cfg) as s:
         s.register("r", quail.DocumentProvider.from_table(pa.table({"id": list(range(4)), "body": bodies}),
