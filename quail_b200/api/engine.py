@@ -528,7 +528,7 @@ class ModelEngine:
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
                       offsets=offsets, copy=c.kind == "extract", drops=c.drops)
-            if c.stop is not None and c.kind == "map":
+            if c.stop is not None and c.kind in ("map", "extract"):
                 rc.stop_test = (lambda r, gen, c=c: self._stop_decision(c, gen))
             if c.guard is not None:
                 deps = G.calls_of(c.guard)

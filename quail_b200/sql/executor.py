@@ -807,11 +807,17 @@ class Executor:
         if len(calls) != 1:
             return {}
         (key, call), = calls.items()
-        if call["name"] != "AI.MAP" or not partial.reads_answer_alone(conjunct, key, node_key):
+        if call["name"] not in ("AI.MAP", "AI.EXTRACT") or not partial.reads_answer_alone(conjunct, key, node_key):
             return {}
+        field = None
+        if call["name"] == "AI.EXTRACT":
+            # an extraction's test reads one field of its struct; that question's decode stops
+            field = partial.extraction_field(conjunct, key, node_key)
+            if field is None:
+                return {}
         here = sum(1 for n in walk(conjunct) if is_model_call(n) and node_key(n) == key)
         total = getattr(self, "call_counts", {}).get(key)
-        return {key: {"test": conjunct, "when_true": total is not None and total == here}}
+        return {key: {"test": conjunct, "field": field, "when_true": total is not None and total == here}}
 
     def run_filters(self, rel: Relation, calls: list[BoundCall]) -> Relation:
         """AI.IF calls as one guarded chain over the relation's documents."""
@@ -925,9 +931,12 @@ class Executor:
                 for qi, q in enumerate(c.questions):
                     bp = (P.bind_d1_read_prompt(q, self.turn) if self.model.layout == "d1"
                           else P.bind_extract_prompt(q, self.turn))
+                    stop = None
+                    if c.stop is not None and c.fields is not None and c.fields[qi] == c.stop.get("field"):
+                        stop = {**c.stop, "call": c.key}
                     expanded.append(BoundCall(key=f"{c.key}#{qi}", kind="extract", preamble=bp.preamble,
                                               tail=bp.tail, doc_expr=c.doc_expr, max_tokens=c.max_tokens,
-                                              drops=False, guard=guard))
+                                              drops=False, guard=guard, stop=stop))
             else:
                 expanded.append(BoundCall(**{**c.__dict__, "guard": guard}))
         got = self._engine_region(cs[0].preamble, docs, expanded) if docs else []
@@ -972,14 +981,10 @@ class Executor:
         if self.engine is None:
             raise QueryError("this query needs a model; the session has none")
         from quail_b200.api.engine import CallSpec
-        from quail_b200.sql import partial
         specs = [CallSpec(kind=c.kind, tail=c.tail, name=c.key, labels=c.labels, max_tokens=c.max_tokens,
                           probabilities=c.probabilities, pooling=c.pooling, segments=c.segments, read=c.read,
-                          letters=c.letters, drops=c.drops, guard=c.guard,
-                          stop=None if c.stop is None else (
-                              lambda text, c=c: partial.decide(c.stop["test"], c.key, partial.Completions(text),
-                                                               node_key)),
-                          stop_when_true=bool(c.stop and c.stop["when_true"]))
+                          letters=c.letters, drops=c.drops, guard=c.guard, stop=_stop_test(c),
+                          stop_when_true=bool(c.stop and c.stop["when_true"] and c.kind == "map"))
                  for c in calls]
         out = self.engine.run_region(preamble, docs, specs)
         self._record(out.stats, "quail.region[" + ",".join(c.kind for c in calls) + "]")
@@ -1627,6 +1632,28 @@ def _to_pylist(v):
     if isinstance(v, pa.Scalar):
         return v.as_py()
     return v.to_pylist()
+
+
+def _stop_test(c: BoundCall):
+    """text so far -> decision of the WHERE test of call c's answer (quail_b200.sql.partial), or
+    None. A map answer is its text; an extraction answer one field of its struct, which may still
+    be NULL (found nothing), so it is only ever decided NOT TRUE."""
+    from quail_b200.sql import partial
+    if c.stop is None:
+        return None
+    test = c.stop["test"]
+    if c.kind == "map":
+        return lambda text: partial.decide(test, c.key, partial.Completions(text), node_key)
+    if c.kind == "extract" and c.stop.get("field") is not None:
+        call, field = c.stop["call"], c.stop["field"]
+
+        def decide(text):
+            prefix = partial.extraction_prefix(text)
+            if prefix is None:
+                return partial.UNDECIDED
+            return partial.decide(test, call, partial.Completions(prefix, may_be_null=True), node_key, field)
+        return decide
+    return None
 
 
 def _clean_phrase(text):

@@ -1,4 +1,4 @@
-"""Conditions decided on an AI.MAP answer while the model is still writing it.
+"""Conditions decided on an AI.MAP or AI.EXTRACT answer while the model is still writing it.
 
 The text decoded so far, `w`, limits the complete answers still possible,
 C(w): every text that starts with `w` (the answer may also end right here).
@@ -302,10 +302,11 @@ def _starts_with(t: Text, s) -> frozenset:
 
 
 class _Eval:
-    def __init__(self, answer_key: str, c: Completions, key_of):
+    def __init__(self, answer_key: str, c: Completions, key_of, field: str | None = None):
         self.key = answer_key
         self.c = c
         self.key_of = key_of
+        self.field = field            # an extraction's struct field the answer is (None: the call itself)
 
     def __call__(self, e):
         t = e.get("type")
@@ -313,8 +314,12 @@ class _Eval:
             return Known(e.get("value"))
         if t == "call" and e.get("name") == "HINT":
             return self(e["args"][0])
+        if (self.field is not None and t == "subscript" and isinstance(e.get("arg"), dict)
+                and self.key_of(e["arg"]) == self.key):
+            idx = e.get("index", {})
+            return Text(self.c) if idx.get("type") == "literal" and idx.get("value") == self.field else UNKNOWN
         if t == "call" and self.key_of(e) == self.key:
-            return Text(self.c)
+            return Text(self.c) if self.field is None else UNKNOWN
         if t == "unary" and e.get("op") == "NOT":
             return Truth(frozenset(_not(v) for v in _truth(self(e["arg"]))))
         if t == "unary" and e.get("op") == "-":
@@ -436,10 +441,11 @@ class _Eval:
         return UNKNOWN
 
 
-def decide(expr: dict, answer_key: str, completions: Completions, key_of) -> str:
+def decide(expr: dict, answer_key: str, completions: Completions, key_of, field: str | None = None) -> str:
     """TRUE, NOT_TRUE or UNDECIDED for condition `expr` over the answers C(w) of the model
-    call whose key (`key_of(node)`) is `answer_key`."""
-    vals = _truth(_Eval(answer_key, completions, key_of)(expr))
+    call whose key (`key_of(node)`) is `answer_key` (with `field`: of that extraction's field,
+    read as `call['field']`)."""
+    vals = _truth(_Eval(answer_key, completions, key_of, field)(expr))
     if vals == frozenset({True}):
         return TRUE
     if True not in vals:
@@ -464,6 +470,49 @@ def reads_answer_alone(expr: dict, answer_key: str, key_of) -> bool:
             return False
         return all(ok(v) for k, v in n.items() if k != "type")
     return ok(expr)
+
+
+def extraction_prefix(text: str) -> str | None:
+    """The text every complete extraction answer starts with, given its decoded text so far
+    (the answer is the text stripped, without a leading "Phrase:"), or None while that is not
+    known yet (the text so far could still become the "Phrase:" label)."""
+    s = partial_text(text).strip()
+    low = s.lower()
+    if len(s) < 7 and "phrase:".startswith(low):
+        return None
+    if low.startswith("phrase:"):
+        s = s[7:].strip()
+    return s
+
+
+def extraction_field(expr: dict, answer_key: str, key_of) -> str | None:
+    """The one struct field `expr` reads of the extraction `answer_key` (every read is
+    call['field'] with the same literal field), or None."""
+    fields = set()
+    bare = [False]
+
+    def visit(n, under_subscript=False):
+        if isinstance(n, list):
+            for x in n:
+                visit(x)
+            return
+        if not isinstance(n, dict):
+            return
+        if n.get("type") == "subscript" and isinstance(n.get("arg"), dict) and key_of(n["arg"]) == answer_key:
+            idx = n.get("index", {})
+            if idx.get("type") == "literal" and isinstance(idx.get("value"), str):
+                fields.add(idx["value"])
+            else:
+                bare[0] = True
+            return
+        if n.get("type") == "call" and key_of(n) == answer_key:
+            bare[0] = True
+            return
+        for k, v in n.items():
+            if k != "type":
+                visit(v)
+    visit(expr)
+    return fields.pop() if len(fields) == 1 and not bare[0] else None
 
 
 def partial_text(text: str) -> str:

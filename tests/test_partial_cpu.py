@@ -176,3 +176,35 @@ def test_map_answers_stop_once_the_test_is_decided():
             assert on.report.get("stopped_early", 0) > 0
             assert "stopped_early" not in off.report
             assert on.report["fresh_tokens"] < off.report["fresh_tokens"]
+
+
+def test_extraction_field_and_prefix_rules():
+    e, k = _cond("AI.EXTRACT(body, {'year': 'Which year?'})['year'] LIKE '2027%'")
+    assert Pt.extraction_field(e, k, node_key) == "year"
+    # an extraction may still answer NULL: a test is only ever decided NOT TRUE
+    assert Pt.decide(e, k, Pt.Completions("2027", may_be_null=True), node_key, "year") == Pt.UNDECIDED
+    assert Pt.decide(e, k, Pt.Completions("2026", may_be_null=True), node_key, "year") == Pt.NOT_TRUE
+    e2, k2 = _cond("AI.EXTRACT(body, {'a': 'A?', 'b': 'B?'})['a'] = AI.EXTRACT(body, {'a': 'A?', 'b': 'B?'})['b']")
+    assert Pt.extraction_field(e2, k2, node_key) is None          # two fields: no single answer to stop
+    assert Pt.extraction_prefix("  Phr") is None                  # may still be the "Phrase:" label
+    assert Pt.extraction_prefix("Phrase: 2027 ") == "2027"
+    assert Pt.extraction_prefix(" the end ") == "the end"
+
+
+def test_extraction_stop_wiring():
+    """The executor attaches the WHERE test to the one question whose field it reads, and that
+    question's decode gets a test of its text so far."""
+    from quail_b200.sql.executor import BoundCall, _stop_test
+    x = "AI.EXTRACT(body, {'who': 'Who?', 'year': 'Which year?'})"
+    e, k = _cond(f"{x}['year'] LIKE '2027%'")
+    ex = Executor({}, None)
+    ex.call_counts = {k: 1}
+    stops = ex._answer_stops(e)
+    assert stops[k]["field"] == "year" and stops[k]["test"] is e
+    b = BoundCall(key=f"{k}#1", kind="extract", preamble="", tail="", doc_expr={}, stop={**stops[k], "call": k})
+    test = _stop_test(b)
+    assert test("Phrase: 2026") == Pt.NOT_TRUE
+    assert test(" 20") == Pt.UNDECIDED and test("Phra") == Pt.UNDECIDED
+    e2, k2 = _cond(f"{x}['year'] = {x}['who']")
+    ex.call_counts = {k2: 2}
+    assert ex._answer_stops(e2) == {}
