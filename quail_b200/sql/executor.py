@@ -1018,7 +1018,9 @@ class Executor:
         ORDER BY keys (if any) read no model call: the rows are then sorted
         before any model call, so each slice's output is final.
         """
-        if "from" not in node or node.get("distinct") or node.get("having") or node.get("group_by"):
+        if "from" not in node or node.get("having") or node.get("group_by"):
+            return None
+        if node.get("distinct") and not self._distinct_keeps_every_row(node):
             return None
         items = node["items"]
         if any(is_aggregate(n) for it in items for n in walk(it["expr"])):
@@ -1039,6 +1041,31 @@ class Executor:
         off = int(literal_value(node["offset"])) if node.get("offset") else 0
         lim = int(literal_value(node["limit"])) if node.get("limit") is not None else None
         return {"order": order, "offset": off, "limit": lim}
+
+    def _distinct_keeps_every_row(self, node) -> bool:
+        """A DISTINCT over one table's rows whose SELECT list includes that table's key (a
+        DocumentProvider's id column, or *) removes no row, so it needs no whole-table pass and
+        a LIMIT above it reaches the model calls below. Reference:
+        crates/quail-datafusion/src/rules/distinct.rs."""
+        frm = node.get("from") or []
+        if len(frm) != 1 or node.get("joins") or frm[0].get("type") != "table":
+            return False
+        name = frm[0]["name"].lower()
+        if name in self.ctes:
+            return False
+        prov = next((p for k, p in self.catalog.items() if k.lower() == name), None)
+        key = getattr(prov, "id_col", None)
+        if key is None:
+            return False
+        alias = (frm[0].get("alias") or frm[0]["name"]).lower()
+        for it in node["items"]:
+            e = it["expr"]
+            if e.get("type") == "star" and e.get("table") in (None, alias, name):
+                return True
+            if (e.get("type") == "column" and e["name"].lower() == key.lower()
+                    and (e.get("table") or alias).lower() in (alias, name)):
+                return True
+        return False
 
     def _filter_selectivity(self, ai: list) -> float:
         est = 1.0

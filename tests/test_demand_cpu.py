@@ -132,3 +132,15 @@ def _run_on(n, seed, sql):
     s.register("reviews", quail.DocumentProvider.from_table(_table(n, seed=seed), id_col="id"))
     s.attach_engine(oracle)
     return s.sql(sql).collect(), len(oracle.asked), oracle
+
+
+def test_distinct_over_the_key_keeps_the_limit_fetch():
+    """DISTINCT with the table's id column removes no row: the LIMIT still stops the model early."""
+    sql = f"SELECT DISTINCT id, stars FROM reviews WHERE {IF_ENDING} LIMIT 6"
+    on, asked_on, _ = _run(sql, pushdown=True)
+    off, asked_off, _ = _run(sql, pushdown=False)
+    assert on.num_rows == 6 and on.to_pylist() == off.to_pylist()
+    assert asked_on < asked_off
+    # without the key the DISTINCT may merge rows: every row is asked
+    _, asked_nokey, _ = _run(f"SELECT DISTINCT stars FROM reviews WHERE {IF_ENDING} LIMIT 3", pushdown=True)
+    assert asked_nokey == asked_off
