@@ -65,6 +65,7 @@ def main():
     if args.impl == "reference":
         return reference_arm(args)
 
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -92,8 +93,14 @@ def main():
     slots = Budgets.for_model(cfg, "b200", gpus=1).state_slots(cfg) if cfg.is_hybrid else 0
     arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=slots)
     nt = len(SYNTHETIC_TRUE_IDS)
-    call = lambda suffix: Call(kind="filter", suffix=suffix, true_cols=list(range(nt)),  # noqa: E731
-                               false_cols=list(range(nt, 2 * nt)), name="if")
+
+    def call(suffix):
+        if cfg.canvas_tokens:
+            # a canvas model (DiffusionGemma) reads its answer at the canvas row after the question
+            from quail_b200.models.gemma4 import canvas_ids
+            suffix = np.concatenate([suffix, canvas_ids(cfg)]).astype(np.int32)
+        return Call(kind="filter", suffix=suffix, true_cols=list(range(nt)), false_cols=list(range(nt, 2 * nt)),
+                    name="if")
 
     # ---------------------------------------------------------------- device-timed steps
     steps_total = args.warmup + args.steps + 2
