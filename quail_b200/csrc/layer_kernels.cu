@@ -425,6 +425,7 @@ void rmsnorm_quant(const torch::Tensor& x, const torch::Tensor& w, double eps, c
   QB_NORM_CASE(1024)
   QB_NORM_CASE(2048)
   QB_NORM_CASE(2560)
+  QB_NORM_CASE(2816)
   QB_NORM_CASE(4096)
   QB_NORM_CASE(5120)
 #undef QB_NORM_CASE
@@ -456,6 +457,7 @@ void quant_mx_ss(const torch::Tensor& x, torch::Tensor& y8, torch::Tensor& sf, t
   QB_QSS_CASE(1024)
   QB_QSS_CASE(2048)
   QB_QSS_CASE(2560)
+  QB_QSS_CASE(2816)
   QB_QSS_CASE(4096)
   QB_QSS_CASE(5120)
 #undef QB_QSS_CASE
@@ -488,6 +490,7 @@ void rmsnorm_quant_mx(const torch::Tensor& x, const torch::Tensor& w, double eps
   QB_NORM_MX(1024)
   QB_NORM_MX(2048)
   QB_NORM_MX(2560)
+  QB_NORM_MX(2816)
   QB_NORM_MX(4096)
   QB_NORM_MX(5120)
 #undef QB_NORM_MX
@@ -581,6 +584,7 @@ void final_norm_readout(const torch::Tensor& x, const torch::Tensor& rows, const
   QB_RO_CASE(1024)
   QB_RO_CASE(2048)
   QB_RO_CASE(2560)
+  QB_RO_CASE(2816)
   QB_RO_CASE(4096)
   QB_RO_CASE(5120)
 #undef QB_RO_CASE

@@ -904,6 +904,7 @@ void moe_combine(const torch::Tensor& comb, int64_t M, int64_t topk, const torch
   }
   QB_MOE_CASE(1024)
   QB_MOE_CASE(2048)
+  QB_MOE_CASE(2816)
   QB_MOE_CASE(4096)
 #undef QB_MOE_CASE
   TORCH_CHECK(false, "moe_combine: unsupported hidden size ", H);

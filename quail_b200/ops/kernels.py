@@ -130,6 +130,7 @@ def quant_mx_ss(x: torch.Tensor, *, out=None, out_sf=None, ss=None, rows: int | 
     RMSNorm the GEMM applies (gemm_mx(row_ss=...))."""
     T = x.shape[0] if rows is None else rows
     H = x.shape[1]
+    _check_hidden(H, "quant_mx_ss")
     out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device) if out is None else out
     out_sf = torch.empty(sf_bytes(T, H), dtype=torch.uint8, device=x.device) if out_sf is None else out_sf
     ss = torch.empty(T, 1, dtype=torch.float32, device=x.device) if ss is None else ss
@@ -188,6 +189,7 @@ def rmsnorm_quant_mx(x: torch.Tensor, w: torch.Tensor, eps: float, *, out=None, 
     """RMSNorm -> (e4m3 [T, H], UE8M0 scale bytes, one per 32 columns)."""
     T = x.shape[0] if rows is None else rows
     H = x.shape[1]
+    _check_hidden(H, "rmsnorm_quant_mx")
     if out is None:
         out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
     if out_sf is None:
@@ -215,11 +217,23 @@ def embed_gather(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | Non
     return out
 
 
+# hidden sizes the row kernels (RMSNorm + quantization, final norm readout) are instantiated for
+NORM_HIDDEN = frozenset({256, 512, 1024, 2048, 2560, 2816, 4096, 5120})
+
+
+def _check_hidden(H: int, what: str) -> None:
+    """Refuse a hidden size the native row kernels are not built for here, in Python: the native
+    check would raise inside the extension instead."""
+    if H not in NORM_HIDDEN:
+        raise ValueError(f"{what}: hidden size {H} is not built; built: {sorted(NORM_HIDDEN)}")
+
+
 def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, *, fp8: bool = True,
                   out=None, out_scale=None, rows: int | None = None):
     """RMSNorm of x's first `rows` rows -> (e4m3 [T, H], scales [H/128, T]) or bf16."""
     T = x.shape[0] if rows is None else rows
     H = x.shape[1]
+    _check_hidden(H, "rmsnorm_quant")
     if fp8:
         if out is None:
             out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=x.device)
@@ -477,6 +491,7 @@ def sae_features(x: torch.Tensor, w_enc: torch.Tensor, b_enc: torch.Tensor, keep
 
 def final_norm_readout(x, rows, norm_w, eps: float, head_rows, *, logits=None, normed=None):
     """Gather rows of x, final RMSNorm, logits against the retained head rows."""
+    _check_hidden(x.shape[1], "final_norm_readout")
     if logits is None:
         logits = torch.empty(rows.numel(), head_rows.shape[0], dtype=torch.float32, device=x.device)
     count_launch()

@@ -39,6 +39,9 @@ class EPState:
         import torch.distributed as dist
         from quail_b200 import ops
         assert cfg.is_moe and cfg.fp8
+        if cfg.hidden not in (1024, 2048, 2816, 4096):
+            # the combine kernel is instantiated per hidden size; refuse others here, in Python
+            raise ValueError(f"the expert combine is not built for hidden size {cfg.hidden}")
         self.cfg = cfg
         self.device = torch.device(device)
         self.group = group
