@@ -521,13 +521,22 @@ class ModelEngine:
                 offsets = tuple(sum(lens[i + 1:]) for i in c.read) + (0,)
             else:
                 suffix = tok.encode(c.tail)
-            if canvas:
+            answer_canvas = canvas and c.kind == "classify" and self.cfg.canvas_answer_rows > 0
+            if canvas and not answer_canvas:
                 # the canvas row after the question: the answer is read there
                 from quail_b200.models.gemma4 import canvas_ids
                 suffix = np.concatenate([suffix, canvas_ids(self.cfg)]).astype(np.int32)
             rc = Call(kind=c.kind, suffix=suffix, name=c.name, max_tokens=c.max_tokens,
                       stop_ids=tuple(tok.eos_ids), probabilities=c.probabilities, pooling=c.pooling,
                       offsets=offsets, copy=c.kind == "extract", drops=c.drops)
+            if answer_canvas:
+                # a classification reads row 0 of an answer canvas after the question (draws
+                # repeat an uncertain first answer)
+                from quail_b200.models.gemma4 import CANVAS_ENTROPY_NATS
+                from quail_b200.models.gemma4 import answer_canvas as make_canvas
+                rc.canvas = (lambda r, d: make_canvas(self.cfg, r, d))
+                rc.draws = max(1, int(self.config.canvas_draws))
+                rc.entropy = CANVAS_ENTROPY_NATS
             if c.stop is not None and c.kind in ("map", "extract"):
                 rc.stop_test = (lambda r, gen, c=c: self._stop_decision(c, gen))
             if c.guard is not None:

@@ -108,6 +108,12 @@ class Call:
     # map: stop_test(row, tokens so far) -> "continue" | "stop": the answer ends early once a
     # test of it is decided on its text so far (quail_b200.sql.partial)
     stop_test: object = None
+    # lettered classify on a canvas model: canvas(row, draw) -> the answer canvas's token ids, a
+    # follow-up read both ways after the question; the letters are read at its row 0. A first
+    # draw whose label entropy exceeds `entropy` is averaged with draws 1 .. draws-1
+    canvas: object = None
+    draws: int = 1
+    entropy: float = 0.1
 
 
 @dataclass
@@ -131,6 +137,7 @@ class RegionRun:
         self.asked = 0
         self.fresh_tokens = 0
         self.stopped_early = 0                # answers ended once their test was decided
+        self._canvas_probs: dict = {}         # (row, call) -> label probabilities of its canvas draws
         self._next = [0] * len(docs)          # next call index to submit per row
         self._pending = [0] * len(docs)       # calls in flight per row
         self._label_parts: dict = {}
@@ -431,10 +438,52 @@ class RegionRun:
         call = self.calls[ci]
         key, reads, pos, own_len = self._question(r, ci)
         self.fresh_tokens += len(call.suffix)
+        if call.canvas is not None:
+            # the question is prefilled without a readout; the answer canvas reads it
+            self.ex.submit(Task(np_rows=True, key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=False,
+                                on_done=lambda t, row, r=r, ci=ci: self._canvas_draws(r, ci, (0,)),
+                                free_after=False))
+            return
         self.ex.submit(Task(np_rows=True, key=key, tokens=call.suffix, pos_start=pos, reads=reads, readout=True,
                             full_readout=self._needs_full(call), reserve_tokens=self._reserve(call), topk=call.copy,
                             readout_rows=self._pooled_rows(call, len(call.suffix)), bidirectional=self.isolated,
                             on_done=lambda t, row, r=r, ci=ci: self._answered(r, ci, row), free_after=False))
+
+    def _canvas_draws(self, r: int, ci: int, draws) -> None:
+        """Submit answer canvases `draws` of row r's call ci: each a follow-up of the question
+        (prompt, document, question), its rows read both ways, read out at its row 0."""
+        call = self.calls[ci]
+        key, reads, pos, own_len = self._question(r, ci)
+        for d in draws:
+            toks = call.canvas(r, d)
+            self.fresh_tokens += len(toks)
+            self.ex.submit(Task(np_rows=True, key=("cv", r, ci, d), tokens=toks, pos_start=pos + own_len,
+                                             reads=reads + [(key, own_len)], readout=True, readout_rows=(0,),
+                                             bidirectional=True, free_after=True,
+                                             on_done=lambda t, row, r=r, ci=ci, d=d: self._canvas_read(r, ci, d, row)))
+
+    def _canvas_read(self, r: int, ci: int, draw: int, row) -> None:
+        call = self.calls[ci]
+        res = self.results[r]
+        vals = np.asarray(row, dtype=np.float64).reshape(-1)
+        scores = np.asarray([vals[c] for c in call.letter_cols])
+        e = np.exp(scores - scores.max())
+        p = e / e.sum()
+        acc = self._canvas_probs.setdefault((r, ci), [])
+        acc.append(p)
+        if draw == 0:
+            entropy = float(-(p * np.log(np.maximum(p, 1e-30))).sum())
+            if call.draws > 1 and entropy > call.entropy:
+                self._canvas_draws(r, ci, range(1, call.draws))
+                return
+        elif len(acc) < call.draws:
+            return
+        mean = np.mean(self._canvas_probs.pop((r, ci)), axis=0)
+        res.values[call.name] = int(np.argmax(mean))
+        if call.probabilities:
+            res.values[call.name + "#probs"] = [float(x) for x in mean]
+        self.asked += 1
+        self._finish_call(r, ci)
 
     def _submit_isolated(self) -> None:
         """Every document as one block read both ways; then its calls, all as follow-ups."""

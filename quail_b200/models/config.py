@@ -100,6 +100,11 @@ class DecoderConfig:
     final_softcap: float = 0.0       # logits -> c * tanh(logits / c) when > 0
     canvas_tokens: int = 0           # diffusion canvas rows after each question (0: none)
     canvas_seed: int = 0
+    # a classification's answer canvas: rows read each other both ways; row 0 a random id per
+    # document and draw, row 1 the turn close, the rest padding; row 0 holds the answer
+    canvas_answer_rows: int = 0
+    canvas_turn_close: int = 106
+    canvas_pad: int = 0
 
     @property
     def bidirectional(self) -> bool:
@@ -383,7 +388,7 @@ DIFFUSION_GEMMA_26B = DecoderConfig(
     num_experts=128, top_k=8, moe_intermediate=704, max_position=131_072, layer_kinds=_DG_KINDS, arch="gemma4",
     sliding_window=1024, full_kv_heads=2, full_head_dim=512, full_rope_theta=1_000_000.0, full_rotary_pairs=0.25,
     k_eq_v=True, attn_scale=1.0, hidden_act="gelu_tanh", embed_scale=2816 ** 0.5, final_softcap=30.0,
-    canvas_tokens=1, canvas_seed=20_260_514, prompt_layout="letters",
+    canvas_tokens=1, canvas_seed=20_260_514, prompt_layout="letters", canvas_answer_rows=16,
     turn_prefix="<bos><|turn>system\nYou are an expert at text analysis<turn|>\n<|turn>user\n",
     turn_suffix="<turn|>\n<|turn>model\n<|channel>thought\n<channel|>")
 # the CPU model (fp32; checked against Hugging Face's Gemma4TextModel) and the GPU kernels' shapes

@@ -55,6 +55,21 @@ def canvas_ids(cfg: DecoderConfig) -> np.ndarray:
     return (CANVAS_TOKEN_BASE + rng.integers(0, cfg.vocab, max(cfg.canvas_tokens, 0))).astype(np.int32)
 
 
+# a first draw whose label distribution has at most this entropy (nats) is kept; others are
+# averaged over further draws of the answer canvas
+CANVAS_ENTROPY_NATS = 0.1
+
+
+def answer_canvas(cfg: DecoderConfig, doc: int, draw: int) -> np.ndarray:
+    """A classification's answer canvas for document `doc` and draw `draw`, marked: row 0 a
+    random vocabulary id (seeded by the canvas seed, the document and the draw), row 1 the turn
+    close, the rest padding. Every row is a canvas row; they read each other both ways."""
+    ids = np.full(cfg.canvas_answer_rows, cfg.canvas_pad, dtype=np.int64)
+    ids[1] = cfg.canvas_turn_close
+    ids[0] = np.random.default_rng((cfg.canvas_seed, doc, draw)).integers(0, cfg.vocab)
+    return (CANVAS_TOKEN_BASE + ids).astype(np.int32)
+
+
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return F.gelu(x, approximate="tanh")
 

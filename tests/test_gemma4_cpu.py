@@ -168,18 +168,59 @@ def test_scores_are_read_at_the_canvas_row(engine):
         assert v["s"] == pytest.approx(1.0 / (1.0 + np.exp(-margin)), abs=1e-4)
 
 
-def test_classify_is_the_best_letter_at_the_canvas_row(engine):
+def _hf_canvas_probs(hf, m, prompt, canvas, letter_ids):
+    """Hugging Face's Gemma 4 on prompt + answer canvas: the prompt causal, the canvas rows
+    reading the whole prompt (sliding layers: within the window) and each other both ways;
+    canvas rows embedded through the canvas norm. Softmax of the letters at canvas row 0."""
+    ids = torch.as_tensor(np.concatenate([prompt, canvas]).astype(np.int64))
+    n, L = len(prompt), len(prompt) + len(canvas)
+    emb = G.embed_rows(ids, m.embed, CFG.embed_scale, m.canvas_norm, CFG.rms_eps)[None]
+    i = torch.arange(L)[:, None]
+    j = torch.arange(L)[None, :]
+    see = (j <= i) | ((i >= n) & (j >= n))
+    slide = see & ((j > i - CFG.sliding_window) | ((i >= n) & (j >= n)))
+    neg = torch.finfo(torch.float32).min
+
+    def mask(ok):
+        return torch.where(ok, 0.0, neg)[None, None].float()
+    with torch.no_grad():
+        logits = hf(inputs_embeds=emb, attention_mask={"full_attention": mask(see),
+                                                       "sliding_attention": mask(slide)}).logits[0, n].float()
+    return torch.softmax(logits[letter_ids], 0).numpy()
+
+
+def test_classify_reads_row_zero_of_the_answer_canvas(engine):
+    """Letters at row 0 of a 16-row answer canvas read both ways, against Hugging Face's model
+    with that mask; an uncertain first draw is averaged over the further draws."""
     from quail_b200.api import prompts as P
     from quail_b200.api.engine import CallSpec
+    ckpt = G.random_gemma4(CFG, seed=engine.config.seed, dtype=torch.float32)
+    hf = _hf(ckpt)
+    hf.config._attn_implementation = "eager"
     labels = ["praise", "complaint", "question"]
     bp = P.bind_letters_classify_prompt(None, labels, turn=P.prompt_model(CFG).turn)
     assert bp.letters == ["A", "B", "C"] and "- B: complaint" in bp.tail
     out = engine.run_region(bp.preamble, DOCS, [CallSpec(kind="classify", tail=bp.tail, name="k", labels=labels,
-                                                         letters=bp.letters)])
-    ids = [int(engine.tokenizer.encode(x)[0]) for x in bp.letters]
-    for doc, v in zip(DOCS, out.values):
-        row = _canvas_logits(engine, bp, doc, ids)
-        assert v["k"] == labels[int(row.argmax())]
+                                                         letters=bp.letters, probabilities=True)])
+    tok = engine.tokenizer
+    ids = [int(tok.encode(x)[0]) for x in bp.letters]
+    draws = engine.config.canvas_draws
+    for r, (doc, v) in enumerate(zip(DOCS, out.values)):
+        prompt = np.concatenate([tok.encode(bp.preamble), tok.encode(doc), tok.encode(bp.tail)])
+        first = _hf_canvas_probs(hf, engine.model, prompt, G.answer_canvas(CFG, r, 0), ids)
+        entropy = float(-(first * np.log(first)).sum())
+        ps = [first] if entropy <= G.CANVAS_ENTROPY_NATS else [first] + [
+            _hf_canvas_probs(hf, engine.model, prompt, G.answer_canvas(CFG, r, d), ids) for d in range(1, draws)]
+        mean = np.mean(ps, axis=0)
+        assert v["k"] == labels[int(np.argmax(mean))]
+        assert np.allclose(v["k#probs"], mean, atol=1e-4), (v["k#probs"], mean)
+
+
+def test_answer_canvas_rows():
+    c0, c1 = G.answer_canvas(CFG, 3, 0), G.answer_canvas(CFG, 3, 1)
+    assert len(c0) == CFG.canvas_answer_rows and (c0 >= G.CANVAS_TOKEN_BASE).all()
+    assert c0[1] - G.CANVAS_TOKEN_BASE == CFG.canvas_turn_close and (c0[2:] - G.CANVAS_TOKEN_BASE == CFG.canvas_pad).all()
+    assert (G.answer_canvas(CFG, 3, 0) == c0).all() and c0[0] != c1[0]     # seeded per document and draw
 
 
 def test_sql_on_the_canvas_model():
