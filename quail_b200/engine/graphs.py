@@ -48,8 +48,12 @@ class _Entry:
                       "blocks": 0}
         self.total = sum(self.sizes.values())
         self.buf = torch.zeros(self.total, dtype=torch.int32, device=device)
-        self.stage = torch.empty(self.total, dtype=torch.int32, pin_memory=True)
-        self.copy_done = None
+        # two pinned staging images, used in turn: filling one waits only for the copy out of
+        # the other two passes back, so the host stays a pass ahead of the replays (with one
+        # image it waited for the previous pass's copy, which is queued behind its replay)
+        self.stages = [torch.empty(self.total, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self.copies = [None, None]
+        self.turn = 0
         self.graph = None
         self.out = None
         self.launches = 0
@@ -90,13 +94,15 @@ class _Entry:
             # hybrid models: real rows carry their state slots; padding starts from zeros and keeps nothing
             img["state_io"][:T] = np.asarray(host["state_io"]).reshape(-1, 2)[:T]
         flat = np.concatenate([img[k].reshape(-1) for k in PARTS])
-        if self.copy_done is not None:
-            self.copy_done.synchronize()
-        self.stage.copy_(torch.from_numpy(flat))
-        self.buf.copy_(self.stage, non_blocking=True)
+        i = self.turn
+        self.turn ^= 1
+        if self.copies[i] is not None:
+            self.copies[i].synchronize()
+        self.stages[i].copy_(torch.from_numpy(flat))
+        self.buf.copy_(self.stages[i], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
-        self.copy_done = ev
+        self.copies[i] = ev
         return int(flat.nbytes)
 
 

@@ -47,7 +47,10 @@ def main():
 
     cfg = MODEL_CONFIGS[args.model]
     pipe = build_pipeline(cfg, dev, answer_ids=list(range(8)))
-    arena = KVArena(cfg.layers, args.pages, 128, cfg.num_kv_heads, cfg.head_dim, device=dev)
+    from quail_b200.planner.budgets import Budgets
+    # hybrids keep a recurrent state slot per running row beside the KV pages
+    slots = Budgets.for_model(cfg, "b200", gpus=1).state_slots(cfg) if cfg.is_hybrid else 0
+    arena = KVArena.for_model(cfg, args.pages, 128, device=dev, state_slots=slots)
 
     def region(rows, seed, graphs):
         wl = make_workload(rows, median=250, sigma=0.6, hi=4096, suffix_tokens=24, seed=seed)
