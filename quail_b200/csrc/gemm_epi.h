@@ -11,6 +11,7 @@ enum Epi : int {
   kEpiQkvRope = 4,     // per 128-column head: q/k RMSNorm + NeoX RoPE; q -> q_out, k/v -> paged cache
   kEpiResidualMx = 5,  // D = acc + R (bf16), and D as e4m3 + UE8M0 per 32 columns, row sums of squares
   kEpiGegluBf16 = 6,   // D = gelu_tanh(g) * u (bf16), gate/up interleaved as for SwiGLU
+  kEpiGegluFp8 = 7,    // MX GEMM: Y = e4m3(gelu_tanh(g) * u) + UE8M0 scales, as kEpiSwigluFp8
 };
 
 }  // namespace qb

@@ -355,7 +355,13 @@ __global__ void __launch_bounds__(64 + kMxBN, 1)
         const int out0 = tn * (BN / 2) + h * 64;
         if (out0 >= p.N / 2) continue;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i] = silu_f(acc[i]) * acc[64 + i];
+        for (int i = 0; i < 64; ++i) {
+          if constexpr (EPI == kEpiGegluFp8) {
+            acc[i] = gelu_tanh_f(acc[i]) * acc[64 + i];
+          } else {
+            acc[i] = silu_f(acc[i]) * acc[64 + i];
+          }
+        }
         if constexpr (EPI == kEpiSwigluBf16) {
           __nv_bfloat16* dst = p.D + (size_t)m * p.ldd + out0;
 #pragma unroll
@@ -445,8 +451,8 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
   p.num_m_tiles = (M + 127) / 128;
   p.n_fast = M > N ? 1 : 0;
   p.num_n_tiles = (N + kMxBN - 1) / kMxBN;
-  if (epi == kEpiSwigluFp8) {
-    TORCH_CHECK(N % kMxBN == 0, "SwiGLU: N must be a multiple of 256");
+  if (epi == kEpiSwigluFp8 || epi == kEpiGegluFp8) {
+    TORCH_CHECK(N % kMxBN == 0, "SwiGLU / GeGLU: N must be a multiple of 256");
     TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.size(0) == M && out.size(1) == N / 2 &&
                     out.stride(1) == 1 && out.stride(0) % 16 == 0,
                 "SwiGLU fp8 output");
@@ -499,6 +505,7 @@ void gemm_mx(const torch::Tensor& a, const torch::Tensor& sfa, const torch::Tens
     case kEpiResidualMx: launch_mx<kEpiResidualMx>(ta, tb, p, st, dev); break;
     case kEpiSwigluFp8: launch_mx<kEpiSwigluFp8>(ta, tb, p, st, dev); break;
     case kEpiSwigluBf16: launch_mx<kEpiSwigluBf16>(ta, tb, p, st, dev); break;
+    case kEpiGegluFp8: launch_mx<kEpiGegluFp8>(ta, tb, p, st, dev); break;
     default: TORCH_CHECK(false, "gemm_mx: unknown epilogue ", epi);
   }
 }

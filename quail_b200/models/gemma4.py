@@ -354,6 +354,14 @@ class DiffusionGemmaPipeline:
             u = _pad_rows(ckpt[p + "mlp.up_proj.weight"].to(dev, torch.float32), I_pad)
             L["wgu"] = interleave_gate_up(torch.cat([g, u]).to(bf)).contiguous()
             L["wd"] = _pad_cols(ckpt[p + "mlp.down_proj.weight"].to(dev, torch.float32), I_pad).to(bf).contiguous()
+            if cfg.fp8:
+                # fp8 checkpoints: the projections run on the MX (block-scaled e4m3) GEMM
+                L["wqkv8"], L["sqkv"] = quantize_weight_mx(L["wqkv"].float())
+                L["wo8"], L["so"] = quantize_weight_mx(L["wo"].float())
+                L["wgu8"], L["sgu"] = interleave_gate_up_mx(torch.cat([g, u]))
+                L["wd8"], L["sd"] = quantize_weight_mx(L["wd"].float())
+                for k in ("wqkv", "wo", "wgu", "wd"):
+                    del L[k]
             if cfg.is_moe:
                 L.update(ln_post_ffn1=t(p + "post_feedforward_layernorm_1.weight"),
                          ln_post_ffn2=t(p + "post_feedforward_layernorm_2.weight"),
@@ -423,7 +431,12 @@ class DiffusionGemmaPipeline:
         for i, L in enumerate(self.layers):
             kh, d = L["kh"], L["d"]
             QH = cfg.num_q_heads
-            p = ops.gemm(x, L["wqkv"])
+            mx = "wqkv8" in L
+            if mx:
+                x8, xs = ops.quant_rows_mx(x)
+                p = ops.gemm_mx(x8, xs, L["wqkv8"], L["sqkv"])
+            else:
+                p = ops.gemm(x, L["wqkv"])
             kc, vc = arena.layer(i)
             q = torch.empty(T, QH, d, dtype=torch.bfloat16, device=dev)
             ops.count_launch(1)
@@ -432,9 +445,18 @@ class DiffusionGemmaPipeline:
             o = torch.empty(T, QH * d, dtype=torch.bfloat16, device=dev)
             ops.small_attention(q, kc, vc, chunk.seqs if L["full"] else seqs_w, chunk.tiles, chunk.dseqs,
                                 chunk.page_list, self.scale, o, None, 0)
-            a = ops.gemm(o, L["wo"])
+            if mx:
+                o8, os_ = ops.quant_rows_mx(o)
+                a = ops.gemm_mx(o8, os_, L["wo8"], L["so"])
+            else:
+                a = ops.gemm(o, L["wo"])
             x = ops.post_norm_add_norm(a, h, L["ln_post_attn"], L["ln_pre_ffn"], eps)
-            dense = ops.gemm(ops.gemm(x, L["wgu"], epi=ops.EPI_GEGLU_BF16), L["wd"])
+            if mx:
+                x8, xs = ops.quant_rows_mx(x)
+                g8, gs = ops.gemm_mx(x8, xs, L["wgu8"], L["sgu"], epi=ops.EPI_GEGLU_FP8)
+                dense = ops.gemm_mx(g8, gs, L["wd8"], L["sd"])
+            else:
+                dense = ops.gemm(ops.gemm(x, L["wgu"], epi=ops.EPI_GEGLU_BF16), L["wd"])
             if cfg.is_moe:
                 xb = ops.rmsnorm_quant(h, L["router_in"], eps, fp8=False)
                 x8, xs = ops.rmsnorm_quant_mx(h, L["ln_pre_ffn2"], eps)

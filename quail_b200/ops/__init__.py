@@ -13,6 +13,7 @@ from quail_b200.ops.kernels import (  # noqa: F401
     EPI_RESIDUAL,
     EPI_SWIGLU_BF16,
     EPI_GEGLU_BF16,
+    EPI_GEGLU_FP8,
     EPI_SWIGLU_FP8,
     chunk_attention,
     decode_attention,

@@ -30,6 +30,7 @@ EPI_RESIDUAL = 1
 EPI_SWIGLU_FP8 = 2
 EPI_SWIGLU_BF16 = 3
 EPI_GEGLU_BF16 = 6
+EPI_GEGLU_FP8 = 7
 EPI_RESIDUAL_MX = 5
 
 
@@ -103,7 +104,7 @@ def gemm_mx(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     C = native()
     M, N = a.shape[0], b.shape[0]
     count_launch()
-    if epi == EPI_SWIGLU_FP8:
+    if epi in (EPI_SWIGLU_FP8, EPI_GEGLU_FP8):
         if out is None:
             out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a.device)
         if out_sf is None:

@@ -34,11 +34,14 @@ def _run(model, cfg, dtype, chunk_tokens=256):
     return torch.stack([got[i] for i in range(len(docs))])
 
 
-def test_pipeline_tracks_the_statement():
+@pytest.mark.parametrize("weights", ["bf16", "fp8"])
+def test_pipeline_tracks_the_statement(weights):
+    """bf16 weights: the projections on the bf16 GEMM; fp8 weights: on the MX GEMM (the GeGLU
+    epilogue writing e4m3 for the down projection), against the unquantized statement."""
     from quail_b200 import ops
     from quail_b200.models import gemma4 as G
     from quail_b200.models.config import MODEL_CONFIGS
-    cfg = MODEL_CONFIGS["diffusion-gemma-gpu-tiny"]
+    cfg = MODEL_CONFIGS["diffusion-gemma-gpu-tiny"].with_(weight_dtype=weights)
     ckpt = G.random_gemma4(cfg, seed=5, device=DEV, dtype=torch.bfloat16)
     ids = list(range(16))
     pipe = G.DiffusionGemmaPipeline(cfg, ckpt, DEV, head_rows=ids)
@@ -48,8 +51,10 @@ def test_pipeline_tracks_the_statement():
     assert ops.read_and_clear_error(0) == 0
     d = (got - want).norm() / want.norm()
     corr = torch.corrcoef(torch.stack([got.flatten(), want.flatten()]))[0, 1]
-    print(f"diffusion-gemma kernel-vs-fp32: rel {d:.4f}, corr {corr:.4f}")
-    assert d < 0.15 and corr > 0.98
+    print(f"diffusion-gemma {weights} kernel-vs-fp32: rel {d:.4f}, corr {corr:.4f}")
+    # measured: bf16 0.075 / 0.997; fp8 0.225 / 0.974 (e4m3 activations at every projection over
+    # four layers; one GeGLU fp8 GEMM alone is within 0.046 of its dequantized operands' product)
+    assert d < (0.15 if weights == "bf16" else 0.3) and corr > (0.98 if weights == "bf16" else 0.96)
     # the same chunks in one pass and split across passes agree on the kernels too
     again = _run(pipe, cfg, torch.bfloat16, chunk_tokens=96)
     assert (again - got).norm() / got.norm() < 0.05
